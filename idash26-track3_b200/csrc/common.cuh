@@ -1,0 +1,135 @@
+// Shared definitions of the DeepDTAGen 2PC library: status codes, ring types,
+// key-layout arithmetic.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "../../include/ddg_fss.h"
+
+namespace ddg {
+
+inline uint64_t align256(uint64_t x) { return (x + 255u) & ~uint64_t(255); }
+
+// status-returning CUDA check: records the first failure and returns from the
+// calling function with DDG_ERR_CUDA
+#define DDG_CUDA(expr)                                                                        \
+    do {                                                                                      \
+        cudaError_t _e = (expr);                                                              \
+        if (_e != cudaSuccess) {                                                              \
+            ::ddg::set_last_error("%s:%d %s: %s", __FILE__, __LINE__, #expr, cudaGetErrorString(_e)); \
+            return DDG_ERR_CUDA;                                                              \
+        }                                                                                     \
+    } while (0)
+
+#define DDG_CHECK(cond, code, ...)              \
+    do {                                        \
+        if (!(cond)) {                          \
+            ::ddg::set_last_error(__VA_ARGS__); \
+            return (code);                      \
+        }                                       \
+    } while (0)
+
+#define DDG_TRY(expr)                \
+    do {                             \
+        int _s = (expr);             \
+        if (_s != DDG_OK) return _s; \
+    } while (0)
+
+void set_last_error(const char *fmt, ...);
+
+// ---------------------------------------------------------------- key layouts
+
+// gate kinds (the comparison-based nonlinear layers)
+enum GateKind { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3 };
+
+inline bool gate_has_hi(int kind) { return kind != GATE_LRS; }
+inline bool gate_has_lo(int kind) { return kind != GATE_RELU; }
+inline int gate_nwords(int kind)
+{
+    switch (kind) {
+    case GATE_RELU: return 4;
+    case GATE_RELU_ARS: return 8;
+    case GATE_ARS: return 6;
+    default: return 4;
+    }
+}
+
+// DCF key arrays of N elements, structure-of-arrays, every array 256-byte aligned:
+//   root[N] (16 B) | cw[L][N] (16 B, level-major) | leaf[N] (16 B) | mu[ceil(N/32)] (u32 bits)
+struct DcfLayout {
+    int d = 0, L = 0;
+    uint64_t root = 0, cw = 0, leaf = 0, mu = 0, end = 0;
+};
+
+inline int dcf_levels(int d) { return d > 7 ? d - 7 : 0; }
+
+inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base)
+{
+    DcfLayout l;
+    l.d = d;
+    l.L = dcf_levels(d);
+    l.root = align256(base);
+    l.cw = align256(l.root + 16 * n);
+    l.leaf = align256(l.cw + 16 * n * uint64_t(l.L));
+    l.mu = align256(l.leaf + 16 * n);
+    l.end = align256(l.mu + 4 * ((n + 31) / 32));
+    return l;
+}
+
+// one gate op: [hi DCF over n-1 bits] [lo DCF over s bits] [nwords x N ring words]
+struct GateLayout {
+    int kind = 0, bw = 0, s = 0;
+    uint64_t n = 0;
+    bool hi = false, lo = false;
+    DcfLayout H, Lo;
+    int nwords = 0;
+    uint64_t words = 0, bytes = 0;
+};
+
+inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base = 0)
+{
+    GateLayout g;
+    g.kind = kind, g.bw = bw, g.s = s, g.n = n;
+    g.hi = gate_has_hi(kind);
+    g.lo = gate_has_lo(kind);
+    uint64_t off = align256(base);
+    if (g.hi) {
+        g.H = dcf_layout(bw - 1, n, off);
+        off = g.H.end;
+    }
+    if (g.lo) {
+        g.Lo = dcf_layout(s, n, off);
+        off = g.Lo.end;
+    }
+    g.nwords = gate_nwords(kind);
+    g.words = align256(off);
+    g.bytes = align256(g.words + uint64_t(g.nwords) * n * uint64_t(bw / 8)) - align256(base);
+    return g;
+}
+
+// DCF view handed to kernels (device pointers)
+struct DcfView {
+    const uint8_t *root, *cw, *leaf;
+    const uint32_t *mu;
+};
+
+struct DcfOut {
+    uint8_t *root0, *root1, *cw0, *cw1, *leaf0, *leaf1;
+    uint32_t *mu0, *mu1;
+};
+
+inline DcfView dcf_view(const uint8_t *key, const DcfLayout &l)
+{
+    return DcfView{key + l.root, key + l.cw, key + l.leaf, reinterpret_cast<const uint32_t *>(key + l.mu)};
+}
+
+// dealer PRG purposes
+enum Purpose : uint32_t {
+    P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4, P_ROUT = 5, P_BITS = 6,
+    P_MASK = 8,    // input / output masks of linear ops
+    P_SHARE = 16,  // share0 of dealer word k uses purpose P_SHARE + k
+};
+
+}  // namespace ddg

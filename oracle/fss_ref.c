@@ -1,0 +1,562 @@
+/*
+ * fss_ref.c -- CPU restatement of the FSS primitives used on the online
+ * 2PC inference path.  TEST INFRASTRUCTURE ONLY: it is linked by tests/,
+ * by __graft_entry__.smoke() and by bench.py's cpu_baseline leg as a checker.
+ * The product (libddg.so) never links or calls it.
+ *
+ * Why this file exists
+ * --------------------
+ * The reference's FSS arithmetic (DCF/DPF tree evaluation, DReLU + select,
+ * DPF-LUT, truncation) is un-vendored EzPC GPU-MPC code (reference
+ * gpu_mpc/ddg_orca_base.h:1 names commit 66d9cddc); it is not present, so the
+ * reference's key formats cannot be reproduced.  This build therefore uses
+ * its own published-algorithm FSS scheme, restated here byte-for-byte in plain
+ * C so the CUDA kernels can be checked share-for-share:
+ *
+ *  - AES-128 as in FIPS-197 (S-box derived from the GF(2^8) inverse plus the
+ *    affine map; pinned by the FIPS-197 appendix C.1 vector that the
+ *    reference's own test uses, gpu_mpc/lss/lss_test.cpp:52-70).
+ *  - Fixed-key circular-correlation-robust hash H(x) = pi(sigma(x)) ^ sigma(x)
+ *    with sigma(lo,hi) = (hi, lo^hi) (Guo, Katz, Wang, Yu, "Efficient and
+ *    secure multiparty computation from fixed-key block ciphers", S&P 2020).
+ *  - Half-tree DPF (Guo, Yang, Wang, Zhang, Xie, Liu, Zhao, EUROCRYPT 2023):
+ *    on-path seeds differ by a fixed Delta with lsb(Delta)=1, the control bit
+ *    is lsb(seed), the right child is left ^ parent, one H call per level.
+ *  - DCF 1{x < alpha} derived from that DPF: XOR of the control bits of the
+ *    right siblings of x's path at every level where x goes left, plus a
+ *    128-bit early-termination leaf holding 1{y < alpha_low}.
+ *  - Gates (ReLU, ReLU o ARS, ARS, LRS of a non-negative value) built from a
+ *    high (n-1)-bit DCF and a low s-bit DCF, as documented in gate_keygen.
+ *  - DPF look-up table over an 8-bit domain (secure_adj_norm.h:139-184 table
+ *    t[0]=0, t[d]=llround(2^s/sqrt(d)) for 1<=d<=nmax).
+ *
+ * All integer arithmetic is on uint64_t reduced to n bits (n = 32 or 64).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ AES */
+
+static uint8_t SBOX[256];
+static int sbox_ready = 0;
+
+static uint8_t xtime(uint8_t a) { return (uint8_t)((a << 1) ^ ((a & 0x80) ? 0x1b : 0)); }
+
+static uint8_t gmul(uint8_t a, uint8_t b)
+{
+    uint8_t p = 0;
+    while (b) {
+        if (b & 1) p ^= a;
+        a = xtime(a);
+        b >>= 1;
+    }
+    return p;
+}
+
+static uint8_t rotl8(uint8_t x, int k) { return (uint8_t)((x << k) | (x >> (8 - k))); }
+
+static void build_sbox(void)
+{
+    for (int x = 0; x < 256; x++) {
+        /* multiplicative inverse in GF(2^8): x^254 (0 maps to 0) */
+        uint8_t inv = 0;
+        if (x) {
+            uint8_t r = 1, base = (uint8_t)x;
+            int e = 254;
+            while (e) {
+                if (e & 1) r = gmul(r, base);
+                base = gmul(base, base);
+                e >>= 1;
+            }
+            inv = r;
+        }
+        SBOX[x] = (uint8_t)(inv ^ rotl8(inv, 1) ^ rotl8(inv, 2) ^ rotl8(inv, 3) ^ rotl8(inv, 4) ^ 0x63);
+    }
+    sbox_ready = 1;
+}
+
+typedef struct { uint8_t rk[176]; } aes_ks;
+
+void ref_aes128_expand(const uint8_t key[16], aes_ks *ks)
+{
+    if (!sbox_ready) build_sbox();
+    memcpy(ks->rk, key, 16);
+    uint8_t rcon = 1;
+    for (int i = 4; i < 44; i++) {
+        uint8_t t[4];
+        memcpy(t, ks->rk + 4 * (i - 1), 4);
+        if (i % 4 == 0) {
+            uint8_t t0 = t[0];
+            t[0] = (uint8_t)(SBOX[t[1]] ^ rcon);
+            t[1] = SBOX[t[2]];
+            t[2] = SBOX[t[3]];
+            t[3] = SBOX[t0];
+            rcon = xtime(rcon);
+        }
+        for (int k = 0; k < 4; k++) ks->rk[4 * i + k] = (uint8_t)(ks->rk[4 * (i - 4) + k] ^ t[k]);
+    }
+}
+
+void ref_aes128_encrypt(const aes_ks *ks, const uint8_t in[16], uint8_t out[16])
+{
+    uint8_t st[16], tmp[16];
+    for (int i = 0; i < 16; i++) st[i] = (uint8_t)(in[i] ^ ks->rk[i]);
+    for (int round = 1; round <= 10; round++) {
+        for (int i = 0; i < 16; i++) st[i] = SBOX[st[i]];
+        /* ShiftRows: byte (row r, col c) lives at r + 4c */
+        for (int c = 0; c < 4; c++)
+            for (int r = 0; r < 4; r++) tmp[r + 4 * c] = st[r + 4 * ((c + r) & 3)];
+        if (round != 10) {
+            for (int c = 0; c < 4; c++) {
+                uint8_t a0 = tmp[4 * c], a1 = tmp[4 * c + 1], a2 = tmp[4 * c + 2], a3 = tmp[4 * c + 3];
+                st[4 * c + 0] = (uint8_t)(gmul(a0, 2) ^ gmul(a1, 3) ^ a2 ^ a3);
+                st[4 * c + 1] = (uint8_t)(a0 ^ gmul(a1, 2) ^ gmul(a2, 3) ^ a3);
+                st[4 * c + 2] = (uint8_t)(a0 ^ a1 ^ gmul(a2, 2) ^ gmul(a3, 3));
+                st[4 * c + 3] = (uint8_t)(gmul(a0, 3) ^ a1 ^ a2 ^ gmul(a3, 2));
+            }
+        } else {
+            memcpy(st, tmp, 16);
+        }
+        for (int i = 0; i < 16; i++) st[i] ^= ks->rk[16 * round + i];
+    }
+    memcpy(out, st, 16);
+}
+
+/* ------------------------------------------------------- fixed-key hashes */
+
+static const char KEY_H[17] = "ddg-halftree-H:0"; /* tree-node hash key */
+static const char KEY_C[17] = "ddg-halftree-C:1"; /* leaf conversion key */
+static aes_ks ks_h, ks_c;
+static int fixed_ready = 0;
+
+static void fixed_init(void)
+{
+    ref_aes128_expand((const uint8_t *)KEY_H, &ks_h);
+    ref_aes128_expand((const uint8_t *)KEY_C, &ks_c);
+    fixed_ready = 1;
+}
+
+static void sigma(const uint8_t x[16], uint8_t y[16])
+{
+    /* x = lo (bytes 0..7) || hi (bytes 8..15);  sigma(x) = hi || (lo ^ hi) */
+    for (int i = 0; i < 8; i++) {
+        y[i] = x[8 + i];
+        y[8 + i] = (uint8_t)(x[i] ^ x[8 + i]);
+    }
+}
+
+static void ccr(const aes_ks *ks, const uint8_t x[16], uint8_t out[16])
+{
+    uint8_t sx[16], e[16];
+    sigma(x, sx);
+    ref_aes128_encrypt(ks, sx, e);
+    for (int i = 0; i < 16; i++) out[i] = (uint8_t)(e[i] ^ sx[i]);
+}
+
+void ref_hash_h(const uint8_t x[16], uint8_t out[16])
+{
+    if (!fixed_ready) fixed_init();
+    ccr(&ks_h, x, out);
+}
+
+void ref_hash_c(const uint8_t x[16], uint8_t out[16])
+{
+    if (!fixed_ready) fixed_init();
+    ccr(&ks_c, x, out);
+}
+
+/* ------------------------------------------------------------ dealer PRG */
+
+/* dealer key bytes: seed (8 bytes LE) || "dealerK1" */
+void ref_dealer_key(uint64_t seed, aes_ks *ks)
+{
+    uint8_t k[16];
+    for (int i = 0; i < 8; i++) k[i] = (uint8_t)(seed >> (8 * i));
+    memcpy(k + 8, "dealerK1", 8);
+    ref_aes128_expand(k, ks);
+}
+
+/* one pseudo-random block for (op, purpose, index): AES_K(index || op || purpose) */
+void ref_prg(const aes_ks *ks, uint32_t op, uint32_t purpose, uint64_t idx, uint8_t out[16])
+{
+    uint8_t pt[16];
+    for (int i = 0; i < 8; i++) pt[i] = (uint8_t)(idx >> (8 * i));
+    for (int i = 0; i < 4; i++) pt[8 + i] = (uint8_t)(op >> (8 * i));
+    for (int i = 0; i < 4; i++) pt[12 + i] = (uint8_t)(purpose >> (8 * i));
+    ref_aes128_encrypt(ks, pt, out);
+}
+
+static uint64_t nmask(int n) { return n >= 64 ? ~0ULL : ((1ULL << n) - 1); }
+
+static uint64_t ring_of(const uint8_t b[16], int n)
+{
+    uint64_t v = 0;
+    for (int i = 0; i < 8; i++) v |= (uint64_t)b[i] << (8 * i);
+    return v & nmask(n);
+}
+
+/* ------------------------------------------------------------------- DCF */
+
+static int tree_levels(int d) { return d > 7 ? d - 7 : 0; }
+
+static void xor16(uint8_t *a, const uint8_t *b)
+{
+    for (int i = 0; i < 16; i++) a[i] ^= b[i];
+}
+
+static int block_bit(const uint8_t b[16], int y) { return (b[y >> 3] >> (y & 7)) & 1; }
+
+/*
+ * Keys for 1{x < alpha} over d-bit x.  Levels j = 0..L-1 consume x's bits from
+ * the most significant down; the last min(d,7) bits index the 128-bit leaf.
+ * cw receives L blocks (16 bytes each).
+ */
+void ref_dcf_keygen(int d, uint64_t alpha, const uint8_t s0[16], const uint8_t delta_in[16],
+                    uint8_t root0[16], uint8_t root1[16], uint8_t *cw, uint8_t leafcw[16])
+{
+    if (!fixed_ready) fixed_init();
+    int L = tree_levels(d), lb = d - L;
+    uint8_t delta[16], cur[2][16], h[2][16];
+    memcpy(delta, delta_in, 16);
+    delta[0] |= 1;
+    memcpy(cur[0], s0, 16);
+    memcpy(cur[1], s0, 16);
+    xor16(cur[1], delta);
+    memcpy(root0, cur[0], 16);
+    memcpy(root1, cur[1], 16);
+    for (int j = 0; j < L; j++) {
+        int a = (int)((alpha >> (d - 1 - j)) & 1);
+        ccr(&ks_h, cur[0], h[0]);
+        ccr(&ks_h, cur[1], h[1]);
+        uint8_t *c = cw + 16 * j;
+        for (int i = 0; i < 16; i++) c[i] = (uint8_t)(h[0][i] ^ h[1][i] ^ (a ? 0 : delta[i]));
+        for (int b = 0; b < 2; b++) {
+            int t = cur[b][0] & 1;
+            uint8_t cl[16];
+            for (int i = 0; i < 16; i++) cl[i] = (uint8_t)(h[b][i] ^ (t ? c[i] : 0));
+            if (a) xor16(cur[b], cl); /* right child: left ^ parent */
+            else memcpy(cur[b], cl, 16);
+        }
+    }
+    uint8_t g0[16], g1[16], m[16];
+    memset(m, 0, 16);
+    uint64_t al = alpha & ((1ULL << lb) - 1);
+    for (uint64_t y = 0; y < al; y++) m[y >> 3] |= (uint8_t)(1u << (y & 7));
+    ccr(&ks_c, cur[0], g0);
+    ccr(&ks_c, cur[1], g1);
+    for (int i = 0; i < 16; i++) leafcw[i] = (uint8_t)(g0[i] ^ g1[i] ^ m[i]);
+}
+
+/* party's XOR share of 1{x < alpha} */
+int ref_dcf_eval(int d, uint64_t x, const uint8_t root[16], const uint8_t *cw, const uint8_t leafcw[16])
+{
+    if (!fixed_ready) fixed_init();
+    int L = tree_levels(d), lb = d - L;
+    uint8_t s[16], h[16], cl[16];
+    memcpy(s, root, 16);
+    int c = 0;
+    for (int j = 0; j < L; j++) {
+        int xj = (int)((x >> (d - 1 - j)) & 1);
+        int t = s[0] & 1;
+        ccr(&ks_h, s, h);
+        for (int i = 0; i < 16; i++) cl[i] = (uint8_t)(h[i] ^ (t ? cw[16 * j + i] : 0));
+        if (!xj) {
+            c ^= (cl[0] ^ s[0]) & 1; /* lsb of the right sibling */
+            memcpy(s, cl, 16);
+        } else {
+            xor16(s, cl);
+        }
+    }
+    int t = s[0] & 1;
+    uint8_t g[16];
+    ccr(&ks_c, s, g);
+    if (t) xor16(g, leafcw);
+    c ^= block_bit(g, (int)(x & ((1ULL << lb) - 1)));
+    return c;
+}
+
+/* ----------------------------------------------------------------- gates */
+
+enum { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3 };
+
+enum {
+    P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4,
+    P_ROUT = 5, P_BITS = 6, P_SHARE = 16
+};
+
+typedef struct {
+    uint8_t hi_root[16];
+    uint8_t hi_cw[56][16];
+    uint8_t hi_leaf[16];
+    int32_t hi_mu;
+    uint8_t lo_root[16];
+    uint8_t lo_cw[56][16];
+    uint8_t lo_leaf[16];
+    int32_t lo_mu;
+    uint64_t w[8];
+} ref_gate_key;
+
+int ref_gate_has_hi(int kind) { return kind != GATE_LRS; }
+int ref_gate_has_lo(int kind) { return kind != GATE_RELU; }
+int ref_gate_nwords(int kind)
+{
+    switch (kind) {
+    case GATE_RELU: return 4;
+    case GATE_RELU_ARS: return 8;
+    case GATE_ARS: return 6;
+    default: return 4;
+    }
+}
+
+/*
+ * Dealer side for one element.  r_in is the input mask (x_hat = x + r_in),
+ * the output mask is drawn from the PRG and returned.
+ *
+ * Notation: r_m = msb(r_in), r_l = r_in mod 2^(n-1), r_H = r_in >> s,
+ * r_L = r_in mod 2^s.  The high DCF opens c_hat = 1{xh_l < r_l} ^ rho_c, the
+ * low DCF opens cL_hat = 1{xh_L < r_L} ^ rho_L; e = r_m ^ rho_c.
+ * Word lists (additively shared in Z_2^n):
+ *   RELU     : e, r, e*r, r_y
+ *   RELU_ARS : e, r_H, e*r_H, rho_L, e*rho_L, r_m, e*r_m, r_y
+ *   ARS      : r_H, rho_L, rho_c, r_m, r_m*rho_c, r_y
+ *   LRS      : r_H, rho_L, r_m, r_y
+ */
+uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint64_t i,
+                         uint64_t r_in, ref_gate_key *k0, ref_gate_key *k1)
+{
+    aes_ks ks;
+    ref_dealer_key(seed, &ks);
+    uint64_t M = nmask(n);
+    uint8_t blk[16], blk2[16];
+    memset(k0, 0, sizeof(*k0));
+    memset(k1, 0, sizeof(*k1));
+    r_in &= M;
+
+    ref_prg(&ks, op, P_ROUT, i, blk);
+    uint64_t r_y = ring_of(blk, n);
+    ref_prg(&ks, op, P_BITS, i, blk);
+    int mu0h = blk[0] & 1, mu1h = (blk[0] >> 1) & 1, mu0l = (blk[0] >> 2) & 1, mu1l = (blk[0] >> 3) & 1;
+    int rho_c = mu0h ^ mu1h, rho_L = mu0l ^ mu1l;
+
+    uint64_t r_m = (r_in >> (n - 1)) & 1;
+    uint64_t r_l = r_in & (M >> 1);
+    uint64_t r_H = r_in >> s;
+    uint64_t r_L = r_in & ((1ULL << s) - 1);
+    uint64_t e = r_m ^ (uint64_t)rho_c;
+
+    if (ref_gate_has_hi(kind)) {
+        ref_prg(&ks, op, P_HI_S0, i, blk);
+        ref_prg(&ks, op, P_HI_DELTA, i, blk2);
+        ref_dcf_keygen(n - 1, r_l, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
+        memcpy(k1->hi_cw, k0->hi_cw, sizeof(k0->hi_cw));
+        memcpy(k1->hi_leaf, k0->hi_leaf, 16);
+        k0->hi_mu = mu0h;
+        k1->hi_mu = mu1h;
+    }
+    if (ref_gate_has_lo(kind)) {
+        ref_prg(&ks, op, P_LO_S0, i, blk);
+        ref_prg(&ks, op, P_LO_DELTA, i, blk2);
+        ref_dcf_keygen(s, r_L, blk, blk2, k0->lo_root, k1->lo_root, &k0->lo_cw[0][0], k0->lo_leaf);
+        memcpy(k1->lo_cw, k0->lo_cw, sizeof(k0->lo_cw));
+        memcpy(k1->lo_leaf, k0->lo_leaf, 16);
+        k0->lo_mu = mu0l;
+        k1->lo_mu = mu1l;
+    }
+    uint64_t v[8];
+    int nw = ref_gate_nwords(kind);
+    switch (kind) {
+    case GATE_RELU:
+        v[0] = e; v[1] = r_in; v[2] = e * r_in; v[3] = r_y;
+        break;
+    case GATE_RELU_ARS:
+        v[0] = e; v[1] = r_H; v[2] = e * r_H; v[3] = (uint64_t)rho_L;
+        v[4] = e * (uint64_t)rho_L; v[5] = r_m; v[6] = e * r_m; v[7] = r_y;
+        break;
+    case GATE_ARS:
+        v[0] = r_H; v[1] = (uint64_t)rho_L; v[2] = (uint64_t)rho_c; v[3] = r_m;
+        v[4] = r_m * (uint64_t)rho_c; v[5] = r_y;
+        break;
+    default:
+        v[0] = r_H; v[1] = (uint64_t)rho_L; v[2] = r_m; v[3] = r_y;
+        break;
+    }
+    for (int w = 0; w < nw; w++) {
+        ref_prg(&ks, op, P_SHARE + (uint32_t)w, i, blk);
+        uint64_t a = ring_of(blk, n);
+        k0->w[w] = a;
+        k1->w[w] = (v[w] - a) & M;
+    }
+    return r_y;
+}
+
+/* round 1: the party's two output bits (bit0 = high DCF, bit1 = low DCF) */
+int ref_gate_round1(int kind, int n, int s, uint64_t xhat, const ref_gate_key *k)
+{
+    uint64_t M = nmask(n);
+    xhat &= M;
+    int out = 0;
+    if (ref_gate_has_hi(kind))
+        out |= (ref_dcf_eval(n - 1, xhat & (M >> 1), k->hi_root, &k->hi_cw[0][0], k->hi_leaf) ^ k->hi_mu) & 1;
+    if (ref_gate_has_lo(kind))
+        out |= ((ref_dcf_eval(s, xhat & ((1ULL << s) - 1), k->lo_root, &k->lo_cw[0][0], k->lo_leaf) ^ k->lo_mu) & 1)
+               << 1;
+    return out;
+}
+
+/* round 2: party's additive share of the masked output, given the opened bits */
+uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int c_hat, int cl_hat,
+                         const ref_gate_key *k)
+{
+    uint64_t M = nmask(n);
+    xhat &= M;
+    uint64_t p0 = party == 0 ? 1 : 0;
+    uint64_t mh = (xhat >> (n - 1)) & 1;
+    uint64_t xH = xhat >> s;
+    uint64_t two_ns = 1ULL << (n - s); /* n - s < 64 */
+    const uint64_t *w = k->w;
+    uint64_t q = 1 ^ mh ^ (uint64_t)c_hat;   /* public part of DReLU */
+    uint64_t a1 = 1 - 2 * q;                  /* 1 - 2q  (mod 2^n) */
+    uint64_t cl = (uint64_t)cl_hat;
+    uint64_t b1 = 1 - 2 * cl;                 /* 1 - 2*cL_hat */
+    uint64_t y = 0;
+    switch (kind) {
+    case GATE_RELU:
+        y = p0 * q * xhat + a1 * xhat * w[0] - q * w[1] - a1 * w[2] + w[3];
+        break;
+    case GATE_RELU_ARS:
+        y = p0 * (q * xH - q * cl) + w[0] * (a1 * xH - a1 * cl) - q * w[1] - a1 * w[2] - q * b1 * w[3] -
+            a1 * b1 * w[4] + two_ns * (1 - mh) * (q * w[5] + a1 * w[6]) + w[7];
+        break;
+    case GATE_ARS: {
+        uint64_t ch = (uint64_t)c_hat;
+        uint64_t pub = xH - cl + two_ns * (mh * ch - mh);
+        y = p0 * pub - w[0] - b1 * w[1] +
+            two_ns * (mh * (1 - 2 * ch) * w[2] + ((1 - 2 * mh) * ch + mh) * w[3] + (1 - 2 * mh) * (1 - 2 * ch) * w[4]) +
+            w[5];
+        break;
+    }
+    default:
+        y = p0 * (xH - cl) - w[0] - b1 * w[1] + two_ns * (1 - mh) * w[2] + w[3];
+        break;
+    }
+    return y & M;
+}
+
+/* ------------------------------------------------------------ DPF-LUT */
+
+typedef struct {
+    uint8_t root[16];
+    uint8_t cw[8][16];
+    uint8_t cwv[16];
+    uint64_t rout;
+} ref_lut_key;
+
+static int lut_epl(int n) { return 128 / n; }
+static int lut_lb(int n) { return n == 32 ? 2 : 1; }
+
+static uint64_t slot(const uint8_t b[16], int n, int k)
+{
+    uint64_t v = 0;
+    int bytes = n / 8;
+    for (int i = 0; i < bytes; i++) v |= (uint64_t)b[k * bytes + i] << (8 * i);
+    return v;
+}
+
+static void set_slot(uint8_t b[16], int n, int k, uint64_t v)
+{
+    int bytes = n / 8;
+    for (int i = 0; i < bytes; i++) b[k * bytes + i] = (uint8_t)(v >> (8 * i));
+}
+
+/* keys for the point function e_alpha over the 8-bit domain with payload 1 */
+void ref_lut_keygen(int n, uint64_t seed, uint32_t op, uint64_t i, uint64_t alpha, uint64_t r_out,
+                    ref_lut_key *k0, ref_lut_key *k1)
+{
+    if (!fixed_ready) fixed_init();
+    aes_ks ks;
+    ref_dealer_key(seed, &ks);
+    uint64_t M = nmask(n);
+    int lb = lut_lb(n), L = 8 - lb, epl = lut_epl(n);
+    uint8_t s0[16], delta[16], cur[2][16], h[2][16], blk[16];
+    memset(k0, 0, sizeof(*k0));
+    memset(k1, 0, sizeof(*k1));
+    alpha &= 255;
+    ref_prg(&ks, op, P_HI_S0, i, s0);
+    ref_prg(&ks, op, P_HI_DELTA, i, delta);
+    delta[0] |= 1;
+    memcpy(cur[0], s0, 16);
+    memcpy(cur[1], s0, 16);
+    xor16(cur[1], delta);
+    memcpy(k0->root, cur[0], 16);
+    memcpy(k1->root, cur[1], 16);
+    for (int j = 0; j < L; j++) {
+        int a = (int)((alpha >> (7 - j)) & 1);
+        ccr(&ks_h, cur[0], h[0]);
+        ccr(&ks_h, cur[1], h[1]);
+        for (int q = 0; q < 16; q++) k0->cw[j][q] = (uint8_t)(h[0][q] ^ h[1][q] ^ (a ? 0 : delta[q]));
+        for (int b = 0; b < 2; b++) {
+            int t = cur[b][0] & 1;
+            uint8_t cl[16];
+            for (int q = 0; q < 16; q++) cl[q] = (uint8_t)(h[b][q] ^ (t ? k0->cw[j][q] : 0));
+            if (a) xor16(cur[b], cl);
+            else memcpy(cur[b], cl, 16);
+        }
+    }
+    memcpy(k1->cw, k0->cw, sizeof(k0->cw));
+    int t0 = cur[0][0] & 1;
+    uint8_t g0[16], g1[16];
+    ccr(&ks_c, cur[0], g0);
+    ccr(&ks_c, cur[1], g1);
+    int alo = (int)(alpha & (uint64_t)(epl - 1));
+    for (int kk = 0; kk < epl; kk++) {
+        uint64_t want = kk == alo ? 1 : 0;
+        uint64_t v = (want - slot(g0, n, kk) + slot(g1, n, kk)) & M;
+        if (!t0) v = (0 - v) & M; /* t0 - t1 = -1 */
+        set_slot(k0->cwv, n, kk, v);
+    }
+    memcpy(k1->cwv, k0->cwv, 16);
+    ref_prg(&ks, op, P_SHARE, i, blk);
+    uint64_t a = ring_of(blk, n);
+    k0->rout = a;
+    k1->rout = (r_out - a) & M;
+}
+
+/* party's share of table[(xhat - alpha) mod 256] + r_out */
+uint64_t ref_lut_eval(int n, int party, uint64_t xhat, const uint64_t *table, const ref_lut_key *k)
+{
+    if (!fixed_ready) fixed_init();
+    uint64_t M = nmask(n);
+    int lb = lut_lb(n), L = 8 - lb, epl = lut_epl(n);
+    uint64_t acc = 0;
+    for (int p = 0; p < (1 << L); p++) {
+        uint8_t s[16], h[16], cl[16];
+        memcpy(s, k->root, 16);
+        for (int j = 0; j < L; j++) {
+            int xj = (p >> (L - 1 - j)) & 1;
+            int t = s[0] & 1;
+            ccr(&ks_h, s, h);
+            for (int q = 0; q < 16; q++) cl[q] = (uint8_t)(h[q] ^ (t ? k->cw[j][q] : 0));
+            if (xj) xor16(s, cl);
+            else memcpy(s, cl, 16);
+        }
+        int t = s[0] & 1;
+        uint8_t g[16];
+        ccr(&ks_c, s, g);
+        for (int kk = 0; kk < epl; kk++) {
+            uint64_t v = (slot(g, n, kk) + (t ? slot(k->cwv, n, kk) : 0)) & M;
+            if (party) v = (0 - v) & M;
+            uint64_t y = (uint64_t)(p * epl + kk);
+            acc += v * table[(xhat - y) & 255];
+        }
+    }
+    return (acc + k->rout) & M;
+}
+
+/* the public 8-bit degree table of secure_adj_norm.h:139-184 */
+void ref_invsqrt_table(int scale, int nmax, uint64_t *table)
+{
+    for (int d = 0; d < 256; d++) table[d] = 0;
+    double q = ldexp(1.0, scale);
+    for (int d = 1; d <= nmax && d < 256; d++) table[d] = (uint64_t)llround(q / sqrt((double)d));
+}

@@ -1,0 +1,192 @@
+"""ctypes view of oracle/fss_ref.c -- TEST INFRASTRUCTURE ONLY.
+
+Imported by tests/, by ``__graft_entry__.smoke()`` and by bench.py's
+cpu_baseline leg as the checker of the CUDA FSS kernels.  Nothing in the
+product package imports it.
+
+The C file restates, in plain byte-oriented C, this build's FSS scheme
+(AES-128, the half-tree DCF/DPF, the comparison gates and the 8-bit DPF
+look-up table); see the header of fss_ref.c for the published algorithms it
+follows and for the reference call sites it replaces
+(gpu_mpc/ddg_orca.h:83-123, gpu_mpc/secure_adj_norm.h:498-520).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "libfss_ref.so")
+
+GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS = 0, 1, 2, 3
+GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4}
+
+
+def build() -> str:
+    src = os.path.join(_HERE, "fss_ref.c")
+    if not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
+        subprocess.check_call(["make", "-s", "-C", _HERE, "libfss_ref.so"])
+    return _SO
+
+
+class GateKey(ctypes.Structure):
+    _fields_ = [
+        ("hi_root", ctypes.c_uint8 * 16),
+        ("hi_cw", (ctypes.c_uint8 * 16) * 56),
+        ("hi_leaf", ctypes.c_uint8 * 16),
+        ("hi_mu", ctypes.c_int32),
+        ("lo_root", ctypes.c_uint8 * 16),
+        ("lo_cw", (ctypes.c_uint8 * 16) * 56),
+        ("lo_leaf", ctypes.c_uint8 * 16),
+        ("lo_mu", ctypes.c_int32),
+        ("w", ctypes.c_uint64 * 8),
+    ]
+
+
+class LutKey(ctypes.Structure):
+    _fields_ = [
+        ("root", ctypes.c_uint8 * 16),
+        ("cw", (ctypes.c_uint8 * 16) * 8),
+        ("cwv", ctypes.c_uint8 * 16),
+        ("rout", ctypes.c_uint64),
+    ]
+
+
+class AesKs(ctypes.Structure):
+    _fields_ = [("rk", ctypes.c_uint8 * 176)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        L = ctypes.CDLL(build())
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        L.ref_aes128_expand.argtypes = [u8p, ctypes.POINTER(AesKs)]
+        L.ref_aes128_encrypt.argtypes = [ctypes.POINTER(AesKs), u8p, u8p]
+        L.ref_hash_h.argtypes = [u8p, u8p]
+        L.ref_hash_c.argtypes = [u8p, u8p]
+        L.ref_dealer_key.argtypes = [ctypes.c_uint64, ctypes.POINTER(AesKs)]
+        L.ref_prg.argtypes = [ctypes.POINTER(AesKs), ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, u8p]
+        L.ref_dcf_keygen.argtypes = [ctypes.c_int, ctypes.c_uint64, u8p, u8p, u8p, u8p, u8p, u8p]
+        L.ref_dcf_eval.argtypes = [ctypes.c_int, ctypes.c_uint64, u8p, u8p, u8p]
+        L.ref_dcf_eval.restype = ctypes.c_int
+        L.ref_gate_keygen.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32,
+                                      ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(GateKey),
+                                      ctypes.POINTER(GateKey)]
+        L.ref_gate_keygen.restype = ctypes.c_uint64
+        L.ref_gate_round1.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                      ctypes.POINTER(GateKey)]
+        L.ref_gate_round1.restype = ctypes.c_int
+        L.ref_gate_round2.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(GateKey)]
+        L.ref_gate_round2.restype = ctypes.c_uint64
+        L.ref_lut_keygen.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64,
+                                     ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(LutKey),
+                                     ctypes.POINTER(LutKey)]
+        L.ref_lut_eval.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
+                                   ctypes.POINTER(LutKey)]
+        L.ref_lut_eval.restype = ctypes.c_uint64
+        L.ref_invsqrt_table.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)]
+        _lib = L
+    return _lib
+
+
+def _buf(b: bytes):
+    return (ctypes.c_uint8 * len(b)).from_buffer_copy(b)
+
+
+def aes128(key: bytes, pt: bytes) -> bytes:
+    ks = AesKs()
+    lib().ref_aes128_expand(_buf(key), ctypes.byref(ks))
+    out = (ctypes.c_uint8 * 16)()
+    lib().ref_aes128_encrypt(ctypes.byref(ks), _buf(pt), out)
+    return bytes(out)
+
+
+def hash_h(x: bytes) -> bytes:
+    out = (ctypes.c_uint8 * 16)()
+    lib().ref_hash_h(_buf(x), out)
+    return bytes(out)
+
+
+def hash_c(x: bytes) -> bytes:
+    out = (ctypes.c_uint8 * 16)()
+    lib().ref_hash_c(_buf(x), out)
+    return bytes(out)
+
+
+def prg(seed: int, op: int, purpose: int, idx: int) -> bytes:
+    ks = AesKs()
+    lib().ref_dealer_key(seed, ctypes.byref(ks))
+    out = (ctypes.c_uint8 * 16)()
+    lib().ref_prg(ctypes.byref(ks), op, purpose, idx, out)
+    return bytes(out)
+
+
+def dcf_keygen(d: int, alpha: int, s0: bytes, delta: bytes):
+    L = max(d - 7, 0)
+    r0, r1 = (ctypes.c_uint8 * 16)(), (ctypes.c_uint8 * 16)()
+    cw = (ctypes.c_uint8 * (16 * max(L, 1)))()
+    leaf = (ctypes.c_uint8 * 16)()
+    lib().ref_dcf_keygen(d, alpha, _buf(s0), _buf(delta), r0, r1, cw, leaf)
+    return bytes(r0), bytes(r1), bytes(cw)[: 16 * L], bytes(leaf)
+
+
+def dcf_eval(d: int, x: int, root: bytes, cw: bytes, leaf: bytes) -> int:
+    return lib().ref_dcf_eval(d, x, _buf(root), _buf(cw if cw else b"\0" * 16), _buf(leaf))
+
+
+def gate_keygen(kind: int, n: int, s: int, seed: int, op: int, i: int, r_in: int):
+    k0, k1 = GateKey(), GateKey()
+    r_out = lib().ref_gate_keygen(kind, n, s, seed, op, i, r_in, ctypes.byref(k0), ctypes.byref(k1))
+    return k0, k1, r_out
+
+
+def gate_round1(kind: int, n: int, s: int, xhat: int, key: GateKey) -> int:
+    return lib().ref_gate_round1(kind, n, s, xhat, ctypes.byref(key))
+
+
+def gate_round2(kind: int, n: int, s: int, party: int, xhat: int, c_hat: int, cl_hat: int, key: GateKey) -> int:
+    return lib().ref_gate_round2(kind, n, s, party, xhat, c_hat, cl_hat, ctypes.byref(key))
+
+
+def gate_eval_pair(kind: int, n: int, s: int, xhat: int, k0: GateKey, k1: GateKey) -> int:
+    """Both parties, both rounds, with the openings done in place: returns y_hat."""
+    b0 = gate_round1(kind, n, s, xhat, k0)
+    b1 = gate_round1(kind, n, s, xhat, k1)
+    o = b0 ^ b1
+    y0 = gate_round2(kind, n, s, 0, xhat, o & 1, (o >> 1) & 1, k0)
+    y1 = gate_round2(kind, n, s, 1, xhat, o & 1, (o >> 1) & 1, k1)
+    return (y0 + y1) & ((1 << n) - 1)
+
+
+def lut_keygen(n: int, seed: int, op: int, i: int, alpha: int, r_out: int):
+    k0, k1 = LutKey(), LutKey()
+    lib().ref_lut_keygen(n, seed, op, i, alpha, r_out, ctypes.byref(k0), ctypes.byref(k1))
+    return k0, k1
+
+
+def lut_eval(n: int, party: int, xhat: int, table, key: LutKey) -> int:
+    t = (ctypes.c_uint64 * 256)(*[int(v) for v in table])
+    return lib().ref_lut_eval(n, party, xhat, t, ctypes.byref(key))
+
+
+def invsqrt_table(scale: int, nmax: int) -> np.ndarray:
+    t = (ctypes.c_uint64 * 256)()
+    lib().ref_invsqrt_table(scale, nmax, t)
+    return np.array(list(t), dtype=np.uint64)
+
+
+def gate_key_bytes(key: GateKey) -> dict:
+    """Flatten one element's key into the SoA fields the CUDA layout stores."""
+    return {
+        "hi_root": bytes(key.hi_root), "hi_cw": bytes(key.hi_cw), "hi_leaf": bytes(key.hi_leaf),
+        "hi_mu": key.hi_mu, "lo_root": bytes(key.lo_root), "lo_cw": bytes(key.lo_cw),
+        "lo_leaf": bytes(key.lo_leaf), "lo_mu": key.lo_mu, "w": list(key.w),
+    }

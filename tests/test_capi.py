@@ -1,0 +1,33 @@
+"""The C-ABI library loads and exports every function include/ddg_fss.h declares (no GPU needed)."""
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(REPO, "include", "ddg_fss.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ddg_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_functions():
+    assert "ddg_gate_round1" in declared_functions()
+
+
+def test_library_exports_every_declared_symbol(ddg):
+    L = ddg.lib()
+    missing = [f for f in declared_functions() if not hasattr(L, f)]
+    assert not missing, missing
+    assert set(declared_functions()) <= set(ddg.SIGNATURES), "python signature table incomplete"
+
+
+def test_argument_errors_are_status_codes(ddg):
+    with pytest.raises(ddg.DdgError) as e:
+        ddg.gate_round1(9, 32, 12, 10, None, None, None, None)
+    assert e.value.code == 1
+    with pytest.raises(ddg.DdgError):
+        ddg.gate_round2(0, 48, 12, 10, 0, None, None, None, None, None, None, None)
+    assert ddg.gate_key_bytes(0, 32, 12, 1000) > 1000 * 400
