@@ -45,6 +45,20 @@ SIGNATURES = {
     "ddg_gate_round1": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round2": (_i32, [_i32, _i32, _i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_aes_chain": (_i32, [_u64, _i32, _vp, _vp]),
+    "ddg_party_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32]),
+    "ddg_party_destroy": (_i32, [_vp]),
+    "ddg_party_set_weights": (_i32, [_vp, _vp, _u64]),
+    "ddg_party_bind_keys": (_i32, [_vp, _vp, _u64]),
+    "ddg_party_stream": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "ddg_party_stats": (_i32, [_vp, ctypes.POINTER(_u64)]),
+    "ddg_pair_local": (_i32, [_vp, _vp]),
+    "ddg_nccl_unique_id": (_i32, [_vp]),
+    "ddg_party_connect_nccl": (_i32, [_vp, _vp, _i32, _i32, _i32]),
+    "ddg_party_set_timeout": (_i32, [_vp, _i32]),
+    "ddg_forward_key_bytes": (_u64, [_i32, _i32, _i32]),
+    "ddg_forward_eval": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
+    "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
+    "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
 }
 
 
@@ -94,3 +108,104 @@ def gate_round2(kind, bw, scale, n, party, d_xhat, d_hi_own, d_hi_peer, d_lo_own
                 stream=None):
     check(lib().ddg_gate_round2(kind, bw, scale, n, party, d_xhat, d_hi_own, d_hi_peer, d_lo_own, d_lo_peer, d_key,
                                 d_share, stream))
+
+
+# ---------------------------------------------------------------- parties
+
+def forward_key_bytes(bw: int, scale: int, batch: int) -> int:
+    return int(lib().ddg_forward_key_bytes(bw, scale, batch))
+
+
+def dealer_forward(bw, scale, batch, seed, weights_blob, device, d_key0, d_key1, stream=None):
+    """GPU dealer: both parties' keys for one forward of `batch` samples.
+    `weights_blob` is the int64 weights.bin content (numpy array)."""
+    import numpy as np
+
+    blob = np.ascontiguousarray(weights_blob, dtype=np.int64)
+    check(lib().ddg_dealer_forward(bw, scale, batch, seed, blob.ctypes.data, blob.size, device, d_key0, d_key1,
+                                   stream))
+
+
+class Party:
+    """One evaluator (party 0 or 1) of the online phase: mirrors the reference's
+    DDGOrcaBatched backend object (gpu_mpc/ddg_orca_batched.h:87-206) plus its
+    GpuPeer.  Keys are a device region bound with bind_keys(); weights are the
+    int64 weights.bin blob."""
+
+    def __init__(self, party: int, bw: int, scale: int = 12, device: int = 0):
+        h = _vp()
+        check(lib().ddg_party_create(ctypes.byref(h), party, bw, scale, device))
+        self.h, self.party, self.bw, self.scale, self.device = h, party, bw, scale, device
+
+    def close(self):
+        if self.h:
+            lib().ddg_party_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_weights(self, blob):
+        import numpy as np
+
+        b = np.ascontiguousarray(blob, dtype=np.int64)
+        check(lib().ddg_party_set_weights(self.h, b.ctypes.data, b.size))
+
+    def bind_keys(self, d_ptr: int, nbytes: int):
+        check(lib().ddg_party_bind_keys(self.h, d_ptr, nbytes))
+
+    @property
+    def stream(self) -> int:
+        s = _vp()
+        check(lib().ddg_party_stream(self.h, ctypes.byref(s)))
+        return s.value or 0
+
+    def stats(self) -> dict:
+        out = (_u64 * 3)()
+        check(lib().ddg_party_stats(self.h, out))
+        return {"bytes_sent": int(out[0]), "rounds": int(out[1]), "key_bytes_used": int(out[2])}
+
+    def connect_nccl(self, unique_id: bytes, nranks: int, rank: int, peer_rank: int):
+        buf = ctypes.create_string_buffer(bytes(unique_id), 128)
+        check(lib().ddg_party_connect_nccl(self.h, buf, nranks, rank, peer_rank))
+
+    def set_timeout(self, ms: int):
+        check(lib().ddg_party_set_timeout(self.h, ms))
+
+    def forward(self, batch, x, adj, mask, prot, on_host=False):
+        """One online forward.  x/adj/mask/prot: this party's shares (device
+        pointers, or host pointers with on_host=True).  Returns (raw ring
+        outputs as int64, affinities) on party 0, (None, None) on party 1."""
+        import numpy as np
+
+        raw = np.zeros(batch, dtype=np.int64)
+        aff = np.zeros(batch, dtype=np.float64)
+        check(lib().ddg_forward_eval(self.h, batch, x, adj, mask, prot, int(on_host), raw.ctypes.data,
+                                     aff.ctypes.data))
+        return (raw, aff) if self.party == 0 else (None, None)
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    check(lib().ddg_nccl_unique_id(buf))
+    return buf.raw
+
+
+def pair_local(p0: Party, p1: Party):
+    check(lib().ddg_pair_local(p0.h, p1.h))
+
+
+def forward_pair(p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
+    """Both parties of an in-process pair, each on its own host thread.
+    inputs0/1: (x, adj, mask, protein) share pointers. Returns (raw, affinity)."""
+    import numpy as np
+
+    a0 = (_vp * 4)(*inputs0)
+    a1 = (_vp * 4)(*inputs1)
+    raw = np.zeros(batch, dtype=np.int64)
+    aff = np.zeros(batch, dtype=np.float64)
+    check(lib().ddg_forward_eval_pair(p0.h, p1.h, batch, a0, a1, int(on_host), raw.ctypes.data, aff.ctypes.data))
+    return raw, aff

@@ -1,5 +1,10 @@
 // extern "C" entry points of libddg.so (declared in include/ddg_fss.h).
+#include <string>
+#include <thread>
+
 #include "aes_dev.cuh"
+#include "channel.cuh"
+#include "forward.cuh"
 #include "gates.cuh"
 
 using namespace ddg;
@@ -73,6 +78,168 @@ int ddg_aes_chain(uint64_t threads, int iters, uint32_t *d_out, void *stream)
 {
     DDG_CHECK(threads > 0 && iters > 0 && d_out, DDG_ERR_ARG, "bad aes_chain arguments");
     return aes_chain(threads, iters, d_out, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------ parties
+
+struct ddg_party {
+    ddg::Party P;
+};
+
+int ddg_party_create(ddg_party **out, int party, int bw, int scale, int device)
+{
+    DDG_CHECK(out, DDG_ERR_ARG, "null out");
+    DDG_CHECK(party == 0 || party == 1, DDG_ERR_ARG, "party must be 0 or 1");
+    DDG_TRY(check_gate_args(0, bw, scale));
+    DDG_CUDA(cudaSetDevice(device));
+    auto *h = new ddg_party();
+    h->P.party = party, h->P.bw = bw, h->P.s = scale, h->P.device = device;
+    cudaError_t e = cudaStreamCreateWithFlags(&h->P.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete h;
+        set_last_error("cudaStreamCreate: %s", cudaGetErrorString(e));
+        return DDG_ERR_CUDA;
+    }
+    *out = h;
+    return DDG_OK;
+}
+
+int ddg_party_destroy(ddg_party *h)
+{
+    if (!h) return DDG_OK;
+    cudaSetDevice(h->P.device);
+    cudaStreamSynchronize(h->P.stream);
+    h->P.w.release();
+    for (int i = 0; i < 4; i++)
+        if (h->P.in_buf[i]) cudaFree(h->P.in_buf[i]);
+    if (h->P.owns_chan) delete h->P.chan;
+    cudaStreamDestroy(h->P.stream);
+    delete h;
+    return DDG_OK;
+}
+
+int ddg_party_set_weights(ddg_party *h, const int64_t *h_blob, uint64_t n)
+{
+    DDG_CHECK(h && h_blob, DDG_ERR_ARG, "null argument");
+    return h->P.w.load(h_blob, n, h->P.bw, h->P.s, h->P.device);
+}
+
+int ddg_party_bind_keys(ddg_party *h, const void *d_keys, uint64_t bytes)
+{
+    DDG_CHECK(h && d_keys, DDG_ERR_ARG, "null argument");
+    h->P.keys = static_cast<const uint8_t *>(d_keys);
+    h->P.key_bytes = bytes;
+    return DDG_OK;
+}
+
+int ddg_party_stream(ddg_party *h, void **stream)
+{
+    DDG_CHECK(h && stream, DDG_ERR_ARG, "null argument");
+    *stream = h->P.stream;
+    return DDG_OK;
+}
+
+int ddg_party_stats(ddg_party *h, uint64_t *out3)
+{
+    DDG_CHECK(h && out3, DDG_ERR_ARG, "null argument");
+    out3[0] = h->P.stats.bytes_sent;
+    out3[1] = h->P.stats.rounds;
+    out3[2] = h->P.stats.key_bytes_used;
+    return DDG_OK;
+}
+
+int ddg_pair_local(ddg_party *p0, ddg_party *p1)
+{
+    DDG_CHECK(p0 && p1 && p0 != p1, DDG_ERR_ARG, "need two distinct parties");
+    DDG_CHECK(p0->P.party == 0 && p1->P.party == 1, DDG_ERR_ARG, "pair (party 0, party 1) in that order");
+    DDG_CHECK(p0->P.bw == p1->P.bw && p0->P.s == p1->P.s, DDG_ERR_ARG, "parties disagree on bw/scale");
+    if (p0->P.device != p1->P.device) {
+        int can = 0;
+        DDG_CUDA(cudaDeviceCanAccessPeer(&can, p1->P.device, p0->P.device));
+        DDG_CHECK(can, DDG_ERR_ARG, "devices %d and %d have no peer access", p0->P.device, p1->P.device);
+    }
+    auto *c = new LocalPairChannel(p0->P.device, p1->P.device);
+    p0->P.chan = c, p1->P.chan = c;
+    p0->P.owns_chan = true, p1->P.owns_chan = false;
+    return DDG_OK;
+}
+
+int ddg_nccl_unique_id(void *out128)
+{
+    DDG_CHECK(out128, DDG_ERR_ARG, "null out");
+    return nccl_unique_id(out128);
+}
+
+int ddg_party_connect_nccl(ddg_party *h, const void *id128, int nranks, int rank, int peer_rank)
+{
+    DDG_CHECK(h && id128, DDG_ERR_ARG, "null argument");
+    int st = DDG_OK;
+    Channel *c = make_nccl_channel(id128, nranks, rank, peer_rank, h->P.device, &st);
+    DDG_TRY(st);
+    if (h->P.owns_chan) delete h->P.chan;
+    h->P.chan = c, h->P.owns_chan = true;
+    return DDG_OK;
+}
+
+int ddg_party_set_timeout(ddg_party *h, int timeout_ms)
+{
+    DDG_CHECK(h && h->P.chan && timeout_ms > 0, DDG_ERR_ARG, "bad timeout or no channel");
+    h->P.chan->timeout_ms = timeout_ms;
+    return DDG_OK;
+}
+
+uint64_t ddg_forward_key_bytes(int bw, int scale, int batch)
+{
+    if (check_gate_args(0, bw, scale) != DDG_OK || batch <= 0) return 0;
+    return forward_key_bytes(bw, scale, batch);
+}
+
+int ddg_forward_eval(ddg_party *h, int batch, const void *x_share, const void *adj_share, const void *mask_share,
+                     const void *protein_share, int on_host, int64_t *h_out_raw, double *h_affinity)
+{
+    DDG_CHECK(h && batch > 0 && x_share && adj_share && mask_share && protein_share, DDG_ERR_ARG, "bad argument");
+    DDG_CHECK(h->P.key_bytes >= forward_key_bytes(h->P.bw, h->P.s, batch), DDG_ERR_KEY,
+              "bound key region (%llu B) smaller than one forward of batch %d",
+              (unsigned long long)h->P.key_bytes, batch);
+    return forward_eval(h->P, batch, x_share, adj_share, mask_share, protein_share, on_host != 0, h_out_raw,
+                        h_affinity);
+}
+
+int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
+                          int on_host, int64_t *h_out_raw, double *h_affinity)
+{
+    DDG_CHECK(p0 && p1 && in0 && in1, DDG_ERR_ARG, "null argument");
+    int st1 = DDG_OK;
+    std::string err1;
+    std::thread t([&] {
+        st1 = ddg_forward_eval(p1, batch, in1[0], in1[1], in1[2], in1[3], on_host, nullptr, nullptr);
+        if (st1 != DDG_OK) err1 = ddg::last_error();
+    });
+    int st0 = ddg_forward_eval(p0, batch, in0[0], in0[1], in0[2], in0[3], on_host, h_out_raw, h_affinity);
+    if (st0 != DDG_OK) {
+        if (auto *lp = dynamic_cast<LocalPairChannel *>(p0->P.chan)) lp->fail();
+    }
+    t.join();
+    if (st0 == DDG_OK && st1 != DDG_OK) {
+        set_last_error("party 1: %s", err1.c_str());
+        return st1;
+    }
+    return st0;
+}
+
+int ddg_dealer_forward(int bw, int scale, int batch, uint64_t seed, const int64_t *h_weights, uint64_t n_weights,
+                       int device, void *d_key0, void *d_key1, void *stream)
+{
+    DDG_TRY(check_gate_args(0, bw, scale));
+    DDG_CHECK(batch > 0 && h_weights && d_key0 && d_key1, DDG_ERR_ARG, "bad argument");
+    DDG_CUDA(cudaSetDevice(device));
+    DevWeights w;
+    DDG_TRY(w.load(h_weights, n_weights, bw, scale, device));
+    int st = dealer_forward(bw, scale, batch, seed, w, static_cast<uint8_t *>(d_key0), static_cast<uint8_t *>(d_key1),
+                            static_cast<cudaStream_t>(stream));
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    w.release();
+    return st;
 }
 
 }  // extern "C"

@@ -1,0 +1,60 @@
+// Inter-party channels.  An opening sends this party's share and makes the
+// peer's share readable on this party's device; the caller adds (or XORs).
+// Replaces GpuPeer::reconstructInPlace (gpu_mpc/utils/gpu_comms.h:291-302;
+// sigma_comms.cpp:106-150: D2H -> TCP -> H2D per opening).
+//   LocalPairChannel: both parties in one process (two host threads).  Same
+//     device: zero-copy, the consumer reads the peer's buffer after waiting on
+//     the peer's event.  Different devices: cudaMemcpyPeerAsync over NVLink.
+//   NcclChannel: one party per process, grouped ncclSend/ncclRecv with the
+//     paired rank on the party's stream.
+#pragma once
+#include <condition_variable>
+#include <cstdint>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ddg {
+
+struct Channel {
+    virtual ~Channel() {}
+    // Send `bytes` at `send` (ready once work queued on `st` so far is done);
+    // on return *peer points at the peer's bytes, readable by work queued on
+    // `st` afterwards.  `recv` is a device buffer of `bytes` the channel may
+    // use for the copy.
+    virtual int exchange(int party, cudaStream_t st, const void *send, uint64_t bytes, void *recv,
+                         const void **peer) = 0;
+    // both parties reach this point; afterwards each party's stream has waited
+    // for all work the peer queued before it
+    virtual int barrier(int party, cudaStream_t st) = 0;
+    virtual bool same_device() const { return false; }
+    uint64_t bytes_sent[2] = {0, 0};
+    uint64_t rounds[2] = {0, 0};
+    int timeout_ms = 60000;
+};
+
+struct LocalPairChannel : Channel {
+    struct Slot {
+        const void *ptr = nullptr;
+        uint64_t bytes = 0;
+        uint64_t gen = 0;
+    };
+    std::mutex mu;
+    std::condition_variable cv;
+    Slot slot[2][2];        // [party][gen & 1]
+    uint64_t gen[2] = {0, 0};
+    cudaEvent_t ev[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+    int dev[2] = {0, 0};
+    bool broken = false;
+    LocalPairChannel(int dev0, int dev1);
+    ~LocalPairChannel() override;
+    int exchange(int party, cudaStream_t st, const void *send, uint64_t bytes, void *recv, const void **peer) override;
+    int barrier(int party, cudaStream_t st) override;
+    bool same_device() const override { return dev[0] == dev[1]; }
+    void fail();  // wake a waiting peer with an error (the other party gave up)
+};
+
+Channel *make_nccl_channel(const void *unique_id, int nranks, int rank, int peer_rank, int device, int *status);
+int nccl_unique_id(void *out128);
+
+}  // namespace ddg

@@ -1,0 +1,303 @@
+// Elementwise kernels of the online graph and of the dealer: openings,
+// Beaver products with row/column broadcast (secure_adj_norm.h:609-651 mul1 /
+// mul2, deepdtagen.h:198 mask multiply), the max-pool tree level data movement
+// (masked_maxpool_layer.h:72-126, fused into index arithmetic instead of
+// cudaMemcpy2D + per-pair copies), the per-row concat (deepdtagen.h:45-100),
+// degree row sums (secure_adj_norm.h:44-78) and the dealer's PRG fills.
+#include "aes_dev.cuh"
+#include "gates.cuh"
+#include "linear.cuh"
+
+namespace ddg {
+
+static int ew_grid(uint64_t n)
+{
+    static int sms = 0;
+    if (!sms) sms = device_sms();
+    uint64_t blocks = (n + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 16;
+    return int(blocks < cap ? (blocks ? blocks : 1) : cap);
+}
+
+#define GRID_STRIDE(i, n) \
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < (n); i += uint64_t(gridDim.x) * blockDim.x)
+
+template <typename T>
+__global__ void k_add(T *out, const T *a, const T *b, uint64_t n)
+{
+    GRID_STRIDE(i, n) out[i] = a[i] + b[i];
+}
+
+template <typename T>
+__global__ void k_sub(T *out, const T *a, const T *b, uint64_t n)
+{
+    GRID_STRIDE(i, n) out[i] = a[i] - b[i];
+}
+
+template <typename T>
+int ew_add(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st)
+{
+    if (!n) return DDG_OK;
+    k_add<T><<<ew_grid(n), 256, 0, st>>>(out, a, b, n);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+int ew_sub(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st)
+{
+    if (!n) return DDG_OK;
+    k_sub<T><<<ew_grid(n), 256, 0, st>>>(out, a, b, n);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+__device__ __forceinline__ uint64_t bc_index(uint64_t e, int bc, int R, int C)
+{
+    if (bc == BC_ROW) return e / uint64_t(C);                                   // (b*R + i)
+    if (bc == BC_COL) return (e / (uint64_t(R) * C)) * uint64_t(C) + e % uint64_t(C);  // (b*C + j)
+    return e;
+}
+
+template <typename T>
+__global__ void k_beaver(T p0, uint64_t n, int bc, int R, int C, const T *xh, const T *yh, const T *msx, const T *msy,
+                         const T *Z, T *out)
+{
+    GRID_STRIDE(e, n)
+    {
+        const uint64_t j = bc_index(e, bc, R, C);
+        const T x = xh[e], y = yh[j];
+        out[e] = p0 * x * y - x * msy[j] - msx[e] * y + Z[e];
+    }
+}
+
+template <typename T>
+int beaver_ew(int party, const EwShape &sh, Bcast bc, const T *xh, const T *yh, const T *msx, const T *msy, const T *Z,
+              T *out, cudaStream_t st)
+{
+    if (!sh.n) return DDG_OK;
+    k_beaver<T><<<ew_grid(sh.n), 256, 0, st>>>(party == 0 ? T(1) : T(0), sh.n, int(bc), sh.R, sh.C, xh, yh, msx, msy,
+                                               Z, out);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+__global__ void k_beaver_z(uint64_t n, int bc, int R, int C, const T *rx, const T *ry, const T *rout, T *Z)
+{
+    GRID_STRIDE(e, n) Z[e] = rx[e] * ry[bc_index(e, bc, R, C)] + rout[e];
+}
+
+template <typename T>
+int beaver_ew_z(const EwShape &sh, Bcast bc, const T *rx, const T *ry, const T *rout, T *Z, cudaStream_t st)
+{
+    if (!sh.n) return DDG_OK;
+    k_beaver_z<T><<<ew_grid(sh.n), 256, 0, st>>>(sh.n, int(bc), sh.R, sh.C, rx, ry, rout, Z);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+// one warp per row: lanes stride over the columns, shuffle reduction
+template <typename T>
+__global__ void k_rowsum(const T *a, const T *m, T *out, uint64_t rows, int cols)
+{
+    const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+    for (uint64_t r = warp; r < rows; r += nwarps) {
+        T s = 0;
+        for (int j = lane; j < cols; j += 32) s += a[r * cols + j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if (lane == 0) out[r] = s + (m ? m[r] : T(0));
+    }
+}
+
+template <typename T>
+int rowsum_plus(const T *a, const T *m, T *out, uint64_t rows, int cols, cudaStream_t st)
+{
+    if (!rows) return DDG_OK;
+    k_rowsum<T><<<ew_grid(rows * 32), 256, 0, st>>>(a, m, out, rows, cols);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+__global__ void k_pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F)
+{
+    const int pairs = cnt / 2;
+    const uint64_t n = uint64_t(B) * pairs * F;
+    GRID_STRIDE(e, n)
+    {
+        const int f = int(e % F);
+        const uint64_t bp = e / F;
+        const int p = int(bp % pairs);
+        const uint64_t b = bp / pairs;
+        const uint64_t base = (b * cnt + 2 * p) * uint64_t(F) + f;
+        const T ev = cur[base], od = cur[base + F];
+        even[e] = ev;
+        diff[e] = od - ev;
+    }
+}
+
+template <typename T>
+int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st)
+{
+    const uint64_t n = uint64_t(B) * (cnt / 2) * F;
+    if (!n) return DDG_OK;
+    k_pool_split<T><<<ew_grid(n), 256, 0, st>>>(cur, even, diff, B, cnt, F);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+__global__ void k_pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F)
+{
+    const int pairs = cnt / 2, nxt = pairs + (cnt & 1);
+    const uint64_t n = uint64_t(B) * nxt * F;
+    GRID_STRIDE(e, n)
+    {
+        const int f = int(e % F);
+        const uint64_t bq = e / F;
+        const int q = int(bq % nxt);
+        const uint64_t b = bq / nxt;
+        T v;
+        if (q < pairs) {
+            const uint64_t s = (b * pairs + q) * uint64_t(F) + f;
+            v = even[s] + relu[s];
+        } else {
+            v = cur[(b * cnt + (cnt - 1)) * uint64_t(F) + f];
+        }
+        next[e] = v;
+    }
+}
+
+template <typename T>
+int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F, cudaStream_t st)
+{
+    const uint64_t n = uint64_t(B) * (cnt / 2 + (cnt & 1)) * F;
+    if (!n) return DDG_OK;
+    k_pool_merge<T><<<ew_grid(n), 256, 0, st>>>(even, relu, cur, next, B, cnt, F);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+__global__ void k_concat(const T *a, const T *b, T *out, int B, int wa, int wb)
+{
+    const int w = wa + wb;
+    const uint64_t n = uint64_t(B) * w;
+    GRID_STRIDE(e, n)
+    {
+        const uint64_t r = e / w;
+        const int c = int(e % w);
+        out[e] = c < wa ? a[r * wa + c] : (b ? b[r * wb + (c - wa)] : T(0));
+    }
+}
+
+template <typename T>
+int concat_rows(const T *a, const T *b, T *out, int B, int wa, int wb, cudaStream_t st)
+{
+    const uint64_t n = uint64_t(B) * (wa + wb);
+    if (!n) return DDG_OK;
+    k_concat<T><<<ew_grid(n), 256, 0, st>>>(a, b, out, B, wa, wb);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+__global__ void k_unmask_ars(const T *xh, const T *r, T *out, uint64_t n, int s)
+{
+    using S = typename std::conditional<sizeof(T) == 4, int32_t, int64_t>::type;
+    GRID_STRIDE(i, n) out[i] = T(S(T(xh[i] - r[i])) >> s);
+}
+
+template <typename T>
+int unmask_ars(const T *xh, const T *r, T *out, uint64_t n, int s, cudaStream_t st)
+{
+    if (!n) return DDG_OK;
+    k_unmask_ars<T><<<ew_grid(n), 256, 0, st>>>(xh, r, out, n, s);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+__global__ void k_i64_to_ring(const int64_t *in, T *out, uint64_t n, int shl)
+{
+    GRID_STRIDE(i, n) out[i] = T(uint64_t(in[i]) << shl);
+}
+
+template <typename T>
+int i64_to_ring(const int64_t *in, T *out, uint64_t n, int shl, cudaStream_t st)
+{
+    if (!n) return DDG_OK;
+    k_i64_to_ring<T><<<ew_grid(n), 256, 0, st>>>(in, out, n, shl);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+// ------------------------------------------------------------ dealer PRG
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_prg_split(const T *v, uint64_t n, const __grid_constant__ AesKey dk, uint32_t op,
+                                                   uint32_t purpose, T *s0, T *s1)
+{
+    extern __shared__ uint32_t smem_tab[];
+    aes_stage_tables(smem_tab);
+    __syncthreads();
+    AesLane A(smem_tab);
+    GRID_STRIDE(i, n)
+    {
+        Blk b = A.prg(dk.rk, op, purpose, i);
+        T r;
+        if constexpr (sizeof(T) == 4) r = b.w[0];
+        else r = uint64_t(b.w[0]) | (uint64_t(b.w[1]) << 32);
+        if (s0) s0[i] = r;
+        if (s1) s1[i] = (v ? v[i] : T(0)) - r;
+    }
+}
+
+template <typename T>
+static int prg_launch(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uint32_t purpose, T *s0, T *s1,
+                      cudaStream_t st)
+{
+    if (!n) return DDG_OK;
+    DDG_TRY(aes_device_init());
+    DDG_CUDA(cudaFuncSetAttribute(k_prg_split<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
+    static int sms = 0;
+    if (!sms) sms = device_sms();
+    uint64_t blocks = (n + 255) / 256, cap = uint64_t(sms) * 3;
+    k_prg_split<T><<<int(blocks < cap ? blocks : cap), 256, AES_SMEM_BYTES, st>>>(v, n, dk, op, purpose, s0, s1);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+int prg_fill(T *out, uint64_t n, const AesKey &dk, uint32_t op, uint32_t purpose, cudaStream_t st)
+{
+    return prg_launch<T>(nullptr, n, dk, op, purpose, out, nullptr, st);
+}
+
+template <typename T>
+int split_shares(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uint32_t purpose, T *s0, T *s1, cudaStream_t st)
+{
+    return prg_launch<T>(v, n, dk, op, purpose, s0, s1, st);
+}
+
+#define INST(T)                                                                                                  \
+    template int ew_add<T>(T *, const T *, const T *, uint64_t, cudaStream_t);                                   \
+    template int ew_sub<T>(T *, const T *, const T *, uint64_t, cudaStream_t);                                   \
+    template int beaver_ew<T>(int, const EwShape &, Bcast, const T *, const T *, const T *, const T *, const T *, \
+                              T *, cudaStream_t);                                                                \
+    template int beaver_ew_z<T>(const EwShape &, Bcast, const T *, const T *, const T *, T *, cudaStream_t);     \
+    template int rowsum_plus<T>(const T *, const T *, T *, uint64_t, int, cudaStream_t);                         \
+    template int pool_split<T>(const T *, T *, T *, int, int, int, cudaStream_t);                                \
+    template int pool_merge<T>(const T *, const T *, const T *, T *, int, int, int, cudaStream_t);               \
+    template int concat_rows<T>(const T *, const T *, T *, int, int, int, cudaStream_t);                         \
+    template int unmask_ars<T>(const T *, const T *, T *, uint64_t, int, cudaStream_t);                          \
+    template int i64_to_ring<T>(const int64_t *, T *, uint64_t, int, cudaStream_t);                              \
+    template int prg_fill<T>(T *, uint64_t, const AesKey &, uint32_t, uint32_t, cudaStream_t);                   \
+    template int split_shares<T>(const T *, uint64_t, const AesKey &, uint32_t, uint32_t, T *, T *, cudaStream_t);
+INST(uint32_t)
+INST(uint64_t)
+
+}  // namespace ddg

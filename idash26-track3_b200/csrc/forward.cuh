@@ -1,0 +1,61 @@
+// The affinity-branch graph and the party / dealer contexts that walk it.
+#pragma once
+#include <vector>
+
+#include "channel.cuh"
+#include "common.cuh"
+
+namespace ddg {
+
+constexpr int NMAX = 138, FEAT = 94, POOL = 376, PROT = 128;
+constexpr int NLAYERS = 9;
+// (in, out) per layer, forward order: gcn 0-2, drug fc 3-4, fusion 5-8
+// (reference gpu_mpc/deepdtagen_inference.cu:113-123)
+constexpr int LAYER_IN[NLAYERS] = {94, 188, 282, 376, 1024, 256, 1024, 512, 256};
+constexpr int LAYER_OUT[NLAYERS] = {188, 282, 376, 1024, 128, 1024, 512, 256, 1};
+
+inline uint64_t weights_elems()
+{
+    uint64_t n = 0;
+    for (int l = 0; l < NLAYERS; l++) n += uint64_t(LAYER_IN[l]) * LAYER_OUT[l] + LAYER_OUT[l];
+    return n;
+}
+
+// device copy of the public weights as ring elements: W (in,out) and b << s
+struct DevWeights {
+    int bw = 0, s = 0, device = -1;
+    void *W[NLAYERS] = {};
+    void *b2s[NLAYERS] = {};
+    void *table = nullptr;  // 256-entry inverse-sqrt degree table
+    int load(const int64_t *h_blob, uint64_t n, int bw_, int s_, int device_);
+    void release();
+};
+
+// per-forward statistics of one party
+struct PartyStats {
+    uint64_t bytes_sent = 0, rounds = 0, key_bytes_used = 0;
+    double ms_total = 0;
+};
+
+struct Party {
+    int party = 0, bw = 32, s = 12, device = 0;
+    cudaStream_t stream = nullptr;
+    Channel *chan = nullptr;
+    bool owns_chan = false;
+    const uint8_t *keys = nullptr;
+    uint64_t key_bytes = 0;
+    DevWeights w;
+    PartyStats stats;
+    // device staging of host inputs (kept across forwards)
+    void *in_buf[4] = {};
+    uint64_t in_cap[4] = {};
+    int ensure_input(int which, uint64_t bytes);
+};
+
+uint64_t forward_key_bytes(int bw, int s, int B);
+int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
+                 bool on_host, int64_t *h_out_raw, double *h_aff);
+int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uint8_t *k0, uint8_t *k1,
+                   cudaStream_t st);
+
+}  // namespace ddg

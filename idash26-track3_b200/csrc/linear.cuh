@@ -1,0 +1,97 @@
+// Linear / elementwise building blocks of the online graph and the dealer.
+#pragma once
+#include "aes_dev.cuh"
+#include "common.cuh"
+
+namespace ddg {
+
+template <typename T>
+struct GemmArgs {
+    int M = 0, N = 0, K = 0, batch = 1;
+    const T *A1 = nullptr, *B1 = nullptr, *B1m = nullptr;
+    int64_t lda1 = 0, ldb1 = 0, sA1 = 0, sB1 = 0, sB1m = 0;
+    T s1 = 1;
+    const T *A2 = nullptr, *B2 = nullptr;
+    int64_t lda2 = 0, ldb2 = 0, sA2 = 0, sB2 = 0;
+    T sign = 1;
+    const T *bias = nullptr;
+    const T *Add = nullptr;
+    int64_t ldAdd = 0, sAdd = 0;
+    T *C = nullptr;
+    int64_t ldc = 0, sC = 0;
+};
+
+template <typename T>
+int ring_gemm(const GemmArgs<T> &a, cudaStream_t st);
+
+// broadcast pattern of the second operand of an elementwise product over
+// (B, R, C) = (batch, rows, cols):  none (same shape), row (index b*R + i),
+// col (index b*C + j)
+enum Bcast { BC_NONE = 0, BC_ROW = 1, BC_COL = 2 };
+
+struct EwShape {
+    uint64_t n = 0;     // elements of the output
+    int R = 1, C = 1;   // rows/cols for the broadcast patterns
+};
+
+template <typename T>
+int ew_add(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st);
+template <typename T>
+int ew_sub(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st);
+
+// party share of x*y: p0*xh*yh - xh*[r_y] - [r_x]*yh + Z
+template <typename T>
+int beaver_ew(int party, const EwShape &sh, Bcast bc, const T *xh, const T *yh, const T *msx, const T *msy, const T *Z,
+              T *out, cudaStream_t st);
+// dealer: Z = r_x * r_y + r_out
+template <typename T>
+int beaver_ew_z(const EwShape &sh, Bcast bc, const T *rx, const T *ry, const T *rout, T *Z, cudaStream_t st);
+
+// out[row] = sum_j a[row, j] + m[row]   (rows x cols)
+template <typename T>
+int rowsum_plus(const T *a, const T *m, T *out, uint64_t rows, int cols, cudaStream_t st);
+
+// max-pool tree level over cur (B, cnt, F): even[b,p,f] = cur[b,2p,f],
+// diff[b,p,f] = cur[b,2p+1,f] - cur[b,2p,f] for p < cnt/2
+template <typename T>
+int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st);
+// next[b,p,f] = even[b,p,f] + relu[b,p,f] (p < cnt/2), carried cur[b,cnt-1,f] if cnt odd
+template <typename T>
+int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F, cudaStream_t st);
+
+// out (B, wa+wb) = [a (B, wa) | b (B, wb)] per row
+template <typename T>
+int concat_rows(const T *a, const T *b, T *out, int B, int wa, int wb, cudaStream_t st);
+
+// out[i] = arithmetic shift of (xh[i] - r[i]) by s  (revealed output)
+template <typename T>
+int unmask_ars(const T *xh, const T *r, T *out, uint64_t n, int s, cudaStream_t st);
+
+// dealer randomness: out[i] = ring(AES_K(i || op || purpose))
+template <typename T>
+int prg_fill(T *out, uint64_t n, const AesKey &dk, uint32_t op, uint32_t purpose, cudaStream_t st);
+// dealer sharing: s0[i] = ring(AES_K(i || op || purpose)), s1 = v - s0 (either output may be null)
+template <typename T>
+int split_shares(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uint32_t purpose, T *s0, T *s1,
+                 cudaStream_t st);
+// widen an int64 host-layout array to ring elements, optionally shifted left
+template <typename T>
+int i64_to_ring(const int64_t *in, T *out, uint64_t n, int shl, cudaStream_t st);
+
+// ------------------------------------------------------------------ DPF LUT (lut.cu)
+
+// key layout of n lookups: root[n] 16 B | cw[L][n] 16 B | cwv[n] 16 B | rout share[n] words
+struct LutLayout {
+    int bw = 0, L = 0;
+    uint64_t n = 0, root = 0, cw = 0, cwv = 0, rout = 0, bytes = 0;
+};
+LutLayout lut_layout(int bw, uint64_t n, uint64_t base = 0);
+
+template <typename T>
+int lut_keygen(const LutLayout &L, const AesKey &dk, uint32_t op, const T *alpha_mask, const T *rout, uint8_t *k0,
+               uint8_t *k1, cudaStream_t st);
+template <typename T>
+int lut_eval(const LutLayout &L, int party, const T *xhat, const T *table, const uint8_t *key, T *share,
+             cudaStream_t st);
+
+}  // namespace ddg

@@ -1,0 +1,126 @@
+// Ring GEMMs over Z_2^32 / Z_2^64 on the CUDA cores (integer multiply-add
+// wraps modulo 2^bits natively).  One kernel serves every linear layer:
+//
+//   C[b] = sign * ( A1[b] . (s1*B1[b] - B1m[b])  -  A2[b] . B2[b] ) + bias + Add[b]
+//
+// * FC, secret x public weight (FC<T> behind DDGOrcaBase::matmul 4-arg,
+//   gpu_mpc/ddg_orca_base.h:208-271): party 0: A1 = x_hat, B1 = W, bias, Add =
+//   its key words; dealer: sign = -1, A1 = r_x, B1 = W, Add = r_y.
+// * Beaver, secret x secret per sample (DDGOrcaBase::matmul 3-arg,
+//   ddg_orca_base.h:170-205, batched loop of sytorch/layers/layers.h:67-90):
+//   A1 = A_hat, B1 = H_hat (s1 = 1 for party 0, 0 for party 1), B1m = [r_H],
+//   A2 = [r_A], B2 = H_hat, Add = [r_A r_H + r_P]; all B samples in one launch.
+// Tiles: 64x64 outputs per 256-thread CTA, 4x4 per thread, K step 16,
+// operands staged through shared memory.
+#include "common.cuh"
+#include "linear.cuh"
+
+namespace ddg {
+
+constexpr int GT = 64, GK = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256) ring_gemm_kernel(const __grid_constant__ GemmArgs<T> a)
+{
+    __shared__ T As[GK][GT + 1];
+    __shared__ T Bs[GK][GT];
+    const int b = blockIdx.z;
+    const int m0 = blockIdx.y * GT, n0 = blockIdx.x * GT;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    T acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0;
+
+    for (int phase = 0; phase < 2; phase++) {
+        const T *A = phase == 0 ? a.A1 : a.A2;
+        const T *B = phase == 0 ? a.B1 : a.B2;
+        if (A == nullptr) continue;
+        const T *Bm = phase == 0 ? a.B1m : nullptr;
+        const T s1 = phase == 0 ? a.s1 : T(1);
+        const int64_t lda = phase == 0 ? a.lda1 : a.lda2, ldb = phase == 0 ? a.ldb1 : a.ldb2;
+        A += int64_t(b) * (phase == 0 ? a.sA1 : a.sA2);
+        if (B) B += int64_t(b) * (phase == 0 ? a.sB1 : a.sB2);
+        if (Bm) Bm += int64_t(b) * a.sB1m;
+        T sub[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sub[i][j] = 0;
+        for (int k0 = 0; k0 < a.K; k0 += GK) {
+            // A tile GT x GK: 1024 elements, 4 per thread
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                int idx = threadIdx.x + q * 256;
+                int r = idx / GK, c = idx % GK;
+                int gm = m0 + r, gk = k0 + c;
+                As[c][r] = (gm < a.M && gk < a.K) ? A[int64_t(gm) * lda + gk] : T(0);
+            }
+            // B tile GK x GT
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                int idx = threadIdx.x + q * 256;
+                int r = idx / GT, c = idx % GT;
+                int gk = k0 + r, gn = n0 + c;
+                T v = 0;
+                if (gk < a.K && gn < a.N) {
+                    int64_t o = int64_t(gk) * ldb + gn;
+                    if (B) v = s1 * B[o];
+                    if (Bm) v -= Bm[o];
+                }
+                Bs[r][c] = v;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int kk = 0; kk < GK; kk++) {
+                T av[4], bv[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+                for (int j = 0; j < 4; j++) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) sub[i][j] += av[i] * bv[j];
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = phase == 0 ? sub[i][j] : acc[i][j] - sub[i][j];
+    }
+    const T *Add = a.Add ? a.Add + int64_t(b) * a.sAdd : nullptr;
+    T *C = a.C + int64_t(b) * a.sC;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int gm = m0 + ty * 4 + i;
+        if (gm >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int gn = n0 + tx * 4 + j;
+            if (gn >= a.N) continue;
+            T v = a.sign * acc[i][j];
+            if (a.bias) v += a.bias[gn];
+            if (Add) v += Add[int64_t(gm) * a.ldAdd + gn];
+            C[int64_t(gm) * a.ldc + gn] = v;
+        }
+    }
+}
+
+template <typename T>
+int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
+{
+    if (a.M == 0 || a.N == 0 || a.batch == 0) return DDG_OK;
+    dim3 grid((a.N + GT - 1) / GT, (a.M + GT - 1) / GT, a.batch);
+    DDG_CHECK(grid.y <= 65535 && grid.z <= 65535, DDG_ERR_ARG, "gemm grid too large (M=%d batch=%d)", a.M, a.batch);
+    ring_gemm_kernel<T><<<grid, 256, 0, st>>>(a);
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template int ring_gemm<uint32_t>(const GemmArgs<uint32_t> &, cudaStream_t);
+template int ring_gemm<uint64_t>(const GemmArgs<uint64_t> &, cudaStream_t);
+
+}  // namespace ddg

@@ -1,0 +1,116 @@
+"""End-to-end online forward (dealer + two parties on one GPU) against the oracle.
+
+The reference's integration gate (tests/test_mpc_online_gate.py:91-151) runs
+dealer + 2 evaluators and compares the revealed AFFINITY[i] with a plaintext
+model; here the two parties run as two host threads on cuda:0 with the GPU
+dealer's keys, and the revealed 2s->s outputs must equal
+oracle.ring_forward.protocol_forward bit for bit.
+"""
+import numpy as np
+import pytest
+
+from oracle import ring_forward as RF
+from tests.gpu_util import dev_bytes, ptr, to_dev
+
+S = 12
+
+
+def setup_pair(ddg, synth, bw, B, seed=123, wseed=5):
+    q = synth.quantize_weights(synth.affinity_weights(wseed), S)
+    blob = synth.weights_blob(q)
+    kb = ddg.forward_key_bytes(bw, S, B)
+    k0, k1 = dev_bytes(kb), dev_bytes(kb)
+    ddg.dealer_forward(bw, S, B, seed, blob, 0, ptr(k0), ptr(k1))
+    p0, p1 = ddg.Party(0, bw, S, 0), ddg.Party(1, bw, S, 0)
+    for p, k in ((p0, k0), (p1, k1)):
+        p.set_weights(blob)
+        p.bind_keys(ptr(k), kb)
+    ddg.pair_local(p0, p1)
+    return q, p0, p1, (k0, k1)
+
+
+def dev_inputs(inp):
+    keep = []
+    ins = []
+    for p in (0, 1):
+        arrs = [to_dev(np.asarray(inp.x_sh[p])), to_dev(np.asarray(inp.adj_sh[p])), to_dev(np.asarray(inp.mask_sh[p])),
+                to_dev(np.asarray(inp.protein_sh[p]))]
+        keep += arrs
+        ins.append([ptr(a) for a in arrs])
+    return ins, keep
+
+
+def expected(inp, q, bw):
+    return RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, S)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bw", [32, 64])
+def test_forward_bit_exact(ddg, synth, cuda, bw):
+    B = 3
+    inp = synth.Inputs(B, bw, seed=21, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B)
+    ins, keep = dev_inputs(inp)
+    raw, aff = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    want_raw, want_aff = expected(inp, q, bw)
+    assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)), (raw, want_raw)
+    assert np.array_equal(aff, want_aff)
+    st = p0.stats()
+    assert st["rounds"] > 50 and st["key_bytes_used"] <= ddg.forward_key_bytes(bw, S, B)
+
+
+@pytest.mark.gpu
+def test_forward_host_inputs_and_repeat(ddg, synth, cuda):
+    """Host (pinned or pageable) share buffers; keys re-used for a second forward
+    (timing-only key reuse, as the reference's benchmark loop rewinds keyBuf)."""
+    bw, B = 32, 4
+    inp = synth.Inputs(B, bw, seed=5, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=9)
+    host = []
+    for p in (0, 1):
+        arrs = [np.ascontiguousarray(inp.x_sh[p]), np.ascontiguousarray(inp.adj_sh[p]),
+                np.ascontiguousarray(inp.mask_sh[p]), np.ascontiguousarray(inp.protein_sh[p])]
+        host.append(arrs)
+    want_raw, want_aff = expected(inp, q, bw)
+    for _ in range(2):
+        raw, aff = ddg.forward_pair(p0, p1, B, [a.ctypes.data for a in host[0]], [a.ctypes.data for a in host[1]],
+                                    on_host=True)
+        assert np.array_equal(aff, want_aff)
+
+
+@pytest.mark.gpu
+def test_forward_edge_graphs(ddg, synth, cuda):
+    """kiba-shaped graphs (up to 100 atoms), a 138-atom graph, and an all-zero
+    padding sample (degree 0 -> table[0] = 0; deepdtagen_inference.cu:72-79)."""
+    bw, B = 64, 3
+    inp = synth.Inputs(B, bw, seed=8, atoms=(10, 100), with_protein_cnn=False)
+    rng = np.random.default_rng(1)
+    X, A, m = synth.gen_graph(rng, 138, 138)
+    inp.X_float[1], inp.A_raw[1], inp.mask[1] = X, A, m
+    inp.X_float[2] = 0
+    inp.A_raw[2] = 0
+    inp.mask[2] = 0
+    mask_tiled = np.broadcast_to(inp.mask[:, :, None], (B, 138, 376))
+    inp.x_ring = synth.to_ring(inp.X_float, S, bw)
+    inp.adj_ring = synth.to_ring(inp.A_raw, 0, bw)
+    inp.mask_ring = synth.to_ring(mask_tiled, S, bw)
+    inp.x_sh = synth.split_shares(inp.x_ring, 1, bw)
+    inp.adj_sh = synth.split_shares(inp.adj_ring, 2, bw)
+    inp.mask_sh = synth.split_shares(inp.mask_ring, 3, bw)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=77)
+    ins, keep = dev_inputs(inp)
+    raw, aff = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    want_raw, want_aff = expected(inp, q, bw)
+    assert np.array_equal(aff, want_aff)
+
+
+@pytest.mark.gpu
+def test_forward_rejects_short_key_region(ddg, synth, cuda):
+    bw, B = 32, 2
+    inp = synth.Inputs(B, bw, seed=3, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B)
+    p0.bind_keys(ptr(keep_k[0]), 1024)
+    ins, keep = dev_inputs(inp)
+    with pytest.raises(ddg.DdgError) as e:
+        ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    assert e.value.code == 3
