@@ -44,6 +44,12 @@ SIGNATURES = {
     "ddg_gate_keygen": (_i32, [_i32, _i32, _i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round1": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round2": (_i32, [_i32, _i32, _i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_lut_key_bytes": (_u64, [_i32, _u64]),
+    "ddg_lut_keygen": (_i32, [_i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_lut_eval": (_i32, [_i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_mul_share": (_i32, [_i32, _i32, _u64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_matmul_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_fc_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_aes_chain": (_i32, [_u64, _i32, _vp, _vp]),
     "ddg_party_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32]),
     "ddg_party_destroy": (_i32, [_vp]),
@@ -59,6 +65,9 @@ SIGNATURES = {
     "ddg_forward_eval": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
     "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
+    "ddg_launch_count": (_u64, []),
+    "ddg_party_enable_dcf_timing": (_i32, [_vp, _i32]),
+    "ddg_party_dcf_timing": (_i32, [_vp, ctypes.POINTER(ctypes.c_double)]),
 }
 
 
@@ -168,6 +177,15 @@ class Party:
         check(lib().ddg_party_stats(self.h, out))
         return {"bytes_sent": int(out[0]), "rounds": int(out[1]), "key_bytes_used": int(out[2])}
 
+    def enable_dcf_timing(self, on: bool = True):
+        check(lib().ddg_party_enable_dcf_timing(self.h, int(on)))
+
+    def dcf_timing(self) -> dict:
+        out = (ctypes.c_double * 6)()
+        check(lib().ddg_party_dcf_timing(self.h, out))
+        keys = ("launches", "bytes", "aes_blocks", "sum_ms", "union_ms", "pair_union_ms")
+        return dict(zip(keys, [float(v) for v in out]))
+
     def connect_nccl(self, unique_id: bytes, nranks: int, rank: int, peer_rank: int):
         buf = ctypes.create_string_buffer(bytes(unique_id), 128)
         check(lib().ddg_party_connect_nccl(self.h, buf, nranks, rank, peer_rank))
@@ -209,3 +227,7 @@ def forward_pair(p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
     aff = np.zeros(batch, dtype=np.float64)
     check(lib().ddg_forward_eval_pair(p0.h, p1.h, batch, a0, a1, int(on_host), raw.ctypes.data, aff.ctypes.data))
     return raw, aff
+
+
+def launch_count() -> int:
+    return int(lib().ddg_launch_count())

@@ -29,6 +29,7 @@ int aes_chain(uint64_t threads, int iters, uint32_t *out, cudaStream_t st)
     int sms = device_sms();
     uint64_t need = (threads + 255) / 256, full = uint64_t(sms) * 3;
     aes_chain_kernel<<<int(need < full ? need : full), 256, AES_SMEM_BYTES, st>>>(threads, iters, out);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }

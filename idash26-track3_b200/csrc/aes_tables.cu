@@ -1,5 +1,6 @@
 // Host-side AES-128 material (S-box from the GF(2^8) inverse and affine map,
 // the T0 table, FIPS-197 key expansion) and its per-device upload.
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -102,6 +103,16 @@ int aes_device_init()
     done[dev] = 1;
     return DDG_OK;
 }
+
+// ----------------------------------------------------------------- counters
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(); }
+
+static thread_local DcfTiming *t_dcf_sink = nullptr;
+DcfTiming *dcf_timing_sink() { return t_dcf_sink; }
+void set_dcf_timing_sink(DcfTiming *t) { t_dcf_sink = t; }
 
 // ----------------------------------------------------------------- errors
 

@@ -224,8 +224,28 @@ int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *c
         set_last_error("party 1: %s", err1.c_str());
         return st1;
     }
+    if (st0 == DDG_OK) st0 = pair_dcf_union(p0->P, p1->P);
     return st0;
 }
+
+int ddg_party_enable_dcf_timing(ddg_party *h, int on)
+{
+    DDG_CHECK(h, DDG_ERR_ARG, "null party");
+    h->P.timing.enabled = on != 0;
+    h->P.dcf = DcfAcc();
+    return DDG_OK;
+}
+
+int ddg_party_dcf_timing(ddg_party *h, double *out6)
+{
+    DDG_CHECK(h && out6, DDG_ERR_ARG, "null argument");
+    const DcfAcc &a = h->P.dcf;
+    double v[6] = {a.launches, a.bytes, a.aes, a.sum_ms, a.union_ms, a.pair_union_ms};
+    for (int i = 0; i < 6; i++) out6[i] = v[i];
+    return DDG_OK;
+}
+
+uint64_t ddg_launch_count(void) { return launch_count(); }
 
 int ddg_dealer_forward(int bw, int scale, int batch, uint64_t seed, const int64_t *h_weights, uint64_t n_weights,
                        int device, void *d_key0, void *d_key1, void *stream)

@@ -39,6 +39,26 @@ inline uint64_t align256(uint64_t x) { return (x + 255u) & ~uint64_t(255); }
 
 void set_last_error(const char *fmt, ...);
 
+// number of kernels this library launched (all devices, all threads)
+void note_launch();
+uint64_t launch_count();
+
+// Optional timing of the DCF (gate round-1) kernels: when a thread has a
+// sink installed, every round-1 launch is bracketed by CUDA events on its
+// stream together with its algorithmic bytes and AES blocks.
+struct DcfTiming {
+    struct Rec {
+        cudaEvent_t a, b;
+        double bytes, aes, evals;
+    };
+    cudaEvent_t ref = nullptr;  // recorded at forward start on the same stream
+    Rec recs[256];
+    int nrec = 0;
+    bool enabled = false;
+};
+DcfTiming *dcf_timing_sink();
+void set_dcf_timing_sink(DcfTiming *t);
+
 // ---------------------------------------------------------------- key layouts
 
 // gate kinds (the comparison-based nonlinear layers)

@@ -38,6 +38,7 @@ int ew_add(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st)
 {
     if (!n) return DDG_OK;
     k_add<T><<<ew_grid(n), 256, 0, st>>>(out, a, b, n);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -47,6 +48,7 @@ int ew_sub(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st)
 {
     if (!n) return DDG_OK;
     k_sub<T><<<ew_grid(n), 256, 0, st>>>(out, a, b, n);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -77,6 +79,7 @@ int beaver_ew(int party, const EwShape &sh, Bcast bc, const T *xh, const T *yh, 
     if (!sh.n) return DDG_OK;
     k_beaver<T><<<ew_grid(sh.n), 256, 0, st>>>(party == 0 ? T(1) : T(0), sh.n, int(bc), sh.R, sh.C, xh, yh, msx, msy,
                                                Z, out);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -92,6 +95,7 @@ int beaver_ew_z(const EwShape &sh, Bcast bc, const T *rx, const T *ry, const T *
 {
     if (!sh.n) return DDG_OK;
     k_beaver_z<T><<<ew_grid(sh.n), 256, 0, st>>>(sh.n, int(bc), sh.R, sh.C, rx, ry, rout, Z);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -117,6 +121,7 @@ int rowsum_plus(const T *a, const T *m, T *out, uint64_t rows, int cols, cudaStr
 {
     if (!rows) return DDG_OK;
     k_rowsum<T><<<ew_grid(rows * 32), 256, 0, st>>>(a, m, out, rows, cols);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -145,6 +150,7 @@ int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream
     const uint64_t n = uint64_t(B) * (cnt / 2) * F;
     if (!n) return DDG_OK;
     k_pool_split<T><<<ew_grid(n), 256, 0, st>>>(cur, even, diff, B, cnt, F);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -177,6 +183,7 @@ int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int c
     const uint64_t n = uint64_t(B) * (cnt / 2 + (cnt & 1)) * F;
     if (!n) return DDG_OK;
     k_pool_merge<T><<<ew_grid(n), 256, 0, st>>>(even, relu, cur, next, B, cnt, F);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -200,6 +207,7 @@ int concat_rows(const T *a, const T *b, T *out, int B, int wa, int wb, cudaStrea
     const uint64_t n = uint64_t(B) * (wa + wb);
     if (!n) return DDG_OK;
     k_concat<T><<<ew_grid(n), 256, 0, st>>>(a, b, out, B, wa, wb);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -216,6 +224,7 @@ int unmask_ars(const T *xh, const T *r, T *out, uint64_t n, int s, cudaStream_t 
 {
     if (!n) return DDG_OK;
     k_unmask_ars<T><<<ew_grid(n), 256, 0, st>>>(xh, r, out, n, s);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -231,6 +240,7 @@ int i64_to_ring(const int64_t *in, T *out, uint64_t n, int shl, cudaStream_t st)
 {
     if (!n) return DDG_OK;
     k_i64_to_ring<T><<<ew_grid(n), 256, 0, st>>>(in, out, n, shl);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -267,6 +277,7 @@ static int prg_launch(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uin
     if (!sms) sms = device_sms();
     uint64_t blocks = (n + 255) / 256, cap = uint64_t(sms) * 3;
     k_prg_split<T><<<int(blocks < cap ? blocks : cap), 256, AES_SMEM_BYTES, st>>>(v, n, dk, op, purpose, s0, s1);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }

@@ -8,6 +8,7 @@
 // key cursor of DDGOrcaBase / DDGOrcaBaseKeygen (ddg_orca_base.h:41-50,
 // 326-374): every op reads (eval) or writes (dealer) the next 256-byte aligned
 // key section.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -649,7 +650,15 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         }
     }
     const uint64_t sent0 = P.chan->bytes_sent[P.party], rounds0 = P.chan->rounds[P.party];
+    P.intervals.clear();
+    if (P.timing.enabled) {
+        if (!P.ref_event) DDG_CUDA(cudaEventCreate(&P.ref_event));
+        DDG_CUDA(cudaEventRecord(P.ref_event, P.stream));
+        P.timing.nrec = 0;
+        set_dcf_timing_sink(&P.timing);
+    }
     affinity_graph<T>(e);
+    set_dcf_timing_sink(nullptr);
     std::vector<T> h(B);
     if (e.err == DDG_OK)
         e.ok(cudaMemcpyAsync(h.data(), e.out, B * sizeof(T), cudaMemcpyDeviceToHost, P.stream) == cudaSuccess
@@ -667,6 +676,20 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         if (auto *lp = dynamic_cast<LocalPairChannel *>(P.chan)) lp->fail();
         return e.err;
     }
+    if (P.timing.enabled) {
+        for (int i = 0; i < P.timing.nrec; i++) {
+            auto &r = P.timing.recs[i];
+            float a = 0, b = 0;
+            cudaEventElapsedTime(&a, P.ref_event, r.a);
+            cudaEventElapsedTime(&b, P.ref_event, r.b);
+            P.intervals.emplace_back(double(a), double(b));
+            P.dcf.launches += 1, P.dcf.bytes += r.bytes, P.dcf.aes += r.aes, P.dcf.sum_ms += double(b - a);
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+        P.timing.nrec = 0;
+        P.dcf.union_ms += union_ms(P.intervals);
+    }
     P.stats.bytes_sent = P.chan->bytes_sent[P.party] - sent0;
     P.stats.rounds = P.chan->rounds[P.party] - rounds0;
     P.stats.key_bytes_used = e.off;
@@ -677,6 +700,36 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         // AFFINITY = int32(value) / 2^s (deepdtagen_inference.cu:594-606)
         if (h_aff) h_aff[i] = double(int32_t(uint32_t(uint64_t(v)))) / double(1ull << P.s);
     }
+    return DDG_OK;
+}
+
+double union_ms(std::vector<std::pair<double, double>> v)
+{
+    std::sort(v.begin(), v.end());
+    double tot = 0, cs = -1, ce = -1;
+    for (auto &iv : v) {
+        if (iv.first > ce) {
+            if (ce > cs) tot += ce - cs;
+            cs = iv.first, ce = iv.second;
+        } else if (iv.second > ce) {
+            ce = iv.second;
+        }
+    }
+    if (ce > cs) tot += ce - cs;
+    return tot;
+}
+
+// union of both parties' DCF launch intervals of the last forward on a common
+// timeline (the two ref events live on the same device)
+int pair_dcf_union(Party &p0, Party &p1)
+{
+    if (!p0.timing.enabled || !p1.timing.enabled || !p0.ref_event || !p1.ref_event) return DDG_OK;
+    DDG_CHECK(p0.device == p1.device, DDG_ERR_ARG, "pair timing needs both parties on one device");
+    float off = 0;
+    DDG_CUDA(cudaEventElapsedTime(&off, p0.ref_event, p1.ref_event));
+    std::vector<std::pair<double, double>> all = p0.intervals;
+    for (auto &iv : p1.intervals) all.emplace_back(iv.first + off, iv.second + off);
+    p0.dcf.pair_union_ms += union_ms(all);
     return DDG_OK;
 }
 

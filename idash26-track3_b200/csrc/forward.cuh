@@ -37,6 +37,13 @@ struct PartyStats {
     double ms_total = 0;
 };
 
+// accumulated DCF-kernel timing (see DcfTiming): launches, algorithmic bytes,
+// AES blocks, summed launch durations, union of this party's launch intervals,
+// union over both parties of an in-process pair (stored on party 0)
+struct DcfAcc {
+    double launches = 0, bytes = 0, aes = 0, sum_ms = 0, union_ms = 0, pair_union_ms = 0;
+};
+
 struct Party {
     int party = 0, bw = 32, s = 12, device = 0;
     cudaStream_t stream = nullptr;
@@ -46,6 +53,10 @@ struct Party {
     uint64_t key_bytes = 0;
     DevWeights w;
     PartyStats stats;
+    DcfTiming timing;
+    DcfAcc dcf;
+    cudaEvent_t ref_event = nullptr;                     // start of the last forward
+    std::vector<std::pair<double, double>> intervals;    // last forward's DCF launches, ms after ref_event
     // device staging of host inputs (kept across forwards)
     void *in_buf[4] = {};
     uint64_t in_cap[4] = {};
@@ -53,6 +64,8 @@ struct Party {
 };
 
 uint64_t forward_key_bytes(int bw, int s, int B);
+double union_ms(std::vector<std::pair<double, double>> v);
+int pair_dcf_union(Party &p0, Party &p1);
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
                  bool on_host, int64_t *h_out_raw, double *h_aff);
 int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uint8_t *k0, uint8_t *k1,

@@ -245,6 +245,7 @@ int gate_keygen_t(const GateLayout &L, uint64_t seed, uint32_t op, const void *r
     if (L.n == 0) return DDG_OK;
     DDG_TRY(set_smem(gate_keygen_kernel<T>));
     gate_keygen_kernel<T><<<aes_grid(L.n, 3), 256, AES_SMEM_BYTES, st>>>(a);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -264,8 +265,27 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
     a.lo = L.lo ? dcf_view(k, L.Lo) : DcfView{};
     a.bits_hi = bits_hi, a.bits_lo = bits_lo;
     DDG_TRY(set_smem(gate_round1_kernel<T>));
+    DcfTiming *tm = dcf_timing_sink();
+    DcfTiming::Rec *rec = nullptr;
+    if (tm && tm->enabled && tm->nrec < int(sizeof(tm->recs) / sizeof(tm->recs[0]))) {
+        rec = &tm->recs[tm->nrec];
+        DDG_CUDA(cudaEventCreate(&rec->a));
+        DDG_CUDA(cudaEventCreate(&rec->b));
+        DDG_CUDA(cudaEventRecord(rec->a, st));
+    }
     gate_round1_kernel<T><<<aes_grid(L.n, 3), 256, AES_SMEM_BYTES, st>>>(a);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
+    if (rec) {
+        DDG_CUDA(cudaEventRecord(rec->b, st));
+        // algorithmic bytes: every key byte of the DCFs once, the input, the output bits
+        const double n = double(L.n);
+        double bytes = n * (L.bw / 8.0), aes = 0;
+        if (L.hi) bytes += n * (16.0 * (L.H.L + 2) + 0.125 + 0.125), aes += n * (L.H.L + 1);
+        if (L.lo) bytes += n * (16.0 * (L.Lo.L + 2) + 0.125 + 0.125), aes += n * (L.Lo.L + 1);
+        rec->bytes = bytes, rec->aes = aes, rec->evals = n * ((L.hi ? 1 : 0) + (L.lo ? 1 : 0));
+        tm->nrec++;
+    }
     return DDG_OK;
 }
 
@@ -290,6 +310,7 @@ int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32
     case GATE_ARS: gate_round2_kernel<T, GATE_ARS><<<grid, 256, 0, st>>>(a); break;
     default: gate_round2_kernel<T, GATE_LRS><<<grid, 256, 0, st>>>(a); break;
     }
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }

@@ -151,12 +151,13 @@ __global__ void __launch_bounds__(256) lut_eval_kernel(const __grid_constant__ L
                 Blk cl = blk_xor(A.hash_h(t), blk_and_mask(cw, 0u - (t.w[0] & 1u)));
                 t = blk_xor(cl, blk_and_mask(t, 0u - bit));
             }
-            const uint32_t tm = 0u - (t.w[0] & 1u);
-            Blk g = blk_xor(A.hash_c(t), blk_and_mask(cwv, tm));
+            const bool tb = t.w[0] & 1u;
+            const Blk g = A.hash_c(t);
             const uint32_t leaf = (uint32_t(lane) << Lr) | uint32_t(q);
 #pragma unroll
             for (int kk = 0; kk < EPL; kk++) {
-                T v = blk_slot<T>(g, kk);
+                // arithmetic leaf: Conv(s) + t * CW_v, slot by slot in Z_2^n
+                T v = blk_slot<T>(g, kk) + (tb ? blk_slot<T>(cwv, kk) : T(0));
                 if (a.party) v = T(0) - v;
                 const uint32_t y = leaf * EPL + kk;
                 acc += v * tab[(uint32_t(x) - y) & 255u];
@@ -184,6 +185,7 @@ int lut_keygen(const LutLayout &L, const AesKey &dk, uint32_t op, const T *alpha
     DDG_CUDA(cudaFuncSetAttribute(lut_keygen_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
     LutKeygenArgs<T> a{L, dk, op, alpha_mask, rout, k0, k1};
     lut_keygen_kernel<T><<<lut_grid(L.n), 256, AES_SMEM_BYTES, st>>>(a);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }
@@ -197,6 +199,7 @@ int lut_eval(const LutLayout &L, int party, const T *xhat, const T *table, const
     DDG_CUDA(cudaFuncSetAttribute(lut_eval_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
     LutEvalArgs<T> a{L, party, xhat, table, key, share};
     lut_eval_kernel<T><<<lut_grid(L.n * 32), 256, AES_SMEM_BYTES, st>>>(a);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }

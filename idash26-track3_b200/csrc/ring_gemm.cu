@@ -116,6 +116,7 @@ int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
     dim3 grid((a.N + GT - 1) / GT, (a.M + GT - 1) / GT, a.batch);
     DDG_CHECK(grid.y <= 65535 && grid.z <= 65535, DDG_ERR_ARG, "gemm grid too large (M=%d batch=%d)", a.M, a.batch);
     ring_gemm_kernel<T><<<grid, 256, 0, st>>>(a);
+    note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
 }

@@ -81,6 +81,115 @@ int ddg_gate_round2(int kind, int bw, int scale, uint64_t n, int party, const vo
                     const uint32_t *d_hi_own, const uint32_t *d_hi_peer, const uint32_t *d_lo_own,
                     const uint32_t *d_lo_peer, const void *d_key, void *d_share, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Parties and the full online forward.
+ *
+ * A ddg_party is one evaluator of the online phase: it replaces the
+ * reference's DDGOrcaBatched backend object together with its GpuPeer
+ * (gpu_mpc/ddg_orca_batched.h:87-141, ddg_orca_base.h:93-116) and the
+ * resident evaluation loop of deepdtagen_inference.cu:422-607.  Its key region
+ * is a device buffer holding one forward's keys in graph order (the reference
+ * reads a key file into a GPU arena, patch:608-686); every op consumes the next
+ * section, as the reference's keyBuf cursor does.
+ * ---------------------------------------------------------------------- */
+typedef struct ddg_party ddg_party;
+
+int ddg_party_create(ddg_party **out, int party, int bw, int scale, int device);
+int ddg_party_destroy(ddg_party *party);
+/* public weights: the int64 weights.bin blob of reference/export_weights.py
+ * (nine layers in forward order, W as (in,out) row-major then b, scale `scale`;
+ * loadWeightsI64 at deepdtagen_inference.cu:121-181 shifts b to 2*scale) */
+int ddg_party_set_weights(ddg_party *party, const int64_t *h_blob, uint64_t n_int64);
+/* bind a device key region (not copied; must outlive the forwards) */
+int ddg_party_bind_keys(ddg_party *party, const void *d_keys, uint64_t bytes);
+/* the party's CUDA stream (all its kernels and copies run on it) */
+int ddg_party_stream(ddg_party *party, void **stream);
+/* last forward: out3 = {bytes sent, openings (rounds), key bytes consumed} */
+int ddg_party_stats(ddg_party *party, uint64_t *out3);
+/* channel between two parties of this process (same or different devices);
+ * zero-copy openings when both live on one device */
+int ddg_pair_local(ddg_party *p0, ddg_party *p1);
+/* channel to the peer in another process: both ranks pass the same 128-byte
+ * NCCL unique id (ddg_nccl_unique_id on one rank, broadcast by the caller) */
+int ddg_nccl_unique_id(void *out128);
+int ddg_party_connect_nccl(ddg_party *party, const void *unique_id128, int nranks, int rank, int peer_rank);
+/* give up (DDG_ERR_PEER) when the peer does not reach an opening in time */
+int ddg_party_set_timeout(ddg_party *party, int timeout_ms);
+
+/* key bytes of one forward of `batch` samples (per party) */
+uint64_t ddg_forward_key_bytes(int bw, int scale, int batch);
+/* One online forward of `batch` samples (replaces DeepDTAGenAffinity::_forward,
+ * gpu_mpc/deepdtagen.h:183-222, with ddgSecureAdjNormEval in front,
+ * secure_adj_norm.h:394-659).  Inputs: this party's additive shares of
+ *   x (batch,138,94) at scale, adj (batch,138,138) raw 0/1 at scale 0,
+ *   mask (batch,138,376) at scale, protein (batch,128) at scale (party 0 holds
+ *   zeros, party 1 the public value; deepdtagen_inference.cu:426-432),
+ * as device pointers, or host pointers when on_host != 0 (copied in).
+ * Outputs (either may be NULL): h_out_raw[batch] = revealed output at scale
+ * (signed), h_affinity[batch] = int32(value) / 2^scale, the reference's
+ * AFFINITY[i] (deepdtagen_inference.cu:594-606). */
+int ddg_forward_eval(ddg_party *party, int batch, const void *x_share, const void *adj_share, const void *mask_share,
+                     const void *protein_share, int on_host, int64_t *h_out_raw, double *h_affinity);
+/* both parties of an in-process pair, party 1 on an internal thread;
+ * in0/in1 = {x, adj, mask, protein} share pointers of party 0 / party 1 */
+int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
+                          int on_host, int64_t *h_out_raw, double *h_affinity);
+/* GPU dealer (replaces DDGOrcaKeygenBatched + ddgSecureAdjNormKeygen,
+ * deepdtagen_inference.cu:283-342): both parties' keys of one forward, fresh
+ * masks from `seed`, into d_key0 / d_key1 (ddg_forward_key_bytes each) */
+int ddg_dealer_forward(int bw, int scale, int batch, uint64_t seed, const int64_t *h_weights, uint64_t n_weights,
+                       int device, void *d_key0, void *d_key1, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Linear layers and the DPF look-up table, one party, no communication.
+ * ---------------------------------------------------------------------- */
+
+/* DPF LUT over an 8-bit domain (replaces gpuKeyGenLUT / gpuDpfLUT of
+ * gpu_mpc/secure_adj_norm.h:270-279, 498-520).  Dealer: point alpha = low 8
+ * bits of d_alpha_mask[i]; output mask d_rout[i] (shared into the keys).
+ * Eval: party's share of table[(x_hat - alpha) mod 256] + r_out; d_table holds
+ * 256 ring elements.  Either key pointer may be NULL (that party is skipped). */
+uint64_t ddg_lut_key_bytes(int bw, uint64_t n);
+int ddg_lut_keygen(int bw, uint64_t n, uint64_t seed, uint32_t op_id, const void *d_alpha_mask, const void *d_rout,
+                   void *d_key0, void *d_key1, void *stream);
+int ddg_lut_eval(int bw, uint64_t n, int party, const void *d_xhat, const void *d_table, const void *d_key,
+                 void *d_share, void *stream);
+
+/* Beaver elementwise product (replaces gpuMul of DDGOrca::mul,
+ * gpu_mpc/ddg_orca.h:43-63, and of secure_adj_norm.h:609-651):
+ *   out = [party==0] x_hat*y_hat - x_hat*[r_y] - [r_x]*y_hat + [r_x r_y + r_z]
+ * bcast: 0 none, 1 y indexed by row (b*rows + i), 2 by column (b*cols + j)
+ * of an element (b, i, j) of a (batch, rows, cols) tensor. */
+int ddg_mul_share(int bw, int party, uint64_t n, int bcast, int rows, int cols, const void *d_xhat, const void *d_yhat,
+                  const void *d_msx, const void *d_msy, const void *d_z, void *d_out, void *stream);
+
+/* Beaver matrix product per sample, secret x secret (replaces gpuMatmul of
+ * DDGOrcaBase::matmul 3-arg, gpu_mpc/ddg_orca_base.h:170-205, looped per
+ * sample in sytorch/layers/layers.h:67-90): for b < batch,
+ *   out[b] = A_hat[b] . ([party==0] B_hat[b] - [r_B][b]) - [r_A][b] . B_hat[b] + Z[b]
+ * A (M x K), B (K x N), out (M x N), row-major, contiguous per sample. */
+int ddg_matmul_share(int bw, int party, int batch, int M, int K, int N, const void *d_ahat, const void *d_bhat,
+                     const void *d_msa, const void *d_msb, const void *d_z, void *d_out, void *stream);
+
+/* Fully connected layer, secret x public weight (replaces FC<T> through
+ * DDGOrcaBase::matmul 4-arg, gpu_mpc/ddg_orca_base.h:208-271):
+ *   party 0: out = x_hat . W + bias2s + C0;  party 1: out = C1
+ * W (K x N) ring, bias2s (N) = bias << scale (may be NULL), C = key words
+ * [r_y - r_x . W]. */
+int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, const void *d_w, const void *d_bias2s,
+                 const void *d_c, void *d_out, void *stream);
+
+/* Kernel accounting.  ddg_launch_count: kernels this library has launched
+ * (process-wide).  DCF timing: when enabled on a party, every gate round-1
+ * (DCF) launch is bracketed by CUDA events on the party's stream; out6 gets
+ * {launches, algorithmic bytes (key bytes + input + output bits), AES blocks,
+ * summed launch ms, ms of the union of this party's launches, ms of the union
+ * of both parties' launches of an in-process pair (party 0 only)},
+ * accumulated since enabling. */
+uint64_t ddg_launch_count(void);
+int ddg_party_enable_dcf_timing(ddg_party *party, int on);
+int ddg_party_dcf_timing(ddg_party *party, double *out6);
+
 /* Diagnostics: `threads` independent chains of `iters` fixed-key tree
  * hashes (one AES-128 each), one word per chain written to d_out.  Gives the
  * AES-blocks/s ceiling of the DCF kernels. */
