@@ -1,0 +1,372 @@
+#!/usr/bin/env python
+"""Online 2PC throughput of the DeepDTAGen affinity branch on B200.
+
+Workload: the full affinity branch -- secure
+adjacency normalisation, GCN x3, masked max-pool, FC head -- at bw=32,
+scale 12, micro-batch B=256 of davis-shaped synthetic graphs, keys resident
+in HBM.  A step is one online forward of B samples by both parties.
+
+  N = 1      : both parties on cuda:0 (two host threads, zero-copy openings)
+  N = 2,4,8  : torchrun, one party per process; ranks 0..k-1 are party 0,
+               ranks k..2k-1 party 1, pair i = (i, k+i) exchanges its openings
+               over NCCL send/recv; every pair runs its own micro-batch (weak
+               scaling, no cross-pair collective on the data path).
+
+value    : samples/s of the whole job, inputs (shares) and keys already in HBM.
+e2e      : the same through the C ABI with host (pinned) share buffers: every
+           step copies both parties' input shares host->device and the
+           revealed affinities device->host.
+roofline : the DCF kernel (gate round 1), algorithmic bytes (key bytes +
+           input + output bits) over the union of its launch intervals,
+           measured with CUDA events on the party streams during the timed
+           region, against the measured HBM copy bandwidth.
+cpu_baseline / --impl reference : the reference's own CPU LSS ReLU backend
+           (gpu_mpc/lss, compiled by oracle/Makefile into oracle/_ref) over
+           loopback, plus the plaintext integer forward of the same graph.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+NMAX, FEAT, POOL, PROT = 138, 94, 376, 128
+RELUS_PER_SAMPLE = 171_076           # 138*(188+282+376) + 376*137 + 2816
+A10_SAMPLES_PER_S = 16 / 0.136       # reference README.md:99-101, A10, B=16, bw=32
+
+# DRAM bytes (read + write) per algorithmic byte of the round-1 DCF kernel,
+# from an ncu capture (profiles/gate_round1_dcf_relu_ars_b16.md: 445.6 MB of
+# DRAM traffic for 442.1 MB of algorithmic bytes in one launch).
+NCU_DRAM_BYTES_PER_ALG_BYTE = 445.6 / 442.1
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--bw", type=int, default=32, choices=[32, 64])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--scale", type=int, default=12)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def config_of(a, n_gpus):
+    pairs = max(n_gpus // 2, 1)
+    return {
+        "workload": f"full affinity branch (adj-norm, GCNx3, masked max-pool, FC head), bw={a.bw}, scale={a.scale}, "
+                    f"B={a.batch} davis-shaped synthetic graphs per pair, keys resident in HBM (BASELINE configs[2])",
+        "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs,
+        "parallelism": "1 GPU, both parties" if n_gpus == 1 else f"{pairs} party pairs over NCCL, one party per GPU",
+        "truncation": "exact (floor) at every site",
+        "l2": "inputs larger than L2: every step streams the full key region (>= 28 GB per party at B=256)",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or f[0] != str(self.index):
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+def cpu_baseline(bw, relu_n=8_000_000, fwd_samples=2):
+    """Reference LSS ReLU over loopback (all host cores) + plaintext integer forward."""
+    cores = os.cpu_count() or 2
+    exe = os.path.join(REPO, "oracle", "_ref", "lss_bench")
+    kind, relu_s_per_sample, detail = "port", None, {}
+    if os.path.exists(exe):
+        r = subprocess.run([exe, str(relu_n), str(bw), str(max(cores // 2, 1))], capture_output=True, text=True,
+                           timeout=600)
+        d = json.loads(r.stdout.strip().splitlines()[-1])
+        if "seconds" in d:
+            kind = "reference"
+            relu_s_per_sample = d["seconds"] * RELUS_PER_SAMPLE / relu_n
+            detail = d
+    from oracle import ring_forward as RF
+
+    synth = importlib.import_module("idash26-track3_b200.synth")
+    inp = synth.Inputs(fwd_samples, bw, seed=3, with_protein_cnn=False)
+    q = synth.quantize_weights(synth.affinity_weights(5), 12)
+    t0 = time.perf_counter()
+    RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, 12)
+    fwd_s = (time.perf_counter() - t0) / fwd_samples
+    per_sample = fwd_s + (relu_s_per_sample or 0.0)
+    sample = (f"reference LSS ReLU (gpu_mpc/lss compiled unmodified, 2 processes over loopback TCP, "
+              f"{max(cores // 2, 1)} OpenMP threads each) on {relu_n} elements at bw={bw}, scaled to "
+              f"{RELUS_PER_SAMPLE} ReLUs/sample; plus the plaintext integer forward (numpy, oracle/ring_forward.py) "
+              f"of {fwd_samples} samples for the linear layers" if kind == "reference" else
+              f"plaintext integer forward only (oracle/ring_forward.py, {fwd_samples} samples); LSS binary absent")
+    return {"value": 1.0 / per_sample, "unit": "samples/s", "cores": cores, "kind": kind, "sample": sample,
+            "relu_s_per_sample": relu_s_per_sample, "linear_s_per_sample": fwd_s, "lss": detail}
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return
+    t_steps = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        cb = cpu_baseline(a.bw, relu_n=2_000_000, fwd_samples=1)
+        if i >= a.warmup:
+            t_steps.append((time.perf_counter() - t0, cb))
+    vals = [cb["value"] for _, cb in t_steps]
+    v = statistics.median(vals)
+    cb = t_steps[-1][1]
+    cb = dict(cb, value=v)
+    line = {"impl": "reference", "metric": "online 2PC samples/sec (full affinity branch)", "value": v,
+            "unit": "samples/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": 1e3 * statistics.median([t for t, _ in t_steps]), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": f"u{a.bw}", "data": "synthetic",
+            "config": config_of(a, world), "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+
+def make_keys(ddg, torch, bw, s, B, seed, blob, device):
+    kb = ddg.forward_key_bytes(bw, s, B)
+    k0 = torch.empty(kb, dtype=torch.uint8, device=device)
+    k1 = torch.empty(kb, dtype=torch.uint8, device=device)
+    ddg.dealer_forward(bw, s, B, seed, blob, device.index, k0.data_ptr(), k1.data_ptr())
+    torch.cuda.synchronize(device)
+    return kb, k0, k1
+
+
+def share_buffers(torch, inp, party, device):
+    import numpy as np
+
+    arrs = [np.ascontiguousarray(x[party]) for x in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)]
+    dev = [torch.from_numpy(a.view(np.uint8).copy()).to(device) for a in arrs]
+    host = [torch.from_numpy(a.view(np.uint8).copy()).pin_memory() for a in arrs]
+    return dev, host
+
+
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        a.gpus = world if world > 1 else a.gpus
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return
+    import numpy as np
+    import torch
+
+    ddg = importlib.import_module("idash26-track3_b200")
+    synth = importlib.import_module("idash26-track3_b200.synth")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        if world % 2:
+            raise SystemExit("multi-GPU runs need an even number of GPUs (one party per GPU)")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
+    B, bw, s = a.batch, a.bw, a.scale
+    blob = synth.weights_blob(synth.quantize_weights(synth.affinity_weights(5), s))
+
+    # -------- parties, keys, inputs
+    if world == 1:
+        pairs, pair = 1, 0
+        kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000, blob, device)
+        inp = synth.Inputs(B, bw, seed=1000)
+        parties = [ddg.Party(0, bw, s, local), ddg.Party(1, bw, s, local)]
+        for p, k in zip(parties, (k0, k1)):
+            p.set_weights(blob)
+            p.bind_keys(k.data_ptr(), kb)
+        ddg.pair_local(parties[0], parties[1])
+        bufs = [share_buffers(torch, inp, p, device) for p in (0, 1)]
+    else:
+        pairs = world // 2
+        pair, party = rank % pairs, rank // pairs
+        peer = rank + pairs if party == 0 else rank - pairs
+        kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000 + pair, blob, device)
+        mine = k0 if party == 0 else k1
+        del k0, k1
+        torch.cuda.empty_cache()
+        inp = synth.Inputs(B, bw, seed=1000 + pair)
+        P = ddg.Party(party, bw, s, local)
+        P.set_weights(blob)
+        P.bind_keys(mine.data_ptr(), kb)
+        uid = [ddg.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        P.connect_nccl(uid[0], world, rank, peer)
+        P.set_timeout(600_000)
+        parties = [P]
+        bufs = [share_buffers(torch, inp, party, device)]
+
+    def step(on_host):
+        if world == 1:
+            ins = [[t.data_ptr() for t in (bufs[p][1] if on_host else bufs[p][0])] for p in (0, 1)]
+            return ddg.forward_pair(parties[0], parties[1], B, ins[0], ins[1], on_host=on_host)
+        ins = [t.data_ptr() for t in (bufs[0][1] if on_host else bufs[0][0])]
+        return parties[0].forward(B, *ins, on_host=on_host)
+
+    stream = torch.cuda.ExternalStream(parties[0].stream, device=device)
+
+    def timed(on_host, k):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            step(on_host)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    for _ in range(a.warmup):
+        step(False)
+    for p in parties:
+        p.enable_dcf_timing(True)
+    clocks = Clocks(local)
+    clocks.start()
+    n0 = ddg.launch_count()
+    ms = timed(False, a.steps)
+    launches = ddg.launch_count() - n0
+    clk = clocks.stop()
+    stats = parties[0].stats()
+    dcf = [p.dcf_timing() for p in parties]
+    for p in parties:
+        p.enable_dcf_timing(False)
+
+    e2e = None
+    if not a.no_e2e:
+        step(True)
+        ms_e2e = timed(True, a.steps)
+        # both parties' input shares of every pair cross host->device each step
+        own = [sum(int(t.numel()) for t in b[1]) for b in bufs]
+        h2d = sum(own) if world == 1 else 2 * own[0]
+        e2e = {"value": pairs * B * a.steps / (ms_e2e / 1e3), "unit": "samples/s",
+               "h2d_bytes_per_step": h2d * pairs, "d2h_bytes_per_step": B * (bw // 8) * pairs,
+               "ms_per_step": ms_e2e / a.steps}
+
+    value = pairs * B * a.steps / (ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    if world == 1:
+        union = dcf[0]["pair_union_ms"]
+        alg = dcf[0]["bytes"] + dcf[1]["bytes"]
+        aes = dcf[0]["aes_blocks"] + dcf[1]["aes_blocks"]
+        nl = dcf[0]["launches"] + dcf[1]["launches"]
+    else:
+        union, alg, aes, nl = dcf[0]["union_ms"], dcf[0]["bytes"], dcf[0]["aes_blocks"], dcf[0]["launches"]
+    achieved = alg / (union / 1e3) / 1e9 if union > 0 else 0.0
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": peak_kind,
+                "traffic": (alg / nl * NCU_DRAM_BYTES_PER_ALG_BYTE) if (nl and NCU_DRAM_BYTES_PER_ALG_BYTE) else None,
+                "kernel": "gate_round1_kernel (DCF evaluation)", "launches": nl,
+                "dcf_share_of_step": union / ms if ms > 0 else None,
+                "aes_gblocks_per_s": aes / (union / 1e3) / 1e9 if union > 0 else 0.0}
+    # AES ceiling on this GPU (the binding roofline of the DCF): fixed-key hash chains
+    out = torch.zeros(148 * 3 * 256 * 8, dtype=torch.int32, device=device)
+    ddg.check(ddg.lib().ddg_aes_chain(out.numel(), 64, out.data_ptr(), None))
+    torch.cuda.synchronize(device)
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(3):
+        ddg.check(ddg.lib().ddg_aes_chain(out.numel(), 64, out.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    eb.record()
+    torch.cuda.synchronize(device)
+    aes_peak = out.numel() * 64 * 3 / (ea.elapsed_time(eb) / 1e3) / 1e9
+    roofline["aes_peak_gblocks_per_s"] = aes_peak
+    roofline["aes_frac"] = roofline["aes_gblocks_per_s"] / aes_peak if aes_peak else None
+
+    cb = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cb = cpu_baseline(bw)
+    if rank == 0:
+        line = {"metric": "online 2PC samples/sec (full affinity branch)", "value": value, "unit": "samples/s",
+                "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": value / A10_SAMPLES_PER_S,
+                "vs_baseline_note": "reference's published 136 ms per batch of 16 on one A10 (README.md:99-101)",
+                "dtype": f"u{bw}", "data": "synthetic", "config": config_of(a, world), "roofline": roofline,
+                "cpu_baseline": cb, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+                "comm": {"bytes_sent_per_party_per_step": stats["bytes_sent"], "rounds_per_step": stats["rounds"],
+                         "bytes_per_sample": 2 * stats["bytes_sent"] / B,
+                         # emulated LAN, full duplex: each party's bytes at 1 Gbps + one 1 ms RTT per opening
+                         "lan_1gbps_1ms_rtt_s_per_step": stats["bytes_sent"] * 8 / 1e9 + stats["rounds"] * 1e-3},
+                "key_bytes_per_party_per_step": kb}
+        print(json.dumps(line), flush=True)
+    for p in parties:
+        p.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
