@@ -44,6 +44,7 @@ SIGNATURES = {
     "ddg_gate_keygen": (_i32, [_i32, _i32, _i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round1": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round2": (_i32, [_i32, _i32, _i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_gate_eval_pair_noalloc": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_lut_key_bytes": (_u64, [_i32, _u64]),
     "ddg_lut_keygen": (_i32, [_i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ddg_lut_eval": (_i32, [_i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp]),

@@ -81,6 +81,24 @@ int ddg_gate_round2(int kind, int bw, int scale, uint64_t n, int party, const vo
                     const uint32_t *d_hi_own, const uint32_t *d_hi_peer, const uint32_t *d_lo_own,
                     const uint32_t *d_lo_peer, const void *d_key, void *d_share, void *stream);
 
+/* Both parties' evaluation of one gate on one device with no device
+ * allocation (no counterpart in the reference, whose GPU code allocates per
+ * op through gpuMalloc).  For callers that cannot call cudaMalloc -- code
+ * inside a host framework that owns all device memory, code that must not hit
+ * the implicit synchronisation of cudaMalloc/cudaFree mid-pipeline, fixed
+ * memory budgets.  Same result as, per party, ddg_gate_round1 + the bit
+ * exchange + ddg_gate_round2 followed by adding the two shares: d_yhat[n] =
+ * f(x) + r_out (masked-public), from d_xhat and both parties' keys.  The
+ * round-1 bits and round-2 shares live in one file-scope device array of
+ * 4.25 MiB held by every GPU that loads the library until exit; at most
+ * DDG_NOALLOC_MAX_N elements per call, larger n is rejected with DDG_ERR_ARG.
+ * Calls share that array: calls that overlap on the GPU race.  The first call
+ * on a device looks up the array's address and uploads the AES tables; make
+ * it before any stream capture. */
+#define DDG_NOALLOC_MAX_N 262144
+int ddg_gate_eval_pair_noalloc(int kind, int bw, int scale, uint64_t n, const void *d_xhat, const void *d_key0,
+                               const void *d_key1, void *d_yhat, void *stream);
+
 /* ------------------------------------------------------------------------
  * Parties and the full online forward.
  *
