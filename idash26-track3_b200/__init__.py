@@ -18,7 +18,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libddg.so")
 
-GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS = 0, 1, 2, 3
+GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT = 0, 1, 2, 3, 4, 5
 
 DDG_OK = 0
 _STATUS = {1: "DDG_ERR_ARG", 2: "DDG_ERR_CUDA", 3: "DDG_ERR_KEY", 4: "DDG_ERR_PEER", 5: "DDG_ERR_STATE",
@@ -99,10 +99,10 @@ def gate_key_bytes(kind: int, bw: int, scale: int, n: int) -> int:
 
 def gate_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
     """Byte offsets of one party's gate key (see ddg_gate_key_layout)."""
-    out = (_u64 * 12)()
+    out = (_u64 * 14)()
     check(lib().ddg_gate_key_layout(kind, bw, scale, n, out))
     keys = ("hi_root", "hi_cw", "hi_leaf", "hi_mu", "lo_root", "lo_cw", "lo_leaf", "lo_mu", "words", "bytes",
-            "hi_levels", "lo_levels")
+            "hi_levels", "lo_levels", "hi_mu_eq", "hi_bits")
     return {k: int(v) for k, v in zip(keys, out)}
 
 

@@ -11,7 +11,7 @@ using namespace ddg;
 
 static int check_gate_args(int kind, int bw, int scale)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS, DDG_ERR_ARG, "gate kind %d out of range", kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_SPLIT, DDG_ERR_ARG, "gate kind %d out of range", kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
     return DDG_OK;
@@ -34,9 +34,9 @@ int ddg_gate_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out)
     DDG_TRY(check_gate_args(kind, bw, scale));
     DDG_CHECK(out != nullptr, DDG_ERR_ARG, "null out");
     GateLayout L = gate_layout(kind, bw, scale, n);
-    uint64_t v[12] = {L.H.root, L.H.cw, L.H.leaf, L.H.mu, L.Lo.root, L.Lo.cw, L.Lo.leaf, L.Lo.mu,
-                      L.words, L.bytes, uint64_t(L.H.L), uint64_t(L.Lo.L)};
-    for (int i = 0; i < 12; i++) out[i] = v[i];
+    uint64_t v[14] = {L.H.root, L.H.cw, L.H.leaf, L.H.mu, L.Lo.root, L.Lo.cw, L.Lo.leaf, L.Lo.mu,
+                      L.words, L.bytes, uint64_t(L.H.L), uint64_t(L.Lo.L), L.H.mu_eq, uint64_t(L.H.d)};
+    for (int i = 0; i < 14; i++) out[i] = v[i];
     return DDG_OK;
 }
 

@@ -62,8 +62,15 @@ void set_dcf_timing_sink(DcfTiming *t);
 // ---------------------------------------------------------------- key layouts
 
 // gate kinds (the comparison-based nonlinear layers)
-enum GateKind { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3 };
+// The *_SPLIT kinds compute the same functions as GATE_RELU / GATE_RELU_ARS
+// but split the (n-1)-bit comparison into a DCF-with-equality over the upper
+// n-1-s bits and the s-bit low DCF: 1{x<a} = 1{U<A} ^ (1{U==A} & 1{V<B}).
+enum GateKind {
+    GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
+    GATE_KIND_END = 6
+};
 
+inline bool gate_is_split(int kind) { return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT; }
 inline bool gate_has_hi(int kind) { return kind != GATE_LRS; }
 inline bool gate_has_lo(int kind) { return kind != GATE_RELU; }
 inline int gate_nwords(int kind)
@@ -72,29 +79,39 @@ inline int gate_nwords(int kind)
     case GATE_RELU: return 4;
     case GATE_RELU_ARS: return 8;
     case GATE_ARS: return 6;
+    case GATE_RELU_SPLIT: return 16;
+    case GATE_RELU_ARS_SPLIT: return 32;
     default: return 4;
     }
 }
+// domain bits of the high DCF
+inline int gate_hi_bits(int kind, int bw, int s) { return gate_is_split(kind) ? bw - 1 - s : bw - 1; }
 
 // DCF key arrays of N elements, structure-of-arrays, every array 256-byte aligned:
 //   root[N] (16 B) | cw[L][N] (16 B, level-major) | leaf[N] (16 B) | mu[ceil(N/32)] (u32 bits)
+//   [| mu_eq[ceil(N/32)] for a DCF with equality output]
+// A plain DCF's leaf covers the low min(d,7) bits (1 bit per slot); a DCF
+// with equality output covers the low 6 bits with 2 bits per slot.
 struct DcfLayout {
     int d = 0, L = 0;
-    uint64_t root = 0, cw = 0, leaf = 0, mu = 0, end = 0;
+    bool eq = false;
+    uint64_t root = 0, cw = 0, leaf = 0, mu = 0, mu_eq = 0, end = 0;
 };
 
 inline int dcf_levels(int d) { return d > 7 ? d - 7 : 0; }
 
-inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base)
+inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base, bool eq = false)
 {
     DcfLayout l;
     l.d = d;
-    l.L = dcf_levels(d);
+    l.eq = eq;
+    l.L = eq ? d - 6 : dcf_levels(d);
     l.root = align256(base);
     l.cw = align256(l.root + 16 * n);
     l.leaf = align256(l.cw + 16 * n * uint64_t(l.L));
     l.mu = align256(l.leaf + 16 * n);
-    l.end = align256(l.mu + 4 * ((n + 31) / 32));
+    l.mu_eq = eq ? align256(l.mu + 4 * ((n + 31) / 32)) : 0;
+    l.end = align256((eq ? l.mu_eq : l.mu) + 4 * ((n + 31) / 32));
     return l;
 }
 
@@ -116,7 +133,7 @@ inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base
     g.lo = gate_has_lo(kind);
     uint64_t off = align256(base);
     if (g.hi) {
-        g.H = dcf_layout(bw - 1, n, off);
+        g.H = dcf_layout(gate_hi_bits(kind, bw, s), n, off, gate_is_split(kind));
         off = g.H.end;
     }
     if (g.lo) {
@@ -132,7 +149,7 @@ inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base
 // DCF view handed to kernels (device pointers)
 struct DcfView {
     const uint8_t *root, *cw, *leaf;
-    const uint32_t *mu;
+    const uint32_t *mu, *mu_eq;
 };
 
 struct DcfOut {
@@ -142,7 +159,8 @@ struct DcfOut {
 
 inline DcfView dcf_view(const uint8_t *key, const DcfLayout &l)
 {
-    return DcfView{key + l.root, key + l.cw, key + l.leaf, reinterpret_cast<const uint32_t *>(key + l.mu)};
+    return DcfView{key + l.root, key + l.cw, key + l.leaf, reinterpret_cast<const uint32_t *>(key + l.mu),
+                   l.eq ? reinterpret_cast<const uint32_t *>(key + l.mu_eq) : nullptr};
 }
 
 // dealer PRG purposes

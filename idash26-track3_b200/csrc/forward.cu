@@ -493,12 +493,13 @@ struct EvalExec : ExecBase<T> {
         GateLayout L = gate_layout(kind, this->bw, this->s, x.n);
         const uint8_t *k = key_at(L.bytes);
         const uint64_t nw = (x.n + 31) / 32;
-        const int nb = (L.hi ? 1 : 0) + (L.lo ? 1 : 0);
+        const int nh = L.hi ? (L.H.eq ? 2 : 1) : 0;  // split gates also open the equality bits
+        const int nb = nh + (L.lo ? 1 : 0);
         uint32_t *bits = static_cast<uint32_t *>(this->alloc_bytes(4 * nw * nb));
-        uint32_t *bh = L.hi ? bits : nullptr, *bl = L.lo ? bits + (L.hi ? nw : 0) : nullptr;
+        uint32_t *bh = L.hi ? bits : nullptr, *bl = L.lo ? bits + nh * nw : nullptr;
         if (this->err == DDG_OK) ok(gate_round1(L, x.v, k, bh, bl, this->st));
         const uint32_t *peer = reinterpret_cast<const uint32_t *>(peer_of(bits, 4 * nw * nb));
-        const uint32_t *ph = L.hi ? peer : nullptr, *pl = L.lo ? peer + (L.hi ? nw : 0) : nullptr;
+        const uint32_t *ph = L.hi ? peer : nullptr, *pl = L.lo ? peer + nh * nw : nullptr;
         T *s = alloc(x.n);
         if (this->err == DDG_OK) ok(gate_round2(L, p, x.v, bh, ph, bl, pl, k, s, this->st));
         Tn<T> t;
@@ -564,7 +565,7 @@ static void affinity_graph(E &x)
         Tn<T> Pm = x.matmul(Ah, H, LAYER_IN[l]);
         Tn<T> AX = x.gate(GATE_LRS, Pm);
         Tn<T> Z = x.fc(AX, l, B * NMAX);
-        H = x.gate(GATE_RELU_ARS, Z);
+        H = x.gate(GATE_RELU_ARS_SPLIT, Z);
     }
     // masked global max-pool (deepdtagen.h:198-202, masked_maxpool_layer.h:72-126)
     EwShape shm;
@@ -575,15 +576,15 @@ static void affinity_graph(E &x)
     while (cnt > 1) {
         Tn<T> even, diff;
         x.pool_split(cur, cnt, even, diff);
-        Tn<T> r = x.gate(GATE_RELU, diff);
+        Tn<T> r = x.gate(GATE_RELU_SPLIT, diff);
         cur = x.pool_merge(even, r, cur, cnt);
         cnt = cnt / 2 + (cnt & 1);
     }
     // head (deepdtagen.h:209-220)
-    Tn<T> d1 = x.gate(GATE_RELU_ARS, x.fc(cur, 3, B));
+    Tn<T> d1 = x.gate(GATE_RELU_ARS_SPLIT, x.fc(cur, 3, B));
     Tn<T> d2 = x.gate(GATE_ARS, x.fc(d1, 4, B));
     Tn<T> f = x.concat(d2, P);
-    for (int l = 5; l < 8; l++) f = x.gate(GATE_RELU_ARS, x.fc(f, l, B));
+    for (int l = 5; l < 8; l++) f = x.gate(GATE_RELU_ARS_SPLIT, x.fc(f, l, B));
     Tn<T> o = x.fc(f, 8, B);
     x.output(o);
 }

@@ -53,8 +53,12 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
             if (L.hi) {
                 DcfOut o{a.k0 + L.H.root, a.k1 + L.H.root, a.k0 + L.H.cw, a.k1 + L.H.cw,
                          a.k0 + L.H.leaf, a.k1 + L.H.leaf, nullptr, nullptr};
-                dcf_keygen(A, uint64_t(r_l), n - 1, A.prg(a.dk.rk, a.op, P_HI_S0, e), A.prg(a.dk.rk, a.op, P_HI_DELTA, e),
-                           o, e, N);
+                if (L.H.eq)
+                    dcfeq_keygen(A, uint64_t(r_l >> s), L.H.d, A.prg(a.dk.rk, a.op, P_HI_S0, e),
+                                 A.prg(a.dk.rk, a.op, P_HI_DELTA, e), o, e, N);
+                else
+                    dcf_keygen(A, uint64_t(r_l), n - 1, A.prg(a.dk.rk, a.op, P_HI_S0, e),
+                               A.prg(a.dk.rk, a.op, P_HI_DELTA, e), o, e, N);
             }
             if (L.lo) {
                 DcfOut o{a.k0 + L.Lo.root, a.k1 + L.Lo.root, a.k0 + L.Lo.cw, a.k1 + L.Lo.cw,
@@ -62,7 +66,12 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
                 dcf_keygen(A, uint64_t(r_L), s, A.prg(a.dk.rk, a.op, P_LO_S0, e), A.prg(a.dk.rk, a.op, P_LO_DELTA, e), o,
                            e, N);
             }
-            T v[8];
+            T v[32];
+            // split gates: monomials of the dealer bits the DReLU bit depends on,
+            // eps = r_m ^ rho_c: eps, rho_L, rho_e, rho_e rho_L, eps rho_L, eps rho_e, eps rho_e rho_L
+            const T rho_e = T(((bits >> 4) ^ (bits >> 5)) & 1u);
+            const T mono[7] = {e_b, rho_L, rho_e, T(rho_e * rho_L), T(e_b * rho_L), T(e_b * rho_e),
+                               T(e_b * rho_e * rho_L)};
             switch (a.kind) {
             case GATE_RELU:
                 v[0] = e_b, v[1] = r, v[2] = e_b * r, v[3] = r_y;
@@ -74,6 +83,19 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
             case GATE_ARS:
                 v[0] = r_H, v[1] = rho_L, v[2] = rho_c, v[3] = r_m, v[4] = r_m * rho_c, v[5] = r_y;
                 break;
+            case GATE_RELU_SPLIT:
+                for (int k = 0; k < 7; k++) v[k] = mono[k], v[8 + k] = mono[k] * r;
+                v[7] = r, v[15] = r_y;
+                break;
+            case GATE_RELU_ARS_SPLIT: {
+                const T nj[3] = {r_H, rho_L, r_m};
+                for (int k = 0; k < 7; k++) v[k] = mono[k];
+                for (int j = 0; j < 3; j++) v[7 + j] = nj[j];
+                for (int k = 0; k < 7; k++)
+                    for (int j = 0; j < 3; j++) v[10 + 3 * k + j] = mono[k] * nj[j];
+                v[31] = r_y;
+                break;
+            }
             default:
                 v[0] = r_H, v[1] = rho_L, v[2] = r_m, v[3] = r_y;
                 break;
@@ -92,11 +114,17 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
         const uint32_t m1h = __ballot_sync(0xFFFFFFFFu, valid && (bits & 2u));
         const uint32_t m0l = __ballot_sync(0xFFFFFFFFu, valid && (bits & 4u));
         const uint32_t m1l = __ballot_sync(0xFFFFFFFFu, valid && (bits & 8u));
+        const uint32_t m0e = __ballot_sync(0xFFFFFFFFu, valid && (bits & 16u));
+        const uint32_t m1e = __ballot_sync(0xFFFFFFFFu, valid && (bits & 32u));
         if ((threadIdx.x & 31) == 0) {
             const uint64_t wi = e >> 5;
             if (L.hi) {
                 reinterpret_cast<uint32_t *>(a.k0 + L.H.mu)[wi] = m0h;
                 reinterpret_cast<uint32_t *>(a.k1 + L.H.mu)[wi] = m1h;
+                if (L.H.eq) {
+                    reinterpret_cast<uint32_t *>(a.k0 + L.H.mu_eq)[wi] = m0e;
+                    reinterpret_cast<uint32_t *>(a.k1 + L.H.mu_eq)[wi] = m1e;
+                }
             }
             if (L.lo) {
                 reinterpret_cast<uint32_t *>(a.k0 + L.Lo.mu)[wi] = m0l;
@@ -110,12 +138,12 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
 
 template <typename T>
 struct Round1Args {
-    int n, s;
+    int n, s, hi_d;
     uint64_t N;
     const T *xhat;
     DcfView hi, lo;
-    bool has_hi, has_lo;
-    uint32_t *bits_hi, *bits_lo;
+    bool has_hi, has_lo, split;
+    uint32_t *bits_hi, *bits_lo;  // split gates: bits_hi[0, nw) compare, [nw, 2nw) equality
 };
 
 template <typename T>
@@ -131,17 +159,26 @@ __global__ void __launch_bounds__(256, 3) gate_round1_kernel(const __grid_consta
     const T lmask = (T(1) << a.s) - 1;
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
         const bool valid = e < N;
-        uint32_t bh = 0, bl = 0;
+        uint32_t bh = 0, bl = 0, be = 0;
         if (valid) {
             const T x = __ldcs(a.xhat + e);
-            if (a.has_hi) bh = dcf_eval(A, uint64_t(x & hmask), a.n - 1, a.hi, e, N);
+            if (a.has_hi) {
+                if (a.split) {
+                    const uint32_t b = dcfeq_eval(A, uint64_t((x & hmask) >> a.s), a.hi_d, a.hi, e, N);
+                    bh = b & 1u, be = b >> 1;
+                } else {
+                    bh = dcf_eval(A, uint64_t(x & hmask), a.n - 1, a.hi, e, N);
+                }
+            }
             if (a.has_lo) bl = dcf_eval(A, uint64_t(x & lmask), a.s, a.lo, e, N);
         }
         const uint32_t wh = __ballot_sync(0xFFFFFFFFu, bh);
         const uint32_t wl = __ballot_sync(0xFFFFFFFFu, bl);
+        const uint32_t we = __ballot_sync(0xFFFFFFFFu, be);
         if ((threadIdx.x & 31) == 0) {
             const uint64_t wi = e >> 5;
             if (a.has_hi) a.bits_hi[wi] = wh ^ __ldcs(a.hi.mu + wi);
+            if (a.split) a.bits_hi[((N + 31) >> 5) + wi] = we ^ __ldcs(a.hi.mu_eq + wi);
             if (a.has_lo) a.bits_lo[wi] = wl ^ __ldcs(a.lo.mu + wi);
         }
     }
@@ -152,7 +189,7 @@ __global__ void __launch_bounds__(256, 3) gate_round1_kernel(const __grid_consta
 template <typename T>
 struct Round2Args {
     int kind, n, s, party;
-    uint64_t N;
+    uint64_t N, nw;
     const T *xhat;
     const uint32_t *hi_own, *hi_peer, *lo_own, *lo_peer;
     const T *words;
@@ -170,9 +207,11 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
         const T x = a.xhat[e];
         const uint64_t wi = e >> 5;
         const uint32_t bi = uint32_t(e & 31);
-        T ch = 0, cl = 0;
+        T ch = 0, cl = 0, eh = 0;
         if (KIND != GATE_LRS) ch = T(((a.hi_own[wi] ^ a.hi_peer[wi]) >> bi) & 1u);
         if (KIND != GATE_RELU) cl = T(((a.lo_own[wi] ^ a.lo_peer[wi]) >> bi) & 1u);
+        if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT)
+            eh = T(((a.hi_own[a.nw + wi] ^ a.hi_peer[a.nw + wi]) >> bi) & 1u);
         const T mh = x >> (n - 1);
         const T xH = x >> s;
         const T *w = a.words + e;
@@ -186,6 +225,36 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
         } else if (KIND == GATE_RELU_ARS) {
             y = p0 * (q * xH - q * cl) + W(0) * (a1 * xH - a1 * cl) - q * W(1) - a1 * W(2) - q * b1 * W(3) -
                 a1 * b1 * W(4) + two_ns * (T(1) - mh) * (q * W(5) + a1 * W(6)) + W(7);
+        } else if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT) {
+            // DReLU = a0 + sum_k ak[k] * mono[k]  (mono: the dealer-bit monomials of the key words)
+            const T se = T(1) - T(2) * eh, sc = b1;
+            const T G0 = eh * cl, GL = eh * sc, Ge = cl * se, GeL = se * sc;
+            const T a0 = q + a1 * G0;
+            const T ak[7] = {a1 * (T(1) - T(2) * G0), a1 * GL, a1 * Ge, a1 * GeL, T(0) - T(2) * a1 * GL,
+                             T(0) - T(2) * a1 * Ge, T(0) - T(2) * a1 * GeL};
+            T sm = 0;
+#pragma unroll
+            for (int k = 0; k < 7; k++) sm += ak[k] * W(k);
+            if (KIND == GATE_RELU_SPLIT) {
+                T sr = 0;
+#pragma unroll
+                for (int k = 0; k < 7; k++) sr += ak[k] * W(8 + k);
+                y = p0 * a0 * x + x * sm - a0 * W(7) - sr + W(15);
+            } else {
+                const T Y0 = xH - cl;
+                const T yj[3] = {T(0) - T(1), T(0) - sc, two_ns * (T(1) - mh)};
+                T sn = 0, smn = 0;
+#pragma unroll
+                for (int j = 0; j < 3; j++) sn += yj[j] * W(7 + j);
+#pragma unroll
+                for (int k = 0; k < 7; k++) {
+                    T t = 0;
+#pragma unroll
+                    for (int j = 0; j < 3; j++) t += yj[j] * W(10 + 3 * k + j);
+                    smn += ak[k] * t;
+                }
+                y = p0 * a0 * Y0 + Y0 * sm + a0 * sn + smn + W(31);
+            }
         } else if (KIND == GATE_ARS) {
             const T pub = xH - cl + two_ns * (mh * ch - mh);
             y = p0 * pub - W(0) - b1 * W(1) +
@@ -257,10 +326,10 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
     DDG_TRY(aes_device_init());
     if (L.n == 0) return DDG_OK;
     Round1Args<T> a;
-    a.n = L.bw, a.s = L.s, a.N = L.n;
+    a.n = L.bw, a.s = L.s, a.N = L.n, a.hi_d = L.H.d;
     a.xhat = static_cast<const T *>(xhat);
     const uint8_t *k = static_cast<const uint8_t *>(key);
-    a.has_hi = L.hi, a.has_lo = L.lo;
+    a.has_hi = L.hi, a.has_lo = L.lo, a.split = L.hi && L.H.eq;
     a.hi = L.hi ? dcf_view(k, L.H) : DcfView{};
     a.lo = L.lo ? dcf_view(k, L.Lo) : DcfView{};
     a.bits_hi = bits_hi, a.bits_lo = bits_lo;
@@ -281,7 +350,7 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
         // algorithmic bytes: every key byte of the DCFs once, the input, the output bits
         const double n = double(L.n);
         double bytes = n * (L.bw / 8.0), aes = 0;
-        if (L.hi) bytes += n * (16.0 * (L.H.L + 2) + 0.125 + 0.125), aes += n * (L.H.L + 1);
+        if (L.hi) bytes += n * (16.0 * (L.H.L + 2) + (L.H.eq ? 0.5 : 0.25)), aes += n * (L.H.L + 1);
         if (L.lo) bytes += n * (16.0 * (L.Lo.L + 2) + 0.125 + 0.125), aes += n * (L.Lo.L + 1);
         rec->bytes = bytes, rec->aes = aes, rec->evals = n * ((L.hi ? 1 : 0) + (L.lo ? 1 : 0));
         tm->nrec++;
@@ -295,7 +364,7 @@ int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32
 {
     if (L.n == 0) return DDG_OK;
     Round2Args<T> a;
-    a.kind = L.kind, a.n = L.bw, a.s = L.s, a.party = party, a.N = L.n;
+    a.kind = L.kind, a.n = L.bw, a.s = L.s, a.party = party, a.N = L.n, a.nw = (L.n + 31) / 32;
     a.xhat = static_cast<const T *>(xhat);
     a.hi_own = hi_own, a.hi_peer = hi_peer, a.lo_own = lo_own, a.lo_peer = lo_peer;
     a.words = reinterpret_cast<const T *>(static_cast<const uint8_t *>(key) + L.words);
@@ -308,6 +377,8 @@ int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32
     case GATE_RELU: gate_round2_kernel<T, GATE_RELU><<<grid, 256, 0, st>>>(a); break;
     case GATE_RELU_ARS: gate_round2_kernel<T, GATE_RELU_ARS><<<grid, 256, 0, st>>>(a); break;
     case GATE_ARS: gate_round2_kernel<T, GATE_ARS><<<grid, 256, 0, st>>>(a); break;
+    case GATE_RELU_SPLIT: gate_round2_kernel<T, GATE_RELU_SPLIT><<<grid, 256, 0, st>>>(a); break;
+    case GATE_RELU_ARS_SPLIT: gate_round2_kernel<T, GATE_RELU_ARS_SPLIT><<<grid, 256, 0, st>>>(a); break;
     default: gate_round2_kernel<T, GATE_LRS><<<grid, 256, 0, st>>>(a); break;
     }
     note_launch();

@@ -62,7 +62,8 @@ int scratch_address(void **out)
 extern "C" int ddg_gate_eval_pair_noalloc(int kind, int bw, int scale, uint64_t n, const void *d_xhat,
                                           const void *d_key0, const void *d_key1, void *d_yhat, void *stream)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS, DDG_ERR_ARG, "gate kind %d out of range", kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS, DDG_ERR_ARG,
+              "gate kind %d out of range for the no-allocation entry point (0..3)", kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
     DDG_CHECK(n <= kMaxN, DDG_ERR_ARG,

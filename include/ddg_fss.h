@@ -35,6 +35,12 @@ extern "C" {
 #define DDG_GATE_RELU_ARS 1  /* y = ReLU(floor(x / 2^scale))   (FC + ReLU)     */
 #define DDG_GATE_ARS 2       /* y = floor(x / 2^scale), signed  (FC, no ReLU)  */
 #define DDG_GATE_LRS 3       /* y = floor(x / 2^scale) for x in [0, 2^(bw-1))   */
+/* Same functions as RELU / RELU_ARS with the (bw-1)-bit comparison split into a
+ * DCF with equality output over the upper bw-1-scale bits and the scale-bit low
+ * DCF: 1{x<a} = 1{U<A} ^ (1{U==A} & 1{V<B}).  20 instead of 25 / 31 AES-128 per
+ * element at bw=32; round 1 emits three bit arrays (see ddg_gate_round1). */
+#define DDG_GATE_RELU_SPLIT 4
+#define DDG_GATE_RELU_ARS_SPLIT 5
 
 const char *ddg_last_error(void);
 int ddg_version(void);
@@ -58,9 +64,10 @@ int ddg_version(void);
 /* bytes of one party's key for n elements */
 uint64_t ddg_gate_key_bytes(int kind, int bw, int scale, uint64_t n);
 
-/* byte offsets of one party's key for n elements, written to out[12]:
+/* byte offsets of one party's key for n elements, written to out[14]:
  *   0 hi_root 1 hi_cw 2 hi_leaf 3 hi_mu 4 lo_root 5 lo_cw 6 lo_leaf 7 lo_mu
  *   8 words 9 total bytes 10 high-DCF tree levels 11 low-DCF tree levels
+ *   12 hi_mu_eq (split kinds) 13 high-DCF domain bits
  * Each DCF is structure-of-arrays: root[n] 16 B, cw[levels][n] 16 B
  * (level-major), leaf[n] 16 B, mu[ceil(n/32)] u32 mask bits; then
  * nwords x n ring words.  Every array starts on a 256-byte boundary. */
@@ -72,7 +79,10 @@ int ddg_gate_keygen(int kind, int bw, int scale, uint64_t n, uint64_t seed, uint
                     void *d_rout, void *d_key0, void *d_key1, void *stream);
 
 /* round 1: d_bits_hi / d_bits_lo hold ceil(n/32) words each (a gate without
- * the high DCF (LRS) or the low DCF (RELU) leaves that array untouched). */
+ * the high DCF (LRS) or the low DCF (RELU) leaves that array untouched); for
+ * the split kinds d_bits_hi holds 2*ceil(n/32) words: the compare bits, then
+ * the equality bits.  Round 2 reads its own and the peer's arrays in the same
+ * layout. */
 int ddg_gate_round1(int kind, int bw, int scale, uint64_t n, const void *d_xhat, const void *d_key,
                     uint32_t *d_bits_hi, uint32_t *d_bits_lo, void *stream);
 

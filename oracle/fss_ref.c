@@ -276,9 +276,84 @@ int ref_dcf_eval(int d, uint64_t x, const uint8_t root[16], const uint8_t *cw, c
     return c;
 }
 
+/*
+ * DCF with an equality output over d-bit x: the same half-tree walk, but the
+ * 128-bit leaf holds 64 slots of 2 bits for the low 6 bits y of x:
+ * bit 2y = 1{y < alpha_low6}, bit 2y+1 = 1{y == alpha_low6}.  Returns the party's
+ * XOR shares of (1{x < alpha}, 1{x == alpha}) as bit0 / bit1.  Used as the upper
+ * part of a split comparison: 1{x < a} over (U,V) = 1{U<A} ^ (1{U==A} & 1{V<B}).
+ */
+void ref_dcfeq_keygen(int d, uint64_t alpha, const uint8_t s0[16], const uint8_t delta_in[16],
+                      uint8_t root0[16], uint8_t root1[16], uint8_t *cw, uint8_t leafcw[16])
+{
+    if (!fixed_ready) fixed_init();
+    int L = d - 6;
+    uint8_t delta[16], cur[2][16], h[2][16];
+    memcpy(delta, delta_in, 16);
+    delta[0] |= 1;
+    memcpy(cur[0], s0, 16);
+    memcpy(cur[1], s0, 16);
+    xor16(cur[1], delta);
+    memcpy(root0, cur[0], 16);
+    memcpy(root1, cur[1], 16);
+    for (int j = 0; j < L; j++) {
+        int a = (int)((alpha >> (d - 1 - j)) & 1);
+        ccr(&ks_h, cur[0], h[0]);
+        ccr(&ks_h, cur[1], h[1]);
+        uint8_t *c = cw + 16 * j;
+        for (int i = 0; i < 16; i++) c[i] = (uint8_t)(h[0][i] ^ h[1][i] ^ (a ? 0 : delta[i]));
+        for (int b = 0; b < 2; b++) {
+            int t = cur[b][0] & 1;
+            uint8_t cl[16];
+            for (int i = 0; i < 16; i++) cl[i] = (uint8_t)(h[b][i] ^ (t ? c[i] : 0));
+            if (a) xor16(cur[b], cl);
+            else memcpy(cur[b], cl, 16);
+        }
+    }
+    uint8_t g0[16], g1[16], m[16];
+    memset(m, 0, 16);
+    int al = (int)(alpha & 63);
+    for (int y = 0; y < 64; y++) {
+        if (y < al) m[(2 * y) >> 3] |= (uint8_t)(1u << ((2 * y) & 7));
+        if (y == al) m[(2 * y + 1) >> 3] |= (uint8_t)(1u << ((2 * y + 1) & 7));
+    }
+    ccr(&ks_c, cur[0], g0);
+    ccr(&ks_c, cur[1], g1);
+    for (int i = 0; i < 16; i++) leafcw[i] = (uint8_t)(g0[i] ^ g1[i] ^ m[i]);
+}
+
+int ref_dcfeq_eval(int d, uint64_t x, const uint8_t root[16], const uint8_t *cw, const uint8_t leafcw[16])
+{
+    if (!fixed_ready) fixed_init();
+    int L = d - 6;
+    uint8_t s[16], h[16], cl[16];
+    memcpy(s, root, 16);
+    int c = 0;
+    for (int j = 0; j < L; j++) {
+        int xj = (int)((x >> (d - 1 - j)) & 1);
+        int t = s[0] & 1;
+        ccr(&ks_h, s, h);
+        for (int i = 0; i < 16; i++) cl[i] = (uint8_t)(h[i] ^ (t ? cw[16 * j + i] : 0));
+        if (!xj) {
+            c ^= (cl[0] ^ s[0]) & 1;
+            memcpy(s, cl, 16);
+        } else {
+            xor16(s, cl);
+        }
+    }
+    int t = s[0] & 1;
+    uint8_t g[16];
+    ccr(&ks_c, s, g);
+    if (t) xor16(g, leafcw);
+    int y = (int)(x & 63);
+    return (c ^ block_bit(g, 2 * y)) | (block_bit(g, 2 * y + 1) << 1);
+}
+
 /* ----------------------------------------------------------------- gates */
 
-enum { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3 };
+enum { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5 };
+
+static int is_split(int kind) { return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT; }
 
 enum {
     P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4,
@@ -290,11 +365,12 @@ typedef struct {
     uint8_t hi_cw[56][16];
     uint8_t hi_leaf[16];
     int32_t hi_mu;
+    int32_t hi_mu_eq;
     uint8_t lo_root[16];
     uint8_t lo_cw[56][16];
     uint8_t lo_leaf[16];
     int32_t lo_mu;
-    uint64_t w[8];
+    uint64_t w[32];
 } ref_gate_key;
 
 int ref_gate_has_hi(int kind) { return kind != GATE_LRS; }
@@ -305,9 +381,13 @@ int ref_gate_nwords(int kind)
     case GATE_RELU: return 4;
     case GATE_RELU_ARS: return 8;
     case GATE_ARS: return 6;
+    case GATE_RELU_SPLIT: return 16;
+    case GATE_RELU_ARS_SPLIT: return 32;
     default: return 4;
     }
 }
+/* domain bits of the high DCF: n-1, or the upper n-1-s bits for split gates */
+int ref_gate_hi_bits(int kind, int n, int s) { return is_split(kind) ? n - 1 - s : n - 1; }
 
 /*
  * Dealer side for one element.  r_in is the input mask (x_hat = x + r_in),
@@ -337,7 +417,8 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
     uint64_t r_y = ring_of(blk, n);
     ref_prg(&ks, op, P_BITS, i, blk);
     int mu0h = blk[0] & 1, mu1h = (blk[0] >> 1) & 1, mu0l = (blk[0] >> 2) & 1, mu1l = (blk[0] >> 3) & 1;
-    int rho_c = mu0h ^ mu1h, rho_L = mu0l ^ mu1l;
+    int mu0e = (blk[0] >> 4) & 1, mu1e = (blk[0] >> 5) & 1;
+    int rho_c = mu0h ^ mu1h, rho_L = mu0l ^ mu1l, rho_e = mu0e ^ mu1e;
 
     uint64_t r_m = (r_in >> (n - 1)) & 1;
     uint64_t r_l = r_in & (M >> 1);
@@ -348,11 +429,18 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
     if (ref_gate_has_hi(kind)) {
         ref_prg(&ks, op, P_HI_S0, i, blk);
         ref_prg(&ks, op, P_HI_DELTA, i, blk2);
-        ref_dcf_keygen(n - 1, r_l, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
+        if (is_split(kind))
+            ref_dcfeq_keygen(n - 1 - s, r_l >> s, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
+        else
+            ref_dcf_keygen(n - 1, r_l, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
         memcpy(k1->hi_cw, k0->hi_cw, sizeof(k0->hi_cw));
         memcpy(k1->hi_leaf, k0->hi_leaf, 16);
         k0->hi_mu = mu0h;
         k1->hi_mu = mu1h;
+        if (is_split(kind)) {
+            k0->hi_mu_eq = mu0e;
+            k1->hi_mu_eq = mu1e;
+        }
     }
     if (ref_gate_has_lo(kind)) {
         ref_prg(&ks, op, P_LO_S0, i, blk);
@@ -363,8 +451,12 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
         k0->lo_mu = mu0l;
         k1->lo_mu = mu1l;
     }
-    uint64_t v[8];
+    uint64_t v[32];
     int nw = ref_gate_nwords(kind);
+    /* split gates: monomials of the dealer bits that the DReLU bit depends on,
+     * eps = r_m ^ rho_c:  eps, rho_L, rho_e, rho_e*rho_L, eps*rho_L, eps*rho_e, eps*rho_e*rho_L */
+    uint64_t ep = r_m ^ (uint64_t)rho_c, pl = (uint64_t)rho_L, pe = (uint64_t)rho_e;
+    uint64_t mono[7] = {ep, pl, pe, pe * pl, ep * pl, ep * pe, ep * pe * pl};
     switch (kind) {
     case GATE_RELU:
         v[0] = e; v[1] = r_in; v[2] = e * r_in; v[3] = r_y;
@@ -377,6 +469,20 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
         v[0] = r_H; v[1] = (uint64_t)rho_L; v[2] = (uint64_t)rho_c; v[3] = r_m;
         v[4] = r_m * (uint64_t)rho_c; v[5] = r_y;
         break;
+    case GATE_RELU_SPLIT:
+        for (int k = 0; k < 7; k++) v[k] = mono[k], v[8 + k] = mono[k] * r_in;
+        v[7] = r_in;
+        v[15] = r_y;
+        break;
+    case GATE_RELU_ARS_SPLIT: {
+        uint64_t nj[3] = {r_H, pl, r_m};
+        for (int k = 0; k < 7; k++) v[k] = mono[k];
+        for (int j = 0; j < 3; j++) v[7 + j] = nj[j];
+        for (int k = 0; k < 7; k++)
+            for (int j = 0; j < 3; j++) v[10 + 3 * k + j] = mono[k] * nj[j];
+        v[31] = r_y;
+        break;
+    }
     default:
         v[0] = r_H; v[1] = (uint64_t)rho_L; v[2] = r_m; v[3] = r_y;
         break;
@@ -390,23 +496,30 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
     return r_y;
 }
 
-/* round 1: the party's two output bits (bit0 = high DCF, bit1 = low DCF) */
+/* round 1: the party's output bits: bit0 = high DCF (compare), bit1 = low DCF,
+ * bit2 = high DCF equality (split gates) */
 int ref_gate_round1(int kind, int n, int s, uint64_t xhat, const ref_gate_key *k)
 {
     uint64_t M = nmask(n);
     xhat &= M;
     int out = 0;
-    if (ref_gate_has_hi(kind))
-        out |= (ref_dcf_eval(n - 1, xhat & (M >> 1), k->hi_root, &k->hi_cw[0][0], k->hi_leaf) ^ k->hi_mu) & 1;
+    if (ref_gate_has_hi(kind)) {
+        if (is_split(kind)) {
+            int b = ref_dcfeq_eval(n - 1 - s, (xhat & (M >> 1)) >> s, k->hi_root, &k->hi_cw[0][0], k->hi_leaf);
+            out |= ((b & 1) ^ k->hi_mu) | ((((b >> 1) & 1) ^ k->hi_mu_eq) << 2);
+        } else {
+            out |= (ref_dcf_eval(n - 1, xhat & (M >> 1), k->hi_root, &k->hi_cw[0][0], k->hi_leaf) ^ k->hi_mu) & 1;
+        }
+    }
     if (ref_gate_has_lo(kind))
         out |= ((ref_dcf_eval(s, xhat & ((1ULL << s) - 1), k->lo_root, &k->lo_cw[0][0], k->lo_leaf) ^ k->lo_mu) & 1)
                << 1;
     return out;
 }
 
-/* round 2: party's additive share of the masked output, given the opened bits */
-uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int c_hat, int cl_hat,
-                         const ref_gate_key *k)
+/* round 2: party's additive share of the masked output, given the opened bits
+ * (bit0 = c_hat, bit1 = cL_hat, bit2 = e_hat) */
+uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int bits, const ref_gate_key *k)
 {
     uint64_t M = nmask(n);
     xhat &= M;
@@ -415,11 +528,16 @@ uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int c
     uint64_t xH = xhat >> s;
     uint64_t two_ns = 1ULL << (n - s); /* n - s < 64 */
     const uint64_t *w = k->w;
-    uint64_t q = 1 ^ mh ^ (uint64_t)c_hat;   /* public part of DReLU */
+    uint64_t ch = (uint64_t)(bits & 1), cl = (uint64_t)((bits >> 1) & 1), eh = (uint64_t)((bits >> 2) & 1);
+    uint64_t q = 1 ^ mh ^ ch;                 /* public part of DReLU */
     uint64_t a1 = 1 - 2 * q;                  /* 1 - 2q  (mod 2^n) */
-    uint64_t cl = (uint64_t)cl_hat;
     uint64_t b1 = 1 - 2 * cl;                 /* 1 - 2*cL_hat */
     uint64_t y = 0;
+    /* split gates: DReLU = a0 + sum_k a[k] * mono[k] (see ref_gate_keygen) */
+    uint64_t su = 1 - 2 * q, se = 1 - 2 * eh, sc = 1 - 2 * cl;
+    uint64_t G0 = eh * cl, GL = eh * sc, Ge = cl * se, GeL = se * sc;
+    uint64_t a0 = q + su * G0;
+    uint64_t a[7] = {su * (1 - 2 * G0), su * GL, su * Ge, su * GeL, 0 - 2 * su * GL, 0 - 2 * su * Ge, 0 - 2 * su * GeL};
     switch (kind) {
     case GATE_RELU:
         y = p0 * q * xhat + a1 * xhat * w[0] - q * w[1] - a1 * w[2] + w[3];
@@ -429,11 +547,27 @@ uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int c
             a1 * b1 * w[4] + two_ns * (1 - mh) * (q * w[5] + a1 * w[6]) + w[7];
         break;
     case GATE_ARS: {
-        uint64_t ch = (uint64_t)c_hat;
         uint64_t pub = xH - cl + two_ns * (mh * ch - mh);
         y = p0 * pub - w[0] - b1 * w[1] +
             two_ns * (mh * (1 - 2 * ch) * w[2] + ((1 - 2 * mh) * ch + mh) * w[3] + (1 - 2 * mh) * (1 - 2 * ch) * w[4]) +
             w[5];
+        break;
+    }
+    case GATE_RELU_SPLIT: {
+        uint64_t sx = 0, sr = 0;
+        for (int t = 0; t < 7; t++) sx += a[t] * w[t], sr += a[t] * w[8 + t];
+        y = p0 * a0 * xhat + xhat * sx - a0 * w[7] - sr + w[15];
+        break;
+    }
+    case GATE_RELU_ARS_SPLIT: {
+        uint64_t Y0 = xH - cl;
+        uint64_t yj[3] = {0 - 1, 0 - sc, two_ns * (1 - mh)};
+        uint64_t sm = 0, sn = 0, smn = 0;
+        for (int t = 0; t < 7; t++) sm += a[t] * w[t];
+        for (int j = 0; j < 3; j++) sn += yj[j] * w[7 + j];
+        for (int t = 0; t < 7; t++)
+            for (int j = 0; j < 3; j++) smn += a[t] * yj[j] * w[10 + 3 * t + j];
+        y = p0 * a0 * Y0 + Y0 * sm + a0 * sn + smn + w[31];
         break;
     }
     default:

@@ -21,8 +21,10 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "libfss_ref.so")
 
-GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS = 0, 1, 2, 3
-GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4}
+GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT = 0, 1, 2, 3, 4, 5
+GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4, GATE_RELU_SPLIT: 16,
+               GATE_RELU_ARS_SPLIT: 32}
+SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT)
 
 
 def build() -> str:
@@ -38,11 +40,12 @@ class GateKey(ctypes.Structure):
         ("hi_cw", (ctypes.c_uint8 * 16) * 56),
         ("hi_leaf", ctypes.c_uint8 * 16),
         ("hi_mu", ctypes.c_int32),
+        ("hi_mu_eq", ctypes.c_int32),
         ("lo_root", ctypes.c_uint8 * 16),
         ("lo_cw", (ctypes.c_uint8 * 16) * 56),
         ("lo_leaf", ctypes.c_uint8 * 16),
         ("lo_mu", ctypes.c_int32),
-        ("w", ctypes.c_uint64 * 8),
+        ("w", ctypes.c_uint64 * 32),
     ]
 
 
@@ -84,7 +87,10 @@ def lib():
                                       ctypes.POINTER(GateKey)]
         L.ref_gate_round1.restype = ctypes.c_int
         L.ref_gate_round2.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
-                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(GateKey)]
+                                      ctypes.c_int, ctypes.POINTER(GateKey)]
+        L.ref_dcfeq_keygen.argtypes = [ctypes.c_int, ctypes.c_uint64, u8p, u8p, u8p, u8p, u8p, u8p]
+        L.ref_dcfeq_eval.argtypes = [ctypes.c_int, ctypes.c_uint64, u8p, u8p, u8p]
+        L.ref_dcfeq_eval.restype = ctypes.c_int
         L.ref_gate_round2.restype = ctypes.c_uint64
         L.ref_lut_keygen.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64,
                                      ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(LutKey),
@@ -142,6 +148,20 @@ def dcf_eval(d: int, x: int, root: bytes, cw: bytes, leaf: bytes) -> int:
     return lib().ref_dcf_eval(d, x, _buf(root), _buf(cw if cw else b"\0" * 16), _buf(leaf))
 
 
+def dcfeq_keygen(d: int, alpha: int, s0: bytes, delta: bytes):
+    L = d - 6
+    r0, r1 = (ctypes.c_uint8 * 16)(), (ctypes.c_uint8 * 16)()
+    cw = (ctypes.c_uint8 * (16 * max(L, 1)))()
+    leaf = (ctypes.c_uint8 * 16)()
+    lib().ref_dcfeq_keygen(d, alpha, _buf(s0), _buf(delta), r0, r1, cw, leaf)
+    return bytes(r0), bytes(r1), bytes(cw)[: 16 * L], bytes(leaf)
+
+
+def dcfeq_eval(d: int, x: int, root: bytes, cw: bytes, leaf: bytes) -> int:
+    """party's shares: bit0 of 1{x < alpha}, bit1 of 1{x == alpha}"""
+    return lib().ref_dcfeq_eval(d, x, _buf(root), _buf(cw if cw else b"\0" * 16), _buf(leaf))
+
+
 def gate_keygen(kind: int, n: int, s: int, seed: int, op: int, i: int, r_in: int):
     k0, k1 = GateKey(), GateKey()
     r_out = lib().ref_gate_keygen(kind, n, s, seed, op, i, r_in, ctypes.byref(k0), ctypes.byref(k1))
@@ -152,8 +172,9 @@ def gate_round1(kind: int, n: int, s: int, xhat: int, key: GateKey) -> int:
     return lib().ref_gate_round1(kind, n, s, xhat, ctypes.byref(key))
 
 
-def gate_round2(kind: int, n: int, s: int, party: int, xhat: int, c_hat: int, cl_hat: int, key: GateKey) -> int:
-    return lib().ref_gate_round2(kind, n, s, party, xhat, c_hat, cl_hat, ctypes.byref(key))
+def gate_round2(kind: int, n: int, s: int, party: int, xhat: int, bits: int, key: GateKey) -> int:
+    """bits: opened round-1 bits, bit0 = high compare, bit1 = low compare, bit2 = high equality."""
+    return lib().ref_gate_round2(kind, n, s, party, xhat, bits, ctypes.byref(key))
 
 
 def gate_eval_pair(kind: int, n: int, s: int, xhat: int, k0: GateKey, k1: GateKey) -> int:
@@ -161,8 +182,8 @@ def gate_eval_pair(kind: int, n: int, s: int, xhat: int, k0: GateKey, k1: GateKe
     b0 = gate_round1(kind, n, s, xhat, k0)
     b1 = gate_round1(kind, n, s, xhat, k1)
     o = b0 ^ b1
-    y0 = gate_round2(kind, n, s, 0, xhat, o & 1, (o >> 1) & 1, k0)
-    y1 = gate_round2(kind, n, s, 1, xhat, o & 1, (o >> 1) & 1, k1)
+    y0 = gate_round2(kind, n, s, 0, xhat, o, k0)
+    y1 = gate_round2(kind, n, s, 1, xhat, o, k1)
     return (y0 + y1) & ((1 << n) - 1)
 
 
@@ -187,6 +208,6 @@ def gate_key_bytes(key: GateKey) -> dict:
     """Flatten one element's key into the SoA fields the CUDA layout stores."""
     return {
         "hi_root": bytes(key.hi_root), "hi_cw": bytes(key.hi_cw), "hi_leaf": bytes(key.hi_leaf),
-        "hi_mu": key.hi_mu, "lo_root": bytes(key.lo_root), "lo_cw": bytes(key.lo_cw),
+        "hi_mu": key.hi_mu, "hi_mu_eq": key.hi_mu_eq, "lo_root": bytes(key.lo_root), "lo_cw": bytes(key.lo_cw),
         "lo_leaf": bytes(key.lo_leaf), "lo_mu": key.lo_mu, "w": list(key.w),
     }

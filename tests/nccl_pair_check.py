@@ -1,0 +1,63 @@
+"""Two-rank check of the NCCL channel: party 0 on rank 0, party 1 on rank 1.
+
+Launched with torchrun (see tests/test_multigpu_gpu.py).  Both ranks run the
+GPU dealer with the same seed (so they hold matching keys), take their own
+party's shares of the same seeded inputs, open every value over NCCL
+send/recv, and rank 0 compares the revealed outputs with the integer oracle.
+Exits non-zero on any mismatch.
+"""
+import datetime
+import importlib
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, REPO)
+
+
+def main():
+    from oracle import ring_forward as RF
+
+    ddg = importlib.import_module("idash26-track3_b200")
+    synth = importlib.import_module("idash26-track3_b200.synth")
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    assert world == 2
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    bw, B, s = int(os.environ.get("DDG_CHECK_BW", "32")), 3, 12
+    q = synth.quantize_weights(synth.affinity_weights(5), s)
+    blob = synth.weights_blob(q)
+    kb = ddg.forward_key_bytes(bw, s, B)
+    k0 = torch.empty(kb, dtype=torch.uint8, device=dev)
+    k1 = torch.empty(kb, dtype=torch.uint8, device=dev)
+    ddg.dealer_forward(bw, s, B, 31, blob, local, k0.data_ptr(), k1.data_ptr())
+    inp = synth.Inputs(B, bw, seed=44, with_protein_cnn=False)
+    P = ddg.Party(rank, bw, s, local)
+    P.set_weights(blob)
+    P.bind_keys((k0 if rank == 0 else k1).data_ptr(), kb)
+    uid = [ddg.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    P.connect_nccl(uid[0], 2, rank, 1 - rank)
+    bufs = [torch.from_numpy(np.ascontiguousarray(a[rank]).view(np.uint8).copy()).to(dev)
+            for a in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)]
+    for _ in range(2):
+        raw, aff = P.forward(B, *[b.data_ptr() for b in bufs])
+    ok = 1
+    if rank == 0:
+        want_raw, want_aff = RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, s)
+        ok = int(np.array_equal(aff, want_aff))
+        print("nccl pair", "OK" if ok else f"MISMATCH {aff} vs {want_aff}", P.stats(), flush=True)
+    flag = torch.tensor([ok])
+    dist.broadcast(flag, src=0)
+    P.close()
+    dist.destroy_process_group()
+    sys.exit(0 if int(flag.item()) else 1)
+
+
+if __name__ == "__main__":
+    main()

@@ -14,14 +14,14 @@ from oracle.ring_forward import Ring
 from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 
 S = 12
-KINDS = [F.GATE_RELU, F.GATE_RELU_ARS, F.GATE_ARS, F.GATE_LRS]
+KINDS = [F.GATE_RELU, F.GATE_RELU_ARS, F.GATE_ARS, F.GATE_LRS, F.GATE_RELU_SPLIT, F.GATE_RELU_ARS_SPLIT]
 
 
 def plain(kind, x, bw):
     R = Ring(bw)
-    if kind == F.GATE_RELU:
+    if kind in (F.GATE_RELU, F.GATE_RELU_SPLIT):
         return R.relu(x)
-    if kind == F.GATE_RELU_ARS:
+    if kind in (F.GATE_RELU_ARS, F.GATE_RELU_ARS_SPLIT):
         return R.relu_ars(x, S)
     if kind == F.GATE_ARS:
         return R.ars(x, S)
@@ -48,6 +48,13 @@ def make_inputs(bw, kind, n, seed):
     x[: min(len(b), n)] = np.array(b[: min(len(b), n)], dtype=dt)
     r = rng.integers(0, hi, size=n, dtype=dt, endpoint=True)
     r[:4] = np.array([0, hi, 1 << (bw - 1), (1 << S) - 1][: min(4, n)], dtype=dt)[: min(4, n)]
+    # every 5th element: x_hat agrees with r on the bits above the low `S` (split-compare equality branch)
+    sel = np.arange(n) % 5 == 4
+    lowmask = dt((1 << S) - 1)
+    xh = (r & ~lowmask) | (rng.integers(0, 1 << S, size=n, dtype=dt) & lowmask)
+    x[sel] = (xh - r).astype(dt)[sel]
+    if kind == F.GATE_LRS:
+        x &= dt(hi >> 1)
     return x, r
 
 
@@ -60,7 +67,7 @@ def run_gate(ddg, kind, bw, n, x, r, seed=5, op=3):
     xh = (x + r).astype(dt)
     d_x = to_dev(xh)
     words = (n + 31) // 32
-    bits = {(p, h): dev_bytes(4 * words) for p in (0, 1) for h in ("hi", "lo")}
+    bits = {(p, h): dev_bytes(8 * words) for p in (0, 1) for h in ("hi", "lo")}
     for p, k in ((0, k0), (1, k1)):
         ddg.gate_round1(kind, bw, S, n, ptr(d_x), ptr(k), ptr(bits[p, "hi"]), ptr(bits[p, "lo"]))
     shares = [dev_bytes(n * (bw // 8)) for _ in range(2)]
@@ -72,7 +79,7 @@ def run_gate(ddg, kind, bw, n, x, r, seed=5, op=3):
 
     torch.cuda.synchronize()
     return dict(k0=k0.cpu().numpy(), k1=k1.cpu().numpy(), rout=from_dev(d_ro, dt, n),
-                bits={kk: from_dev(v, np.uint32, words) for kk, v in bits.items()},
+                bits={kk: from_dev(v, np.uint32, 2 * words) for kk, v in bits.items()},
                 y0=from_dev(shares[0], dt, n), y1=from_dev(shares[1], dt, n), xh=xh)
 
 
@@ -88,7 +95,9 @@ def key_fields(blob, lay, n, e, bw):
                       for j in range(L))
         leaf = blob[lay[f"{side}_leaf"] + 16 * e: lay[f"{side}_leaf"] + 16 * e + 16].tobytes()
         mu = (int(blob[lay[f"{side}_mu"]:].view(np.uint32)[e // 32]) >> (e % 32)) & 1
-        f[side] = (root, cw, leaf, mu)
+        mu_eq = (int(blob[lay["hi_mu_eq"]:].view(np.uint32)[e // 32]) >> (e % 32)) & 1 if (
+            side == "hi" and lay["hi_mu_eq"]) else 0
+        f[side] = (root, cw, leaf, mu, mu_eq)
     return f
 
 
@@ -114,6 +123,7 @@ def test_gate_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
                 L = lay["hi_levels"]
                 assert g["hi"][0] == rb["hi_root"] and g["hi"][1] == rb["hi_cw"][: 16 * L]
                 assert g["hi"][2] == rb["hi_leaf"] and g["hi"][3] == rb["hi_mu"]
+                assert g["hi"][4] == (rb["hi_mu_eq"] if kind in F.SPLIT_KINDS else 0)
             if "lo" in g:
                 L = lay["lo_levels"]
                 assert g["lo"][0] == rb["lo_root"] and g["lo"][1] == rb["lo_cw"][: 16 * L]
@@ -122,14 +132,17 @@ def test_gate_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
             assert int(w0[wi * n + e]) == k0.w[wi] and int(w1[wi * n + e]) == k1.w[wi]
         b0 = F.gate_round1(kind, bw, S, int(out["xh"][e]), k0)
         b1 = F.gate_round1(kind, bw, S, int(out["xh"][e]), k1)
+        words = (n + 31) // 32
         for p, bb in ((0, b0), (1, b1)):
             if kind != F.GATE_LRS:
                 assert (int(out["bits"][p, "hi"][e // 32]) >> (e % 32)) & 1 == bb & 1
+            if kind in F.SPLIT_KINDS:
+                assert (int(out["bits"][p, "hi"][words + e // 32]) >> (e % 32)) & 1 == (bb >> 2) & 1
             if kind != F.GATE_RELU:
                 assert (int(out["bits"][p, "lo"][e // 32]) >> (e % 32)) & 1 == (bb >> 1) & 1
         o = b0 ^ b1
-        assert int(out["y0"][e]) == F.gate_round2(kind, bw, S, 0, int(out["xh"][e]), o & 1, (o >> 1) & 1, k0)
-        assert int(out["y1"][e]) == F.gate_round2(kind, bw, S, 1, int(out["xh"][e]), o & 1, (o >> 1) & 1, k1)
+        assert int(out["y0"][e]) == F.gate_round2(kind, bw, S, 0, int(out["xh"][e]), o, k0)
+        assert int(out["y1"][e]) == F.gate_round2(kind, bw, S, 1, int(out["xh"][e]), o, k1)
     y = (out["y0"] + out["y1"] - out["rout"]).astype(dt)
     assert np.array_equal(y, plain(kind, x, bw))
 
