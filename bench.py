@@ -60,7 +60,13 @@ def parse():
     ap.add_argument("--scale", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
+                    help="streaming regime (BASELINE configs[4]): keys of NCHUNKS forwards per party live in pinned "
+                         "host memory and are streamed into HBM through the double-buffered key stream, cyclically")
+    a = ap.parse_args()
+    if a.stream and a.batch == 256:
+        a.batch = 64  # one chunk per party is ~6.4 GB at bw=32
+    return a
 
 
 def measured_peaks():
@@ -74,6 +80,14 @@ def measured_peaks():
 
 def config_of(a, n_gpus):
     pairs = max(n_gpus // 2, 1)
+    if a.stream:
+        return {
+            "workload": f"streaming regime (BASELINE configs[4]): full affinity branch, bw={a.bw}, scale={a.scale}, "
+                        f"B={a.batch} per pair per step, keys streamed host->HBM every step from a ring of "
+                        f"{a.stream} pinned chunks per party (timing-only key reuse)",
+            "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs, "stream_chunks": a.stream,
+            "parallelism": "1 GPU, both parties" if n_gpus == 1 else f"{pairs} party pairs over NCCL, one party per GPU",
+            "l2": "inputs larger than L2: every step copies and streams a full key chunk per party"}
     return {
         "workload": f"full affinity branch (adj-norm, GCNx3, masked max-pool, FC head), bw={a.bw}, scale={a.scale}, "
                     f"B={a.batch} davis-shaped synthetic graphs per pair, keys resident in HBM (BASELINE configs[2])",
@@ -233,28 +247,47 @@ def main():
     blob = synth.weights_blob(synth.quantize_weights(synth.affinity_weights(5), s))
 
     # -------- parties, keys, inputs
+    streams = []
     if world == 1:
         pairs, pair = 1, 0
-        kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000, blob, device)
         inp = synth.Inputs(B, bw, seed=1000)
         parties = [ddg.Party(0, bw, s, local), ddg.Party(1, bw, s, local)]
-        for p, k in zip(parties, (k0, k1)):
-            p.set_weights(blob)
-            p.bind_keys(k.data_ptr(), kb)
+        if a.stream:
+            kb = ddg.forward_key_bytes(bw, s, B)
+            chunks = ddg.dealer_chunks(bw, s, B, [1000 + i for i in range(a.stream)], blob, local)
+            for p in parties:
+                p.set_weights(blob)
+            streams = [ddg.KeyStream(p, B) for p in parties]
+            for c in chunks:
+                for ks, h in zip(streams, c):
+                    ks.add_host_chunk(h.data_ptr())
+        else:
+            kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000, blob, device)
+            for p, k in zip(parties, (k0, k1)):
+                p.set_weights(blob)
+                p.bind_keys(k.data_ptr(), kb)
         ddg.pair_local(parties[0], parties[1])
         bufs = [share_buffers(torch, inp, p, device) for p in (0, 1)]
     else:
         pairs = world // 2
         pair, party = rank % pairs, rank // pairs
         peer = rank + pairs if party == 0 else rank - pairs
-        kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000 + pair, blob, device)
-        mine = k0 if party == 0 else k1
-        del k0, k1
-        torch.cuda.empty_cache()
         inp = synth.Inputs(B, bw, seed=1000 + pair)
         P = ddg.Party(party, bw, s, local)
         P.set_weights(blob)
-        P.bind_keys(mine.data_ptr(), kb)
+        if a.stream:
+            kb = ddg.forward_key_bytes(bw, s, B)
+            chunks = ddg.dealer_chunks(bw, s, B, [1000 + 97 * pair + i for i in range(a.stream)], blob, local)
+            streams = [ddg.KeyStream(P, B)]
+            for c in chunks:
+                streams[0].add_host_chunk(c[party].data_ptr())
+            chunks = [(c[party],) for c in chunks]
+        else:
+            kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000 + pair, blob, device)
+            mine = k0 if party == 0 else k1
+            del k0, k1
+            torch.cuda.empty_cache()
+            P.bind_keys(mine.data_ptr(), kb)
         uid = [ddg.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         P.connect_nccl(uid[0], world, rank, peer)
@@ -265,8 +298,12 @@ def main():
     def step(on_host):
         if world == 1:
             ins = [[t.data_ptr() for t in (bufs[p][1] if on_host else bufs[p][0])] for p in (0, 1)]
+            if streams:
+                return ddg.forward_pair_streamed(streams[0], streams[1], ins[0], ins[1], on_host=on_host)
             return ddg.forward_pair(parties[0], parties[1], B, ins[0], ins[1], on_host=on_host)
         ins = [t.data_ptr() for t in (bufs[0][1] if on_host else bufs[0][0])]
+        if streams:
+            return streams[0].forward(*ins, on_host=on_host)
         return parties[0].forward(B, *ins, on_host=on_host)
 
     stream = torch.cuda.ExternalStream(parties[0].stream, device=device)
@@ -291,6 +328,7 @@ def main():
 
     for _ in range(a.warmup):
         step(False)
+    ks_before = [ks.stats() for ks in streams]
     for p in parties:
         p.enable_dcf_timing(True)
     clocks = Clocks(local)
@@ -301,6 +339,15 @@ def main():
     clk = clocks.stop()
     stats = parties[0].stats()
     dcf = [p.dcf_timing() for p in parties]
+    stream_info = None
+    if streams:
+        after = [ks.stats() for ks in streams]
+        copied = sum(x["bytes"] - y["bytes"] for x, y in zip(after, ks_before))
+        copy_ms = sum(x["copy_ms"] - y["copy_ms"] for x, y in zip(after, ks_before))
+        stream_info = {"chunk_bytes": ddg.key_chunk_bytes(bw, s, B), "chunks_per_party": a.stream,
+                       "h2d_bytes_per_step_per_gpu": copied / a.steps,
+                       "h2d_gbs_during_copies": copied / (copy_ms / 1e3) / 1e9 if copy_ms else None,
+                       "h2d_gbs_over_step": copied / (ms / 1e3) / 1e9}
     for p in parties:
         p.enable_dcf_timing(False)
 
@@ -359,8 +406,10 @@ def main():
                          "bytes_per_sample": 2 * stats["bytes_sent"] / B,
                          # emulated LAN, full duplex: each party's bytes at 1 Gbps + one 1 ms RTT per opening
                          "lan_1gbps_1ms_rtt_s_per_step": stats["bytes_sent"] * 8 / 1e9 + stats["rounds"] * 1e-3},
-                "key_bytes_per_party_per_step": kb}
+                "key_bytes_per_party_per_step": kb, "stream": stream_info}
         print(json.dumps(line), flush=True)
+    for ks in streams:
+        ks.close()
     for p in parties:
         p.close()
     if dist:

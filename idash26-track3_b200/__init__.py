@@ -67,6 +67,19 @@ SIGNATURES = {
     "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
     "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
     "ddg_launch_count": (_u64, []),
+    "ddg_key_chunk_bytes": (_u64, [_i32, _i32, _i32]),
+    "ddg_key_checksum": (_i32, [_vp, _u64, ctypes.POINTER(_u64), _vp]),
+    "ddg_key_chunk_seal": (_i32, [_vp, _i32, _i32, _i32, _u64, _vp]),
+    "ddg_key_chunk_verify": (_i32, [_vp, _i32, _i32, _i32, ctypes.POINTER(_u64), _vp]),
+    "ddg_keystream_create": (_i32, [ctypes.POINTER(_vp), _vp, _i32]),
+    "ddg_keystream_destroy": (_i32, [_vp]),
+    "ddg_keystream_add_host_chunk": (_i32, [_vp, _vp]),
+    "ddg_keystream_open_file": (_i32, [_vp, ctypes.c_char_p, _i32]),
+    "ddg_keystream_set_verify": (_i32, [_vp, _i32]),
+    "ddg_keystream_stats": (_i32, [_vp, ctypes.POINTER(ctypes.c_double)]),
+    "ddg_forward_eval_streamed": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
+    "ddg_forward_eval_pair_streamed": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp,
+                                              _vp]),
     "ddg_party_enable_dcf_timing": (_i32, [_vp, _i32]),
     "ddg_party_dcf_timing": (_i32, [_vp, ctypes.POINTER(ctypes.c_double)]),
 }
@@ -232,3 +245,109 @@ def forward_pair(p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
 
 def launch_count() -> int:
     return int(lib().ddg_launch_count())
+
+
+# ---------------------------------------------------------------- key chunks / streaming
+
+def key_chunk_bytes(bw: int, scale: int, batch: int) -> int:
+    return int(lib().ddg_key_chunk_bytes(bw, scale, batch))
+
+
+def key_chunk_seal(d_chunk: int, bw: int, scale: int, batch: int, index: int, stream=None):
+    check(lib().ddg_key_chunk_seal(d_chunk, bw, scale, batch, index, stream))
+
+
+def key_chunk_verify(d_chunk: int, bw: int, scale: int, batch: int, stream=None) -> int:
+    idx = _u64()
+    check(lib().ddg_key_chunk_verify(d_chunk, bw, scale, batch, ctypes.byref(idx), stream))
+    return int(idx.value)
+
+
+class KeyStream:
+    """Double-buffered key feed of one party (chunks in pinned host memory or a key file)."""
+
+    def __init__(self, party: Party, batch: int):
+        h = _vp()
+        check(lib().ddg_keystream_create(ctypes.byref(h), party.h, batch))
+        self.h, self.party, self.batch = h, party, batch
+
+    def add_host_chunk(self, h_ptr: int):
+        check(lib().ddg_keystream_add_host_chunk(self.h, h_ptr))
+
+    def open_file(self, path: str, nchunks: int):
+        check(lib().ddg_keystream_open_file(self.h, path.encode(), nchunks))
+
+    def set_verify(self, on: bool = True):
+        check(lib().ddg_keystream_set_verify(self.h, int(on)))
+
+    def stats(self) -> dict:
+        out = (ctypes.c_double * 5)()
+        check(lib().ddg_keystream_stats(self.h, out))
+        return dict(zip(("chunks", "bytes", "copy_ms", "read_ms", "wait_ms"), [float(v) for v in out]))
+
+    def forward(self, x, adj, mask, prot, on_host=False):
+        import numpy as np
+
+        raw = np.zeros(self.batch, dtype=np.int64)
+        aff = np.zeros(self.batch, dtype=np.float64)
+        check(lib().ddg_forward_eval_streamed(self.h, self.batch, x, adj, mask, prot, int(on_host), raw.ctypes.data,
+                                              aff.ctypes.data))
+        return (raw, aff) if self.party.party == 0 else (None, None)
+
+    def close(self):
+        if self.h:
+            lib().ddg_keystream_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def forward_pair_streamed(ks0: KeyStream, ks1: KeyStream, inputs0, inputs1, on_host=False):
+    import numpy as np
+
+    B = ks0.batch
+    a0 = (_vp * 4)(*inputs0)
+    a1 = (_vp * 4)(*inputs1)
+    raw = np.zeros(B, dtype=np.int64)
+    aff = np.zeros(B, dtype=np.float64)
+    check(lib().ddg_forward_eval_pair_streamed(ks0.h, ks1.h, B, a0, a1, int(on_host), raw.ctypes.data,
+                                               aff.ctypes.data))
+    return raw, aff
+
+
+def dealer_chunks(bw: int, scale: int, batch: int, seeds, weights_blob, device: int = 0):
+    """GPU dealer -> sealed key chunks of both parties in pinned host memory.
+
+    Returns [(chunk0, chunk1)] per seed: torch uint8 pinned tensors of
+    key_chunk_bytes(bw, scale, batch) bytes, chunk index = position in `seeds`."""
+    import torch
+
+    cb = key_chunk_bytes(bw, scale, batch)
+    kb = forward_key_bytes(bw, scale, batch)
+    dev = torch.device("cuda", device)
+    d0 = torch.empty(cb, dtype=torch.uint8, device=dev)
+    d1 = torch.empty(cb, dtype=torch.uint8, device=dev)
+    out = []
+    for i, seed in enumerate(seeds):
+        dealer_forward(bw, scale, batch, seed, weights_blob, device, d0.data_ptr(), d1.data_ptr())
+        pair = []
+        for d in (d0, d1):
+            key_chunk_seal(d.data_ptr(), bw, scale, batch, i)
+            h = torch.empty(cb, dtype=torch.uint8, pin_memory=True)
+            h.copy_(d)
+            pair.append(h)
+        out.append(tuple(pair))
+    assert kb <= cb
+    return out
+
+
+def write_key_file(path: str, chunks) -> None:
+    """Chunks back to back (chunk k at k * key_chunk_bytes), as the reference's
+    dealer pwrites them (deepdtagen_inference.cu:383-398)."""
+    with open(path, "wb") as f:
+        for c in chunks:
+            f.write(c.numpy().tobytes())

@@ -6,6 +6,7 @@
 #include "channel.cuh"
 #include "forward.cuh"
 #include "gates.cuh"
+#include "keystream.cuh"
 
 using namespace ddg;
 
@@ -246,6 +247,127 @@ int ddg_party_dcf_timing(ddg_party *h, double *out6)
 }
 
 uint64_t ddg_launch_count(void) { return launch_count(); }
+
+// ------------------------------------------------------------ key chunks / streaming
+
+struct ddg_keystream {
+    KeyStream ks;
+};
+
+uint64_t ddg_key_chunk_bytes(int bw, int scale, int batch)
+{
+    if (check_gate_args(0, bw, scale) != DDG_OK || batch <= 0) return 0;
+    return key_chunk_bytes(bw, scale, batch);
+}
+
+int ddg_key_checksum(const void *d_key, uint64_t bytes, uint64_t *out, void *stream)
+{
+    DDG_CHECK(d_key && out, DDG_ERR_ARG, "null argument");
+    return key_checksum(d_key, bytes, out, static_cast<cudaStream_t>(stream));
+}
+
+int ddg_key_chunk_seal(void *d_chunk, int bw, int scale, int batch, uint64_t chunk_index, void *stream)
+{
+    DDG_TRY(check_gate_args(0, bw, scale));
+    DDG_CHECK(d_chunk && batch > 0, DDG_ERR_ARG, "bad argument");
+    return chunk_seal(d_chunk, bw, scale, batch, chunk_index, static_cast<cudaStream_t>(stream));
+}
+
+int ddg_key_chunk_verify(const void *d_chunk, int bw, int scale, int batch, uint64_t *chunk_index, void *stream)
+{
+    DDG_TRY(check_gate_args(0, bw, scale));
+    DDG_CHECK(d_chunk && batch > 0, DDG_ERR_ARG, "bad argument");
+    ChunkTrailer t;
+    DDG_TRY(chunk_verify(d_chunk, bw, scale, batch, &t, static_cast<cudaStream_t>(stream)));
+    if (chunk_index) *chunk_index = t.index;
+    return DDG_OK;
+}
+
+int ddg_keystream_create(ddg_keystream **out, ddg_party *party, int batch)
+{
+    DDG_CHECK(out && party && batch > 0, DDG_ERR_ARG, "bad argument");
+    auto *h = new ddg_keystream();
+    int st = h->ks.init(&party->P, batch);
+    if (st != DDG_OK) {
+        delete h;
+        return st;
+    }
+    *out = h;
+    return DDG_OK;
+}
+
+int ddg_keystream_destroy(ddg_keystream *ks)
+{
+    delete ks;
+    return DDG_OK;
+}
+
+int ddg_keystream_add_host_chunk(ddg_keystream *ks, const void *h_chunk)
+{
+    DDG_CHECK(ks && h_chunk, DDG_ERR_ARG, "null argument");
+    DDG_CHECK(ks->ks.fd < 0, DDG_ERR_STATE, "key stream already reads a key file");
+    ks->ks.host.push_back(h_chunk);
+    return DDG_OK;
+}
+
+int ddg_keystream_open_file(ddg_keystream *ks, const char *path, int nchunks)
+{
+    DDG_CHECK(ks && path, DDG_ERR_ARG, "null argument");
+    return ks->ks.open_file(path, nchunks);
+}
+
+int ddg_keystream_set_verify(ddg_keystream *ks, int on)
+{
+    DDG_CHECK(ks, DDG_ERR_ARG, "null argument");
+    ks->ks.verify = on != 0;
+    return DDG_OK;
+}
+
+int ddg_keystream_stats(ddg_keystream *ks, double *out5)
+{
+    DDG_CHECK(ks && out5, DDG_ERR_ARG, "null argument");
+    double v[5] = {double(ks->ks.consumed_chunks), ks->ks.bytes_copied, ks->ks.copy_ms, ks->ks.read_ms,
+                   ks->ks.wait_ms};
+    for (int i = 0; i < 5; i++) out5[i] = v[i];
+    return DDG_OK;
+}
+
+int ddg_forward_eval_streamed(ddg_keystream *ks, int batch, const void *x_share, const void *adj_share,
+                              const void *mask_share, const void *protein_share, int on_host, int64_t *h_out_raw,
+                              double *h_affinity)
+{
+    DDG_CHECK(ks && batch == ks->ks.B, DDG_ERR_ARG, "key stream was created for batch %d", ks ? ks->ks.B : 0);
+    int st = ks->ks.begin_forward();
+    if (st == DDG_OK)
+        st = forward_eval(*ks->ks.P, batch, x_share, adj_share, mask_share, protein_share, on_host != 0, h_out_raw,
+                          h_affinity);
+    else if (auto *lp = dynamic_cast<LocalPairChannel *>(ks->ks.P->chan))
+        lp->fail();
+    return ks->ks.end_forward(st);
+}
+
+int ddg_forward_eval_pair_streamed(ddg_keystream *ks0, ddg_keystream *ks1, int batch, const void *const *in0,
+                                   const void *const *in1, int on_host, int64_t *h_out_raw, double *h_affinity)
+{
+    DDG_CHECK(ks0 && ks1 && in0 && in1, DDG_ERR_ARG, "null argument");
+    int st1 = DDG_OK;
+    std::string err1;
+    std::thread t([&] {
+        st1 = ddg_forward_eval_streamed(ks1, batch, in1[0], in1[1], in1[2], in1[3], on_host, nullptr, nullptr);
+        if (st1 != DDG_OK) err1 = ddg::last_error();
+    });
+    int st0 = ddg_forward_eval_streamed(ks0, batch, in0[0], in0[1], in0[2], in0[3], on_host, h_out_raw, h_affinity);
+    if (st0 != DDG_OK) {
+        if (auto *lp = dynamic_cast<LocalPairChannel *>(ks0->ks.P->chan)) lp->fail();
+    }
+    t.join();
+    if (st0 == DDG_OK && st1 != DDG_OK) {
+        set_last_error("party 1: %s", err1.c_str());
+        return st1;
+    }
+    if (st0 == DDG_OK) st0 = pair_dcf_union(*ks0->ks.P, *ks1->ks.P);
+    return st0;
+}
 
 int ddg_dealer_forward(int bw, int scale, int batch, uint64_t seed, const int64_t *h_weights, uint64_t n_weights,
                        int device, void *d_key0, void *d_key1, void *stream)

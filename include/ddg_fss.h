@@ -169,6 +169,47 @@ int ddg_dealer_forward(int bw, int scale, int batch, uint64_t seed, const int64_
                        int device, void *d_key0, void *d_key1, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Key chunks and streaming (replaces the chunked key file and the streaming
+ * evaluation of deepdtagen_inference.cu:344-416 and :608-826: 4 KiB-padded
+ * chunks, 2 pinned + 2 device slots, a copy stream and events).
+ *
+ * A chunk is one forward's key region + zero padding + a 64-byte trailer
+ * (magic "DDGKEY01", bw, scale, batch, chunk index, key bytes, checksum),
+ * ddg_key_chunk_bytes long (a multiple of 4 KiB).  A key file is chunks
+ * back to back; chunk k starts at k * ddg_key_chunk_bytes.
+ * ---------------------------------------------------------------------- */
+uint64_t ddg_key_chunk_bytes(int bw, int scale, int batch);
+/* position-keyed 64-bit sum of the 8-byte words of a device buffer */
+int ddg_key_checksum(const void *d_key, uint64_t bytes, uint64_t *out, void *stream);
+/* write the trailer (with the checksum) into a device chunk whose first
+ * ddg_forward_key_bytes hold a dealer's key region */
+int ddg_key_chunk_seal(void *d_chunk, int bw, int scale, int batch, uint64_t chunk_index, void *stream);
+/* DDG_ERR_KEY if the trailer is missing, for other parameters, or the checksum differs */
+int ddg_key_chunk_verify(const void *d_chunk, int bw, int scale, int batch, uint64_t *chunk_index, void *stream);
+
+/* A key stream feeds one party's forwards from chunks outside HBM: two
+ * device slots; before forward k the copy of chunk k+1 is queued on the
+ * stream's own copy stream, behind the forward that last used its slot, so it
+ * runs during forward k.  Sources: pinned host chunks (used cyclically in the
+ * order added) or a key file of nchunks chunks read cyclically by an I/O
+ * thread (pread into two pinned staging buffers). */
+typedef struct ddg_keystream ddg_keystream;
+int ddg_keystream_create(ddg_keystream **out, ddg_party *party, int batch);
+int ddg_keystream_destroy(ddg_keystream *ks);
+int ddg_keystream_add_host_chunk(ddg_keystream *ks, const void *h_chunk);
+int ddg_keystream_open_file(ddg_keystream *ks, const char *path, int nchunks);
+/* verify every chunk's trailer and checksum on the GPU before use */
+int ddg_keystream_set_verify(ddg_keystream *ks, int on);
+/* out5 = {chunks consumed, bytes copied, summed H2D copy ms, summed file read ms, ms waited for the reader} */
+int ddg_keystream_stats(ddg_keystream *ks, double *out5);
+/* ddg_forward_eval / ddg_forward_eval_pair with the keys of the next chunk */
+int ddg_forward_eval_streamed(ddg_keystream *ks, int batch, const void *x_share, const void *adj_share,
+                              const void *mask_share, const void *protein_share, int on_host, int64_t *h_out_raw,
+                              double *h_affinity);
+int ddg_forward_eval_pair_streamed(ddg_keystream *ks0, ddg_keystream *ks1, int batch, const void *const *in0,
+                                   const void *const *in1, int on_host, int64_t *h_out_raw, double *h_affinity);
+
+/* ------------------------------------------------------------------------
  * Linear layers and the DPF look-up table, one party, no communication.
  * ---------------------------------------------------------------------- */
 
