@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--scale", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--lanes", type=int, default=0,
+                    help="N>1: half-batch lanes per rank, each with its own NCCL communicator, so one lane computes "
+                         "while the other waits on an opening (default 2 for N>1)")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
                     help="streaming regime (BASELINE configs[4]): keys of NCHUNKS forwards per party live in pinned "
                          "host memory and are streamed into HBM through the double-buffered key stream, cyclically")
@@ -67,6 +70,18 @@ def parse():
     if a.stream and a.batch == 256:
         a.batch = 64  # one chunk per party is ~6.4 GB at bw=32
     return a
+
+
+def roles(rank: int, world: int):
+    """Party layout of a run on `world` GPUs: (pairs, pair index, party, peer rank).
+    Ranks 0..k-1 are party 0, ranks k..2k-1 party 1; pair i = (i, k+i)."""
+    if world == 1:
+        return 1, 0, None, None
+    if world % 2:
+        raise ValueError("multi-GPU runs need an even number of GPUs (one party per GPU)")
+    pairs = world // 2
+    pair, party = rank % pairs, rank // pairs
+    return pairs, pair, party, rank + pairs if party == 0 else rank - pairs
 
 
 def measured_peaks():
@@ -92,7 +107,8 @@ def config_of(a, n_gpus):
         "workload": f"full affinity branch (adj-norm, GCNx3, masked max-pool, FC head), bw={a.bw}, scale={a.scale}, "
                     f"B={a.batch} davis-shaped synthetic graphs per pair, keys resident in HBM (BASELINE configs[2])",
         "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs,
-        "parallelism": "1 GPU, both parties" if n_gpus == 1 else f"{pairs} party pairs over NCCL, one party per GPU",
+        "parallelism": "1 GPU, both parties" if n_gpus == 1 else
+        f"{pairs} party pairs over NCCL, one party per GPU, {a.lanes or 2} half-batch lanes per GPU",
         "truncation": "exact (floor) at every site",
         "l2": "inputs larger than L2: every step streams the full key region (>= 28 GB per party at B=256)",
     }
@@ -201,6 +217,16 @@ def run_reference(a, rank, world):
 
 # ------------------------------------------------------------------ our arm
 
+class _StreamLane:
+    """adapts a KeyStream to the forward(batch, x, adj, mask, prot, on_host) call of a lane"""
+
+    def __init__(self, ks):
+        self.ks = ks
+
+    def forward(self, batch, x, adj, mask, prot, on_host=False):
+        return self.ks.forward(x, adj, mask, prot, on_host=on_host)
+
+
 def make_keys(ddg, torch, bw, s, B, seed, blob, device):
     kb = ddg.forward_key_bytes(bw, s, B)
     k0 = torch.empty(kb, dtype=torch.uint8, device=device)
@@ -210,10 +236,11 @@ def make_keys(ddg, torch, bw, s, B, seed, blob, device):
     return kb, k0, k1
 
 
-def share_buffers(torch, inp, party, device):
+def share_buffers(torch, inp, party, device, rows=None):
     import numpy as np
 
-    arrs = [np.ascontiguousarray(x[party]) for x in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)]
+    sl = slice(None) if rows is None else slice(*rows)
+    arrs = [np.ascontiguousarray(x[party][sl]) for x in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)]
     dev = [torch.from_numpy(a.view(np.uint8).copy()).to(device) for a in arrs]
     host = [torch.from_numpy(a.view(np.uint8).copy()).pin_memory() for a in arrs]
     return dev, host
@@ -269,31 +296,39 @@ def main():
         ddg.pair_local(parties[0], parties[1])
         bufs = [share_buffers(torch, inp, p, device) for p in (0, 1)]
     else:
-        pairs = world // 2
-        pair, party = rank % pairs, rank // pairs
-        peer = rank + pairs if party == 0 else rank - pairs
+        pairs, pair, party, peer = roles(rank, world)
+        lanes = a.lanes or 2
+        if B % lanes:
+            raise SystemExit(f"--batch {B} not divisible by --lanes {lanes}")
+        Bl = B // lanes
         inp = synth.Inputs(B, bw, seed=1000 + pair)
-        P = ddg.Party(party, bw, s, local)
-        P.set_weights(blob)
-        if a.stream:
-            kb = ddg.forward_key_bytes(bw, s, B)
-            chunks = ddg.dealer_chunks(bw, s, B, [1000 + 97 * pair + i for i in range(a.stream)], blob, local)
-            streams = [ddg.KeyStream(P, B)]
-            for c in chunks:
-                streams[0].add_host_chunk(c[party].data_ptr())
-            chunks = [(c[party],) for c in chunks]
-        else:
-            kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000 + pair, blob, device)
-            mine = k0 if party == 0 else k1
-            del k0, k1
-            torch.cuda.empty_cache()
-            P.bind_keys(mine.data_ptr(), kb)
-        uid = [ddg.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        P.connect_nccl(uid[0], world, rank, peer)
-        P.set_timeout(600_000)
-        parties = [P]
-        bufs = [share_buffers(torch, inp, party, device)]
+        uids = [[ddg.nccl_unique_id() for _ in range(lanes)] if rank == 0 else None]
+        dist.broadcast_object_list(uids, src=0)
+        parties, keep_keys = [], []
+        for lane in range(lanes):
+            P = ddg.Party(party, bw, s, local)
+            P.set_weights(blob)
+            seed = 1000 + 97 * pair + 7 * lane
+            if a.stream:
+                kb = ddg.forward_key_bytes(bw, s, Bl)
+                chunks = ddg.dealer_chunks(bw, s, Bl, [seed + i for i in range(a.stream)], blob, local)
+                ks = ddg.KeyStream(P, Bl)
+                for c in chunks:
+                    ks.add_host_chunk(c[party].data_ptr())
+                keep_keys.append([c[party] for c in chunks])
+                del chunks
+                streams.append(ks)
+            else:
+                kb, k0, k1 = make_keys(ddg, torch, bw, s, Bl, seed, blob, device)
+                mine = k0 if party == 0 else k1
+                del k0, k1
+                torch.cuda.empty_cache()
+                P.bind_keys(mine.data_ptr(), kb)
+                keep_keys.append(mine)
+            P.connect_nccl(uids[0][lane], world, rank, peer)
+            P.set_timeout(600_000)
+            parties.append(P)
+        bufs = [share_buffers(torch, inp, party, device, (lane * Bl, (lane + 1) * Bl)) for lane in range(lanes)]
 
     def step(on_host):
         if world == 1:
@@ -301,11 +336,16 @@ def main():
             if streams:
                 return ddg.forward_pair_streamed(streams[0], streams[1], ins[0], ins[1], on_host=on_host)
             return ddg.forward_pair(parties[0], parties[1], B, ins[0], ins[1], on_host=on_host)
-        ins = [t.data_ptr() for t in (bufs[0][1] if on_host else bufs[0][0])]
+        ins = [[t.data_ptr() for t in (b[1] if on_host else b[0])] for b in bufs]
         if streams:
-            return streams[0].forward(*ins, on_host=on_host)
-        return parties[0].forward(B, *ins, on_host=on_host)
+            out = ddg.forward_lanes([_StreamLane(ks) for ks in streams], B // len(parties), ins, on_host)
+        else:
+            out = ddg.forward_lanes(parties, B // len(parties), ins, on_host)
+        if timing_on[0] and len(parties) > 1:
+            ddg.parties_dcf_union(parties)
+        return out
 
+    timing_on = [False]
     stream = torch.cuda.ExternalStream(parties[0].stream, device=device)
 
     def timed(on_host, k):
@@ -331,13 +371,20 @@ def main():
     ks_before = [ks.stats() for ks in streams]
     for p in parties:
         p.enable_dcf_timing(True)
+    timing_on[0] = True
     clocks = Clocks(local)
     clocks.start()
     n0 = ddg.launch_count()
     ms = timed(False, a.steps)
     launches = ddg.launch_count() - n0
     clk = clocks.stop()
+    timing_on[0] = False
     stats = parties[0].stats()
+    if world > 1:
+        lane_stats = [p.stats() for p in parties]
+        stats = {"bytes_sent": sum(x["bytes_sent"] for x in lane_stats), "rounds": lane_stats[0]["rounds"],
+                 "key_bytes_used": sum(x["key_bytes_used"] for x in lane_stats)}
+        kb = sum(ddg.forward_key_bytes(bw, s, B // len(parties)) for _ in parties)
     dcf = [p.dcf_timing() for p in parties]
     stream_info = None
     if streams:
@@ -357,7 +404,7 @@ def main():
         ms_e2e = timed(True, a.steps)
         # both parties' input shares of every pair cross host->device each step
         own = [sum(int(t.numel()) for t in b[1]) for b in bufs]
-        h2d = sum(own) if world == 1 else 2 * own[0]
+        h2d = sum(own) if world == 1 else 2 * sum(own)
         e2e = {"value": pairs * B * a.steps / (ms_e2e / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": h2d * pairs, "d2h_bytes_per_step": B * (bw // 8) * pairs,
                "ms_per_step": ms_e2e / a.steps}
@@ -370,7 +417,10 @@ def main():
         aes = dcf[0]["aes_blocks"] + dcf[1]["aes_blocks"]
         nl = dcf[0]["launches"] + dcf[1]["launches"]
     else:
-        union, alg, aes, nl = dcf[0]["union_ms"], dcf[0]["bytes"], dcf[0]["aes_blocks"], dcf[0]["launches"]
+        union = dcf[0]["pair_union_ms"] if len(parties) > 1 else dcf[0]["union_ms"]
+        alg = sum(d["bytes"] for d in dcf)
+        aes = sum(d["aes_blocks"] for d in dcf)
+        nl = sum(d["launches"] for d in dcf)
     achieved = alg / (union / 1e3) / 1e9 if union > 0 else 0.0
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": peak_kind,

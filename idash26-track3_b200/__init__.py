@@ -52,6 +52,7 @@ SIGNATURES = {
     "ddg_matmul_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_fc_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_aes_chain": (_i32, [_u64, _i32, _vp, _vp]),
+    "ddg_aes_chain_variant": (_i32, [_u64, _i32, _i32, _vp, _vp]),
     "ddg_party_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32]),
     "ddg_party_destroy": (_i32, [_vp]),
     "ddg_party_set_weights": (_i32, [_vp, _vp, _u64]),
@@ -82,6 +83,7 @@ SIGNATURES = {
                                               _vp]),
     "ddg_party_enable_dcf_timing": (_i32, [_vp, _i32]),
     "ddg_party_dcf_timing": (_i32, [_vp, ctypes.POINTER(ctypes.c_double)]),
+    "ddg_parties_dcf_union": (_i32, [ctypes.POINTER(_vp), _i32]),
 }
 
 
@@ -351,3 +353,33 @@ def write_key_file(path: str, chunks) -> None:
     with open(path, "wb") as f:
         for c in chunks:
             f.write(c.numpy().tobytes())
+
+
+def parties_dcf_union(parties):
+    arr = (_vp * len(parties))(*[p.h for p in parties])
+    check(lib().ddg_parties_dcf_union(arr, len(parties)))
+
+
+def forward_lanes(parties, batch_per_lane, inputs, on_host=False):
+    """Run one forward on each of several parties of this process concurrently
+    (one host thread each; the library releases the GIL).  inputs[i] =
+    (x, adj, mask, protein) pointers of lane i.  Returns the lanes' (raw, aff)."""
+    import threading
+
+    results, errors = [None] * len(parties), [None] * len(parties)
+
+    def run(i):
+        try:
+            results[i] = parties[i].forward(batch_per_lane, *inputs[i], on_host=on_host)
+        except Exception as e:  # re-raised in the caller
+            errors[i] = e
+
+    ts = [threading.Thread(target=run, args=(i,)) for i in range(len(parties))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for e in errors:
+        if e is not None:
+            raise e
+    return results

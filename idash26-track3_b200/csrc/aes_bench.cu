@@ -7,6 +7,7 @@
 
 namespace ddg {
 
+template <bool IMAD>
 __global__ void __launch_bounds__(256, 3) aes_chain_kernel(uint64_t threads, int iters, uint32_t *out)
 {
     extern __shared__ uint32_t smem_tab[];
@@ -17,18 +18,21 @@ __global__ void __launch_bounds__(256, 3) aes_chain_kernel(uint64_t threads, int
         Blk b;
         b.w[0] = uint32_t(t), b.w[1] = uint32_t(t >> 32), b.w[2] = 0x9e3779b9u, b.w[3] = 0x7f4a7c15u;
 #pragma unroll 1
-        for (int i = 0; i < iters; i++) b = A.hash_h(b);
+        for (int i = 0; i < iters; i++) b = A.ccr<IMAD>(b, c_fixed.h.rk);
         out[t] = b.w[0] ^ b.w[1] ^ b.w[2] ^ b.w[3];
     }
 }
 
-int aes_chain(uint64_t threads, int iters, uint32_t *out, cudaStream_t st)
+// variant: 0 = the build's default round, 1 = shifts/PRMT only, 2 = multiply-add offload
+int aes_chain(uint64_t threads, int iters, uint32_t *out, cudaStream_t st, int variant)
 {
     DDG_TRY(aes_device_init());
-    DDG_CUDA(cudaFuncSetAttribute(aes_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
+    const bool imad = variant == 0 ? bool(DDG_AES_IMAD) : variant == 2;
+    auto kern = imad ? aes_chain_kernel<true> : aes_chain_kernel<false>;
+    DDG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
     int sms = device_sms();
     uint64_t need = (threads + 255) / 256, full = uint64_t(sms) * 3;
-    aes_chain_kernel<<<int(need < full ? need : full), 256, AES_SMEM_BYTES, st>>>(threads, iters, out);
+    kern<<<int(need < full ? need : full), 256, AES_SMEM_BYTES, st>>>(threads, iters, out);
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;

@@ -11,6 +11,10 @@
 #pragma once
 #include <cstdint>
 
+#ifndef DDG_AES_IMAD
+#define DDG_AES_IMAD 1
+#endif
+
 namespace ddg {
 
 constexpr int AES_SMEM_BYTES = 256 * 256;
@@ -19,10 +23,13 @@ struct AesKey {
     uint32_t rk[44];
 };
 
-// fixed public keys of the tree hash and the leaf conversion
+// fixed public keys of the tree hash and the leaf conversion; `m256` holds
+// the constant 256, read from constant memory so that multiplies by it stay
+// integer multiply-adds (FMA pipe) instead of being folded into shifts (ALU pipe)
 struct FixedKeys {
     AesKey h;
     AesKey c;
+    uint32_t m256;
 };
 
 extern __constant__ FixedKeys c_fixed;   // defined in aes_tables.cu
@@ -63,26 +70,54 @@ struct AesLane {
         return *reinterpret_cast<const uint32_t *>(tab + __byte_perm(w, off2, 0x5504u | (uint32_t(k) << 4)));
     }
 
+    // T2 lookup of byte 3 with the address formed on the FMA pipe:
+    // ((w * 2^-24) >> 0) * 256 + off = umulhi(w, 256) * 256 + off
+    __device__ __forceinline__ uint32_t t2_b3_fma(uint32_t w) const
+    {
+        const uint32_t m = c_fixed.m256;
+        return *reinterpret_cast<const uint32_t *>(tab + (__umulhi(w, m) * m + off2));
+    }
+    // rotl8 on the FMA pipe: v * 256 + (v >> 24)
+    __device__ __forceinline__ uint32_t rot8_fma(uint32_t v) const
+    {
+        const uint32_t m = c_fixed.m256;
+        return v * m + __umulhi(v, m);
+    }
+
+    // IMAD = true: the byte-3 lookups and the rotations use integer multiply-adds
+    template <bool IMAD = DDG_AES_IMAD>
     __device__ __forceinline__ void encrypt(Blk &b, const uint32_t *__restrict__ rk) const
     {
         uint32_t s0 = b.w[0] ^ rk[0], s1 = b.w[1] ^ rk[1], s2 = b.w[2] ^ rk[2], s3 = b.w[3] ^ rk[3];
 #pragma unroll
         for (int r = 1; r < 10; r++) {
-            uint32_t v0 = t0(s1, 1) ^ t2(s3, 3);
-            uint32_t u0 = t0(s0, 0) ^ t2(s2, 2) ^ rk[4 * r + 0] ^ __funnelshift_l(v0, v0, 8);
-            uint32_t v1 = t0(s2, 1) ^ t2(s0, 3);
-            uint32_t u1 = t0(s1, 0) ^ t2(s3, 2) ^ rk[4 * r + 1] ^ __funnelshift_l(v1, v1, 8);
-            uint32_t v2 = t0(s3, 1) ^ t2(s1, 3);
-            uint32_t u2 = t0(s2, 0) ^ t2(s0, 2) ^ rk[4 * r + 2] ^ __funnelshift_l(v2, v2, 8);
-            uint32_t v3 = t0(s0, 1) ^ t2(s2, 3);
-            uint32_t u3 = t0(s3, 0) ^ t2(s1, 2) ^ rk[4 * r + 3] ^ __funnelshift_l(v3, v3, 8);
+            uint32_t u0, u1, u2, u3;
+            if (IMAD) {
+                uint32_t v0 = t0(s1, 1) ^ t2_b3_fma(s3);
+                u0 = t0(s0, 0) ^ t2(s2, 2) ^ rk[4 * r + 0] ^ rot8_fma(v0);
+                uint32_t v1 = t0(s2, 1) ^ t2_b3_fma(s0);
+                u1 = t0(s1, 0) ^ t2(s3, 2) ^ rk[4 * r + 1] ^ rot8_fma(v1);
+                uint32_t v2 = t0(s3, 1) ^ t2_b3_fma(s1);
+                u2 = t0(s2, 0) ^ t2(s0, 2) ^ rk[4 * r + 2] ^ rot8_fma(v2);
+                uint32_t v3 = t0(s0, 1) ^ t2_b3_fma(s2);
+                u3 = t0(s3, 0) ^ t2(s1, 2) ^ rk[4 * r + 3] ^ rot8_fma(v3);
+            } else {
+                uint32_t v0 = t0(s1, 1) ^ t2(s3, 3);
+                u0 = t0(s0, 0) ^ t2(s2, 2) ^ rk[4 * r + 0] ^ __funnelshift_l(v0, v0, 8);
+                uint32_t v1 = t0(s2, 1) ^ t2(s0, 3);
+                u1 = t0(s1, 0) ^ t2(s3, 2) ^ rk[4 * r + 1] ^ __funnelshift_l(v1, v1, 8);
+                uint32_t v2 = t0(s3, 1) ^ t2(s1, 3);
+                u2 = t0(s2, 0) ^ t2(s0, 2) ^ rk[4 * r + 2] ^ __funnelshift_l(v2, v2, 8);
+                uint32_t v3 = t0(s0, 1) ^ t2(s2, 3);
+                u3 = t0(s3, 0) ^ t2(s1, 2) ^ rk[4 * r + 3] ^ __funnelshift_l(v3, v3, 8);
+            }
             s0 = u0, s1 = u1, s2 = u2, s3 = u3;
         }
         // last round: SubBytes + ShiftRows + AddRoundKey
         // column c bytes: S(b0(s_c)), S(b1(s_c+1)), S(b2(s_c+2)), S(b3(s_c+3))
         auto last = [&](uint32_t a, uint32_t bb, uint32_t c, uint32_t d) {
             uint32_t lo = __byte_perm(t2(a, 0), t0(bb, 1), 0x3250u);  // byte0 = T2 b0, byte1 = T0 b1
-            uint32_t hi = __byte_perm(t0(c, 2), t2(d, 3), 0x7210u);   // byte2 = T0 b2, byte3 = T2 b3
+            uint32_t hi = __byte_perm(t0(c, 2), IMAD ? t2_b3_fma(d) : t2(d, 3), 0x7210u);  // byte2 = T0 b2, byte3 = T2 b3
             return __byte_perm(lo, hi, 0x7610u);
         };
         b.w[0] = last(s0, s1, s2, s3) ^ rk[40];
@@ -92,6 +127,7 @@ struct AesLane {
     }
 
     // correlation-robust hash pi(sigma(x)) ^ sigma(x), sigma(lo,hi) = (hi, lo^hi)
+    template <bool IMAD = DDG_AES_IMAD>
     __device__ __forceinline__ Blk ccr(const Blk &x, const uint32_t *__restrict__ rk) const
     {
         Blk s;
@@ -100,7 +136,7 @@ struct AesLane {
         s.w[2] = x.w[0] ^ x.w[2];
         s.w[3] = x.w[1] ^ x.w[3];
         Blk e = s;
-        encrypt(e, rk);
+        encrypt<IMAD>(e, rk);
         e.w[0] ^= s.w[0], e.w[1] ^= s.w[1], e.w[2] ^= s.w[2], e.w[3] ^= s.w[3];
         return e;
     }

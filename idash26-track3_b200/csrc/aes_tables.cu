@@ -48,6 +48,7 @@ static void host_tables()
     }
     aes_expand_host(reinterpret_cast<const uint8_t *>("ddg-halftree-H:0"), h_fixed.h);
     aes_expand_host(reinterpret_cast<const uint8_t *>("ddg-halftree-C:1"), h_fixed.c);
+    h_fixed.m256 = 256;
 }
 
 void aes_expand_host(const uint8_t key[16], AesKey &out)

@@ -1,6 +1,7 @@
 // extern "C" entry points of libddg.so (declared in include/ddg_fss.h).
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "aes_dev.cuh"
 #include "channel.cuh"
@@ -78,7 +79,14 @@ int ddg_gate_round2(int kind, int bw, int scale, uint64_t n, int party, const vo
 int ddg_aes_chain(uint64_t threads, int iters, uint32_t *d_out, void *stream)
 {
     DDG_CHECK(threads > 0 && iters > 0 && d_out, DDG_ERR_ARG, "bad aes_chain arguments");
-    return aes_chain(threads, iters, d_out, static_cast<cudaStream_t>(stream));
+    return aes_chain(threads, iters, d_out, static_cast<cudaStream_t>(stream), 0);
+}
+
+int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_out, void *stream)
+{
+    DDG_CHECK(threads > 0 && iters > 0 && d_out && variant >= 0 && variant <= 2, DDG_ERR_ARG,
+              "bad aes_chain arguments");
+    return aes_chain(threads, iters, d_out, static_cast<cudaStream_t>(stream), variant);
 }
 
 // ------------------------------------------------------------ parties
@@ -247,6 +255,17 @@ int ddg_party_dcf_timing(ddg_party *h, double *out6)
 }
 
 uint64_t ddg_launch_count(void) { return launch_count(); }
+
+int ddg_parties_dcf_union(ddg_party *const *parties, int n)
+{
+    DDG_CHECK(parties && n > 0, DDG_ERR_ARG, "bad argument");
+    std::vector<Party *> ps(n);
+    for (int i = 0; i < n; i++) {
+        DDG_CHECK(parties[i], DDG_ERR_ARG, "null party");
+        ps[i] = &parties[i]->P;
+    }
+    return parties_dcf_union(ps.data(), n);
+}
 
 // ------------------------------------------------------------ key chunks / streaming
 

@@ -724,13 +724,24 @@ double union_ms(std::vector<std::pair<double, double>> v)
 // timeline (the two ref events live on the same device)
 int pair_dcf_union(Party &p0, Party &p1)
 {
-    if (!p0.timing.enabled || !p1.timing.enabled || !p0.ref_event || !p1.ref_event) return DDG_OK;
-    DDG_CHECK(p0.device == p1.device, DDG_ERR_ARG, "pair timing needs both parties on one device");
-    float off = 0;
-    DDG_CUDA(cudaEventElapsedTime(&off, p0.ref_event, p1.ref_event));
-    std::vector<std::pair<double, double>> all = p0.intervals;
-    for (auto &iv : p1.intervals) all.emplace_back(iv.first + off, iv.second + off);
-    p0.dcf.pair_union_ms += union_ms(all);
+    Party *ps[2] = {&p0, &p1};
+    return parties_dcf_union(ps, 2);
+}
+
+// union of several parties' DCF launch intervals of their last forwards, on
+// the timeline of ps[0] (all on one device); accumulated on ps[0]
+int parties_dcf_union(Party *const *ps, int n)
+{
+    for (int i = 0; i < n; i++)
+        if (!ps[i]->timing.enabled || !ps[i]->ref_event) return DDG_OK;
+    std::vector<std::pair<double, double>> all = ps[0]->intervals;
+    for (int i = 1; i < n; i++) {
+        DDG_CHECK(ps[i]->device == ps[0]->device, DDG_ERR_ARG, "DCF interval union needs one device");
+        float off = 0;
+        DDG_CUDA(cudaEventElapsedTime(&off, ps[0]->ref_event, ps[i]->ref_event));
+        for (auto &iv : ps[i]->intervals) all.emplace_back(iv.first + off, iv.second + off);
+    }
+    ps[0]->dcf.pair_union_ms += union_ms(all);
     return DDG_OK;
 }
 

@@ -66,6 +66,7 @@ struct Party {
 uint64_t forward_key_bytes(int bw, int s, int B);
 double union_ms(std::vector<std::pair<double, double>> v);
 int pair_dcf_union(Party &p0, Party &p1);
+int parties_dcf_union(Party *const *ps, int n);
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
                  bool on_host, int64_t *h_out_raw, double *h_aff);
 int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uint8_t *k0, uint8_t *k1,

@@ -12,6 +12,6 @@ int gate_round1(const GateLayout &L, const void *xhat, const void *key, uint32_t
 int gate_round2(const GateLayout &L, int party, const void *xhat, const uint32_t *hi_own, const uint32_t *hi_peer,
                 const uint32_t *lo_own, const uint32_t *lo_peer, const void *key, void *share, cudaStream_t st);
 
-int aes_chain(uint64_t threads, int iters, uint32_t *out, cudaStream_t st);
+int aes_chain(uint64_t threads, int iters, uint32_t *out, cudaStream_t st, int variant = 0);
 
 }  // namespace ddg

@@ -258,11 +258,19 @@ int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, con
 uint64_t ddg_launch_count(void);
 int ddg_party_enable_dcf_timing(ddg_party *party, int on);
 int ddg_party_dcf_timing(ddg_party *party, double *out6);
+/* after a forward of several parties on one device (e.g. two half-batch
+ * lanes of one party): add the union of their DCF launch intervals to
+ * parties[0]'s pair-union total (out6[5]) */
+int ddg_parties_dcf_union(ddg_party *const *parties, int n);
 
 /* Diagnostics: `threads` independent chains of `iters` fixed-key tree
  * hashes (one AES-128 each), one word per chain written to d_out.  Gives the
  * AES-blocks/s ceiling of the DCF kernels. */
 int ddg_aes_chain(uint64_t threads, int iters, uint32_t *d_out, void *stream);
+/* the same with the AES round variant chosen: 0 = the build's default,
+ * 1 = byte extraction and rotations on the integer ALU (shifts / PRMT),
+ * 2 = byte-3 extraction and rotations as integer multiply-adds */
+int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_out, void *stream);
 
 #ifdef __cplusplus
 }
