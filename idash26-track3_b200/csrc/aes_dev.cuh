@@ -11,8 +11,12 @@
 #pragma once
 #include <cstdint>
 
+// DDG_AES_IMAD = 1 moves the byte-3 table addresses and the 8-bit rotations
+// from the integer ALU pipe to integer multiply-adds.  Measured on B200 with the
+// ddg_aes_chain_variant probe it is slower (38.8 vs 46.4 G blocks/s), so the
+// ALU form (PRMT / funnel shift) is the default.
 #ifndef DDG_AES_IMAD
-#define DDG_AES_IMAD 1
+#define DDG_AES_IMAD 0
 #endif
 
 namespace ddg {
