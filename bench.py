@@ -60,13 +60,18 @@ def parse():
     ap.add_argument("--scale", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--lanes", type=int, default=0,
-                    help="N>1: half-batch lanes per rank, each with its own NCCL communicator, so one lane computes "
-                         "while the other waits on an opening (default 2 for N>1)")
+    ap.add_argument("--lanes", type=int, default=1,
+                    help="N>1: batch lanes per rank, each with its own NCCL communicator and host thread.  Only 1 "
+                         "is accepted: two lanes (two communicators used concurrently from two threads per GPU) "
+                         "stalled for 900 s on the first 2-GPU run, cause not established")
+    ap.add_argument("--gemm", default="tensor", choices=["tensor", "cuda-cores"],
+                    help="ring GEMM engine: tcgen05 limb products (default) or the CUDA-core kernel")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
                     help="streaming regime (BASELINE configs[4]): keys of NCHUNKS forwards per party live in pinned "
                          "host memory and are streamed into HBM through the double-buffered key stream, cyclically")
     a = ap.parse_args()
+    if a.lanes != 1:
+        raise SystemExit("--lanes: only 1 lane per rank is supported (see --help)")
     if a.stream and a.batch == 256:
         a.batch = 64  # one chunk per party is ~6.4 GB at bw=32
     return a
@@ -108,9 +113,10 @@ def config_of(a, n_gpus):
                     f"B={a.batch} davis-shaped synthetic graphs per pair, keys resident in HBM (BASELINE configs[2])",
         "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs,
         "parallelism": "1 GPU, both parties" if n_gpus == 1 else
-        f"{pairs} party pairs over NCCL, one party per GPU, {a.lanes or 2} half-batch lanes per GPU",
+        f"{pairs} party pairs over NCCL, one party per GPU",
         "truncation": "exact (floor) at every site",
-        "l2": "inputs larger than L2: every step streams the full key region (>= 28 GB per party at B=256)",
+        "gemm": "tcgen05 kind::i8 limb products" if a.gemm == "tensor" else "CUDA-core integer multiply-add",
+        "l2": "inputs larger than L2: every step streams the full key region (>= 24 GB per party at B=256)",
     }
 
 
@@ -261,6 +267,7 @@ def main():
 
     ddg = importlib.import_module("idash26-track3_b200")
     synth = importlib.import_module("idash26-track3_b200.synth")
+    ddg.gemm_path(ddg.GEMM_TENSOR if a.gemm == "tensor" else ddg.GEMM_CUDA_CORES)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None
@@ -297,7 +304,7 @@ def main():
         bufs = [share_buffers(torch, inp, p, device) for p in (0, 1)]
     else:
         pairs, pair, party, peer = roles(rank, world)
-        lanes = a.lanes or 2
+        lanes = a.lanes
         if B % lanes:
             raise SystemExit(f"--batch {B} not divisible by --lanes {lanes}")
         Bl = B // lanes

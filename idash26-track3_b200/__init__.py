@@ -18,7 +18,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libddg.so")
 
-GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT = 0, 1, 2, 3, 4, 5
+GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT = range(7)
 
 DDG_OK = 0
 _STATUS = {1: "DDG_ERR_ARG", 2: "DDG_ERR_CUDA", 3: "DDG_ERR_KEY", 4: "DDG_ERR_PEER", 5: "DDG_ERR_STATE",
@@ -51,8 +51,11 @@ SIGNATURES = {
     "ddg_mul_share": (_i32, [_i32, _i32, _u64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_matmul_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_fc_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_gemm_path": (_i32, [_i32]),
+    "ddg_gemm_status": (_i32, []),
     "ddg_aes_chain": (_i32, [_u64, _i32, _vp, _vp]),
     "ddg_aes_chain_variant": (_i32, [_u64, _i32, _i32, _vp, _vp]),
+    "ddg_aes_tables": (_i32, [_i32]),
     "ddg_party_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32]),
     "ddg_party_destroy": (_i32, [_vp]),
     "ddg_party_set_weights": (_i32, [_vp, _vp, _u64]),
@@ -114,10 +117,10 @@ def gate_key_bytes(kind: int, bw: int, scale: int, n: int) -> int:
 
 def gate_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
     """Byte offsets of one party's gate key (see ddg_gate_key_layout)."""
-    out = (_u64 * 14)()
+    out = (_u64 * 16)()
     check(lib().ddg_gate_key_layout(kind, bw, scale, n, out))
     keys = ("hi_root", "hi_cw", "hi_leaf", "hi_mu", "lo_root", "lo_cw", "lo_leaf", "lo_mu", "words", "bytes",
-            "hi_levels", "lo_levels", "hi_mu_eq", "hi_bits")
+            "hi_levels", "lo_levels", "hi_mu_eq", "hi_bits", "hi_shift", "lo_bits")
     return {k: int(v) for k, v in zip(keys, out)}
 
 
@@ -247,6 +250,25 @@ def forward_pair(p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
 
 def launch_count() -> int:
     return int(lib().ddg_launch_count())
+
+
+GEMM_TENSOR, GEMM_CUDA_CORES, GEMM_TENSOR_BK, GEMM_TENSOR_WIDE = 0, 1, 2, 3
+
+
+def gemm_path(path: int):
+    """Ring GEMM engine: GEMM_TENSOR (default, tcgen05 limb products),
+    GEMM_CUDA_CORES, or the tensor-core layout/tile variants."""
+    check(lib().ddg_gemm_path(path))
+
+
+def aes_tables(tables: int):
+    """AES engine of every FSS kernel: 4 (default) or 2 staged round tables."""
+    check(lib().ddg_aes_tables(tables))
+
+
+def gemm_status():
+    """Raise DdgError if a tensor-core GEMM gave up on a bounded wait (clears the flag)."""
+    check(lib().ddg_gemm_status())
 
 
 # ---------------------------------------------------------------- key chunks / streaming

@@ -14,6 +14,10 @@ namespace ddg {
 __constant__ FixedKeys c_fixed;
 __device__ uint32_t g_T0[256];
 
+static std::atomic<int> g_aes_tables{4};
+int aes_tables() { return g_aes_tables.load(); }
+void set_aes_tables(int nt) { g_aes_tables.store(nt == 2 ? 2 : 4); }
+
 static uint8_t h_sbox[256];
 static uint32_t h_T0[256];
 static FixedKeys h_fixed;
@@ -48,7 +52,6 @@ static void host_tables()
     }
     aes_expand_host(reinterpret_cast<const uint8_t *>("ddg-halftree-H:0"), h_fixed.h);
     aes_expand_host(reinterpret_cast<const uint8_t *>("ddg-halftree-C:1"), h_fixed.c);
-    h_fixed.m256 = 256;
 }
 
 void aes_expand_host(const uint8_t key[16], AesKey &out)

@@ -13,9 +13,10 @@ using namespace ddg;
 
 static int check_gate_args(int kind, int bw, int scale)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_SPLIT, DDG_ERR_ARG, "gate kind %d out of range", kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS_SPLIT, DDG_ERR_ARG, "gate kind %d out of range", kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
+    DDG_CHECK(kind != DDG_GATE_LRS_SPLIT || scale >= 2, DDG_ERR_ARG, "split LRS needs scale >= 2 (got %d)", scale);
     return DDG_OK;
 }
 
@@ -36,9 +37,10 @@ int ddg_gate_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out)
     DDG_TRY(check_gate_args(kind, bw, scale));
     DDG_CHECK(out != nullptr, DDG_ERR_ARG, "null out");
     GateLayout L = gate_layout(kind, bw, scale, n);
-    uint64_t v[14] = {L.H.root, L.H.cw, L.H.leaf, L.H.mu, L.Lo.root, L.Lo.cw, L.Lo.leaf, L.Lo.mu,
-                      L.words, L.bytes, uint64_t(L.H.L), uint64_t(L.Lo.L), L.H.mu_eq, uint64_t(L.H.d)};
-    for (int i = 0; i < 14; i++) out[i] = v[i];
+    uint64_t v[16] = {L.H.root, L.H.cw, L.H.leaf, L.H.mu, L.Lo.root, L.Lo.cw, L.Lo.leaf, L.Lo.mu,
+                      L.words, L.bytes, uint64_t(L.H.L), uint64_t(L.Lo.L), L.H.mu_eq, uint64_t(L.H.d),
+                      uint64_t(L.hi_shift), uint64_t(L.Lo.d)};
+    for (int i = 0; i < 16; i++) out[i] = v[i];
     return DDG_OK;
 }
 
@@ -84,9 +86,16 @@ int ddg_aes_chain(uint64_t threads, int iters, uint32_t *d_out, void *stream)
 
 int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_out, void *stream)
 {
-    DDG_CHECK(threads > 0 && iters > 0 && d_out && variant >= 0 && variant <= 2, DDG_ERR_ARG,
+    DDG_CHECK(threads > 0 && iters > 0 && d_out && (variant == 0 || variant == 2 || variant == 4), DDG_ERR_ARG,
               "bad aes_chain arguments");
     return aes_chain(threads, iters, d_out, static_cast<cudaStream_t>(stream), variant);
+}
+
+int ddg_aes_tables(int tables)
+{
+    DDG_CHECK(tables == 2 || tables == 4, DDG_ERR_ARG, "AES engine: 2 or 4 staged tables (got %d)", tables);
+    set_aes_tables(tables);
+    return DDG_OK;
 }
 
 // ------------------------------------------------------------ parties

@@ -129,4 +129,13 @@ int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, con
                     : fc_t<uint64_t>(party, M, K, N, d_xhat, d_w, d_bias2s, d_c, d_out, st);
 }
 
+int ddg_gemm_path(int path)
+{
+    DDG_CHECK(path >= 0 && path <= 3, DDG_ERR_ARG, "gemm path must be 0..3 (got %d)", path);
+    set_gemm_path(path);
+    return DDG_OK;
+}
+
+int ddg_gemm_status(void) { return ring_gemm_tc_error(true); }
+
 }  // extern "C"

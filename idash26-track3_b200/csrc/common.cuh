@@ -62,15 +62,22 @@ void set_dcf_timing_sink(DcfTiming *t);
 // ---------------------------------------------------------------- key layouts
 
 // gate kinds (the comparison-based nonlinear layers)
-// The *_SPLIT kinds compute the same functions as GATE_RELU / GATE_RELU_ARS
+// The RELU*_SPLIT kinds compute the same functions as GATE_RELU / GATE_RELU_ARS
 // but split the (n-1)-bit comparison into a DCF-with-equality over the upper
 // n-1-s bits and the s-bit low DCF: 1{x<a} = 1{U<A} ^ (1{U==A} & 1{V<B}).
+// GATE_LRS_SPLIT computes GATE_LRS with its s-bit carry comparison split the
+// same way into V1 (upper s - s2 bits, DCF with equality) and V2 (low s2 =
+// min(7, s-1) bits, plain DCF): 2 instead of s-6 AES-128 per element.
 enum GateKind {
     GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
-    GATE_KIND_END = 6
+    GATE_LRS_SPLIT = 6, GATE_KIND_END = 7
 };
 
-inline bool gate_is_split(int kind) { return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT; }
+// the high DCF has an equality output (three round-1 bit arrays)
+inline bool gate_is_split(int kind)
+{
+    return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT || kind == GATE_LRS_SPLIT;
+}
 inline bool gate_has_hi(int kind) { return kind != GATE_LRS; }
 inline bool gate_has_lo(int kind) { return kind != GATE_RELU; }
 inline int gate_nwords(int kind)
@@ -81,11 +88,25 @@ inline int gate_nwords(int kind)
     case GATE_ARS: return 6;
     case GATE_RELU_SPLIT: return 16;
     case GATE_RELU_ARS_SPLIT: return 32;
+    case GATE_LRS_SPLIT: return 7;
     default: return 4;
     }
 }
-// domain bits of the high DCF
-inline int gate_hi_bits(int kind, int bw, int s) { return gate_is_split(kind) ? bw - 1 - s : bw - 1; }
+// bits of the low part V2 of a GATE_LRS_SPLIT carry comparison
+__host__ __device__ inline int lrs_split_lo_bits(int s) { return s - 1 < 7 ? s - 1 : 7; }
+// domain bits of the high DCF and the shift that brings its input bits down
+inline int gate_hi_bits(int kind, int bw, int s)
+{
+    if (kind == GATE_LRS_SPLIT) return s - lrs_split_lo_bits(s);
+    return gate_is_split(kind) ? bw - 1 - s : bw - 1;
+}
+inline int gate_hi_shift(int kind, int s)
+{
+    if (kind == GATE_LRS_SPLIT) return lrs_split_lo_bits(s);
+    return gate_is_split(kind) ? s : 0;
+}
+// domain bits of the low DCF
+inline int gate_lo_bits(int kind, int s) { return kind == GATE_LRS_SPLIT ? lrs_split_lo_bits(s) : s; }
 
 // DCF key arrays of N elements, structure-of-arrays, every array 256-byte aligned:
 //   root[N] (16 B) | cw[L][N] (16 B, level-major) | leaf[N] (16 B) | mu[ceil(N/32)] (u32 bits)
@@ -99,13 +120,14 @@ struct DcfLayout {
 };
 
 inline int dcf_levels(int d) { return d > 7 ? d - 7 : 0; }
+inline int dcfeq_levels(int d) { return d > 6 ? d - 6 : 0; }
 
 inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base, bool eq = false)
 {
     DcfLayout l;
     l.d = d;
     l.eq = eq;
-    l.L = eq ? d - 6 : dcf_levels(d);
+    l.L = eq ? dcfeq_levels(d) : dcf_levels(d);
     l.root = align256(base);
     l.cw = align256(l.root + 16 * n);
     l.leaf = align256(l.cw + 16 * n * uint64_t(l.L));
@@ -115,9 +137,10 @@ inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base, bool eq = false)
     return l;
 }
 
-// one gate op: [hi DCF over n-1 bits] [lo DCF over s bits] [nwords x N ring words]
+// one gate op: [hi DCF over hi_bits] [lo DCF over lo_bits] [nwords x N ring words]
+// The hi DCF reads bits [hi_shift, hi_shift + H.d) of x_hat, the lo DCF bits [0, Lo.d).
 struct GateLayout {
-    int kind = 0, bw = 0, s = 0;
+    int kind = 0, bw = 0, s = 0, hi_shift = 0;
     uint64_t n = 0;
     bool hi = false, lo = false;
     DcfLayout H, Lo;
@@ -134,10 +157,11 @@ inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base
     uint64_t off = align256(base);
     if (g.hi) {
         g.H = dcf_layout(gate_hi_bits(kind, bw, s), n, off, gate_is_split(kind));
+        g.hi_shift = gate_hi_shift(kind, s);
         off = g.H.end;
     }
     if (g.lo) {
-        g.Lo = dcf_layout(s, n, off);
+        g.Lo = dcf_layout(gate_lo_bits(kind, s), n, off);
         off = g.Lo.end;
     }
     g.nwords = gate_nwords(kind);

@@ -14,7 +14,8 @@ namespace ddg {
 // Party's XOR share of 1{x < alpha} for d-bit x.  Key arrays are read once
 // with streaming loads; the next level's correction word is fetched one level
 // ahead so its latency hides under the current level's AES.
-__device__ __forceinline__ uint32_t dcf_eval(const AesLane &A, uint64_t x, int d, const DcfView &k, uint64_t e,
+template <class E>
+__device__ __forceinline__ uint32_t dcf_eval(const E &A, uint64_t x, int d, const DcfView &k, uint64_t e,
                                              uint64_t N)
 {
     const int L = d > 7 ? d - 7 : 0;
@@ -44,16 +45,18 @@ __device__ __forceinline__ uint32_t dcf_eval(const AesLane &A, uint64_t x, int d
 
 // DCF with equality output: returns the party's XOR shares of 1{x < alpha}
 // (bit 0) and 1{x == alpha} (bit 1) for d-bit x; the leaf holds, for the low
-// 6 bits y of x, 1{y < alpha_low6} at bit 2y and 1{y == alpha_low6} at 2y+1.
-__device__ __forceinline__ uint32_t dcfeq_eval(const AesLane &A, uint64_t x, int d, const DcfView &k, uint64_t e,
+// min(d, 6) bits y of x, 1{y < alpha_low} at bit 2y and 1{y == alpha_low} at 2y+1.
+template <class E>
+__device__ __forceinline__ uint32_t dcfeq_eval(const E &A, uint64_t x, int d, const DcfView &k, uint64_t e,
                                                uint64_t N)
 {
-    const int L = d - 6;
+    const int L = d > 6 ? d - 6 : 0;
     Blk s = ld_blk_stream(k.root + 16 * e);
     uint32_t c = 0;
     const uint8_t *cwp = k.cw + 16 * e;
     const uint64_t stride = 16 * N;
-    Blk nxt = ld_blk_stream(cwp);
+    Blk nxt;
+    if (L > 0) nxt = ld_blk_stream(cwp);
 #pragma unroll 1
     for (int j = 0; j < L; j++) {
         Blk cw = nxt;
@@ -84,7 +87,8 @@ __device__ __forceinline__ Blk lower_mask(uint32_t v)
 }
 
 // Dealer: both parties' keys for 1{x < alpha}, written at element e.
-__device__ __forceinline__ void dcf_keygen(const AesLane &A, uint64_t alpha, int d, Blk s0, Blk delta,
+template <class E>
+__device__ __forceinline__ void dcf_keygen(const E &A, uint64_t alpha, int d, Blk s0, Blk delta,
                                            const DcfOut &o, uint64_t e, uint64_t N)
 {
     const int L = d > 7 ? d - 7 : 0;
@@ -112,10 +116,11 @@ __device__ __forceinline__ void dcf_keygen(const AesLane &A, uint64_t alpha, int
 }
 
 // Dealer: both parties' keys of the DCF with equality output.
-__device__ __forceinline__ void dcfeq_keygen(const AesLane &A, uint64_t alpha, int d, Blk s0, Blk delta,
+template <class E>
+__device__ __forceinline__ void dcfeq_keygen(const E &A, uint64_t alpha, int d, Blk s0, Blk delta,
                                              const DcfOut &o, uint64_t e, uint64_t N)
 {
-    const int L = d - 6;
+    const int L = d > 6 ? d - 6 : 0;
     delta.w[0] |= 1u;
     Blk cur0 = s0, cur1 = blk_xor(s0, delta);
     st_blk(o.root0 + 16 * e, cur0);

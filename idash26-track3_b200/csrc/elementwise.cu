@@ -247,14 +247,15 @@ int i64_to_ring(const int64_t *in, T *out, uint64_t n, int shl, cudaStream_t st)
 
 // ------------------------------------------------------------ dealer PRG
 
-template <typename T>
-__global__ void __launch_bounds__(256) k_prg_split(const T *v, uint64_t n, const __grid_constant__ AesKey dk, uint32_t op,
-                                                   uint32_t purpose, T *s0, T *s1)
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) k_prg_split(const T *v, uint64_t n,
+                                                                   const __grid_constant__ AesKey dk, uint32_t op,
+                                                                   uint32_t purpose, T *s0, T *s1)
 {
     extern __shared__ uint32_t smem_tab[];
-    aes_stage_tables(smem_tab);
+    E::stage(smem_tab);
     __syncthreads();
-    AesLane A(smem_tab);
+    E A(smem_tab);
     GRID_STRIDE(i, n)
     {
         Blk b = A.prg(dk.rk, op, purpose, i);
@@ -272,11 +273,15 @@ static int prg_launch(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uin
 {
     if (!n) return DDG_OK;
     DDG_TRY(aes_device_init());
-    DDG_CUDA(cudaFuncSetAttribute(k_prg_split<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
-    static int sms = 0;
-    if (!sms) sms = device_sms();
-    uint64_t blocks = (n + 255) / 256, cap = uint64_t(sms) * 3;
-    k_prg_split<T><<<int(blocks < cap ? blocks : cap), 256, AES_SMEM_BYTES, st>>>(v, n, dk, op, purpose, s0, s1);
+    if (aes_tables() == 4) {
+        using E = AesLane4;
+        DDG_CUDA(cudaFuncSetAttribute(k_prg_split<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, E::SMEM));
+        k_prg_split<T, E><<<aes_blocks<E>(n), E::THREADS, E::SMEM, st>>>(v, n, dk, op, purpose, s0, s1);
+    } else {
+        using E = AesLane2;
+        DDG_CUDA(cudaFuncSetAttribute(k_prg_split<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, E::SMEM));
+        k_prg_split<T, E><<<aes_blocks<E>(n), E::THREADS, E::SMEM, st>>>(v, n, dk, op, purpose, s0, s1);
+    }
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;

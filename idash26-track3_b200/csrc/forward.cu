@@ -558,12 +558,12 @@ static void affinity_graph(E &x)
     sh.n = nA, sh.R = NMAX, sh.C = NMAX;
     Tn<T> L = x.mul(A, t, BC_ROW, sh);
     Tn<T> W = x.mul(L, t, BC_COL, sh);
-    Tn<T> Ah = x.gate(GATE_LRS, W);
+    Tn<T> Ah = x.gate(GATE_LRS_SPLIT, W);
     // GCN x3, aggregate first (gcn_layer.h:107-116)
     Tn<T> H = X;
     for (int l = 0; l < 3; l++) {
         Tn<T> Pm = x.matmul(Ah, H, LAYER_IN[l]);
-        Tn<T> AX = x.gate(GATE_LRS, Pm);
+        Tn<T> AX = x.gate(GATE_LRS_SPLIT, Pm);
         Tn<T> Z = x.fc(AX, l, B * NMAX);
         H = x.gate(GATE_RELU_ARS_SPLIT, Z);
     }
@@ -571,7 +571,7 @@ static void affinity_graph(E &x)
     EwShape shm;
     shm.n = nM;
     Tn<T> prod = x.mul(H, M, BC_NONE, shm);
-    Tn<T> cur = x.gate(GATE_LRS, prod);
+    Tn<T> cur = x.gate(GATE_LRS_SPLIT, prod);
     int cnt = NMAX;
     while (cnt > 1) {
         Tn<T> even, diff;
@@ -619,6 +619,7 @@ static int dealer_t(int bw, int s, int B, uint64_t seed, const DevWeights &w, ui
             e.err = DDG_ERR_CUDA;
         }
     }
+    if (e.err == DDG_OK) e.err = ring_gemm_tc_check(st);
     e.free_all();
     return e.err;
 }
@@ -673,6 +674,7 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         set_last_error("forward: %s", cudaGetErrorString(ce));
         e.err = DDG_ERR_CUDA;
     }
+    if (e.err == DDG_OK) e.err = ring_gemm_tc_check(P.stream);
     if (e.err != DDG_OK) {
         if (auto *lp = dynamic_cast<LocalPairChannel *>(P.chan)) lp->fail();
         return e.err;

@@ -25,13 +25,13 @@ struct GateKeygenArgs {
     GateLayout lay;
 };
 
-template <typename T>
-__global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant__ GateKeygenArgs<T> a)
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const __grid_constant__ GateKeygenArgs<T> a)
 {
     extern __shared__ uint32_t smem_tab[];
-    aes_stage_tables(smem_tab);
+    E::stage(smem_tab);
     __syncthreads();
-    AesLane A(smem_tab);
+    E A(smem_tab);
     const GateLayout &L = a.lay;
     const int n = a.n, s = a.s;
     const uint64_t N = a.N;
@@ -46,24 +46,25 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
             const T rho_c = T((bits ^ (bits >> 1)) & 1u);
             const T rho_L = T(((bits >> 2) ^ (bits >> 3)) & 1u);
             const T r_m = r >> (n - 1);
-            const T r_l = r & (T(~T(0)) >> 1);
             const T r_H = r >> s;
-            const T r_L = r & ((T(1) << s) - 1);
             const T e_b = r_m ^ rho_c;
             if (L.hi) {
+                // comparison threshold: bits [hi_shift, hi_shift + d) of the input mask
+                const uint64_t alpha = uint64_t(r >> L.hi_shift) & ((uint64_t(1) << L.H.d) - 1);
                 DcfOut o{a.k0 + L.H.root, a.k1 + L.H.root, a.k0 + L.H.cw, a.k1 + L.H.cw,
                          a.k0 + L.H.leaf, a.k1 + L.H.leaf, nullptr, nullptr};
                 if (L.H.eq)
-                    dcfeq_keygen(A, uint64_t(r_l >> s), L.H.d, A.prg(a.dk.rk, a.op, P_HI_S0, e),
-                                 A.prg(a.dk.rk, a.op, P_HI_DELTA, e), o, e, N);
+                    dcfeq_keygen(A, alpha, L.H.d, A.prg(a.dk.rk, a.op, P_HI_S0, e), A.prg(a.dk.rk, a.op, P_HI_DELTA, e),
+                                 o, e, N);
                 else
-                    dcf_keygen(A, uint64_t(r_l), n - 1, A.prg(a.dk.rk, a.op, P_HI_S0, e),
-                               A.prg(a.dk.rk, a.op, P_HI_DELTA, e), o, e, N);
+                    dcf_keygen(A, alpha, L.H.d, A.prg(a.dk.rk, a.op, P_HI_S0, e), A.prg(a.dk.rk, a.op, P_HI_DELTA, e),
+                               o, e, N);
             }
             if (L.lo) {
+                const uint64_t alpha = uint64_t(r) & ((uint64_t(1) << L.Lo.d) - 1);
                 DcfOut o{a.k0 + L.Lo.root, a.k1 + L.Lo.root, a.k0 + L.Lo.cw, a.k1 + L.Lo.cw,
                          a.k0 + L.Lo.leaf, a.k1 + L.Lo.leaf, nullptr, nullptr};
-                dcf_keygen(A, uint64_t(r_L), s, A.prg(a.dk.rk, a.op, P_LO_S0, e), A.prg(a.dk.rk, a.op, P_LO_DELTA, e), o,
+                dcf_keygen(A, alpha, L.Lo.d, A.prg(a.dk.rk, a.op, P_LO_S0, e), A.prg(a.dk.rk, a.op, P_LO_DELTA, e), o,
                            e, N);
             }
             T v[32];
@@ -86,6 +87,10 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
             case GATE_RELU_SPLIT:
                 for (int k = 0; k < 7; k++) v[k] = mono[k], v[8 + k] = mono[k] * r;
                 v[7] = r, v[15] = r_y;
+                break;
+            case GATE_LRS_SPLIT:
+                // carry = c1 + e1*c2 (exclusive terms); masks rho_c (c1), rho_e (e1), rho_L (c2)
+                v[0] = r_H, v[1] = rho_c, v[2] = rho_e, v[3] = rho_L, v[4] = rho_e * rho_L, v[5] = r_m, v[6] = r_y;
                 break;
             case GATE_RELU_ARS_SPLIT: {
                 const T nj[3] = {r_H, rho_L, r_m};
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(256) gate_keygen_kernel(const __grid_constant_
 
 template <typename T>
 struct Round1Args {
-    int n, s, hi_d;
+    int n, s, hi_d, hi_shift, lo_d;
     uint64_t N;
     const T *xhat;
     DcfView hi, lo;
@@ -146,31 +151,32 @@ struct Round1Args {
     uint32_t *bits_hi, *bits_lo;  // split gates: bits_hi[0, nw) compare, [nw, 2nw) equality
 };
 
-template <typename T>
-__global__ void __launch_bounds__(256, 3) gate_round1_kernel(const __grid_constant__ Round1Args<T> a)
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_round1_kernel(const __grid_constant__ Round1Args<T> a)
 {
     extern __shared__ uint32_t smem_tab[];
-    aes_stage_tables(smem_tab);
+    E::stage(smem_tab);
     __syncthreads();
-    AesLane A(smem_tab);
+    E A(smem_tab);
     const uint64_t N = a.N;
     const uint64_t Npad = (N + 31) & ~uint64_t(31);
-    const T hmask = T(~T(0)) >> 1;
-    const T lmask = (T(1) << a.s) - 1;
+    const T hmask = (T(1) << a.hi_d) - 1;
+    const T lmask = (T(1) << a.lo_d) - 1;
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
         const bool valid = e < N;
         uint32_t bh = 0, bl = 0, be = 0;
         if (valid) {
             const T x = __ldcs(a.xhat + e);
             if (a.has_hi) {
+                const uint64_t xh = uint64_t((x >> a.hi_shift) & hmask);
                 if (a.split) {
-                    const uint32_t b = dcfeq_eval(A, uint64_t((x & hmask) >> a.s), a.hi_d, a.hi, e, N);
+                    const uint32_t b = dcfeq_eval(A, xh, a.hi_d, a.hi, e, N);
                     bh = b & 1u, be = b >> 1;
                 } else {
-                    bh = dcf_eval(A, uint64_t(x & hmask), a.n - 1, a.hi, e, N);
+                    bh = dcf_eval(A, xh, a.hi_d, a.hi, e, N);
                 }
             }
-            if (a.has_lo) bl = dcf_eval(A, uint64_t(x & lmask), a.s, a.lo, e, N);
+            if (a.has_lo) bl = dcf_eval(A, uint64_t(x & lmask), a.lo_d, a.lo, e, N);
         }
         const uint32_t wh = __ballot_sync(0xFFFFFFFFu, bh);
         const uint32_t wl = __ballot_sync(0xFFFFFFFFu, bl);
@@ -210,7 +216,7 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
         T ch = 0, cl = 0, eh = 0;
         if (KIND != GATE_LRS) ch = T(((a.hi_own[wi] ^ a.hi_peer[wi]) >> bi) & 1u);
         if (KIND != GATE_RELU) cl = T(((a.lo_own[wi] ^ a.lo_peer[wi]) >> bi) & 1u);
-        if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT)
+        if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT || KIND == GATE_LRS_SPLIT)
             eh = T(((a.hi_own[a.nw + wi] ^ a.hi_peer[a.nw + wi]) >> bi) & 1u);
         const T mh = x >> (n - 1);
         const T xH = x >> s;
@@ -255,6 +261,11 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
                 }
                 y = p0 * a0 * Y0 + Y0 * sm + a0 * sn + smn + W(31);
             }
+        } else if (KIND == GATE_LRS_SPLIT) {
+            // carry = c1 + e1*c2 with c1 = ch ^ rho_c, e1 = eh ^ rho_e, c2 = cl ^ rho_L
+            const T sc1 = T(1) - T(2) * ch, se = T(1) - T(2) * eh;
+            y = p0 * (xH - ch - eh * cl) - W(0) - sc1 * W(1) - cl * se * W(2) - eh * b1 * W(3) - se * b1 * W(4) +
+                two_ns * (T(1) - mh) * W(5) + W(6);
         } else if (KIND == GATE_ARS) {
             const T pub = xH - cl + two_ns * (mh * ch - mh);
             y = p0 * pub - W(0) - b1 * W(1) +
@@ -270,32 +281,36 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
 
 // ---------------------------------------------------------------- launchers
 
-static int g_num_sms = 0;
-
 int device_sms()
 {
     int dev = 0;
     DDG_CUDA(cudaGetDevice(&dev));
     int sms = 0;
     DDG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    g_num_sms = sms;
     return sms;
 }
 
-template <typename K>
+template <class E, typename K>
 static int set_smem(K kernel)
 {
-    DDG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
+    DDG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, E::SMEM));
     return DDG_OK;
 }
 
-static int aes_grid(uint64_t N, int per_sm)
+template <typename T, class E>
+static int keygen_launch(const GateKeygenArgs<T> &a, cudaStream_t st)
 {
-    int sms = device_sms();
-    if (sms <= 0) sms = 148;
-    uint64_t need = (N + 255) / 256;
-    uint64_t full = uint64_t(sms) * per_sm;
-    return int(need < full ? (need ? need : 1) : full);
+    DDG_TRY(set_smem<E>(gate_keygen_kernel<T, E>));
+    gate_keygen_kernel<T, E><<<aes_blocks<E>(a.N), E::THREADS, E::SMEM, st>>>(a);
+    return DDG_OK;
+}
+
+template <typename T, class E>
+static int round1_launch(const Round1Args<T> &a, cudaStream_t st)
+{
+    DDG_TRY(set_smem<E>(gate_round1_kernel<T, E>));
+    gate_round1_kernel<T, E><<<aes_blocks<E>(a.N), E::THREADS, E::SMEM, st>>>(a);
+    return DDG_OK;
 }
 
 template <typename T>
@@ -312,8 +327,7 @@ int gate_keygen_t(const GateLayout &L, uint64_t seed, uint32_t op, const void *r
     a.k1 = static_cast<uint8_t *>(k1);
     a.lay = L;
     if (L.n == 0) return DDG_OK;
-    DDG_TRY(set_smem(gate_keygen_kernel<T>));
-    gate_keygen_kernel<T><<<aes_grid(L.n, 3), 256, AES_SMEM_BYTES, st>>>(a);
+    DDG_TRY((aes_tables() == 4 ? keygen_launch<T, AesLane4>(a, st) : keygen_launch<T, AesLane2>(a, st)));
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
@@ -326,14 +340,13 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
     DDG_TRY(aes_device_init());
     if (L.n == 0) return DDG_OK;
     Round1Args<T> a;
-    a.n = L.bw, a.s = L.s, a.N = L.n, a.hi_d = L.H.d;
+    a.n = L.bw, a.s = L.s, a.N = L.n, a.hi_d = L.H.d, a.hi_shift = L.hi_shift, a.lo_d = L.Lo.d;
     a.xhat = static_cast<const T *>(xhat);
     const uint8_t *k = static_cast<const uint8_t *>(key);
     a.has_hi = L.hi, a.has_lo = L.lo, a.split = L.hi && L.H.eq;
     a.hi = L.hi ? dcf_view(k, L.H) : DcfView{};
     a.lo = L.lo ? dcf_view(k, L.Lo) : DcfView{};
     a.bits_hi = bits_hi, a.bits_lo = bits_lo;
-    DDG_TRY(set_smem(gate_round1_kernel<T>));
     DcfTiming *tm = dcf_timing_sink();
     DcfTiming::Rec *rec = nullptr;
     if (tm && tm->enabled && tm->nrec < int(sizeof(tm->recs) / sizeof(tm->recs[0]))) {
@@ -342,7 +355,7 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
         DDG_CUDA(cudaEventCreate(&rec->b));
         DDG_CUDA(cudaEventRecord(rec->a, st));
     }
-    gate_round1_kernel<T><<<aes_grid(L.n, 3), 256, AES_SMEM_BYTES, st>>>(a);
+    DDG_TRY((aes_tables() == 4 ? round1_launch<T, AesLane4>(a, st) : round1_launch<T, AesLane2>(a, st)));
     note_launch();
     DDG_CUDA(cudaGetLastError());
     if (rec) {
@@ -379,6 +392,7 @@ int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32
     case GATE_ARS: gate_round2_kernel<T, GATE_ARS><<<grid, 256, 0, st>>>(a); break;
     case GATE_RELU_SPLIT: gate_round2_kernel<T, GATE_RELU_SPLIT><<<grid, 256, 0, st>>>(a); break;
     case GATE_RELU_ARS_SPLIT: gate_round2_kernel<T, GATE_RELU_ARS_SPLIT><<<grid, 256, 0, st>>>(a); break;
+    case GATE_LRS_SPLIT: gate_round2_kernel<T, GATE_LRS_SPLIT><<<grid, 256, 0, st>>>(a); break;
     default: gate_round2_kernel<T, GATE_LRS><<<grid, 256, 0, st>>>(a); break;
     }
     note_launch();

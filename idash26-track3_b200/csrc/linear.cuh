@@ -21,8 +21,20 @@ struct GemmArgs {
     int64_t ldc = 0, sC = 0;
 };
 
+// tensor-core limb GEMM where the shape allows (ring_gemm_tc.cu), else the CUDA-core kernel
 template <typename T>
 int ring_gemm(const GemmArgs<T> &a, cudaStream_t st);
+// the CUDA-core kernel (ring_gemm.cu)
+template <typename T>
+int ring_gemm_simt(const GemmArgs<T> &a, cudaStream_t st);
+// DDG_OK unless a tensor-core GEMM launch gave up on one of its bounded waits
+// since the last clear (reads a device word: synchronises with the device)
+int ring_gemm_tc_error(bool clear);
+// the same check ordered on stream st (waits for st only; does not clear)
+int ring_gemm_tc_check(cudaStream_t st);
+// 0: tensor cores where the shape allows (default), 1: CUDA cores only
+void set_gemm_path(int path);
+int gemm_path();
 
 // broadcast pattern of the second operand of an elementwise product over
 // (B, R, C) = (batch, rows, cols):  none (same shape), row (index b*R + i),

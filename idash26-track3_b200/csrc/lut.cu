@@ -60,13 +60,13 @@ struct LutKeygenArgs {
     uint8_t *k0, *k1;
 };
 
-template <typename T>
-__global__ void __launch_bounds__(256) lut_keygen_kernel(const __grid_constant__ LutKeygenArgs<T> a)
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) lut_keygen_kernel(const __grid_constant__ LutKeygenArgs<T> a)
 {
     extern __shared__ uint32_t smem_tab[];
-    aes_stage_tables(smem_tab);
+    E::stage(smem_tab);
     __syncthreads();
-    AesLane A(smem_tab);
+    E A(smem_tab);
     constexpr int EPL = 16 / sizeof(T);
     const uint64_t n = a.L.n;
     const int L = a.L.L;
@@ -116,15 +116,15 @@ struct LutEvalArgs {
     T *share;
 };
 
-template <typename T>
-__global__ void __launch_bounds__(256) lut_eval_kernel(const __grid_constant__ LutEvalArgs<T> a)
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) lut_eval_kernel(const __grid_constant__ LutEvalArgs<T> a)
 {
     extern __shared__ uint32_t smem_tab[];
     __shared__ T tab[256];
-    aes_stage_tables(smem_tab);
+    E::stage(smem_tab);
     for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = a.table[i];
     __syncthreads();
-    AesLane A(smem_tab);
+    E A(smem_tab);
     constexpr int EPL = 16 / sizeof(T);
     const uint64_t n = a.L.n;
     const int L = a.L.L, Lr = L - 5;
@@ -169,11 +169,20 @@ __global__ void __launch_bounds__(256) lut_eval_kernel(const __grid_constant__ L
     }
 }
 
-static int lut_grid(uint64_t threads)
+template <typename T, class E>
+static int lut_keygen_launch(const LutKeygenArgs<T> &a, cudaStream_t st)
 {
-    int sms = device_sms();
-    uint64_t need = (threads + 255) / 256, full = uint64_t(sms > 0 ? sms : 148) * 3;
-    return int(need < full ? (need ? need : 1) : full);
+    DDG_CUDA(cudaFuncSetAttribute(lut_keygen_kernel<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, E::SMEM));
+    lut_keygen_kernel<T, E><<<aes_blocks<E>(a.L.n), E::THREADS, E::SMEM, st>>>(a);
+    return DDG_OK;
+}
+
+template <typename T, class E>
+static int lut_eval_launch(const LutEvalArgs<T> &a, cudaStream_t st)
+{
+    DDG_CUDA(cudaFuncSetAttribute(lut_eval_kernel<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, E::SMEM));
+    lut_eval_kernel<T, E><<<aes_blocks<E>(a.L.n * 32), E::THREADS, E::SMEM, st>>>(a);  // a warp per lookup
+    return DDG_OK;
 }
 
 template <typename T>
@@ -182,9 +191,8 @@ int lut_keygen(const LutLayout &L, const AesKey &dk, uint32_t op, const T *alpha
 {
     if (!L.n) return DDG_OK;
     DDG_TRY(aes_device_init());
-    DDG_CUDA(cudaFuncSetAttribute(lut_keygen_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
     LutKeygenArgs<T> a{L, dk, op, alpha_mask, rout, k0, k1};
-    lut_keygen_kernel<T><<<lut_grid(L.n), 256, AES_SMEM_BYTES, st>>>(a);
+    DDG_TRY((aes_tables() == 4 ? lut_keygen_launch<T, AesLane4>(a, st) : lut_keygen_launch<T, AesLane2>(a, st)));
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
@@ -196,9 +204,8 @@ int lut_eval(const LutLayout &L, int party, const T *xhat, const T *table, const
 {
     if (!L.n) return DDG_OK;
     DDG_TRY(aes_device_init());
-    DDG_CUDA(cudaFuncSetAttribute(lut_eval_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AES_SMEM_BYTES));
     LutEvalArgs<T> a{L, party, xhat, table, key, share};
-    lut_eval_kernel<T><<<lut_grid(L.n * 32), 256, AES_SMEM_BYTES, st>>>(a);
+    DDG_TRY((aes_tables() == 4 ? lut_eval_launch<T, AesLane4>(a, st) : lut_eval_launch<T, AesLane2>(a, st)));
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;

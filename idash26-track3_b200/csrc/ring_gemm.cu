@@ -1,5 +1,7 @@
 // Ring GEMMs over Z_2^32 / Z_2^64 on the CUDA cores (integer multiply-add
-// wraps modulo 2^bits natively).  One kernel serves every linear layer:
+// wraps modulo 2^bits natively).  The tensor-core kernel (ring_gemm_tc.cu) is
+// the default; this one serves reduction lengths beyond its exactness bound
+// and the comparison tests.  One kernel serves every linear layer:
 //
 //   C[b] = sign * ( A1[b] . (s1*B1[b] - B1m[b])  -  A2[b] . B2[b] ) + bias + Add[b]
 //
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(256) ring_gemm_kernel(const __grid_constant__ 
 }
 
 template <typename T>
-int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
+int ring_gemm_simt(const GemmArgs<T> &a, cudaStream_t st)
 {
     if (a.M == 0 || a.N == 0 || a.batch == 0) return DDG_OK;
     dim3 grid((a.N + GT - 1) / GT, (a.M + GT - 1) / GT, a.batch);
@@ -121,7 +123,7 @@ int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
     return DDG_OK;
 }
 
-template int ring_gemm<uint32_t>(const GemmArgs<uint32_t> &, cudaStream_t);
-template int ring_gemm<uint64_t>(const GemmArgs<uint64_t> &, cudaStream_t);
+template int ring_gemm_simt<uint32_t>(const GemmArgs<uint32_t> &, cudaStream_t);
+template int ring_gemm_simt<uint64_t>(const GemmArgs<uint64_t> &, cudaStream_t);
 
 }  // namespace ddg

@@ -1,0 +1,460 @@
+// Ring GEMMs over Z_2^32 / Z_2^64 on the 5th-generation tensor cores.
+//
+// Same contract as the CUDA-core kernel in ring_gemm.cu (GemmArgs):
+//
+//   C[b] = sign * ( A1[b] . (s1*B1[b] - B1m[b])  -  A2[b] . B2[b] ) + bias + Add[b]
+//
+// Exactness by 8-bit limb splitting.  Every ring element a = sum_i a_i 2^(8i)
+// with unsigned bytes a_i (P = sizeof(T) limbs).  Modulo 2^(8P)
+//
+//   (A.B)[m,n] = sum_{s<P} 2^(8s) * S_s[m,n],   S_s = sum_{i+j=s} A_i . B_j ,
+//
+// so only the P(P+1)/2 limb products with i+j < P are needed (10 for Z_2^32,
+// 36 for Z_2^64).  Each A_i . B_j is a u8 x u8 GEMM with exact int32
+// accumulation (tcgen05.mma kind::i8); the P partial sums S_s live side by
+// side in tensor memory and the epilogue recombines them with shifts, so the
+// result is exact modulo 2^(8P) as long as no S_s exceeds 2^31 before its
+// shift, i.e. (s+1) * K * 255^2 < 2^31 for every s (K <= 4096 at P = 8,
+// K <= 8192 at P = 4; the host sends larger K to the CUDA-core kernel).
+//
+// The two products of the Beaver form are one GEMM over the concatenated
+// reduction dimension: C = [A1 | A2] . [sign*(s1*B1 - B1m) ; -sign*B2], so
+// the B operand is formed (and negated) in the loader, modulo 2^(8P).
+//
+// Per CTA: a 128 x BN output tile, 256 threads.  The K loop moves 32 ring
+// elements of K per stage (one MMA K-step for 8-bit operands).  All threads
+// load the stage's A (128 x 32) and B (32 x BN) ring elements from global
+// memory, split them into P byte planes with byte permutes and store the
+// planes in shared memory in the canonical no-swizzle UMMA layouts (A K-major,
+// B either MN-major or K-major).  After fence.proxy.async + a CTA barrier one
+// thread issues the limb MMAs for the stage and commits them to the stage's
+// mbarrier; the stage is rewritten only after that mbarrier completes.  Two
+// stages: the loads of stage k+1 are in flight while the MMAs of stage k run.
+// Every mbarrier wait is bounded (about two seconds of %globaltimer); a wait
+// that gives up sets the error word and the CTA skips to freeing its tensor
+// memory, so a fault in this logic shows up as a status code, not a hang.
+#include "common.cuh"
+#include "linear.cuh"
+
+namespace ddg {
+
+namespace {
+
+constexpr int TC_BM = 128;       // tile rows (TMEM lanes)
+constexpr int TC_BK = 32;        // K elements per stage = one kind::i8 MMA K-step
+constexpr int TC_THREADS = 256;  // 8 warps
+constexpr uint64_t TC_WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// shared-memory matrix descriptor, no swizzle (layout type 0), version 1
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+    return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+           (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
+}
+
+// instruction descriptor of kind::i8: u8 x u8 -> s32, A K-major, M = 128
+__host__ __device__ constexpr uint32_t i8_idesc(int bn, bool b_mn_major)
+{
+    return (2u << 4)                          // D format s32
+           | (0u << 7) | (0u << 10)           // A, B unsigned 8-bit
+           | ((b_mn_major ? 1u : 0u) << 16)   // B major
+           | (uint32_t(bn >> 3) << 17)        // N >> 3
+           | (uint32_t(TC_BM >> 4) << 24);    // M >> 4
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// wait until the phase with the given parity of `bar` has completed; false
+// after TC_WAIT_NS (or 2^26 polls) without completion
+__device__ bool mbar_wait(uint64_t *bar, uint32_t parity)
+{
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1; it < (1u << 26); ++it) {
+        if (mbar_test(bar, parity)) return true;
+        if ((it & 255u) == 0 && global_ns() - t0 > TC_WAIT_NS) return false;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// the four byte planes of four consecutive 32-bit words: plane q holds byte q of e0..e3
+__device__ __forceinline__ void byte_planes(uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3, uint32_t (&p)[4])
+{
+    const uint32_t lo01 = __byte_perm(e0, e1, 0x5140), lo23 = __byte_perm(e2, e3, 0x5140);
+    const uint32_t hi01 = __byte_perm(e0, e1, 0x7362), hi23 = __byte_perm(e2, e3, 0x7362);
+    p[0] = __byte_perm(lo01, lo23, 0x5410);
+    p[1] = __byte_perm(lo01, lo23, 0x7632);
+    p[2] = __byte_perm(hi01, hi23, 0x5410);
+    p[3] = __byte_perm(hi01, hi23, 0x7632);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_planes(uint8_t *base, uint32_t plane_bytes, uint32_t off, const T (&e)[4])
+{
+    uint32_t p[4];
+    byte_planes(uint32_t(e[0]), uint32_t(e[1]), uint32_t(e[2]), uint32_t(e[3]), p);
+#pragma unroll
+    for (int q = 0; q < 4; q++) *reinterpret_cast<uint32_t *>(base + q * plane_bytes + off) = p[q];
+    if constexpr (sizeof(T) == 8) {
+        byte_planes(uint32_t(uint64_t(e[0]) >> 32), uint32_t(uint64_t(e[1]) >> 32), uint32_t(uint64_t(e[2]) >> 32),
+                    uint32_t(uint64_t(e[3]) >> 32), p);
+#pragma unroll
+        for (int q = 0; q < 4; q++) *reinterpret_cast<uint32_t *>(base + (4 + q) * plane_bytes + off) = p[q];
+    }
+}
+
+constexpr int tmem_cols(int n)
+{
+    int c = 32;
+    while (c < n) c <<= 1;
+    return c;
+}
+
+// Per-stage shared-memory and tensor-memory budget of one CTA.
+template <typename T, int BN, bool B_MN>
+struct TcShape {
+    static constexpr int P = int(sizeof(T));
+    static constexpr int A_PLANE = TC_BM * TC_BK;  // bytes of one A byte plane per stage
+    static constexpr int B_PLANE = BN * TC_BK;     // bytes of one B byte plane per stage
+    static constexpr int STAGE = P * (A_PLANE + B_PLANE);
+    // 8 KiB of slack after the two stages: a descriptor whose strides the
+    // hardware read differently from this layout still stays inside the CTA's
+    // shared memory (the tests then fail on values, not on an address)
+    static constexpr int SMEM = 2 * STAGE + 8192;
+    static constexpr int NCOL = tmem_cols(P * BN);
+    static constexpr int A_ITEMS = TC_BM * TC_BK / 4 / TC_THREADS;  // 4-element items per thread
+    static constexpr int B_ITEMS = BN * TC_BK / 4 / TC_THREADS;
+    static_assert(P * BN <= 512, "accumulators exceed tensor memory");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+    static_assert(B_ITEMS >= 1, "B tile too small for the loader mapping");
+};
+
+template <typename T, int BN, bool B_MN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    ring_gemm_tc_kernel(const __grid_constant__ GemmArgs<T> a, int nk0, int nk1, uint32_t *err)
+{
+    using S = TcShape<T, BN, B_MN>;
+    constexpr int P = S::P;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ uint32_t s_tmem;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.z;
+    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
+    const int nk = nk0 + nk1;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
+                     "r"(S::NCOL)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    // per-batch operand bases
+    const T *A1 = a.A1 + int64_t(b) * a.sA1;
+    const T *A2 = a.A2 ? a.A2 + int64_t(b) * a.sA2 : nullptr;
+    const T *B1 = a.B1 ? a.B1 + int64_t(b) * a.sB1 : nullptr;
+    const T *B1m = a.B1m ? a.B1m + int64_t(b) * a.sB1m : nullptr;
+    const T *B2 = a.B2 ? a.B2 + int64_t(b) * a.sB2 : nullptr;
+    const T sgn = a.sign, s1 = a.s1;
+
+    // loader item coordinates (fixed per thread): A item j covers row ar[j],
+    // K elements 4*akq .. 4*akq+3 of the stage; see the layout notes above.
+    const int akq = 4 * (warp & 1) + (lane & 3);
+    T ra[S::A_ITEMS][4], rb[S::B_ITEMS][4];
+
+    auto load_stage = [&](int kb) {
+        const bool ph1 = kb >= nk0;
+        const int kbase = (ph1 ? kb - nk0 : kb) * TC_BK;
+        const T *A = ph1 ? A2 : A1;
+        const int64_t lda = ph1 ? a.lda2 : a.lda1;
+#pragma unroll
+        for (int j = 0; j < S::A_ITEMS; j++) {
+            const int row = 8 * (warp >> 1) + 32 * j + (lane >> 2);
+            const int m = m0 + row, k = kbase + 4 * akq;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                ra[j][e] = (m < a.M && k + e < a.K) ? __ldg(A + int64_t(m) * lda + k + e) : T(0);
+        }
+        const int64_t ldb = ph1 ? a.ldb2 : a.ldb1;
+#pragma unroll
+        for (int j = 0; j < S::B_ITEMS; j++) {
+            const int w = warp + 8 * j;  // warp-slot index of this item
+            int k, n, dk, dn;            // element e sits at (k + e*dk, n + e*dn)
+            if constexpr (B_MN) {
+                constexpr int NG = BN / 16;
+                k = kbase + 8 * (w / NG) + (lane >> 2), n = n0 + 16 * (w % NG) + 4 * (lane & 3), dk = 0, dn = 1;
+            } else {
+                k = kbase + 16 * (w & 1) + 4 * (lane & 3), n = n0 + 8 * (w >> 1) + (lane >> 2), dk = 1, dn = 0;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int ke = k + e * dk, ne = n + e * dn;
+                T v = 0;
+                if (ke < a.K && ne < a.N) {
+                    const int64_t o = int64_t(ke) * ldb + ne;
+                    if (ph1) {
+                        v = T(0) - sgn * __ldg(B2 + o);
+                    } else {
+                        if (B1) v = s1 * __ldg(B1 + o);
+                        if (B1m) v -= __ldg(B1m + o);
+                        v *= sgn;
+                    }
+                }
+                rb[j][e] = v;
+            }
+        }
+    };
+
+    auto store_stage = [&](int st) {
+        uint8_t *base = smem + st * S::STAGE;
+#pragma unroll
+        for (int j = 0; j < S::A_ITEMS; j++) {
+            const int row = 8 * (warp >> 1) + 32 * j + (lane >> 2);
+            const uint32_t off = (row >> 3) * 256 + (akq >> 2) * 128 + (row & 7) * 16 + (akq & 3) * 4;
+            store_planes<T>(base, S::A_PLANE, off, ra[j]);
+        }
+        uint8_t *bbase = base + P * S::A_PLANE;
+#pragma unroll
+        for (int j = 0; j < S::B_ITEMS; j++) {
+            const int w = warp + 8 * j;
+            uint32_t off;
+            if constexpr (B_MN) {
+                constexpr int NG = BN / 16;
+                off = (w % NG) * 128 + (w / NG) * (8 * BN) + 4 * lane;
+            } else {
+                off = (w >> 1) * 256 + (w & 1) * 128 + 4 * lane;
+            }
+            store_planes<T>(bbase, S::B_PLANE, off, rb[j]);
+        }
+    };
+
+    constexpr uint32_t IDESC = i8_idesc(BN, B_MN);
+    constexpr uint32_t B_LBO = B_MN ? 8 * BN : 128, B_SBO = B_MN ? 128 : 256;
+    bool ok = true;
+
+    if (nk > 0) load_stage(0);
+    for (int kb = 0; kb < nk; kb++) {
+        const int st = kb & 1;
+        // stage st is free once the MMAs committed two K-steps ago have completed
+        bool mine = true;
+        if (kb >= 2) mine = mbar_wait(&bars[st], uint32_t(((kb >> 1) - 1) & 1));
+        if (mine) store_stage(st);
+        if (kb + 1 < nk) load_stage(kb + 1);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        // CTA-uniform: every thread leaves the loop together if any wait gave up
+        if (!__syncthreads_and(mine ? 1 : 0)) {
+            ok = false;
+            break;
+        }
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t sa = smem_addr(smem + st * S::STAGE);
+            const uint32_t sb = sa + P * S::A_PLANE;
+#pragma unroll
+            for (int i = 0; i < P; i++) {
+                const uint64_t da = smem_desc(sa + i * S::A_PLANE, 128, 256);
+#pragma unroll
+                for (int j = 0; j + i < P; j++) {
+                    const uint64_t db = smem_desc(sb + j * S::B_PLANE, B_LBO, B_SBO);
+                    mma_i8(tmem + uint32_t((i + j) * BN), da, db, IDESC, (kb > 0 || i > 0) ? 1u : 0u);
+                }
+            }
+            mma_commit(&bars[st]);
+        }
+    }
+    // the last commit covers every MMA issued before it
+    if (ok && nk > 0) ok = mbar_wait(&bars[(nk - 1) & 1], uint32_t(((nk - 1) >> 1) & 1));
+    // a CTA-uniform verdict: every thread saw the same barrier phases unless one timed out
+    const int all_ok = __syncthreads_and(ok ? 1 : 0);
+    tc_fence_after();
+
+    if (all_ok) {
+        // epilogue: warp w reads TMEM lanes 32*(w%4).. (rows) and half (w/4) of the columns
+        const int q = warp & 3, h = warp >> 2;
+        const int m = m0 + 32 * q + lane;
+        const T *Add = a.Add ? a.Add + int64_t(b) * a.sAdd : nullptr;
+        T *C = a.C + int64_t(b) * a.sC;
+#pragma unroll 1
+        for (int c = h * (BN / 2); c < (h + 1) * (BN / 2); c += 8) {
+            T r[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) r[e] = 0;
+#pragma unroll
+            for (int s = 0; s < P; s++) {
+                uint32_t v[8];
+                tmem_ld8(tmem + (uint32_t(32 * q) << 16) + uint32_t(s * BN + c), v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 8; e++) r[e] += T(v[e]) << (8 * s);
+            }
+            if (m < a.M) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int n = n0 + c + e;
+                    if (n < a.N) {
+                        T v = r[e];
+                        if (a.bias) v += a.bias[n];
+                        if (Add) v += Add[int64_t(m) * a.ldAdd + n];
+                        C[int64_t(m) * a.ldc + n] = v;
+                    }
+                }
+            }
+        }
+    } else if (tid == 0) {
+        atomicOr(err, 1u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::NCOL) : "memory");
+    }
+}
+
+__device__ uint32_t g_tc_err;
+
+// 0: tensor cores, B MN-major, 64-column tiles (default); 1: CUDA cores only;
+// 2: tensor cores, B K-major; 3: tensor cores, 128-column tiles (Z_2^32) or
+// 32-column tiles (Z_2^64).  2 and 3 exist for the layout/tile comparison tests.
+int g_gemm_path = 0;
+
+template <typename T, int BN, bool B_MN>
+int launch_tc(const GemmArgs<T> &a, cudaStream_t st)
+{
+    using S = TcShape<T, BN, B_MN>;
+    auto kern = ring_gemm_tc_kernel<T, BN, B_MN>;
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    DDG_CUDA(cudaGetDevice(&dev));
+    if (configured_dev != dev) {
+        DDG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM));
+        configured_dev = dev;
+    }
+    uint32_t *err = nullptr;
+    DDG_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_tc_err));
+    DDG_CHECK(a.A1 && a.C && (!a.A2 || a.B2), DDG_ERR_ARG, "gemm: missing operand");
+    const int nk0 = (a.K + TC_BK - 1) / TC_BK;
+    const int nk1 = a.A2 ? nk0 : 0;
+    dim3 grid((a.N + BN - 1) / BN, (a.M + TC_BM - 1) / TC_BM, a.batch);
+    DDG_CHECK(grid.y <= 65535 && grid.z <= 65535, DDG_ERR_ARG, "gemm grid too large (M=%d batch=%d)", a.M, a.batch);
+    kern<<<grid, TC_THREADS, S::SMEM, st>>>(a, nk0, nk1, err);
+    note_launch();
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+}  // namespace
+
+int ring_gemm_tc_error(bool clear)
+{
+    uint32_t v = 0;
+    DDG_CUDA(cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(v)));
+    if (clear && v) {
+        const uint32_t z = 0;
+        DDG_CUDA(cudaMemcpyToSymbol(g_tc_err, &z, sizeof(z)));
+    }
+    DDG_CHECK(v == 0, DDG_ERR_CUDA, "tensor-core ring GEMM: an mbarrier wait gave up (error word %u)", v);
+    return DDG_OK;
+}
+
+int ring_gemm_tc_check(cudaStream_t st)
+{
+    uint32_t v = 0;
+    DDG_CUDA(cudaMemcpyFromSymbolAsync(&v, g_tc_err, sizeof(v), 0, cudaMemcpyDeviceToHost, st));
+    DDG_CUDA(cudaStreamSynchronize(st));
+    DDG_CHECK(v == 0, DDG_ERR_CUDA, "tensor-core ring GEMM: an mbarrier wait gave up (error word %u)", v);
+    return DDG_OK;
+}
+
+void set_gemm_path(int path) { g_gemm_path = path; }
+int gemm_path() { return g_gemm_path; }
+
+// largest reduction length (per phase) whose limb sums stay below 2^31
+template <typename T>
+constexpr int tc_max_k()
+{
+    return sizeof(T) == 4 ? 8192 : 4096;
+}
+
+template <typename T>
+int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
+{
+    if (a.M == 0 || a.N == 0 || a.batch == 0) return DDG_OK;
+    const int ktot = a.A2 ? 2 * a.K : a.K;
+    if (g_gemm_path == 1 || a.K == 0 || ktot > tc_max_k<T>()) return ring_gemm_simt<T>(a, st);
+    if (g_gemm_path == 2) return launch_tc<T, 64, false>(a, st);
+    if (g_gemm_path == 3) return launch_tc<T, sizeof(T) == 4 ? 128 : 32, true>(a, st);
+    return launch_tc<T, 64, true>(a, st);
+}
+
+template int ring_gemm<uint32_t>(const GemmArgs<uint32_t> &, cudaStream_t);
+template int ring_gemm<uint64_t>(const GemmArgs<uint64_t> &, cudaStream_t);
+
+}  // namespace ddg

@@ -41,6 +41,13 @@ extern "C" {
  * element at bw=32; round 1 emits three bit arrays (see ddg_gate_round1). */
 #define DDG_GATE_RELU_SPLIT 4
 #define DDG_GATE_RELU_ARS_SPLIT 5
+/* Same function as LRS with the scale-bit carry comparison 1{x_low < r_low}
+ * split into a DCF with equality output over its upper scale-s2 bits and a
+ * plain DCF over its low s2 = min(7, scale-1) bits: carry = c1 + e1*c2 (the
+ * two terms are exclusive).  2 instead of scale-6 AES-128 per element (2 vs 6
+ * at scale 12) for 7 key words instead of 4; scale >= 2.  Round 1 emits three
+ * bit arrays like the other split kinds. */
+#define DDG_GATE_LRS_SPLIT 6
 
 const char *ddg_last_error(void);
 int ddg_version(void);
@@ -64,10 +71,11 @@ int ddg_version(void);
 /* bytes of one party's key for n elements */
 uint64_t ddg_gate_key_bytes(int kind, int bw, int scale, uint64_t n);
 
-/* byte offsets of one party's key for n elements, written to out[14]:
+/* byte offsets of one party's key for n elements, written to out[16]:
  *   0 hi_root 1 hi_cw 2 hi_leaf 3 hi_mu 4 lo_root 5 lo_cw 6 lo_leaf 7 lo_mu
  *   8 words 9 total bytes 10 high-DCF tree levels 11 low-DCF tree levels
- *   12 hi_mu_eq (split kinds) 13 high-DCF domain bits
+ *   12 hi_mu_eq (split kinds) 13 high-DCF domain bits 14 position of the
+ *   high DCF's lowest input bit in x_hat 15 low-DCF domain bits
  * Each DCF is structure-of-arrays: root[n] 16 B, cw[levels][n] 16 B
  * (level-major), leaf[n] 16 B, mu[ceil(n/32)] u32 mask bits; then
  * nwords x n ring words.  Every array starts on a 256-byte boundary. */
@@ -248,6 +256,20 @@ int ddg_matmul_share(int bw, int party, int batch, int M, int K, int N, const vo
 int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, const void *d_w, const void *d_bias2s,
                  const void *d_c, void *d_out, void *stream);
 
+/* Ring GEMM engine of ddg_matmul_share / ddg_fc_share and the forward.
+ * path 0 (default): tcgen05 tensor cores, 8-bit limb products with int32
+ * accumulation recombined modulo 2^bw, operand B MN-major in shared memory,
+ * 128 x 64 output tiles; 1: CUDA cores (integer multiply-add); 2: tensor
+ * cores with B K-major; 3: tensor cores with 128 x 128 (bw 32) or 128 x 32
+ * (bw 64) tiles.  Reduction lengths beyond the limb sums' exactness bound
+ * (K > 8192 at bw 32, K > 4096 at bw 64, counting both Beaver products) always
+ * use the CUDA cores.  Process-wide setting.
+ * ddg_gemm_status: DDG_OK, or DDG_ERR_CUDA when a tensor-core GEMM gave up on
+ * one of its bounded internal waits since the last call (and clears the
+ * flag); synchronises with the device. */
+int ddg_gemm_path(int path);
+int ddg_gemm_status(void);
+
 /* Kernel accounting.  ddg_launch_count: kernels this library has launched
  * (process-wide).  DCF timing: when enabled on a party, every gate round-1
  * (DCF) launch is bracketed by CUDA events on the party's stream; out6 gets
@@ -267,10 +289,15 @@ int ddg_parties_dcf_union(ddg_party *const *parties, int n);
  * hashes (one AES-128 each), one word per chain written to d_out.  Gives the
  * AES-blocks/s ceiling of the DCF kernels. */
 int ddg_aes_chain(uint64_t threads, int iters, uint32_t *d_out, void *stream);
-/* the same with the AES round variant chosen: 0 = the build's default,
- * 1 = byte extraction and rotations on the integer ALU (shifts / PRMT),
- * 2 = byte-3 extraction and rotations as integer multiply-adds */
+/* the same with the AES engine chosen: 0 = the one in use (ddg_aes_tables),
+ * 2 or 4 = that many staged round tables */
 int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_out, void *stream);
+/* AES engine of every FSS kernel (DCF evaluation and key generation, DPF
+ * LUT, dealer PRG), process-wide: 4 (default) stages T0..T3 in 128 KiB of
+ * shared memory, one 768-thread CTA per SM, 6 integer-pipe instructions per
+ * round column; 2 stages T0 and T2 in 64 KiB, three 256-thread CTAs per SM,
+ * 8 instructions per column (T1 ^ T3 as an 8-bit rotation).  Same outputs. */
+int ddg_aes_tables(int tables);
 
 #ifdef __cplusplus
 }

@@ -287,7 +287,7 @@ void ref_dcfeq_keygen(int d, uint64_t alpha, const uint8_t s0[16], const uint8_t
                       uint8_t root0[16], uint8_t root1[16], uint8_t *cw, uint8_t leafcw[16])
 {
     if (!fixed_ready) fixed_init();
-    int L = d - 6;
+    int L = d > 6 ? d - 6 : 0;
     uint8_t delta[16], cur[2][16], h[2][16];
     memcpy(delta, delta_in, 16);
     delta[0] |= 1;
@@ -325,7 +325,7 @@ void ref_dcfeq_keygen(int d, uint64_t alpha, const uint8_t s0[16], const uint8_t
 int ref_dcfeq_eval(int d, uint64_t x, const uint8_t root[16], const uint8_t *cw, const uint8_t leafcw[16])
 {
     if (!fixed_ready) fixed_init();
-    int L = d - 6;
+    int L = d > 6 ? d - 6 : 0;
     uint8_t s[16], h[16], cl[16];
     memcpy(s, root, 16);
     int c = 0;
@@ -351,9 +351,17 @@ int ref_dcfeq_eval(int d, uint64_t x, const uint8_t root[16], const uint8_t *cw,
 
 /* ----------------------------------------------------------------- gates */
 
-enum { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5 };
+enum { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
+       GATE_LRS_SPLIT = 6 };
 
-static int is_split(int kind) { return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT; }
+/* kinds whose high DCF has an equality output */
+static int is_split(int kind)
+{
+    return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT || kind == GATE_LRS_SPLIT;
+}
+/* GATE_LRS_SPLIT: the s-bit carry comparison over (V1, V2), V2 the low
+ * lrs_lo_bits(s) bits: 1{V < B} = 1{V1 < B1} + 1{V1 == B1} * 1{V2 < B2} */
+static int lrs_lo_bits(int s) { return s - 1 < 7 ? s - 1 : 7; }
 
 enum {
     P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4,
@@ -383,11 +391,17 @@ int ref_gate_nwords(int kind)
     case GATE_ARS: return 6;
     case GATE_RELU_SPLIT: return 16;
     case GATE_RELU_ARS_SPLIT: return 32;
+    case GATE_LRS_SPLIT: return 7;
     default: return 4;
     }
 }
-/* domain bits of the high DCF: n-1, or the upper n-1-s bits for split gates */
-int ref_gate_hi_bits(int kind, int n, int s) { return is_split(kind) ? n - 1 - s : n - 1; }
+/* domain bits of the high DCF: n-1, the upper n-1-s bits for the split ReLU
+ * gates, the upper s - lrs_lo_bits(s) carry bits for GATE_LRS_SPLIT */
+int ref_gate_hi_bits(int kind, int n, int s)
+{
+    if (kind == GATE_LRS_SPLIT) return s - lrs_lo_bits(s);
+    return is_split(kind) ? n - 1 - s : n - 1;
+}
 
 /*
  * Dealer side for one element.  r_in is the input mask (x_hat = x + r_in),
@@ -426,7 +440,23 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
     uint64_t r_L = r_in & ((1ULL << s) - 1);
     uint64_t e = r_m ^ (uint64_t)rho_c;
 
-    if (ref_gate_has_hi(kind)) {
+    if (kind == GATE_LRS_SPLIT) {
+        int lo = lrs_lo_bits(s), hi = s - lo;
+        ref_prg(&ks, op, P_HI_S0, i, blk);
+        ref_prg(&ks, op, P_HI_DELTA, i, blk2);
+        ref_dcfeq_keygen(hi, r_L >> lo, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
+        memcpy(k1->hi_cw, k0->hi_cw, sizeof(k0->hi_cw));
+        memcpy(k1->hi_leaf, k0->hi_leaf, 16);
+        k0->hi_mu = mu0h, k1->hi_mu = mu1h;
+        k0->hi_mu_eq = mu0e, k1->hi_mu_eq = mu1e;
+        ref_prg(&ks, op, P_LO_S0, i, blk);
+        ref_prg(&ks, op, P_LO_DELTA, i, blk2);
+        ref_dcf_keygen(lo, r_L & ((1ULL << lo) - 1), blk, blk2, k0->lo_root, k1->lo_root, &k0->lo_cw[0][0],
+                       k0->lo_leaf);
+        memcpy(k1->lo_cw, k0->lo_cw, sizeof(k0->lo_cw));
+        memcpy(k1->lo_leaf, k0->lo_leaf, 16);
+        k0->lo_mu = mu0l, k1->lo_mu = mu1l;
+    } else if (ref_gate_has_hi(kind)) {
         ref_prg(&ks, op, P_HI_S0, i, blk);
         ref_prg(&ks, op, P_HI_DELTA, i, blk2);
         if (is_split(kind))
@@ -442,7 +472,7 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
             k1->hi_mu_eq = mu1e;
         }
     }
-    if (ref_gate_has_lo(kind)) {
+    if (ref_gate_has_lo(kind) && kind != GATE_LRS_SPLIT) {
         ref_prg(&ks, op, P_LO_S0, i, blk);
         ref_prg(&ks, op, P_LO_DELTA, i, blk2);
         ref_dcf_keygen(s, r_L, blk, blk2, k0->lo_root, k1->lo_root, &k0->lo_cw[0][0], k0->lo_leaf);
@@ -474,6 +504,10 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
         v[7] = r_in;
         v[15] = r_y;
         break;
+    case GATE_LRS_SPLIT:
+        /* carry = c1 + e1*c2; masks rho_c (c1), rho_e (e1), rho_L (c2) */
+        v[0] = r_H; v[1] = (uint64_t)rho_c; v[2] = pe; v[3] = pl; v[4] = pe * pl; v[5] = r_m; v[6] = r_y;
+        break;
     case GATE_RELU_ARS_SPLIT: {
         uint64_t nj[3] = {r_H, pl, r_m};
         for (int k = 0; k < 7; k++) v[k] = mono[k];
@@ -503,6 +537,14 @@ int ref_gate_round1(int kind, int n, int s, uint64_t xhat, const ref_gate_key *k
     uint64_t M = nmask(n);
     xhat &= M;
     int out = 0;
+    if (kind == GATE_LRS_SPLIT) {
+        int lo = lrs_lo_bits(s), hi = s - lo;
+        int b = ref_dcfeq_eval(hi, (xhat >> lo) & ((1ULL << hi) - 1), k->hi_root, &k->hi_cw[0][0], k->hi_leaf);
+        out |= ((b & 1) ^ k->hi_mu) | ((((b >> 1) & 1) ^ k->hi_mu_eq) << 2);
+        out |= ((ref_dcf_eval(lo, xhat & ((1ULL << lo) - 1), k->lo_root, &k->lo_cw[0][0], k->lo_leaf) ^ k->lo_mu) & 1)
+               << 1;
+        return out;
+    }
     if (ref_gate_has_hi(kind)) {
         if (is_split(kind)) {
             int b = ref_dcfeq_eval(n - 1 - s, (xhat & (M >> 1)) >> s, k->hi_root, &k->hi_cw[0][0], k->hi_leaf);
@@ -557,6 +599,13 @@ uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int b
         uint64_t sx = 0, sr = 0;
         for (int t = 0; t < 7; t++) sx += a[t] * w[t], sr += a[t] * w[8 + t];
         y = p0 * a0 * xhat + xhat * sx - a0 * w[7] - sr + w[15];
+        break;
+    }
+    case GATE_LRS_SPLIT: {
+        /* bits: ch = c1_hat, eh = e1_hat, cl = c2_hat */
+        uint64_t sc1 = 1 - 2 * ch, se1 = 1 - 2 * eh, sc2 = 1 - 2 * cl;
+        y = p0 * (xH - ch - eh * cl) - w[0] - sc1 * w[1] - cl * se1 * w[2] - eh * sc2 * w[3] - se1 * sc2 * w[4] +
+            two_ns * (1 - mh) * w[5] + w[6];
         break;
     }
     case GATE_RELU_ARS_SPLIT: {

@@ -21,10 +21,11 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "libfss_ref.so")
 
-GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT = 0, 1, 2, 3, 4, 5
+GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT = range(7)
 GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4, GATE_RELU_SPLIT: 16,
-               GATE_RELU_ARS_SPLIT: 32}
-SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT)
+               GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7}
+# kinds whose high DCF also outputs equality (three round-1 bit arrays)
+SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT)
 
 
 def build() -> str:

@@ -31,3 +31,17 @@ def test_argument_errors_are_status_codes(ddg):
     with pytest.raises(ddg.DdgError):
         ddg.gate_round2(0, 48, 12, 10, 0, None, None, None, None, None, None, None)
     assert ddg.gate_key_bytes(0, 32, 12, 1000) > 1000 * 400
+
+
+def test_split_lrs_layout(ddg):
+    """The split-carry LRS gate: a 5-bit DCF with equality output over carry
+    bits 7..11 and a 7-bit DCF over bits 0..6, both leaf-only (no tree
+    levels), 7 key words; smaller keys than the single 12-bit DCF."""
+    lay = ddg.gate_key_layout(ddg.GATE_LRS_SPLIT, 32, 12, 1000)
+    assert (lay["hi_bits"], lay["hi_shift"], lay["lo_bits"]) == (5, 7, 7)
+    assert lay["hi_levels"] == 0 and lay["lo_levels"] == 0 and lay["hi_mu_eq"] > 0
+    assert ddg.gate_key_bytes(ddg.GATE_LRS_SPLIT, 32, 12, 1 << 16) < ddg.gate_key_bytes(ddg.GATE_LRS, 32, 12, 1 << 16)
+    with pytest.raises(ddg.DdgError):
+        ddg.gate_key_layout(ddg.GATE_LRS_SPLIT, 32, 1, 10)
+    with pytest.raises(ddg.DdgError):
+        ddg.gate_key_layout(ddg.GATE_LRS_SPLIT + 1, 32, 12, 10)

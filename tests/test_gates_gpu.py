@@ -14,7 +14,9 @@ from oracle.ring_forward import Ring
 from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 
 S = 12
-KINDS = [F.GATE_RELU, F.GATE_RELU_ARS, F.GATE_ARS, F.GATE_LRS, F.GATE_RELU_SPLIT, F.GATE_RELU_ARS_SPLIT]
+KINDS = [F.GATE_RELU, F.GATE_RELU_ARS, F.GATE_ARS, F.GATE_LRS, F.GATE_RELU_SPLIT, F.GATE_RELU_ARS_SPLIT,
+         F.GATE_LRS_SPLIT]
+LRS_KINDS = (F.GATE_LRS, F.GATE_LRS_SPLIT)
 
 
 def plain(kind, x, bw):
@@ -32,7 +34,7 @@ def boundary(bw, kind):
     M = (1 << bw) - 1
     v = [0, 1, 2, M, M - 1, 1 << (bw - 1), (1 << (bw - 1)) - 1, (1 << (bw - 1)) + 1, (1 << S) - 1, 1 << S,
          (1 << S) + 1, M - (1 << S) + 1, M - (1 << S)]
-    if kind == F.GATE_LRS:
+    if kind in LRS_KINDS:
         v = [x & (M >> 1) for x in v]
     return v
 
@@ -42,7 +44,7 @@ def make_inputs(bw, kind, n, seed):
     dt = ring_dt(bw)
     hi = np.iinfo(dt).max
     x = rng.integers(0, hi, size=n, dtype=dt, endpoint=True)
-    if kind == F.GATE_LRS:
+    if kind in LRS_KINDS:
         x &= dt(hi >> 1)
     b = boundary(bw, kind)
     x[: min(len(b), n)] = np.array(b[: min(len(b), n)], dtype=dt)
@@ -53,7 +55,13 @@ def make_inputs(bw, kind, n, seed):
     lowmask = dt((1 << S) - 1)
     xh = (r & ~lowmask) | (rng.integers(0, 1 << S, size=n, dtype=dt) & lowmask)
     x[sel] = (xh - r).astype(dt)[sel]
-    if kind == F.GATE_LRS:
+    # every 7th element: x_hat agrees with r on carry bits 5..11 (split LRS equality branch)
+    sel2 = np.arange(n) % 7 == 3
+    m31 = dt(31)
+    xh2 = (r & ~m31) | (rng.integers(0, 32, size=n, dtype=dt) & m31)
+    xh2 = (xh2 + (rng.integers(0, 1 << 16, size=n, dtype=dt) << dt(12))).astype(dt)
+    x[sel2] = (xh2 - r).astype(dt)[sel2]
+    if kind in LRS_KINDS:
         x &= dt(hi >> 1)
     return x, r
 
@@ -163,3 +171,31 @@ def test_gate_empty_is_noop(ddg, cuda):
     for kind in KINDS:
         ddg.gate_round1(kind, 32, S, 0, None, None, None, None)
         ddg.gate_round2(kind, 32, S, 0, 0, None, None, None, None, None, None, None)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bw", [32, 64])
+def test_aes_engines_agree(ddg, cuda, bw):
+    """The two AES engines (two staged round tables + rotation, four staged
+    tables) give identical keys, round-1 bits and shares, and identical hash
+    chains in the throughput probe."""
+    import torch
+
+    kind, n = F.GATE_RELU_ARS_SPLIT, 5000
+    x, r = make_inputs(bw, kind, n, seed=bw + 1)
+    outs = []
+    try:
+        for nt in (2, 4):
+            ddg.aes_tables(nt)
+            outs.append(run_gate(ddg, kind, bw, n, x, r, seed=77, op=9))
+            chain = torch.zeros(4096, dtype=torch.int32, device="cuda")
+            ddg.check(ddg.lib().ddg_aes_chain_variant(4096, 16, nt, chain.data_ptr(), None))
+            torch.cuda.synchronize()
+            outs[-1]["chain"] = chain.cpu().numpy()
+    finally:
+        ddg.aes_tables(4)
+    a, b = outs
+    for k in ("k0", "k1", "rout", "y0", "y1", "chain"):
+        assert np.array_equal(a[k], b[k]), k
+    for kk in a["bits"]:
+        assert np.array_equal(a["bits"][kk], b["bits"][kk])

@@ -30,7 +30,7 @@ def test_dcf_compares(d):
             assert c == int(x < alpha)
 
 
-@pytest.mark.parametrize("d", [7, 12, 19, 51])
+@pytest.mark.parametrize("d", [1, 5, 6, 7, 12, 19, 51])
 def test_dcfeq_compares_and_equals(d):
     rng = np.random.default_rng(d + 100)
     for _ in range(25):
@@ -38,13 +38,13 @@ def test_dcfeq_compares_and_equals(d):
         k = F.dcfeq_keygen(d, alpha, rng.bytes(16), rng.bytes(16))
         xs = [int(v) for v in rng.integers(0, 1 << d, size=6, dtype=np.uint64)]
         xs += [alpha, max(alpha - 1, 0), min(alpha + 1, (1 << d) - 1), alpha ^ 1, alpha ^ 64, 0, (1 << d) - 1]
-        for x in xs:
+        for x in (v & ((1 << d) - 1) for v in xs):
             b = F.dcfeq_eval(d, x, k[0], k[2], k[3]) ^ F.dcfeq_eval(d, x, k[1], k[2], k[3])
             assert b & 1 == int(x < alpha) and (b >> 1) & 1 == int(x == alpha)
 
 
 @pytest.mark.parametrize("bw", [32, 64])
-@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4, 5])
+@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4, 5, 6])
 def test_gate_functionality(bw, kind):
     M = (1 << bw) - 1
     rng = np.random.default_rng(bw + kind)
@@ -56,13 +56,15 @@ def test_gate_functionality(bw, kind):
             x = ((r & ~((1 << 12) - 1)) + int(rng.integers(0, 1 << 12)) - r) & M
         if i % 4 == 2:
             x = [0, 1, M, 1 << (bw - 1), (1 << (bw - 1)) - 1, (1 << 12) - 1, M - 4095][i % 7]
-        if kind == 3:
+        if i % 4 == 3:  # x_hat agrees with r on carry bits 5..11: the split LRS equality branch
+            x = ((r & ~31) + int(rng.integers(0, 32)) - r + (int(rng.integers(0, 1 << 20)) << 12)) & M
+        if kind in (3, 6):
             x &= M >> 1
         k0, k1, ry = F.gate_keygen(kind, bw, 12, 3, 1, i, r)
         y = (F.gate_eval_pair(kind, bw, 12, (x + r) & M, k0, k1) - ry) & M
         xa = np.array([x], dtype=np.uint64)
-        want = [R.relu(xa), R.relu_ars(xa, 12), R.ars(xa, 12), R.red(R.signed(xa) >> 12), R.relu(xa),
-                R.relu_ars(xa, 12)][kind]
+        lrs = R.red(R.signed(xa) >> 12)
+        want = [R.relu(xa), R.relu_ars(xa, 12), R.ars(xa, 12), lrs, R.relu(xa), R.relu_ars(xa, 12), lrs][kind]
         assert y == int(want[0])
 
 
