@@ -64,6 +64,8 @@ def parse():
                     help="N>1: batch lanes per rank, each with its own NCCL communicator and host thread.  Only 1 "
                          "is accepted: two lanes (two communicators used concurrently from two threads per GPU) "
                          "stalled for 900 s on the first 2-GPU run, cause not established")
+    ap.add_argument("--aes-tables", type=int, default=4, choices=[2, 4],
+                    help="AES engine: 4 staged round tables (default) or 2 tables + rotation")
     ap.add_argument("--gemm", default="tensor", choices=["tensor", "cuda-cores"],
                     help="ring GEMM engine: tcgen05 limb products (default) or the CUDA-core kernel")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
@@ -98,6 +100,12 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def atoms_of(bw):
+    """Atom-count range of the synthetic graphs: davis-shaped U[10,60] for the
+    bw=32 config, kiba-shaped U[10,100] for the bw=64 config ([3])."""
+    return (10, 60) if bw == 32 else (10, 100)
+
+
 def config_of(a, n_gpus):
     pairs = max(n_gpus // 2, 1)
     if a.stream:
@@ -110,12 +118,15 @@ def config_of(a, n_gpus):
             "l2": "inputs larger than L2: every step copies and streams a full key chunk per party"}
     return {
         "workload": f"full affinity branch (adj-norm, GCNx3, masked max-pool, FC head), bw={a.bw}, scale={a.scale}, "
-                    f"B={a.batch} davis-shaped synthetic graphs per pair, keys resident in HBM (BASELINE configs[2])",
+                    f"B={a.batch} {'davis' if a.bw == 32 else 'kiba'}-shaped synthetic graphs (atoms "
+                    f"U{list(atoms_of(a.bw))}) per pair, keys resident in HBM "
+                    f"(BASELINE configs[{2 if a.bw == 32 else 3}])",
         "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs,
         "parallelism": "1 GPU, both parties" if n_gpus == 1 else
         f"{pairs} party pairs over NCCL, one party per GPU",
         "truncation": "exact (floor) at every site",
         "gemm": "tcgen05 kind::i8 limb products" if a.gemm == "tensor" else "CUDA-core integer multiply-add",
+        "aes": f"T-table AES, {a.aes_tables} round tables staged in shared memory",
         "l2": "inputs larger than L2: every step streams the full key region (>= 24 GB per party at B=256)",
     }
 
@@ -268,6 +279,7 @@ def main():
     ddg = importlib.import_module("idash26-track3_b200")
     synth = importlib.import_module("idash26-track3_b200.synth")
     ddg.gemm_path(ddg.GEMM_TENSOR if a.gemm == "tensor" else ddg.GEMM_CUDA_CORES)
+    ddg.aes_tables(a.aes_tables)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None
@@ -284,7 +296,7 @@ def main():
     streams = []
     if world == 1:
         pairs, pair = 1, 0
-        inp = synth.Inputs(B, bw, seed=1000)
+        inp = synth.Inputs(B, bw, seed=1000, atoms=atoms_of(bw))
         parties = [ddg.Party(0, bw, s, local), ddg.Party(1, bw, s, local)]
         if a.stream:
             kb = ddg.forward_key_bytes(bw, s, B)
@@ -308,7 +320,7 @@ def main():
         if B % lanes:
             raise SystemExit(f"--batch {B} not divisible by --lanes {lanes}")
         Bl = B // lanes
-        inp = synth.Inputs(B, bw, seed=1000 + pair)
+        inp = synth.Inputs(B, bw, seed=1000 + pair, atoms=atoms_of(bw))
         uids = [[ddg.nccl_unique_id() for _ in range(lanes)] if rank == 0 else None]
         dist.broadcast_object_list(uids, src=0)
         parties, keep_keys = [], []

@@ -173,10 +173,11 @@ struct TcShape {
     static constexpr int A_PLANE = TC_BM * TC_BK;  // bytes of one A byte plane per stage
     static constexpr int B_PLANE = BN * TC_BK;     // bytes of one B byte plane per stage
     static constexpr int STAGE = P * (A_PLANE + B_PLANE);
-    // 8 KiB of slack after the two stages: a descriptor whose strides the
-    // hardware read differently from this layout still stays inside the CTA's
-    // shared memory (the tests then fail on values, not on an address)
-    static constexpr int SMEM = 2 * STAGE + 8192;
+    // The operand tiles start on a 1024-byte boundary of the shared window
+    // (after the barriers and up to 1 KiB of alignment padding), and 8 KiB of
+    // slack follow the two stages so that a descriptor read differently from
+    // this layout still stays inside the CTA's shared memory.
+    static constexpr int SMEM = 32 + 1024 + 2 * STAGE + 8192;
     static constexpr int NCOL = tmem_cols(P * BN);
     static constexpr int A_ITEMS = TC_BM * TC_BK / 4 / TC_THREADS;  // 4-element items per thread
     static constexpr int B_ITEMS = BN * TC_BK / 4 / TC_THREADS;
@@ -191,9 +192,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 {
     using S = TcShape<T, BN, B_MN>;
     constexpr int P = S::P;
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[2];
-    __shared__ uint32_t s_tmem;
+    // Dynamic shared memory only: [2 mbarriers | TMEM address | pad to 1024 | stage 0 | stage 1 | slack].
+    // With the barriers as static __shared__ variables beside the dynamic
+    // array, the MMAs read every operand tile 32 bytes below the address in
+    // its descriptor (measured on B200: the products matched a model shifted
+    // by exactly -32 B for A and B), so this kernel declares no static shared
+    // memory.
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem_raw);
+    uint32_t &s_tmem = *reinterpret_cast<uint32_t *>(smem_raw + 16);
+    uint8_t *const smem = smem_raw + 32 + ((1024u - ((smem_addr(smem_raw) + 32u) & 1023u)) & 1023u);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.z;
@@ -207,8 +215,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        mbar_init(bars + 0, 1);
+        mbar_init(bars + 1, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
