@@ -38,15 +38,19 @@ import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
+# stdout carries exactly one JSON line: NCCL's own log lines (its version
+# banner included) go to stderr
+os.environ.setdefault("NCCL_DEBUG", "WARN")
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 NMAX, FEAT, POOL, PROT = 138, 94, 376, 128
 RELUS_PER_SAMPLE = 171_076           # 138*(188+282+376) + 376*137 + 2816
 A10_SAMPLES_PER_S = 16 / 0.136       # reference README.md:99-101, A10, B=16, bw=32
 
 # DRAM bytes (read + write) per algorithmic byte of the round-1 DCF kernel,
-# from an ncu capture (profiles/gate_round1_dcf_relu_ars_b16.md: 445.6 MB of
-# DRAM traffic for 442.1 MB of algorithmic bytes in one launch).
-NCU_DRAM_BYTES_PER_ALG_BYTE = 445.6 / 442.1
+# from an ncu capture (profiles/gate_round1_dcf_relu_ars_split_b16.md: 300.0 MB
+# of DRAM traffic for 295.9 MB of algorithmic bytes in one launch).
+NCU_DRAM_BYTES_PER_ALG_BYTE = 300.0 / 295.9
 
 
 def parse():
@@ -66,12 +70,17 @@ def parse():
                          "stalled for 900 s on the first 2-GPU run, cause not established")
     ap.add_argument("--aes-tables", type=int, default=4, choices=[2, 4],
                     help="AES engine: 4 staged round tables (default) or 2 tables + rotation")
+    ap.add_argument("--relu-split", type=int, default=0, choices=[0, 2, 3],
+                    help="comparison split of the ReLU gates: 3 parts (fewest AES) or 2 (smaller keys); "
+                         "0 = 3 with resident keys, 2 with --stream")
     ap.add_argument("--gemm", default="tensor", choices=["tensor", "cuda-cores"],
                     help="ring GEMM engine: tcgen05 limb products (default) or the CUDA-core kernel")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
                     help="streaming regime (BASELINE configs[4]): keys of NCHUNKS forwards per party live in pinned "
                          "host memory and are streamed into HBM through the double-buffered key stream, cyclically")
     a = ap.parse_args()
+    if a.relu_split == 0:
+        a.relu_split = 2 if a.stream else 3
     if a.lanes != 1:
         raise SystemExit("--lanes: only 1 lane per rank is supported (see --help)")
     if a.stream and a.batch == 256:
@@ -114,6 +123,7 @@ def config_of(a, n_gpus):
                         f"B={a.batch} per pair per step, keys streamed host->HBM every step from a ring of "
                         f"{a.stream} pinned chunks per party (timing-only key reuse)",
             "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs, "stream_chunks": a.stream,
+            "relu_split": a.relu_split,
             "parallelism": "1 GPU, both parties" if n_gpus == 1 else f"{pairs} party pairs over NCCL, one party per GPU",
             "l2": "inputs larger than L2: every step copies and streams a full key chunk per party"}
     return {
@@ -127,6 +137,7 @@ def config_of(a, n_gpus):
         "truncation": "exact (floor) at every site",
         "gemm": "tcgen05 kind::i8 limb products" if a.gemm == "tensor" else "CUDA-core integer multiply-add",
         "aes": f"T-table AES, {a.aes_tables} round tables staged in shared memory",
+        "relu_split": a.relu_split,
         "l2": "inputs larger than L2: every step streams the full key region (>= 24 GB per party at B=256)",
     }
 
@@ -280,6 +291,7 @@ def main():
     synth = importlib.import_module("idash26-track3_b200.synth")
     ddg.gemm_path(ddg.GEMM_TENSOR if a.gemm == "tensor" else ddg.GEMM_CUDA_CORES)
     ddg.aes_tables(a.aes_tables)
+    ddg.relu_split(a.relu_split)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None

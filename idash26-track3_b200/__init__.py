@@ -18,7 +18,8 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libddg.so")
 
-GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT = range(7)
+(GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
+ GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3) = range(9)
 
 DDG_OK = 0
 _STATUS = {1: "DDG_ERR_ARG", 2: "DDG_ERR_CUDA", 3: "DDG_ERR_KEY", 4: "DDG_ERR_PEER", 5: "DDG_ERR_STATE",
@@ -56,6 +57,7 @@ SIGNATURES = {
     "ddg_aes_chain": (_i32, [_u64, _i32, _vp, _vp]),
     "ddg_aes_chain_variant": (_i32, [_u64, _i32, _i32, _vp, _vp]),
     "ddg_aes_tables": (_i32, [_i32]),
+    "ddg_relu_split": (_i32, [_i32]),
     "ddg_party_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32]),
     "ddg_party_destroy": (_i32, [_vp]),
     "ddg_party_set_weights": (_i32, [_vp, _vp, _u64]),
@@ -117,10 +119,11 @@ def gate_key_bytes(kind: int, bw: int, scale: int, n: int) -> int:
 
 def gate_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
     """Byte offsets of one party's gate key (see ddg_gate_key_layout)."""
-    out = (_u64 * 16)()
+    out = (_u64 * 22)()
     check(lib().ddg_gate_key_layout(kind, bw, scale, n, out))
     keys = ("hi_root", "hi_cw", "hi_leaf", "hi_mu", "lo_root", "lo_cw", "lo_leaf", "lo_mu", "words", "bytes",
-            "hi_levels", "lo_levels", "hi_mu_eq", "hi_bits", "hi_shift", "lo_bits")
+            "hi_levels", "lo_levels", "hi_mu_eq", "hi_bits", "hi_shift", "lo_bits", "mid_root", "mid_cw", "mid_leaf",
+            "mid_mu", "mid_mu_eq", "mid_levels")
     return {k: int(v) for k, v in zip(keys, out)}
 
 
@@ -264,6 +267,13 @@ def gemm_path(path: int):
 def aes_tables(tables: int):
     """AES engine of every FSS kernel: 4 (default) or 2 staged round tables."""
     check(lib().ddg_aes_tables(tables))
+
+
+def relu_split(parts: int):
+    """Comparison split of the forward's ReLU gates: 3 (default, fewest AES) or 2
+    (smaller keys).  Dealer and evaluators must use the same setting (it changes
+    the key layout)."""
+    check(lib().ddg_relu_split(parts))
 
 
 def gemm_status():

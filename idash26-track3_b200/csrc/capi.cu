@@ -13,10 +13,13 @@ using namespace ddg;
 
 static int check_gate_args(int kind, int bw, int scale)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS_SPLIT, DDG_ERR_ARG, "gate kind %d out of range", kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_SPLIT3, DDG_ERR_ARG, "gate kind %d out of range",
+              kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
     DDG_CHECK(kind != DDG_GATE_LRS_SPLIT || scale >= 2, DDG_ERR_ARG, "split LRS needs scale >= 2 (got %d)", scale);
+    DDG_CHECK(!gate_is_split3(kind) || scale + SPLIT3_MID < bw - 1, DDG_ERR_ARG,
+              "three-part split needs scale + %d < bw - 1 (scale %d, bw %d)", SPLIT3_MID, scale, bw);
     return DDG_OK;
 }
 
@@ -37,10 +40,11 @@ int ddg_gate_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out)
     DDG_TRY(check_gate_args(kind, bw, scale));
     DDG_CHECK(out != nullptr, DDG_ERR_ARG, "null out");
     GateLayout L = gate_layout(kind, bw, scale, n);
-    uint64_t v[16] = {L.H.root, L.H.cw, L.H.leaf, L.H.mu, L.Lo.root, L.Lo.cw, L.Lo.leaf, L.Lo.mu,
+    uint64_t v[22] = {L.H.root, L.H.cw, L.H.leaf, L.H.mu, L.Lo.root, L.Lo.cw, L.Lo.leaf, L.Lo.mu,
                       L.words, L.bytes, uint64_t(L.H.L), uint64_t(L.Lo.L), L.H.mu_eq, uint64_t(L.H.d),
-                      uint64_t(L.hi_shift), uint64_t(L.Lo.d)};
-    for (int i = 0; i < 16; i++) out[i] = v[i];
+                      uint64_t(L.hi_shift), uint64_t(L.Lo.d), L.Mi.root, L.Mi.cw, L.Mi.leaf, L.Mi.mu, L.Mi.mu_eq,
+                      uint64_t(L.Mi.L)};
+    for (int i = 0; i < 22; i++) out[i] = v[i];
     return DDG_OK;
 }
 
@@ -91,6 +95,13 @@ int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_
     return aes_chain(threads, iters, d_out, static_cast<cudaStream_t>(stream), variant);
 }
 
+int ddg_relu_split(int parts)
+{
+    DDG_CHECK(parts == 2 || parts == 3, DDG_ERR_ARG, "ReLU split: 2 or 3 parts (got %d)", parts);
+    set_relu_parts(parts);
+    return DDG_OK;
+}
+
 int ddg_aes_tables(int tables)
 {
     DDG_CHECK(tables == 2 || tables == 4, DDG_ERR_ARG, "AES engine: 2 or 4 staged tables (got %d)", tables);
@@ -128,8 +139,8 @@ int ddg_party_destroy(ddg_party *h)
     cudaSetDevice(h->P.device);
     cudaStreamSynchronize(h->P.stream);
     h->P.w.release();
-    for (int i = 0; i < 4; i++)
-        if (h->P.in_buf[i]) cudaFree(h->P.in_buf[i]);
+    if (h->P.copy_stream) cudaStreamSynchronize(h->P.copy_stream);
+    h->P.release_inputs();
     if (h->P.owns_chan) delete h->P.chan;
     cudaStreamDestroy(h->P.stream);
     delete h;

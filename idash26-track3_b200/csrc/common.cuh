@@ -68,15 +68,23 @@ void set_dcf_timing_sink(DcfTiming *t);
 // GATE_LRS_SPLIT computes GATE_LRS with its s-bit carry comparison split the
 // same way into V1 (upper s - s2 bits, DCF with equality) and V2 (low s2 =
 // min(7, s-1) bits, plain DCF): 2 instead of s-6 AES-128 per element.
+// GATE_RELU_SPLIT3 / GATE_RELU_ARS_SPLIT3 split the (n-1)-bit comparison in
+// three: U1 (upper bits, DCF with equality), U2 (the SPLIT3_MID bits above the
+// low s bits, DCF with equality) and V (the low s bits, plain DCF):
+// 1{x<a} = c1 + e1*(c2 + e2*cL), every sum exclusive.  15 AES per element at
+// bw=32 instead of 20, for 40 / 80 key words instead of 16 / 32.
 enum GateKind {
     GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
-    GATE_LRS_SPLIT = 6, GATE_KIND_END = 7
+    GATE_LRS_SPLIT = 6, GATE_RELU_SPLIT3 = 7, GATE_RELU_ARS_SPLIT3 = 8, GATE_KIND_END = 9
 };
+constexpr int SPLIT3_MID = 6;
+constexpr int SPLIT3_NMONO = 19;  // dealer-bit monomials of the three-part DReLU bit
 
-// the high DCF has an equality output (three round-1 bit arrays)
+inline bool gate_is_split3(int kind) { return kind == GATE_RELU_SPLIT3 || kind == GATE_RELU_ARS_SPLIT3; }
+// the high DCF has an equality output (three round-1 bit arrays, five with a middle DCF)
 inline bool gate_is_split(int kind)
 {
-    return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT || kind == GATE_LRS_SPLIT;
+    return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT || kind == GATE_LRS_SPLIT || gate_is_split3(kind);
 }
 inline bool gate_has_hi(int kind) { return kind != GATE_LRS; }
 inline bool gate_has_lo(int kind) { return kind != GATE_RELU; }
@@ -89,6 +97,8 @@ inline int gate_nwords(int kind)
     case GATE_RELU_SPLIT: return 16;
     case GATE_RELU_ARS_SPLIT: return 32;
     case GATE_LRS_SPLIT: return 7;
+    case GATE_RELU_SPLIT3: return 40;
+    case GATE_RELU_ARS_SPLIT3: return 80;
     default: return 4;
     }
 }
@@ -98,11 +108,13 @@ __host__ __device__ inline int lrs_split_lo_bits(int s) { return s - 1 < 7 ? s -
 inline int gate_hi_bits(int kind, int bw, int s)
 {
     if (kind == GATE_LRS_SPLIT) return s - lrs_split_lo_bits(s);
+    if (gate_is_split3(kind)) return bw - 1 - s - SPLIT3_MID;
     return gate_is_split(kind) ? bw - 1 - s : bw - 1;
 }
 inline int gate_hi_shift(int kind, int s)
 {
     if (kind == GATE_LRS_SPLIT) return lrs_split_lo_bits(s);
+    if (gate_is_split3(kind)) return s + SPLIT3_MID;
     return gate_is_split(kind) ? s : 0;
 }
 // domain bits of the low DCF
@@ -137,13 +149,14 @@ inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base, bool eq = false)
     return l;
 }
 
-// one gate op: [hi DCF over hi_bits] [lo DCF over lo_bits] [nwords x N ring words]
-// The hi DCF reads bits [hi_shift, hi_shift + H.d) of x_hat, the lo DCF bits [0, Lo.d).
+// one gate op: [hi DCF over hi_bits] [mid DCF] [lo DCF over lo_bits] [nwords x N ring words]
+// The hi DCF reads bits [hi_shift, hi_shift + H.d) of x_hat, the middle DCF
+// (three-part split kinds) bits [s, s + SPLIT3_MID), the lo DCF bits [0, Lo.d).
 struct GateLayout {
     int kind = 0, bw = 0, s = 0, hi_shift = 0;
     uint64_t n = 0;
-    bool hi = false, lo = false;
-    DcfLayout H, Lo;
+    bool hi = false, mid = false, lo = false;
+    DcfLayout H, Mi, Lo;
     int nwords = 0;
     uint64_t words = 0, bytes = 0;
 };
@@ -159,6 +172,11 @@ inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base
         g.H = dcf_layout(gate_hi_bits(kind, bw, s), n, off, gate_is_split(kind));
         g.hi_shift = gate_hi_shift(kind, s);
         off = g.H.end;
+    }
+    g.mid = gate_is_split3(kind);
+    if (g.mid) {
+        g.Mi = dcf_layout(SPLIT3_MID, n, off, true);
+        off = g.Mi.end;
     }
     if (g.lo) {
         g.Lo = dcf_layout(gate_lo_bits(kind, s), n, off);
@@ -191,6 +209,7 @@ inline DcfView dcf_view(const uint8_t *key, const DcfLayout &l)
 enum Purpose : uint32_t {
     P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4, P_ROUT = 5, P_BITS = 6,
     P_MASK = 8,    // input / output masks of linear ops
+    P_MID_S0 = 9, P_MID_DELTA = 10,  // middle DCF of the three-part split gates
     P_SHARE = 16,  // share0 of dealer word k uses purpose P_SHARE + k
 };
 

@@ -9,6 +9,7 @@
 // 326-374): every op reads (eval) or writes (dealer) the next 256-byte aligned
 // key section.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -82,6 +83,23 @@ void DevWeights::release()
     }
     if (table) cudaFree(table);
     table = nullptr;
+}
+
+int Party::ensure_copy_stream()
+{
+    if (copy_stream) return DDG_OK;
+    DDG_CUDA(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking));
+    for (auto &ev : in_ev) DDG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    return DDG_OK;
+}
+
+void Party::release_inputs()
+{
+    for (int i = 0; i < 4; i++)
+        if (in_buf[i]) cudaFree(in_buf[i]), in_buf[i] = nullptr, in_cap[i] = 0;
+    for (auto &ev : in_ev)
+        if (ev) cudaEventDestroy(ev), ev = nullptr;
+    if (copy_stream) cudaStreamDestroy(copy_stream), copy_stream = nullptr;
 }
 
 int Party::ensure_input(int which, uint64_t bytes)
@@ -356,7 +374,15 @@ struct EvalExec : ExecBase<T> {
     Party *P = nullptr;
     int p = 0;
     const T *in[4] = {};
+    cudaEvent_t in_ready[4] = {};  // host inputs: copy-stream event to wait on before first use
     T *out = nullptr;
+
+    void wait_input(int which)
+    {
+        if (in_ready[which] && this->err == DDG_OK)
+            ok(cudaStreamWaitEvent(this->st, in_ready[which], 0) == cudaSuccess ? DDG_OK : DDG_ERR_CUDA);
+        in_ready[which] = nullptr;
+    }
 
     const uint8_t *key_at(uint64_t bytes)
     {
@@ -389,6 +415,7 @@ struct EvalExec : ExecBase<T> {
         t.n = n;
         t.ms0 = reinterpret_cast<const T *>(key_at(words(n)));
         T *sh = alloc(n);
+        wait_input(which);
         if (this->err == DDG_OK) ok(ew_add<T>(sh, in[which], t.ms0, n, this->st));
         t.v = open(sh, n);
         return t;
@@ -400,6 +427,7 @@ struct EvalExec : ExecBase<T> {
         const T *ms = reinterpret_cast<const T *>(key_at(words(rows)));
         t.ms0 = ms;
         T *sh = alloc(rows);
+        wait_input(IN_ADJ);
         if (this->err == DDG_OK) ok(rowsum_plus<T>(in[IN_ADJ], ms, sh, rows, cols, this->st));
         t.v = open(sh, rows);
         return t;
@@ -408,6 +436,7 @@ struct EvalExec : ExecBase<T> {
     {
         Tn<T> t;
         t.n = n;
+        wait_input(which);
         t.v = open(in[which], n);
         return t;
     }
@@ -493,7 +522,8 @@ struct EvalExec : ExecBase<T> {
         GateLayout L = gate_layout(kind, this->bw, this->s, x.n);
         const uint8_t *k = key_at(L.bytes);
         const uint64_t nw = (x.n + 31) / 32;
-        const int nh = L.hi ? (L.H.eq ? 2 : 1) : 0;  // split gates also open the equality bits
+        // split gates also open the equality bits, three-part splits the middle DCF's two bits
+        const int nh = L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0;
         const int nb = nh + (L.lo ? 1 : 0);
         uint32_t *bits = static_cast<uint32_t *>(this->alloc_bytes(4 * nw * nb));
         uint32_t *bh = L.hi ? bits : nullptr, *bl = L.lo ? bits + nh * nw : nullptr;
@@ -540,18 +570,28 @@ struct EvalExec : ExecBase<T> {
 
 // ------------------------------------------------------------------ the graph
 
+// comparison split of the ReLU gates: 3 parts (default; fewest AES) or 2
+// (smaller keys: 94.8 vs 111.8 MB per sample and party at bw=32).  Key sizes
+// differ, so dealer and evaluators must run with the same setting.
+static std::atomic<int> g_relu_parts{3};
+void set_relu_parts(int parts) { g_relu_parts.store(parts == 2 ? 2 : 3); }
+static int relu_parts(int) { return g_relu_parts.load(); }
+
 template <typename T, class E>
 static void affinity_graph(E &x)
 {
     const int B = x.B;
+    const bool three = relu_parts(x.bw) == 3;
+    const int RELU = three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
+    const int RELU_ARS = three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
     const uint64_t nX = uint64_t(B) * NMAX * FEAT, nA = uint64_t(B) * NMAX * NMAX, nM = uint64_t(B) * NMAX * POOL;
     // leaves: x, mask, raw adjacency and its masked degree, the public protein
     // (deepdtagen_inference.cu:503-529 registerLeaf; secure_adj_norm.h:414-493)
-    Tn<T> X = x.reveal_input(IN_X, nX);
-    Tn<T> M = x.reveal_input(IN_MASK, nM);
+    // Each leaf is revealed right before its first use, so that host inputs
+    // still in flight on the party's copy stream (features, mask, protein)
+    // overlap the layers before it; the key sections follow the same order.
     Tn<T> A = x.reveal_input(IN_ADJ, nA);
     Tn<T> D = x.reveal_degree(uint64_t(B) * NMAX, NMAX);
-    Tn<T> P = x.reveal_public(IN_PROT, uint64_t(B) * PROT);
     // A_hat = floor(A * t_i * t_j / 2^s), t = LUT[deg] (secure_adj_norm.h:498-651)
     Tn<T> t = x.lut(D);
     EwShape sh;
@@ -560,31 +600,34 @@ static void affinity_graph(E &x)
     Tn<T> W = x.mul(L, t, BC_COL, sh);
     Tn<T> Ah = x.gate(GATE_LRS_SPLIT, W);
     // GCN x3, aggregate first (gcn_layer.h:107-116)
+    Tn<T> X = x.reveal_input(IN_X, nX);
     Tn<T> H = X;
     for (int l = 0; l < 3; l++) {
         Tn<T> Pm = x.matmul(Ah, H, LAYER_IN[l]);
         Tn<T> AX = x.gate(GATE_LRS_SPLIT, Pm);
         Tn<T> Z = x.fc(AX, l, B * NMAX);
-        H = x.gate(GATE_RELU_ARS_SPLIT, Z);
+        H = x.gate(RELU_ARS, Z);
     }
     // masked global max-pool (deepdtagen.h:198-202, masked_maxpool_layer.h:72-126)
     EwShape shm;
     shm.n = nM;
+    Tn<T> M = x.reveal_input(IN_MASK, nM);
     Tn<T> prod = x.mul(H, M, BC_NONE, shm);
     Tn<T> cur = x.gate(GATE_LRS_SPLIT, prod);
     int cnt = NMAX;
     while (cnt > 1) {
         Tn<T> even, diff;
         x.pool_split(cur, cnt, even, diff);
-        Tn<T> r = x.gate(GATE_RELU_SPLIT, diff);
+        Tn<T> r = x.gate(RELU, diff);
         cur = x.pool_merge(even, r, cur, cnt);
         cnt = cnt / 2 + (cnt & 1);
     }
     // head (deepdtagen.h:209-220)
-    Tn<T> d1 = x.gate(GATE_RELU_ARS_SPLIT, x.fc(cur, 3, B));
+    Tn<T> d1 = x.gate(RELU_ARS, x.fc(cur, 3, B));
     Tn<T> d2 = x.gate(GATE_ARS, x.fc(d1, 4, B));
+    Tn<T> P = x.reveal_public(IN_PROT, uint64_t(B) * PROT);
     Tn<T> f = x.concat(d2, P);
-    for (int l = 5; l < 8; l++) f = x.gate(GATE_RELU_ARS_SPLIT, x.fc(f, l, B));
+    for (int l = 5; l < 8; l++) f = x.gate(RELU_ARS, x.fc(f, l, B));
     Tn<T> o = x.fc(f, 8, B);
     x.output(o);
 }
@@ -642,14 +685,22 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
     const uint64_t sizes[4] = {uint64_t(B) * NMAX * FEAT, uint64_t(B) * NMAX * NMAX, uint64_t(B) * NMAX * POOL,
                                uint64_t(B) * PROT};
     const void *src[4] = {x_sh, adj_sh, mask_sh, prot_sh};
-    for (int i = 0; i < 4; i++) {
-        if (on_host) {
+    if (on_host) {
+        // host -> device on the party's copy stream, in order of first use; the
+        // graph waits on each input's event right before revealing it
+        DDG_TRY(P.ensure_copy_stream());
+        DDG_CUDA(cudaEventRecord(P.in_ev[4], P.stream));
+        DDG_CUDA(cudaStreamWaitEvent(P.copy_stream, P.in_ev[4], 0));  // buffers free: the last forward is done
+        for (int i : {int(IN_ADJ), int(IN_X), int(IN_MASK), int(IN_PROT)}) {
             DDG_TRY(P.ensure_input(i, sizes[i] * sizeof(T)));
-            DDG_CUDA(cudaMemcpyAsync(P.in_buf[i], src[i], sizes[i] * sizeof(T), cudaMemcpyHostToDevice, P.stream));
+            DDG_CUDA(cudaMemcpyAsync(P.in_buf[i], src[i], sizes[i] * sizeof(T), cudaMemcpyHostToDevice,
+                                     P.copy_stream));
+            DDG_CUDA(cudaEventRecord(P.in_ev[i], P.copy_stream));
             e.in[i] = static_cast<const T *>(P.in_buf[i]);
-        } else {
-            e.in[i] = static_cast<const T *>(src[i]);
+            e.in_ready[i] = P.in_ev[i];
         }
+    } else {
+        for (int i = 0; i < 4; i++) e.in[i] = static_cast<const T *>(src[i]);
     }
     const uint64_t sent0 = P.chan->bytes_sent[P.party], rounds0 = P.chan->rounds[P.party];
     P.intervals.clear();
@@ -675,6 +726,14 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         e.err = DDG_ERR_CUDA;
     }
     if (e.err == DDG_OK) e.err = ring_gemm_tc_check(P.stream);
+    // the caller may reuse its host buffers once this returns
+    if (P.copy_stream) {
+        ce = cudaStreamSynchronize(P.copy_stream);
+        if (e.err == DDG_OK && ce != cudaSuccess) {
+            set_last_error("forward input copy: %s", cudaGetErrorString(ce));
+            e.err = DDG_ERR_CUDA;
+        }
+    }
     if (e.err != DDG_OK) {
         if (auto *lp = dynamic_cast<LocalPairChannel *>(P.chan)) lp->fail();
         return e.err;

@@ -57,13 +57,19 @@ struct Party {
     DcfAcc dcf;
     cudaEvent_t ref_event = nullptr;                     // start of the last forward
     std::vector<std::pair<double, double>> intervals;    // last forward's DCF launches, ms after ref_event
-    // device staging of host inputs (kept across forwards)
+    // device staging of host inputs (kept across forwards), copied on a side
+    // stream; in_ev[0..3] mark each input's arrival, in_ev[4] the start of a forward
     void *in_buf[4] = {};
     uint64_t in_cap[4] = {};
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t in_ev[5] = {};
     int ensure_input(int which, uint64_t bytes);
+    int ensure_copy_stream();
+    void release_inputs();
 };
 
 uint64_t forward_key_bytes(int bw, int s, int B);
+void set_relu_parts(int parts);
 double union_ms(std::vector<std::pair<double, double>> v);
 int pair_dcf_union(Party &p0, Party &p1);
 int parties_dcf_union(Party *const *ps, int n);

@@ -11,6 +11,42 @@
 
 namespace ddg {
 
+// ------------------------------------------------- three-part split algebra
+//
+// DReLU bit d = q ^ eps ^ t with q = 1 ^ m_hat ^ c1_hat public, eps = r_m ^
+// rho_c1 and t = e1*(c2 + e2*cL) in {0,1}.  Every true bit is b = b_hat +
+// (1 - 2 b_hat) rho_b, so t is multilinear in (rho_e1, rho_c2, rho_e2, rho_L)
+// over nine monomials, and
+//   d = q + (1-2q) [tau_1 + (1 - 2 tau_1) eps + sum tau_m m - 2 sum tau_m eps m].
+// The dealer shares the 19 monomials [eps, m (9), eps*m (9)]; m runs over
+//   rho_c2, rho_L, rho_e2, rho_e2 rho_L, rho_e1, rho_e1 rho_c2, rho_e1 rho_L,
+//   rho_e1 rho_e2, rho_e1 rho_e2 rho_L.
+
+template <typename T>
+__device__ __forceinline__ void split3_monomials(T ep, T pe1, T pc2, T pL, T pe2, T (&m)[SPLIT3_NMONO])
+{
+    const T t[9] = {pc2, pL, pe2, T(pe2 * pL), pe1, T(pe1 * pc2), T(pe1 * pL), T(pe1 * pe2), T(pe1 * pe2 * pL)};
+    m[0] = ep;
+#pragma unroll
+    for (int k = 0; k < 9; k++) m[1 + k] = t[k], m[10 + k] = T(ep * t[k]);
+}
+
+// public coefficients of the 19 monomials; returns the constant term a0
+template <typename T>
+__device__ __forceinline__ T split3_coeffs(T q, T e1h, T c2h, T e2h, T cLh, T (&a)[SPLIT3_NMONO])
+{
+    const T su = T(1) - T(2) * q, se1 = T(1) - T(2) * e1h, sc2 = T(1) - T(2) * c2h, se2 = T(1) - T(2) * e2h,
+            sL = T(1) - T(2) * cLh;
+    // g = c2 + e2*cL = g0 + gc rho_c2 + gL rho_L + ge rho_e2 + geL rho_e2 rho_L
+    const T g0 = c2h + e2h * cLh, gc = sc2, gL = e2h * sL, ge = cLh * se2, geL = se2 * sL;
+    const T t1 = e1h * g0;
+    const T tau[9] = {e1h * gc, e1h * gL, e1h * ge, e1h * geL, se1 * g0, se1 * gc, se1 * gL, se1 * ge, se1 * geL};
+    a[0] = su * (T(1) - T(2) * t1);
+#pragma unroll
+    for (int k = 0; k < 9; k++) a[1 + k] = su * tau[k], a[10 + k] = T(0) - T(2) * su * tau[k];
+    return q + su * t1;
+}
+
 // ---------------------------------------------------------------- keygen
 
 template <typename T>
@@ -60,6 +96,13 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                     dcf_keygen(A, alpha, L.H.d, A.prg(a.dk.rk, a.op, P_HI_S0, e), A.prg(a.dk.rk, a.op, P_HI_DELTA, e),
                                o, e, N);
             }
+            if (L.mid) {
+                const uint64_t alpha = uint64_t(r >> s) & ((uint64_t(1) << SPLIT3_MID) - 1);
+                DcfOut o{a.k0 + L.Mi.root, a.k1 + L.Mi.root, a.k0 + L.Mi.cw, a.k1 + L.Mi.cw,
+                         a.k0 + L.Mi.leaf, a.k1 + L.Mi.leaf, nullptr, nullptr};
+                dcfeq_keygen(A, alpha, SPLIT3_MID, A.prg(a.dk.rk, a.op, P_MID_S0, e),
+                             A.prg(a.dk.rk, a.op, P_MID_DELTA, e), o, e, N);
+            }
             if (L.lo) {
                 const uint64_t alpha = uint64_t(r) & ((uint64_t(1) << L.Lo.d) - 1);
                 DcfOut o{a.k0 + L.Lo.root, a.k1 + L.Lo.root, a.k0 + L.Lo.cw, a.k1 + L.Lo.cw,
@@ -67,7 +110,7 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                 dcf_keygen(A, alpha, L.Lo.d, A.prg(a.dk.rk, a.op, P_LO_S0, e), A.prg(a.dk.rk, a.op, P_LO_DELTA, e), o,
                            e, N);
             }
-            T v[32];
+            T v[80];
             // split gates: monomials of the dealer bits the DReLU bit depends on,
             // eps = r_m ^ rho_c: eps, rho_L, rho_e, rho_e rho_L, eps rho_L, eps rho_e, eps rho_e rho_L
             const T rho_e = T(((bits >> 4) ^ (bits >> 5)) & 1u);
@@ -92,6 +135,24 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                 // carry = c1 + e1*c2 (exclusive terms); masks rho_c (c1), rho_e (e1), rho_L (c2)
                 v[0] = r_H, v[1] = rho_c, v[2] = rho_e, v[3] = rho_L, v[4] = rho_e * rho_L, v[5] = r_m, v[6] = r_y;
                 break;
+            case GATE_RELU_SPLIT3:
+            case GATE_RELU_ARS_SPLIT3: {
+                const T rho_m = T(((bits >> 6) ^ (bits >> 7)) & 1u), rho_me = T(((bits >> 8) ^ (bits >> 9)) & 1u);
+                T m3[SPLIT3_NMONO];
+                split3_monomials<T>(e_b, rho_e, rho_m, rho_L, rho_me, m3);
+                if (a.kind == GATE_RELU_SPLIT3) {
+                    for (int k = 0; k < SPLIT3_NMONO; k++) v[k] = m3[k], v[20 + k] = m3[k] * r;
+                    v[19] = r, v[39] = r_y;
+                } else {
+                    const T nj[3] = {r_H, rho_L, r_m};
+                    for (int k = 0; k < SPLIT3_NMONO; k++) v[k] = m3[k];
+                    for (int j = 0; j < 3; j++) v[19 + j] = nj[j];
+                    for (int k = 0; k < SPLIT3_NMONO; k++)
+                        for (int j = 0; j < 3; j++) v[22 + 3 * k + j] = m3[k] * nj[j];
+                    v[79] = r_y;
+                }
+                break;
+            }
             case GATE_RELU_ARS_SPLIT: {
                 const T nj[3] = {r_H, rho_L, r_m};
                 for (int k = 0; k < 7; k++) v[k] = mono[k];
@@ -121,6 +182,10 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
         const uint32_t m1l = __ballot_sync(0xFFFFFFFFu, valid && (bits & 8u));
         const uint32_t m0e = __ballot_sync(0xFFFFFFFFu, valid && (bits & 16u));
         const uint32_t m1e = __ballot_sync(0xFFFFFFFFu, valid && (bits & 32u));
+        const uint32_t m0m = __ballot_sync(0xFFFFFFFFu, valid && (bits & 64u));
+        const uint32_t m1m = __ballot_sync(0xFFFFFFFFu, valid && (bits & 128u));
+        const uint32_t m0me = __ballot_sync(0xFFFFFFFFu, valid && (bits & 256u));
+        const uint32_t m1me = __ballot_sync(0xFFFFFFFFu, valid && (bits & 512u));
         if ((threadIdx.x & 31) == 0) {
             const uint64_t wi = e >> 5;
             if (L.hi) {
@@ -130,6 +195,12 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                     reinterpret_cast<uint32_t *>(a.k0 + L.H.mu_eq)[wi] = m0e;
                     reinterpret_cast<uint32_t *>(a.k1 + L.H.mu_eq)[wi] = m1e;
                 }
+            }
+            if (L.mid) {
+                reinterpret_cast<uint32_t *>(a.k0 + L.Mi.mu)[wi] = m0m;
+                reinterpret_cast<uint32_t *>(a.k1 + L.Mi.mu)[wi] = m1m;
+                reinterpret_cast<uint32_t *>(a.k0 + L.Mi.mu_eq)[wi] = m0me;
+                reinterpret_cast<uint32_t *>(a.k1 + L.Mi.mu_eq)[wi] = m1me;
             }
             if (L.lo) {
                 reinterpret_cast<uint32_t *>(a.k0 + L.Lo.mu)[wi] = m0l;
@@ -146,9 +217,11 @@ struct Round1Args {
     int n, s, hi_d, hi_shift, lo_d;
     uint64_t N;
     const T *xhat;
-    DcfView hi, lo;
-    bool has_hi, has_lo, split;
-    uint32_t *bits_hi, *bits_lo;  // split gates: bits_hi[0, nw) compare, [nw, 2nw) equality
+    DcfView hi, mid, lo;
+    bool has_hi, has_mid, has_lo, split;
+    // split gates: bits_hi[0, nw) compare, [nw, 2nw) equality; with a middle
+    // DCF also [2nw, 3nw) its compare and [3nw, 4nw) its equality
+    uint32_t *bits_hi, *bits_lo;
 };
 
 template <typename T, class E>
@@ -164,7 +237,7 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_round1_kernel(const 
     const T lmask = (T(1) << a.lo_d) - 1;
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
         const bool valid = e < N;
-        uint32_t bh = 0, bl = 0, be = 0;
+        uint32_t bh = 0, bl = 0, be = 0, bm = 0, bme = 0;
         if (valid) {
             const T x = __ldcs(a.xhat + e);
             if (a.has_hi) {
@@ -176,15 +249,26 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_round1_kernel(const 
                     bh = dcf_eval(A, xh, a.hi_d, a.hi, e, N);
                 }
             }
+            if (a.has_mid) {
+                const uint32_t b =
+                    dcfeq_eval(A, uint64_t((x >> a.s) & T((1u << SPLIT3_MID) - 1)), SPLIT3_MID, a.mid, e, N);
+                bm = b & 1u, bme = b >> 1;
+            }
             if (a.has_lo) bl = dcf_eval(A, uint64_t(x & lmask), a.lo_d, a.lo, e, N);
         }
         const uint32_t wh = __ballot_sync(0xFFFFFFFFu, bh);
         const uint32_t wl = __ballot_sync(0xFFFFFFFFu, bl);
         const uint32_t we = __ballot_sync(0xFFFFFFFFu, be);
+        const uint32_t wm = __ballot_sync(0xFFFFFFFFu, bm);
+        const uint32_t wme = __ballot_sync(0xFFFFFFFFu, bme);
         if ((threadIdx.x & 31) == 0) {
-            const uint64_t wi = e >> 5;
+            const uint64_t wi = e >> 5, nw = (N + 31) >> 5;
             if (a.has_hi) a.bits_hi[wi] = wh ^ __ldcs(a.hi.mu + wi);
-            if (a.split) a.bits_hi[((N + 31) >> 5) + wi] = we ^ __ldcs(a.hi.mu_eq + wi);
+            if (a.split) a.bits_hi[nw + wi] = we ^ __ldcs(a.hi.mu_eq + wi);
+            if (a.has_mid) {
+                a.bits_hi[2 * nw + wi] = wm ^ __ldcs(a.mid.mu + wi);
+                a.bits_hi[3 * nw + wi] = wme ^ __ldcs(a.mid.mu_eq + wi);
+            }
             if (a.has_lo) a.bits_lo[wi] = wl ^ __ldcs(a.lo.mu + wi);
         }
     }
@@ -216,7 +300,8 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
         T ch = 0, cl = 0, eh = 0;
         if (KIND != GATE_LRS) ch = T(((a.hi_own[wi] ^ a.hi_peer[wi]) >> bi) & 1u);
         if (KIND != GATE_RELU) cl = T(((a.lo_own[wi] ^ a.lo_peer[wi]) >> bi) & 1u);
-        if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT || KIND == GATE_LRS_SPLIT)
+        if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT || KIND == GATE_LRS_SPLIT ||
+            KIND == GATE_RELU_SPLIT3 || KIND == GATE_RELU_ARS_SPLIT3)
             eh = T(((a.hi_own[a.nw + wi] ^ a.hi_peer[a.nw + wi]) >> bi) & 1u);
         const T mh = x >> (n - 1);
         const T xH = x >> s;
@@ -260,6 +345,34 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
                     smn += ak[k] * t;
                 }
                 y = p0 * a0 * Y0 + Y0 * sm + a0 * sn + smn + W(31);
+            }
+        } else if (KIND == GATE_RELU_SPLIT3 || KIND == GATE_RELU_ARS_SPLIT3) {
+            const T cm = T(((a.hi_own[2 * a.nw + wi] ^ a.hi_peer[2 * a.nw + wi]) >> bi) & 1u);
+            const T em = T(((a.hi_own[3 * a.nw + wi] ^ a.hi_peer[3 * a.nw + wi]) >> bi) & 1u);
+            T ak[SPLIT3_NMONO];
+            const T a0 = split3_coeffs<T>(q, eh, cm, em, cl, ak);
+            T sm = 0;
+#pragma unroll
+            for (int k = 0; k < SPLIT3_NMONO; k++) sm += ak[k] * W(k);
+            if (KIND == GATE_RELU_SPLIT3) {
+                T sr = 0;
+#pragma unroll
+                for (int k = 0; k < SPLIT3_NMONO; k++) sr += ak[k] * W(20 + k);
+                y = p0 * a0 * x + x * sm - a0 * W(19) - sr + W(39);
+            } else {
+                const T Y0 = xH - cl;
+                const T yj[3] = {T(0) - T(1), T(0) - b1, two_ns * (T(1) - mh)};
+                T sn = 0, smn = 0;
+#pragma unroll
+                for (int j = 0; j < 3; j++) sn += yj[j] * W(19 + j);
+#pragma unroll
+                for (int k = 0; k < SPLIT3_NMONO; k++) {
+                    T t = 0;
+#pragma unroll
+                    for (int j = 0; j < 3; j++) t += yj[j] * W(22 + 3 * k + j);
+                    smn += ak[k] * t;
+                }
+                y = p0 * a0 * Y0 + Y0 * sm + a0 * sn + smn + W(79);
             }
         } else if (KIND == GATE_LRS_SPLIT) {
             // carry = c1 + e1*c2 with c1 = ch ^ rho_c, e1 = eh ^ rho_e, c2 = cl ^ rho_L
@@ -343,8 +456,9 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
     a.n = L.bw, a.s = L.s, a.N = L.n, a.hi_d = L.H.d, a.hi_shift = L.hi_shift, a.lo_d = L.Lo.d;
     a.xhat = static_cast<const T *>(xhat);
     const uint8_t *k = static_cast<const uint8_t *>(key);
-    a.has_hi = L.hi, a.has_lo = L.lo, a.split = L.hi && L.H.eq;
+    a.has_hi = L.hi, a.has_mid = L.mid, a.has_lo = L.lo, a.split = L.hi && L.H.eq;
     a.hi = L.hi ? dcf_view(k, L.H) : DcfView{};
+    a.mid = L.mid ? dcf_view(k, L.Mi) : DcfView{};
     a.lo = L.lo ? dcf_view(k, L.Lo) : DcfView{};
     a.bits_hi = bits_hi, a.bits_lo = bits_lo;
     DcfTiming *tm = dcf_timing_sink();
@@ -364,6 +478,7 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
         const double n = double(L.n);
         double bytes = n * (L.bw / 8.0), aes = 0;
         if (L.hi) bytes += n * (16.0 * (L.H.L + 2) + (L.H.eq ? 0.5 : 0.25)), aes += n * (L.H.L + 1);
+        if (L.mid) bytes += n * (16.0 * (L.Mi.L + 2) + 0.5), aes += n * (L.Mi.L + 1);
         if (L.lo) bytes += n * (16.0 * (L.Lo.L + 2) + 0.125 + 0.125), aes += n * (L.Lo.L + 1);
         rec->bytes = bytes, rec->aes = aes, rec->evals = n * ((L.hi ? 1 : 0) + (L.lo ? 1 : 0));
         tm->nrec++;
@@ -393,6 +508,8 @@ int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32
     case GATE_RELU_SPLIT: gate_round2_kernel<T, GATE_RELU_SPLIT><<<grid, 256, 0, st>>>(a); break;
     case GATE_RELU_ARS_SPLIT: gate_round2_kernel<T, GATE_RELU_ARS_SPLIT><<<grid, 256, 0, st>>>(a); break;
     case GATE_LRS_SPLIT: gate_round2_kernel<T, GATE_LRS_SPLIT><<<grid, 256, 0, st>>>(a); break;
+    case GATE_RELU_SPLIT3: gate_round2_kernel<T, GATE_RELU_SPLIT3><<<grid, 256, 0, st>>>(a); break;
+    case GATE_RELU_ARS_SPLIT3: gate_round2_kernel<T, GATE_RELU_ARS_SPLIT3><<<grid, 256, 0, st>>>(a); break;
     default: gate_round2_kernel<T, GATE_LRS><<<grid, 256, 0, st>>>(a); break;
     }
     note_launch();

@@ -48,6 +48,14 @@ extern "C" {
  * at scale 12) for 7 key words instead of 4; scale >= 2.  Round 1 emits three
  * bit arrays like the other split kinds. */
 #define DDG_GATE_LRS_SPLIT 6
+/* Same functions as RELU / RELU_ARS with the (bw-1)-bit comparison split in
+ * three: the upper bits U1 and the 6 bits U2 above the low scale bits V, each
+ * of U1, U2 a DCF with equality output, V the scale-bit DCF:
+ * 1{x<a} = c1 + e1*(c2 + e2*cL).  15 instead of 20 AES-128 per element at
+ * bw=32 for 40 / 80 key words instead of 16 / 32; scale + 6 < bw - 1.  Round 1
+ * emits five bit arrays (see ddg_gate_round1). */
+#define DDG_GATE_RELU_SPLIT3 7
+#define DDG_GATE_RELU_ARS_SPLIT3 8
 
 const char *ddg_last_error(void);
 int ddg_version(void);
@@ -71,11 +79,13 @@ int ddg_version(void);
 /* bytes of one party's key for n elements */
 uint64_t ddg_gate_key_bytes(int kind, int bw, int scale, uint64_t n);
 
-/* byte offsets of one party's key for n elements, written to out[16]:
+/* byte offsets of one party's key for n elements, written to out[22]:
  *   0 hi_root 1 hi_cw 2 hi_leaf 3 hi_mu 4 lo_root 5 lo_cw 6 lo_leaf 7 lo_mu
  *   8 words 9 total bytes 10 high-DCF tree levels 11 low-DCF tree levels
  *   12 hi_mu_eq (split kinds) 13 high-DCF domain bits 14 position of the
  *   high DCF's lowest input bit in x_hat 15 low-DCF domain bits
+ *   16 mid_root 17 mid_cw 18 mid_leaf 19 mid_mu 20 mid_mu_eq 21 middle-DCF
+ *   tree levels (three-part split kinds; 0 otherwise)
  * Each DCF is structure-of-arrays: root[n] 16 B, cw[levels][n] 16 B
  * (level-major), leaf[n] 16 B, mu[ceil(n/32)] u32 mask bits; then
  * nwords x n ring words.  Every array starts on a 256-byte boundary. */
@@ -89,8 +99,9 @@ int ddg_gate_keygen(int kind, int bw, int scale, uint64_t n, uint64_t seed, uint
 /* round 1: d_bits_hi / d_bits_lo hold ceil(n/32) words each (a gate without
  * the high DCF (LRS) or the low DCF (RELU) leaves that array untouched); for
  * the split kinds d_bits_hi holds 2*ceil(n/32) words: the compare bits, then
- * the equality bits.  Round 2 reads its own and the peer's arrays in the same
- * layout. */
+ * the equality bits; for the three-part split kinds 4*ceil(n/32) words: then
+ * the middle DCF's compare and equality bits.  Round 2 reads its own and the
+ * peer's arrays in the same layout. */
 int ddg_gate_round1(int kind, int bw, int scale, uint64_t n, const void *d_xhat, const void *d_key,
                     uint32_t *d_bits_hi, uint32_t *d_bits_lo, void *stream);
 
@@ -298,6 +309,12 @@ int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_
  * round column; 2 stages T0 and T2 in 64 KiB, three 256-thread CTAs per SM,
  * 8 instructions per column (T1 ^ T3 as an 8-bit rotation).  Same outputs. */
 int ddg_aes_tables(int tables);
+/* Comparison split of the forward's ReLU gates, process-wide: 3 (default,
+ * DDG_GATE_RELU*_SPLIT3: fewest AES) or 2 (DDG_GATE_RELU*_SPLIT: smaller
+ * keys, for key-streaming regimes).  It changes the key layout: the dealer
+ * (ddg_dealer_forward, ddg_forward_key_bytes) and both evaluators must run
+ * with the same setting. */
+int ddg_relu_split(int parts);
 
 #ifdef __cplusplus
 }

@@ -352,12 +352,18 @@ int ref_dcfeq_eval(int d, uint64_t x, const uint8_t root[16], const uint8_t *cw,
 /* ----------------------------------------------------------------- gates */
 
 enum { GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
-       GATE_LRS_SPLIT = 6 };
+       GATE_LRS_SPLIT = 6, GATE_RELU_SPLIT3 = 7, GATE_RELU_ARS_SPLIT3 = 8 };
+
+/* three-part split ReLU gates: the (n-1)-bit compare over (U1, U2, V) with
+ * U2 = SPLIT3_MID bits above the low s bits V and U1 the rest:
+ * 1{x_l < r_l} = c1 + e1*(c2 + e2*cL), every sum exclusive */
+#define SPLIT3_MID 6
+static int is_split3(int kind) { return kind == GATE_RELU_SPLIT3 || kind == GATE_RELU_ARS_SPLIT3; }
 
 /* kinds whose high DCF has an equality output */
 static int is_split(int kind)
 {
-    return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT || kind == GATE_LRS_SPLIT;
+    return kind == GATE_RELU_SPLIT || kind == GATE_RELU_ARS_SPLIT || kind == GATE_LRS_SPLIT || is_split3(kind);
 }
 /* GATE_LRS_SPLIT: the s-bit carry comparison over (V1, V2), V2 the low
  * lrs_lo_bits(s) bits: 1{V < B} = 1{V1 < B1} + 1{V1 == B1} * 1{V2 < B2} */
@@ -365,7 +371,7 @@ static int lrs_lo_bits(int s) { return s - 1 < 7 ? s - 1 : 7; }
 
 enum {
     P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4,
-    P_ROUT = 5, P_BITS = 6, P_SHARE = 16
+    P_ROUT = 5, P_BITS = 6, P_MID_S0 = 9, P_MID_DELTA = 10, P_SHARE = 16
 };
 
 typedef struct {
@@ -378,7 +384,12 @@ typedef struct {
     uint8_t lo_cw[56][16];
     uint8_t lo_leaf[16];
     int32_t lo_mu;
-    uint64_t w[32];
+    uint8_t mid_root[16];
+    uint8_t mid_cw[56][16];
+    uint8_t mid_leaf[16];
+    int32_t mid_mu;
+    int32_t mid_mu_eq;
+    uint64_t w[80];
 } ref_gate_key;
 
 int ref_gate_has_hi(int kind) { return kind != GATE_LRS; }
@@ -392,14 +403,60 @@ int ref_gate_nwords(int kind)
     case GATE_RELU_SPLIT: return 16;
     case GATE_RELU_ARS_SPLIT: return 32;
     case GATE_LRS_SPLIT: return 7;
+    case GATE_RELU_SPLIT3: return 40;
+    case GATE_RELU_ARS_SPLIT3: return 80;
     default: return 4;
     }
+}
+
+/*
+ * Three-part split: the DReLU bit d = q ^ eps ^ t with q = 1^m_hat^c1_hat
+ * public, eps = r_m ^ rho_c1, and t = e1*(c2 + e2*cL) in {0,1}.  With every
+ * true bit b = b_hat + (1-2 b_hat) rho_b, t is multilinear in the mask bits
+ * (rho_e1, rho_c2, rho_e2, rho_L) over the nine monomials SPLIT3_T below, and
+ *   d = q + (1-2q) [tau_1 + (1-2 tau_1) eps + sum tau_m m - 2 sum tau_m eps m].
+ * Dealer words carry the 19 monomials [eps, m (9), eps*m (9)].
+ */
+#define SPLIT3_NMONO 19
+/* mask-bit monomials of t, as bit sets over (e1, c2, L, e2) = bits 0..3 */
+static const int SPLIT3_T[9] = {2, 4, 8, 12, 1, 3, 5, 9, 13};
+
+static void split3_monomials(uint64_t ep, uint64_t pe1, uint64_t p2, uint64_t pL, uint64_t pe2, uint64_t mono[19])
+{
+    const uint64_t var[4] = {pe1, p2, pL, pe2};
+    mono[0] = ep;
+    for (int k = 0; k < 9; k++) {
+        uint64_t v = 1;
+        for (int b = 0; b < 4; b++)
+            if (SPLIT3_T[k] >> b & 1) v *= var[b];
+        mono[1 + k] = v;
+        mono[10 + k] = ep * v;
+    }
+}
+
+/* evaluator: a0 and the coefficients of the 19 monomials (mod 2^64) */
+static uint64_t split3_coeffs(uint64_t q, uint64_t e1h, uint64_t c2h, uint64_t e2h, uint64_t cLh, uint64_t a[19])
+{
+    const uint64_t su = 1 - 2 * q, se1 = 1 - 2 * e1h, sc2 = 1 - 2 * c2h, se2 = 1 - 2 * e2h, sL = 1 - 2 * cLh;
+    /* g = c2 + e2*cL = g0 + gc*rho_c2 + gL*rho_L + ge*rho_e2 + geL*rho_e2*rho_L */
+    const uint64_t g0 = c2h + e2h * cLh, gc = sc2, gL = e2h * sL, ge = cLh * se2, geL = se2 * sL;
+    /* t = e1*g: constant and the SPLIT3_T monomials in order */
+    const uint64_t t1 = e1h * g0;
+    const uint64_t tau[9] = {e1h * gc, e1h * gL, e1h * ge, e1h * geL, se1 * g0, se1 * gc, se1 * gL, se1 * ge,
+                             se1 * geL};
+    a[0] = su * (1 - 2 * t1);
+    for (int k = 0; k < 9; k++) {
+        a[1 + k] = su * tau[k];
+        a[10 + k] = 0 - 2 * su * tau[k];
+    }
+    return q + su * t1;
 }
 /* domain bits of the high DCF: n-1, the upper n-1-s bits for the split ReLU
  * gates, the upper s - lrs_lo_bits(s) carry bits for GATE_LRS_SPLIT */
 int ref_gate_hi_bits(int kind, int n, int s)
 {
     if (kind == GATE_LRS_SPLIT) return s - lrs_lo_bits(s);
+    if (is_split3(kind)) return n - 1 - s - SPLIT3_MID;
     return is_split(kind) ? n - 1 - s : n - 1;
 }
 
@@ -432,7 +489,10 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
     ref_prg(&ks, op, P_BITS, i, blk);
     int mu0h = blk[0] & 1, mu1h = (blk[0] >> 1) & 1, mu0l = (blk[0] >> 2) & 1, mu1l = (blk[0] >> 3) & 1;
     int mu0e = (blk[0] >> 4) & 1, mu1e = (blk[0] >> 5) & 1;
+    /* three-part split: the middle DCF's compare (bits 6/7) and equality (bits 8/9) masks */
+    int mu0m = (blk[0] >> 6) & 1, mu1m = (blk[0] >> 7) & 1, mu0me = blk[1] & 1, mu1me = (blk[1] >> 1) & 1;
     int rho_c = mu0h ^ mu1h, rho_L = mu0l ^ mu1l, rho_e = mu0e ^ mu1e;
+    int rho_m = mu0m ^ mu1m, rho_me = mu0me ^ mu1me;
 
     uint64_t r_m = (r_in >> (n - 1)) & 1;
     uint64_t r_l = r_in & (M >> 1);
@@ -459,7 +519,10 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
     } else if (ref_gate_has_hi(kind)) {
         ref_prg(&ks, op, P_HI_S0, i, blk);
         ref_prg(&ks, op, P_HI_DELTA, i, blk2);
-        if (is_split(kind))
+        if (is_split3(kind))
+            ref_dcfeq_keygen(n - 1 - s - SPLIT3_MID, r_l >> (s + SPLIT3_MID), blk, blk2, k0->hi_root, k1->hi_root,
+                             &k0->hi_cw[0][0], k0->hi_leaf);
+        else if (is_split(kind))
             ref_dcfeq_keygen(n - 1 - s, r_l >> s, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
         else
             ref_dcf_keygen(n - 1, r_l, blk, blk2, k0->hi_root, k1->hi_root, &k0->hi_cw[0][0], k0->hi_leaf);
@@ -472,6 +535,16 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
             k1->hi_mu_eq = mu1e;
         }
     }
+    if (is_split3(kind)) {
+        ref_prg(&ks, op, P_MID_S0, i, blk);
+        ref_prg(&ks, op, P_MID_DELTA, i, blk2);
+        ref_dcfeq_keygen(SPLIT3_MID, (r_in >> s) & ((1ULL << SPLIT3_MID) - 1), blk, blk2, k0->mid_root, k1->mid_root,
+                         &k0->mid_cw[0][0], k0->mid_leaf);
+        memcpy(k1->mid_cw, k0->mid_cw, sizeof(k0->mid_cw));
+        memcpy(k1->mid_leaf, k0->mid_leaf, 16);
+        k0->mid_mu = mu0m, k1->mid_mu = mu1m;
+        k0->mid_mu_eq = mu0me, k1->mid_mu_eq = mu1me;
+    }
     if (ref_gate_has_lo(kind) && kind != GATE_LRS_SPLIT) {
         ref_prg(&ks, op, P_LO_S0, i, blk);
         ref_prg(&ks, op, P_LO_DELTA, i, blk2);
@@ -481,8 +554,10 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
         k0->lo_mu = mu0l;
         k1->lo_mu = mu1l;
     }
-    uint64_t v[32];
+    uint64_t v[80];
     int nw = ref_gate_nwords(kind);
+    uint64_t m3[SPLIT3_NMONO];
+    split3_monomials(r_m ^ (uint64_t)rho_c, (uint64_t)rho_e, (uint64_t)rho_m, (uint64_t)rho_L, (uint64_t)rho_me, m3);
     /* split gates: monomials of the dealer bits that the DReLU bit depends on,
      * eps = r_m ^ rho_c:  eps, rho_L, rho_e, rho_e*rho_L, eps*rho_L, eps*rho_e, eps*rho_e*rho_L */
     uint64_t ep = r_m ^ (uint64_t)rho_c, pl = (uint64_t)rho_L, pe = (uint64_t)rho_e;
@@ -508,6 +583,20 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
         /* carry = c1 + e1*c2; masks rho_c (c1), rho_e (e1), rho_L (c2) */
         v[0] = r_H; v[1] = (uint64_t)rho_c; v[2] = pe; v[3] = pl; v[4] = pe * pl; v[5] = r_m; v[6] = r_y;
         break;
+    case GATE_RELU_SPLIT3:
+        for (int k = 0; k < SPLIT3_NMONO; k++) v[k] = m3[k], v[20 + k] = m3[k] * r_in;
+        v[19] = r_in;
+        v[39] = r_y;
+        break;
+    case GATE_RELU_ARS_SPLIT3: {
+        uint64_t nj[3] = {r_H, pl, r_m};
+        for (int k = 0; k < SPLIT3_NMONO; k++) v[k] = m3[k];
+        for (int j = 0; j < 3; j++) v[19 + j] = nj[j];
+        for (int k = 0; k < SPLIT3_NMONO; k++)
+            for (int j = 0; j < 3; j++) v[22 + 3 * k + j] = m3[k] * nj[j];
+        v[79] = r_y;
+        break;
+    }
     case GATE_RELU_ARS_SPLIT: {
         uint64_t nj[3] = {r_H, pl, r_m};
         for (int k = 0; k < 7; k++) v[k] = mono[k];
@@ -531,7 +620,8 @@ uint64_t ref_gate_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uin
 }
 
 /* round 1: the party's output bits: bit0 = high DCF (compare), bit1 = low DCF,
- * bit2 = high DCF equality (split gates) */
+ * bit2 = high DCF equality (split gates), bit3 / bit4 = middle DCF compare /
+ * equality (three-part split gates) */
 int ref_gate_round1(int kind, int n, int s, uint64_t xhat, const ref_gate_key *k)
 {
     uint64_t M = nmask(n);
@@ -546,7 +636,14 @@ int ref_gate_round1(int kind, int n, int s, uint64_t xhat, const ref_gate_key *k
         return out;
     }
     if (ref_gate_has_hi(kind)) {
-        if (is_split(kind)) {
+        if (is_split3(kind)) {
+            int d = n - 1 - s - SPLIT3_MID;
+            int b = ref_dcfeq_eval(d, (xhat & (M >> 1)) >> (s + SPLIT3_MID), k->hi_root, &k->hi_cw[0][0], k->hi_leaf);
+            out |= ((b & 1) ^ k->hi_mu) | ((((b >> 1) & 1) ^ k->hi_mu_eq) << 2);
+            b = ref_dcfeq_eval(SPLIT3_MID, (xhat >> s) & ((1ULL << SPLIT3_MID) - 1), k->mid_root, &k->mid_cw[0][0],
+                               k->mid_leaf);
+            out |= (((b & 1) ^ k->mid_mu) << 3) | ((((b >> 1) & 1) ^ k->mid_mu_eq) << 4);
+        } else if (is_split(kind)) {
             int b = ref_dcfeq_eval(n - 1 - s, (xhat & (M >> 1)) >> s, k->hi_root, &k->hi_cw[0][0], k->hi_leaf);
             out |= ((b & 1) ^ k->hi_mu) | ((((b >> 1) & 1) ^ k->hi_mu_eq) << 2);
         } else {
@@ -560,7 +657,8 @@ int ref_gate_round1(int kind, int n, int s, uint64_t xhat, const ref_gate_key *k
 }
 
 /* round 2: party's additive share of the masked output, given the opened bits
- * (bit0 = c_hat, bit1 = cL_hat, bit2 = e_hat) */
+ * (bit0 = c_hat, bit1 = cL_hat, bit2 = e_hat, bit3 / bit4 = the middle DCF's
+ * c2_hat / e2_hat) */
 uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int bits, const ref_gate_key *k)
 {
     uint64_t M = nmask(n);
@@ -599,6 +697,27 @@ uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int b
         uint64_t sx = 0, sr = 0;
         for (int t = 0; t < 7; t++) sx += a[t] * w[t], sr += a[t] * w[8 + t];
         y = p0 * a0 * xhat + xhat * sx - a0 * w[7] - sr + w[15];
+        break;
+    }
+    case GATE_RELU_SPLIT3:
+    case GATE_RELU_ARS_SPLIT3: {
+        uint64_t a3[SPLIT3_NMONO];
+        uint64_t b0 = split3_coeffs(q, eh, (uint64_t)((bits >> 3) & 1), (uint64_t)((bits >> 4) & 1), cl, a3);
+        uint64_t sm = 0;
+        for (int t = 0; t < SPLIT3_NMONO; t++) sm += a3[t] * w[t];
+        if (kind == GATE_RELU_SPLIT3) {
+            uint64_t sr = 0;
+            for (int t = 0; t < SPLIT3_NMONO; t++) sr += a3[t] * w[20 + t];
+            y = p0 * b0 * xhat + xhat * sm - b0 * w[19] - sr + w[39];
+        } else {
+            uint64_t Y0 = xH - cl;
+            uint64_t yj[3] = {0 - 1, 0 - sc, two_ns * (1 - mh)};
+            uint64_t sn = 0, smn = 0;
+            for (int j = 0; j < 3; j++) sn += yj[j] * w[19 + j];
+            for (int t = 0; t < SPLIT3_NMONO; t++)
+                for (int j = 0; j < 3; j++) smn += a3[t] * yj[j] * w[22 + 3 * t + j];
+            y = p0 * b0 * Y0 + Y0 * sm + b0 * sn + smn + w[79];
+        }
         break;
     }
     case GATE_LRS_SPLIT: {

@@ -21,11 +21,14 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "libfss_ref.so")
 
-GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT = range(7)
+(GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
+ GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3) = range(9)
 GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4, GATE_RELU_SPLIT: 16,
-               GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7}
-# kinds whose high DCF also outputs equality (three round-1 bit arrays)
-SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT)
+               GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7, GATE_RELU_SPLIT3: 40, GATE_RELU_ARS_SPLIT3: 80}
+# kinds whose high DCF also outputs equality (three round-1 bit arrays or more)
+SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT, GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3)
+# kinds with a middle DCF with equality output (five round-1 bit arrays)
+SPLIT3_KINDS = (GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3)
 
 
 def build() -> str:
@@ -46,7 +49,12 @@ class GateKey(ctypes.Structure):
         ("lo_cw", (ctypes.c_uint8 * 16) * 56),
         ("lo_leaf", ctypes.c_uint8 * 16),
         ("lo_mu", ctypes.c_int32),
-        ("w", ctypes.c_uint64 * 32),
+        ("mid_root", ctypes.c_uint8 * 16),
+        ("mid_cw", (ctypes.c_uint8 * 16) * 56),
+        ("mid_leaf", ctypes.c_uint8 * 16),
+        ("mid_mu", ctypes.c_int32),
+        ("mid_mu_eq", ctypes.c_int32),
+        ("w", ctypes.c_uint64 * 80),
     ]
 
 
@@ -150,7 +158,7 @@ def dcf_eval(d: int, x: int, root: bytes, cw: bytes, leaf: bytes) -> int:
 
 
 def dcfeq_keygen(d: int, alpha: int, s0: bytes, delta: bytes):
-    L = d - 6
+    L = max(d - 6, 0)
     r0, r1 = (ctypes.c_uint8 * 16)(), (ctypes.c_uint8 * 16)()
     cw = (ctypes.c_uint8 * (16 * max(L, 1)))()
     leaf = (ctypes.c_uint8 * 16)()
@@ -174,7 +182,8 @@ def gate_round1(kind: int, n: int, s: int, xhat: int, key: GateKey) -> int:
 
 
 def gate_round2(kind: int, n: int, s: int, party: int, xhat: int, bits: int, key: GateKey) -> int:
-    """bits: opened round-1 bits, bit0 = high compare, bit1 = low compare, bit2 = high equality."""
+    """bits: opened round-1 bits, bit0 = high compare, bit1 = low compare, bit2 = high equality,
+    bit3 / bit4 = middle compare / equality (three-part split kinds)."""
     return lib().ref_gate_round2(kind, n, s, party, xhat, bits, ctypes.byref(key))
 
 
@@ -210,5 +219,7 @@ def gate_key_bytes(key: GateKey) -> dict:
     return {
         "hi_root": bytes(key.hi_root), "hi_cw": bytes(key.hi_cw), "hi_leaf": bytes(key.hi_leaf),
         "hi_mu": key.hi_mu, "hi_mu_eq": key.hi_mu_eq, "lo_root": bytes(key.lo_root), "lo_cw": bytes(key.lo_cw),
-        "lo_leaf": bytes(key.lo_leaf), "lo_mu": key.lo_mu, "w": list(key.w),
+        "lo_leaf": bytes(key.lo_leaf), "lo_mu": key.lo_mu, "mid_root": bytes(key.mid_root),
+        "mid_cw": bytes(key.mid_cw), "mid_leaf": bytes(key.mid_leaf), "mid_mu": key.mid_mu,
+        "mid_mu_eq": key.mid_mu_eq, "w": list(key.w),
     }

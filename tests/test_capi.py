@@ -44,4 +44,20 @@ def test_split_lrs_layout(ddg):
     with pytest.raises(ddg.DdgError):
         ddg.gate_key_layout(ddg.GATE_LRS_SPLIT, 32, 1, 10)
     with pytest.raises(ddg.DdgError):
-        ddg.gate_key_layout(ddg.GATE_LRS_SPLIT + 1, 32, 12, 10)
+        ddg.gate_key_layout(ddg.GATE_RELU_ARS_SPLIT3 + 1, 32, 12, 10)
+
+
+def test_three_part_split_layout(ddg):
+    """Three-part split ReLU at bw=32, scale 12: a 13-bit DCF with equality
+    (7 levels) over bits 18..30, a 6-bit one (leaf only) over bits 12..17 and
+    the 12-bit DCF (5 levels); 15 AES per element in all."""
+    for kind, words in ((ddg.GATE_RELU_SPLIT3, 40), (ddg.GATE_RELU_ARS_SPLIT3, 80)):
+        lay = ddg.gate_key_layout(kind, 32, 12, 1000)
+        assert (lay["hi_bits"], lay["hi_shift"], lay["hi_levels"]) == (13, 18, 7)
+        assert lay["mid_levels"] == 0 and lay["mid_mu_eq"] > lay["mid_mu"] > lay["mid_root"] > lay["hi_mu_eq"]
+        assert (lay["lo_bits"], lay["lo_levels"]) == (12, 5) and lay["lo_root"] > lay["mid_mu_eq"]
+        aes = lay["hi_levels"] + 1 + lay["mid_levels"] + 1 + lay["lo_levels"] + 1
+        assert aes == 15
+        assert lay["bytes"] - lay["words"] >= words * 4 * 1000
+    with pytest.raises(ddg.DdgError):  # scale + 6 must stay below bw - 1
+        ddg.gate_key_layout(ddg.GATE_RELU_SPLIT3, 32, 25, 10)

@@ -15,15 +15,15 @@ from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 
 S = 12
 KINDS = [F.GATE_RELU, F.GATE_RELU_ARS, F.GATE_ARS, F.GATE_LRS, F.GATE_RELU_SPLIT, F.GATE_RELU_ARS_SPLIT,
-         F.GATE_LRS_SPLIT]
+         F.GATE_LRS_SPLIT, F.GATE_RELU_SPLIT3, F.GATE_RELU_ARS_SPLIT3]
 LRS_KINDS = (F.GATE_LRS, F.GATE_LRS_SPLIT)
 
 
 def plain(kind, x, bw):
     R = Ring(bw)
-    if kind in (F.GATE_RELU, F.GATE_RELU_SPLIT):
+    if kind in (F.GATE_RELU, F.GATE_RELU_SPLIT, F.GATE_RELU_SPLIT3):
         return R.relu(x)
-    if kind in (F.GATE_RELU_ARS, F.GATE_RELU_ARS_SPLIT):
+    if kind in (F.GATE_RELU_ARS, F.GATE_RELU_ARS_SPLIT, F.GATE_RELU_ARS_SPLIT3):
         return R.relu_ars(x, S)
     if kind == F.GATE_ARS:
         return R.ars(x, S)
@@ -61,6 +61,11 @@ def make_inputs(bw, kind, n, seed):
     xh2 = (r & ~m31) | (rng.integers(0, 32, size=n, dtype=dt) & m31)
     xh2 = (xh2 + (rng.integers(0, 1 << 16, size=n, dtype=dt) << dt(12))).astype(dt)
     x[sel2] = (xh2 - r).astype(dt)[sel2]
+    # every 11th element: x_hat agrees with r on bits 18..bw-2 (three-part split: U1 equal)
+    sel3 = np.arange(n) % 11 == 6
+    lo18 = dt((1 << 18) - 1)
+    xh3 = (r & ~lo18) | (rng.integers(0, 1 << 18, size=n, dtype=dt) & lo18)
+    x[sel3] = (xh3 - r).astype(dt)[sel3]
     if kind in LRS_KINDS:
         x &= dt(hi >> 1)
     return x, r
@@ -75,7 +80,7 @@ def run_gate(ddg, kind, bw, n, x, r, seed=5, op=3):
     xh = (x + r).astype(dt)
     d_x = to_dev(xh)
     words = (n + 31) // 32
-    bits = {(p, h): dev_bytes(8 * words) for p in (0, 1) for h in ("hi", "lo")}
+    bits = {(p, h): dev_bytes(16 * words) for p in (0, 1) for h in ("hi", "lo")}  # up to 4 arrays of bits
     for p, k in ((0, k0), (1, k1)):
         ddg.gate_round1(kind, bw, S, n, ptr(d_x), ptr(k), ptr(bits[p, "hi"]), ptr(bits[p, "lo"]))
     shares = [dev_bytes(n * (bw // 8)) for _ in range(2)]
@@ -87,14 +92,14 @@ def run_gate(ddg, kind, bw, n, x, r, seed=5, op=3):
 
     torch.cuda.synchronize()
     return dict(k0=k0.cpu().numpy(), k1=k1.cpu().numpy(), rout=from_dev(d_ro, dt, n),
-                bits={kk: from_dev(v, np.uint32, 2 * words) for kk, v in bits.items()},
+                bits={kk: from_dev(v, np.uint32, 4 * words) for kk, v in bits.items()},
                 y0=from_dev(shares[0], dt, n), y1=from_dev(shares[1], dt, n), xh=xh)
 
 
 def key_fields(blob, lay, n, e, bw):
     """One element's key out of the SoA blob, in the oracle's per-element form."""
     f = {}
-    for side in ("hi", "lo"):
+    for side in ("hi", "mid", "lo"):
         L = lay[f"{side}_levels"]
         if lay[f"{side}_root"] == 0 and lay[f"{side}_cw"] == 0:
             continue
@@ -103,8 +108,8 @@ def key_fields(blob, lay, n, e, bw):
                       for j in range(L))
         leaf = blob[lay[f"{side}_leaf"] + 16 * e: lay[f"{side}_leaf"] + 16 * e + 16].tobytes()
         mu = (int(blob[lay[f"{side}_mu"]:].view(np.uint32)[e // 32]) >> (e % 32)) & 1
-        mu_eq = (int(blob[lay["hi_mu_eq"]:].view(np.uint32)[e // 32]) >> (e % 32)) & 1 if (
-            side == "hi" and lay["hi_mu_eq"]) else 0
+        mu_eq = (int(blob[lay[f"{side}_mu_eq"]:].view(np.uint32)[e // 32]) >> (e % 32)) & 1 if (
+            side in ("hi", "mid") and lay[f"{side}_mu_eq"]) else 0
         f[side] = (root, cw, leaf, mu, mu_eq)
     return f
 
@@ -136,6 +141,11 @@ def test_gate_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
                 L = lay["lo_levels"]
                 assert g["lo"][0] == rb["lo_root"] and g["lo"][1] == rb["lo_cw"][: 16 * L]
                 assert g["lo"][2] == rb["lo_leaf"] and g["lo"][3] == rb["lo_mu"]
+            if "mid" in g:
+                L = lay["mid_levels"]
+                assert g["mid"][0] == rb["mid_root"] and g["mid"][1] == rb["mid_cw"][: 16 * L]
+                assert g["mid"][2] == rb["mid_leaf"] and g["mid"][3] == rb["mid_mu"]
+                assert g["mid"][4] == rb["mid_mu_eq"]
         for wi in range(nw):
             assert int(w0[wi * n + e]) == k0.w[wi] and int(w1[wi * n + e]) == k1.w[wi]
         b0 = F.gate_round1(kind, bw, S, int(out["xh"][e]), k0)
@@ -146,6 +156,9 @@ def test_gate_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
                 assert (int(out["bits"][p, "hi"][e // 32]) >> (e % 32)) & 1 == bb & 1
             if kind in F.SPLIT_KINDS:
                 assert (int(out["bits"][p, "hi"][words + e // 32]) >> (e % 32)) & 1 == (bb >> 2) & 1
+            if kind in F.SPLIT3_KINDS:
+                assert (int(out["bits"][p, "hi"][2 * words + e // 32]) >> (e % 32)) & 1 == (bb >> 3) & 1
+                assert (int(out["bits"][p, "hi"][3 * words + e // 32]) >> (e % 32)) & 1 == (bb >> 4) & 1
             if kind != F.GATE_RELU:
                 assert (int(out["bits"][p, "lo"][e // 32]) >> (e % 32)) & 1 == (bb >> 1) & 1
         o = b0 ^ b1

@@ -44,7 +44,7 @@ def test_dcfeq_compares_and_equals(d):
 
 
 @pytest.mark.parametrize("bw", [32, 64])
-@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4, 5, 6])
+@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4, 5, 6, 7, 8])
 def test_gate_functionality(bw, kind):
     M = (1 << bw) - 1
     rng = np.random.default_rng(bw + kind)
@@ -58,13 +58,17 @@ def test_gate_functionality(bw, kind):
             x = [0, 1, M, 1 << (bw - 1), (1 << (bw - 1)) - 1, (1 << 12) - 1, M - 4095][i % 7]
         if i % 4 == 3:  # x_hat agrees with r on carry bits 5..11: the split LRS equality branch
             x = ((r & ~31) + int(rng.integers(0, 32)) - r + (int(rng.integers(0, 1 << 20)) << 12)) & M
+        if i % 8 == 5:  # x_hat agrees with r on bits 18..30 (three-part split: U1 equal, U2/V decide)
+            x = ((r & ~((1 << 18) - 1)) + int(rng.integers(0, 1 << 18)) - r) & M
+            x ^= int(rng.integers(0, 2)) << (bw - 1)
         if kind in (3, 6):
             x &= M >> 1
         k0, k1, ry = F.gate_keygen(kind, bw, 12, 3, 1, i, r)
         y = (F.gate_eval_pair(kind, bw, 12, (x + r) & M, k0, k1) - ry) & M
         xa = np.array([x], dtype=np.uint64)
         lrs = R.red(R.signed(xa) >> 12)
-        want = [R.relu(xa), R.relu_ars(xa, 12), R.ars(xa, 12), lrs, R.relu(xa), R.relu_ars(xa, 12), lrs][kind]
+        want = [R.relu(xa), R.relu_ars(xa, 12), R.ars(xa, 12), lrs, R.relu(xa), R.relu_ars(xa, 12), lrs,
+                R.relu(xa), R.relu_ars(xa, 12)][kind]
         assert y == int(want[0])
 
 
