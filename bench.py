@@ -38,10 +38,18 @@ import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
-# stdout carries exactly one JSON line: NCCL's own log lines (its version
-# banner included) go to stderr
-os.environ.setdefault("NCCL_DEBUG", "WARN")
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+# stdout carries exactly one JSON line.  Everything else that a library may
+# write to file descriptor 1 (NCCL prints its version banner there) goes to
+# stderr: fd 1 is pointed at stderr and the JSON line is written to a
+# duplicate of the original stdout.
+_JSON_OUT = os.fdopen(os.dup(1), "w", buffering=1)
+os.dup2(2, 1)
+sys.stdout = sys.stderr
+
+
+def emit(line: dict):
+    _JSON_OUT.write(json.dumps(line) + "\n")
+    _JSON_OUT.flush()
 
 NMAX, FEAT, POOL, PROT = 138, 94, 376, 128
 RELUS_PER_SAMPLE = 171_076           # 138*(188+282+376) + 376*137 + 2816
@@ -240,7 +248,7 @@ def run_reference(a, rank, world):
             "scaling": "weak", "vs_baseline": None, "dtype": f"u{a.bw}", "data": "synthetic",
             "config": config_of(a, world), "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ------------------------------------------------------------------ our arm
@@ -488,7 +496,7 @@ def main():
                          # emulated LAN, full duplex: each party's bytes at 1 Gbps + one 1 ms RTT per opening
                          "lan_1gbps_1ms_rtt_s_per_step": stats["bytes_sent"] * 8 / 1e9 + stats["rounds"] * 1e-3},
                 "key_bytes_per_party_per_step": kb, "stream": stream_info}
-        print(json.dumps(line), flush=True)
+        emit(line)
     for ks in streams:
         ks.close()
     for p in parties:
