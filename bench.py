@@ -38,18 +38,24 @@ import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
-# stdout carries exactly one JSON line.  Everything else that a library may
-# write to file descriptor 1 (NCCL prints its version banner there) goes to
-# stderr: fd 1 is pointed at stderr and the JSON line is written to a
-# duplicate of the original stdout.
-_JSON_OUT = os.fdopen(os.dup(1), "w", buffering=1)
-os.dup2(2, 1)
-sys.stdout = sys.stderr
+_JSON_OUT = None
+
+
+def stdout_for_json_only():
+    """stdout carries exactly one JSON line.  Everything else that a library
+    may write to file descriptor 1 (NCCL prints its version banner there) goes
+    to stderr: fd 1 is pointed at stderr and the JSON line is written to a
+    duplicate of the original stdout."""
+    global _JSON_OUT
+    _JSON_OUT = os.fdopen(os.dup(1), "w", buffering=1)
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
 
 
 def emit(line: dict):
-    _JSON_OUT.write(json.dumps(line) + "\n")
-    _JSON_OUT.flush()
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 NMAX, FEAT, POOL, PROT = 138, 94, 376, 128
 RELUS_PER_SAMPLE = 171_076           # 138*(188+282+376) + 376*137 + 2816
@@ -153,47 +159,70 @@ def config_of(a, n_gpus):
 # ------------------------------------------------------------------ clocks
 
 class Clocks:
+    """nvidia-smi samples of the job's GPUs (every 50 ms) with host timestamps,
+    taken by one process (rank 0) for all of them.  The sampler starts before
+    the warm-up steps and has produced a sample before the timed region opens;
+    `window(t0, t1)` keeps the samples taken inside the timed region (the
+    nearest one on each side when the region is shorter than the sampling
+    period) and reports their median SM clock and every active reason."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, index):
-        self.index = index
-        self.p = None
+    def __init__(self, indices):
+        self.indices = {str(i) for i in indices}
+        self.p, self.samples, self.thread = None, [], None
 
     def start(self):
+        import threading
+
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                       "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.p = None
+            return
+
+        def reader():
+            for line in self.p.stdout:
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9 or f[0] not in self.indices:
+                    continue
+                try:
+                    rec = (time.time(), float(f[1]), float(f[2]),
+                           [nm for nm, v in zip(self.NAMES, f[5:9]) if v.lower().startswith("active")])
+                except ValueError:
+                    continue
+                self.samples.append(rec)
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        t = time.time()
+        while not self.samples and time.time() - t < 10 and self.p.poll() is None:
+            time.sleep(0.02)
 
     def stop(self):
-        if not self.p:
-            return None
-        self.p.terminate()
-        try:
-            out, _ = self.p.communicate(timeout=5)
-        except Exception:
-            self.p.kill()
-            out, _ = self.p.communicate()
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in out.splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9 or f[0] != str(self.index):
-                continue
+        if self.p:
+            self.p.terminate()
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+            if self.thread:
+                self.thread.join(timeout=5)
+
+    def window(self, t0, t1):
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        inside = [r for r in self.samples if t0 <= r[0] <= t1]
+        if not inside:  # region shorter than the sampling period: one period of margin on both sides
+            inside = [r for r in self.samples if t0 - 0.06 <= r[0] <= t1 + 0.06]
+        if not inside:
+            return None
+        reasons = sorted({nm for r in inside for nm in r[3]})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": inside[-1][2], "reasons": reasons,
+                "samples": len(inside)}
 
 
 # ------------------------------------------------------------------ CPU baseline
@@ -341,7 +370,9 @@ def main():
             raise SystemExit(f"--batch {B} not divisible by --lanes {lanes}")
         Bl = B // lanes
         inp = synth.Inputs(B, bw, seed=1000 + pair, atoms=atoms_of(bw))
-        uids = [[ddg.nccl_unique_id() for _ in range(lanes)] if rank == 0 else None]
+        # one two-rank NCCL communicator per party pair (and lane): a pair's
+        # openings never involve the other ranks
+        uids = [[[ddg.nccl_unique_id() for _ in range(lanes)] for _ in range(pairs)] if rank == 0 else None]
         dist.broadcast_object_list(uids, src=0)
         parties, keep_keys = [], []
         for lane in range(lanes):
@@ -364,7 +395,7 @@ def main():
                 torch.cuda.empty_cache()
                 P.bind_keys(mine.data_ptr(), kb)
                 keep_keys.append(mine)
-            P.connect_nccl(uids[0][lane], world, rank, peer)
+            P.connect_nccl(uids[0][pair][lane], 2, party, 1 - party)
             P.set_timeout(600_000)
             parties.append(P)
         bufs = [share_buffers(torch, inp, party, device, (lane * Bl, (lane + 1) * Bl)) for lane in range(lanes)]
@@ -387,16 +418,20 @@ def main():
     timing_on = [False]
     stream = torch.cuda.ExternalStream(parties[0].stream, device=device)
 
-    def timed(on_host, k):
+    def timed(on_host, k, wall=None):
         if dist:
             dist.barrier()
         torch.cuda.synchronize(device)
+        if wall is not None:
+            wall[0] = time.time()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(k):
             step(on_host)
         e1.record(stream)
         torch.cuda.synchronize(device)
+        if wall is not None:
+            wall[1] = time.time()
         ms = e0.elapsed_time(e1)
         if dist:
             t = torch.tensor([ms], device=device)
@@ -405,18 +440,21 @@ def main():
             dist.barrier()
         return ms
 
+    clocks = Clocks(range(world) if world > 1 else [local])
+    if rank == 0:
+        clocks.start()
     for _ in range(a.warmup):
         step(False)
     ks_before = [ks.stats() for ks in streams]
     for p in parties:
         p.enable_dcf_timing(True)
     timing_on[0] = True
-    clocks = Clocks(local)
-    clocks.start()
     n0 = ddg.launch_count()
-    ms = timed(False, a.steps)
+    tw = [0.0, 0.0]
+    ms = timed(False, a.steps, tw)
     launches = ddg.launch_count() - n0
-    clk = clocks.stop()
+    clocks.stop()
+    clk = clocks.window(*tw)
     timing_on[0] = False
     stats = parties[0].stats()
     if world > 1:
@@ -507,4 +545,5 @@ def main():
 
 
 if __name__ == "__main__":
+    stdout_for_json_only()
     main()

@@ -2,7 +2,8 @@
 
 Each csrc/*.cu / *.cpp is compiled to _build/<name>.o (rebuilt when it or any
 header in csrc/ or include/ is newer), then linked into ./libddg.so next to
-this file.  NCCL comes from the pip-installed nvidia-nccl package torch ships
+this file, and the command-line drop-in cli/ddg_inference.cpp into
+./ddg_inference against it.  NCCL comes from the pip-installed nvidia-nccl package torch ships
 with, with the system copy as a fallback.
 """
 from __future__ import annotations
@@ -100,7 +101,24 @@ def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> 
         r = subprocess.run(link, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stderr)
+    build_cli(force)
     return LIB
+
+
+def build_cli(force: bool = False) -> str:
+    """The command-line drop-in (cli/ddg_inference.cpp), linked against the
+    in-tree libddg.so with an $ORIGIN run path."""
+    src = os.path.join(HERE, "cli", "ddg_inference.cpp")
+    out = os.path.join(HERE, "ddg_inference")
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= max(os.path.getmtime(src),
+                                                                        os.path.getmtime(LIB), _headers_mtime()):
+        return out
+    cmd = [_nvcc(), "-O2", "-std=c++17", "-I" + os.path.join(REPO, "include"), src, "-o", out,
+           "-L" + HERE, "-lddg", "-Xlinker", "-rpath=$ORIGIN", "-lpthread"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("ddg_inference build failed:\n" + r.stderr)
+    return out
 
 
 if __name__ == "__main__":

@@ -56,6 +56,10 @@ struct DcfTiming {
     int nrec = 0;
     bool enabled = false;
 };
+// keep freed stream-ordered allocations of the device's default memory pool
+// cached (release threshold = infinity), once per device (forward.cu)
+int keep_pool_memory(int device);
+
 DcfTiming *dcf_timing_sink();
 void set_dcf_timing_sink(DcfTiming *t);
 

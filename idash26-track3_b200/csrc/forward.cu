@@ -112,15 +112,15 @@ int Party::ensure_input(int which, uint64_t bytes)
     return DDG_OK;
 }
 
-static int keep_pool_memory(int device)
+int keep_pool_memory(int device)
 {
-    static bool done[64] = {};
-    if (device < 64 && done[device]) return DDG_OK;
+    static std::atomic<bool> done[64] = {};
+    if (device >= 0 && device < 64 && done[device].load()) return DDG_OK;
     cudaMemPool_t pool;
     DDG_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
     uint64_t thr = ~uint64_t(0);
     DDG_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
-    if (device < 64) done[device] = true;
+    if (device >= 0 && device < 64) done[device].store(true);
     return DDG_OK;
 }
 

@@ -269,10 +269,12 @@ int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, con
 
 /* Ring GEMM engine of ddg_matmul_share / ddg_fc_share and the forward.
  * path 0 (default): tcgen05 tensor cores, 8-bit limb products with int32
- * accumulation recombined modulo 2^bw, operand B MN-major in shared memory,
- * 128 x 64 output tiles; 1: CUDA cores (integer multiply-add); 2: tensor
+ * accumulation recombined modulo 2^bw; at bw 32 with even row strides and
+ * 8-byte aligned operands (and no Beaver operand rewrite) the kernel with
+ * asynchronous (cp.async) operand staging and 128 x 128 tiles, otherwise
+ * operand B MN-major in shared memory with 128 x 64 tiles (128 x 32 at bw 64); 1: CUDA cores (integer multiply-add); 2: tensor
  * cores with B K-major; 3: tensor cores with 128 x 128 (bw 32) or 128 x 32
- * (bw 64) tiles.  Reduction lengths beyond the limb sums' exactness bound
+ * (bw 64) tiles; 4: tensor cores, 128 x 64 tiles, synchronous staging.  Reduction lengths beyond the limb sums' exactness bound
  * (K > 8192 at bw 32, K > 4096 at bw 64, counting both Beaver products) always
  * use the CUDA cores.  Process-wide setting.
  * ddg_gemm_status: DDG_OK, or DDG_ERR_CUDA when a tensor-core GEMM gave up on

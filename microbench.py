@@ -18,7 +18,8 @@ Prints one JSON object.  Everything goes through libddg.so's C ABI on cuda:0:
 * lut  -- 2^20 DPF look-ups into the 139-entry 2^12/sqrt(k) table.
 * gemm -- the GCN layer-3 ring GEMMs at B samples: the FC (B*138 x 282) .
   (282 x 376) and the per-sample Beaver product (138 x 138) . (138 x 282),
-  on the tensor cores (tcgen05 kind::i8 limb products) and on the CUDA cores.
+  on the tensor cores (tcgen05 kind::i8 limb products; default and wide
+  column tiles) and on the CUDA cores.
 * aes  -- the fixed-key AES ceiling of both AES engines.
 
 Timing: CUDA events on the launching stream after warm-up launches; the
@@ -167,7 +168,8 @@ def run_gemm(ddg, torch, a):
         # Beaver: per sample (138 x 138) . (138 x 282), both products
         Ah, Hh, mA, mH, Z, s = rnd(B, 138, 138), rnd(B, 138, 282), rnd(B, 138, 138), rnd(B, 138, 282), \
             rnd(B, 138, 282), rnd(B, 138, 282)
-        for path, pname in ((ddg.GEMM_TENSOR, "tensor"), (ddg.GEMM_CUDA_CORES, "cuda_cores")):
+        for path, pname in ((ddg.GEMM_TENSOR, "tensor"), (ddg.GEMM_TENSOR_WIDE, "tensor_wide"),
+                            (ddg.GEMM_CUDA_CORES, "cuda_cores")):
             ddg.gemm_path(path)
             t = timeit(torch, lambda: ddg.check(L.ddg_fc_share(bw, 0, M, K, N, x.data_ptr(), W.data_ptr(),
                                                                b2s.data_ptr(), c.data_ptr(), out.data_ptr(), st)))

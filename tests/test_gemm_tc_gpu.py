@@ -14,7 +14,7 @@ import pytest
 
 from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 
-PATHS = [0, 2, 3, 1]
+PATHS = [0, 4, 2, 3, 1]
 
 
 def rnd(rng, bw, shape):
@@ -102,7 +102,7 @@ def test_fc_paths(engine, cuda, path, bw, shape):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("path", [0, 2, 3])
+@pytest.mark.parametrize("path", [0, 4, 2, 3])
 @pytest.mark.parametrize("bw,K", [(32, 4096), (64, 2048)])
 def test_limb_sums_at_the_exactness_bound(engine, cuda, path, bw, K):
     """Party 0's Beaver share with every byte of both concatenated operands at

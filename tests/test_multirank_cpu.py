@@ -1,7 +1,7 @@
 """Host-side logic of the multi-GPU path on CPU ranks (gloo, world size 2).
 
 Covers what bench.py's torchrun path does outside the library: the party
-layout (pair i = ranks (i, k+i)), broadcasting the per-lane NCCL unique ids,
+layout (pair i = ranks (i, k+i)), broadcasting the per-pair NCCL unique ids,
 the max-over-ranks reduction of the timed region, and failure detection: a
 rank that dies before a collective makes the survivor's collective fail within
 the process-group timeout instead of hanging (the reference has no failure
@@ -36,11 +36,12 @@ def _worker_layout(rank, world, port, q):
 
     _init(rank, world, port)
     pairs, pair, party, peer = bench.roles(rank, world)
-    uids = [[os.urandom(128) for _ in range(2)] if rank == 0 else None]
+    # one id per party pair (and lane), as bench.py broadcasts them
+    uids = [[[os.urandom(128) for _ in range(1)] for _ in range(pairs)] if rank == 0 else None]
     dist.broadcast_object_list(uids, src=0)
     t = torch.tensor([10.0 + rank])
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    q.put((rank, pairs, pair, party, peer, uids[0][0][:8], float(t.item())))
+    q.put((rank, pairs, pair, party, peer, uids[0][pair][0][:8], float(t.item())))
     dist.barrier()
     dist.destroy_process_group()
 
