@@ -423,7 +423,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // bias + Add: the host folds s1, B1m and the Beaver minus sign into B1 / B2
 // beforehand.  128 x 128 output tiles (four 128-column s32 accumulators = all
 // 512 TMEM columns), B MN-major.  Needs even row strides and 8-byte aligned
-// operands (the host checks, and otherwise uses ring_gemm_tc_kernel).
+// operands (the host checks, and otherwise uses ring_gemm_tc_kernel).  The
+// kernel itself also takes a second product (A2 . B2) for callers that
+// prepare its B operand.
 // Raw tiles are stored row-major with the 16-byte chunk index XOR-ed by
 // 4 * (row & 1), which keeps the 16-byte shared loads of the split step free
 // of bank conflicts.
@@ -599,18 +601,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) ring_gemm_tc2_kernel(const __gr
     }
 }
 
-// B1' = sign-free s1*B1 - B1m and B2' = -B2 for the Beaver form (n elements each)
-__global__ void k_beaver_operands(uint64_t n, uint32_t s1, const uint32_t *B1, const uint32_t *B1m, const uint32_t *B2,
-                                  uint32_t *o1, uint32_t *o2)
-{
-    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
-        uint32_t v = B1 ? s1 * B1[i] : 0u;
-        if (B1m) v -= B1m[i];
-        o1[i] = v;
-        if (o2) o2[i] = 0u - B2[i];
-    }
-}
-
 __device__ uint32_t g_tc_err;
 
 // 0: tensor cores (default): for Z_2^32 the asynchronous-staging kernel where
@@ -646,30 +636,18 @@ int launch_tc(const GemmArgs<T> &a, cudaStream_t st)
     return DDG_OK;
 }
 
-// the asynchronous-staging kernel for Z_2^32 when the operands allow it; 1 = launched, 0 = not eligible
+// the asynchronous-staging kernel for Z_2^32 when the operands allow it
+// (*launched = 1), else nothing (*launched = 0).  The Beaver form (B1m, s1,
+// a second product) is left to ring_gemm_tc_kernel, whose loader folds those
+// terms: rewriting the B operands first for this kernel measured slower.
 int launch_tc2(const GemmArgs<uint32_t> &a, cudaStream_t st, int *launched)
 {
     *launched = 0;
-    const bool beaver = a.A2 != nullptr;
-    const bool prepass = beaver || a.B1m || a.s1 != 1u || !a.B1;
-    // the Beaver form would need its B operands rewritten first (an extra pass
-    // over them); measured slower than the synchronous kernel, which folds them
-    // in its loader
-    if (prepass) return DDG_OK;
     auto even = [](int64_t v) { return (v & 1) == 0; };
     auto al8 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; };
-    if (!even(a.lda1) || !even(a.sA1) || !al8(a.A1)) return DDG_OK;
-    if (beaver && (!even(a.lda2) || !even(a.sA2) || !al8(a.A2))) return DDG_OK;
-    const int64_t kn = int64_t(a.K) * a.N;
-    if (prepass) {
-        // the B operands are rewritten contiguously: they must be contiguous per batch entry already
-        if ((a.B1 && (a.ldb1 != a.N || a.sB1 != kn)) || (a.B1m && (a.ldb1 != a.N || a.sB1m != kn)) ||
-            (beaver && (a.ldb2 != a.N || a.sB2 != kn)) || !even(a.N))
-            return DDG_OK;
-    } else if (!even(a.ldb1) || !even(a.sB1) || !al8(a.B1)) {
-        return DDG_OK;
-    }
-    DDG_CHECK(a.A1 && a.C && (!a.A2 || a.B2), DDG_ERR_ARG, "gemm: missing operand");
+    if (a.A2 || a.B1m || a.s1 != 1u || !a.B1) return DDG_OK;
+    if (!even(a.lda1) || !even(a.sA1) || !al8(a.A1) || !even(a.ldb1) || !even(a.sB1) || !al8(a.B1)) return DDG_OK;
+    DDG_CHECK(a.A1 && a.C, DDG_ERR_ARG, "gemm: missing operand");
     static thread_local int configured_dev = -1;
     int dev = 0;
     DDG_CUDA(cudaGetDevice(&dev));
@@ -681,32 +659,16 @@ int launch_tc2(const GemmArgs<uint32_t> &a, cudaStream_t st, int *launched)
     DDG_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_tc_err));
     Gemm2Args g;
     g.M = a.M, g.N = a.N, g.K = a.K;
-    g.nk0 = (a.K + TC_BK - 1) / TC_BK;
-    g.nk1 = beaver ? g.nk0 : 0;
-    g.A1 = a.A1, g.A2 = a.A2, g.lda1 = a.lda1, g.lda2 = a.lda2, g.sA1 = a.sA1, g.sA2 = a.sA2;
-    g.B1 = a.B1, g.B2 = a.B2, g.ldb1 = a.ldb1, g.ldb2 = a.ldb2, g.sB1 = a.sB1, g.sB2 = a.sB2;
+    g.nk0 = (a.K + TC_BK - 1) / TC_BK, g.nk1 = 0;
+    g.A1 = a.A1, g.A2 = nullptr, g.lda1 = a.lda1, g.lda2 = 0, g.sA1 = a.sA1, g.sA2 = 0;
+    g.B1 = a.B1, g.B2 = nullptr, g.ldb1 = a.ldb1, g.ldb2 = 0, g.sB1 = a.sB1, g.sB2 = 0;
     g.sign = a.sign, g.bias = a.bias, g.Add = a.Add, g.ldAdd = a.ldAdd, g.sAdd = a.sAdd;
     g.C = a.C, g.ldc = a.ldc, g.sC = a.sC;
-    uint32_t *tmp = nullptr;
-    const uint64_t n = uint64_t(a.batch) * uint64_t(kn);
-    if (prepass) {
-        DDG_TRY(keep_pool_memory(dev));
-        DDG_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&tmp), (beaver ? 2 : 1) * n * sizeof(uint32_t), st));
-        const uint64_t blocks = (n + 255) / 256;
-        k_beaver_operands<<<unsigned(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(n, a.s1, a.B1, a.B1m,
-                                                                                  beaver ? a.B2 : nullptr, tmp,
-                                                                                  beaver ? tmp + n : nullptr);
-        note_launch();
-        g.B1 = tmp, g.ldb1 = a.N, g.sB1 = kn;
-        if (beaver) g.B2 = tmp + n, g.ldb2 = a.N, g.sB2 = kn;
-    }
     dim3 grid((a.N + TC2_BN - 1) / TC2_BN, (a.M + TC_BM - 1) / TC_BM, a.batch);
     DDG_CHECK(grid.y <= 65535 && grid.z <= 65535, DDG_ERR_ARG, "gemm grid too large (M=%d batch=%d)", a.M, a.batch);
     ring_gemm_tc2_kernel<<<grid, TC_THREADS, TC2_SMEM, st>>>(g, err);
     note_launch();
-    cudaError_t e = cudaGetLastError();
-    if (tmp) cudaFreeAsync(tmp, st);
-    DDG_CHECK(e == cudaSuccess, DDG_ERR_CUDA, "ring_gemm_tc2: %s", cudaGetErrorString(e));
+    DDG_CUDA(cudaGetLastError());
     *launched = 1;
     return DDG_OK;
 }
