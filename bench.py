@@ -9,8 +9,10 @@ in HBM.  A step is one online forward of B samples by both parties.
   N = 1      : both parties on cuda:0 (two host threads, zero-copy openings)
   N = 2,4,8  : torchrun, one party per process; ranks 0..k-1 are party 0,
                ranks k..2k-1 party 1, pair i = (i, k+i) exchanges its openings
-               over NCCL send/recv; every pair runs its own micro-batch (weak
-               scaling, no cross-pair collective on the data path).
+               over CUDA IPC (--comm ipc: send slots read in place over NVLink)
+               or NCCL send/recv (--comm nccl); every pair runs its own
+               micro-batch (weak scaling, no cross-pair collective on the data
+               path).
 
 value    : samples/s of the whole job, inputs (shares) and keys already in HBM.
 e2e      : the same through the C ABI with host (pinned) share buffers: every
@@ -35,6 +37,7 @@ import statistics
 import subprocess
 import sys
 import time
+import uuid
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
@@ -82,6 +85,9 @@ def parse():
                     help="N>1: batch lanes per rank, each with its own NCCL communicator and host thread.  Only 1 "
                          "is accepted: two lanes (two communicators used concurrently from two threads per GPU) "
                          "stalled for 900 s on the first 2-GPU run, cause not established")
+    ap.add_argument("--comm", default="ipc", choices=["ipc", "nccl"],
+                    help="N>1: openings between the two parties of a pair over CUDA IPC (default; both ranks on one "
+                         "node) or NCCL send/recv")
     ap.add_argument("--aes-tables", type=int, default=4, choices=[2, 4],
                     help="AES engine: 4 staged round tables (default) or 2 tables + rotation")
     ap.add_argument("--relu-split", type=int, default=0, choices=[0, 2, 3],
@@ -129,6 +135,13 @@ def atoms_of(bw):
     return (10, 60) if bw == 32 else (10, 100)
 
 
+def parallelism(a, n_gpus):
+    if n_gpus == 1:
+        return "1 GPU, both parties"
+    over = "CUDA IPC (peer slots read over NVLink)" if a.comm == "ipc" else "NCCL send/recv"
+    return f"{n_gpus // 2} party pairs over {over}, one party per GPU"
+
+
 def config_of(a, n_gpus):
     pairs = max(n_gpus // 2, 1)
     if a.stream:
@@ -138,7 +151,7 @@ def config_of(a, n_gpus):
                         f"{a.stream} pinned chunks per party (timing-only key reuse)",
             "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs, "stream_chunks": a.stream,
             "relu_split": a.relu_split,
-            "parallelism": "1 GPU, both parties" if n_gpus == 1 else f"{pairs} party pairs over NCCL, one party per GPU",
+            "parallelism": parallelism(a, n_gpus),
             "l2": "inputs larger than L2: every step copies and streams a full key chunk per party"}
     return {
         "workload": f"full affinity branch (adj-norm, GCNx3, masked max-pool, FC head), bw={a.bw}, scale={a.scale}, "
@@ -146,8 +159,7 @@ def config_of(a, n_gpus):
                     f"U{list(atoms_of(a.bw))}) per pair, keys resident in HBM "
                     f"(BASELINE configs[{2 if a.bw == 32 else 3}])",
         "bw": a.bw, "scale": a.scale, "batch_per_pair": a.batch, "pairs": pairs,
-        "parallelism": "1 GPU, both parties" if n_gpus == 1 else
-        f"{pairs} party pairs over NCCL, one party per GPU",
+        "parallelism": parallelism(a, n_gpus),
         "truncation": "exact (floor) at every site",
         "gemm": "tcgen05 kind::i8 limb products" if a.gemm == "tensor" else "CUDA-core integer multiply-add",
         "aes": f"T-table AES, {a.aes_tables} round tables staged in shared memory",
@@ -370,9 +382,13 @@ def main():
             raise SystemExit(f"--batch {B} not divisible by --lanes {lanes}")
         Bl = B // lanes
         inp = synth.Inputs(B, bw, seed=1000 + pair, atoms=atoms_of(bw))
-        # one two-rank NCCL communicator per party pair (and lane): a pair's
-        # openings never involve the other ranks
-        uids = [[[ddg.nccl_unique_id() for _ in range(lanes)] for _ in range(pairs)] if rank == 0 else None]
+        # one channel per party pair (and lane): a pair's openings never
+        # involve the other ranks
+        if a.comm == "ipc":
+            tag = uuid.uuid4().hex[:16]
+            uids = [[[f"ddg_{tag}_{i}_{l}" for l in range(lanes)] for i in range(pairs)] if rank == 0 else None]
+        else:
+            uids = [[[ddg.nccl_unique_id() for _ in range(lanes)] for _ in range(pairs)] if rank == 0 else None]
         dist.broadcast_object_list(uids, src=0)
         parties, keep_keys = [], []
         for lane in range(lanes):
@@ -395,8 +411,11 @@ def main():
                 torch.cuda.empty_cache()
                 P.bind_keys(mine.data_ptr(), kb)
                 keep_keys.append(mine)
-            P.connect_nccl(uids[0][pair][lane], 2, party, 1 - party)
             P.set_timeout(600_000)
+            if a.comm == "ipc":
+                P.connect_ipc(uids[0][pair][lane], ddg.forward_max_exchange_bytes(bw, s, Bl))
+            else:
+                P.connect_nccl(uids[0][pair][lane], 2, party, 1 - party)
             parties.append(P)
         bufs = [share_buffers(torch, inp, party, device, (lane * Bl, (lane + 1) * Bl)) for lane in range(lanes)]
 

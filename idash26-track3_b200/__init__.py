@@ -68,6 +68,8 @@ SIGNATURES = {
     "ddg_nccl_unique_id": (_i32, [_vp]),
     "ddg_party_connect_nccl": (_i32, [_vp, _vp, _i32, _i32, _i32]),
     "ddg_party_set_timeout": (_i32, [_vp, _i32]),
+    "ddg_party_connect_ipc": (_i32, [_vp, ctypes.c_char_p, _u64]),
+    "ddg_forward_max_exchange_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_forward_key_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_forward_eval": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
@@ -212,6 +214,10 @@ class Party:
         buf = ctypes.create_string_buffer(bytes(unique_id), 128)
         check(lib().ddg_party_connect_nccl(self.h, buf, nranks, rank, peer_rank))
 
+    def connect_ipc(self, name: str, slot_bytes: int):
+        """Two party processes on one node: openings through CUDA IPC (see ddg_party_connect_ipc)."""
+        check(lib().ddg_party_connect_ipc(self.h, name.encode(), slot_bytes))
+
     def set_timeout(self, ms: int):
         check(lib().ddg_party_set_timeout(self.h, ms))
 
@@ -249,6 +255,10 @@ def forward_pair(p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
     aff = np.zeros(batch, dtype=np.float64)
     check(lib().ddg_forward_eval_pair(p0.h, p1.h, batch, a0, a1, int(on_host), raw.ctypes.data, aff.ctypes.data))
     return raw, aff
+
+
+def forward_max_exchange_bytes(bw: int, scale: int, batch: int) -> int:
+    return int(lib().ddg_forward_max_exchange_bytes(bw, scale, batch))
 
 
 def launch_count() -> int:

@@ -1,4 +1,5 @@
 // extern "C" entry points of libddg.so (declared in include/ddg_fss.h).
+#include <cstring>
 #include <string>
 #include <thread>
 #include <vector>
@@ -205,15 +206,36 @@ int ddg_party_connect_nccl(ddg_party *h, const void *id128, int nranks, int rank
     int st = DDG_OK;
     Channel *c = make_nccl_channel(id128, nranks, rank, peer_rank, h->P.device, &st);
     DDG_TRY(st);
+    c->timeout_ms = h->P.timeout_ms;
     if (h->P.owns_chan) delete h->P.chan;
     h->P.chan = c, h->P.owns_chan = true;
     return DDG_OK;
 }
 
+int ddg_party_connect_ipc(ddg_party *h, const char *name, uint64_t slot_bytes)
+{
+    DDG_CHECK(h && name && *name && slot_bytes, DDG_ERR_ARG, "bad argument");
+    DDG_CHECK(std::strlen(name) < 200 && !std::strchr(name, '/'), DDG_ERR_ARG, "bad shared-memory name");
+    int st = DDG_OK;
+    Channel *c = make_ipc_channel(name, h->P.party, h->P.device, slot_bytes, h->P.timeout_ms, &st);
+    DDG_TRY(st);
+    if (h->P.owns_chan) delete h->P.chan;
+    h->P.chan = c, h->P.owns_chan = true;
+    return DDG_OK;
+}
+
+uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch)
+{
+    if (check_gate_args(0, bw, scale) != DDG_OK || batch <= 0) return 0;
+    // the widest opening of the graph: a (batch, 138, 376) ring tensor
+    return uint64_t(batch) * NMAX * POOL * uint64_t(bw / 8);
+}
+
 int ddg_party_set_timeout(ddg_party *h, int timeout_ms)
 {
-    DDG_CHECK(h && h->P.chan && timeout_ms > 0, DDG_ERR_ARG, "bad timeout or no channel");
-    h->P.chan->timeout_ms = timeout_ms;
+    DDG_CHECK(h && timeout_ms > 0, DDG_ERR_ARG, "bad timeout");
+    h->P.timeout_ms = timeout_ms;
+    if (h->P.chan) h->P.chan->timeout_ms = timeout_ms;
     return DDG_OK;
 }
 

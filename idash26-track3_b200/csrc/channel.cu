@@ -1,5 +1,13 @@
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <atomic>
 #include <chrono>
 #include <cstring>
+#include <string>
+#include <thread>
 
 #include "channel.cuh"
 
@@ -78,6 +86,237 @@ int LocalPairChannel::barrier(int party, cudaStream_t st)
     DDG_TRY(exchange(party, st, nullptr, 0, nullptr, &dummy));
     rounds[party] -= 1;
     return DDG_OK;
+}
+
+// ------------------------------------------------------------------ IPC channel
+//
+// Two party processes on one node, one GPU each.  Every party owns S = 4
+// send slots of `slot_bytes` in one cudaMalloc'd arena, exported with
+// cudaIpcGetMemHandle, and two interprocess events per slot: "posted" (its
+// share of generation g sits in slot g % S) and "read" (it has finished
+// reading the peer's slot g % S).  A POSIX shared-memory block carries the
+// handles and, per party, the last generation posted and the last one read.
+// Exchange g of party p:
+//   1. the read of generation g - 1 is complete on p's stream: record read[(g-1)%S], publish read = g - 1;
+//   2. slot g % S is free once the peer has read generation g - S: wait (host,
+//      bounded) for its read >= g - S, then make the stream wait on its read[g%S];
+//   3. copy the share into the slot, record posted[g%S], publish posted = g;
+//   4. wait (host, bounded) for the peer's posted >= g, make the stream wait on
+//      its posted[g%S]; the peer's share is then read in place over NVLink.
+// An event is re-recorded only after the host has seen the generation it
+// guards consumed, so every stream wait binds to the right record.  Host
+// waits give up after timeout_ms with DDG_ERR_PEER and mark the block failed,
+// which the peer then also reports.  Teardown: each party's stream is idle
+// before its channel is destroyed; the arena is freed only once the peer has
+// said (or timed out saying) that it is closing too, so no kernel of the peer
+// can still be reading it.
+
+struct IpcShared {
+    std::atomic<uint32_t> ready[2], closing[2];
+    std::atomic<uint32_t> failed;
+    std::atomic<uint64_t> posted[2], read[2];
+    uint64_t slot_bytes;
+    cudaIpcMemHandle_t arena[2];
+    cudaIpcEventHandle_t ev_posted[2][4], ev_read[2][4];
+};
+
+struct IpcChannel : Channel {
+    static constexpr int S = 4;
+    int party = 0, device = 0;
+    uint64_t slot_bytes = 0, gen = 0;
+    std::string shm_name;
+    IpcShared *sh = nullptr;
+    uint8_t *arena = nullptr, *peer_arena = nullptr;
+    cudaEvent_t posted[S] = {}, read[S] = {}, peer_posted[S] = {}, peer_read[S] = {};
+
+    ~IpcChannel() override
+    {
+        cudaSetDevice(device);
+        if (sh && sh->ready[party].load()) {
+            sh->closing[party].store(1, std::memory_order_release);
+            const auto t0 = std::chrono::steady_clock::now();
+            while (sh->ready[1 - party].load() && !sh->closing[1 - party].load(std::memory_order_acquire) &&
+                   !sh->failed.load() &&
+                   std::chrono::steady_clock::now() - t0 < std::chrono::milliseconds(timeout_ms))
+                std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        }
+        if (peer_arena) cudaIpcCloseMemHandle(peer_arena);
+        for (int i = 0; i < S; i++) {
+            for (cudaEvent_t e : {posted[i], read[i], peer_posted[i], peer_read[i]})
+                if (e) cudaEventDestroy(e);
+        }
+        if (arena) cudaFree(arena);
+        if (sh) munmap(sh, sizeof(IpcShared));
+        if (party == 0 && !shm_name.empty()) shm_unlink(shm_name.c_str());
+    }
+
+    int wait_for(std::atomic<uint64_t> &v, uint64_t target, const char *what)
+    {
+        const auto t0 = std::chrono::steady_clock::now();
+        for (uint64_t it = 0; v.load(std::memory_order_acquire) < target; it++) {
+            if (sh->failed.load()) {
+                set_last_error("peer party failed (IPC channel)");
+                return DDG_ERR_PEER;
+            }
+            if ((it & 1023) == 0 && std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+                sh->failed.store(1);
+                set_last_error("peer party did not reach %s %llu within %d ms", what, (unsigned long long)target,
+                               timeout_ms);
+                return DDG_ERR_PEER;
+            }
+            if (it > 4096) std::this_thread::yield();
+        }
+        return DDG_OK;
+    }
+
+    int finish_read(cudaStream_t st)
+    {
+        if (gen == 0) return DDG_OK;
+        DDG_CUDA(cudaEventRecord(read[(gen - 1) % S], st));
+        sh->read[party].store(gen, std::memory_order_release);
+        return DDG_OK;
+    }
+
+    int exchange(int p, cudaStream_t st, const void *send, uint64_t bytes, void *recv, const void **peer) override
+    {
+        (void)recv;
+        const int q = 1 - p;
+        DDG_CHECK(bytes <= slot_bytes, DDG_ERR_ARG, "IPC exchange of %llu bytes exceeds the %llu-byte slots",
+                  (unsigned long long)bytes, (unsigned long long)slot_bytes);
+        DDG_TRY(finish_read(st));  // generation gen (the previous exchange) has been read by work queued on st
+        const uint64_t g = ++gen;
+        const int s = int((g - 1) % S);
+        if (g > uint64_t(S)) {
+            DDG_TRY(wait_for(sh->read[q], g - S, "read of generation"));
+            DDG_CUDA(cudaStreamWaitEvent(st, peer_read[s], 0));
+        }
+        uint8_t *slot = arena + uint64_t(s) * slot_bytes;
+        if (bytes) DDG_CUDA(cudaMemcpyAsync(slot, send, bytes, cudaMemcpyDeviceToDevice, st));
+        DDG_CUDA(cudaEventRecord(posted[s], st));
+        sh->posted[p].store(g, std::memory_order_release);
+        DDG_TRY(wait_for(sh->posted[q], g, "posting of generation"));
+        DDG_CUDA(cudaStreamWaitEvent(st, peer_posted[s], 0));
+        *peer = peer_arena + uint64_t(s) * slot_bytes;
+        bytes_sent[p] += bytes;
+        rounds[p] += 1;
+        return DDG_OK;
+    }
+
+    bool needs_recv_buffer() const override { return false; }  // the peer's slot is read in place
+
+    int barrier(int p, cudaStream_t st) override
+    {
+        // an empty exchange: both parties posted everything before it, and the
+        // reads of the last real exchange are published
+        const void *dummy = nullptr;
+        DDG_TRY(exchange(p, st, nullptr, 0, nullptr, &dummy));
+        rounds[p] -= 1;
+        return DDG_OK;
+    }
+};
+
+Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot_bytes, int timeout_ms, int *status)
+{
+    *status = DDG_ERR_PEER;
+    auto fail = [&](int code, const char *fmt, const char *a) {
+        set_last_error(fmt, a);
+        *status = code;
+        return static_cast<Channel *>(nullptr);
+    };
+    if (cudaSetDevice(device) != cudaSuccess) return fail(DDG_ERR_CUDA, "cudaSetDevice failed%s", "");
+    auto *c = new IpcChannel();
+    c->party = party, c->device = device, c->slot_bytes = (slot_bytes + 255) & ~uint64_t(255);
+    c->timeout_ms = timeout_ms;
+    c->shm_name = std::string("/") + name;
+    // party 0 creates and sizes the block, party 1 opens it once it exists
+    int fd = -1;
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        fd = party == 0 ? shm_open(c->shm_name.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600)
+                        : shm_open(c->shm_name.c_str(), O_RDWR, 0600);
+        if (fd >= 0) {
+            struct stat stt;
+            if (party == 0) {
+                if (ftruncate(fd, sizeof(IpcShared)) != 0) {
+                    close(fd);
+                    delete c;
+                    return fail(DDG_ERR_PEER, "cannot size the shared block %s", name);
+                }
+                break;
+            }
+            if (fstat(fd, &stt) == 0 && uint64_t(stt.st_size) >= sizeof(IpcShared)) break;
+            close(fd);
+            fd = -1;
+        } else if (party == 0) {
+            delete c;
+            return fail(DDG_ERR_PEER, "cannot create the shared block %s (name in use?)", name);
+        }
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+            delete c;
+            return fail(DDG_ERR_PEER, "party 0 never created the shared block %s", name);
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(2));
+    }
+    void *m = mmap(nullptr, sizeof(IpcShared), PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    close(fd);
+    if (m == MAP_FAILED) {
+        delete c;
+        return fail(DDG_ERR_PEER, "cannot map the shared block %s", name);
+    }
+    c->sh = static_cast<IpcShared *>(m);
+    IpcShared *sh = c->sh;
+    // own arena and events, published in the block
+    const int S = IpcChannel::S;
+    if (cudaMalloc(&c->arena, uint64_t(S) * c->slot_bytes) != cudaSuccess ||
+        cudaIpcGetMemHandle(&sh->arena[party], c->arena) != cudaSuccess) {
+        c->sh->failed.store(1);  // the peer stops waiting on us
+        delete c;
+        return fail(DDG_ERR_CUDA, "IPC arena allocation / export failed%s", "");
+    }
+    for (int i = 0; i < S; i++) {
+        if (cudaEventCreateWithFlags(&c->posted[i], cudaEventDisableTiming | cudaEventInterprocess) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->read[i], cudaEventDisableTiming | cudaEventInterprocess) != cudaSuccess ||
+            cudaIpcGetEventHandle(&sh->ev_posted[party][i], c->posted[i]) != cudaSuccess ||
+            cudaIpcGetEventHandle(&sh->ev_read[party][i], c->read[i]) != cudaSuccess) {
+            c->sh->failed.store(1);  // the peer stops waiting on us
+            delete c;
+            return fail(DDG_ERR_CUDA, "IPC event creation / export failed%s", "");
+        }
+    }
+    if (party == 0) sh->slot_bytes = c->slot_bytes;
+    sh->ready[party].store(1, std::memory_order_release);
+    const auto t1 = std::chrono::steady_clock::now();
+    while (!sh->ready[1 - party].load(std::memory_order_acquire)) {
+        if (sh->failed.load() || std::chrono::steady_clock::now() - t1 > std::chrono::milliseconds(timeout_ms)) {
+            c->sh->failed.store(1);  // the peer stops waiting on us
+            delete c;
+            return fail(DDG_ERR_PEER, "the peer party never joined the shared block %s", name);
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (sh->slot_bytes != c->slot_bytes) {
+        c->sh->failed.store(1);  // the peer stops waiting on us
+        delete c;
+        return fail(DDG_ERR_ARG, "the two parties asked for different IPC slot sizes%s", "");
+    }
+    const int q = 1 - party;
+    void *pa = nullptr;
+    if (cudaIpcOpenMemHandle(&pa, sh->arena[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        c->sh->failed.store(1);  // the peer stops waiting on us
+        delete c;
+        return fail(DDG_ERR_CUDA, "cannot map the peer's IPC arena (are both GPUs on this node?)%s", "");
+    }
+    c->peer_arena = static_cast<uint8_t *>(pa);
+    for (int i = 0; i < S; i++) {
+        if (cudaIpcOpenEventHandle(&c->peer_posted[i], sh->ev_posted[q][i]) != cudaSuccess ||
+            cudaIpcOpenEventHandle(&c->peer_read[i], sh->ev_read[q][i]) != cudaSuccess) {
+            c->sh->failed.store(1);  // the peer stops waiting on us
+            delete c;
+            return fail(DDG_ERR_CUDA, "cannot open the peer's IPC events%s", "");
+        }
+    }
+    *status = DDG_OK;
+    return c;
 }
 
 #ifdef DDG_HAVE_NCCL

@@ -7,6 +7,9 @@
 //     the peer's event.  Different devices: cudaMemcpyPeerAsync over NVLink.
 //   NcclChannel: one party per process, grouped ncclSend/ncclRecv with the
 //     paired rank on the party's stream.
+//   IpcChannel: one party per process, both on one node: CUDA-IPC send slots
+//     read in place over NVLink, ordered by interprocess events and a shared-
+//     memory block of generation counters.
 #pragma once
 #include <condition_variable>
 #include <cstdint>
@@ -28,6 +31,8 @@ struct Channel {
     // for all work the peer queued before it
     virtual int barrier(int party, cudaStream_t st) = 0;
     virtual bool same_device() const { return false; }
+    // exchange() needs the caller's `recv` buffer (it copies the peer's bytes there)
+    virtual bool needs_recv_buffer() const { return !same_device(); }
     uint64_t bytes_sent[2] = {0, 0};
     uint64_t rounds[2] = {0, 0};
     int timeout_ms = 60000;
@@ -55,6 +60,9 @@ struct LocalPairChannel : Channel {
 };
 
 Channel *make_nccl_channel(const void *unique_id, int nranks, int rank, int peer_rank, int device, int *status);
+// CUDA-IPC channel between two party processes on one node (channel.cu); both
+// call it with the same `name` (a POSIX shared-memory name, no slash)
+Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot_bytes, int timeout_ms, int *status);
 int nccl_unique_id(void *out128);
 
 }  // namespace ddg

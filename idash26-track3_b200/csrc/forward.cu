@@ -397,7 +397,7 @@ struct EvalExec : ExecBase<T> {
     const T *peer_of(const void *send, uint64_t bytes)
     {
         if (this->err != DDG_OK) return nullptr;
-        void *recv = P->chan->same_device() ? nullptr : this->alloc_bytes(bytes);
+        void *recv = P->chan->needs_recv_buffer() ? this->alloc_bytes(bytes) : nullptr;
         const void *peer = nullptr;
         ok(P->chan->exchange(p, this->st, send, bytes, recv, &peer));
         return static_cast<const T *>(peer);

@@ -49,6 +49,7 @@ struct Party {
     cudaStream_t stream = nullptr;
     Channel *chan = nullptr;
     bool owns_chan = false;
+    int timeout_ms = 60000;  // bound on every wait for the peer (applied to the channel)
     const uint8_t *keys = nullptr;
     uint64_t key_bytes = 0;
     DevWeights w;

@@ -160,6 +160,17 @@ int ddg_pair_local(ddg_party *p0, ddg_party *p1);
  * NCCL unique id (ddg_nccl_unique_id on one rank, broadcast by the caller) */
 int ddg_nccl_unique_id(void *out128);
 int ddg_party_connect_nccl(ddg_party *party, const void *unique_id128, int nranks, int rank, int peer_rank);
+/* The two parties as two processes on one node (one GPU each): openings go
+ * through CUDA IPC.  Each party exports four send slots of slot_bytes (at
+ * least ddg_forward_max_exchange_bytes) and interprocess events; a POSIX
+ * shared-memory block `name` (no slash, the same for both parties, unused on
+ * the node; party 0 creates and removes it) carries the handles and the
+ * generation counters.  A party reads the peer's slot in place over NVLink.
+ * Waits on the peer are bounded by the party's timeout (ddg_party_set_timeout
+ * before connecting, default 60 s) and end in DDG_ERR_PEER. */
+int ddg_party_connect_ipc(ddg_party *party, const char *name, uint64_t slot_bytes);
+/* the largest single opening of one forward of `batch` samples, in bytes */
+uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch);
 /* give up (DDG_ERR_PEER) when the peer does not reach an opening in time */
 int ddg_party_set_timeout(ddg_party *party, int timeout_ms);
 

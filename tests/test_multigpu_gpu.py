@@ -1,4 +1,4 @@
-"""Openings over NCCL between two processes on two GPUs (skipped with fewer GPUs)."""
+"""Openings over NCCL and over CUDA IPC between two processes on two GPUs (skipped with fewer GPUs)."""
 import os
 import subprocess
 import sys
@@ -9,13 +9,14 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("comm", ["nccl", "ipc"])
 @pytest.mark.parametrize("bw", ["32", "64"])
-def test_nccl_pair_forward_bit_exact(cuda, bw):
+def test_pair_forward_bit_exact(cuda, bw, comm):
     if cuda.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    env = dict(os.environ, DDG_CHECK_BW=bw, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, DDG_CHECK_BW=bw, DDG_CHECK_COMM=comm, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
                         "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29531",
-                        os.path.join(REPO, "tests", "nccl_pair_check.py")], env=env, capture_output=True, text=True)
+                        os.path.join(REPO, "tests", "pair_check.py")], env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "nccl pair OK" in r.stdout
+    assert f"{comm} pair OK" in r.stdout
