@@ -93,6 +93,9 @@ def parse():
     ap.add_argument("--relu-split", type=int, default=0, choices=[0, 2, 3],
                     help="comparison split of the ReLU gates: 3 parts (fewest AES) or 2 (smaller keys); "
                          "0 = 3 with resident keys, 2 with --stream")
+    ap.add_argument("--relu-backend", default="dcf", choices=["dcf", "ot"],
+                    help="comparison backend of the ReLU gates: DCF keys (split per --relu-split) or OT-leaf digit "
+                         "tables with a Beaver AND tree")
     ap.add_argument("--gemm", default="tensor", choices=["tensor", "cuda-cores"],
                     help="ring GEMM engine: tcgen05 limb products (default) or the CUDA-core kernel")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
@@ -164,7 +167,9 @@ def config_of(a, n_gpus):
         "gemm": "tcgen05 kind::i8 limb products" if a.gemm == "tensor" else "CUDA-core integer multiply-add",
         "aes": f"T-table AES, {a.aes_tables} round tables staged in shared memory",
         "relu_split": a.relu_split,
-        "l2": "inputs larger than L2: every step streams the full key region (>= 24 GB per party at B=256)",
+        "relu_backend": a.relu_backend,
+        "l2": "inputs larger than L2: every step streams each party's full key region (GBs; "
+              "key_bytes_per_party_per_step in the line)",
     }
 
 
@@ -341,6 +346,7 @@ def main():
     ddg.gemm_path(ddg.GEMM_TENSOR if a.gemm == "tensor" else ddg.GEMM_CUDA_CORES)
     ddg.aes_tables(a.aes_tables)
     ddg.relu_split(a.relu_split)
+    ddg.relu_backend(ddg.RELU_OT if a.relu_backend == "ot" else ddg.RELU_DCF)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None

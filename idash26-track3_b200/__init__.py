@@ -19,7 +19,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libddg.so")
 
 (GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
- GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3) = range(9)
+ GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT) = range(11)
+# comparison backends of the forward's ReLU gates (relu_backend)
+RELU_DCF, RELU_OT = 0, 1
 
 DDG_OK = 0
 _STATUS = {1: "DDG_ERR_ARG", 2: "DDG_ERR_CUDA", 3: "DDG_ERR_KEY", 4: "DDG_ERR_PEER", 5: "DDG_ERR_STATE",
@@ -45,6 +47,7 @@ SIGNATURES = {
     "ddg_gate_keygen": (_i32, [_i32, _i32, _i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round1": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round2": (_i32, [_i32, _i32, _i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_ot_key_layout": (_i32, [_i32, _i32, _i32, _u64, ctypes.POINTER(_u64)]),
     "ddg_gate_eval_pair_noalloc": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_lut_key_bytes": (_u64, [_i32, _u64]),
     "ddg_lut_keygen": (_i32, [_i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
@@ -58,6 +61,9 @@ SIGNATURES = {
     "ddg_aes_chain_variant": (_i32, [_u64, _i32, _i32, _vp, _vp]),
     "ddg_aes_tables": (_i32, [_i32]),
     "ddg_relu_split": (_i32, [_i32]),
+    "ddg_relu_backend": (_i32, [_i32]),
+    "ddg_gate_eval_pair": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_gate_round1_arrays": (_i32, [_i32, _i32, _i32]),
     "ddg_party_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32]),
     "ddg_party_destroy": (_i32, [_vp]),
     "ddg_party_set_weights": (_i32, [_vp, _vp, _u64]),
@@ -127,6 +133,25 @@ def gate_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
             "hi_levels", "lo_levels", "hi_mu_eq", "hi_bits", "hi_shift", "lo_bits", "mid_root", "mid_cw", "mid_leaf",
             "mid_mu", "mid_mu_eq", "mid_levels")
     return {k: int(v) for k, v in zip(keys, out)}
+
+
+def ot_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
+    """Byte offsets and plan of one party's OT-gate key (see ddg_ot_key_layout)."""
+    out = (_u64 * 10)()
+    check(lib().ddg_ot_key_layout(kind, bw, scale, n, out))
+    keys = ("ks", "recv", "c0", "words", "bytes", "slots", "digits", "g0", "levels", "combines")
+    return {k: int(v) for k, v in zip(keys, out)}
+
+
+def gate_round1_arrays(kind: int, bw: int, scale: int) -> int:
+    """ceil(n/32)-word bit arrays of a kind's comparison bits (round-1 layout)."""
+    return int(lib().ddg_gate_round1_arrays(kind, bw, scale))
+
+
+def gate_eval_pair(kind, bw, scale, n, d_xhat, d_key0, d_key1, d_bits0, d_bits1, d_share0, d_share1, stream=None):
+    """Both parties of one gate on one device (every round, openings in place); see ddg_gate_eval_pair."""
+    check(lib().ddg_gate_eval_pair(kind, bw, scale, n, d_xhat, d_key0, d_key1, d_bits0, d_bits1, d_share0,
+                                   d_share1, stream))
 
 
 def gate_keygen(kind, bw, scale, n, seed, op_id, d_rin, d_rout, d_key0, d_key1, stream=None):
@@ -284,6 +309,13 @@ def relu_split(parts: int):
     (smaller keys).  Dealer and evaluators must use the same setting (it changes
     the key layout)."""
     check(lib().ddg_relu_split(parts))
+
+
+def relu_backend(backend: int):
+    """Comparison backend of the forward's ReLU gates: RELU_DCF (default; DCF keys, split per
+    relu_split) or RELU_OT (garbled radix-16 digit tables + Beaver AND tree, GATE_RELU*_OT).
+    Dealer and evaluators must use the same setting (it changes the key layout)."""
+    check(lib().ddg_relu_backend(backend))
 
 
 def gemm_status():

@@ -26,7 +26,8 @@
 //
 // Environment: DDG_WEIGHTS_BIN (default <sampledir>/weights.bin), DDG_NUM_CHUNKS
 // (default ceil(N / B)), DDG_SEED, DDG_DEVICE, DDG_PEER_PORT, DDG_RELU_SPLIT
-// (2 or 3; must match between dealer and evaluators).
+// (2 or 3) and DDG_RELU_BACKEND (dcf or ot); both must match between dealer
+// and evaluators.
 // Exit status 0 on success, 1 on usage errors, 2 on library or I/O errors.
 #include <arpa/inet.h>
 #include <fcntl.h>
@@ -227,8 +228,11 @@ int dealer(const Args &a)
     const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     FILE *m = std::fopen((a.keydir + "/meta.json").c_str(), "w");
     if (m) {
-        std::fprintf(m, "{\n  \"B\": %d,\n  \"NC\": %ld,\n  \"N\": %llu,\n  \"bw\": %d,\n  \"scale\": %d\n}\n", a.B, NC,
-                     (unsigned long long)N, a.bw, a.scale);
+        const char *be = std::getenv("DDG_RELU_BACKEND");
+        std::fprintf(m,
+                     "{\n  \"B\": %d,\n  \"NC\": %ld,\n  \"N\": %llu,\n  \"bw\": %d,\n  \"scale\": %d,\n"
+                     "  \"relu_backend\": \"%s\"\n}\n",
+                     a.B, NC, (unsigned long long)N, a.bw, a.scale, be && std::strcmp(be, "ot") == 0 ? "ot" : "dcf");
         std::fclose(m);
     }
     std::fprintf(stderr, "dealer: %ld chunk(s) of B=%d, %.1f MB per chunk and party, %.2f s\n", NC, a.B, cb / 1e6, s);
@@ -384,6 +388,9 @@ int main(int argc, char **argv)
         die(1, "bad arguments (bw 32|64, role 0|1, party 0|1|2, B > 0)");
     const long split = env_long("DDG_RELU_SPLIT", 3);
     check(ddg_relu_split(int(split)), "DDG_RELU_SPLIT");
+    const char *be = std::getenv("DDG_RELU_BACKEND");
+    if (be && std::strcmp(be, "ot") != 0 && std::strcmp(be, "dcf") != 0) die(1, "DDG_RELU_BACKEND must be dcf or ot");
+    check(ddg_relu_backend(be && std::strcmp(be, "ot") == 0 ? DDG_RELU_OT : DDG_RELU_DCF), "DDG_RELU_BACKEND");
     ::mkdir(a.keydir.c_str(), 0755);
     return a.role == 0 ? dealer(a) : evaluate(a);
 }

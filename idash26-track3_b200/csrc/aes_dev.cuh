@@ -203,6 +203,7 @@ __device__ __forceinline__ int blk_bit(const Blk &b, uint32_t y)
 
 // host side (aes_tables.cu)
 void aes_expand_host(const uint8_t key[16], AesKey &out);
+void aes_encrypt_host(const AesKey &k, const uint32_t in[4], uint32_t out[4]);
 void aes_host_init();
 AesKey dealer_key(uint64_t seed);
 int aes_device_init();

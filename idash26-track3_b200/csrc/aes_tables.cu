@@ -79,6 +79,37 @@ void aes_expand_host(const uint8_t key[16], AesKey &out)
 
 void aes_host_init() { std::call_once(h_once, host_tables); }
 
+// FIPS-197 encryption of one block (column words, little-endian bytes)
+void aes_encrypt_host(const AesKey &k, const uint32_t in[4], uint32_t out[4])
+{
+    aes_host_init();
+    uint8_t st[16], t[16];
+    auto add_key = [&](int r) {
+        for (int i = 0; i < 16; i++) st[i] ^= uint8_t(k.rk[4 * r + i / 4] >> (8 * (i % 4)));
+    };
+    for (int i = 0; i < 16; i++) st[i] = uint8_t(in[i / 4] >> (8 * (i % 4)));
+    add_key(0);
+    for (int r = 1; r <= 10; r++) {
+        for (int c = 0; c < 4; c++)  // SubBytes + ShiftRows: row j of column c comes from column c + j
+            for (int j = 0; j < 4; j++) t[4 * c + j] = h_sbox[st[4 * ((c + j) % 4) + j]];
+        if (r < 10) {
+            for (int c = 0; c < 4; c++) {  // MixColumns
+                const uint8_t a0 = t[4 * c], a1 = t[4 * c + 1], a2 = t[4 * c + 2], a3 = t[4 * c + 3];
+                st[4 * c] = uint8_t(xt(a0) ^ xt(a1) ^ a1 ^ a2 ^ a3);
+                st[4 * c + 1] = uint8_t(a0 ^ xt(a1) ^ xt(a2) ^ a2 ^ a3);
+                st[4 * c + 2] = uint8_t(a0 ^ a1 ^ xt(a2) ^ xt(a3) ^ a3);
+                st[4 * c + 3] = uint8_t(xt(a0) ^ a0 ^ a1 ^ a2 ^ xt(a3));
+            }
+        } else {
+            memcpy(st, t, 16);
+        }
+        add_key(r);
+    }
+    for (int c = 0; c < 4; c++)
+        out[c] = uint32_t(st[4 * c]) | (uint32_t(st[4 * c + 1]) << 8) | (uint32_t(st[4 * c + 2]) << 16) |
+                 (uint32_t(st[4 * c + 3]) << 24);
+}
+
 // dealer key: seed (8 bytes LE) || "dealerK1"
 AesKey dealer_key(uint64_t seed)
 {

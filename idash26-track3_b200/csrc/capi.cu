@@ -9,18 +9,20 @@
 #include "forward.cuh"
 #include "gates.cuh"
 #include "keystream.cuh"
+#include "ot.cuh"
 
 using namespace ddg;
 
 static int check_gate_args(int kind, int bw, int scale)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_SPLIT3, DDG_ERR_ARG, "gate kind %d out of range",
-              kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_OT, DDG_ERR_ARG, "gate kind %d out of range", kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
     DDG_CHECK(kind != DDG_GATE_LRS_SPLIT || scale >= 2, DDG_ERR_ARG, "split LRS needs scale >= 2 (got %d)", scale);
     DDG_CHECK(!gate_is_split3(kind) || scale + SPLIT3_MID < bw - 1, DDG_ERR_ARG,
               "three-part split needs scale + %d < bw - 1 (scale %d, bw %d)", SPLIT3_MID, scale, bw);
+    DDG_CHECK(!gate_is_ot(kind) || ot_plan_cached(bw, scale).ok, DDG_ERR_ARG, "no OT-gate plan for bw %d, scale %d",
+              bw, scale);
     return DDG_OK;
 }
 
@@ -81,6 +83,98 @@ int ddg_gate_round2(int kind, int bw, int scale, uint64_t n, int party, const vo
     DDG_CHECK(n == 0 || !L.lo || (d_lo_own && d_lo_peer), DDG_ERR_ARG, "gate needs low-DCF bits");
     return gate_round2(L, party, d_xhat, d_hi_own, d_hi_peer, d_lo_own, d_lo_peer, d_key, d_share,
                        static_cast<cudaStream_t>(stream));
+}
+
+int ddg_ot_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out)
+{
+    DDG_TRY(check_gate_args(kind, bw, scale));
+    DDG_CHECK(gate_is_ot(kind) && out != nullptr, DDG_ERR_ARG, "OT gate kind and out[10] required");
+    GateLayout L = gate_layout(kind, bw, scale, n);
+    const OtPlan &P = ot_plan_cached(bw, scale);
+    const uint64_t v[10] = {L.ot_ks, L.ot_recv, L.ot_c0, L.words, L.bytes, uint64_t(L.ot_gmax),
+                            uint64_t(P.D), uint64_t(P.G0), uint64_t(P.levels), uint64_t(P.ncomb)};
+    for (int i = 0; i < 10; i++) out[i] = v[i];
+    return DDG_OK;
+}
+
+int ddg_gate_round1_arrays(int kind, int bw, int scale)
+{
+    if (check_gate_args(kind, bw, scale) != DDG_OK) return 0;
+    GateLayout L = gate_layout(kind, bw, scale, 1);
+    if (L.ot) return 3;
+    return (L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0) + (L.lo ? 1 : 0);
+}
+
+int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xhat, const void *d_key0,
+                       const void *d_key1, uint32_t *d_bits0, uint32_t *d_bits1, void *d_share0, void *d_share1,
+                       void *stream)
+{
+    DDG_TRY(check_gate_args(kind, bw, scale));
+    DDG_CHECK(n == 0 || (d_xhat && d_key0 && d_key1 && d_share0 && d_share1), DDG_ERR_ARG, "null pointer");
+    if (n == 0) return DDG_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    GateLayout L = gate_layout(kind, bw, scale, n);
+    const uint64_t nw = (n + 31) / 32;
+    const int nb = ddg_gate_round1_arrays(kind, bw, scale), nh = L.ot ? 2 : nb - (L.lo ? 1 : 0);
+    std::vector<void *> tmp;
+    int err = DDG_OK;
+    auto grab = [&](uint64_t bytes) -> void * {
+        void *p = nullptr;
+        if (err == DDG_OK && cudaMallocAsync(&p, bytes ? bytes : 16, st) != cudaSuccess) {
+            set_last_error("cudaMallocAsync(%llu) failed", (unsigned long long)bytes);
+            err = DDG_ERR_CUDA;
+        }
+        if (p) tmp.push_back(p);
+        return p;
+    };
+    auto ok = [&](int s) {
+        if (err == DDG_OK) err = s;
+        return err == DDG_OK;
+    };
+    uint32_t *b[2] = {d_bits0 ? d_bits0 : static_cast<uint32_t *>(grab(4 * nw * nb)),
+                      d_bits1 ? d_bits1 : static_cast<uint32_t *>(grab(4 * nw * nb))};
+    const void *key[2] = {d_key0, d_key1};
+    if (!L.ot) {
+        for (int p = 0; p < 2 && err == DDG_OK; p++)
+            ok(gate_round1(L, d_xhat, key[p], L.hi ? b[p] : nullptr, L.lo ? b[p] + nh * nw : nullptr, st));
+    } else {
+        const OtPlan &P = ot_plan_cached(bw, scale);
+        uint32_t *tab[2];
+        uint64_t *state[2];
+        void *tri[2];
+        uint32_t *o[2][OT_MAX_LEVELS + 1] = {};
+        for (int p = 0; p < 2; p++) {
+            tab[p] = static_cast<uint32_t *>(grab(4 * uint64_t(P.Gmax) * n));
+            state[p] = static_cast<uint64_t *>(grab(8 * n));
+            tri[p] = grab(16 * uint64_t(P.naux) * n);
+            for (int l = 1; l <= P.levels; l++) o[p][l] = static_cast<uint32_t *>(grab(4 * n));
+        }
+        for (int p = 0; p < 2 && err == DDG_OK; p++) ok(ot_garble(L, p, d_xhat, key[p], tab[p], state[p], tri[p], st));
+        for (int l = 1; l <= P.levels + 1 && err == DDG_OK; l++)
+            for (int p = 0; p < 2 && err == DDG_OK; p++) {
+                const int q = 1 - p;
+                const bool last = l == P.levels + 1;
+                ok(ot_level(L, p, l, key[p], tab[q], o[p][l - 1], o[q][l - 1], state[p], tri[p], last ? nullptr : o[p][l],
+                            last ? b[p] : nullptr, last ? b[p] + 2 * nw : nullptr, st));
+            }
+    }
+    void *sh[2] = {d_share0, d_share1};
+    for (int p = 0; p < 2 && err == DDG_OK; p++) {
+        const int q = 1 - p;
+        const bool lo = L.lo || L.ot;
+        ok(gate_round2(L, p, d_xhat, b[p], b[q], lo ? b[p] + nh * nw : nullptr, lo ? b[q] + nh * nw : nullptr, key[p],
+                       sh[p], st));
+    }
+    for (void *p : tmp) cudaFreeAsync(p, st);
+    return err;
+}
+
+int ddg_relu_backend(int backend)
+{
+    DDG_CHECK(backend == DDG_RELU_DCF || backend == DDG_RELU_OT, DDG_ERR_ARG, "ReLU backend: %d or %d (got %d)",
+              DDG_RELU_DCF, DDG_RELU_OT, backend);
+    set_relu_backend(backend);
+    return DDG_OK;
 }
 
 int ddg_aes_chain(uint64_t threads, int iters, uint32_t *d_out, void *stream)
@@ -227,8 +321,15 @@ int ddg_party_connect_ipc(ddg_party *h, const char *name, uint64_t slot_bytes)
 uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch)
 {
     if (check_gate_args(0, bw, scale) != DDG_OK || batch <= 0) return 0;
-    // the widest opening of the graph: a (batch, 138, 376) ring tensor
-    return uint64_t(batch) * NMAX * POOL * uint64_t(bw / 8);
+    // the widest opening of the graph: a (batch, 138, 376) ring tensor, or
+    // with the OT backend the garbled tables of the ReLU over it
+    const uint64_t n = uint64_t(batch) * NMAX * POOL;
+    uint64_t per = uint64_t(bw / 8);
+    if (relu_backend() == DDG_RELU_OT) {
+        const uint64_t t = 4ull * uint64_t(ot_gmax(bw, scale));
+        per = t > per ? t : per;
+    }
+    return n * per;
 }
 
 int ddg_party_set_timeout(ddg_party *h, int timeout_ms)

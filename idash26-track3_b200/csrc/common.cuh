@@ -77,14 +77,25 @@ void set_dcf_timing_sink(DcfTiming *t);
 // low s bits, DCF with equality) and V (the low s bits, plain DCF):
 // 1{x<a} = c1 + e1*(c2 + e2*cL), every sum exclusive.  15 AES per element at
 // bw=32 instead of 20, for 40 / 80 key words instead of 16 / 32.
+// GATE_RELU_OT / GATE_RELU_ARS_OT compute GATE_RELU_SPLIT / GATE_RELU_ARS_SPLIT
+// with the same dealer words and round 2, but obtain the split comparison bits
+// from garbled radix-16 digit tables and a Beaver AND tree (ot.cuh) instead of
+// DCF keys: no AES tree, a few key bytes per element, more rounds.
 enum GateKind {
     GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
-    GATE_LRS_SPLIT = 6, GATE_RELU_SPLIT3 = 7, GATE_RELU_ARS_SPLIT3 = 8, GATE_KIND_END = 9
+    GATE_LRS_SPLIT = 6, GATE_RELU_SPLIT3 = 7, GATE_RELU_ARS_SPLIT3 = 8, GATE_RELU_OT = 9, GATE_RELU_ARS_OT = 10,
+    GATE_KIND_END = 11
 };
 constexpr int SPLIT3_MID = 6;
 constexpr int SPLIT3_NMONO = 19;  // dealer-bit monomials of the three-part DReLU bit
 
 inline bool gate_is_split3(int kind) { return kind == GATE_RELU_SPLIT3 || kind == GATE_RELU_ARS_SPLIT3; }
+inline bool gate_is_ot(int kind) { return kind == GATE_RELU_OT || kind == GATE_RELU_ARS_OT; }
+// the kind whose dealer words and round 2 a gate uses
+__host__ __device__ inline int gate_word_kind(int kind)
+{
+    return kind == GATE_RELU_OT ? GATE_RELU_SPLIT : kind == GATE_RELU_ARS_OT ? GATE_RELU_ARS_SPLIT : kind;
+}
 // the high DCF has an equality output (three round-1 bit arrays, five with a middle DCF)
 inline bool gate_is_split(int kind)
 {
@@ -94,7 +105,7 @@ inline bool gate_has_hi(int kind) { return kind != GATE_LRS; }
 inline bool gate_has_lo(int kind) { return kind != GATE_RELU; }
 inline int gate_nwords(int kind)
 {
-    switch (kind) {
+    switch (gate_word_kind(kind)) {
     case GATE_RELU: return 4;
     case GATE_RELU_ARS: return 8;
     case GATE_ARS: return 6;
@@ -156,22 +167,41 @@ inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base, bool eq = false)
 // one gate op: [hi DCF over hi_bits] [mid DCF] [lo DCF over lo_bits] [nwords x N ring words]
 // The hi DCF reads bits [hi_shift, hi_shift + H.d) of x_hat, the middle DCF
 // (three-part split kinds) bits [s, s + SPLIT3_MID), the lo DCF bits [0, Lo.d).
+// OT kinds: [ot_ks: 44 u32 round keys] [ot_recv: ot_gmax x N bytes] [ot_c0: N u32] [words]
 struct GateLayout {
     int kind = 0, bw = 0, s = 0, hi_shift = 0;
     uint64_t n = 0;
-    bool hi = false, mid = false, lo = false;
+    bool hi = false, mid = false, lo = false, ot = false;
     DcfLayout H, Mi, Lo;
+    int ot_gmax = 0;
+    uint64_t ot_ks = 0, ot_recv = 0, ot_c0 = 0;
     int nwords = 0;
     uint64_t words = 0, bytes = 0;
 };
+
+// digits party 0 garbles in an OT gate over an n-bit ring at scale s (the
+// larger half of ceil((n-1-s)/4) + ceil(s/4) radix-16 digits)
+inline int ot_gmax(int bw, int s) { return ((bw - 1 - s + 3) / 4 + (s + 3) / 4 + 1) / 2; }
 
 inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base = 0)
 {
     GateLayout g;
     g.kind = kind, g.bw = bw, g.s = s, g.n = n;
+    uint64_t off = align256(base);
+    if (gate_is_ot(kind)) {
+        g.ot = true;
+        g.ot_gmax = ot_gmax(bw, s);
+        g.ot_ks = off;
+        g.ot_recv = align256(g.ot_ks + 176);
+        g.ot_c0 = align256(g.ot_recv + uint64_t(g.ot_gmax) * n);
+        off = align256(g.ot_c0 + 4 * n);
+        g.nwords = gate_nwords(kind);
+        g.words = off;
+        g.bytes = align256(g.words + uint64_t(g.nwords) * n * uint64_t(bw / 8)) - align256(base);
+        return g;
+    }
     g.hi = gate_has_hi(kind);
     g.lo = gate_has_lo(kind);
-    uint64_t off = align256(base);
     if (g.hi) {
         g.H = dcf_layout(gate_hi_bits(kind, bw, s), n, off, gate_is_split(kind));
         g.hi_shift = gate_hi_shift(kind, s);
@@ -214,7 +244,8 @@ enum Purpose : uint32_t {
     P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4, P_ROUT = 5, P_BITS = 6,
     P_MASK = 8,    // input / output masks of linear ops
     P_MID_S0 = 9, P_MID_DELTA = 10,  // middle DCF of the three-part split gates
-    P_SHARE = 16,  // share0 of dealer word k uses purpose P_SHARE + k
+                                     // 0x100..0x12f: OT gates (ot.cuh)
+    P_SHARE = 16,  // share0 of dealer word k uses purpose P_SHARE + k (k < 80)
 };
 
 }  // namespace ddg

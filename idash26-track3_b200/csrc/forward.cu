@@ -16,6 +16,7 @@
 
 #include "forward.cuh"
 #include "gates.cuh"
+#include "ot.cuh"
 #include "linear.cuh"
 
 namespace ddg {
@@ -517,10 +518,42 @@ struct EvalExec : ExecBase<T> {
         t.v = open(s, n);
         return t;
     }
+    // OT gates: garbled digit tables, then one AND-tree level per round; the
+    // last level writes the masked comparison bits in the split-gate layout
+    // (bits_hi = [lt | eq], bits_lo = lt), opened and consumed by round 2
+    Tn<T> gate_ot(const GateLayout &L, const uint8_t *k, const Tn<T> &x)
+    {
+        const OtPlan &Pl = ot_plan_cached(this->bw, this->s);
+        const uint64_t n = x.n, nw = (n + 31) / 32;
+        uint32_t *tab = static_cast<uint32_t *>(this->alloc_bytes(4 * uint64_t(Pl.Gmax) * n));
+        uint64_t *state = static_cast<uint64_t *>(this->alloc_bytes(8 * n));
+        void *tri = this->alloc_bytes(16 * uint64_t(Pl.naux) * n);
+        if (this->err == DDG_OK) ok(ot_garble(L, p, x.v, k, tab, state, tri, this->st));
+        const uint32_t *ptab = reinterpret_cast<const uint32_t *>(peer_of(tab, 4 * uint64_t(Pl.Gmax) * n));
+        const uint32_t *oo = nullptr, *po = nullptr;
+        for (int l = 1; l <= Pl.levels; l++) {
+            uint32_t *o = static_cast<uint32_t *>(this->alloc_bytes(4 * n));
+            if (this->err == DDG_OK) ok(ot_level(L, p, l, k, ptab, oo, po, state, tri, o, nullptr, nullptr, this->st));
+            po = reinterpret_cast<const uint32_t *>(peer_of(o, 4 * n));
+            oo = o;
+        }
+        uint32_t *bits = static_cast<uint32_t *>(this->alloc_bytes(4 * nw * 3));
+        if (this->err == DDG_OK)
+            ok(ot_level(L, p, Pl.levels + 1, k, ptab, oo, po, state, tri, nullptr, bits, bits + 2 * nw, this->st));
+        const uint32_t *peer = reinterpret_cast<const uint32_t *>(peer_of(bits, 4 * nw * 3));
+        T *sh = alloc(n);
+        if (this->err == DDG_OK)
+            ok(gate_round2(L, p, x.v, bits, peer, bits + 2 * nw, peer ? peer + 2 * nw : nullptr, k, sh, this->st));
+        Tn<T> t;
+        t.n = n;
+        t.v = open(sh, n);
+        return t;
+    }
     Tn<T> gate(int kind, const Tn<T> &x)
     {
         GateLayout L = gate_layout(kind, this->bw, this->s, x.n);
         const uint8_t *k = key_at(L.bytes);
+        if (L.ot) return gate_ot(L, k, x);
         const uint64_t nw = (x.n + 31) / 32;
         // split gates also open the equality bits, three-part splits the middle DCF's two bits
         const int nh = L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0;
@@ -576,14 +609,19 @@ struct EvalExec : ExecBase<T> {
 static std::atomic<int> g_relu_parts{3};
 void set_relu_parts(int parts) { g_relu_parts.store(parts == 2 ? 2 : 3); }
 static int relu_parts(int) { return g_relu_parts.load(); }
+// comparison backend of the ReLU gates: DCF keys (split per relu_parts) or
+// OT-leaf digit tables with a Beaver AND tree (GATE_RELU*_OT)
+static std::atomic<int> g_relu_backend{DDG_RELU_DCF};
+void set_relu_backend(int backend) { g_relu_backend.store(backend == DDG_RELU_OT ? DDG_RELU_OT : DDG_RELU_DCF); }
+int relu_backend() { return g_relu_backend.load(); }
 
 template <typename T, class E>
 static void affinity_graph(E &x)
 {
     const int B = x.B;
-    const bool three = relu_parts(x.bw) == 3;
-    const int RELU = three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
-    const int RELU_ARS = three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
+    const bool three = relu_parts(x.bw) == 3, ot = g_relu_backend.load() == DDG_RELU_OT;
+    const int RELU = ot ? GATE_RELU_OT : three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
+    const int RELU_ARS = ot ? GATE_RELU_ARS_OT : three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
     const uint64_t nX = uint64_t(B) * NMAX * FEAT, nA = uint64_t(B) * NMAX * NMAX, nM = uint64_t(B) * NMAX * POOL;
     // leaves: x, mask, raw adjacency and its masked degree, the public protein
     // (deepdtagen_inference.cu:503-529 registerLeaf; secure_adj_norm.h:414-493)

@@ -71,6 +71,8 @@ struct Party {
 
 uint64_t forward_key_bytes(int bw, int s, int B);
 void set_relu_parts(int parts);
+void set_relu_backend(int backend);  // DDG_RELU_DCF or DDG_RELU_OT
+int relu_backend();
 double union_ms(std::vector<std::pair<double, double>> v);
 int pair_dcf_union(Party &p0, Party &p1);
 int parties_dcf_union(Party *const *ps, int n);

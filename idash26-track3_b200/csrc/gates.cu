@@ -8,6 +8,7 @@
 // (ddg_orca.h:112-123, ddg_orca_batched.h:161-200).
 #include "dcf_dev.cuh"
 #include "gates.cuh"
+#include "ot.cuh"
 
 namespace ddg {
 
@@ -59,6 +60,8 @@ struct GateKeygenArgs {
     T *rout;
     uint8_t *k0, *k1;
     GateLayout lay;
+    OtPlan ot;          // OT kinds: the digit plan and the two parties' keys K_0, K_1
+    AesKey prk0, prk1;
 };
 
 template <typename T, class E>
@@ -103,6 +106,21 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                 dcfeq_keygen(A, alpha, SPLIT3_MID, A.prg(a.dk.rk, a.op, P_MID_S0, e),
                              A.prg(a.dk.rk, a.op, P_MID_DELTA, e), o, e, N);
             }
+            if (L.ot) {
+                const uint32_t rc = (bits ^ (bits >> 1)) & 1u, rl = ((bits >> 2) ^ (bits >> 3)) & 1u,
+                               re = ((bits >> 4) ^ (bits >> 5)) & 1u;
+                ot_keygen_elem(A, a.ot, a.prk0.rk, a.prk1.rk, e, N, uint64_t(r), rc, re, rl, a.k0 + L.ot_recv,
+                               a.k1 + L.ot_recv, reinterpret_cast<uint32_t *>(a.k0 + L.ot_c0));
+                reinterpret_cast<uint32_t *>(a.k1 + L.ot_c0)[e] = 0u;
+                // party 0 receives D - G0 digits: its unused last slot is zeroed
+                for (int t = a.ot.D - a.ot.G0; t < L.ot_gmax; t++) a.k0[L.ot_recv + uint64_t(t) * N + e] = 0;
+                if (e == 0) {
+                    for (int i = 0; i < 44; i++) {
+                        reinterpret_cast<uint32_t *>(a.k0 + L.ot_ks)[i] = a.prk0.rk[i];
+                        reinterpret_cast<uint32_t *>(a.k1 + L.ot_ks)[i] = a.prk1.rk[i];
+                    }
+                }
+            }
             if (L.lo) {
                 const uint64_t alpha = uint64_t(r) & ((uint64_t(1) << L.Lo.d) - 1);
                 DcfOut o{a.k0 + L.Lo.root, a.k1 + L.Lo.root, a.k0 + L.Lo.cw, a.k1 + L.Lo.cw,
@@ -116,7 +134,7 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
             const T rho_e = T(((bits >> 4) ^ (bits >> 5)) & 1u);
             const T mono[7] = {e_b, rho_L, rho_e, T(rho_e * rho_L), T(e_b * rho_L), T(e_b * rho_e),
                                T(e_b * rho_e * rho_L)};
-            switch (a.kind) {
+            switch (gate_word_kind(a.kind)) {
             case GATE_RELU:
                 v[0] = e_b, v[1] = r, v[2] = e_b * r, v[3] = r_y;
                 break;
@@ -439,6 +457,12 @@ int gate_keygen_t(const GateLayout &L, uint64_t seed, uint32_t op, const void *r
     a.k0 = static_cast<uint8_t *>(k0);
     a.k1 = static_cast<uint8_t *>(k1);
     a.lay = L;
+    if (L.ot) {
+        a.ot = ot_plan_cached(L.bw, L.s);
+        DDG_CHECK(a.ot.ok, DDG_ERR_ARG, "no OT-gate plan for bw %d, scale %d", L.bw, L.s);
+        a.prk0 = ot_party_key(a.dk, op, 0);
+        a.prk1 = ot_party_key(a.dk, op, 1);
+    }
     if (L.n == 0) return DDG_OK;
     DDG_TRY((aes_tables() == 4 ? keygen_launch<T, AesLane4>(a, st) : keygen_launch<T, AesLane2>(a, st)));
     note_launch();
@@ -450,6 +474,7 @@ template <typename T>
 int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32_t *bits_hi, uint32_t *bits_lo,
                   cudaStream_t st)
 {
+    DDG_CHECK(!L.ot, DDG_ERR_ARG, "OT gates have no one-shot round 1 (garble, then the AND-tree levels)");
     DDG_TRY(aes_device_init());
     if (L.n == 0) return DDG_OK;
     Round1Args<T> a;
@@ -501,7 +526,7 @@ int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32
     uint64_t blocks = (L.n + 255) / 256;
     uint64_t cap = uint64_t(sms > 0 ? sms : 148) * 8;
     int grid = int(blocks < cap ? blocks : cap);
-    switch (L.kind) {
+    switch (gate_word_kind(L.kind)) {
     case GATE_RELU: gate_round2_kernel<T, GATE_RELU><<<grid, 256, 0, st>>>(a); break;
     case GATE_RELU_ARS: gate_round2_kernel<T, GATE_RELU_ARS><<<grid, 256, 0, st>>>(a); break;
     case GATE_ARS: gate_round2_kernel<T, GATE_ARS><<<grid, 256, 0, st>>>(a); break;

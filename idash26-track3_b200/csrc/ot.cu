@@ -1,0 +1,268 @@
+// OT-leaf comparison gates: the evaluators' kernels (garble, AND-tree levels)
+// and the dealer's part of the key (called from the gate keygen kernel).
+// The protocol, the digit plan and the key layout are described in ot.cuh.
+//
+// Reference call sites replaced: DDGOrca::relu with the LSS backend switched
+// on (DDG_LSS_RELU=1: gpu_mpc/lss/lss_online.cpp relu, lss_compare.cpp
+// compare_gt / AND tree; bridged to the masked-public GPU pipeline as
+// lss_protocol.md section 8 describes).
+#include <mutex>
+
+#include "ot.cuh"
+
+namespace ddg {
+
+// ---------------------------------------------------------------- host plan
+
+const OtPlan &ot_plan_cached(int bw, int s)
+{
+    static OtPlan plans[2][64];
+    static std::once_flag once;
+    std::call_once(once, [] {
+        for (int b = 0; b < 2; b++)
+            for (int sc = 1; sc < 64; sc++) plans[b][sc] = ot_plan(b ? 64 : 32, sc);
+    });
+    return plans[bw == 64 ? 1 : 0][s > 0 && s < 64 ? s : 0];
+}
+
+AesKey ot_party_key(const AesKey &dk, uint32_t op, int party)
+{
+    const uint32_t in[4] = {uint32_t(party), 0u, op, P_OT_PARTY};
+    uint32_t out[4];
+    aes_encrypt_host(dk, in, out);
+    uint8_t k[16];
+    for (int i = 0; i < 16; i++) k[i] = uint8_t(out[i / 4] >> (8 * (i % 4)));
+    AesKey r;
+    aes_expand_host(k, r);
+    return r;
+}
+
+// ---------------------------------------------------------------- device helpers
+
+__device__ __forceinline__ uint32_t aux_bit(const Blk &a0, const Blk &a1, int i)
+{
+    return uint32_t(blk_bit(i < 128 ? a0 : a1, uint32_t(i & 127)));
+}
+
+__device__ __forceinline__ uint32_t st_bit(uint64_t st, int i) { return uint32_t(st >> i) & 1u; }
+
+// ---------------------------------------------------------------- garble
+
+template <typename T>
+struct OtGarbleArgs {
+    OtPlan P;
+    int party;
+    uint64_t N;
+    const T *xhat;
+    const uint32_t *ks;  // the party's 44 round keys in its gate key
+    uint32_t *tables;    // [local digit][N]
+    uint64_t *state;     // [N] digit shares of the garbled digits
+    uint4 *tri;          // [naux][N] aux blocks
+};
+
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) ot_garble_kernel(const __grid_constant__ OtGarbleArgs<T> a)
+{
+    extern __shared__ uint32_t smem_tab[];
+    uint32_t *rk = smem_tab + E::SMEM / 4;
+    E::stage(smem_tab);
+    if (threadIdx.x < 44) rk[threadIdx.x] = a.ks[threadIdx.x];
+    __syncthreads();
+    E A(smem_tab);
+    const OtPlan &P = a.P;
+    const uint64_t N = a.N;
+    const int p = a.party, G = P.garbled_by(p), g0 = p == 0 ? 0 : P.G0;
+    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < N; e += uint64_t(gridDim.x) * blockDim.x) {
+        const uint64_t x = uint64_t(__ldcs(a.xhat + e));
+        const Blk x0 = A.prg(rk, 0, P_OT_AUX, e);
+        Blk x1 = x0;
+        if (P.naux > 1) x1 = A.prg(rk, 0, P_OT_AUX + 1, e);
+        uint64_t st = 0;
+        Blk pad = x0;
+        for (int t = 0; t < G; t++) {
+            if ((t & 3) == 0) pad = A.prg(rk, 0, P_OT_PAD + uint32_t(t >> 2), e);
+            const int g = g0 + t, w = P.width(g);
+            const uint32_t wm = (1u << w) - 1u;
+            uint32_t delta = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) delta |= aux_bit(x0, x1, 6 * t + i) << i;
+            delta &= wm;
+            const uint32_t slt = aux_bit(x0, x1, 6 * t + 4), seq = aux_bit(x0, x1, 6 * t + 5);
+            const uint32_t xd = uint32_t(x >> P.shift(g)) & wm;
+            const uint32_t pw = (t & 3) == 0 ? pad.w[0] : (t & 3) == 1 ? pad.w[1] : (t & 3) == 2 ? pad.w[2] : pad.w[3];
+            a.tables[uint64_t(t) * N + e] = ot_table(xd, w, delta, slt, seq, pw);
+            st |= (uint64_t(slt) << (2 * g)) | (uint64_t(seq) << (2 * g + 1));
+        }
+        a.state[e] = st;
+        a.tri[e] = make_uint4(x0.w[0], x0.w[1], x0.w[2], x0.w[3]);
+        if (P.naux > 1) a.tri[N + e] = make_uint4(x1.w[0], x1.w[1], x1.w[2], x1.w[3]);
+    }
+}
+
+// ---------------------------------------------------------------- AND-tree levels
+
+struct OtLevelArgs {
+    OtPlan P;
+    int party, level;  // level 1..levels+1
+    uint64_t N, nw;
+    const uint8_t *recv;         // level 1: the party's receiver records [slot][N]
+    const uint32_t *peer_tables; // level 1: the peer's tables [slot][N]
+    const uint32_t *c0;          // party 0's explicit triple c bits [N]
+    const uint32_t *open_own, *open_peer;  // level >= 2: the previous level's openings
+    uint64_t *state;
+    const uint4 *tri;
+    uint32_t *open_out;          // level <= levels
+    uint32_t *bits_hi, *bits_lo; // level == levels + 1: masked comparison bits (split-gate layout)
+};
+
+__global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
+{
+    const OtPlan &P = a.P;
+    const uint64_t N = a.N;
+    const int p = a.party, l = a.level;
+    const uint64_t Npad = (N + 31) & ~uint64_t(31);
+    const uint32_t p0 = p == 0 ? 1u : 0u;
+    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
+        const bool valid = e < N;
+        uint32_t hl = 0, he = 0, ll = 0;
+        if (valid) {
+            uint64_t st = a.state[e];
+            const uint4 t0 = a.tri[e];
+            uint4 t1 = t0;
+            if (P.naux > 1) t1 = a.tri[N + e];
+            const Blk x0{{t0.x, t0.y, t0.z, t0.w}}, x1{{t1.x, t1.y, t1.z, t1.w}};
+            if (l == 1) {
+                // shares of the digits the peer garbled: T[c] ^ k_c
+                const int q = 1 - p, G = P.garbled_by(q), g0 = q == 0 ? 0 : P.G0;
+                for (int t = 0; t < G; t++) {
+                    const uint32_t rec = a.recv[uint64_t(t) * N + e];
+                    const uint32_t word = a.peer_tables[uint64_t(t) * N + e];
+                    const uint32_t c = rec & 15u;
+                    const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
+                    const int g = g0 + t;
+                    st |= (uint64_t(lt) << (2 * g)) | (uint64_t(eq) << (2 * g + 1));
+                }
+            } else {
+                // close level l - 1: z = c ^ f a ^ e b ^ [p = 0] e f
+                const uint32_t O = a.open_own[e] ^ a.open_peer[e];
+                const uint32_t cw = p == 0 ? a.c0[e] : 0u;
+                const int qa = P.lvl_first[l - 2], qb = P.lvl_first[l - 1];
+                for (int q = qa; q < qb; q++) {
+                    const OtComb &C = P.comb[q];
+                    const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
+                    const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
+                    const uint32_t ta = aux_bit(x0, x1, tb), tb1 = aux_bit(x0, x1, tb + 1),
+                                   tb2 = aux_bit(x0, x1, tb + 2);
+                    const uint32_t c = p == 0 ? (cw >> (2 * q)) & 1u : aux_bit(x0, x1, tb + 3);
+                    const uint32_t c2 = p == 0 ? (cw >> (2 * q + 1)) & 1u : aux_bit(x0, x1, tb + 4);
+                    const uint32_t lt = st_bit(st, base + 2 * C.h) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
+                    const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
+                    const int o = base + 2 * C.out;
+                    st = (st & ~(uint64_t(3) << o)) | (uint64_t(lt) << o) | (uint64_t(eq) << (o + 1));
+                }
+#pragma unroll
+                for (int pt = 0; pt < 2; pt++) {
+                    const int from = P.pass_from[l - 1][pt];
+                    if (from >= 0) {
+                        const int b = 2 * P.base[pt], o = b + 2 * P.pass_to[l - 1][pt];
+                        const uint64_t v = (st >> (b + 2 * from)) & 3u;
+                        st = (st & ~(uint64_t(3) << o)) | (v << o);
+                    }
+                }
+            }
+            if (l <= P.levels) {
+                // open level l: e = eq_H ^ a, f = lt_L ^ b, f' = eq_L ^ b'
+                uint32_t w = 0;
+                const int qa = P.lvl_first[l - 1], qb = P.lvl_first[l];
+                for (int q = qa; q < qb; q++) {
+                    const OtComb &C = P.comb[q];
+                    const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
+                    const uint32_t eH = st_bit(st, base + 2 * C.h + 1), lL = st_bit(st, base + 2 * C.l),
+                                   eL = st_bit(st, base + 2 * C.l + 1);
+                    w |= ((eH ^ aux_bit(x0, x1, tb)) << (3 * j)) | ((lL ^ aux_bit(x0, x1, tb + 1)) << (3 * j + 1));
+                    if (C.eq) w |= (eL ^ aux_bit(x0, x1, tb + 2)) << (3 * j + 2);
+                }
+                a.open_out[e] = w;
+                a.state[e] = st;
+            } else {
+                hl = st_bit(st, 0), he = st_bit(st, 1), ll = st_bit(st, 2 * P.base[1]);
+            }
+        }
+        if (l > P.levels) {
+            const uint32_t wh = __ballot_sync(0xFFFFFFFFu, hl), we = __ballot_sync(0xFFFFFFFFu, he),
+                           wl = __ballot_sync(0xFFFFFFFFu, ll);
+            if ((threadIdx.x & 31) == 0) {
+                const uint64_t wi = e >> 5;
+                a.bits_hi[wi] = wh, a.bits_hi[a.nw + wi] = we, a.bits_lo[wi] = wl;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+
+template <typename T, class E>
+static int garble_launch(const OtGarbleArgs<T> &a, cudaStream_t st)
+{
+    const int smem = E::SMEM + 256;
+    DDG_CUDA(cudaFuncSetAttribute(ot_garble_kernel<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ot_garble_kernel<T, E><<<aes_blocks<E>(a.N), E::THREADS, smem, st>>>(a);
+    return DDG_OK;
+}
+
+int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, uint64_t *state,
+              void *tri, cudaStream_t st)
+{
+    DDG_TRY(aes_device_init());
+    if (L.n == 0) return DDG_OK;
+    const OtPlan &P = ot_plan_cached(L.bw, L.s);
+    DDG_CHECK(P.ok, DDG_ERR_ARG, "no OT-gate plan for bw %d, scale %d", L.bw, L.s);
+    const uint8_t *k = static_cast<const uint8_t *>(key);
+    if (L.bw == 32) {
+        OtGarbleArgs<uint32_t> a{P, party, L.n, static_cast<const uint32_t *>(xhat),
+                                 reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state,
+                                 static_cast<uint4 *>(tri)};
+        DDG_TRY((aes_tables() == 4 ? garble_launch<uint32_t, AesLane4>(a, st) : garble_launch<uint32_t, AesLane2>(a, st)));
+    } else {
+        OtGarbleArgs<uint64_t> a{P, party, L.n, static_cast<const uint64_t *>(xhat),
+                                 reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state,
+                                 static_cast<uint4 *>(tri)};
+        DDG_TRY((aes_tables() == 4 ? garble_launch<uint64_t, AesLane4>(a, st) : garble_launch<uint64_t, AesLane2>(a, st)));
+    }
+    note_launch();
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
+             const uint32_t *open_own, const uint32_t *open_peer, uint64_t *state, const void *tri,
+             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st)
+{
+    if (L.n == 0) return DDG_OK;
+    const OtPlan &P = ot_plan_cached(L.bw, L.s);
+    DDG_CHECK(P.ok && level >= 1 && level <= P.levels + 1, DDG_ERR_ARG, "OT level %d out of range", level);
+    const uint8_t *k = static_cast<const uint8_t *>(key);
+    OtLevelArgs a;
+    a.P = P, a.party = party, a.level = level, a.N = L.n, a.nw = (L.n + 31) / 32;
+    a.recv = k + L.ot_recv;
+    a.peer_tables = peer_tables;
+    a.c0 = reinterpret_cast<const uint32_t *>(k + L.ot_c0);
+    a.open_own = open_own, a.open_peer = open_peer;
+    a.state = state;
+    a.tri = static_cast<const uint4 *>(tri);
+    a.open_out = open_out, a.bits_hi = bits_hi, a.bits_lo = bits_lo;
+    const int sms = device_sms();
+    const uint64_t blocks = (L.n + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
+    ot_level_kernel<<<int(blocks < cap ? blocks : cap), 256, 0, st>>>(a);
+    note_launch();
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+uint64_t ot_scratch_bytes(const GateLayout &L)
+{
+    const OtPlan &P = ot_plan_cached(L.bw, L.s);
+    return uint64_t(L.n) * (4ull * P.Gmax + 8 + 16ull * P.naux);
+}
+
+}  // namespace ddg

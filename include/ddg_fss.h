@@ -56,6 +56,25 @@ extern "C" {
  * emits five bit arrays (see ddg_gate_round1). */
 #define DDG_GATE_RELU_SPLIT3 7
 #define DDG_GATE_RELU_ARS_SPLIT3 8
+/* Same functions (and the same dealer words and round 2) as RELU_SPLIT /
+ * RELU_ARS_SPLIT, with the comparison bits computed interactively instead of
+ * from DCF keys, after the reference's LSS ReLU backend
+ * (gpu_mpc/lss/lss_compare.cpp, lss_protocol.md sections 1-2, 5): the
+ * (bw-1-scale)- and scale-bit parts are cut into radix-16 digits, each digit
+ * garbled by one party as a 16-entry (lt, eq) table the other party reads at
+ * its dealer-given index, and the digits are combined by a tree of Beaver AND
+ * gates, one round per level (3 levels at bw=32, 4 at bw=64).  Each party
+ * regenerates its own randomness from a per-gate AES key: about 4 AES-128
+ * and 9 key bytes per element and party at bw=32 besides the 16 / 32 words,
+ * against 15-20 AES and 160-290 DCF key bytes.  Round 1 is interactive: run
+ * these kinds through the forward or ddg_gate_eval_pair; ddg_gate_round1
+ * refuses them.  Round 2 is that of the SPLIT kinds (three bit arrays). */
+#define DDG_GATE_RELU_OT 9
+#define DDG_GATE_RELU_ARS_OT 10
+
+/* ReLU comparison backends of the forward (ddg_relu_backend) */
+#define DDG_RELU_DCF 0
+#define DDG_RELU_OT 1
 
 const char *ddg_last_error(void);
 int ddg_version(void);
@@ -90,6 +109,12 @@ uint64_t ddg_gate_key_bytes(int kind, int bw, int scale, uint64_t n);
  * (level-major), leaf[n] 16 B, mu[ceil(n/32)] u32 mask bits; then
  * nwords x n ring words.  Every array starts on a 256-byte boundary. */
 int ddg_gate_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out);
+/* OT kinds: byte offsets of one party's key for n elements, written to out[10]:
+ *   0 round keys of the party's AES key (44 u32) 1 receiver records (slots x n
+ *   bytes: choice | pad_lt << 4 | pad_eq << 5) 2 party 0's triple c bits (n u32;
+ *   zero in party 1's key) 3 words 4 total bytes 5 receiver slots 6 digits
+ *   7 digits garbled by party 0 8 AND-tree levels 9 AND-tree combines */
+int ddg_ot_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out);
 
 /* dealer: both parties' keys for n elements with input masks d_rin (n ring
  * elements); writes the output masks d_rout.  Deterministic in (seed, op_id). */
@@ -169,7 +194,8 @@ int ddg_party_connect_nccl(ddg_party *party, const void *unique_id128, int nrank
  * Waits on the peer are bounded by the party's timeout (ddg_party_set_timeout
  * before connecting, default 60 s) and end in DDG_ERR_PEER. */
 int ddg_party_connect_ipc(ddg_party *party, const char *name, uint64_t slot_bytes);
-/* the largest single opening of one forward of `batch` samples, in bytes */
+/* the largest single exchange of one forward of `batch` samples, in bytes
+ * (with the OT ReLU backend selected: its garbled tables) */
 uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch);
 /* give up (DDG_ERR_PEER) when the peer does not reach an opening in time */
 int ddg_party_set_timeout(ddg_party *party, int timeout_ms);
@@ -328,6 +354,22 @@ int ddg_aes_tables(int tables);
  * (ddg_dealer_forward, ddg_forward_key_bytes) and both evaluators must run
  * with the same setting. */
 int ddg_relu_split(int parts);
+/* Comparison backend of the forward's ReLU gates, process-wide:
+ * DDG_RELU_DCF (default; the split chosen by ddg_relu_split) or DDG_RELU_OT
+ * (DDG_GATE_RELU*_OT).  It changes the key layout like ddg_relu_split. */
+int ddg_relu_backend(int backend);
+
+/* Test and measurement helper: both parties of one gate on one device, every
+ * opening done in place (the peer's buffers read directly).  d_bits0/1
+ * (optional, ddg_gate_round1_arrays() x ceil(n/32) words each) receive each
+ * party's masked comparison-bit shares in the round-1 layout of the kind (for
+ * the OT kinds that of the SPLIT kinds: [hi lt | hi eq | lo lt]); d_share0/1
+ * each party's additive share of the masked output y + r_out. */
+int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xhat, const void *d_key0,
+                       const void *d_key1, uint32_t *d_bits0, uint32_t *d_bits1, void *d_share0, void *d_share1,
+                       void *stream);
+/* number of ceil(n/32)-word bit arrays of a kind's comparison bits (0 on bad arguments) */
+int ddg_gate_round1_arrays(int kind, int bw, int scale);
 
 #ifdef __cplusplus
 }

@@ -745,6 +745,276 @@ uint64_t ref_gate_round2(int kind, int n, int s, int party, uint64_t xhat, int b
     return y & M;
 }
 
+/* --------------------------------------------------- OT-leaf comparison gates
+ *
+ * GATE_RELU_OT (9) / GATE_RELU_ARS_OT (10): the functions and dealer words of
+ * GATE_RELU_SPLIT / GATE_RELU_ARS_SPLIT, with the split comparison bits
+ *   hi: 1{U < A}, 1{U == A} over bits [s, n-1);  lo: 1{V < B} over bits [0, s)
+ * (each XORed with its dealer mask bit rho_c, rho_e, rho_L) computed by the
+ * millionaires' structure of the reference's LSS backend
+ * (gpu_mpc/lss/lss_compare.cpp, lss_protocol.md sections 1-2 and 5): radix-16
+ * digits, one garbled 16-entry (lt, eq) table per digit read by the other
+ * party at a dealer-given index c = (mask digit + delta) mod 16, then a tree
+ * of Beaver ANDs combining node pairs (H = 2i+1, L = 2i):
+ *   lt = lt_H ^ (eq_H & lt_L),  eq = eq_H & eq_L,
+ * an odd top node passing up; the root AND of a part carries its mask bit in
+ * the triple (c = ab ^ rho).  Each party's randomness: K_p = AES_dealer(p ||
+ * op || 0x100); aux block j = AES_Kp(i || 0 || 0x110 + j): per garbled local
+ * digit t, delta at bits 6t..6t+3 and (s_lt, s_eq) at 6t+4, 6t+5, then per
+ * combine q (a, b, b', c1, c1') at 6*Gmax + 5q; pad block j = AES_Kp(i || 0 ||
+ * 0x120 + j), digit t's pads = 32-bit word t mod 4 of block t / 4.  Party 0
+ * holds its triple c bits explicitly (c0: bits 2q, 2q+1); party 1 uses c1.
+ * Written independently of the CUDA code from that description. */
+enum { GATE_RELU_OT = 9, GATE_RELU_ARS_OT = 10 };
+enum { OT_P_PARTY = 0x100, OT_P_AUX = 0x110, OT_P_PAD = 0x120 };
+#define OT_MAXD 18
+#define OT_MAXC 16
+
+typedef struct {
+    int n, s, D, G0, nd[2], levels, ncomb, tri0, naux;
+    int cpart[OT_MAXC], ch[OT_MAXC], cl[OT_MAXC], cout[OT_MAXC], ceq[OT_MAXC], croot[OT_MAXC], clevel[OT_MAXC];
+    int pfrom[8][2], pto[8][2];
+} ot_plan_t;
+
+static int ot_plan_build(int n, int s, ot_plan_t *P)
+{
+    memset(P, 0, sizeof(*P));
+    P->n = n, P->s = s;
+    int bits[2] = {n - 1 - s, s};
+    if (bits[0] < 1 || bits[1] < 1) return 0;
+    P->nd[0] = (bits[0] + 3) / 4, P->nd[1] = (bits[1] + 3) / 4;
+    P->D = P->nd[0] + P->nd[1];
+    if (P->D > OT_MAXD) return 0;
+    P->G0 = (P->D + 1) / 2;
+    int k[2] = {P->nd[0], P->nd[1]}, q = 0, l = 0;
+    while (k[0] > 1 || k[1] > 1) {
+        l++;
+        if (l > 7) return 0;
+        for (int p = 0; p < 2; p++) {
+            P->pfrom[l][p] = P->pto[l][p] = -1;
+            if (k[p] <= 1) continue;
+            int nk = (k[p] + 1) / 2;
+            for (int i = 0; i < k[p] / 2; i++) {
+                if (q >= OT_MAXC) return 0;
+                P->cpart[q] = p, P->ch[q] = 2 * i + 1, P->cl[q] = 2 * i, P->cout[q] = i;
+                P->ceq[q] = (i > 0 || p == 0), P->croot[q] = (nk == 1), P->clevel[q] = l;
+                q++;
+            }
+            if (k[p] & 1) P->pfrom[l][p] = k[p] - 1, P->pto[l][p] = k[p] / 2;
+            k[p] = nk;
+        }
+    }
+    P->levels = l, P->ncomb = q, P->tri0 = 6 * P->G0;
+    P->naux = (P->tri0 + 5 * q + 127) / 128;
+    return P->naux <= 2;
+}
+
+static int ot_part(const ot_plan_t *P, int g) { return g < P->nd[0] ? 0 : 1; }
+static int ot_shift(const ot_plan_t *P, int g) { return g < P->nd[0] ? P->s + 4 * g : 4 * (g - P->nd[0]); }
+static int ot_width(const ot_plan_t *P, int g)
+{
+    int bits = g < P->nd[0] ? P->n - 1 - P->s : P->s, j = g < P->nd[0] ? g : g - P->nd[0];
+    return bits - 4 * j < 4 ? bits - 4 * j : 4;
+}
+static int ot_garbler(const ot_plan_t *P, int g) { return g < P->G0 ? 0 : 1; }
+static int ot_local(const ot_plan_t *P, int g) { return g < P->G0 ? g : g - P->G0; }
+
+typedef struct {
+    uint8_t ks[176];     /* expanded AES key K_p (round keys, bytes) */
+    uint8_t recv[OT_MAXD]; /* choice | pad_lt << 4 | pad_eq << 5 per receiver slot */
+    uint32_t c0;         /* party 0's triple c bits (0 for party 1) */
+    uint64_t w[32];      /* dealer words of the SPLIT kind */
+} ref_ot_key;
+
+int ref_ot_plan_info(int n, int s, int *out6)
+{
+    ot_plan_t P;
+    if (!ot_plan_build(n, s, &P)) return 0;
+    out6[0] = P.D, out6[1] = P.G0, out6[2] = P.levels, out6[3] = P.ncomb, out6[4] = P.naux, out6[5] = P.tri0;
+    return 1;
+}
+
+/* bit y of the party's aux blocks */
+static int ot_aux_bit(const uint8_t aux[2][16], int y) { return block_bit(aux[y >> 7], y & 127); }
+
+static void ot_party_blocks(const ot_plan_t *P, const aes_ks *kp, uint64_t i, uint8_t aux[2][16])
+{
+    memset(aux, 0, 32);
+    for (int j = 0; j < P->naux; j++) ref_prg(kp, 0, OT_P_AUX + (uint32_t)j, i, aux[j]);
+}
+
+static uint32_t ot_pad_word(const aes_ks *kp, uint64_t i, int t)
+{
+    uint8_t b[16];
+    ref_prg(kp, 0, OT_P_PAD + (uint32_t)(t / 4), i, b);
+    const uint8_t *w = b + 4 * (t % 4);
+    return (uint32_t)w[0] | ((uint32_t)w[1] << 8) | ((uint32_t)w[2] << 16) | ((uint32_t)w[3] << 24);
+}
+
+/* The mask bits of the SPLIT kinds come from the same P_BITS block as in ref_gate_keygen. */
+uint64_t ref_ot_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint64_t i, uint64_t r_in,
+                       ref_ot_key *k0, ref_ot_key *k1)
+{
+    ot_plan_t P;
+    memset(k0, 0, sizeof(*k0));
+    memset(k1, 0, sizeof(*k1));
+    if (!ot_plan_build(n, s, &P)) return 0;
+    static ref_gate_key g0, g1; /* words of the SPLIT kind (its DCF parts are unused) */
+    int wk = kind == GATE_RELU_OT ? GATE_RELU_SPLIT : GATE_RELU_ARS_SPLIT;
+    uint64_t r_out = ref_gate_keygen(wk, n, s, seed, op, i, r_in, &g0, &g1);
+    memcpy(k0->w, g0.w, sizeof(k0->w));
+    memcpy(k1->w, g1.w, sizeof(k1->w));
+
+    aes_ks dk, kp[2];
+    ref_dealer_key(seed, &dk);
+    uint8_t blk[16];
+    for (int p = 0; p < 2; p++) {
+        ref_prg(&dk, op, OT_P_PARTY, (uint64_t)p, blk);
+        ref_aes128_expand(blk, &kp[p]);
+    }
+    memcpy(k0->ks, kp[0].rk, 176);
+    memcpy(k1->ks, kp[1].rk, 176);
+    ref_prg(&dk, op, P_BITS, i, blk);
+    int rho_c = (blk[0] ^ (blk[0] >> 1)) & 1, rho_L = ((blk[0] >> 2) ^ (blk[0] >> 3)) & 1,
+        rho_e = ((blk[0] >> 4) ^ (blk[0] >> 5)) & 1;
+    uint64_t M = nmask(n);
+    r_in &= M;
+    uint64_t rhi = (r_in >> s) & ((1ULL << (n - 1 - s)) - 1), rlo = r_in & ((1ULL << s) - 1);
+    uint8_t aux[2][2][16];
+    ot_party_blocks(&P, &kp[0], i, aux[0]);
+    ot_party_blocks(&P, &kp[1], i, aux[1]);
+    ref_ot_key *kk[2] = {k0, k1};
+    for (int g = 0; g < P.D; g++) {
+        int pg = ot_garbler(&P, g), t = ot_local(&P, g), w = ot_width(&P, g), part = ot_part(&P, g);
+        uint32_t wm = (1u << w) - 1;
+        uint32_t delta = 0;
+        for (int b = 0; b < 4; b++) delta |= (uint32_t)ot_aux_bit(aux[pg], 6 * t + b) << b;
+        delta &= wm;
+        uint32_t alpha = (uint32_t)((part == 0 ? rhi >> (4 * g) : rlo >> (4 * (g - P.nd[0])))) & wm;
+        uint32_t c = (alpha + delta) & wm;
+        uint32_t pw = ot_pad_word(&kp[pg], i, t);
+        int klt = (pw >> c) & 1, keq = (pw >> (16 + c)) & 1;
+        if (P.nd[part] == 1) {
+            klt ^= part == 0 ? rho_c : rho_L;
+            keq ^= part == 0 ? rho_e : 0;
+        }
+        kk[1 - pg]->recv[t] = (uint8_t)(c | (klt << 4) | (keq << 5));
+    }
+    uint32_t cw = 0;
+    for (int q = 0; q < P.ncomb; q++) {
+        int tb = P.tri0 + 5 * q;
+        int a = ot_aux_bit(aux[0], tb) ^ ot_aux_bit(aux[1], tb);
+        int b = ot_aux_bit(aux[0], tb + 1) ^ ot_aux_bit(aux[1], tb + 1);
+        int b2 = ot_aux_bit(aux[0], tb + 2) ^ ot_aux_bit(aux[1], tb + 2);
+        int c = (a & b) ^ ot_aux_bit(aux[1], tb + 3), c2 = (a & b2) ^ ot_aux_bit(aux[1], tb + 4);
+        if (P.croot[q]) {
+            c ^= P.cpart[q] == 0 ? rho_c : rho_L;
+            c2 ^= P.cpart[q] == 0 ? rho_e : 0;
+        }
+        cw |= ((uint32_t)c << (2 * q)) | ((uint32_t)(P.ceq[q] ? c2 : 0) << (2 * q + 1));
+    }
+    k0->c0 = cw;
+    k1->c0 = 0;
+    return r_out;
+}
+
+/* the garbler's table word: entry u (u < 2^w) = (1{xd < u - delta}, 1{xd == u - delta}) ^ (s_lt, s_eq) ^ pad */
+static uint32_t ot_table_word(uint32_t xd, int w, uint32_t delta, int slt, int seq, uint32_t pad)
+{
+    uint32_t W = 1u << w, word = 0;
+    for (uint32_t u = 0; u < W; u++) {
+        uint32_t v = (u + W - delta) % W;
+        word |= (uint32_t)((xd < v) ^ slt) << u;
+        word |= (uint32_t)((xd == v) ^ seq) << (16 + u);
+    }
+    uint32_t m = (W == 32 ? 0 : ((1u << W) - 1));
+    return word ^ (pad & (m | (m << 16)));
+}
+
+/*
+ * Both parties' online protocol for one element, openings in place.  Returns
+ * through bits0 / bits1 each party's masked comparison-bit shares in the
+ * round-1 encoding of ref_gate_round1 (bit0 hi lt, bit1 lo lt, bit2 hi eq);
+ * tables0 / tables1 (optional, G0 words) receive each party's garbled tables.
+ */
+void ref_ot_eval_pair(int kind, int n, int s, uint64_t xhat, uint64_t i, const ref_ot_key *k0,
+                      const ref_ot_key *k1, int *bits0, int *bits1, uint32_t *tables0, uint32_t *tables1)
+{
+    (void)kind;
+    ot_plan_t P;
+    *bits0 = *bits1 = 0;
+    if (!ot_plan_build(n, s, &P)) return;
+    const ref_ot_key *kk[2] = {k0, k1};
+    xhat &= nmask(n);
+    aes_ks kp[2];
+    uint8_t aux[2][2][16];
+    uint32_t tab[2][OT_MAXD];
+    uint64_t st[2] = {0, 0};
+    for (int p = 0; p < 2; p++) {
+        memcpy(kp[p].rk, kk[p]->ks, 176);
+        ot_party_blocks(&P, &kp[p], i, aux[p]);
+    }
+    /* message 1: garbled tables; own digit shares */
+    for (int g = 0; g < P.D; g++) {
+        int pg = ot_garbler(&P, g), t = ot_local(&P, g), w = ot_width(&P, g);
+        uint32_t wm = (1u << w) - 1, delta = 0;
+        for (int b = 0; b < 4; b++) delta |= (uint32_t)ot_aux_bit(aux[pg], 6 * t + b) << b;
+        delta &= wm;
+        int slt = ot_aux_bit(aux[pg], 6 * t + 4), seq = ot_aux_bit(aux[pg], 6 * t + 5);
+        uint32_t xd = (uint32_t)(xhat >> ot_shift(&P, g)) & wm;
+        tab[pg][t] = ot_table_word(xd, w, delta, slt, seq, ot_pad_word(&kp[pg], i, t));
+        st[pg] |= ((uint64_t)slt << (2 * g)) | ((uint64_t)seq << (2 * g + 1));
+    }
+    if (tables0)
+        for (int t = 0; t < P.G0; t++) tables0[t] = t < P.G0 ? tab[0][t] : 0;
+    if (tables1)
+        for (int t = 0; t < P.D - P.G0; t++) tables1[t] = tab[1][t];
+    /* receivers: T[c] ^ k_c */
+    for (int g = 0; g < P.D; g++) {
+        int pg = ot_garbler(&P, g), t = ot_local(&P, g), pr = 1 - pg;
+        uint32_t rec = kk[pr]->recv[t], c = rec & 15, word = tab[pg][t];
+        uint64_t lt = ((word >> c) ^ (rec >> 4)) & 1, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1;
+        st[pr] |= (lt << (2 * g)) | (eq << (2 * g + 1));
+    }
+    /* AND-tree levels */
+    for (int l = 1; l <= P.levels; l++) {
+        int e_[OT_MAXC], f_[OT_MAXC], f2_[OT_MAXC];
+        for (int q = 0; q < P.ncomb; q++) {
+            if (P.clevel[q] != l) continue;
+            int base = 2 * (P.cpart[q] == 0 ? 0 : P.nd[0]), tb = P.tri0 + 5 * q;
+            e_[q] = f_[q] = f2_[q] = 0;
+            for (int p = 0; p < 2; p++) {
+                e_[q] ^= (int)((st[p] >> (base + 2 * P.ch[q] + 1)) & 1) ^ ot_aux_bit(aux[p], tb);
+                f_[q] ^= (int)((st[p] >> (base + 2 * P.cl[q])) & 1) ^ ot_aux_bit(aux[p], tb + 1);
+                if (P.ceq[q]) f2_[q] ^= (int)((st[p] >> (base + 2 * P.cl[q] + 1)) & 1) ^ ot_aux_bit(aux[p], tb + 2);
+            }
+        }
+        for (int p = 0; p < 2; p++) {
+            for (int q = 0; q < P.ncomb; q++) {
+                if (P.clevel[q] != l) continue;
+                int base = 2 * (P.cpart[q] == 0 ? 0 : P.nd[0]), tb = P.tri0 + 5 * q;
+                int a = ot_aux_bit(aux[p], tb), b = ot_aux_bit(aux[p], tb + 1), b2 = ot_aux_bit(aux[p], tb + 2);
+                int c = p == 0 ? (int)((k0->c0 >> (2 * q)) & 1) : ot_aux_bit(aux[1], tb + 3);
+                int c2 = p == 0 ? (int)((k0->c0 >> (2 * q + 1)) & 1) : ot_aux_bit(aux[1], tb + 4);
+                int p0 = p == 0;
+                int lt = (int)((st[p] >> (base + 2 * P.ch[q])) & 1) ^ c ^ (f_[q] & a) ^ (e_[q] & b) ^ (p0 & e_[q] & f_[q]);
+                int eq = P.ceq[q] ? (c2 ^ (f2_[q] & a) ^ (e_[q] & b2) ^ (p0 & e_[q] & f2_[q])) : 0;
+                int o = base + 2 * P.cout[q];
+                st[p] = (st[p] & ~(3ULL << o)) | ((uint64_t)lt << o) | ((uint64_t)eq << (o + 1));
+            }
+            for (int pt = 0; pt < 2; pt++) {
+                if (P.pfrom[l][pt] < 0) continue;
+                int b = 2 * (pt == 0 ? 0 : P.nd[0]), o = b + 2 * P.pto[l][pt];
+                uint64_t v = (st[p] >> (b + 2 * P.pfrom[l][pt])) & 3;
+                st[p] = (st[p] & ~(3ULL << o)) | (v << o);
+            }
+        }
+    }
+    int *out[2] = {bits0, bits1};
+    for (int p = 0; p < 2; p++)
+        *out[p] = (int)(st[p] & 1) | ((int)((st[p] >> (2 * P.nd[0])) & 1) << 1) | ((int)((st[p] >> 1) & 1) << 2);
+}
+
 /* ------------------------------------------------------------ DPF-LUT */
 
 typedef struct {

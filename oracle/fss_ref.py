@@ -22,9 +22,13 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "libfss_ref.so")
 
 (GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
- GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3) = range(9)
+ GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT) = range(11)
 GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4, GATE_RELU_SPLIT: 16,
-               GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7, GATE_RELU_SPLIT3: 40, GATE_RELU_ARS_SPLIT3: 80}
+               GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7, GATE_RELU_SPLIT3: 40, GATE_RELU_ARS_SPLIT3: 80,
+               GATE_RELU_OT: 16, GATE_RELU_ARS_OT: 32}
+# OT-leaf kinds and the SPLIT kind whose words and round 2 they use
+OT_KINDS = (GATE_RELU_OT, GATE_RELU_ARS_OT)
+OT_WORD_KIND = {GATE_RELU_OT: GATE_RELU_SPLIT, GATE_RELU_ARS_OT: GATE_RELU_ARS_SPLIT}
 # kinds whose high DCF also outputs equality (three round-1 bit arrays or more)
 SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT, GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3)
 # kinds with a middle DCF with equality output (five round-1 bit arrays)
@@ -55,6 +59,15 @@ class GateKey(ctypes.Structure):
         ("mid_mu", ctypes.c_int32),
         ("mid_mu_eq", ctypes.c_int32),
         ("w", ctypes.c_uint64 * 80),
+    ]
+
+
+class OtKey(ctypes.Structure):
+    _fields_ = [
+        ("ks", ctypes.c_uint8 * 176),
+        ("recv", ctypes.c_uint8 * 18),
+        ("c0", ctypes.c_uint32),
+        ("w", ctypes.c_uint64 * 32),
     ]
 
 
@@ -108,6 +121,15 @@ def lib():
                                    ctypes.POINTER(LutKey)]
         L.ref_lut_eval.restype = ctypes.c_uint64
         L.ref_invsqrt_table.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)]
+        L.ref_ot_plan_info.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        L.ref_ot_plan_info.restype = ctypes.c_int
+        L.ref_ot_keygen.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32,
+                                    ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(OtKey), ctypes.POINTER(OtKey)]
+        L.ref_ot_keygen.restype = ctypes.c_uint64
+        u32p = ctypes.POINTER(ctypes.c_uint32)
+        L.ref_ot_eval_pair.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64,
+                                       ctypes.POINTER(OtKey), ctypes.POINTER(OtKey), ctypes.POINTER(ctypes.c_int),
+                                       ctypes.POINTER(ctypes.c_int), u32p, u32p]
         _lib = L
     return _lib
 
@@ -195,6 +217,45 @@ def gate_eval_pair(kind: int, n: int, s: int, xhat: int, k0: GateKey, k1: GateKe
     y0 = gate_round2(kind, n, s, 0, xhat, o, k0)
     y1 = gate_round2(kind, n, s, 1, xhat, o, k1)
     return (y0 + y1) & ((1 << n) - 1)
+
+
+def ot_plan_info(n: int, s: int) -> dict:
+    o = (ctypes.c_int * 6)()
+    if not lib().ref_ot_plan_info(n, s, o):
+        raise ValueError(f"no OT plan for n={n} s={s}")
+    return dict(zip(("digits", "g0", "levels", "combines", "naux", "tri0"), list(o)))
+
+
+def ot_keygen(kind: int, n: int, s: int, seed: int, op: int, i: int, r_in: int):
+    k0, k1 = OtKey(), OtKey()
+    r_out = lib().ref_ot_keygen(kind, n, s, seed, op, i, r_in, ctypes.byref(k0), ctypes.byref(k1))
+    return k0, k1, r_out
+
+
+def ot_eval_pair(kind: int, n: int, s: int, xhat: int, i: int, k0: OtKey, k1: OtKey):
+    """Both parties' OT comparison protocol for element i: (bits0, bits1, tables0, tables1), bits in the
+    round-1 encoding (bit0 hi compare, bit1 lo compare, bit2 hi equality), tables = each party's garbled words."""
+    b0, b1 = ctypes.c_int(), ctypes.c_int()
+    t0, t1 = (ctypes.c_uint32 * 18)(), (ctypes.c_uint32 * 18)()
+    lib().ref_ot_eval_pair(kind, n, s, xhat, i, ctypes.byref(k0), ctypes.byref(k1), ctypes.byref(b0),
+                           ctypes.byref(b1), t0, t1)
+    info = ot_plan_info(n, s)
+    return b0.value, b1.value, list(t0)[: info["g0"]], list(t1)[: info["digits"] - info["g0"]]
+
+
+def ot_round2(kind: int, n: int, s: int, party: int, xhat: int, bits: int, key: OtKey) -> int:
+    """round 2 of an OT kind = round 2 of its SPLIT kind over the opened bits and the key's words"""
+    g = GateKey()
+    for j in range(32):
+        g.w[j] = key.w[j]
+    return gate_round2(OT_WORD_KIND[kind], n, s, party, xhat, bits, g)
+
+
+def ot_gate_pair(kind: int, n: int, s: int, xhat: int, i: int, k0: OtKey, k1: OtKey) -> int:
+    """Both parties, every round: returns y_hat = y + r_out."""
+    b0, b1, _, _ = ot_eval_pair(kind, n, s, xhat, i, k0, k1)
+    o = b0 ^ b1
+    return (ot_round2(kind, n, s, 0, xhat, o, k0) + ot_round2(kind, n, s, 1, xhat, o, k1)) & ((1 << n) - 1)
 
 
 def lut_keygen(n: int, seed: int, op: int, i: int, alpha: int, r_out: int):

@@ -44,7 +44,35 @@ def test_split_lrs_layout(ddg):
     with pytest.raises(ddg.DdgError):
         ddg.gate_key_layout(ddg.GATE_LRS_SPLIT, 32, 1, 10)
     with pytest.raises(ddg.DdgError):
-        ddg.gate_key_layout(ddg.GATE_RELU_ARS_SPLIT3 + 1, 32, 12, 10)
+        ddg.gate_key_layout(ddg.GATE_RELU_ARS_OT + 1, 32, 12, 10)
+
+
+def test_ot_gate_layout(ddg):
+    """OT-leaf ReLU kinds: 44 round keys, one receiver byte per digit slot,
+    party 0's c word, then the SPLIT kind's 16 / 32 words.  bw=32, scale 12:
+    19 + 12 bits in 5 + 3 radix-16 digits, 4 garbled by each party, 3 AND
+    levels, 6 combines; bw=64: 13 + 3 digits, 4 levels, 14 combines."""
+    from oracle import fss_ref as F
+
+    for bw, plan in ((32, (8, 4, 3, 6)), (64, (16, 8, 4, 14))):
+        for kind, words in ((ddg.GATE_RELU_OT, 16), (ddg.GATE_RELU_ARS_OT, 32)):
+            n = 1000
+            lay = ddg.ot_key_layout(kind, bw, 12, n)
+            assert (lay["digits"], lay["g0"], lay["levels"], lay["combines"]) == plan
+            info = F.ot_plan_info(bw, 12)
+            assert (info["digits"], info["g0"], info["levels"], info["combines"]) == plan
+            assert lay["ks"] == 0 and lay["recv"] >= 176 and lay["c0"] >= lay["recv"] + lay["slots"] * n
+            assert lay["words"] >= lay["c0"] + 4 * n
+            assert lay["bytes"] == ddg.gate_key_bytes(kind, bw, 12, n) >= lay["words"] + words * (bw // 8) * n
+            # smaller keys than any DCF form of the same function
+            split = ddg.GATE_RELU_SPLIT if kind == ddg.GATE_RELU_OT else ddg.GATE_RELU_ARS_SPLIT
+            assert lay["bytes"] < ddg.gate_key_bytes(split, bw, 12, n)
+        assert ddg.gate_round1_arrays(ddg.GATE_RELU_OT, bw, 12) == 3
+    with pytest.raises(ddg.DdgError) as e:  # the interactive kinds have no one-shot round 1
+        ddg.gate_round1(ddg.GATE_RELU_OT, 32, 12, 10, 1, 1, 1, 1)
+    assert e.value.code == 1
+    with pytest.raises(ddg.DdgError):
+        ddg.ot_key_layout(ddg.GATE_RELU_SPLIT, 32, 12, 10)
 
 
 def test_three_part_split_layout(ddg):

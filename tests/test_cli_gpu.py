@@ -58,20 +58,26 @@ def test_usage_errors_exit_1():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("backend", ["dcf", "ot"])
 @pytest.mark.parametrize("bw", [32, 64])
-def test_dealer_then_both_parties_in_one_process(synth, cuda, tmp_path, bw):
+def test_dealer_then_both_parties_in_one_process(synth, cuda, tmp_path, bw, backend):
     N, B = 5, 2  # three chunks, the last one partial
     sampledir, want = dataset(synth, tmp_path, bw, N, seed=31 + bw)
     keydir = tmp_path / "keys"
-    r = run([bw, S, 0, 2, keydir, sampledir, B])
+    env = {"DDG_RELU_BACKEND": backend}
+    r = run([bw, S, 0, 2, keydir, sampledir, B], env=env)
     assert r.returncode == 0, r.stderr
     meta = json.loads((keydir / "meta.json").read_text())
-    assert (meta["B"], meta["NC"], meta["N"], meta["bw"]) == (B, 3, N, bw)
+    assert (meta["B"], meta["NC"], meta["N"], meta["bw"], meta["relu_backend"]) == (B, 3, N, bw, backend)
     for p in (0, 1):
         assert (keydir / f"DeepDTAGen_{bw}_{S}_party{p}_inference_key{p}.dat").stat().st_size > 0
-    r = run([bw, S, 1, 2, keydir, sampledir, B])
+    r = run([bw, S, 1, 2, keydir, sampledir, B], env=env)
     assert r.returncode == 0, r.stderr
     assert affinities(r.stdout) == want
+    # evaluators with the other backend expect another key layout and refuse the file
+    other = {"DDG_RELU_BACKEND": "dcf" if backend == "ot" else "ot"}
+    r = run([bw, S, 1, 2, keydir, sampledir, B], env=other)
+    assert r.returncode == 2
 
 
 @pytest.mark.gpu

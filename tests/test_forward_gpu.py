@@ -60,6 +60,34 @@ def test_forward_bit_exact(ddg, synth, cuda, bw):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("bw", [32, 64])
+@pytest.mark.parametrize("mode", ["split2", "ot"])
+def test_forward_bit_exact_other_relu_forms(ddg, synth, cuda, bw, mode):
+    """The two other ReLU comparison forms give the same revealed outputs:
+    the two-part DCF split and the OT-leaf backend (digit tables + AND tree,
+    several rounds per gate, its own key layout)."""
+    B = 3
+    try:
+        if mode == "ot":
+            ddg.relu_backend(ddg.RELU_OT)
+        else:
+            ddg.relu_split(2)
+        inp = synth.Inputs(B, bw, seed=22, with_protein_cnn=False)
+        q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=321)
+        ins, keep = dev_inputs(inp)
+        for _ in range(2):
+            raw, aff = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+            want_raw, want_aff = expected(inp, q, bw)
+            assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)), (raw, want_raw)
+            assert np.array_equal(aff, want_aff)
+        st = p0.stats()
+        assert st["key_bytes_used"] <= ddg.forward_key_bytes(bw, S, B)
+    finally:
+        ddg.relu_backend(ddg.RELU_DCF)
+        ddg.relu_split(3)
+
+
+@pytest.mark.gpu
 def test_forward_host_inputs_and_repeat(ddg, synth, cuda):
     """Host (pinned or pageable) share buffers; keys re-used for a second forward
     (timing-only key reuse, as the reference's benchmark loop rewinds keyBuf)."""
