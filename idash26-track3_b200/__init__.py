@@ -312,8 +312,8 @@ def relu_split(parts: int):
 
 
 def relu_backend(backend: int):
-    """Comparison backend of the forward's ReLU gates: RELU_DCF (default; DCF keys, split per
-    relu_split) or RELU_OT (garbled radix-16 digit tables + Beaver AND tree, GATE_RELU*_OT).
+    """Comparison backend of the forward's ReLU gates: RELU_OT (default; garbled radix-16 digit
+    tables + Beaver AND tree, GATE_RELU*_OT) or RELU_DCF (DCF keys, split per relu_split).
     Dealer and evaluators must use the same setting (it changes the key layout)."""
     check(lib().ddg_relu_backend(backend))
 

@@ -26,8 +26,8 @@
 //
 // Environment: DDG_WEIGHTS_BIN (default <sampledir>/weights.bin), DDG_NUM_CHUNKS
 // (default ceil(N / B)), DDG_SEED, DDG_DEVICE, DDG_PEER_PORT, DDG_RELU_SPLIT
-// (2 or 3) and DDG_RELU_BACKEND (dcf or ot); both must match between dealer
-// and evaluators.
+// (2 or 3) and DDG_RELU_BACKEND (ot, the default, or dcf); both must match
+// between dealer and evaluators.
 // Exit status 0 on success, 1 on usage errors, 2 on library or I/O errors.
 #include <arpa/inet.h>
 #include <fcntl.h>
@@ -229,10 +229,11 @@ int dealer(const Args &a)
     FILE *m = std::fopen((a.keydir + "/meta.json").c_str(), "w");
     if (m) {
         const char *be = std::getenv("DDG_RELU_BACKEND");
+        be = be && std::strcmp(be, "dcf") == 0 ? "dcf" : "ot";
         std::fprintf(m,
                      "{\n  \"B\": %d,\n  \"NC\": %ld,\n  \"N\": %llu,\n  \"bw\": %d,\n  \"scale\": %d,\n"
                      "  \"relu_backend\": \"%s\"\n}\n",
-                     a.B, NC, (unsigned long long)N, a.bw, a.scale, be && std::strcmp(be, "ot") == 0 ? "ot" : "dcf");
+                     a.B, NC, (unsigned long long)N, a.bw, a.scale, be);
         std::fclose(m);
     }
     std::fprintf(stderr, "dealer: %ld chunk(s) of B=%d, %.1f MB per chunk and party, %.2f s\n", NC, a.B, cb / 1e6, s);
@@ -390,7 +391,7 @@ int main(int argc, char **argv)
     check(ddg_relu_split(int(split)), "DDG_RELU_SPLIT");
     const char *be = std::getenv("DDG_RELU_BACKEND");
     if (be && std::strcmp(be, "ot") != 0 && std::strcmp(be, "dcf") != 0) die(1, "DDG_RELU_BACKEND must be dcf or ot");
-    check(ddg_relu_backend(be && std::strcmp(be, "ot") == 0 ? DDG_RELU_OT : DDG_RELU_DCF), "DDG_RELU_BACKEND");
+    check(ddg_relu_backend(be && std::strcmp(be, "dcf") == 0 ? DDG_RELU_DCF : DDG_RELU_OT), "DDG_RELU_BACKEND");
     ::mkdir(a.keydir.c_str(), 0755);
     return a.role == 0 ? dealer(a) : evaluate(a);
 }

@@ -149,6 +149,26 @@ static thread_local DcfTiming *t_dcf_sink = nullptr;
 DcfTiming *dcf_timing_sink() { return t_dcf_sink; }
 void set_dcf_timing_sink(DcfTiming *t) { t_dcf_sink = t; }
 
+int TimedLaunch::begin(cudaStream_t st)
+{
+    DcfTiming *tm = t_dcf_sink;
+    if (!tm || !tm->enabled || tm->nrec >= int(sizeof(tm->recs) / sizeof(tm->recs[0]))) return DDG_OK;
+    rec = &tm->recs[tm->nrec];
+    DDG_CUDA(cudaEventCreate(&rec->a));
+    DDG_CUDA(cudaEventCreate(&rec->b));
+    DDG_CUDA(cudaEventRecord(rec->a, st));
+    return DDG_OK;
+}
+
+int TimedLaunch::end(cudaStream_t st, double bytes, double aes, double evals)
+{
+    if (!rec) return DDG_OK;
+    DDG_CUDA(cudaEventRecord(rec->b, st));
+    rec->bytes = bytes, rec->aes = aes, rec->evals = evals;
+    t_dcf_sink->nrec++;
+    return DDG_OK;
+}
+
 // ----------------------------------------------------------------- errors
 
 static thread_local char t_err[512] = "";

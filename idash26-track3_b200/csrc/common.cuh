@@ -43,9 +43,10 @@ void set_last_error(const char *fmt, ...);
 void note_launch();
 uint64_t launch_count();
 
-// Optional timing of the DCF (gate round-1) kernels: when a thread has a
-// sink installed, every round-1 launch is bracketed by CUDA events on its
-// stream together with its algorithmic bytes and AES blocks.
+// Optional timing of the comparison kernels (DCF gate round 1; OT garble and
+// AND-tree levels): when a thread has a sink installed, every such launch is
+// bracketed by CUDA events on its stream together with its algorithmic bytes
+// and AES blocks.
 struct DcfTiming {
     struct Rec {
         cudaEvent_t a, b;
@@ -62,6 +63,13 @@ int keep_pool_memory(int device);
 
 DcfTiming *dcf_timing_sink();
 void set_dcf_timing_sink(DcfTiming *t);
+
+// brackets one comparison-kernel launch with events when a sink is installed
+struct TimedLaunch {
+    DcfTiming::Rec *rec = nullptr;
+    int begin(cudaStream_t st);
+    int end(cudaStream_t st, double bytes, double aes, double evals);
+};
 
 // ---------------------------------------------------------------- key layouts
 

@@ -609,9 +609,10 @@ struct EvalExec : ExecBase<T> {
 static std::atomic<int> g_relu_parts{3};
 void set_relu_parts(int parts) { g_relu_parts.store(parts == 2 ? 2 : 3); }
 static int relu_parts(int) { return g_relu_parts.load(); }
-// comparison backend of the ReLU gates: DCF keys (split per relu_parts) or
-// OT-leaf digit tables with a Beaver AND tree (GATE_RELU*_OT)
-static std::atomic<int> g_relu_backend{DDG_RELU_DCF};
+// comparison backend of the ReLU gates: OT-leaf digit tables with a Beaver
+// AND tree (GATE_RELU*_OT, default: 2 AES and ~8 key bytes per element and
+// party besides the words) or DCF keys (split per relu_parts)
+static std::atomic<int> g_relu_backend{DDG_RELU_OT};
 void set_relu_backend(int backend) { g_relu_backend.store(backend == DDG_RELU_OT ? DDG_RELU_OT : DDG_RELU_DCF); }
 int relu_backend() { return g_relu_backend.load(); }
 

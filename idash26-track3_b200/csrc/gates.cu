@@ -335,6 +335,12 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
             y = p0 * (q * xH - q * cl) + W(0) * (a1 * xH - a1 * cl) - q * W(1) - a1 * W(2) - q * b1 * W(3) -
                 a1 * b1 * W(4) + two_ns * (T(1) - mh) * (q * W(5) + a1 * W(6)) + W(7);
         } else if (KIND == GATE_RELU_SPLIT || KIND == GATE_RELU_ARS_SPLIT) {
+            // every dealer word of the element in flight at once (the kernel is HBM-bound)
+            constexpr int NWD = KIND == GATE_RELU_SPLIT ? 16 : 32;
+            T wv[NWD];
+#pragma unroll
+            for (int k = 0; k < NWD; k++) wv[k] = W(k);
+            auto W = [&](int k) { return wv[k]; };
             // DReLU = a0 + sum_k ak[k] * mono[k]  (mono: the dealer-bit monomials of the key words)
             const T se = T(1) - T(2) * eh, sc = b1;
             const T G0 = eh * cl, GL = eh * sc, Ge = cl * se, GeL = se * sc;
@@ -486,28 +492,18 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
     a.mid = L.mid ? dcf_view(k, L.Mi) : DcfView{};
     a.lo = L.lo ? dcf_view(k, L.Lo) : DcfView{};
     a.bits_hi = bits_hi, a.bits_lo = bits_lo;
-    DcfTiming *tm = dcf_timing_sink();
-    DcfTiming::Rec *rec = nullptr;
-    if (tm && tm->enabled && tm->nrec < int(sizeof(tm->recs) / sizeof(tm->recs[0]))) {
-        rec = &tm->recs[tm->nrec];
-        DDG_CUDA(cudaEventCreate(&rec->a));
-        DDG_CUDA(cudaEventCreate(&rec->b));
-        DDG_CUDA(cudaEventRecord(rec->a, st));
-    }
+    TimedLaunch tl;
+    DDG_TRY(tl.begin(st));
     DDG_TRY((aes_tables() == 4 ? round1_launch<T, AesLane4>(a, st) : round1_launch<T, AesLane2>(a, st)));
     note_launch();
     DDG_CUDA(cudaGetLastError());
-    if (rec) {
-        DDG_CUDA(cudaEventRecord(rec->b, st));
-        // algorithmic bytes: every key byte of the DCFs once, the input, the output bits
-        const double n = double(L.n);
-        double bytes = n * (L.bw / 8.0), aes = 0;
-        if (L.hi) bytes += n * (16.0 * (L.H.L + 2) + (L.H.eq ? 0.5 : 0.25)), aes += n * (L.H.L + 1);
-        if (L.mid) bytes += n * (16.0 * (L.Mi.L + 2) + 0.5), aes += n * (L.Mi.L + 1);
-        if (L.lo) bytes += n * (16.0 * (L.Lo.L + 2) + 0.125 + 0.125), aes += n * (L.Lo.L + 1);
-        rec->bytes = bytes, rec->aes = aes, rec->evals = n * ((L.hi ? 1 : 0) + (L.lo ? 1 : 0));
-        tm->nrec++;
-    }
+    // algorithmic bytes: every key byte of the DCFs once, the input, the output bits
+    const double n = double(L.n);
+    double bytes = n * (L.bw / 8.0), aes = 0;
+    if (L.hi) bytes += n * (16.0 * (L.H.L + 2) + (L.H.eq ? 0.5 : 0.25)), aes += n * (L.H.L + 1);
+    if (L.mid) bytes += n * (16.0 * (L.Mi.L + 2) + 0.5), aes += n * (L.Mi.L + 1);
+    if (L.lo) bytes += n * (16.0 * (L.Lo.L + 2) + 0.125 + 0.125), aes += n * (L.Lo.L + 1);
+    DDG_TRY(tl.end(st, bytes, aes, n * ((L.hi ? 1 : 0) + (L.lo ? 1 : 0))));
     return DDG_OK;
 }
 

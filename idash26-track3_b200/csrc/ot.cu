@@ -60,7 +60,43 @@ struct OtGarbleArgs {
     uint4 *tri;          // [naux][N] aux blocks
 };
 
-template <typename T, class E>
+// One element of party PARTY's first message.  With a compile-time plan every
+// digit's shift, width and bit offsets are constants after unrolling.
+template <int PARTY, typename T, class E>
+__device__ __forceinline__ void garble_elem(const E &A, const OtPlan &P, const OtGarbleArgs<T> &a, const uint32_t *rk,
+                                            uint64_t e)
+{
+    const uint64_t N = a.N;
+    const int G = P.garbled_by(PARTY), g0 = PARTY == 0 ? 0 : P.G0;
+    const uint64_t x = uint64_t(__ldcs(a.xhat + e));
+    const Blk x0 = A.prg(rk, 0, P_OT_AUX, e);
+    Blk x1 = x0;
+    if (P.naux > 1) x1 = A.prg(rk, 0, P_OT_AUX + 1, e);
+    uint64_t st = 0;
+    Blk pad = x0;
+#pragma unroll
+    for (int t = 0; t < OT_MAX_DIGITS / 2; t++) {
+        if (t >= G) break;
+        if ((t & 3) == 0) pad = A.prg(rk, 0, P_OT_PAD + uint32_t(t >> 2), e);
+        const int g = g0 + t, w = P.width(g);
+        const uint32_t wm = (1u << w) - 1u;
+        uint32_t delta = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) delta |= aux_bit(x0, x1, 6 * t + i) << i;
+        delta &= wm;
+        const uint32_t slt = aux_bit(x0, x1, 6 * t + 4), seq = aux_bit(x0, x1, 6 * t + 5);
+        const uint32_t xd = uint32_t(x >> P.shift(g)) & wm;
+        const uint32_t pw = (t & 3) == 0 ? pad.w[0] : (t & 3) == 1 ? pad.w[1] : (t & 3) == 2 ? pad.w[2] : pad.w[3];
+        __stcs(a.tables + uint64_t(t) * N + e, ot_table(xd, w, delta, slt, seq, pw));
+        st |= (uint64_t(slt) << (2 * g)) | (uint64_t(seq) << (2 * g + 1));
+    }
+    a.state[e] = st;
+    a.tri[e] = make_uint4(x0.w[0], x0.w[1], x0.w[2], x0.w[3]);
+    if (P.naux > 1) a.tri[N + e] = make_uint4(x1.w[0], x1.w[1], x1.w[2], x1.w[3]);
+}
+
+// NB, SB: the (bw, scale) whose plan is compiled in; 0, 0 = the plan in the arguments
+template <typename T, class E, int NB, int SB, int PARTY>
 __global__ void __launch_bounds__(E::THREADS, E::CTAS) ot_garble_kernel(const __grid_constant__ OtGarbleArgs<T> a)
 {
     extern __shared__ uint32_t smem_tab[];
@@ -69,33 +105,13 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) ot_garble_kernel(const __
     if (threadIdx.x < 44) rk[threadIdx.x] = a.ks[threadIdx.x];
     __syncthreads();
     E A(smem_tab);
-    const OtPlan &P = a.P;
-    const uint64_t N = a.N;
-    const int p = a.party, G = P.garbled_by(p), g0 = p == 0 ? 0 : P.G0;
-    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < N; e += uint64_t(gridDim.x) * blockDim.x) {
-        const uint64_t x = uint64_t(__ldcs(a.xhat + e));
-        const Blk x0 = A.prg(rk, 0, P_OT_AUX, e);
-        Blk x1 = x0;
-        if (P.naux > 1) x1 = A.prg(rk, 0, P_OT_AUX + 1, e);
-        uint64_t st = 0;
-        Blk pad = x0;
-        for (int t = 0; t < G; t++) {
-            if ((t & 3) == 0) pad = A.prg(rk, 0, P_OT_PAD + uint32_t(t >> 2), e);
-            const int g = g0 + t, w = P.width(g);
-            const uint32_t wm = (1u << w) - 1u;
-            uint32_t delta = 0;
-#pragma unroll
-            for (int i = 0; i < 4; i++) delta |= aux_bit(x0, x1, 6 * t + i) << i;
-            delta &= wm;
-            const uint32_t slt = aux_bit(x0, x1, 6 * t + 4), seq = aux_bit(x0, x1, 6 * t + 5);
-            const uint32_t xd = uint32_t(x >> P.shift(g)) & wm;
-            const uint32_t pw = (t & 3) == 0 ? pad.w[0] : (t & 3) == 1 ? pad.w[1] : (t & 3) == 2 ? pad.w[2] : pad.w[3];
-            a.tables[uint64_t(t) * N + e] = ot_table(xd, w, delta, slt, seq, pw);
-            st |= (uint64_t(slt) << (2 * g)) | (uint64_t(seq) << (2 * g + 1));
+    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < a.N; e += uint64_t(gridDim.x) * blockDim.x) {
+        if constexpr (NB != 0) {
+            constexpr OtPlan P = ot_plan(NB, SB);
+            garble_elem<PARTY>(A, P, a, rk, e);
+        } else {
+            garble_elem<PARTY>(A, a.P, a, rk, e);
         }
-        a.state[e] = st;
-        a.tri[e] = make_uint4(x0.w[0], x0.w[1], x0.w[2], x0.w[3]);
-        if (P.naux > 1) a.tri[N + e] = make_uint4(x1.w[0], x1.w[1], x1.w[2], x1.w[3]);
     }
 }
 
@@ -115,80 +131,104 @@ struct OtLevelArgs {
     uint32_t *bits_hi, *bits_lo; // level == levels + 1: masked comparison bits (split-gate layout)
 };
 
-__global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
+// One element of party PARTY at AND-tree level l (see ot_level): returns the
+// three masked output bits at the last level.
+template <int PARTY>
+__device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a, int l, uint64_t e, uint32_t &hl,
+                                           uint32_t &he, uint32_t &ll)
 {
-    const OtPlan &P = a.P;
     const uint64_t N = a.N;
-    const int p = a.party, l = a.level;
-    const uint64_t Npad = (N + 31) & ~uint64_t(31);
-    const uint32_t p0 = p == 0 ? 1u : 0u;
-    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
-        const bool valid = e < N;
-        uint32_t hl = 0, he = 0, ll = 0;
-        if (valid) {
-            uint64_t st = a.state[e];
-            const uint4 t0 = a.tri[e];
-            uint4 t1 = t0;
-            if (P.naux > 1) t1 = a.tri[N + e];
-            const Blk x0{{t0.x, t0.y, t0.z, t0.w}}, x1{{t1.x, t1.y, t1.z, t1.w}};
-            if (l == 1) {
-                // shares of the digits the peer garbled: T[c] ^ k_c
-                const int q = 1 - p, G = P.garbled_by(q), g0 = q == 0 ? 0 : P.G0;
-                for (int t = 0; t < G; t++) {
-                    const uint32_t rec = a.recv[uint64_t(t) * N + e];
-                    const uint32_t word = a.peer_tables[uint64_t(t) * N + e];
-                    const uint32_t c = rec & 15u;
-                    const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
-                    const int g = g0 + t;
-                    st |= (uint64_t(lt) << (2 * g)) | (uint64_t(eq) << (2 * g + 1));
-                }
-            } else {
-                // close level l - 1: z = c ^ f a ^ e b ^ [p = 0] e f
-                const uint32_t O = a.open_own[e] ^ a.open_peer[e];
-                const uint32_t cw = p == 0 ? a.c0[e] : 0u;
-                const int qa = P.lvl_first[l - 2], qb = P.lvl_first[l - 1];
-                for (int q = qa; q < qb; q++) {
-                    const OtComb &C = P.comb[q];
-                    const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
-                    const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
-                    const uint32_t ta = aux_bit(x0, x1, tb), tb1 = aux_bit(x0, x1, tb + 1),
-                                   tb2 = aux_bit(x0, x1, tb + 2);
-                    const uint32_t c = p == 0 ? (cw >> (2 * q)) & 1u : aux_bit(x0, x1, tb + 3);
-                    const uint32_t c2 = p == 0 ? (cw >> (2 * q + 1)) & 1u : aux_bit(x0, x1, tb + 4);
-                    const uint32_t lt = st_bit(st, base + 2 * C.h) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
-                    const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
-                    const int o = base + 2 * C.out;
-                    st = (st & ~(uint64_t(3) << o)) | (uint64_t(lt) << o) | (uint64_t(eq) << (o + 1));
-                }
+    constexpr uint32_t p0 = PARTY == 0 ? 1u : 0u;
+    uint64_t st = a.state[e];
+    const uint4 t0 = a.tri[e];
+    uint4 t1 = t0;
+    if (P.naux > 1) t1 = a.tri[N + e];
+    const Blk x0{{t0.x, t0.y, t0.z, t0.w}}, x1{{t1.x, t1.y, t1.z, t1.w}};
+    if (l == 1) {
+        // shares of the digits the peer garbled: T[c] ^ k_c
+        constexpr int q = 1 - PARTY;
+        const int G = P.garbled_by(q), g0 = q == 0 ? 0 : P.G0;
 #pragma unroll
-                for (int pt = 0; pt < 2; pt++) {
-                    const int from = P.pass_from[l - 1][pt];
-                    if (from >= 0) {
-                        const int b = 2 * P.base[pt], o = b + 2 * P.pass_to[l - 1][pt];
-                        const uint64_t v = (st >> (b + 2 * from)) & 3u;
-                        st = (st & ~(uint64_t(3) << o)) | (v << o);
-                    }
-                }
-            }
-            if (l <= P.levels) {
-                // open level l: e = eq_H ^ a, f = lt_L ^ b, f' = eq_L ^ b'
-                uint32_t w = 0;
-                const int qa = P.lvl_first[l - 1], qb = P.lvl_first[l];
-                for (int q = qa; q < qb; q++) {
-                    const OtComb &C = P.comb[q];
-                    const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
-                    const uint32_t eH = st_bit(st, base + 2 * C.h + 1), lL = st_bit(st, base + 2 * C.l),
-                                   eL = st_bit(st, base + 2 * C.l + 1);
-                    w |= ((eH ^ aux_bit(x0, x1, tb)) << (3 * j)) | ((lL ^ aux_bit(x0, x1, tb + 1)) << (3 * j + 1));
-                    if (C.eq) w |= (eL ^ aux_bit(x0, x1, tb + 2)) << (3 * j + 2);
-                }
-                a.open_out[e] = w;
-                a.state[e] = st;
-            } else {
-                hl = st_bit(st, 0), he = st_bit(st, 1), ll = st_bit(st, 2 * P.base[1]);
+        for (int t = 0; t < OT_MAX_DIGITS / 2; t++) {
+            if (t >= G) break;
+            const uint32_t rec = __ldcs(a.recv + uint64_t(t) * N + e);
+            const uint32_t word = __ldcs(a.peer_tables + uint64_t(t) * N + e);
+            const uint32_t c = rec & 15u;
+            const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
+            const int g = g0 + t;
+            st |= (uint64_t(lt) << (2 * g)) | (uint64_t(eq) << (2 * g + 1));
+        }
+    } else {
+        // close level l - 1: z = c ^ f a ^ e b ^ [p = 0] e f
+        const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
+        const uint32_t cw = PARTY == 0 ? __ldcs(a.c0 + e) : 0u;
+        const int qa = P.lvl_first[l - 2];
+#pragma unroll
+        for (int q = 0; q < OT_MAX_COMB; q++) {
+            if (q >= P.ncomb) break;
+            if (P.level_of(q) != l - 1) continue;
+            const OtComb &C = P.comb[q];
+            const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
+            const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
+            const uint32_t ta = aux_bit(x0, x1, tb), tb1 = aux_bit(x0, x1, tb + 1), tb2 = aux_bit(x0, x1, tb + 2);
+            const uint32_t c = PARTY == 0 ? (cw >> (2 * q)) & 1u : aux_bit(x0, x1, tb + 3);
+            const uint32_t c2 = PARTY == 0 ? (cw >> (2 * q + 1)) & 1u : aux_bit(x0, x1, tb + 4);
+            const uint32_t lt = st_bit(st, base + 2 * C.h) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
+            const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
+            const int o = base + 2 * C.out;
+            st = (st & ~(uint64_t(3) << o)) | (uint64_t(lt) << o) | (uint64_t(eq) << (o + 1));
+        }
+#pragma unroll
+        for (int pt = 0; pt < 2; pt++) {
+            const int from = P.pass_from[l - 1][pt];
+            if (from >= 0) {
+                const int b = 2 * P.base[pt], o = b + 2 * P.pass_to[l - 1][pt];
+                const uint64_t v = (st >> (b + 2 * from)) & 3u;
+                st = (st & ~(uint64_t(3) << o)) | (v << o);
             }
         }
-        if (l > P.levels) {
+    }
+    if (l <= P.levels) {
+        // open level l: e = eq_H ^ a, f = lt_L ^ b, f' = eq_L ^ b'
+        uint32_t w = 0;
+        const int qa = P.lvl_first[l - 1];
+#pragma unroll
+        for (int q = 0; q < OT_MAX_COMB; q++) {
+            if (q >= P.ncomb) break;
+            if (P.level_of(q) != l) continue;
+            const OtComb &C = P.comb[q];
+            const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
+            const uint32_t eH = st_bit(st, base + 2 * C.h + 1), lL = st_bit(st, base + 2 * C.l),
+                           eL = st_bit(st, base + 2 * C.l + 1);
+            w |= ((eH ^ aux_bit(x0, x1, tb)) << (3 * j)) | ((lL ^ aux_bit(x0, x1, tb + 1)) << (3 * j + 1));
+            if (C.eq) w |= (eL ^ aux_bit(x0, x1, tb + 2)) << (3 * j + 2);
+        }
+        a.open_out[e] = w;
+        a.state[e] = st;
+    } else {
+        hl = st_bit(st, 0), he = st_bit(st, 1), ll = st_bit(st, 2 * P.base[1]);
+    }
+}
+
+// LV: the level compiled in (0 = a.level)
+template <int NB, int SB, int PARTY, int LV>
+__global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
+{
+    const uint64_t N = a.N;
+    const int l = LV ? LV : a.level;
+    const uint64_t Npad = (N + 31) & ~uint64_t(31);
+    const bool last = l > a.P.levels;
+    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
+        uint32_t hl = 0, he = 0, ll = 0;
+        if (e < N) {
+            if constexpr (NB != 0) {
+                constexpr OtPlan P = ot_plan(NB, SB);
+                level_elem<PARTY>(P, a, l, e, hl, he, ll);
+            } else {
+                level_elem<PARTY>(a.P, a, l, e, hl, he, ll);
+            }
+        }
+        if (last) {
             const uint32_t wh = __ballot_sync(0xFFFFFFFFu, hl), we = __ballot_sync(0xFFFFFFFFu, he),
                            wl = __ballot_sync(0xFFFFFFFFu, ll);
             if ((threadIdx.x & 31) == 0) {
@@ -201,13 +241,23 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
 
 // ---------------------------------------------------------------- launchers
 
-template <typename T, class E>
+template <typename T, class E, int NB, int SB, int PARTY>
 static int garble_launch(const OtGarbleArgs<T> &a, cudaStream_t st)
 {
     const int smem = E::SMEM + 256;
-    DDG_CUDA(cudaFuncSetAttribute(ot_garble_kernel<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    ot_garble_kernel<T, E><<<aes_blocks<E>(a.N), E::THREADS, smem, st>>>(a);
+    auto k = ot_garble_kernel<T, E, NB, SB, PARTY>;
+    DDG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    k<<<aes_blocks<E>(a.N), E::THREADS, smem, st>>>(a);
     return DDG_OK;
+}
+
+// the plan compiled in for (bw, scale) = (32, 12) / (64, 12), else the runtime plan
+template <typename T, class E>
+static int garble_dispatch(const OtGarbleArgs<T> &a, int s, cudaStream_t st)
+{
+    constexpr int NB = sizeof(T) == 4 ? 32 : 64;
+    if (s == 12) return a.party == 0 ? garble_launch<T, E, NB, 12, 0>(a, st) : garble_launch<T, E, NB, 12, 1>(a, st);
+    return a.party == 0 ? garble_launch<T, E, 0, 0, 0>(a, st) : garble_launch<T, E, 0, 0, 1>(a, st);
 }
 
 int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, uint64_t *state,
@@ -217,21 +267,43 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
     if (L.n == 0) return DDG_OK;
     const OtPlan &P = ot_plan_cached(L.bw, L.s);
     DDG_CHECK(P.ok, DDG_ERR_ARG, "no OT-gate plan for bw %d, scale %d", L.bw, L.s);
+    DDG_CHECK(party == 0 || party == 1, DDG_ERR_ARG, "party must be 0 or 1");
     const uint8_t *k = static_cast<const uint8_t *>(key);
+    TimedLaunch tl;
+    DDG_TRY(tl.begin(st));
     if (L.bw == 32) {
         OtGarbleArgs<uint32_t> a{P, party, L.n, static_cast<const uint32_t *>(xhat),
                                  reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state,
                                  static_cast<uint4 *>(tri)};
-        DDG_TRY((aes_tables() == 4 ? garble_launch<uint32_t, AesLane4>(a, st) : garble_launch<uint32_t, AesLane2>(a, st)));
+        DDG_TRY((aes_tables() == 4 ? garble_dispatch<uint32_t, AesLane4>(a, L.s, st)
+                                   : garble_dispatch<uint32_t, AesLane2>(a, L.s, st)));
     } else {
         OtGarbleArgs<uint64_t> a{P, party, L.n, static_cast<const uint64_t *>(xhat),
                                  reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state,
                                  static_cast<uint4 *>(tri)};
-        DDG_TRY((aes_tables() == 4 ? garble_launch<uint64_t, AesLane4>(a, st) : garble_launch<uint64_t, AesLane2>(a, st)));
+        DDG_TRY((aes_tables() == 4 ? garble_dispatch<uint64_t, AesLane4>(a, L.s, st)
+                                   : garble_dispatch<uint64_t, AesLane2>(a, L.s, st)));
     }
     note_launch();
     DDG_CUDA(cudaGetLastError());
+    // algorithmic bytes: the input, the tables, the digit shares and the aux blocks written
+    const double n = double(L.n), G = P.garbled_by(party);
+    DDG_TRY(tl.end(st, n * (L.bw / 8.0 + 4.0 * G + 8.0 + 16.0 * P.naux), n * (P.naux + P.npad[party]), n));
     return DDG_OK;
+}
+
+// a compiled-in plan also compiles in the level (every node and bit offset a constant)
+template <int NB, int SB, int PARTY>
+static void level_launch(const OtLevelArgs &a, int grid, cudaStream_t st)
+{
+    switch (a.level) {
+    case 1: ot_level_kernel<NB, SB, PARTY, 1><<<grid, 256, 0, st>>>(a); break;
+    case 2: ot_level_kernel<NB, SB, PARTY, 2><<<grid, 256, 0, st>>>(a); break;
+    case 3: ot_level_kernel<NB, SB, PARTY, 3><<<grid, 256, 0, st>>>(a); break;
+    case 4: ot_level_kernel<NB, SB, PARTY, 4><<<grid, 256, 0, st>>>(a); break;
+    case 5: ot_level_kernel<NB, SB, PARTY, 5><<<grid, 256, 0, st>>>(a); break;
+    default: ot_level_kernel<NB, SB, PARTY, 0><<<grid, 256, 0, st>>>(a); break;
+    }
 }
 
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
@@ -253,9 +325,26 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     a.open_out = open_out, a.bits_hi = bits_hi, a.bits_lo = bits_lo;
     const int sms = device_sms();
     const uint64_t blocks = (L.n + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
-    ot_level_kernel<<<int(blocks < cap ? blocks : cap), 256, 0, st>>>(a);
+    const int grid = int(blocks < cap ? blocks : cap);
+    TimedLaunch tl;
+    DDG_TRY(tl.begin(st));
+    if (L.s == 12 && L.bw == 32)
+        party == 0 ? level_launch<32, 12, 0>(a, grid, st) : level_launch<32, 12, 1>(a, grid, st);
+    else if (L.s == 12)
+        party == 0 ? level_launch<64, 12, 0>(a, grid, st) : level_launch<64, 12, 1>(a, grid, st);
+    else
+        party == 0 ? ot_level_kernel<0, 0, 0, 0><<<grid, 256, 0, st>>>(a)
+                   : ot_level_kernel<0, 0, 1, 0><<<grid, 256, 0, st>>>(a);
     note_launch();
     DDG_CUDA(cudaGetLastError());
+    // algorithmic bytes: state and aux blocks in; level 1 the receiver records and
+    // the peer's tables, later levels both parties' openings (+ party 0's c
+    // word); state and openings out, or the three bit arrays at the last level
+    const double n = double(L.n), Gq = P.garbled_by(1 - party);
+    double bytes = n * (8.0 + 16.0 * P.naux);
+    bytes += level == 1 ? n * 5.0 * Gq : n * (8.0 + (party == 0 ? 4.0 : 0.0));
+    bytes += level <= P.levels ? n * 12.0 : n * 3.0 / 8.0;
+    DDG_TRY(tl.end(st, bytes, 0.0, n));
     return DDG_OK;
 }
 

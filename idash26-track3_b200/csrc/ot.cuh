@@ -94,23 +94,32 @@ struct OtPlan {
     int npad[2] = {0, 0};               // pad blocks of party 0 / 1
     bool ok = false;
 
-    __host__ __device__ int garbler(int g) const { return g < G0 ? 0 : 1; }
-    __host__ __device__ int local(int g) const { return g < G0 ? g : g - G0; }
-    __host__ __device__ int part_of(int g) const { return g < nd[0] ? 0 : 1; }
+    __host__ __device__ constexpr int garbler(int g) const { return g < G0 ? 0 : 1; }
+    __host__ __device__ constexpr int local(int g) const { return g < G0 ? g : g - G0; }
+    __host__ __device__ constexpr int part_of(int g) const { return g < nd[0] ? 0 : 1; }
     // bit position of digit g in x_hat / r, and its width
-    __host__ __device__ int shift(int g) const { return g < nd[0] ? s + OT_W * g : OT_W * (g - nd[0]); }
-    __host__ __device__ int width(int g) const
+    __host__ __device__ constexpr int shift(int g) const { return g < nd[0] ? s + OT_W * g : OT_W * (g - nd[0]); }
+    __host__ __device__ constexpr int width(int g) const
     {
         const int bits = g < nd[0] ? n - 1 - s : s;
         const int j = g < nd[0] ? g : g - nd[0];
         const int rem = bits - OT_W * j;
         return rem < OT_W ? rem : OT_W;
     }
-    __host__ __device__ int garbled_by(int p) const { return p == 0 ? G0 : D - G0; }
+    __host__ __device__ constexpr int garbled_by(int p) const { return p == 0 ? G0 : D - G0; }
+    // AND-tree level (1-based) of combine q
+    __host__ __device__ constexpr int level_of(int q) const
+    {
+        int l = 1;
+        while (l <= levels && q >= lvl_first[l]) l++;
+        return l;
+    }
 };
 
 // Plan for an n-bit ring and scale s: hi = bits [s, n-1), lo = bits [0, s).
-inline OtPlan ot_plan(int n, int s)
+// constexpr, so kernels specialised for a (bw, scale) see every digit, node
+// and bit position as a compile-time constant.
+__host__ __device__ constexpr OtPlan ot_plan(int n, int s)
 {
     OtPlan P;
     P.n = n, P.s = s;

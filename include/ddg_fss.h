@@ -348,15 +348,16 @@ int ddg_aes_chain_variant(uint64_t threads, int iters, int variant, uint32_t *d_
  * round column; 2 stages T0 and T2 in 64 KiB, three 256-thread CTAs per SM,
  * 8 instructions per column (T1 ^ T3 as an 8-bit rotation).  Same outputs. */
 int ddg_aes_tables(int tables);
-/* Comparison split of the forward's ReLU gates, process-wide: 3 (default,
+/* Comparison split of the forward's ReLU gates under the DCF backend
+ * (ddg_relu_backend(DDG_RELU_DCF)), process-wide: 3 (default,
  * DDG_GATE_RELU*_SPLIT3: fewest AES) or 2 (DDG_GATE_RELU*_SPLIT: smaller
- * keys, for key-streaming regimes).  It changes the key layout: the dealer
+ * keys).  It changes the key layout: the dealer
  * (ddg_dealer_forward, ddg_forward_key_bytes) and both evaluators must run
  * with the same setting. */
 int ddg_relu_split(int parts);
 /* Comparison backend of the forward's ReLU gates, process-wide:
- * DDG_RELU_DCF (default; the split chosen by ddg_relu_split) or DDG_RELU_OT
- * (DDG_GATE_RELU*_OT).  It changes the key layout like ddg_relu_split. */
+ * DDG_RELU_OT (default; DDG_GATE_RELU*_OT) or DDG_RELU_DCF (the split chosen
+ * by ddg_relu_split).  It changes the key layout like ddg_relu_split. */
 int ddg_relu_backend(int backend);
 
 /* Test and measurement helper: both parties of one gate on one device, every
