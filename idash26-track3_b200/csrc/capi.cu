@@ -139,14 +139,14 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
             ok(gate_round1(L, d_xhat, key[p], L.hi ? b[p] : nullptr, L.lo ? b[p] + nh * nw : nullptr, st));
     } else {
         const OtPlan &P = ot_plan_cached(bw, scale);
-        uint32_t *tab[2];
-        uint64_t *state[2];
-        void *tri[2];
+        const OtScratch sc = ot_scratch_bytes(L);
+        uint32_t *tab[2], *tri[2];
+        void *state[2];
         uint32_t *o[2][OT_MAX_LEVELS + 1] = {};
         for (int p = 0; p < 2; p++) {
-            tab[p] = static_cast<uint32_t *>(grab(4 * uint64_t(P.Gmax) * n));
-            state[p] = static_cast<uint64_t *>(grab(8 * n));
-            tri[p] = grab(16 * uint64_t(P.naux) * n);
+            tab[p] = static_cast<uint32_t *>(grab(sc.tables));
+            state[p] = grab(sc.state);
+            tri[p] = static_cast<uint32_t *>(grab(sc.tri));
             for (int l = 1; l <= P.levels; l++) o[p][l] = static_cast<uint32_t *>(grab(4 * n));
         }
         for (int p = 0; p < 2 && err == DDG_OK; p++) ok(ot_garble(L, p, d_xhat, key[p], tab[p], state[p], tri[p], st));

@@ -525,11 +525,12 @@ struct EvalExec : ExecBase<T> {
     {
         const OtPlan &Pl = ot_plan_cached(this->bw, this->s);
         const uint64_t n = x.n, nw = (n + 31) / 32;
-        uint32_t *tab = static_cast<uint32_t *>(this->alloc_bytes(4 * uint64_t(Pl.Gmax) * n));
-        uint64_t *state = static_cast<uint64_t *>(this->alloc_bytes(8 * n));
-        void *tri = this->alloc_bytes(16 * uint64_t(Pl.naux) * n);
+        const OtScratch sc = ot_scratch_bytes(L);
+        uint32_t *tab = static_cast<uint32_t *>(this->alloc_bytes(sc.tables));
+        void *state = this->alloc_bytes(sc.state);
+        uint32_t *tri = static_cast<uint32_t *>(this->alloc_bytes(sc.tri));
         if (this->err == DDG_OK) ok(ot_garble(L, p, x.v, k, tab, state, tri, this->st));
-        const uint32_t *ptab = reinterpret_cast<const uint32_t *>(peer_of(tab, 4 * uint64_t(Pl.Gmax) * n));
+        const uint32_t *ptab = reinterpret_cast<const uint32_t *>(peer_of(tab, sc.tables));
         const uint32_t *oo = nullptr, *po = nullptr;
         for (int l = 1; l <= Pl.levels; l++) {
             uint32_t *o = static_cast<uint32_t *>(this->alloc_bytes(4 * n));

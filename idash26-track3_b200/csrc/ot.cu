@@ -44,7 +44,37 @@ __device__ __forceinline__ uint32_t aux_bit(const Blk &a0, const Blk &a1, int i)
     return uint32_t(blk_bit(i < 128 ? a0 : a1, uint32_t(i & 127)));
 }
 
-__device__ __forceinline__ uint32_t st_bit(uint64_t st, int i) { return uint32_t(st >> i) & 1u; }
+template <typename ST>
+__device__ __forceinline__ uint32_t st_bit(ST st, int i) { return uint32_t(st >> i) & 1u; }
+
+// 32 bits of the concatenated aux blocks x0 || x1 from bit pos (pos + 32 <= 256)
+__device__ __forceinline__ uint32_t aux_word(const Blk &x0, const Blk &x1, int pos)
+{
+    const int k = pos >> 5, r = pos & 31;
+    auto w = [&](int i) { return i < 4 ? (i == 0 ? x0.w[0] : i == 1 ? x0.w[1] : i == 2 ? x0.w[2] : x0.w[3])
+                                       : (i == 4 ? x1.w[0] : i == 5 ? x1.w[1] : i == 6 ? x1.w[2] : x1.w[3]); };
+    const uint32_t lo = w(k), hi = k + 1 < 8 ? w(k + 1) : 0u;
+    return r ? __funnelshift_r(lo, hi, uint32_t(r)) : lo;
+}
+
+// triple bit i (= 5q + field) of the stored triple words
+__device__ __forceinline__ uint32_t tri_bit(const uint32_t (&t)[3], int i)
+{
+    const int k = i >> 5;
+    return ((k == 0 ? t[0] : k == 1 ? t[1] : t[2]) >> (i & 31)) & 1u;
+}
+
+// the digit-share state: 32 bits when 2 D <= 32 (every specialised plan), else 64
+template <typename ST>
+__device__ __forceinline__ ST load_state(const void *state, uint64_t e)
+{
+    return static_cast<const ST *>(state)[e];
+}
+template <typename ST>
+__device__ __forceinline__ void store_state(void *state, uint64_t e, ST st)
+{
+    static_cast<ST *>(state)[e] = st;
+}
 
 // ---------------------------------------------------------------- garble
 
@@ -56,13 +86,13 @@ struct OtGarbleArgs {
     const T *xhat;
     const uint32_t *ks;  // the party's 44 round keys in its gate key
     uint32_t *tables;    // [local digit][N]
-    uint64_t *state;     // [N] digit shares of the garbled digits
-    uint4 *tri;          // [naux][N] aux blocks
+    void *state;         // [N] digit shares of the garbled digits (u32 or u64)
+    uint32_t *tri;       // [tri_words][N] triple bits
 };
 
 // One element of party PARTY's first message.  With a compile-time plan every
 // digit's shift, width and bit offsets are constants after unrolling.
-template <int PARTY, typename T, class E>
+template <int PARTY, typename ST, typename T, class E>
 __device__ __forceinline__ void garble_elem(const E &A, const OtPlan &P, const OtGarbleArgs<T> &a, const uint32_t *rk,
                                             uint64_t e)
 {
@@ -72,7 +102,7 @@ __device__ __forceinline__ void garble_elem(const E &A, const OtPlan &P, const O
     const Blk x0 = A.prg(rk, 0, P_OT_AUX, e);
     Blk x1 = x0;
     if (P.naux > 1) x1 = A.prg(rk, 0, P_OT_AUX + 1, e);
-    uint64_t st = 0;
+    ST st = 0;
     Blk pad = x0;
 #pragma unroll
     for (int t = 0; t < OT_MAX_DIGITS / 2; t++) {
@@ -88,11 +118,12 @@ __device__ __forceinline__ void garble_elem(const E &A, const OtPlan &P, const O
         const uint32_t xd = uint32_t(x >> P.shift(g)) & wm;
         const uint32_t pw = (t & 3) == 0 ? pad.w[0] : (t & 3) == 1 ? pad.w[1] : (t & 3) == 2 ? pad.w[2] : pad.w[3];
         __stcs(a.tables + uint64_t(t) * N + e, ot_table(xd, w, delta, slt, seq, pw));
-        st |= (uint64_t(slt) << (2 * g)) | (uint64_t(seq) << (2 * g + 1));
+        st |= (ST(slt) << (2 * g)) | (ST(seq) << (2 * g + 1));
     }
-    a.state[e] = st;
-    a.tri[e] = make_uint4(x0.w[0], x0.w[1], x0.w[2], x0.w[3]);
-    if (P.naux > 1) a.tri[N + e] = make_uint4(x1.w[0], x1.w[1], x1.w[2], x1.w[3]);
+    store_state<ST>(a.state, e, st);
+#pragma unroll
+    for (int w = 0; w < 3; w++)
+        if (w < P.tri_words()) a.tri[uint64_t(w) * N + e] = aux_word(x0, x1, P.tri0 + 32 * w);
 }
 
 // NB, SB: the (bw, scale) whose plan is compiled in; 0, 0 = the plan in the arguments
@@ -108,9 +139,12 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) ot_garble_kernel(const __
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < a.N; e += uint64_t(gridDim.x) * blockDim.x) {
         if constexpr (NB != 0) {
             constexpr OtPlan P = ot_plan(NB, SB);
-            garble_elem<PARTY>(A, P, a, rk, e);
+            static_assert(P.state_bytes() == 4, "compiled-in plans keep a 32-bit state");
+            garble_elem<PARTY, uint32_t>(A, P, a, rk, e);
+        } else if (a.P.state_bytes() == 4) {
+            garble_elem<PARTY, uint32_t>(A, a.P, a, rk, e);
         } else {
-            garble_elem<PARTY>(A, a.P, a, rk, e);
+            garble_elem<PARTY, uint64_t>(A, a.P, a, rk, e);
         }
     }
 }
@@ -125,25 +159,25 @@ struct OtLevelArgs {
     const uint32_t *peer_tables; // level 1: the peer's tables [slot][N]
     const uint32_t *c0;          // party 0's explicit triple c bits [N]
     const uint32_t *open_own, *open_peer;  // level >= 2: the previous level's openings
-    uint64_t *state;
-    const uint4 *tri;
+    void *state;
+    const uint32_t *tri;         // [tri_words][N]
     uint32_t *open_out;          // level <= levels
     uint32_t *bits_hi, *bits_lo; // level == levels + 1: masked comparison bits (split-gate layout)
 };
 
 // One element of party PARTY at AND-tree level l (see ot_level): returns the
 // three masked output bits at the last level.
-template <int PARTY>
+template <int PARTY, typename ST>
 __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a, int l, uint64_t e, uint32_t &hl,
                                            uint32_t &he, uint32_t &ll)
 {
     const uint64_t N = a.N;
     constexpr uint32_t p0 = PARTY == 0 ? 1u : 0u;
-    uint64_t st = a.state[e];
-    const uint4 t0 = a.tri[e];
-    uint4 t1 = t0;
-    if (P.naux > 1) t1 = a.tri[N + e];
-    const Blk x0{{t0.x, t0.y, t0.z, t0.w}}, x1{{t1.x, t1.y, t1.z, t1.w}};
+    ST st = load_state<ST>(a.state, e);
+    uint32_t tw[3] = {0u, 0u, 0u};
+#pragma unroll
+    for (int w = 0; w < 3; w++)
+        if (w < P.tri_words()) tw[w] = __ldcs(a.tri + uint64_t(w) * N + e);
     if (l == 1) {
         // shares of the digits the peer garbled: T[c] ^ k_c
         constexpr int q = 1 - PARTY;
@@ -156,7 +190,7 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             const uint32_t c = rec & 15u;
             const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
             const int g = g0 + t;
-            st |= (uint64_t(lt) << (2 * g)) | (uint64_t(eq) << (2 * g + 1));
+            st |= (ST(lt) << (2 * g)) | (ST(eq) << (2 * g + 1));
         }
     } else {
         // close level l - 1: z = c ^ f a ^ e b ^ [p = 0] e f
@@ -168,23 +202,23 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             if (q >= P.ncomb) break;
             if (P.level_of(q) != l - 1) continue;
             const OtComb &C = P.comb[q];
-            const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
+            const int j = q - qa, tb = 5 * q, base = 2 * P.base[C.part];
             const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
-            const uint32_t ta = aux_bit(x0, x1, tb), tb1 = aux_bit(x0, x1, tb + 1), tb2 = aux_bit(x0, x1, tb + 2);
-            const uint32_t c = PARTY == 0 ? (cw >> (2 * q)) & 1u : aux_bit(x0, x1, tb + 3);
-            const uint32_t c2 = PARTY == 0 ? (cw >> (2 * q + 1)) & 1u : aux_bit(x0, x1, tb + 4);
+            const uint32_t ta = tri_bit(tw, tb), tb1 = tri_bit(tw, tb + 1), tb2 = tri_bit(tw, tb + 2);
+            const uint32_t c = PARTY == 0 ? (cw >> (2 * q)) & 1u : tri_bit(tw, tb + 3);
+            const uint32_t c2 = PARTY == 0 ? (cw >> (2 * q + 1)) & 1u : tri_bit(tw, tb + 4);
             const uint32_t lt = st_bit(st, base + 2 * C.h) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
             const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
             const int o = base + 2 * C.out;
-            st = (st & ~(uint64_t(3) << o)) | (uint64_t(lt) << o) | (uint64_t(eq) << (o + 1));
+            st = (st & ~(ST(3) << o)) | (ST(lt) << o) | (ST(eq) << (o + 1));
         }
 #pragma unroll
         for (int pt = 0; pt < 2; pt++) {
             const int from = P.pass_from[l - 1][pt];
             if (from >= 0) {
                 const int b = 2 * P.base[pt], o = b + 2 * P.pass_to[l - 1][pt];
-                const uint64_t v = (st >> (b + 2 * from)) & 3u;
-                st = (st & ~(uint64_t(3) << o)) | (v << o);
+                const ST v = (st >> (b + 2 * from)) & ST(3);
+                st = (st & ~(ST(3) << o)) | (v << o);
             }
         }
     }
@@ -197,14 +231,14 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             if (q >= P.ncomb) break;
             if (P.level_of(q) != l) continue;
             const OtComb &C = P.comb[q];
-            const int j = q - qa, tb = P.tri0 + 5 * q, base = 2 * P.base[C.part];
+            const int j = q - qa, tb = 5 * q, base = 2 * P.base[C.part];
             const uint32_t eH = st_bit(st, base + 2 * C.h + 1), lL = st_bit(st, base + 2 * C.l),
                            eL = st_bit(st, base + 2 * C.l + 1);
-            w |= ((eH ^ aux_bit(x0, x1, tb)) << (3 * j)) | ((lL ^ aux_bit(x0, x1, tb + 1)) << (3 * j + 1));
-            if (C.eq) w |= (eL ^ aux_bit(x0, x1, tb + 2)) << (3 * j + 2);
+            w |= ((eH ^ tri_bit(tw, tb)) << (3 * j)) | ((lL ^ tri_bit(tw, tb + 1)) << (3 * j + 1));
+            if (C.eq) w |= (eL ^ tri_bit(tw, tb + 2)) << (3 * j + 2);
         }
         a.open_out[e] = w;
-        a.state[e] = st;
+        store_state<ST>(a.state, e, st);
     } else {
         hl = st_bit(st, 0), he = st_bit(st, 1), ll = st_bit(st, 2 * P.base[1]);
     }
@@ -223,9 +257,11 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
         if (e < N) {
             if constexpr (NB != 0) {
                 constexpr OtPlan P = ot_plan(NB, SB);
-                level_elem<PARTY>(P, a, l, e, hl, he, ll);
+                level_elem<PARTY, uint32_t>(P, a, l, e, hl, he, ll);
+            } else if (a.P.state_bytes() == 4) {
+                level_elem<PARTY, uint32_t>(a.P, a, l, e, hl, he, ll);
             } else {
-                level_elem<PARTY>(a.P, a, l, e, hl, he, ll);
+                level_elem<PARTY, uint64_t>(a.P, a, l, e, hl, he, ll);
             }
         }
         if (last) {
@@ -260,8 +296,8 @@ static int garble_dispatch(const OtGarbleArgs<T> &a, int s, cudaStream_t st)
     return a.party == 0 ? garble_launch<T, E, 0, 0, 0>(a, st) : garble_launch<T, E, 0, 0, 1>(a, st);
 }
 
-int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, uint64_t *state,
-              void *tri, cudaStream_t st)
+int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, void *state,
+              uint32_t *tri, cudaStream_t st)
 {
     DDG_TRY(aes_device_init());
     if (L.n == 0) return DDG_OK;
@@ -273,14 +309,12 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
     DDG_TRY(tl.begin(st));
     if (L.bw == 32) {
         OtGarbleArgs<uint32_t> a{P, party, L.n, static_cast<const uint32_t *>(xhat),
-                                 reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state,
-                                 static_cast<uint4 *>(tri)};
+                                 reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state, tri};
         DDG_TRY((aes_tables() == 4 ? garble_dispatch<uint32_t, AesLane4>(a, L.s, st)
                                    : garble_dispatch<uint32_t, AesLane2>(a, L.s, st)));
     } else {
         OtGarbleArgs<uint64_t> a{P, party, L.n, static_cast<const uint64_t *>(xhat),
-                                 reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state,
-                                 static_cast<uint4 *>(tri)};
+                                 reinterpret_cast<const uint32_t *>(k + L.ot_ks), tables, state, tri};
         DDG_TRY((aes_tables() == 4 ? garble_dispatch<uint64_t, AesLane4>(a, L.s, st)
                                    : garble_dispatch<uint64_t, AesLane2>(a, L.s, st)));
     }
@@ -288,7 +322,8 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
     DDG_CUDA(cudaGetLastError());
     // algorithmic bytes: the input, the tables, the digit shares and the aux blocks written
     const double n = double(L.n), G = P.garbled_by(party);
-    DDG_TRY(tl.end(st, n * (L.bw / 8.0 + 4.0 * G + 8.0 + 16.0 * P.naux), n * (P.naux + P.npad[party]), n));
+    DDG_TRY(tl.end(st, n * (L.bw / 8.0 + 4.0 * G + P.state_bytes() + 4.0 * P.tri_words()), n * (P.naux + P.npad[party]),
+                   n));
     return DDG_OK;
 }
 
@@ -307,7 +342,7 @@ static void level_launch(const OtLevelArgs &a, int grid, cudaStream_t st)
 }
 
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
-             const uint32_t *open_own, const uint32_t *open_peer, uint64_t *state, const void *tri,
+             const uint32_t *open_own, const uint32_t *open_peer, void *state, const uint32_t *tri,
              uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st)
 {
     if (L.n == 0) return DDG_OK;
@@ -321,7 +356,7 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     a.c0 = reinterpret_cast<const uint32_t *>(k + L.ot_c0);
     a.open_own = open_own, a.open_peer = open_peer;
     a.state = state;
-    a.tri = static_cast<const uint4 *>(tri);
+    a.tri = tri;
     a.open_out = open_out, a.bits_hi = bits_hi, a.bits_lo = bits_lo;
     const int sms = device_sms();
     const uint64_t blocks = (L.n + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
@@ -341,17 +376,18 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     // the peer's tables, later levels both parties' openings (+ party 0's c
     // word); state and openings out, or the three bit arrays at the last level
     const double n = double(L.n), Gq = P.garbled_by(1 - party);
-    double bytes = n * (8.0 + 16.0 * P.naux);
+    double bytes = n * (P.state_bytes() + 4.0 * P.tri_words());
     bytes += level == 1 ? n * 5.0 * Gq : n * (8.0 + (party == 0 ? 4.0 : 0.0));
-    bytes += level <= P.levels ? n * 12.0 : n * 3.0 / 8.0;
+    bytes += level <= P.levels ? n * (4.0 + P.state_bytes()) : n * 3.0 / 8.0;
     DDG_TRY(tl.end(st, bytes, 0.0, n));
     return DDG_OK;
 }
 
-uint64_t ot_scratch_bytes(const GateLayout &L)
+OtScratch ot_scratch_bytes(const GateLayout &L)
 {
     const OtPlan &P = ot_plan_cached(L.bw, L.s);
-    return uint64_t(L.n) * (4ull * P.Gmax + 8 + 16ull * P.naux);
+    const uint64_t n = L.n;
+    return OtScratch{4ull * uint64_t(P.Gmax) * n, uint64_t(P.state_bytes()) * n, 4ull * uint64_t(P.tri_words()) * n};
 }
 
 }  // namespace ddg

@@ -107,6 +107,10 @@ struct OtPlan {
         return rem < OT_W ? rem : OT_W;
     }
     __host__ __device__ constexpr int garbled_by(int p) const { return p == 0 ? G0 : D - G0; }
+    // evaluator scratch per element: digit-share state (2 bits per node) and
+    // the triple bits (a, b, b', c1, c1') of every combine, 32-bit words
+    __host__ __device__ constexpr int state_bytes() const { return 2 * D <= 32 ? 4 : 8; }
+    __host__ __device__ constexpr int tri_words() const { return (5 * ncomb + 31) / 32; }
     // AND-tree level (1-based) of combine q
     __host__ __device__ constexpr int level_of(int q) const
     {
@@ -234,17 +238,20 @@ const OtPlan &ot_plan_cached(int bw, int s);
 // K_p = AES_dk(p || op || P_OT_PARTY), expanded
 AesKey ot_party_key(const AesKey &dk, uint32_t op, int party);
 // party's first message: its garbled tables [Gmax][N] u32, its digit shares
-// (state[N]) and its aux blocks (tri: naux x N x 16 bytes)
-int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, uint64_t *state,
-              void *tri, cudaStream_t st);
+// (state: N x state_bytes()) and its triple bits (tri: [tri_words()][N] u32)
+int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, void *state,
+              uint32_t *tri, cudaStream_t st);
 // level 1..levels: (level 1: take the peer's tables) close the previous level
 // with both parties' openings, open this level's ANDs into open_out;
 // level levels + 1: close the last level and write the masked comparison bits
 // (bits_hi: [lt | eq] x ceil(N/32) words, bits_lo: lt)
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
-             const uint32_t *open_own, const uint32_t *open_peer, uint64_t *state, const void *tri,
+             const uint32_t *open_own, const uint32_t *open_peer, void *state, const uint32_t *tri,
              uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st);
-// scratch of one party's OT gate: tables + state + aux blocks
-uint64_t ot_scratch_bytes(const GateLayout &L);
+// scratch of one party's OT gate, bytes: garbled tables, state, triple bits
+struct OtScratch {
+    uint64_t tables, state, tri;
+};
+OtScratch ot_scratch_bytes(const GateLayout &L);
 
 }  // namespace ddg
