@@ -93,9 +93,10 @@ def parse():
     ap.add_argument("--relu-split", type=int, default=0, choices=[0, 2, 3],
                     help="comparison split of the ReLU gates: 3 parts (fewest AES) or 2 (smaller keys); "
                          "0 = 3 with resident keys, 2 with --stream")
-    ap.add_argument("--relu-backend", default="ot", choices=["ot", "dcf"],
-                    help="comparison backend of the ReLU gates: OT-leaf digit tables with a Beaver AND tree "
-                         "(default) or DCF keys (split per --relu-split)")
+    ap.add_argument("--relu-backend", default="tt", choices=["tt", "ot", "dcf"],
+                    help="comparison backend of the ReLU and truncation gates: dealer digit truth tables with a "
+                         "Beaver AND tree (default), OT-leaf digit tables with the same tree (ReLU only), or DCF "
+                         "keys (split per --relu-split)")
     ap.add_argument("--gemm", default="tensor", choices=["tensor", "cuda-cores"],
                     help="ring GEMM engine: tcgen05 limb products (default) or the CUDA-core kernel")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
@@ -346,7 +347,7 @@ def main():
     ddg.gemm_path(ddg.GEMM_TENSOR if a.gemm == "tensor" else ddg.GEMM_CUDA_CORES)
     ddg.aes_tables(a.aes_tables)
     ddg.relu_split(a.relu_split)
-    ddg.relu_backend(ddg.RELU_OT if a.relu_backend == "ot" else ddg.RELU_DCF)
+    ddg.relu_backend({"tt": ddg.RELU_TT, "ot": ddg.RELU_OT, "dcf": ddg.RELU_DCF}[a.relu_backend])
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None
@@ -527,9 +528,11 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": peak_kind,
                 "traffic": (alg / nl * NCU_DRAM_BYTES_PER_ALG_BYTE) if (nl and NCU_DRAM_BYTES_PER_ALG_BYTE) else None,
-                "kernel": ("comparison kernels: ot_garble_kernel + ot_level_kernel (ReLU gates) and "
-                           "gate_round1_kernel (DCF, truncation gates)" if a.relu_backend == "ot" else
-                           "gate_round1_kernel (DCF evaluation)"), "launches": nl,
+                "kernel": {"tt": "comparison kernels: ot_level_kernel (truth tables + AND-tree levels of the "
+                                 "ReLU and truncation gates)",
+                           "ot": "comparison kernels: ot_garble_kernel + ot_level_kernel (ReLU gates) and "
+                                 "gate_round1_kernel (DCF, truncation gates)",
+                           "dcf": "gate_round1_kernel (DCF evaluation)"}[a.relu_backend], "launches": nl,
                 "dcf_share_of_step": union / ms if ms > 0 else None,
                 "aes_gblocks_per_s": aes / (union / 1e3) / 1e9 if union > 0 else 0.0}
     # AES ceiling on this GPU (the binding roofline of the DCF): fixed-key hash chains

@@ -19,9 +19,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libddg.so")
 
 (GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
- GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT) = range(11)
+ GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT, GATE_RELU_TT, GATE_RELU_ARS_TT,
+ GATE_LRS_TT) = range(14)
 # comparison backends of the forward's ReLU gates (relu_backend)
-RELU_DCF, RELU_OT = 0, 1
+RELU_DCF, RELU_OT, RELU_TT = 0, 1, 2
 
 DDG_OK = 0
 _STATUS = {1: "DDG_ERR_ARG", 2: "DDG_ERR_CUDA", 3: "DDG_ERR_KEY", 4: "DDG_ERR_PEER", 5: "DDG_ERR_STATE",
@@ -48,6 +49,7 @@ SIGNATURES = {
     "ddg_gate_round1": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_gate_round2": (_i32, [_i32, _i32, _i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_ot_key_layout": (_i32, [_i32, _i32, _i32, _u64, ctypes.POINTER(_u64)]),
+    "ddg_tt_key_layout": (_i32, [_i32, _i32, _i32, _u64, ctypes.POINTER(_u64)]),
     "ddg_gate_eval_pair_noalloc": (_i32, [_i32, _i32, _i32, _u64, _vp, _vp, _vp, _vp, _vp]),
     "ddg_lut_key_bytes": (_u64, [_i32, _u64]),
     "ddg_lut_keygen": (_i32, [_i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
@@ -140,6 +142,14 @@ def ot_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
     out = (_u64 * 10)()
     check(lib().ddg_ot_key_layout(kind, bw, scale, n, out))
     keys = ("ks", "recv", "c0", "words", "bytes", "slots", "digits", "g0", "levels", "combines")
+    return {k: int(v) for k, v in zip(keys, out)}
+
+
+def tt_key_layout(kind: int, bw: int, scale: int, n: int) -> dict:
+    """Byte offsets and plan of one party's truth-table gate key (see ddg_tt_key_layout)."""
+    out = (_u64 * 8)()
+    check(lib().ddg_tt_key_layout(kind, bw, scale, n, out))
+    keys = ("tables", "rows", "tri", "tri_words", "words", "bytes", "digits", "levels")
     return {k: int(v) for k, v in zip(keys, out)}
 
 
@@ -312,8 +322,9 @@ def relu_split(parts: int):
 
 
 def relu_backend(backend: int):
-    """Comparison backend of the forward's ReLU gates: RELU_OT (default; garbled radix-16 digit
-    tables + Beaver AND tree, GATE_RELU*_OT) or RELU_DCF (DCF keys, split per relu_split).
+    """Comparison backend of the forward's ReLU gates: RELU_TT (default; dealer digit truth tables +
+    Beaver AND tree, GATE_RELU*_TT, and GATE_LRS_TT at the truncation sites), RELU_OT (garbled
+    radix-16 digit tables + the same tree, GATE_RELU*_OT) or RELU_DCF (DCF keys, split per relu_split).
     Dealer and evaluators must use the same setting (it changes the key layout)."""
     check(lib().ddg_relu_backend(backend))
 

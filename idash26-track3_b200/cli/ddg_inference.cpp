@@ -26,8 +26,8 @@
 //
 // Environment: DDG_WEIGHTS_BIN (default <sampledir>/weights.bin), DDG_NUM_CHUNKS
 // (default ceil(N / B)), DDG_SEED, DDG_DEVICE, DDG_PEER_PORT, DDG_RELU_SPLIT
-// (2 or 3) and DDG_RELU_BACKEND (ot, the default, or dcf); both must match
-// between dealer and evaluators.
+// (2 or 3) and DDG_RELU_BACKEND (tt, the default, ot or dcf); both must
+// match between dealer and evaluators.
 // Exit status 0 on success, 1 on usage errors, 2 on library or I/O errors.
 #include <arpa/inet.h>
 #include <fcntl.h>
@@ -75,6 +75,17 @@ long env_long(const char *name, long dflt)
 {
     const char *v = std::getenv(name);
     return v && *v ? std::strtol(v, nullptr, 10) : dflt;
+}
+
+// DDG_RELU_BACKEND: tt (default), ot or dcf
+int relu_backend_env()
+{
+    const char *v = std::getenv("DDG_RELU_BACKEND");
+    if (!v || !*v || std::strcmp(v, "tt") == 0) return DDG_RELU_TT;
+    if (std::strcmp(v, "ot") == 0) return DDG_RELU_OT;
+    if (std::strcmp(v, "dcf") == 0) return DDG_RELU_DCF;
+    die(1, "DDG_RELU_BACKEND must be tt, ot or dcf");
+    return DDG_RELU_TT;
 }
 
 std::string env_str(const char *name, const std::string &dflt)
@@ -228,8 +239,8 @@ int dealer(const Args &a)
     const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     FILE *m = std::fopen((a.keydir + "/meta.json").c_str(), "w");
     if (m) {
-        const char *be = std::getenv("DDG_RELU_BACKEND");
-        be = be && std::strcmp(be, "dcf") == 0 ? "dcf" : "ot";
+        const char *names[3] = {"dcf", "ot", "tt"};
+        const char *be = names[relu_backend_env()];
         std::fprintf(m,
                      "{\n  \"B\": %d,\n  \"NC\": %ld,\n  \"N\": %llu,\n  \"bw\": %d,\n  \"scale\": %d,\n"
                      "  \"relu_backend\": \"%s\"\n}\n",
@@ -389,9 +400,7 @@ int main(int argc, char **argv)
         die(1, "bad arguments (bw 32|64, role 0|1, party 0|1|2, B > 0)");
     const long split = env_long("DDG_RELU_SPLIT", 3);
     check(ddg_relu_split(int(split)), "DDG_RELU_SPLIT");
-    const char *be = std::getenv("DDG_RELU_BACKEND");
-    if (be && std::strcmp(be, "ot") != 0 && std::strcmp(be, "dcf") != 0) die(1, "DDG_RELU_BACKEND must be dcf or ot");
-    check(ddg_relu_backend(be && std::strcmp(be, "dcf") == 0 ? DDG_RELU_DCF : DDG_RELU_OT), "DDG_RELU_BACKEND");
+    check(ddg_relu_backend(relu_backend_env()), "DDG_RELU_BACKEND");
     ::mkdir(a.keydir.c_str(), 0755);
     return a.role == 0 ? dealer(a) : evaluate(a);
 }

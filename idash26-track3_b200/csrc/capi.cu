@@ -15,7 +15,7 @@ using namespace ddg;
 
 static int check_gate_args(int kind, int bw, int scale)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_OT, DDG_ERR_ARG, "gate kind %d out of range", kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS_TT, DDG_ERR_ARG, "gate kind %d out of range", kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
     DDG_CHECK(kind != DDG_GATE_LRS_SPLIT || scale >= 2, DDG_ERR_ARG, "split LRS needs scale >= 2 (got %d)", scale);
@@ -23,6 +23,8 @@ static int check_gate_args(int kind, int bw, int scale)
               "three-part split needs scale + %d < bw - 1 (scale %d, bw %d)", SPLIT3_MID, scale, bw);
     DDG_CHECK(!gate_is_ot(kind) || ot_plan_cached(bw, scale).ok, DDG_ERR_ARG, "no OT-gate plan for bw %d, scale %d",
               bw, scale);
+    DDG_CHECK(!gate_is_tt(kind) || tt_plan_of(kind, bw, scale).ok, DDG_ERR_ARG,
+              "no truth-table plan for bw %d, scale %d", bw, scale);
     return DDG_OK;
 }
 
@@ -102,6 +104,7 @@ int ddg_gate_round1_arrays(int kind, int bw, int scale)
     if (check_gate_args(kind, bw, scale) != DDG_OK) return 0;
     GateLayout L = gate_layout(kind, bw, scale, 1);
     if (L.ot) return 3;
+    if (L.tt) return kind == GATE_LRS_TT ? 1 : 3;
     return (L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0) + (L.lo ? 1 : 0);
 }
 
@@ -115,7 +118,7 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     GateLayout L = gate_layout(kind, bw, scale, n);
     const uint64_t nw = (n + 31) / 32;
-    const int nb = ddg_gate_round1_arrays(kind, bw, scale), nh = L.ot ? 2 : nb - (L.lo ? 1 : 0);
+    const int nb = ddg_gate_round1_arrays(kind, bw, scale), nh = (L.ot || L.tt) ? 2 : nb - (L.lo ? 1 : 0);
     std::vector<void *> tmp;
     int err = DDG_OK;
     auto grab = [&](uint64_t bytes) -> void * {
@@ -134,45 +137,61 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
     uint32_t *b[2] = {d_bits0 ? d_bits0 : static_cast<uint32_t *>(grab(4 * nw * nb)),
                       d_bits1 ? d_bits1 : static_cast<uint32_t *>(grab(4 * nw * nb))};
     const void *key[2] = {d_key0, d_key1};
-    if (!L.ot) {
+    if (!L.ot && !L.tt) {
         for (int p = 0; p < 2 && err == DDG_OK; p++)
             ok(gate_round1(L, d_xhat, key[p], L.hi ? b[p] : nullptr, L.lo ? b[p] + nh * nw : nullptr, st));
     } else {
-        const OtPlan &P = ot_plan_cached(bw, scale);
+        const OtPlan &P = gate_digit_plan(L);
         const OtScratch sc = ot_scratch_bytes(L);
-        uint32_t *tab[2], *tri[2];
+        const bool hi = P.nd[0] != 0;
+        uint32_t *tab[2] = {}, *tri[2] = {};
         void *state[2];
         uint32_t *o[2][OT_MAX_LEVELS + 1] = {};
         for (int p = 0; p < 2; p++) {
-            tab[p] = static_cast<uint32_t *>(grab(sc.tables));
+            if (L.ot) tab[p] = static_cast<uint32_t *>(grab(sc.tables)), tri[p] = static_cast<uint32_t *>(grab(sc.tri));
             state[p] = grab(sc.state);
-            tri[p] = static_cast<uint32_t *>(grab(sc.tri));
             for (int l = 1; l <= P.levels; l++) o[p][l] = static_cast<uint32_t *>(grab(4 * n));
         }
-        for (int p = 0; p < 2 && err == DDG_OK; p++) ok(ot_garble(L, p, d_xhat, key[p], tab[p], state[p], tri[p], st));
+        if (L.ot)
+            for (int p = 0; p < 2 && err == DDG_OK; p++)
+                ok(ot_garble(L, p, d_xhat, key[p], tab[p], state[p], tri[p], st));
         for (int l = 1; l <= P.levels + 1 && err == DDG_OK; l++)
             for (int p = 0; p < 2 && err == DDG_OK; p++) {
                 const int q = 1 - p;
                 const bool last = l == P.levels + 1;
                 ok(ot_level(L, p, l, key[p], tab[q], o[p][l - 1], o[q][l - 1], state[p], tri[p], last ? nullptr : o[p][l],
-                            last ? b[p] : nullptr, last ? b[p] + 2 * nw : nullptr, st));
+                            last && hi ? b[p] : nullptr, last ? b[p] + (hi ? 2 : 0) * nw : nullptr, st, d_xhat));
             }
     }
     void *sh[2] = {d_share0, d_share1};
+    const bool has_hi = L.hi || L.ot || (L.tt && kind != GATE_LRS_TT);
+    const bool has_lo = L.lo || L.ot || L.tt;
+    const int lo_at = L.tt && kind == GATE_LRS_TT ? 0 : nh;
     for (int p = 0; p < 2 && err == DDG_OK; p++) {
         const int q = 1 - p;
-        const bool lo = L.lo || L.ot;
-        ok(gate_round2(L, p, d_xhat, b[p], b[q], lo ? b[p] + nh * nw : nullptr, lo ? b[q] + nh * nw : nullptr, key[p],
-                       sh[p], st));
+        ok(gate_round2(L, p, d_xhat, has_hi ? b[p] : nullptr, has_hi ? b[q] : nullptr, has_lo ? b[p] + lo_at * nw : nullptr,
+                       has_lo ? b[q] + lo_at * nw : nullptr, key[p], sh[p], st));
     }
     for (void *p : tmp) cudaFreeAsync(p, st);
     return err;
 }
 
+int ddg_tt_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out)
+{
+    DDG_TRY(check_gate_args(kind, bw, scale));
+    DDG_CHECK(gate_is_tt(kind) && out != nullptr, DDG_ERR_ARG, "truth-table gate kind and out[8] required");
+    GateLayout L = gate_layout(kind, bw, scale, n);
+    const OtPlan P = tt_plan_of(kind, bw, scale);
+    const uint64_t v[8] = {L.tt_tables, uint64_t(L.tt_rows), L.tt_tri, uint64_t(L.tt_triw), L.words, L.bytes,
+                           uint64_t(P.D), uint64_t(P.levels)};
+    for (int i = 0; i < 8; i++) out[i] = v[i];
+    return DDG_OK;
+}
+
 int ddg_relu_backend(int backend)
 {
-    DDG_CHECK(backend == DDG_RELU_DCF || backend == DDG_RELU_OT, DDG_ERR_ARG, "ReLU backend: %d or %d (got %d)",
-              DDG_RELU_DCF, DDG_RELU_OT, backend);
+    DDG_CHECK(backend == DDG_RELU_DCF || backend == DDG_RELU_OT || backend == DDG_RELU_TT, DDG_ERR_ARG,
+              "ReLU backend: %d, %d or %d (got %d)", DDG_RELU_DCF, DDG_RELU_OT, DDG_RELU_TT, backend);
     set_relu_backend(backend);
     return DDG_OK;
 }

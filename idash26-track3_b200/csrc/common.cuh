@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/ddg_fss.h"
+#include "digit_plan.cuh"
 
 namespace ddg {
 
@@ -89,21 +90,35 @@ struct TimedLaunch {
 // with the same dealer words and round 2, but obtain the split comparison bits
 // from garbled radix-16 digit tables and a Beaver AND tree (ot.cuh) instead of
 // DCF keys: no AES tree, a few key bytes per element, more rounds.
+// GATE_RELU_TT / GATE_RELU_ARS_TT / GATE_LRS_TT compute GATE_RELU_SPLIT /
+// GATE_RELU_ARS_SPLIT / GATE_LRS with their dealer words and round 2; the
+// comparison bits come from dealer-shared digit truth tables read at the
+// public digits of x_hat and the same AND tree (no AES, no table message).
 enum GateKind {
     GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
     GATE_LRS_SPLIT = 6, GATE_RELU_SPLIT3 = 7, GATE_RELU_ARS_SPLIT3 = 8, GATE_RELU_OT = 9, GATE_RELU_ARS_OT = 10,
-    GATE_KIND_END = 11
+    GATE_RELU_TT = 11, GATE_RELU_ARS_TT = 12, GATE_LRS_TT = 13, GATE_KIND_END = 14
 };
 constexpr int SPLIT3_MID = 6;
 constexpr int SPLIT3_NMONO = 19;  // dealer-bit monomials of the three-part DReLU bit
 
 inline bool gate_is_split3(int kind) { return kind == GATE_RELU_SPLIT3 || kind == GATE_RELU_ARS_SPLIT3; }
 inline bool gate_is_ot(int kind) { return kind == GATE_RELU_OT || kind == GATE_RELU_ARS_OT; }
+inline bool gate_is_tt(int kind) { return kind == GATE_RELU_TT || kind == GATE_RELU_ARS_TT || kind == GATE_LRS_TT; }
 // the kind whose dealer words and round 2 a gate uses
 __host__ __device__ inline int gate_word_kind(int kind)
 {
-    return kind == GATE_RELU_OT ? GATE_RELU_SPLIT : kind == GATE_RELU_ARS_OT ? GATE_RELU_ARS_SPLIT : kind;
+    switch (kind) {
+    case GATE_RELU_OT:
+    case GATE_RELU_TT: return GATE_RELU_SPLIT;
+    case GATE_RELU_ARS_OT:
+    case GATE_RELU_ARS_TT: return GATE_RELU_ARS_SPLIT;
+    case GATE_LRS_TT: return GATE_LRS;
+    default: return kind;
+    }
 }
+// the digit plan of a TT kind
+inline OtPlan tt_plan_of(int kind, int bw, int s) { return digit_plan(bw, s, kind == GATE_LRS_TT ? PLAN_TT_LRS : PLAN_TT_RELU); }
 // the high DCF has an equality output (three round-1 bit arrays, five with a middle DCF)
 inline bool gate_is_split(int kind)
 {
@@ -176,13 +191,14 @@ inline DcfLayout dcf_layout(int d, uint64_t n, uint64_t base, bool eq = false)
 // The hi DCF reads bits [hi_shift, hi_shift + H.d) of x_hat, the middle DCF
 // (three-part split kinds) bits [s, s + SPLIT3_MID), the lo DCF bits [0, Lo.d).
 // OT kinds: [ot_ks: 44 u32 round keys] [ot_recv: ot_gmax x N bytes] [ot_c0: N u32] [words]
+// TT kinds: [tt_tables: tt_rows x N u32] [tt_tri: tt_triw x N u32] [words]
 struct GateLayout {
     int kind = 0, bw = 0, s = 0, hi_shift = 0;
     uint64_t n = 0;
-    bool hi = false, mid = false, lo = false, ot = false;
+    bool hi = false, mid = false, lo = false, ot = false, tt = false;
     DcfLayout H, Mi, Lo;
-    int ot_gmax = 0;
-    uint64_t ot_ks = 0, ot_recv = 0, ot_c0 = 0;
+    int ot_gmax = 0, tt_rows = 0, tt_triw = 0;
+    uint64_t ot_ks = 0, ot_recv = 0, ot_c0 = 0, tt_tables = 0, tt_tri = 0;
     int nwords = 0;
     uint64_t words = 0, bytes = 0;
 };
@@ -196,6 +212,18 @@ inline GateLayout gate_layout(int kind, int bw, int s, uint64_t n, uint64_t base
     GateLayout g;
     g.kind = kind, g.bw = bw, g.s = s, g.n = n;
     uint64_t off = align256(base);
+    if (gate_is_tt(kind)) {
+        const OtPlan P = tt_plan_of(kind, bw, s);
+        g.tt = true;
+        g.tt_rows = P.rows, g.tt_triw = P.tri_words();
+        g.tt_tables = off;
+        g.tt_tri = align256(g.tt_tables + 4 * uint64_t(g.tt_rows) * n);
+        off = align256(g.tt_tri + 4 * uint64_t(g.tt_triw) * n);
+        g.nwords = gate_nwords(kind);
+        g.words = off;
+        g.bytes = align256(g.words + uint64_t(g.nwords) * n * uint64_t(bw / 8)) - align256(base);
+        return g;
+    }
     if (gate_is_ot(kind)) {
         g.ot = true;
         g.ot_gmax = ot_gmax(bw, s);
@@ -252,7 +280,7 @@ enum Purpose : uint32_t {
     P_HI_S0 = 1, P_HI_DELTA = 2, P_LO_S0 = 3, P_LO_DELTA = 4, P_ROUT = 5, P_BITS = 6,
     P_MASK = 8,    // input / output masks of linear ops
     P_MID_S0 = 9, P_MID_DELTA = 10,  // middle DCF of the three-part split gates
-                                     // 0x100..0x12f: OT gates (ot.cuh)
+                                     // 0x100..0x12f: OT gates (ot.cuh), 0x140..: TT gates
     P_SHARE = 16,  // share0 of dealer word k uses purpose P_SHARE + k (k < 80)
 };
 

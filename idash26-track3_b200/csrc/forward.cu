@@ -518,33 +518,44 @@ struct EvalExec : ExecBase<T> {
         t.v = open(s, n);
         return t;
     }
-    // OT gates: garbled digit tables, then one AND-tree level per round; the
-    // last level writes the masked comparison bits in the split-gate layout
-    // (bits_hi = [lt | eq], bits_lo = lt), opened and consumed by round 2
-    Tn<T> gate_ot(const GateLayout &L, const uint8_t *k, const Tn<T> &x)
+    // AND-tree gates.  OT kinds: garbled digit tables first (one message);
+    // TT kinds start from their own digit truth tables.  Then one AND-tree
+    // level per round; the last level writes the masked comparison bits in the
+    // split-gate layout (bits_hi = [lt | eq], bits_lo = lt; GATE_LRS_TT only
+    // bits_lo), opened and consumed by round 2.
+    Tn<T> gate_digits(const GateLayout &L, const uint8_t *k, const Tn<T> &x)
     {
-        const OtPlan &Pl = ot_plan_cached(this->bw, this->s);
+        const OtPlan &Pl = gate_digit_plan(L);
         const uint64_t n = x.n, nw = (n + 31) / 32;
         const OtScratch sc = ot_scratch_bytes(L);
-        uint32_t *tab = static_cast<uint32_t *>(this->alloc_bytes(sc.tables));
         void *state = this->alloc_bytes(sc.state);
-        uint32_t *tri = static_cast<uint32_t *>(this->alloc_bytes(sc.tri));
-        if (this->err == DDG_OK) ok(ot_garble(L, p, x.v, k, tab, state, tri, this->st));
-        const uint32_t *ptab = reinterpret_cast<const uint32_t *>(peer_of(tab, sc.tables));
+        uint32_t *tri = nullptr;
+        const uint32_t *ptab = nullptr;
+        if (L.ot) {
+            uint32_t *tab = static_cast<uint32_t *>(this->alloc_bytes(sc.tables));
+            tri = static_cast<uint32_t *>(this->alloc_bytes(sc.tri));
+            if (this->err == DDG_OK) ok(ot_garble(L, p, x.v, k, tab, state, tri, this->st));
+            ptab = reinterpret_cast<const uint32_t *>(peer_of(tab, sc.tables));
+        }
         const uint32_t *oo = nullptr, *po = nullptr;
         for (int l = 1; l <= Pl.levels; l++) {
             uint32_t *o = static_cast<uint32_t *>(this->alloc_bytes(4 * n));
-            if (this->err == DDG_OK) ok(ot_level(L, p, l, k, ptab, oo, po, state, tri, o, nullptr, nullptr, this->st));
+            if (this->err == DDG_OK)
+                ok(ot_level(L, p, l, k, ptab, oo, po, state, tri, o, nullptr, nullptr, this->st, x.v));
             po = reinterpret_cast<const uint32_t *>(peer_of(o, 4 * n));
             oo = o;
         }
-        uint32_t *bits = static_cast<uint32_t *>(this->alloc_bytes(4 * nw * 3));
+        const int nb = Pl.nd[0] ? 3 : 1;  // hi lt, hi eq, lo lt / lo lt only
+        uint32_t *bits = static_cast<uint32_t *>(this->alloc_bytes(4 * nw * nb));
+        uint32_t *bl = bits + (nb - 1) * nw;
         if (this->err == DDG_OK)
-            ok(ot_level(L, p, Pl.levels + 1, k, ptab, oo, po, state, tri, nullptr, bits, bits + 2 * nw, this->st));
-        const uint32_t *peer = reinterpret_cast<const uint32_t *>(peer_of(bits, 4 * nw * 3));
+            ok(ot_level(L, p, Pl.levels + 1, k, ptab, oo, po, state, tri, nullptr, nb == 3 ? bits : nullptr, bl,
+                        this->st, x.v));
+        const uint32_t *peer = reinterpret_cast<const uint32_t *>(peer_of(bits, 4 * nw * nb));
         T *sh = alloc(n);
         if (this->err == DDG_OK)
-            ok(gate_round2(L, p, x.v, bits, peer, bits + 2 * nw, peer ? peer + 2 * nw : nullptr, k, sh, this->st));
+            ok(gate_round2(L, p, x.v, nb == 3 ? bits : nullptr, nb == 3 ? peer : nullptr, bl,
+                           peer ? peer + (nb - 1) * nw : nullptr, k, sh, this->st));
         Tn<T> t;
         t.n = n;
         t.v = open(sh, n);
@@ -554,7 +565,7 @@ struct EvalExec : ExecBase<T> {
     {
         GateLayout L = gate_layout(kind, this->bw, this->s, x.n);
         const uint8_t *k = key_at(L.bytes);
-        if (L.ot) return gate_ot(L, k, x);
+        if (L.ot || L.tt) return gate_digits(L, k, x);
         const uint64_t nw = (x.n + 31) / 32;
         // split gates also open the equality bits, three-part splits the middle DCF's two bits
         const int nh = L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0;
@@ -610,20 +621,27 @@ struct EvalExec : ExecBase<T> {
 static std::atomic<int> g_relu_parts{3};
 void set_relu_parts(int parts) { g_relu_parts.store(parts == 2 ? 2 : 3); }
 static int relu_parts(int) { return g_relu_parts.load(); }
-// comparison backend of the ReLU gates: OT-leaf digit tables with a Beaver
-// AND tree (GATE_RELU*_OT, default: 2 AES and ~8 key bytes per element and
-// party besides the words) or DCF keys (split per relu_parts)
-static std::atomic<int> g_relu_backend{DDG_RELU_OT};
-void set_relu_backend(int backend) { g_relu_backend.store(backend == DDG_RELU_OT ? DDG_RELU_OT : DDG_RELU_DCF); }
+// comparison backend of the ReLU (and truncation) gates: dealer truth tables
+// per digit with a Beaver AND tree (GATE_RELU*_TT and GATE_LRS_TT at the
+// truncation sites; default: no AES online), OT-leaf digit tables with the
+// same tree (GATE_RELU*_OT: 2 AES and ~8 key bytes per element and party
+// besides the words) or DCF keys (split per relu_parts)
+static std::atomic<int> g_relu_backend{DDG_RELU_TT};
+void set_relu_backend(int backend)
+{
+    g_relu_backend.store(backend == DDG_RELU_OT || backend == DDG_RELU_TT ? backend : DDG_RELU_DCF);
+}
 int relu_backend() { return g_relu_backend.load(); }
 
 template <typename T, class E>
 static void affinity_graph(E &x)
 {
     const int B = x.B;
-    const bool three = relu_parts(x.bw) == 3, ot = g_relu_backend.load() == DDG_RELU_OT;
-    const int RELU = ot ? GATE_RELU_OT : three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
-    const int RELU_ARS = ot ? GATE_RELU_ARS_OT : three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
+    const int be = g_relu_backend.load();
+    const bool three = relu_parts(x.bw) == 3, ot = be == DDG_RELU_OT, tt = be == DDG_RELU_TT;
+    const int RELU = tt ? GATE_RELU_TT : ot ? GATE_RELU_OT : three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
+    const int RELU_ARS = tt ? GATE_RELU_ARS_TT : ot ? GATE_RELU_ARS_OT : three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
+    const int LRS = tt ? GATE_LRS_TT : GATE_LRS_SPLIT;
     const uint64_t nX = uint64_t(B) * NMAX * FEAT, nA = uint64_t(B) * NMAX * NMAX, nM = uint64_t(B) * NMAX * POOL;
     // leaves: x, mask, raw adjacency and its masked degree, the public protein
     // (deepdtagen_inference.cu:503-529 registerLeaf; secure_adj_norm.h:414-493)
@@ -638,13 +656,13 @@ static void affinity_graph(E &x)
     sh.n = nA, sh.R = NMAX, sh.C = NMAX;
     Tn<T> L = x.mul(A, t, BC_ROW, sh);
     Tn<T> W = x.mul(L, t, BC_COL, sh);
-    Tn<T> Ah = x.gate(GATE_LRS_SPLIT, W);
+    Tn<T> Ah = x.gate(LRS, W);
     // GCN x3, aggregate first (gcn_layer.h:107-116)
     Tn<T> X = x.reveal_input(IN_X, nX);
     Tn<T> H = X;
     for (int l = 0; l < 3; l++) {
         Tn<T> Pm = x.matmul(Ah, H, LAYER_IN[l]);
-        Tn<T> AX = x.gate(GATE_LRS_SPLIT, Pm);
+        Tn<T> AX = x.gate(LRS, Pm);
         Tn<T> Z = x.fc(AX, l, B * NMAX);
         H = x.gate(RELU_ARS, Z);
     }
@@ -653,7 +671,7 @@ static void affinity_graph(E &x)
     shm.n = nM;
     Tn<T> M = x.reveal_input(IN_MASK, nM);
     Tn<T> prod = x.mul(H, M, BC_NONE, shm);
-    Tn<T> cur = x.gate(GATE_LRS_SPLIT, prod);
+    Tn<T> cur = x.gate(LRS, prod);
     int cnt = NMAX;
     while (cnt > 1) {
         Tn<T> even, diff;

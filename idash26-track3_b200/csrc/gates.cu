@@ -60,7 +60,7 @@ struct GateKeygenArgs {
     T *rout;
     uint8_t *k0, *k1;
     GateLayout lay;
-    OtPlan ot;          // OT kinds: the digit plan and the two parties' keys K_0, K_1
+    OtPlan ot;          // OT / TT kinds: the digit plan (OT: and the two parties' keys K_0, K_1)
     AesKey prk0, prk1;
 };
 
@@ -120,6 +120,15 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                         reinterpret_cast<uint32_t *>(a.k1 + L.ot_ks)[i] = a.prk1.rk[i];
                     }
                 }
+            }
+            if (L.tt) {
+                const uint32_t rc = (bits ^ (bits >> 1)) & 1u, rl = ((bits >> 2) ^ (bits >> 3)) & 1u,
+                               re = ((bits >> 4) ^ (bits >> 5)) & 1u;
+                tt_keygen_elem(A, a.ot, a.dk.rk, a.op, e, N, uint64_t(r), rc, re, rl,
+                               reinterpret_cast<uint32_t *>(a.k0 + L.tt_tables),
+                               reinterpret_cast<uint32_t *>(a.k1 + L.tt_tables),
+                               reinterpret_cast<uint32_t *>(a.k0 + L.tt_tri),
+                               reinterpret_cast<uint32_t *>(a.k1 + L.tt_tri));
             }
             if (L.lo) {
                 const uint64_t alpha = uint64_t(r) & ((uint64_t(1) << L.Lo.d) - 1);
@@ -469,6 +478,10 @@ int gate_keygen_t(const GateLayout &L, uint64_t seed, uint32_t op, const void *r
         a.prk0 = ot_party_key(a.dk, op, 0);
         a.prk1 = ot_party_key(a.dk, op, 1);
     }
+    if (L.tt) {
+        a.ot = tt_plan_of(L.kind, L.bw, L.s);
+        DDG_CHECK(a.ot.ok, DDG_ERR_ARG, "no truth-table plan for bw %d, scale %d", L.bw, L.s);
+    }
     if (L.n == 0) return DDG_OK;
     DDG_TRY((aes_tables() == 4 ? keygen_launch<T, AesLane4>(a, st) : keygen_launch<T, AesLane2>(a, st)));
     note_launch();
@@ -480,7 +493,7 @@ template <typename T>
 int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32_t *bits_hi, uint32_t *bits_lo,
                   cudaStream_t st)
 {
-    DDG_CHECK(!L.ot, DDG_ERR_ARG, "OT gates have no one-shot round 1 (garble, then the AND-tree levels)");
+    DDG_CHECK(!L.ot && !L.tt, DDG_ERR_ARG, "OT and TT gates have no one-shot round 1 (AND-tree levels)");
     DDG_TRY(aes_device_init());
     if (L.n == 0) return DDG_OK;
     Round1Args<T> a;

@@ -7,6 +7,7 @@
 // compare_gt / AND tree; bridged to the masked-public GPU pipeline as
 // lss_protocol.md section 8 describes).
 #include <mutex>
+#include <type_traits>
 
 #include "ot.cuh"
 
@@ -155,9 +156,11 @@ struct OtLevelArgs {
     OtPlan P;
     int party, level;  // level 1..levels+1
     uint64_t N, nw;
-    const uint8_t *recv;         // level 1: the party's receiver records [slot][N]
-    const uint32_t *peer_tables; // level 1: the peer's tables [slot][N]
-    const uint32_t *c0;          // party 0's explicit triple c bits [N]
+    const uint8_t *recv;         // OT level 1: the party's receiver records [slot][N]
+    const uint32_t *peer_tables; // OT level 1: the peer's tables [slot][N]
+    const uint32_t *c0;          // OT: party 0's explicit triple c bits [N]
+    const void *xhat;            // TT level 1: the masked input (ring words)
+    const uint32_t *tables;      // TT level 1: the party's digit truth-table rows [row][N]
     const uint32_t *open_own, *open_peer;  // level >= 2: the previous level's openings
     void *state;
     const uint32_t *tri;         // [tri_words][N]
@@ -173,12 +176,29 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
 {
     const uint64_t N = a.N;
     constexpr uint32_t p0 = PARTY == 0 ? 1u : 0u;
-    ST st = load_state<ST>(a.state, e);
+    const bool tt = P.mode != PLAN_OT;
+    ST st = (tt && l == 1) ? ST(0) : load_state<ST>(a.state, e);
     uint32_t tw[3] = {0u, 0u, 0u};
 #pragma unroll
     for (int w = 0; w < 3; w++)
         if (w < P.tri_words()) tw[w] = __ldcs(a.tri + uint64_t(w) * N + e);
-    if (l == 1) {
+    if (tt && l == 1) {
+        // the party's share of every digit's (lt, eq): its table read at the public digit
+        const uint64_t x = P.n == 32 ? uint64_t(__ldcs(static_cast<const uint32_t *>(a.xhat) + e))
+                                     : __ldcs(static_cast<const unsigned long long *>(a.xhat) + e);
+#pragma unroll
+        for (int g = 0; g < OT_MAX_DIGITS; g++) {
+            if (g >= P.D) break;
+            const int w = P.width(g), W = 1 << w;
+            const uint32_t xd = uint32_t(x >> P.shift(g)) & uint32_t(W - 1);
+            const uint32_t *tb = a.tables + uint64_t(P.drow0(g)) * N + e;
+            const uint32_t il = xd, ie = uint32_t(W) + xd;
+            const uint32_t lt = (__ldcs(tb + uint64_t(il >> 5) * N) >> (il & 31)) & 1u;
+            uint32_t eq = 0;
+            if (P.deq(g)) eq = (__ldcs(tb + uint64_t(ie >> 5) * N) >> (ie & 31)) & 1u;
+            st |= (ST(lt) << (2 * g)) | (ST(eq) << (2 * g + 1));
+        }
+    } else if (l == 1) {
         // shares of the digits the peer garbled: T[c] ^ k_c
         constexpr int q = 1 - PARTY;
         const int G = P.garbled_by(q), g0 = q == 0 ? 0 : P.G0;
@@ -195,7 +215,8 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
     } else {
         // close level l - 1: z = c ^ f a ^ e b ^ [p = 0] e f
         const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
-        const uint32_t cw = PARTY == 0 ? __ldcs(a.c0 + e) : 0u;
+        const bool cword = !tt && PARTY == 0;  // OT party 0 keeps its triple c bits in a key word
+        const uint32_t cw = cword ? __ldcs(a.c0 + e) : 0u;
         const int qa = P.lvl_first[l - 2];
 #pragma unroll
         for (int q = 0; q < OT_MAX_COMB; q++) {
@@ -205,8 +226,8 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             const int j = q - qa, tb = 5 * q, base = 2 * P.base[C.part];
             const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
             const uint32_t ta = tri_bit(tw, tb), tb1 = tri_bit(tw, tb + 1), tb2 = tri_bit(tw, tb + 2);
-            const uint32_t c = PARTY == 0 ? (cw >> (2 * q)) & 1u : tri_bit(tw, tb + 3);
-            const uint32_t c2 = PARTY == 0 ? (cw >> (2 * q + 1)) & 1u : tri_bit(tw, tb + 4);
+            const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tri_bit(tw, tb + 3);
+            const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tri_bit(tw, tb + 4);
             const uint32_t lt = st_bit(st, base + 2 * C.h) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
             const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
             const int o = base + 2 * C.out;
@@ -240,12 +261,127 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
         a.open_out[e] = w;
         store_state<ST>(a.state, e, st);
     } else {
-        hl = st_bit(st, 0), he = st_bit(st, 1), ll = st_bit(st, 2 * P.base[1]);
+        if (P.nd[0]) hl = st_bit(st, 0), he = st_bit(st, 1);
+        ll = st_bit(st, 2 * P.base[1]);
     }
 }
 
+// ---- the same step with the plan compiled in.  Every digit, combine and
+// pass is visited by a compile-time loop, and plan fields are read only into
+// constexpr locals, so no plan object exists at run time (a constexpr plan
+// object indexed from unrolled loops ended up in local memory).
+template <int I, int END, class F>
+__device__ __forceinline__ void static_for(const F &f)
+{
+    if constexpr (I < END) {
+        f(std::integral_constant<int, I>{});
+        static_for<I + 1, END>(f);
+    }
+}
+
+template <int MODE, int NB, int SB, int PARTY, int L>
+__device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, uint32_t &hl, uint32_t &he,
+                                             uint32_t &ll)
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    static_assert(P.ok && P.state_bytes() == 4, "compiled-in plans keep a 32-bit state");
+    constexpr bool TT = MODE != PLAN_OT;
+    constexpr uint32_t p0 = PARTY == 0 ? 1u : 0u;
+    const uint64_t N = a.N;
+    uint32_t st = 0;
+    if constexpr (!(TT && L == 1)) st = load_state<uint32_t>(a.state, e);
+    uint32_t tw[3] = {0u, 0u, 0u};
+    static_for<0, P.tri_words()>([&](auto wi) {
+        constexpr int w = decltype(wi)::value;
+        tw[w] = __ldcs(a.tri + uint64_t(w) * N + e);
+    });
+    auto tbit = [&](int i) { return (tw[i >> 5] >> (i & 31)) & 1u; };
+    if constexpr (TT && L == 1) {
+        const uint64_t x = NB == 32 ? uint64_t(__ldcs(static_cast<const uint32_t *>(a.xhat) + e))
+                                    : __ldcs(static_cast<const unsigned long long *>(a.xhat) + e);
+        static_for<0, P.D>([&](auto gi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int g = decltype(gi)::value;
+            constexpr int W = 1 << P.width(g), sh = P.shift(g), r0 = P.drow0(g);
+            constexpr bool deq = P.deq(g) != 0;
+            const uint32_t xd = uint32_t(x >> sh) & uint32_t(W - 1);
+            const uint32_t *tb = a.tables + uint64_t(r0) * N + e;
+            const uint32_t ie = uint32_t(W) + xd;
+            uint32_t lt, eq = 0;
+            if constexpr (W <= 32) {
+                lt = (__ldcs(tb) >> xd) & 1u;
+                if constexpr (deq) eq = (__ldcs(tb + uint64_t(ie >> 5) * N) >> (ie & 31)) & 1u;
+            } else {
+                lt = (__ldcs(tb + uint64_t(xd >> 5) * N) >> (xd & 31)) & 1u;
+                if constexpr (deq) eq = (__ldcs(tb + uint64_t(ie >> 5) * N) >> (ie & 31)) & 1u;
+            }
+            st |= (lt << (2 * g)) | (eq << (2 * g + 1));
+        });
+    } else if constexpr (L == 1) {
+        constexpr int q = 1 - PARTY;
+        constexpr int G = P.garbled_by(q), g0 = q == 0 ? 0 : P.G0;
+        static_for<0, G>([&](auto ti) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int t = decltype(ti)::value;
+            const uint32_t rec = __ldcs(a.recv + uint64_t(t) * N + e);
+            const uint32_t word = __ldcs(a.peer_tables + uint64_t(t) * N + e);
+            const uint32_t c = rec & 15u;
+            const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
+            st |= (lt << (2 * (g0 + t))) | (eq << (2 * (g0 + t) + 1));
+        });
+    } else {
+        const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
+        constexpr bool cword = !TT && PARTY == 0;
+        const uint32_t cw = cword ? __ldcs(a.c0 + e) : 0u;
+        constexpr int qa = P.lvl_first[L - 2], qb = P.lvl_first[L - 1];
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value;
+            constexpr int j = q - qa, tb = 5 * q, base = 2 * P.base[P.comb[q].part];
+            constexpr int h = base + 2 * (2 * P.comb[q].out + 1), o = base + 2 * P.comb[q].out;
+            constexpr bool ceq = P.comb[q].eq != 0;
+            const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
+            const uint32_t ta = tbit(tb), tb1 = tbit(tb + 1), tb2 = tbit(tb + 2);
+            const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tbit(tb + 3);
+            const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tbit(tb + 4);
+            const uint32_t lt = ((st >> h) & 1u) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
+            const uint32_t eq = ceq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
+            st = (st & ~(3u << o)) | (lt << o) | (eq << (o + 1));
+        });
+        static_for<0, 2>([&](auto pi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int pt = decltype(pi)::value;
+            constexpr int from = P.pass_from[L - 1][pt];
+            if constexpr (from >= 0) {
+                constexpr int b = 2 * P.base[pt], o = b + 2 * P.pass_to[L - 1][pt];
+                const uint32_t v = (st >> (b + 2 * from)) & 3u;
+                st = (st & ~(3u << o)) | (v << o);
+            }
+        });
+    }
+    if constexpr (L <= P.levels) {
+        uint32_t w = 0;
+        constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value;
+            constexpr int j = q - qa, tb = 5 * q, base = 2 * P.base[P.comb[q].part];
+            constexpr int hb = base + 2 * (2 * P.comb[q].out + 1), lb = base + 2 * (2 * P.comb[q].out);
+            const uint32_t eH = (st >> (hb + 1)) & 1u, lL = (st >> lb) & 1u, eL = (st >> (lb + 1)) & 1u;
+            w |= ((eH ^ tbit(tb)) << (3 * j)) | ((lL ^ tbit(tb + 1)) << (3 * j + 1));
+            if constexpr (P.comb[q].eq != 0) w |= (eL ^ tbit(tb + 2)) << (3 * j + 2);
+        });
+        a.open_out[e] = w;
+        store_state<uint32_t>(a.state, e, st);
+    } else {
+        if constexpr (P.nd[0] != 0) hl = st & 1u, he = (st >> 1) & 1u;
+        ll = (st >> (2 * P.base[1])) & 1u;
+    }
+}
+
+// MODE, NB, SB: the plan compiled in (NB = 0: the plan in the arguments);
 // LV: the level compiled in (0 = a.level)
-template <int NB, int SB, int PARTY, int LV>
+template <int MODE, int NB, int SB, int PARTY, int LV>
 __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
 {
     const uint64_t N = a.N;
@@ -255,9 +391,8 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
         uint32_t hl = 0, he = 0, ll = 0;
         if (e < N) {
-            if constexpr (NB != 0) {
-                constexpr OtPlan P = ot_plan(NB, SB);
-                level_elem<PARTY, uint32_t>(P, a, l, e, hl, he, ll);
+            if constexpr (NB != 0 && LV != 0) {
+                level_elem_c<MODE, NB, SB, PARTY, LV>(a, e, hl, he, ll);
             } else if (a.P.state_bytes() == 4) {
                 level_elem<PARTY, uint32_t>(a.P, a, l, e, hl, he, ll);
             } else {
@@ -269,7 +404,8 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
                            wl = __ballot_sync(0xFFFFFFFFu, ll);
             if ((threadIdx.x & 31) == 0) {
                 const uint64_t wi = e >> 5;
-                a.bits_hi[wi] = wh, a.bits_hi[a.nw + wi] = we, a.bits_lo[wi] = wl;
+                if (a.bits_hi) a.bits_hi[wi] = wh, a.bits_hi[a.nw + wi] = we;
+                a.bits_lo[wi] = wl;
             }
         }
     }
@@ -328,64 +464,95 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
 }
 
 // a compiled-in plan also compiles in the level (every node and bit offset a constant)
-template <int NB, int SB, int PARTY>
+template <int MODE, int NB, int SB, int PARTY>
 static void level_launch(const OtLevelArgs &a, int grid, cudaStream_t st)
 {
     switch (a.level) {
-    case 1: ot_level_kernel<NB, SB, PARTY, 1><<<grid, 256, 0, st>>>(a); break;
-    case 2: ot_level_kernel<NB, SB, PARTY, 2><<<grid, 256, 0, st>>>(a); break;
-    case 3: ot_level_kernel<NB, SB, PARTY, 3><<<grid, 256, 0, st>>>(a); break;
-    case 4: ot_level_kernel<NB, SB, PARTY, 4><<<grid, 256, 0, st>>>(a); break;
-    case 5: ot_level_kernel<NB, SB, PARTY, 5><<<grid, 256, 0, st>>>(a); break;
-    default: ot_level_kernel<NB, SB, PARTY, 0><<<grid, 256, 0, st>>>(a); break;
+    case 1: ot_level_kernel<MODE, NB, SB, PARTY, 1><<<grid, 256, 0, st>>>(a); break;
+    case 2: ot_level_kernel<MODE, NB, SB, PARTY, 2><<<grid, 256, 0, st>>>(a); break;
+    case 3: ot_level_kernel<MODE, NB, SB, PARTY, 3><<<grid, 256, 0, st>>>(a); break;
+    case 4: ot_level_kernel<MODE, NB, SB, PARTY, 4><<<grid, 256, 0, st>>>(a); break;
+    case 5: ot_level_kernel<MODE, NB, SB, PARTY, 5><<<grid, 256, 0, st>>>(a); break;
+    default: ot_level_kernel<MODE, NB, SB, PARTY, 0><<<grid, 256, 0, st>>>(a); break;
     }
+}
+
+template <int MODE, int PARTY>
+static void level_dispatch(const GateLayout &L, const OtLevelArgs &a, int grid, cudaStream_t st)
+{
+    if (L.s == 12 && L.bw == 32) level_launch<MODE, 32, 12, PARTY>(a, grid, st);
+    else if (L.s == 12) level_launch<MODE, 64, 12, PARTY>(a, grid, st);
+    else ot_level_kernel<MODE, 0, 0, PARTY, 0><<<grid, 256, 0, st>>>(a);
+}
+
+const OtPlan &gate_digit_plan(const GateLayout &L)
+{
+    static OtPlan tt[3][2][64];
+    static std::once_flag once;
+    std::call_once(once, [] {
+        for (int b = 0; b < 2; b++)
+            for (int sc = 1; sc < 64; sc++) {
+                tt[1][b][sc] = digit_plan(b ? 64 : 32, sc, PLAN_TT_RELU);
+                tt[2][b][sc] = digit_plan(b ? 64 : 32, sc, PLAN_TT_LRS);
+            }
+    });
+    if (L.ot) return ot_plan_cached(L.bw, L.s);
+    return tt[L.kind == GATE_LRS_TT ? 2 : 1][L.bw == 64 ? 1 : 0][L.s > 0 && L.s < 64 ? L.s : 0];
 }
 
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
              const uint32_t *open_own, const uint32_t *open_peer, void *state, const uint32_t *tri,
-             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st)
+             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat)
 {
     if (L.n == 0) return DDG_OK;
-    const OtPlan &P = ot_plan_cached(L.bw, L.s);
-    DDG_CHECK(P.ok && level >= 1 && level <= P.levels + 1, DDG_ERR_ARG, "OT level %d out of range", level);
+    DDG_CHECK(L.ot || L.tt, DDG_ERR_ARG, "not an AND-tree gate");
+    const OtPlan &P = gate_digit_plan(L);
+    DDG_CHECK(P.ok && level >= 1 && level <= P.levels + 1, DDG_ERR_ARG, "AND-tree level %d out of range", level);
+    DDG_CHECK(party == 0 || party == 1, DDG_ERR_ARG, "party must be 0 or 1");
+    DDG_CHECK(!L.tt || level > 1 || xhat, DDG_ERR_ARG, "truth-table level 1 needs x_hat");
     const uint8_t *k = static_cast<const uint8_t *>(key);
     OtLevelArgs a;
     a.P = P, a.party = party, a.level = level, a.N = L.n, a.nw = (L.n + 31) / 32;
-    a.recv = k + L.ot_recv;
+    a.recv = L.ot ? k + L.ot_recv : nullptr;
     a.peer_tables = peer_tables;
-    a.c0 = reinterpret_cast<const uint32_t *>(k + L.ot_c0);
+    a.c0 = L.ot ? reinterpret_cast<const uint32_t *>(k + L.ot_c0) : nullptr;
+    a.xhat = xhat;
+    a.tables = L.tt ? reinterpret_cast<const uint32_t *>(k + L.tt_tables) : nullptr;
     a.open_own = open_own, a.open_peer = open_peer;
     a.state = state;
-    a.tri = tri;
-    a.open_out = open_out, a.bits_hi = bits_hi, a.bits_lo = bits_lo;
+    a.tri = L.tt ? reinterpret_cast<const uint32_t *>(k + L.tt_tri) : tri;
+    a.open_out = open_out, a.bits_hi = P.nd[0] ? bits_hi : nullptr, a.bits_lo = bits_lo;
     const int sms = device_sms();
     const uint64_t blocks = (L.n + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
     const int grid = int(blocks < cap ? blocks : cap);
     TimedLaunch tl;
     DDG_TRY(tl.begin(st));
-    if (L.s == 12 && L.bw == 32)
-        party == 0 ? level_launch<32, 12, 0>(a, grid, st) : level_launch<32, 12, 1>(a, grid, st);
-    else if (L.s == 12)
-        party == 0 ? level_launch<64, 12, 0>(a, grid, st) : level_launch<64, 12, 1>(a, grid, st);
-    else
-        party == 0 ? ot_level_kernel<0, 0, 0, 0><<<grid, 256, 0, st>>>(a)
-                   : ot_level_kernel<0, 0, 1, 0><<<grid, 256, 0, st>>>(a);
+    if (L.ot) party == 0 ? level_dispatch<PLAN_OT, 0>(L, a, grid, st) : level_dispatch<PLAN_OT, 1>(L, a, grid, st);
+    else if (L.kind == GATE_LRS_TT)
+        party == 0 ? level_dispatch<PLAN_TT_LRS, 0>(L, a, grid, st) : level_dispatch<PLAN_TT_LRS, 1>(L, a, grid, st);
+    else party == 0 ? level_dispatch<PLAN_TT_RELU, 0>(L, a, grid, st) : level_dispatch<PLAN_TT_RELU, 1>(L, a, grid, st);
     note_launch();
     DDG_CUDA(cudaGetLastError());
-    // algorithmic bytes: state and aux blocks in; level 1 the receiver records and
-    // the peer's tables, later levels both parties' openings (+ party 0's c
-    // word); state and openings out, or the three bit arrays at the last level
+    // algorithmic bytes: state and triple words in (the TT first level: x_hat
+    // and the truth-table rows instead of the state); OT level 1 also the
+    // receiver records and the peer's tables, later levels both parties'
+    // openings (+ OT party 0's c word); state and openings out, or the
+    // comparison bit arrays at the last level
     const double n = double(L.n), Gq = P.garbled_by(1 - party);
-    double bytes = n * (P.state_bytes() + 4.0 * P.tri_words());
-    bytes += level == 1 ? n * 5.0 * Gq : n * (8.0 + (party == 0 ? 4.0 : 0.0));
-    bytes += level <= P.levels ? n * (4.0 + P.state_bytes()) : n * 3.0 / 8.0;
+    double bytes = n * 4.0 * P.tri_words();
+    if (L.tt && level == 1) bytes += n * (L.bw / 8.0 + 4.0 * P.rows);
+    else bytes += n * P.state_bytes();
+    if (level > 1) bytes += n * (8.0 + (L.ot && party == 0 ? 4.0 : 0.0));
+    else if (L.ot) bytes += n * 5.0 * Gq;
+    bytes += level <= P.levels ? n * (4.0 + P.state_bytes()) : n * (P.nd[0] ? 3.0 : 1.0) / 8.0;
     DDG_TRY(tl.end(st, bytes, 0.0, n));
     return DDG_OK;
 }
 
 OtScratch ot_scratch_bytes(const GateLayout &L)
 {
-    const OtPlan &P = ot_plan_cached(L.bw, L.s);
+    const OtPlan &P = gate_digit_plan(L);
+    if (L.tt) return OtScratch{0, uint64_t(P.state_bytes()) * L.n, 0};
     const uint64_t n = L.n;
     return OtScratch{4ull * uint64_t(P.Gmax) * n, uint64_t(P.state_bytes()) * n, 4ull * uint64_t(P.tri_words()) * n};
 }

@@ -61,112 +61,13 @@
 
 #include "aes_dev.cuh"
 #include "common.cuh"
+#include "digit_plan.cuh"
 
 namespace ddg {
-
-constexpr int OT_W = 4;                // digit bits (radix 16)
-constexpr int OT_MAX_DIGITS = 18;      // n - 1 <= 63 bits in two parts
-constexpr int OT_MAX_COMB = 16;        // D - 2 combines at most
-constexpr int OT_MAX_LEVELS = 5;       // ceil(log2(16))
-constexpr int OT_MAX_AUX = 2;          // aux PRF blocks per party and element
-constexpr int OT_MAX_PAD = 3;          // pad PRF blocks per party and element (Gmax <= 9)
 
 // PRF purposes of the OT gates: the party keys under the dealer key (clear of
 // the dealer's word shares P_SHARE + k, k < 80), aux and pad blocks under K_p
 enum : uint32_t { P_OT_PARTY = 0x100, P_OT_AUX = 0x110, P_OT_PAD = 0x120 };
-
-struct OtComb {
-    uint8_t part, h, l, out;  // part 0 = hi, 1 = lo; node indices within the part
-    uint8_t eq, root;         // computes eq; produces the part's root
-};
-
-struct OtPlan {
-    int n = 0, s = 0;
-    int D = 0, G0 = 0, Gmax = 0;        // digits; party 0 garbles [0, G0), party 1 [G0, D); Gmax = G0
-    int nd[2] = {0, 0};                 // digits per part (hi, lo)
-    int base[2] = {0, 0};               // global index of a part's first digit
-    int levels = 0, ncomb = 0;
-    int lvl_first[OT_MAX_LEVELS + 2] = {};  // combines of level l (1-based): [lvl_first[l-1], lvl_first[l])
-    // pass-through of an odd top node at level l: part p moves node pass_from to pass_to (-1: none)
-    int8_t pass_from[OT_MAX_LEVELS + 1][2] = {}, pass_to[OT_MAX_LEVELS + 1][2] = {};
-    OtComb comb[OT_MAX_COMB] = {};
-    int aux_bits = 0, naux = 0, tri0 = 0;  // aux bits used, aux blocks, first triple bit (6 * Gmax)
-    int npad[2] = {0, 0};               // pad blocks of party 0 / 1
-    bool ok = false;
-
-    __host__ __device__ constexpr int garbler(int g) const { return g < G0 ? 0 : 1; }
-    __host__ __device__ constexpr int local(int g) const { return g < G0 ? g : g - G0; }
-    __host__ __device__ constexpr int part_of(int g) const { return g < nd[0] ? 0 : 1; }
-    // bit position of digit g in x_hat / r, and its width
-    __host__ __device__ constexpr int shift(int g) const { return g < nd[0] ? s + OT_W * g : OT_W * (g - nd[0]); }
-    __host__ __device__ constexpr int width(int g) const
-    {
-        const int bits = g < nd[0] ? n - 1 - s : s;
-        const int j = g < nd[0] ? g : g - nd[0];
-        const int rem = bits - OT_W * j;
-        return rem < OT_W ? rem : OT_W;
-    }
-    __host__ __device__ constexpr int garbled_by(int p) const { return p == 0 ? G0 : D - G0; }
-    // evaluator scratch per element: digit-share state (2 bits per node) and
-    // the triple bits (a, b, b', c1, c1') of every combine, 32-bit words
-    __host__ __device__ constexpr int state_bytes() const { return 2 * D <= 32 ? 4 : 8; }
-    __host__ __device__ constexpr int tri_words() const { return (5 * ncomb + 31) / 32; }
-    // AND-tree level (1-based) of combine q
-    __host__ __device__ constexpr int level_of(int q) const
-    {
-        int l = 1;
-        while (l <= levels && q >= lvl_first[l]) l++;
-        return l;
-    }
-};
-
-// Plan for an n-bit ring and scale s: hi = bits [s, n-1), lo = bits [0, s).
-// constexpr, so kernels specialised for a (bw, scale) see every digit, node
-// and bit position as a compile-time constant.
-__host__ __device__ constexpr OtPlan ot_plan(int n, int s)
-{
-    OtPlan P;
-    P.n = n, P.s = s;
-    const int hb = n - 1 - s, lb = s;
-    if (hb < 1 || lb < 1) return P;
-    P.nd[0] = (hb + OT_W - 1) / OT_W;
-    P.nd[1] = (lb + OT_W - 1) / OT_W;
-    P.base[0] = 0, P.base[1] = P.nd[0];
-    P.D = P.nd[0] + P.nd[1];
-    if (P.D > OT_MAX_DIGITS) return P;
-    P.G0 = (P.D + 1) / 2;
-    P.Gmax = P.G0;
-    int k[2] = {P.nd[0], P.nd[1]};
-    int q = 0, l = 0;
-    P.lvl_first[0] = 0;
-    while (k[0] > 1 || k[1] > 1) {
-        l++;
-        if (l > OT_MAX_LEVELS) return P;
-        for (int p = 0; p < 2; p++) {
-            P.pass_from[l][p] = -1, P.pass_to[l][p] = -1;
-            if (k[p] <= 1) continue;
-            const int nk = (k[p] + 1) / 2;
-            for (int i = 0; i < k[p] / 2; i++) {
-                if (q >= OT_MAX_COMB) return P;
-                OtComb &c = P.comb[q++];
-                c.part = uint8_t(p), c.h = uint8_t(2 * i + 1), c.l = uint8_t(2 * i), c.out = uint8_t(i);
-                c.root = uint8_t(nk == 1);
-                c.eq = uint8_t(i > 0 || p == 0);
-            }
-            if (k[p] & 1) P.pass_from[l][p] = int8_t(k[p] - 1), P.pass_to[l][p] = int8_t(k[p] / 2);
-            k[p] = nk;
-        }
-        P.lvl_first[l] = q;
-    }
-    P.levels = l, P.ncomb = q;
-    P.tri0 = 6 * P.Gmax;
-    P.aux_bits = P.tri0 + 5 * q;
-    P.naux = (P.aux_bits + 127) / 128;
-    if (P.naux < 1) P.naux = 1;
-    P.npad[0] = (P.G0 + 3) / 4, P.npad[1] = (P.D - P.G0 + 3) / 4;
-    P.ok = P.naux <= OT_MAX_AUX && P.npad[0] <= OT_MAX_PAD && P.npad[1] <= OT_MAX_PAD;
-    return P;
-}
 
 // garbler's table word for digit value xd (width w), rotation delta, share
 // (s_lt, s_eq) and pad word: bit u (u < 2^w) = 1{xd < u - delta} ^ s_lt ^
@@ -231,10 +132,87 @@ __device__ __forceinline__ void ot_keygen_elem(const E &A, const OtPlan &P, cons
     c0[e] = cw;
 }
 
+// ---- truth-table gates, dealer, per element (gate keygen kernel).  Each digit
+// g of x_hat's comparison parts gets a table over its 2^w values: lt bits
+// 1{x < a_g} at [0, 2^w), then (deq) eq bits 1{x == a_g} at [2^w, 2^(w+1)),
+// a_g the mask digit; party 0's rows are dealer-PRG bits, party 1's rows are
+// party 0's XOR the truth table (a part with one digit XORs its mask bits
+// into every entry).  Every combine gets a Beaver triple: party 0's (a, b, b',
+// c, c') and party 1's (a, b, b') from the PRG, party 1's c = ab ^ c0 (^ rho
+// at a part's root), c' likewise.  Both parties' triple bits: 5 per combine.
+enum : uint32_t { P_TT_RAND = 0x140 };
+
+template <class E>
+__device__ __forceinline__ void tt_keygen_elem(const E &A, const OtPlan &P, const uint32_t *dk, uint32_t op,
+                                               uint64_t e, uint64_t N, uint64_t r, uint32_t rho_c, uint32_t rho_e,
+                                               uint32_t rho_L, uint32_t *tab0, uint32_t *tab1, uint32_t *tri0,
+                                               uint32_t *tri1)
+{
+    Blk blk{{0u, 0u, 0u, 0u}};
+    int held = -1;
+    // 32-bit word w of the dealer's random stream for this element
+    auto word = [&](int w) -> uint32_t {
+        const int b = w >> 2;
+        if (b != held) blk = A.prg(dk, op, P_TT_RAND + uint32_t(b), e), held = b;
+        const int k = w & 3;
+        return k == 0 ? blk.w[0] : k == 1 ? blk.w[1] : k == 2 ? blk.w[2] : blk.w[3];
+    };
+    auto bit = [&](int i) -> uint32_t { return (word(i >> 5) >> (i & 31)) & 1u; };
+    const uint64_t rhi = P.nd[0] ? (r >> P.s) & ((uint64_t(1) << P.bits[0]) - 1) : 0;
+    const uint64_t rlo = r & ((uint64_t(1) << P.s) - 1);
+    for (int g = 0; g < P.D; g++) {
+        const int p = P.part_of(g), w = P.width(g), W = 1 << w;
+        const uint64_t wm = W == 64 ? ~uint64_t(0) : (uint64_t(1) << W) - 1;
+        const uint32_t alpha =
+            uint32_t(p == 0 ? rhi >> (P.wid[0] * g) : rlo >> (P.wid[1] * (g - P.nd[0]))) & uint32_t(W - 1);
+        uint64_t lt = alpha ? (uint64_t(1) << alpha) - 1 : 0, eq = uint64_t(1) << alpha;
+        if (P.nd[p] == 1) {
+            if (p == 0 ? rho_c : rho_L) lt ^= wm;
+            if (p == 0 && rho_e) eq ^= wm;
+        }
+        // truth bits as a 128-bit value (lo, hi): lt at [0, W), eq at [W, 2W)
+        uint64_t lo = lt, hi = 0;
+        if (P.deq(g)) {
+            if (W < 64) lo |= eq << W;
+            if (W == 32) hi = 0;
+            if (W == 64) hi = eq;
+        }
+        for (int k = 0; k < P.drows(g); k++) {
+            const int row = P.drow0(g) + k;
+            const uint64_t src = k < 2 ? lo : hi;
+            const uint32_t t = uint32_t(src >> (32 * (k & 1)));
+            const uint32_t s0 = word(row);
+            tab0[uint64_t(row) * N + e] = s0;
+            tab1[uint64_t(row) * N + e] = s0 ^ t;
+        }
+    }
+    const int o0 = 32 * P.rows, o1 = o0 + 5 * P.ncomb;
+    uint32_t t0[3] = {0u, 0u, 0u}, t1[3] = {0u, 0u, 0u};
+    for (int q = 0; q < P.ncomb; q++) {
+        const OtComb &C = P.comb[q];
+        uint32_t v0[5], v1[5];
+        for (int k = 0; k < 5; k++) v0[k] = bit(o0 + 5 * q + k);
+        for (int k = 0; k < 3; k++) v1[k] = bit(o1 + 3 * q + k);
+        const uint32_t a = v0[0] ^ v1[0], b = v0[1] ^ v1[1], b2 = v0[2] ^ v1[2];
+        v1[3] = (a & b) ^ v0[3];
+        v1[4] = (a & b2) ^ v0[4];
+        if (C.root) v1[3] ^= C.part == 0 ? rho_c : rho_L, v1[4] ^= C.part == 0 ? rho_e : 0u;
+        if (!C.eq) v0[4] = 0, v1[4] = 0;
+        for (int k = 0; k < 5; k++) {
+            const int i = 5 * q + k;
+            t0[i >> 5] |= v0[k] << (i & 31);
+            t1[i >> 5] |= v1[k] << (i & 31);
+        }
+    }
+    for (int k = 0; k < P.tri_words(); k++) tri0[uint64_t(k) * N + e] = t0[k], tri1[uint64_t(k) * N + e] = t1[k];
+}
+
 // ---- host side (ot.cu)
 
 // the plan of (bw, s), built once per process
 const OtPlan &ot_plan_cached(int bw, int s);
+// the digit plan of an OT or TT gate's layout (built once per process)
+const OtPlan &gate_digit_plan(const GateLayout &L);
 // K_p = AES_dk(p || op || P_OT_PARTY), expanded
 AesKey ot_party_key(const AesKey &dk, uint32_t op, int party);
 // party's first message: its garbled tables [Gmax][N] u32, its digit shares
@@ -245,9 +223,13 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
 // with both parties' openings, open this level's ANDs into open_out;
 // level levels + 1: close the last level and write the masked comparison bits
 // (bits_hi: [lt | eq] x ceil(N/32) words, bits_lo: lt)
+// Truth-table (TT) kinds run the same levels without a garble step: level 1
+// reads the party's digit tables at the digits of x_hat (xhat, TT only),
+// the triple words come from the key (tri ignored), and the last level writes
+// bits_lo only for GATE_LRS_TT.
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
              const uint32_t *open_own, const uint32_t *open_peer, void *state, const uint32_t *tri,
-             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st);
+             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat = nullptr);
 // scratch of one party's OT gate, bytes: garbled tables, state, triple bits
 struct OtScratch {
     uint64_t tables, state, tri;

@@ -72,9 +72,23 @@ extern "C" {
 #define DDG_GATE_RELU_OT 9
 #define DDG_GATE_RELU_ARS_OT 10
 
+/* Same functions (and the same dealer words and round 2) as RELU_SPLIT /
+ * RELU_ARS_SPLIT / LRS, with the comparison bits from dealer truth tables:
+ * every radix-2^w digit of the compared part of x_hat (public) indexes a
+ * table of 2^w (lt, eq) bit pairs that the dealer XOR-shares between the
+ * parties, and the digits are combined by the Beaver AND tree of the OT
+ * kinds (2 levels at bw=32, 4 at bw=64; 1 for the truncation carry, two
+ * 6-bit digits).  No AES and no table message online; the tables are key
+ * bytes (40 per element and party for the bw=32 ReLU, 24 for the carry).
+ * Round 2 is that of the SPLIT kinds (three bit arrays) or of LRS (one). */
+#define DDG_GATE_RELU_TT 11
+#define DDG_GATE_RELU_ARS_TT 12
+#define DDG_GATE_LRS_TT 13
+
 /* ReLU comparison backends of the forward (ddg_relu_backend) */
 #define DDG_RELU_DCF 0
 #define DDG_RELU_OT 1
+#define DDG_RELU_TT 2
 
 const char *ddg_last_error(void);
 int ddg_version(void);
@@ -115,6 +129,13 @@ int ddg_gate_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out);
  *   zero in party 1's key) 3 words 4 total bytes 5 receiver slots 6 digits
  *   7 digits garbled by party 0 8 AND-tree levels 9 AND-tree combines */
 int ddg_ot_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out);
+/* TT kinds: one party's key for n elements, written to out[8]:
+ *   0 offset of the digit tables (rows x n u32, row-major: a digit's lt bits
+ *   over its 2^w values, then its eq bits, packed from bit 0 of its first row)
+ *   1 table rows 2 offset of the triple words (words x n u32: bits 5q..5q+4 =
+ *   a, b, b', c, c' of combine q) 3 triple words 4 words 5 total bytes
+ *   6 digits 7 AND-tree levels */
+int ddg_tt_key_layout(int kind, int bw, int scale, uint64_t n, uint64_t *out);
 
 /* dealer: both parties' keys for n elements with input masks d_rin (n ring
  * elements); writes the output masks d_rout.  Deterministic in (seed, op_id). */
@@ -356,8 +377,10 @@ int ddg_aes_tables(int tables);
  * with the same setting. */
 int ddg_relu_split(int parts);
 /* Comparison backend of the forward's ReLU gates, process-wide:
- * DDG_RELU_OT (default; DDG_GATE_RELU*_OT) or DDG_RELU_DCF (the split chosen
- * by ddg_relu_split).  It changes the key layout like ddg_relu_split. */
+ * DDG_RELU_TT (default; DDG_GATE_RELU*_TT, and DDG_GATE_LRS_TT at the
+ * truncation sites), DDG_RELU_OT (DDG_GATE_RELU*_OT) or DDG_RELU_DCF (the
+ * split chosen by ddg_relu_split).  It changes the key layout like
+ * ddg_relu_split. */
 int ddg_relu_backend(int backend);
 
 /* Test and measurement helper: both parties of one gate on one device, every

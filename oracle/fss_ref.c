@@ -771,21 +771,48 @@ enum { OT_P_PARTY = 0x100, OT_P_AUX = 0x110, OT_P_PAD = 0x120 };
 #define OT_MAXC 16
 
 typedef struct {
+    int mode; /* 0 = OT, 1 = truth-table ReLU, 2 = truth-table carry */
+    int wid[2], bits[2];
+    int deq[OT_MAXD], drows[OT_MAXD], drow0[OT_MAXD], rows;
     int n, s, D, G0, nd[2], levels, ncomb, tri0, naux;
     int cpart[OT_MAXC], ch[OT_MAXC], cl[OT_MAXC], cout[OT_MAXC], ceq[OT_MAXC], croot[OT_MAXC], clevel[OT_MAXC];
     int pfrom[8][2], pto[8][2];
 } ot_plan_t;
 
-static int ot_plan_build(int n, int s, ot_plan_t *P)
+/* digit width of digit g (the top digit of a part keeps the remainder) */
+static int ot_width(const ot_plan_t *P, int g)
+{
+    int p = g < P->nd[0] ? 0 : 1, j = g < P->nd[0] ? g : g - P->nd[0];
+    int rem = P->bits[p] - P->wid[p] * j;
+    return rem < P->wid[p] ? rem : P->wid[p];
+}
+
+/* Parts: OT and TT ReLU compare bits [s, n-1) (hi) and [0, s) (lo); the TT
+ * carry only [0, s).  Digit widths: OT 4 and 4; TT ReLU 5 (bw=32) or 4, and 4;
+ * TT carry 6.  A digit keeps its equality entries unless it is the lowest
+ * digit of the lo part (whose root needs only lt). */
+static int digit_plan_build(int n, int s, int mode, ot_plan_t *P)
 {
     memset(P, 0, sizeof(*P));
-    P->n = n, P->s = s;
-    int bits[2] = {n - 1 - s, s};
-    if (bits[0] < 1 || bits[1] < 1) return 0;
-    P->nd[0] = (bits[0] + 3) / 4, P->nd[1] = (bits[1] + 3) / 4;
+    P->mode = mode, P->n = n, P->s = s;
+    P->bits[0] = mode == 2 ? 0 : n - 1 - s;
+    P->bits[1] = s;
+    P->wid[0] = mode == 1 && n == 32 ? 5 : 4;
+    P->wid[1] = mode == 2 ? 6 : 4;
+    if ((mode != 2 && P->bits[0] < 1) || P->bits[1] < 1) return 0;
+    P->nd[0] = (P->bits[0] + P->wid[0] - 1) / P->wid[0];
+    P->nd[1] = (P->bits[1] + P->wid[1] - 1) / P->wid[1];
     P->D = P->nd[0] + P->nd[1];
     if (P->D > OT_MAXD) return 0;
-    P->G0 = (P->D + 1) / 2;
+    P->G0 = mode == 0 ? (P->D + 1) / 2 : 0;
+    for (int g = 0, row = 0; g < P->D; g++) {
+        int p = g < P->nd[0] ? 0 : 1, j = g < P->nd[0] ? g : g - P->nd[0];
+        P->deq[g] = j > 0 || p == 0;
+        P->drows[g] = ((1 << ot_width(P, g)) * (P->deq[g] ? 2 : 1) + 31) / 32;
+        P->drow0[g] = row;
+        row += P->drows[g];
+        P->rows = row;
+    }
     int k[2] = {P->nd[0], P->nd[1]}, q = 0, l = 0;
     while (k[0] > 1 || k[1] > 1) {
         l++;
@@ -806,15 +833,15 @@ static int ot_plan_build(int n, int s, ot_plan_t *P)
     }
     P->levels = l, P->ncomb = q, P->tri0 = 6 * P->G0;
     P->naux = (P->tri0 + 5 * q + 127) / 128;
-    return P->naux <= 2;
+    return P->naux <= 2 && 5 * q <= 96 && P->rows <= 24;
 }
 
+static int ot_plan_build(int n, int s, ot_plan_t *P) { return digit_plan_build(n, s, 0, P); }
+
 static int ot_part(const ot_plan_t *P, int g) { return g < P->nd[0] ? 0 : 1; }
-static int ot_shift(const ot_plan_t *P, int g) { return g < P->nd[0] ? P->s + 4 * g : 4 * (g - P->nd[0]); }
-static int ot_width(const ot_plan_t *P, int g)
+static int ot_shift(const ot_plan_t *P, int g)
 {
-    int bits = g < P->nd[0] ? P->n - 1 - P->s : P->s, j = g < P->nd[0] ? g : g - P->nd[0];
-    return bits - 4 * j < 4 ? bits - 4 * j : 4;
+    return g < P->nd[0] ? P->s + P->wid[0] * g : P->wid[1] * (g - P->nd[0]);
 }
 static int ot_garbler(const ot_plan_t *P, int g) { return g < P->G0 ? 0 : 1; }
 static int ot_local(const ot_plan_t *P, int g) { return g < P->G0 ? g : g - P->G0; }
@@ -1013,6 +1040,181 @@ void ref_ot_eval_pair(int kind, int n, int s, uint64_t xhat, uint64_t i, const r
     int *out[2] = {bits0, bits1};
     for (int p = 0; p < 2; p++)
         *out[p] = (int)(st[p] & 1) | ((int)((st[p] >> (2 * P.nd[0])) & 1) << 1) | ((int)((st[p] >> 1) & 1) << 2);
+}
+
+/* ----------------------------------------------- truth-table comparison gates
+ *
+ * GATE_RELU_TT (11) / GATE_RELU_ARS_TT (12) / GATE_LRS_TT (13): the functions
+ * and dealer words of GATE_RELU_SPLIT / GATE_RELU_ARS_SPLIT / GATE_LRS.  The
+ * comparison bits come from dealer truth tables: digit g of the compared part
+ * of x_hat (public) indexes a table of its 2^w values holding (lt, eq) =
+ * (1{x < a_g}, 1{x == a_g}) for the mask digit a_g, XOR-shared between the
+ * parties (party 0's rows from the dealer stream, party 1's = party 0's XOR
+ * the truth table; a one-digit part XORs its mask bit into every entry).  The
+ * digits are combined by the AND tree of the OT gates with Beaver triples
+ * whose bits are all explicit: party 0's (a, b, b', c, c') and party 1's
+ * (a, b, b') from the dealer stream, party 1's c = ab ^ c0 (^ rho at a root).
+ * Dealer stream: 32-bit word w = word w mod 4 of AES_dealer(i || op ||
+ * 0x140 + w / 4); party 0's table rows, then its 5 triple bits per combine,
+ * then party 1's 3.  Written independently of the CUDA code. */
+enum { GATE_RELU_TT = 11, GATE_RELU_ARS_TT = 12, GATE_LRS_TT = 13 };
+#define TT_P_RAND 0x140
+
+typedef struct {
+    uint32_t tab[24]; /* table rows */
+    uint32_t tri[3];  /* triple bits, 5 per combine */
+    uint64_t w[32];   /* dealer words of the word kind */
+} ref_tt_key;
+
+static int tt_mode(int kind) { return kind == GATE_LRS_TT ? 2 : 1; }
+static int tt_word_kind(int kind)
+{
+    return kind == GATE_RELU_TT ? GATE_RELU_SPLIT : kind == GATE_RELU_ARS_TT ? GATE_RELU_ARS_SPLIT : GATE_LRS;
+}
+
+int ref_tt_plan_info(int kind, int n, int s, int *out4)
+{
+    ot_plan_t P;
+    if (!digit_plan_build(n, s, tt_mode(kind), &P)) return 0;
+    out4[0] = P.D, out4[1] = P.rows, out4[2] = P.levels, out4[3] = P.ncomb;
+    return 1;
+}
+
+static uint32_t tt_stream_word(const aes_ks *dk, uint32_t op, uint64_t i, int w)
+{
+    uint8_t b[16];
+    ref_prg(dk, op, TT_P_RAND + (uint32_t)(w / 4), i, b);
+    const uint8_t *p = b + 4 * (w % 4);
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+static int tt_stream_bit(const aes_ks *dk, uint32_t op, uint64_t i, int b)
+{
+    return (int)((tt_stream_word(dk, op, i, b / 32) >> (b % 32)) & 1);
+}
+
+uint64_t ref_tt_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint64_t i, uint64_t r_in,
+                       ref_tt_key *k0, ref_tt_key *k1)
+{
+    ot_plan_t P;
+    memset(k0, 0, sizeof(*k0));
+    memset(k1, 0, sizeof(*k1));
+    if (!digit_plan_build(n, s, tt_mode(kind), &P)) return 0;
+    static ref_gate_key g0, g1;
+    uint64_t r_out = ref_gate_keygen(tt_word_kind(kind), n, s, seed, op, i, r_in, &g0, &g1);
+    memcpy(k0->w, g0.w, sizeof(k0->w));
+    memcpy(k1->w, g1.w, sizeof(k1->w));
+    aes_ks dk;
+    ref_dealer_key(seed, &dk);
+    uint8_t blk[16];
+    ref_prg(&dk, op, P_BITS, i, blk);
+    int rho_c = (blk[0] ^ (blk[0] >> 1)) & 1, rho_L = ((blk[0] >> 2) ^ (blk[0] >> 3)) & 1,
+        rho_e = ((blk[0] >> 4) ^ (blk[0] >> 5)) & 1;
+    r_in &= nmask(n);
+    uint64_t rhi = P.nd[0] ? (r_in >> s) & ((1ULL << P.bits[0]) - 1) : 0, rlo = r_in & ((1ULL << s) - 1);
+    for (int g = 0; g < P.D; g++) {
+        int part = ot_part(&P, g), w = ot_width(&P, g), W = 1 << w;
+        uint32_t alpha = (uint32_t)(part == 0 ? rhi >> (P.wid[0] * g) : rlo >> (P.wid[1] * (g - P.nd[0]))) & (W - 1);
+        /* truth bits: entry x -> lt at bit x, eq at bit W + x */
+        uint32_t truth[4] = {0, 0, 0, 0};
+        for (int x = 0; x < W; x++) {
+            int lt = x < (int)alpha, eq = x == (int)alpha;
+            if (P.nd[part] == 1) {
+                lt ^= part == 0 ? rho_c : rho_L;
+                eq ^= part == 0 ? rho_e : 0;
+            }
+            truth[x / 32] |= (uint32_t)lt << (x % 32);
+            if (P.deq[g]) truth[(W + x) / 32] |= (uint32_t)eq << ((W + x) % 32);
+        }
+        for (int k = 0; k < P.drows[g]; k++) {
+            int row = P.drow0[g] + k;
+            uint32_t s0 = tt_stream_word(&dk, op, i, row);
+            k0->tab[row] = s0;
+            k1->tab[row] = s0 ^ truth[k];
+        }
+    }
+    int o0 = 32 * P.rows, o1 = o0 + 5 * P.ncomb;
+    for (int q = 0; q < P.ncomb; q++) {
+        int v0[5], v1[5];
+        for (int k = 0; k < 5; k++) v0[k] = tt_stream_bit(&dk, op, i, o0 + 5 * q + k);
+        for (int k = 0; k < 3; k++) v1[k] = tt_stream_bit(&dk, op, i, o1 + 3 * q + k);
+        int a = v0[0] ^ v1[0], b = v0[1] ^ v1[1], b2 = v0[2] ^ v1[2];
+        v1[3] = (a & b) ^ v0[3];
+        v1[4] = (a & b2) ^ v0[4];
+        if (P.croot[q]) {
+            v1[3] ^= P.cpart[q] == 0 ? rho_c : rho_L;
+            v1[4] ^= P.cpart[q] == 0 ? rho_e : 0;
+        }
+        if (!P.ceq[q]) v0[4] = v1[4] = 0;
+        for (int k = 0; k < 5; k++) {
+            int bit = 5 * q + k;
+            k0->tri[bit / 32] |= (uint32_t)v0[k] << (bit % 32);
+            k1->tri[bit / 32] |= (uint32_t)v1[k] << (bit % 32);
+        }
+    }
+    return r_out;
+}
+
+/*
+ * Both parties' AND-tree protocol for one element, openings in place: each
+ * party's masked comparison-bit shares in the round-1 encoding (bit0 hi lt,
+ * bit1 lo lt, bit2 hi eq; the carry kind only bit1).
+ */
+void ref_tt_eval_pair(int kind, int n, int s, uint64_t xhat, const ref_tt_key *k0, const ref_tt_key *k1, int *bits0,
+                      int *bits1)
+{
+    ot_plan_t P;
+    *bits0 = *bits1 = 0;
+    if (!digit_plan_build(n, s, tt_mode(kind), &P)) return;
+    const ref_tt_key *kk[2] = {k0, k1};
+    xhat &= nmask(n);
+    uint64_t st[2] = {0, 0};
+    for (int p = 0; p < 2; p++)
+        for (int g = 0; g < P.D; g++) {
+            int W = 1 << ot_width(&P, g);
+            uint32_t x = (uint32_t)(xhat >> ot_shift(&P, g)) & (uint32_t)(W - 1);
+            const uint32_t *t = kk[p]->tab + P.drow0[g];
+            uint64_t lt = (t[x / 32] >> (x % 32)) & 1, eq = 0;
+            if (P.deq[g]) eq = (t[(W + x) / 32] >> ((W + x) % 32)) & 1;
+            st[p] |= (lt << (2 * g)) | (eq << (2 * g + 1));
+        }
+#define TRI(p, b) ((int)((kk[p]->tri[(b) / 32] >> ((b) % 32)) & 1))
+    for (int l = 1; l <= P.levels; l++) {
+        int e_[OT_MAXC], f_[OT_MAXC], f2_[OT_MAXC];
+        for (int q = 0; q < P.ncomb; q++) {
+            if (P.clevel[q] != l) continue;
+            int base = 2 * (P.cpart[q] == 0 ? 0 : P.nd[0]);
+            e_[q] = f_[q] = f2_[q] = 0;
+            for (int p = 0; p < 2; p++) {
+                e_[q] ^= (int)((st[p] >> (base + 2 * P.ch[q] + 1)) & 1) ^ TRI(p, 5 * q);
+                f_[q] ^= (int)((st[p] >> (base + 2 * P.cl[q])) & 1) ^ TRI(p, 5 * q + 1);
+                if (P.ceq[q]) f2_[q] ^= (int)((st[p] >> (base + 2 * P.cl[q] + 1)) & 1) ^ TRI(p, 5 * q + 2);
+            }
+        }
+        for (int p = 0; p < 2; p++) {
+            for (int q = 0; q < P.ncomb; q++) {
+                if (P.clevel[q] != l) continue;
+                int base = 2 * (P.cpart[q] == 0 ? 0 : P.nd[0]), p0 = p == 0;
+                int a = TRI(p, 5 * q), b = TRI(p, 5 * q + 1), b2 = TRI(p, 5 * q + 2), c = TRI(p, 5 * q + 3),
+                    c2 = TRI(p, 5 * q + 4);
+                int lt = (int)((st[p] >> (base + 2 * P.ch[q])) & 1) ^ c ^ (f_[q] & a) ^ (e_[q] & b) ^ (p0 & e_[q] & f_[q]);
+                int eq = P.ceq[q] ? (c2 ^ (f2_[q] & a) ^ (e_[q] & b2) ^ (p0 & e_[q] & f2_[q])) : 0;
+                int o = base + 2 * P.cout[q];
+                st[p] = (st[p] & ~(3ULL << o)) | ((uint64_t)lt << o) | ((uint64_t)eq << (o + 1));
+            }
+            for (int pt = 0; pt < 2; pt++) {
+                if (P.pfrom[l][pt] < 0) continue;
+                int b = 2 * (pt == 0 ? 0 : P.nd[0]), o = b + 2 * P.pto[l][pt];
+                uint64_t v = (st[p] >> (b + 2 * P.pfrom[l][pt])) & 3;
+                st[p] = (st[p] & ~(3ULL << o)) | (v << o);
+            }
+        }
+    }
+#undef TRI
+    int *out[2] = {bits0, bits1};
+    for (int p = 0; p < 2; p++) {
+        int hi = P.nd[0] ? (int)(st[p] & 1) | ((int)((st[p] >> 1) & 1) << 2) : 0;
+        *out[p] = hi | ((int)((st[p] >> (2 * P.nd[0])) & 1) << 1);
+    }
 }
 
 /* ------------------------------------------------------------ DPF-LUT */

@@ -22,13 +22,17 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _SO = os.path.join(_HERE, "libfss_ref.so")
 
 (GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
- GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT) = range(11)
+ GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT, GATE_RELU_TT, GATE_RELU_ARS_TT,
+ GATE_LRS_TT) = range(14)
 GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4, GATE_RELU_SPLIT: 16,
                GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7, GATE_RELU_SPLIT3: 40, GATE_RELU_ARS_SPLIT3: 80,
-               GATE_RELU_OT: 16, GATE_RELU_ARS_OT: 32}
+               GATE_RELU_OT: 16, GATE_RELU_ARS_OT: 32, GATE_RELU_TT: 16, GATE_RELU_ARS_TT: 32, GATE_LRS_TT: 4}
 # OT-leaf kinds and the SPLIT kind whose words and round 2 they use
 OT_KINDS = (GATE_RELU_OT, GATE_RELU_ARS_OT)
 OT_WORD_KIND = {GATE_RELU_OT: GATE_RELU_SPLIT, GATE_RELU_ARS_OT: GATE_RELU_ARS_SPLIT}
+# truth-table kinds and the kind whose words and round 2 they use
+TT_KINDS = (GATE_RELU_TT, GATE_RELU_ARS_TT, GATE_LRS_TT)
+TT_WORD_KIND = {GATE_RELU_TT: GATE_RELU_SPLIT, GATE_RELU_ARS_TT: GATE_RELU_ARS_SPLIT, GATE_LRS_TT: GATE_LRS}
 # kinds whose high DCF also outputs equality (three round-1 bit arrays or more)
 SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT, GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3)
 # kinds with a middle DCF with equality output (five round-1 bit arrays)
@@ -67,6 +71,14 @@ class OtKey(ctypes.Structure):
         ("ks", ctypes.c_uint8 * 176),
         ("recv", ctypes.c_uint8 * 18),
         ("c0", ctypes.c_uint32),
+        ("w", ctypes.c_uint64 * 32),
+    ]
+
+
+class TtKey(ctypes.Structure):
+    _fields_ = [
+        ("tab", ctypes.c_uint32 * 24),
+        ("tri", ctypes.c_uint32 * 3),
         ("w", ctypes.c_uint64 * 32),
     ]
 
@@ -127,6 +139,14 @@ def lib():
                                     ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(OtKey), ctypes.POINTER(OtKey)]
         L.ref_ot_keygen.restype = ctypes.c_uint64
         u32p = ctypes.POINTER(ctypes.c_uint32)
+        L.ref_tt_plan_info.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        L.ref_tt_plan_info.restype = ctypes.c_int
+        L.ref_tt_keygen.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32,
+                                    ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(TtKey), ctypes.POINTER(TtKey)]
+        L.ref_tt_keygen.restype = ctypes.c_uint64
+        L.ref_tt_eval_pair.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                       ctypes.POINTER(TtKey), ctypes.POINTER(TtKey), ctypes.POINTER(ctypes.c_int),
+                                       ctypes.POINTER(ctypes.c_int)]
         L.ref_ot_eval_pair.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64,
                                        ctypes.POINTER(OtKey), ctypes.POINTER(OtKey), ctypes.POINTER(ctypes.c_int),
                                        ctypes.POINTER(ctypes.c_int), u32p, u32p]
@@ -256,6 +276,41 @@ def ot_gate_pair(kind: int, n: int, s: int, xhat: int, i: int, k0: OtKey, k1: Ot
     b0, b1, _, _ = ot_eval_pair(kind, n, s, xhat, i, k0, k1)
     o = b0 ^ b1
     return (ot_round2(kind, n, s, 0, xhat, o, k0) + ot_round2(kind, n, s, 1, xhat, o, k1)) & ((1 << n) - 1)
+
+
+def tt_plan_info(kind: int, n: int, s: int) -> dict:
+    o = (ctypes.c_int * 4)()
+    if not lib().ref_tt_plan_info(kind, n, s, o):
+        raise ValueError(f"no truth-table plan for kind={kind} n={n} s={s}")
+    return dict(zip(("digits", "rows", "levels", "combines"), list(o)))
+
+
+def tt_keygen(kind: int, n: int, s: int, seed: int, op: int, i: int, r_in: int):
+    k0, k1 = TtKey(), TtKey()
+    r_out = lib().ref_tt_keygen(kind, n, s, seed, op, i, r_in, ctypes.byref(k0), ctypes.byref(k1))
+    return k0, k1, r_out
+
+
+def tt_eval_pair(kind: int, n: int, s: int, xhat: int, k0: TtKey, k1: TtKey):
+    """Both parties' truth-table comparison for one element: (bits0, bits1) in the round-1 encoding
+    (bit0 hi compare, bit1 lo compare, bit2 hi equality; the carry kind only bit1)."""
+    b0, b1 = ctypes.c_int(), ctypes.c_int()
+    lib().ref_tt_eval_pair(kind, n, s, xhat, ctypes.byref(k0), ctypes.byref(k1), ctypes.byref(b0), ctypes.byref(b1))
+    return b0.value, b1.value
+
+
+def tt_round2(kind: int, n: int, s: int, party: int, xhat: int, bits: int, key: TtKey) -> int:
+    g = GateKey()
+    for j in range(32):
+        g.w[j] = key.w[j]
+    return gate_round2(TT_WORD_KIND[kind], n, s, party, xhat, bits, g)
+
+
+def tt_gate_pair(kind: int, n: int, s: int, xhat: int, k0: TtKey, k1: TtKey) -> int:
+    """Both parties, every round: returns y_hat = y + r_out."""
+    b0, b1 = tt_eval_pair(kind, n, s, xhat, k0, k1)
+    o = b0 ^ b1
+    return (tt_round2(kind, n, s, 0, xhat, o, k0) + tt_round2(kind, n, s, 1, xhat, o, k1)) & ((1 << n) - 1)
 
 
 def lut_keygen(n: int, seed: int, op: int, i: int, alpha: int, r_out: int):

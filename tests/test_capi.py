@@ -44,7 +44,7 @@ def test_split_lrs_layout(ddg):
     with pytest.raises(ddg.DdgError):
         ddg.gate_key_layout(ddg.GATE_LRS_SPLIT, 32, 1, 10)
     with pytest.raises(ddg.DdgError):
-        ddg.gate_key_layout(ddg.GATE_RELU_ARS_OT + 1, 32, 12, 10)
+        ddg.gate_key_layout(ddg.GATE_LRS_TT + 1, 32, 12, 10)
 
 
 def test_ot_gate_layout(ddg):
@@ -73,6 +73,33 @@ def test_ot_gate_layout(ddg):
     assert e.value.code == 1
     with pytest.raises(ddg.DdgError):
         ddg.ot_key_layout(ddg.GATE_RELU_SPLIT, 32, 12, 10)
+
+
+def test_tt_gate_layout(ddg):
+    """Truth-table kinds: digit tables (ReLU at bw=32: 4 hi digits of 5/5/5/4
+    bits and 3 lo digits of 4, 10 rows; the carry: two 6-bit digits, 6 rows),
+    one triple word, then the words of the SPLIT kind or of LRS; far smaller
+    keys than the DCF kinds and no AES key."""
+    from oracle import fss_ref as F
+
+    cases = ((ddg.GATE_RELU_TT, 32, 10, 7, 2, 16), (ddg.GATE_RELU_ARS_TT, 32, 10, 7, 2, 32),
+             (ddg.GATE_LRS_TT, 32, 6, 2, 1, 4), (ddg.GATE_RELU_ARS_TT, 64, 16, 16, 4, 32),
+             (ddg.GATE_LRS_TT, 64, 6, 2, 1, 4))
+    for kind, bw, rows, digits, levels, words in cases:
+        n = 1000
+        lay = ddg.tt_key_layout(kind, bw, 12, n)
+        assert (lay["rows"], lay["digits"], lay["levels"]) == (rows, digits, levels)
+        info = F.tt_plan_info(kind, bw, 12)
+        assert (info["rows"], info["digits"], info["levels"]) == (rows, digits, levels)
+        assert lay["tables"] == 0 and lay["tri"] >= 4 * rows * n and lay["words"] >= lay["tri"] + 4 * lay["tri_words"] * n
+        assert lay["bytes"] == ddg.gate_key_bytes(kind, bw, 12, n) >= lay["words"] + words * (bw // 8) * n
+    assert ddg.gate_key_bytes(ddg.GATE_RELU_ARS_TT, 32, 12, 1000) < ddg.gate_key_bytes(ddg.GATE_RELU_ARS_SPLIT3, 32,
+                                                                                        12, 1000) / 3
+    assert ddg.gate_key_bytes(ddg.GATE_LRS_TT, 32, 12, 1000) < ddg.gate_key_bytes(ddg.GATE_LRS_SPLIT, 32, 12, 1000)
+    assert ddg.gate_round1_arrays(ddg.GATE_LRS_TT, 32, 12) == 1 and ddg.gate_round1_arrays(ddg.GATE_RELU_TT, 32, 12) == 3
+    with pytest.raises(ddg.DdgError) as e:
+        ddg.gate_round1(ddg.GATE_RELU_TT, 32, 12, 10, 1, 1, 1, 1)
+    assert e.value.code == 1
 
 
 def test_three_part_split_layout(ddg):

@@ -58,7 +58,7 @@ def test_usage_errors_exit_1():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("backend", ["dcf", "ot"])
+@pytest.mark.parametrize("backend", ["tt", "ot", "dcf"])
 @pytest.mark.parametrize("bw", [32, 64])
 def test_dealer_then_both_parties_in_one_process(synth, cuda, tmp_path, bw, backend):
     N, B = 5, 2  # three chunks, the last one partial
@@ -74,8 +74,8 @@ def test_dealer_then_both_parties_in_one_process(synth, cuda, tmp_path, bw, back
     r = run([bw, S, 1, 2, keydir, sampledir, B], env=env)
     assert r.returncode == 0, r.stderr
     assert affinities(r.stdout) == want
-    # evaluators with the other backend expect another key layout and refuse the file
-    other = {"DDG_RELU_BACKEND": "dcf" if backend == "ot" else "ot"}
+    # evaluators with another backend expect another key layout and refuse the file
+    other = {"DDG_RELU_BACKEND": "dcf" if backend != "dcf" else "tt"}
     r = run([bw, S, 1, 2, keydir, sampledir, B], env=other)
     assert r.returncode == 2
 

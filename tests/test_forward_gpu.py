@@ -61,15 +61,19 @@ def test_forward_bit_exact(ddg, synth, cuda, bw):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("bw", [32, 64])
-@pytest.mark.parametrize("mode", ["split2", "split3"])
+@pytest.mark.parametrize("mode", ["split2", "split3", "ot"])
 def test_forward_bit_exact_other_relu_forms(ddg, synth, cuda, bw, mode):
-    """The DCF backend of the ReLU gates (two- and three-part splits, one-shot
-    round 1, their own key layouts) gives the same revealed outputs as the
-    default OT-leaf backend."""
+    """The other comparison backends give the same revealed outputs as the
+    default truth-table backend: DCF keys (two- and three-part splits,
+    one-shot round 1) and the OT-leaf gates (garbled digit tables), each with
+    its own key layout."""
     B = 3
     try:
-        ddg.relu_backend(ddg.RELU_DCF)
-        ddg.relu_split(2 if mode == "split2" else 3)
+        if mode == "ot":
+            ddg.relu_backend(ddg.RELU_OT)
+        else:
+            ddg.relu_backend(ddg.RELU_DCF)
+            ddg.relu_split(2 if mode == "split2" else 3)
         inp = synth.Inputs(B, bw, seed=22, with_protein_cnn=False)
         q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=321)
         ins, keep = dev_inputs(inp)
@@ -81,7 +85,7 @@ def test_forward_bit_exact_other_relu_forms(ddg, synth, cuda, bw, mode):
         st = p0.stats()
         assert st["key_bytes_used"] <= ddg.forward_key_bytes(bw, S, B)
     finally:
-        ddg.relu_backend(ddg.RELU_OT)
+        ddg.relu_backend(ddg.RELU_TT)
         ddg.relu_split(3)
 
 

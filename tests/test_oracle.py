@@ -137,3 +137,42 @@ def test_shares_reconstruct(synth):
     for name in ("x", "adj", "mask"):
         s0, s1 = getattr(inp, name + "_sh")
         assert np.array_equal((s0 + s1).astype(np.uint32), getattr(inp, name + "_ring"))
+
+
+@pytest.mark.parametrize("bw", [32, 64])
+def test_tt_and_ot_gates_match_plaintext_and_dcf_bits(bw):
+    """The AND-tree gates of the C oracle reconstruct the plaintext function
+    and open the same masked comparison bits as the DCF split gate of the same
+    dealer seed (random inputs plus the equality branches of the split)."""
+    import numpy as np
+
+    R = RF.Ring(bw)
+    M = (1 << bw) - 1
+    rng = np.random.default_rng(bw)
+    for kind in F.TT_KINDS + F.OT_KINDS:
+        tt = kind in F.TT_KINDS
+        wk = (F.TT_WORD_KIND if tt else F.OT_WORD_KIND)[kind]
+        for i in range(60):
+            r = int(rng.integers(0, 1 << 62)) * 4 + int(rng.integers(0, 4)) & M
+            x = int(rng.integers(0, 1 << 62)) * 4 & M
+            if i % 3 == 1:
+                x = ((r & ~((1 << 12) - 1)) | int(rng.integers(0, 1 << 12))) - r & M
+            if i % 3 == 2:
+                x = ((r & ~63) | int(rng.integers(0, 64))) - r & M
+            if wk == F.GATE_LRS:
+                x &= M >> 1
+            xh = (x + r) & M
+            if tt:
+                k0, k1, ro = F.tt_keygen(kind, bw, 12, 9, 4, i, r)
+                y = F.tt_gate_pair(kind, bw, 12, xh, k0, k1)
+                b0, b1 = F.tt_eval_pair(kind, bw, 12, xh, k0, k1)
+            else:
+                k0, k1, ro = F.ot_keygen(kind, bw, 12, 9, 4, i, r)
+                y = F.ot_gate_pair(kind, bw, 12, xh, i, k0, k1)
+                b0, b1, _, _ = F.ot_eval_pair(kind, bw, 12, xh, i, k0, k1)
+            want = {F.GATE_RELU_SPLIT: R.relu(x), F.GATE_RELU_ARS_SPLIT: R.relu_ars(x, 12),
+                    F.GATE_LRS: R.red(R.signed(x) >> 12)}[wk]
+            assert (y - ro) & M == int(want)
+            g0, g1, _ = F.gate_keygen(wk, bw, 12, 9, 4, i, r)
+            d = F.gate_round1(wk, bw, 12, xh, g0) ^ F.gate_round1(wk, bw, 12, xh, g1)
+            assert b0 ^ b1 == d & (2 if wk == F.GATE_LRS else 7)
