@@ -7,12 +7,13 @@ scale 12, micro-batch B=256 of davis-shaped synthetic graphs, keys resident
 in HBM.  A step is one online forward of B samples by both parties.
 
   N = 1      : both parties on cuda:0 (two host threads, zero-copy openings)
-  N = 2,4,8  : torchrun, one party per process; ranks 0..k-1 are party 0,
-               ranks k..2k-1 party 1, pair i = (i, k+i) exchanges its openings
-               over CUDA IPC (--comm ipc: send slots read in place over NVLink)
-               or NCCL send/recv (--comm nccl); every pair runs its own
-               micro-batch (weak scaling, no cross-pair collective on the data
-               path).
+  N = 2,4,8  : torchrun, one process per GPU, every pair on its own
+               micro-batch (weak scaling, no collective on the data path).
+               --layout colocated (default): every GPU runs both parties of its
+               own pair, as at N = 1.  --layout split: one party per process,
+               ranks 0..k-1 party 0, ranks k..2k-1 party 1, pair i = (i, k+i)
+               exchanging its openings over CUDA IPC (--comm ipc: send slots
+               read in place over NVLink) or NCCL send/recv (--comm nccl).
 
 value    : samples/s of the whole job, inputs (shares) and keys already in HBM.
 e2e      : the same through the C ABI with host (pinned) share buffers: every
@@ -82,9 +83,17 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--lanes", type=int, default=1,
-                    help="N>1: batch lanes per rank, each with its own NCCL communicator and host thread.  Only 1 "
-                         "is accepted: two lanes (two communicators used concurrently from two threads per GPU) "
-                         "stalled for 900 s on the first 2-GPU run, cause not established")
+                    help="N>1 with --comm ipc: batch lanes per rank, each its own party with its own IPC channel, "
+                         "stream and host thread, so one lane computes while another waits for an opening.  "
+                         "With --comm nccl only 1: two lanes (two communicators used concurrently from two threads "
+                         "per GPU) stalled for 900 s on the first 2-GPU run, cause not established")
+    ap.add_argument("--layout", default="colocated", choices=["colocated", "split"],
+                    help="N>1: colocated = every GPU runs both parties of its own pair on its own micro-batch "
+                         "(openings stay on the device; weak scaling with the per-GPU work of N=1); split = party 0 "
+                         "on ranks 0..N/2-1, party 1 on the others, pair i = (i, N/2+i), openings over NVLink "
+                         "(--comm)")
+    ap.add_argument("--peer-timeout", type=int, default=600,
+                    help="N>1: seconds a party waits for its peer at one opening before giving up")
     ap.add_argument("--comm", default="ipc", choices=["ipc", "nccl"],
                     help="N>1: openings between the two parties of a pair over CUDA IPC (default; both ranks on one "
                          "node) or NCCL send/recv")
@@ -105,8 +114,8 @@ def parse():
     a = ap.parse_args()
     if a.relu_split == 0:
         a.relu_split = 2 if a.stream else 3
-    if a.lanes != 1:
-        raise SystemExit("--lanes: only 1 lane per rank is supported (see --help)")
+    if a.lanes < 1 or (a.lanes != 1 and a.comm != "ipc"):
+        raise SystemExit("--lanes: more than 1 lane per rank needs --comm ipc (see --help)")
     if a.stream and a.batch == 256:
         a.batch = 64  # one chunk per party is ~6.4 GB at bw=32
     return a
@@ -139,15 +148,22 @@ def atoms_of(bw):
     return (10, 60) if bw == 32 else (10, 100)
 
 
+def colocated(a, n_gpus):
+    return n_gpus == 1 or a.layout == "colocated"
+
+
 def parallelism(a, n_gpus):
     if n_gpus == 1:
         return "1 GPU, both parties"
+    if colocated(a, n_gpus):
+        return f"{n_gpus} party pairs, both parties of a pair on one GPU (openings on the device), " \
+               "independent micro-batches per GPU"
     over = "CUDA IPC (peer slots read over NVLink)" if a.comm == "ipc" else "NCCL send/recv"
     return f"{n_gpus // 2} party pairs over {over}, one party per GPU"
 
 
 def config_of(a, n_gpus):
-    pairs = max(n_gpus // 2, 1)
+    pairs = n_gpus if colocated(a, n_gpus) else n_gpus // 2
     if a.stream:
         return {
             "workload": f"streaming regime (BASELINE configs[4]): full affinity branch, bw={a.bw}, scale={a.scale}, "
@@ -354,21 +370,22 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
-        if world % 2:
-            raise SystemExit("multi-GPU runs need an even number of GPUs (one party per GPU)")
+        if world % 2 and a.layout == "split":
+            raise SystemExit("the split layout needs an even number of GPUs (one party per GPU)")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
     B, bw, s = a.batch, a.bw, a.scale
     blob = synth.weights_blob(synth.quantize_weights(synth.affinity_weights(5), s))
 
     # -------- parties, keys, inputs
     streams = []
-    if world == 1:
-        pairs, pair = 1, 0
-        inp = synth.Inputs(B, bw, seed=1000, atoms=atoms_of(bw))
+    colo = colocated(a, world)
+    if colo:
+        pairs, pair = world, rank
+        inp = synth.Inputs(B, bw, seed=1000 + pair, atoms=atoms_of(bw))
         parties = [ddg.Party(0, bw, s, local), ddg.Party(1, bw, s, local)]
         if a.stream:
             kb = ddg.forward_key_bytes(bw, s, B)
-            chunks = ddg.dealer_chunks(bw, s, B, [1000 + i for i in range(a.stream)], blob, local)
+            chunks = ddg.dealer_chunks(bw, s, B, [1000 + 97 * pair + i for i in range(a.stream)], blob, local)
             for p in parties:
                 p.set_weights(blob)
             streams = [ddg.KeyStream(p, B) for p in parties]
@@ -376,7 +393,7 @@ def main():
                 for ks, h in zip(streams, c):
                     ks.add_host_chunk(h.data_ptr())
         else:
-            kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000, blob, device)
+            kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 1000 + 97 * pair, blob, device)
             for p, k in zip(parties, (k0, k1)):
                 p.set_weights(blob)
                 p.bind_keys(k.data_ptr(), kb)
@@ -418,7 +435,7 @@ def main():
                 torch.cuda.empty_cache()
                 P.bind_keys(mine.data_ptr(), kb)
                 keep_keys.append(mine)
-            P.set_timeout(600_000)
+            P.set_timeout(1000 * a.peer_timeout)
             if a.comm == "ipc":
                 P.connect_ipc(uids[0][pair][lane], ddg.forward_max_exchange_bytes(bw, s, Bl))
             else:
@@ -427,7 +444,7 @@ def main():
         bufs = [share_buffers(torch, inp, party, device, (lane * Bl, (lane + 1) * Bl)) for lane in range(lanes)]
 
     def step(on_host):
-        if world == 1:
+        if colo:
             ins = [[t.data_ptr() for t in (bufs[p][1] if on_host else bufs[p][0])] for p in (0, 1)]
             if streams:
                 return ddg.forward_pair_streamed(streams[0], streams[1], ins[0], ins[1], on_host=on_host)
@@ -483,7 +500,7 @@ def main():
     clk = clocks.window(*tw)
     timing_on[0] = False
     stats = parties[0].stats()
-    if world > 1:
+    if not colo:
         lane_stats = [p.stats() for p in parties]
         stats = {"bytes_sent": sum(x["bytes_sent"] for x in lane_stats), "rounds": lane_stats[0]["rounds"],
                  "key_bytes_used": sum(x["key_bytes_used"] for x in lane_stats)}
@@ -507,14 +524,14 @@ def main():
         ms_e2e = timed(True, a.steps)
         # both parties' input shares of every pair cross host->device each step
         own = [sum(int(t.numel()) for t in b[1]) for b in bufs]
-        h2d = sum(own) if world == 1 else 2 * sum(own)
+        h2d = sum(own) if colo else 2 * sum(own)
         e2e = {"value": pairs * B * a.steps / (ms_e2e / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": h2d * pairs, "d2h_bytes_per_step": B * (bw // 8) * pairs,
                "ms_per_step": ms_e2e / a.steps}
 
     value = pairs * B * a.steps / (ms / 1e3)
     peak, peak_kind = measured_peaks()
-    if world == 1:
+    if colo:
         union = dcf[0]["pair_union_ms"]
         alg = dcf[0]["bytes"] + dcf[1]["bytes"]
         aes = dcf[0]["aes_blocks"] + dcf[1]["aes_blocks"]

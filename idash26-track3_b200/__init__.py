@@ -77,6 +77,7 @@ SIGNATURES = {
     "ddg_party_connect_nccl": (_i32, [_vp, _vp, _i32, _i32, _i32]),
     "ddg_party_set_timeout": (_i32, [_vp, _i32]),
     "ddg_party_connect_ipc": (_i32, [_vp, ctypes.c_char_p, _u64]),
+    "ddg_party_exchange_probe": (_i32, [_vp, _u64, _i32, ctypes.POINTER(ctypes.c_double)]),
     "ddg_forward_max_exchange_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_forward_key_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_forward_eval": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
@@ -255,6 +256,12 @@ class Party:
 
     def set_timeout(self, ms: int):
         check(lib().ddg_party_set_timeout(self.h, ms))
+
+    def exchange_probe(self, nbytes: int, iters: int) -> float:
+        """ms per opening of nbytes through this party's channel (both parties call it together)."""
+        out = ctypes.c_double()
+        check(lib().ddg_party_exchange_probe(self.h, nbytes, iters, ctypes.byref(out)))
+        return out.value
 
     def forward(self, batch, x, adj, mask, prot, on_host=False):
         """One online forward.  x/adj/mask/prot: this party's shares (device

@@ -351,6 +351,55 @@ uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch)
     return n * per;
 }
 
+}  // extern "C"
+
+// consumer of a probe exchange: one thread reads the peer's first word
+static __global__ void k_probe_read(const uint32_t *peer, uint32_t *sink)
+{
+    if (threadIdx.x == 0 && blockIdx.x == 0) *sink += peer[0];
+}
+
+extern "C" {
+
+int ddg_party_exchange_probe(ddg_party *h, uint64_t bytes, int iters, double *ms_per_exchange)
+{
+    DDG_CHECK(h && h->P.chan && iters > 0 && ms_per_exchange && bytes >= 4, DDG_ERR_ARG, "bad probe arguments");
+    Party &P = h->P;
+    DDG_CUDA(cudaSetDevice(P.device));
+    cudaStream_t st = P.stream;
+    void *send = nullptr, *recv = nullptr;
+    uint32_t *sink = nullptr;
+    DDG_CUDA(cudaMalloc(&send, bytes));
+    DDG_CUDA(cudaMalloc(&recv, bytes));
+    DDG_CUDA(cudaMalloc(&sink, 4));
+    cudaEvent_t a = nullptr, b = nullptr;
+    DDG_CUDA(cudaEventCreate(&a));
+    DDG_CUDA(cudaEventCreate(&b));
+    int err = DDG_OK;
+    auto one = [&](int i) {
+        if (err != DDG_OK) return;
+        if (cudaMemsetAsync(send, i & 0xff, bytes, st) != cudaSuccess) err = DDG_ERR_CUDA;
+        const void *peer = nullptr;
+        if (err == DDG_OK) err = P.chan->exchange(P.party, st, send, bytes, recv, &peer);
+        if (err == DDG_OK) k_probe_read<<<1, 32, 0, st>>>(static_cast<const uint32_t *>(peer), sink);
+    };
+    for (int i = 0; i < 3; i++) one(i);
+    if (err == DDG_OK) err = P.chan->barrier(P.party, st);
+    if (err == DDG_OK && cudaStreamSynchronize(st) != cudaSuccess) err = DDG_ERR_CUDA;
+    if (err == DDG_OK && cudaEventRecord(a, st) != cudaSuccess) err = DDG_ERR_CUDA;
+    for (int i = 0; i < iters; i++) one(i);
+    if (err == DDG_OK && cudaEventRecord(b, st) != cudaSuccess) err = DDG_ERR_CUDA;
+    if (err == DDG_OK) err = P.chan->barrier(P.party, st);
+    if (err == DDG_OK && cudaStreamSynchronize(st) != cudaSuccess) err = DDG_ERR_CUDA;
+    float ms = 0;
+    if (err == DDG_OK) cudaEventElapsedTime(&ms, a, b);
+    *ms_per_exchange = double(ms) / iters;
+    cudaEventDestroy(a), cudaEventDestroy(b);
+    cudaFree(send), cudaFree(recv), cudaFree(sink);
+    if (err == DDG_ERR_CUDA) set_last_error("exchange probe: CUDA call failed");
+    return err;
+}
+
 int ddg_party_set_timeout(ddg_party *h, int timeout_ms)
 {
     DDG_CHECK(h && timeout_ms > 0, DDG_ERR_ARG, "bad timeout");

@@ -215,6 +215,11 @@ int ddg_party_connect_nccl(ddg_party *party, const void *unique_id128, int nrank
  * Waits on the peer are bounded by the party's timeout (ddg_party_set_timeout
  * before connecting, default 60 s) and end in DDG_ERR_PEER. */
 int ddg_party_connect_ipc(ddg_party *party, const char *name, uint64_t slot_bytes);
+/* Diagnostics: `iters` openings of `bytes` through the party's channel (a
+ * memset as producer, a one-thread read of the peer's bytes as consumer),
+ * both parties calling it together; ms per opening from CUDA events on the
+ * party's stream. */
+int ddg_party_exchange_probe(ddg_party *party, uint64_t bytes, int iters, double *ms_per_exchange);
 /* the largest single exchange of one forward of `batch` samples, in bytes
  * (with the OT ReLU backend selected: its garbled tables) */
 uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch);
