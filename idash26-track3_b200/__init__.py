@@ -54,6 +54,9 @@ SIGNATURES = {
     "ddg_lut_key_bytes": (_u64, [_i32, _u64]),
     "ddg_lut_keygen": (_i32, [_i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ddg_lut_eval": (_i32, [_i32, _u64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_tt_lut_key_bytes": (_u64, [_i32, _u64]),
+    "ddg_tt_lut_keygen": (_i32, [_i32, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ddg_tt_lut_eval": (_i32, [_i32, _u64, _vp, _vp, _vp, _vp]),
     "ddg_mul_share": (_i32, [_i32, _i32, _u64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_matmul_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ddg_fc_share": (_i32, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),

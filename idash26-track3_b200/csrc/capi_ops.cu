@@ -70,6 +70,42 @@ int ddg_lut_keygen(int bw, uint64_t n, uint64_t seed, uint32_t op_id, const void
                                            static_cast<const uint64_t *>(d_rout), k0, k1, st);
 }
 
+uint64_t ddg_tt_lut_key_bytes(int bw, uint64_t n)
+{
+    if (check_bw(bw) != DDG_OK) return 0;
+    return tt_lut_layout(bw, n).bytes;
+}
+
+int ddg_tt_lut_keygen(int bw, uint64_t n, uint64_t seed, uint32_t op_id, const void *d_alpha_mask, const void *d_rout,
+                      const void *d_table, void *d_key0, void *d_key1, void *stream)
+{
+    DDG_TRY(check_bw(bw));
+    DDG_CHECK(n == 0 || (d_alpha_mask && d_rout && d_table && d_key0 && d_key1), DDG_ERR_ARG, "null pointer");
+    TtLutLayout L = tt_lut_layout(bw, n);
+    AesKey dk = dealer_key(seed);
+    auto st = static_cast<cudaStream_t>(stream);
+    auto *k0 = static_cast<uint8_t *>(d_key0), *k1 = static_cast<uint8_t *>(d_key1);
+    return bw == 32 ? tt_lut_keygen<uint32_t>(L, dk, op_id, static_cast<const uint32_t *>(d_alpha_mask),
+                                              static_cast<const uint32_t *>(d_rout),
+                                              static_cast<const uint32_t *>(d_table), k0, k1, st)
+                    : tt_lut_keygen<uint64_t>(L, dk, op_id, static_cast<const uint64_t *>(d_alpha_mask),
+                                              static_cast<const uint64_t *>(d_rout),
+                                              static_cast<const uint64_t *>(d_table), k0, k1, st);
+}
+
+int ddg_tt_lut_eval(int bw, uint64_t n, const void *d_xhat, const void *d_key, void *d_share, void *stream)
+{
+    DDG_TRY(check_bw(bw));
+    DDG_CHECK(n == 0 || (d_xhat && d_key && d_share), DDG_ERR_ARG, "null pointer");
+    TtLutLayout L = tt_lut_layout(bw, n);
+    auto st = static_cast<cudaStream_t>(stream);
+    auto *k = static_cast<const uint8_t *>(d_key);
+    return bw == 32 ? tt_lut_eval<uint32_t>(L, static_cast<const uint32_t *>(d_xhat), k,
+                                            static_cast<uint32_t *>(d_share), st)
+                    : tt_lut_eval<uint64_t>(L, static_cast<const uint64_t *>(d_xhat), k,
+                                            static_cast<uint64_t *>(d_share), st);
+}
+
 int ddg_lut_eval(int bw, uint64_t n, int party, const void *d_xhat, const void *d_table, const void *d_key,
                  void *d_share, void *stream)
 {

@@ -38,8 +38,8 @@ LocalPairChannel::~LocalPairChannel()
 
 void LocalPairChannel::fail()
 {
+    broken.store(true);
     std::lock_guard<std::mutex> g(mu);
-    broken = true;
     cv.notify_all();
 }
 
@@ -47,24 +47,36 @@ int LocalPairChannel::exchange(int party, cudaStream_t st, const void *send, uin
                                const void **peer)
 {
     const int q = 1 - party;
-    std::unique_lock<std::mutex> lk(mu);
     const uint64_t g = ++gen[party];
     cudaEvent_t e = ev[party][g & 1];
     DDG_CUDA(cudaEventRecord(e, st));
-    slot[party][g & 1] = Slot{send, bytes, g};
-    cv.notify_all();
-    const bool ok = cv.wait_for(lk, std::chrono::milliseconds(timeout_ms),
-                                [&] { return broken || slot[q][g & 1].gen == g; });
-    DDG_CHECK(!broken, DDG_ERR_PEER, "peer party failed during exchange %llu", (unsigned long long)g);
-    if (!ok) {
-        broken = true;
+    slot[party][g & 1] = Slot{send, bytes};
+    pub[party].store(g);  // sequentially consistent: ordered against the sleepers check below
+    if (sleepers.load() > 0) {
+        std::lock_guard<std::mutex> lk(mu);
         cv.notify_all();
+    }
+    // the peer's generation g: spin first, then sleep with the deadline
+    bool ready = false;
+    for (int it = 0; it < 200000 && !(ready = pub[q].load() >= g) && !broken.load(); it++) {
+        if (it > 2000) std::this_thread::yield();
+    }
+    if (!ready && !broken.load()) {
+        std::unique_lock<std::mutex> lk(mu);
+        sleepers.fetch_add(1);
+        ready = cv.wait_for(lk, std::chrono::milliseconds(timeout_ms),
+                            [&] { return broken.load() || pub[q].load() >= g; });
+        sleepers.fetch_sub(1);
+        ready = ready && pub[q].load() >= g;
+    }
+    DDG_CHECK(!broken.load(), DDG_ERR_PEER, "peer party failed during exchange %llu", (unsigned long long)g);
+    if (!ready) {
+        fail();
         set_last_error("peer party did not reach exchange %llu within %d ms", (unsigned long long)g, timeout_ms);
         return DDG_ERR_PEER;
     }
     const Slot s = slot[q][g & 1];
     cudaEvent_t pe = ev[q][g & 1];
-    lk.unlock();
     DDG_CHECK(s.bytes == bytes, DDG_ERR_PEER, "exchange %llu size mismatch: %llu vs peer %llu",
               (unsigned long long)g, (unsigned long long)bytes, (unsigned long long)s.bytes);
     DDG_CUDA(cudaStreamWaitEvent(st, pe, 0));

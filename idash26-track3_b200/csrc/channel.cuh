@@ -11,6 +11,7 @@
 //     read in place over NVLink, ordered by interprocess events and a shared-
 //     memory block of generation counters.
 #pragma once
+#include <atomic>
 #include <condition_variable>
 #include <cstdint>
 #include <mutex>
@@ -38,19 +39,27 @@ struct Channel {
     int timeout_ms = 60000;
 };
 
+// Handoff between the two party threads: each exchange publishes the party's
+// buffer for generation g with a release store of pub[party] = g, then spins
+// (bounded) for the peer's g before sleeping on the condition variable; a
+// sleeping waiter is counted in `sleepers` so that a publisher only takes the
+// mutex to notify when someone sleeps.  The spin keeps the handoff of the
+// ~100 openings of a forward at the latency of a cache line, where a futex
+// wake-up costs tens of microseconds of host time that small gates cannot hide.
 struct LocalPairChannel : Channel {
     struct Slot {
         const void *ptr = nullptr;
         uint64_t bytes = 0;
-        uint64_t gen = 0;
     };
     std::mutex mu;
     std::condition_variable cv;
     Slot slot[2][2];        // [party][gen & 1]
     uint64_t gen[2] = {0, 0};
+    std::atomic<uint64_t> pub[2] = {{0}, {0}};
+    std::atomic<int> sleepers{0};
+    std::atomic<bool> broken{false};
     cudaEvent_t ev[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
     int dev[2] = {0, 0};
-    bool broken = false;
     LocalPairChannel(int dev0, int dev1);
     ~LocalPairChannel() override;
     int exchange(int party, cudaStream_t st, const void *send, uint64_t bytes, void *recv, const void **peer) override;

@@ -282,6 +282,7 @@ enum Purpose : uint32_t {
     P_MID_S0 = 9, P_MID_DELTA = 10,  // middle DCF of the three-part split gates
                                      // 0x100..0x12f: OT gates (ot.cuh), 0x140..: TT gates
     P_SHARE = 16,  // share0 of dealer word k uses purpose P_SHARE + k (k < 80)
+    P_TT_LUT = 0x180,  // party 0's truth-table LUT entries
 };
 
 }  // namespace ddg

@@ -180,7 +180,13 @@ struct SizeExec : ExecBase<T> {
     Tn<T> reveal_input(int, uint64_t n) { take(words(n)); auto t = mk(n); t.ms0 = mark; return t; }
     Tn<T> reveal_degree(uint64_t rows, int) { take(words(rows)); auto t = mk(rows); t.ms0 = mark; return t; }
     Tn<T> reveal_public(int, uint64_t n) { return mk(n); }
-    Tn<T> lut(const Tn<T> &d) { take(lut_layout(this->bw, d.n).bytes); auto t = mk(d.n); t.ms0 = mark; return t; }
+    Tn<T> lut(const Tn<T> &d)
+    {
+        take(relu_backend() == DDG_RELU_TT ? tt_lut_layout(this->bw, d.n).bytes : lut_layout(this->bw, d.n).bytes);
+        auto t = mk(d.n);
+        t.ms0 = mark;
+        return t;
+    }
     void ensure_ms(Tn<T> &t) { if (!t.ms0) { take(words(t.n)); t.ms0 = mark; } }
     Tn<T> mul(Tn<T> &a, Tn<T> &b, Bcast, const EwShape &sh) { ensure_ms(a); ensure_ms(b); take(words(sh.n)); return mk(sh.n); }
     Tn<T> matmul(Tn<T> &A, Tn<T> &H, int K)
@@ -252,10 +258,21 @@ struct DealerExec : ExecBase<T> {
     }
     Tn<T> lut(const Tn<T> &d)
     {
-        LutLayout L = lut_layout(this->bw, d.n);
-        uint64_t o = take(L.bytes);
         Tn<T> t;
         t.n = d.n;
+        if (relu_backend() == DDG_RELU_TT) {
+            TtLutLayout L = tt_lut_layout(this->bw, d.n);
+            uint64_t o = take(L.bytes);
+            t.v = rand(d.n);
+            if (this->err == DDG_OK)
+                ok(tt_lut_keygen<T>(L, dk, this->op++, d.v, t.v, static_cast<const T *>(w->table), k0 + o, k1 + o,
+                                    this->st));
+            t.ms0 = reinterpret_cast<const T *>(k0 + o + L.rout);
+            t.ms1 = reinterpret_cast<const T *>(k1 + o + L.rout);
+            return t;
+        }
+        LutLayout L = lut_layout(this->bw, d.n);
+        uint64_t o = take(L.bytes);
         t.v = rand(d.n);
         if (this->err == DDG_OK) ok(lut_keygen<T>(L, dk, this->op++, d.v, t.v, k0 + o, k1 + o, this->st));
         t.ms0 = reinterpret_cast<const T *>(k0 + o + L.rout);
@@ -443,11 +460,19 @@ struct EvalExec : ExecBase<T> {
     }
     Tn<T> lut(const Tn<T> &d)
     {
-        LutLayout L = lut_layout(this->bw, d.n);
-        const uint8_t *k = key_at(L.bytes);
         Tn<T> t;
         t.n = d.n;
         T *sh = alloc(d.n);
+        if (relu_backend() == DDG_RELU_TT) {
+            TtLutLayout L = tt_lut_layout(this->bw, d.n);
+            const uint8_t *k = key_at(L.bytes);
+            if (this->err == DDG_OK) ok(tt_lut_eval<T>(L, d.v, k, sh, this->st));
+            t.v = open(sh, d.n);
+            t.ms0 = reinterpret_cast<const T *>(k + L.rout);
+            return t;
+        }
+        LutLayout L = lut_layout(this->bw, d.n);
+        const uint8_t *k = key_at(L.bytes);
         if (this->err == DDG_OK)
             ok(lut_eval<T>(L, p, d.v, static_cast<const T *>(P->w.table), k, sh, this->st));
         t.v = open(sh, d.n);

@@ -106,4 +106,23 @@ template <typename T>
 int lut_eval(const LutLayout &L, int party, const T *xhat, const T *table, const uint8_t *key, T *share,
              cudaStream_t st);
 
+// ------------------------------------------------------------------ truth-table LUT (lut.cu)
+//
+// The same 8-bit look-up for the truth-table backend: the dealer gives party
+// p a table T_p[256] per lookup with T_0[u] + T_1[u] = table[(u - alpha) mod
+// 256] + r_out (alpha the input mask), and party p's share is T_p[x_hat mod
+// 256]: one word read, no AES.  Layout of n lookups: tab[256][n] words |
+// rout share[n] words (as the DPF layout, for the masks of later products).
+struct TtLutLayout {
+    int bw = 0;
+    uint64_t n = 0, tab = 0, rout = 0, bytes = 0;
+};
+TtLutLayout tt_lut_layout(int bw, uint64_t n, uint64_t base = 0);
+
+template <typename T>
+int tt_lut_keygen(const TtLutLayout &L, const AesKey &dk, uint32_t op, const T *alpha_mask, const T *rout,
+                  const T *table, uint8_t *k0, uint8_t *k1, cudaStream_t st);
+template <typename T>
+int tt_lut_eval(const TtLutLayout &L, const T *xhat, const uint8_t *key, T *share, cudaStream_t st);
+
 }  // namespace ddg

@@ -211,6 +211,109 @@ int lut_eval(const LutLayout &L, int party, const T *xhat, const T *table, const
     return DDG_OK;
 }
 
+// ---------------------------------------------------------------- truth-table LUT
+
+TtLutLayout tt_lut_layout(int bw, uint64_t n, uint64_t base)
+{
+    TtLutLayout l;
+    l.bw = bw;
+    l.n = n;
+    l.tab = align256(base);
+    l.rout = align256(l.tab + 256 * n * uint64_t(bw / 8));
+    l.bytes = align256(l.rout + n * uint64_t(bw / 8)) - align256(base);
+    return l;
+}
+
+template <typename T>
+struct TtLutKeygenArgs {
+    TtLutLayout L;
+    AesKey dk;
+    uint32_t op;
+    const T *alpha_mask, *rout, *table;
+    uint8_t *k0, *k1;
+};
+
+// dealer: party 0's entries from the PRG (4 or 2 words per block), party 1's
+// = table[(u - alpha) mod 256] + r_out - party 0's
+template <typename T, class E>
+__global__ void __launch_bounds__(E::THREADS, E::CTAS) tt_lut_keygen_kernel(const __grid_constant__ TtLutKeygenArgs<T> a)
+{
+    extern __shared__ uint32_t smem_tab[];
+    __shared__ T tab[256];
+    E::stage(smem_tab);
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = a.table[i];
+    __syncthreads();
+    E A(smem_tab);
+    constexpr int EPB = 16 / sizeof(T);
+    const uint64_t n = a.L.n;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
+        const uint32_t alpha = uint32_t(a.alpha_mask[i]) & 255u;
+        const T ro = a.rout[i];
+        T *t0 = reinterpret_cast<T *>(a.k0 + a.L.tab), *t1 = reinterpret_cast<T *>(a.k1 + a.L.tab);
+        for (int b = 0; b < 256 / EPB; b++) {
+            const Blk r = A.prg(a.dk.rk, a.op, P_TT_LUT, uint64_t(b) * n + i);
+#pragma unroll
+            for (int k = 0; k < EPB; k++) {
+                const int u = b * EPB + k;
+                const T s0 = blk_slot<T>(r, k);
+                t0[uint64_t(u) * n + i] = s0;
+                t1[uint64_t(u) * n + i] = T(tab[(uint32_t(u) - alpha) & 255u] + ro - s0);
+            }
+        }
+        const T sh = ring_of<T>(A.prg(a.dk.rk, a.op, P_SHARE, i));
+        reinterpret_cast<T *>(a.k0 + a.L.rout)[i] = sh;
+        reinterpret_cast<T *>(a.k1 + a.L.rout)[i] = ro - sh;
+    }
+}
+
+template <typename T>
+__global__ void tt_lut_eval_kernel(const TtLutLayout L, const T *xhat, const uint8_t *key, T *share)
+{
+    const T *tab = reinterpret_cast<const T *>(key + L.tab);
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < L.n; i += uint64_t(gridDim.x) * blockDim.x)
+        share[i] = __ldcs(tab + uint64_t(uint32_t(xhat[i]) & 255u) * L.n + i);
+}
+
+template <typename T>
+int tt_lut_keygen(const TtLutLayout &L, const AesKey &dk, uint32_t op, const T *alpha_mask, const T *rout,
+                  const T *table, uint8_t *k0, uint8_t *k1, cudaStream_t st)
+{
+    if (!L.n) return DDG_OK;
+    DDG_CHECK(k0 && k1 && table, DDG_ERR_ARG, "truth-table LUT keygen needs both keys and the table");
+    DDG_TRY(aes_device_init());
+    TtLutKeygenArgs<T> a{L, dk, op, alpha_mask, rout, table, k0, k1};
+    if (aes_tables() == 4) {
+        DDG_CUDA(cudaFuncSetAttribute(tt_lut_keygen_kernel<T, AesLane4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      AesLane4::SMEM));
+        tt_lut_keygen_kernel<T, AesLane4><<<aes_blocks<AesLane4>(L.n), AesLane4::THREADS, AesLane4::SMEM, st>>>(a);
+    } else {
+        DDG_CUDA(cudaFuncSetAttribute(tt_lut_keygen_kernel<T, AesLane2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      AesLane2::SMEM));
+        tt_lut_keygen_kernel<T, AesLane2><<<aes_blocks<AesLane2>(L.n), AesLane2::THREADS, AesLane2::SMEM, st>>>(a);
+    }
+    note_launch();
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template <typename T>
+int tt_lut_eval(const TtLutLayout &L, const T *xhat, const uint8_t *key, T *share, cudaStream_t st)
+{
+    if (!L.n) return DDG_OK;
+    const uint64_t blocks = (L.n + 255) / 256;
+    tt_lut_eval_kernel<T><<<int(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(L, xhat, key, share);
+    note_launch();
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template int tt_lut_keygen<uint32_t>(const TtLutLayout &, const AesKey &, uint32_t, const uint32_t *, const uint32_t *,
+                                     const uint32_t *, uint8_t *, uint8_t *, cudaStream_t);
+template int tt_lut_keygen<uint64_t>(const TtLutLayout &, const AesKey &, uint32_t, const uint64_t *, const uint64_t *,
+                                     const uint64_t *, uint8_t *, uint8_t *, cudaStream_t);
+template int tt_lut_eval<uint32_t>(const TtLutLayout &, const uint32_t *, const uint8_t *, uint32_t *, cudaStream_t);
+template int tt_lut_eval<uint64_t>(const TtLutLayout &, const uint64_t *, const uint8_t *, uint64_t *, cudaStream_t);
+
 template int lut_keygen<uint32_t>(const LutLayout &, const AesKey &, uint32_t, const uint32_t *, const uint32_t *,
                                   uint8_t *, uint8_t *, cudaStream_t);
 template int lut_keygen<uint64_t>(const LutLayout &, const AesKey &, uint32_t, const uint64_t *, const uint64_t *,

@@ -305,6 +305,17 @@ int ddg_lut_keygen(int bw, uint64_t n, uint64_t seed, uint32_t op_id, const void
                    void *d_key0, void *d_key1, void *stream);
 int ddg_lut_eval(int bw, uint64_t n, int party, const void *d_xhat, const void *d_table, const void *d_key,
                  void *d_share, void *stream);
+/* Truth-table form of the same look-up (the truth-table backend's, used by
+ * the forward with ddg_relu_backend(DDG_RELU_TT)): the dealer gives party p
+ * a table T_p[256] per lookup with T_0[u] + T_1[u] = table[(u - alpha) mod
+ * 256] + r_out, so party p's share of table[(x_hat - alpha) mod 256] + r_out
+ * is T_p[x_hat mod 256] (one word read, no AES).  Key layout: 256 x n ring
+ * words (entry-major), then n words of the party's share of r_out.  The
+ * dealer needs the public table (256 ring words on the device). */
+uint64_t ddg_tt_lut_key_bytes(int bw, uint64_t n);
+int ddg_tt_lut_keygen(int bw, uint64_t n, uint64_t seed, uint32_t op_id, const void *d_alpha_mask, const void *d_rout,
+                      const void *d_table, void *d_key0, void *d_key1, void *stream);
+int ddg_tt_lut_eval(int bw, uint64_t n, const void *d_xhat, const void *d_key, void *d_share, void *stream);
 
 /* Beaver elementwise product (replaces gpuMul of DDGOrca::mul,
  * gpu_mpc/ddg_orca.h:43-63, and of secure_adj_norm.h:609-651):

@@ -56,6 +56,48 @@ def test_lut_matches_oracle(ddg, cuda, bw):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("bw", [32, 64])
+def test_tt_lut_matches_restated_keys(ddg, cuda, bw):
+    """Truth-table LUT: every key entry equals its restatement (party 0's entry u of
+    lookup i = slot u mod (16 / word) of AES_dealer(i + (u div slots) * n || op || 0x180), party
+    1's = table[(u - alpha) mod 256] + r_out - party 0's), the shares are the entries at
+    x_hat mod 256, and they reconstruct table[degree] + r_out for every degree 0..138."""
+    L = ddg.lib()
+    dt = ring_dt(bw)
+    W = bw // 8
+    rng = np.random.default_rng(bw + 5)
+    degs = np.concatenate([np.arange(139), rng.integers(0, 139, size=61)]).astype(dt)
+    n = degs.size
+    r_deg, r_out = rnd(rng, bw, n), rnd(rng, bw, n)
+    kb = int(L.ddg_tt_lut_key_bytes(bw, n))
+    k0, k1 = dev_bytes(kb), dev_bytes(kb)
+    table = invsqrt_table(12, 138).astype(dt)
+    d_a, d_ro, d_t = to_dev(r_deg), to_dev(r_out), to_dev(table)
+    ddg.check(L.ddg_tt_lut_keygen(bw, n, 3, 11, ptr(d_a), ptr(d_ro), ptr(d_t), ptr(k0), ptr(k1), None))
+    xh = (degs + r_deg).astype(dt)
+    d_x = to_dev(xh)
+    sh = [dev_bytes(n * W) for _ in range(2)]
+    for p, k in ((0, k0), (1, k1)):
+        ddg.check(L.ddg_tt_lut_eval(bw, n, ptr(d_x), ptr(k), ptr(sh[p]), None))
+    sync()
+    s0, s1 = from_dev(sh[0], dt, n), from_dev(sh[1], dt, n)
+    assert np.array_equal((s0 + s1 - r_out).astype(dt), table[degs.astype(np.int64)])
+    t0 = k0.cpu().numpy()[: 256 * n * W].view(dt).reshape(256, n)
+    t1 = k1.cpu().numpy()[: 256 * n * W].view(dt).reshape(256, n)
+    M = (1 << bw) - 1
+    per = 16 // W
+    for i in list(range(0, n, 17)) + [n - 1]:
+        a = int(r_deg[i]) & 255
+        for u in range(0, 256, 37):
+            blk = F.prg(3, 11, 0x180, (u // per) * n + i)
+            e0 = int.from_bytes(blk[W * (u % per): W * (u % per) + W], "little")
+            assert int(t0[u, i]) == e0
+            assert int(t1[u, i]) == (int(table[(u - a) & 255]) + int(r_out[i]) - e0) & M
+        u = int(xh[i]) & 255
+        assert int(s0[i]) == int(t0[u, i]) and int(s1[i]) == int(t1[u, i])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bw", [32, 64])
 @pytest.mark.parametrize("bcast", [0, 1, 2])
 def test_mul_share(ddg, cuda, bw, bcast):
     L = ddg.lib()
