@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(HERE, "libddg.so")
 
 (GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
  GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT, GATE_RELU_TT, GATE_RELU_ARS_TT,
- GATE_LRS_TT) = range(14)
+ GATE_LRS_TT, GATE_RELU_TTF, GATE_RELU_ARS_TTF) = range(16)
 # comparison backends of the forward's ReLU gates (relu_backend)
 RELU_DCF, RELU_OT, RELU_TT = 0, 1, 2
 

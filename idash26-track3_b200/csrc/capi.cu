@@ -15,7 +15,7 @@ using namespace ddg;
 
 static int check_gate_args(int kind, int bw, int scale)
 {
-    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_LRS_TT, DDG_ERR_ARG, "gate kind %d out of range", kind);
+    DDG_CHECK(kind >= DDG_GATE_RELU && kind <= DDG_GATE_RELU_ARS_TTF, DDG_ERR_ARG, "gate kind %d out of range", kind);
     DDG_CHECK(bw == 32 || bw == 64, DDG_ERR_ARG, "bw must be 32 or 64 (got %d)", bw);
     DDG_CHECK(scale >= 1 && scale < bw - 1, DDG_ERR_ARG, "scale %d out of range for bw %d", scale, bw);
     DDG_CHECK(kind != DDG_GATE_LRS_SPLIT || scale >= 2, DDG_ERR_ARG, "split LRS needs scale >= 2 (got %d)", scale);
@@ -104,7 +104,7 @@ int ddg_gate_round1_arrays(int kind, int bw, int scale)
     if (check_gate_args(kind, bw, scale) != DDG_OK) return 0;
     GateLayout L = gate_layout(kind, bw, scale, 1);
     if (L.ot) return 3;
-    if (L.tt) return kind == GATE_LRS_TT ? 1 : 3;
+    if (L.tt) return kind == GATE_LRS_TT ? 1 : tt_mode_of(kind) == PLAN_TT_FULL ? 2 : 3;
     return (L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0) + (L.lo ? 1 : 0);
 }
 
@@ -144,6 +144,7 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
         const OtPlan &P = gate_digit_plan(L);
         const OtScratch sc = ot_scratch_bytes(L);
         const bool hi = P.nd[0] != 0;
+        const int lo_arr = P.mode == PLAN_TT_FULL ? 1 : hi ? 2 : 0;  // index of the lo-compare array
         uint32_t *tab[2] = {}, *tri[2] = {};
         void *state[2];
         uint32_t *o[2][OT_MAX_LEVELS + 1] = {};
@@ -160,13 +161,13 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
                 const int q = 1 - p;
                 const bool last = l == P.levels + 1;
                 ok(ot_level(L, p, l, key[p], tab[q], o[p][l - 1], o[q][l - 1], state[p], tri[p], last ? nullptr : o[p][l],
-                            last && hi ? b[p] : nullptr, last ? b[p] + (hi ? 2 : 0) * nw : nullptr, st, d_xhat));
+                            last && hi ? b[p] : nullptr, last ? b[p] + lo_arr * nw : nullptr, st, d_xhat));
             }
     }
     void *sh[2] = {d_share0, d_share1};
     const bool has_hi = L.hi || L.ot || (L.tt && kind != GATE_LRS_TT);
     const bool has_lo = L.lo || L.ot || L.tt;
-    const int lo_at = L.tt && kind == GATE_LRS_TT ? 0 : nh;
+    const int lo_at = L.tt && kind == GATE_LRS_TT ? 0 : (L.tt && tt_mode_of(kind) == PLAN_TT_FULL) ? 1 : nh;
     for (int p = 0; p < 2 && err == DDG_OK; p++) {
         const int q = 1 - p;
         ok(gate_round2(L, p, d_xhat, has_hi ? b[p] : nullptr, has_hi ? b[q] : nullptr, has_lo ? b[p] + lo_at * nw : nullptr,

@@ -97,14 +97,19 @@ struct TimedLaunch {
 enum GateKind {
     GATE_RELU = 0, GATE_RELU_ARS = 1, GATE_ARS = 2, GATE_LRS = 3, GATE_RELU_SPLIT = 4, GATE_RELU_ARS_SPLIT = 5,
     GATE_LRS_SPLIT = 6, GATE_RELU_SPLIT3 = 7, GATE_RELU_ARS_SPLIT3 = 8, GATE_RELU_OT = 9, GATE_RELU_ARS_OT = 10,
-    GATE_RELU_TT = 11, GATE_RELU_ARS_TT = 12, GATE_LRS_TT = 13, GATE_KIND_END = 14
+    GATE_RELU_TT = 11, GATE_RELU_ARS_TT = 12, GATE_LRS_TT = 13, GATE_RELU_TTF = 14, GATE_RELU_ARS_TTF = 15,
+    GATE_KIND_END = 16
 };
 constexpr int SPLIT3_MID = 6;
 constexpr int SPLIT3_NMONO = 19;  // dealer-bit monomials of the three-part DReLU bit
 
 inline bool gate_is_split3(int kind) { return kind == GATE_RELU_SPLIT3 || kind == GATE_RELU_ARS_SPLIT3; }
 inline bool gate_is_ot(int kind) { return kind == GATE_RELU_OT || kind == GATE_RELU_ARS_OT; }
-inline bool gate_is_tt(int kind) { return kind == GATE_RELU_TT || kind == GATE_RELU_ARS_TT || kind == GATE_LRS_TT; }
+inline bool gate_is_tt(int kind)
+{
+    return kind == GATE_RELU_TT || kind == GATE_RELU_ARS_TT || kind == GATE_LRS_TT || kind == GATE_RELU_TTF ||
+           kind == GATE_RELU_ARS_TTF;
+}
 // the kind whose dealer words and round 2 a gate uses
 __host__ __device__ inline int gate_word_kind(int kind)
 {
@@ -114,11 +119,18 @@ __host__ __device__ inline int gate_word_kind(int kind)
     case GATE_RELU_ARS_OT:
     case GATE_RELU_ARS_TT: return GATE_RELU_ARS_SPLIT;
     case GATE_LRS_TT: return GATE_LRS;
+    case GATE_RELU_TTF: return GATE_RELU;
+    case GATE_RELU_ARS_TTF: return GATE_RELU_ARS;
     default: return kind;
     }
 }
 // the digit plan of a TT kind
-inline OtPlan tt_plan_of(int kind, int bw, int s) { return digit_plan(bw, s, kind == GATE_LRS_TT ? PLAN_TT_LRS : PLAN_TT_RELU); }
+inline int tt_mode_of(int kind)
+{
+    return kind == GATE_LRS_TT ? PLAN_TT_LRS : (kind == GATE_RELU_TTF || kind == GATE_RELU_ARS_TTF) ? PLAN_TT_FULL
+                                                                                                : PLAN_TT_RELU;
+}
+inline OtPlan tt_plan_of(int kind, int bw, int s) { return digit_plan(bw, s, tt_mode_of(kind)); }
 // the high DCF has an equality output (three round-1 bit arrays, five with a middle DCF)
 inline bool gate_is_split(int kind)
 {

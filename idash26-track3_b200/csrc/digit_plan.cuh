@@ -17,14 +17,17 @@ constexpr int OT_MAX_PAD = 3;          // pad PRF blocks per party and element (
 constexpr int TT_MAX_ROWS = 24;        // truth-table rows (32 bits) per element and party
 
 struct OtComb {
-    uint8_t part, h, l, out;  // part 0 = hi, 1 = lo; node indices within the part
-    uint8_t eq, root;         // computes eq; produces the part's root
+    uint8_t part, h, l, out;  // part 0 = hi, 1 = lo, 2 = the cross combine; node indices within the part
+    uint8_t eq, root;         // computes eq; its output is opened (carries a mask bit)
 };
 
 // plan modes: the OT gates' two parts of radix-16 digits; the truth-table
 // (TT) gates' ReLU comparison (hi digits of 5 bits at bw=32, 4 at bw=64; lo
 // digits of 4) and their truncation carry (one part of two 6-bit digits)
-enum : int { PLAN_OT = 0, PLAN_TT_RELU = 1, PLAN_TT_LRS = 2 };
+// PLAN_TT_FULL: the ReLU digits of PLAN_TT_RELU, whose two part roots feed one
+// more AND (the cross combine) giving the full (n-1)-bit comparison, so that
+// round 2 only needs the full compare bit and the lo compare bit
+enum : int { PLAN_OT = 0, PLAN_TT_RELU = 1, PLAN_TT_LRS = 2, PLAN_TT_FULL = 3 };
 
 struct OtPlan {
     int mode = PLAN_OT;
@@ -68,7 +71,25 @@ struct OtPlan {
     // evaluator scratch per element: digit-share state (2 bits per node) and
     // the triple bits (a, b, b', c1, c1') of every combine, 32-bit words
     __host__ __device__ constexpr int state_bytes() const { return 2 * D <= 32 ? 4 : 8; }
-    __host__ __device__ constexpr int tri_words() const { return (5 * ncomb + 31) / 32; }
+    __host__ __device__ constexpr int tri_words() const { return (5 * ncomb + (mode == PLAN_TT_FULL ? 1 : 0) + 31) / 32; }
+    // state bit positions (lt; eq at +1) of combine q's H and L inputs and of
+    // its output.  The cross combine takes the hi root (H) and the lo root (L)
+    // and overwrites the hi root.
+    __host__ __device__ constexpr int hpos(int q) const
+    {
+        return comb[q].part == 2 ? 2 * base[0] : 2 * base[comb[q].part] + 2 * comb[q].h;
+    }
+    __host__ __device__ constexpr int lpos(int q) const
+    {
+        return comb[q].part == 2 ? 2 * base[1] : 2 * base[comb[q].part] + 2 * comb[q].l;
+    }
+    __host__ __device__ constexpr int opos(int q) const
+    {
+        return comb[q].part == 2 ? 2 * base[0] : 2 * base[comb[q].part] + 2 * comb[q].out;
+    }
+    // PLAN_TT_FULL: the party's share of the lo compare's mask bit sits in its
+    // triple words right after the combines' bits
+    __host__ __device__ constexpr int mu_bit() const { return 5 * ncomb; }
     // AND-tree level (1-based) of combine q
     __host__ __device__ constexpr int level_of(int q) const
     {
@@ -89,7 +110,7 @@ __host__ __device__ constexpr OtPlan digit_plan(int n, int s, int mode)
     P.n = n, P.s = s;
     P.bits[0] = mode == PLAN_TT_LRS ? 0 : n - 1 - s;
     P.bits[1] = s;
-    P.wid[0] = mode == PLAN_TT_RELU && n == 32 ? 5 : OT_W;
+    P.wid[0] = (mode == PLAN_TT_RELU || mode == PLAN_TT_FULL) && n == 32 ? 5 : OT_W;
     P.wid[1] = mode == PLAN_TT_LRS ? 6 : OT_W;
     if ((mode != PLAN_TT_LRS && P.bits[0] < 1) || P.bits[1] < 1) return P;
     P.nd[0] = (P.bits[0] + P.wid[0] - 1) / P.wid[0];
@@ -122,12 +143,21 @@ __host__ __device__ constexpr OtPlan digit_plan(int n, int s, int mode)
                 if (q >= OT_MAX_COMB) return P;
                 OtComb &c = P.comb[q++];
                 c.part = uint8_t(p), c.h = uint8_t(2 * i + 1), c.l = uint8_t(2 * i), c.out = uint8_t(i);
-                c.root = uint8_t(nk == 1);
+                c.root = uint8_t(nk == 1 && mode != PLAN_TT_FULL);
                 c.eq = uint8_t(i > 0 || P.peq[p]);
             }
             if (k[p] & 1) P.pass_from[l][p] = int8_t(k[p] - 1), P.pass_to[l][p] = int8_t(k[p] / 2);
             k[p] = nk;
         }
+        P.lvl_first[l] = q;
+    }
+    if (mode == PLAN_TT_FULL) {
+        // one more level: full compare = hi_lt ^ (hi_eq & lo_lt), opened
+        l++;
+        if (l > OT_MAX_LEVELS || q >= OT_MAX_COMB) return P;
+        OtComb &c = P.comb[q++];
+        c.part = 2, c.h = 0, c.l = 0, c.out = 0, c.eq = 0, c.root = 1;
+        P.pass_from[l][0] = P.pass_from[l][1] = -1, P.pass_to[l][0] = P.pass_to[l][1] = -1;
         P.lvl_first[l] = q;
     }
     P.levels = l, P.ncomb = q;

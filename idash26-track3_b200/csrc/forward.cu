@@ -570,16 +570,17 @@ struct EvalExec : ExecBase<T> {
             po = reinterpret_cast<const uint32_t *>(peer_of(o, 4 * n));
             oo = o;
         }
-        const int nb = Pl.nd[0] ? 3 : 1;  // hi lt, hi eq, lo lt / lo lt only
+        // opened bit arrays: hi lt, hi eq, lo lt (split round 2) / full lt, lo lt / lo lt only
+        const int nb = Pl.mode == PLAN_TT_FULL ? 2 : Pl.nd[0] ? 3 : 1;
         uint32_t *bits = static_cast<uint32_t *>(this->alloc_bytes(4 * nw * nb));
         uint32_t *bl = bits + (nb - 1) * nw;
         if (this->err == DDG_OK)
-            ok(ot_level(L, p, Pl.levels + 1, k, ptab, oo, po, state, tri, nullptr, nb == 3 ? bits : nullptr, bl,
+            ok(ot_level(L, p, Pl.levels + 1, k, ptab, oo, po, state, tri, nullptr, nb > 1 ? bits : nullptr, bl,
                         this->st, x.v));
         const uint32_t *peer = reinterpret_cast<const uint32_t *>(peer_of(bits, 4 * nw * nb));
         T *sh = alloc(n);
         if (this->err == DDG_OK)
-            ok(gate_round2(L, p, x.v, nb == 3 ? bits : nullptr, nb == 3 ? peer : nullptr, bl,
+            ok(gate_round2(L, p, x.v, nb > 1 ? bits : nullptr, nb > 1 ? peer : nullptr, bl,
                            peer ? peer + (nb - 1) * nw : nullptr, k, sh, this->st));
         Tn<T> t;
         t.n = n;
@@ -664,8 +665,8 @@ static void affinity_graph(E &x)
     const int B = x.B;
     const int be = g_relu_backend.load();
     const bool three = relu_parts(x.bw) == 3, ot = be == DDG_RELU_OT, tt = be == DDG_RELU_TT;
-    const int RELU = tt ? GATE_RELU_TT : ot ? GATE_RELU_OT : three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
-    const int RELU_ARS = tt ? GATE_RELU_ARS_TT : ot ? GATE_RELU_ARS_OT : three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
+    const int RELU = tt ? GATE_RELU_TTF : ot ? GATE_RELU_OT : three ? GATE_RELU_SPLIT3 : GATE_RELU_SPLIT;
+    const int RELU_ARS = tt ? GATE_RELU_ARS_TTF : ot ? GATE_RELU_ARS_OT : three ? GATE_RELU_ARS_SPLIT3 : GATE_RELU_ARS_SPLIT;
     const int LRS = tt ? GATE_LRS_TT : GATE_LRS_SPLIT;
     const uint64_t nX = uint64_t(B) * NMAX * FEAT, nA = uint64_t(B) * NMAX * NMAX, nM = uint64_t(B) * NMAX * POOL;
     // leaves: x, mask, raw adjacency and its masked degree, the public protein

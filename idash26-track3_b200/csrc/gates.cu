@@ -122,9 +122,7 @@ __global__ void __launch_bounds__(E::THREADS, E::CTAS) gate_keygen_kernel(const 
                 }
             }
             if (L.tt) {
-                const uint32_t rc = (bits ^ (bits >> 1)) & 1u, rl = ((bits >> 2) ^ (bits >> 3)) & 1u,
-                               re = ((bits >> 4) ^ (bits >> 5)) & 1u;
-                tt_keygen_elem(A, a.ot, a.dk.rk, a.op, e, N, uint64_t(r), rc, re, rl,
+                tt_keygen_elem(A, a.ot, a.dk.rk, a.op, e, N, uint64_t(r), bits,
                                reinterpret_cast<uint32_t *>(a.k0 + L.tt_tables),
                                reinterpret_cast<uint32_t *>(a.k1 + L.tt_tables),
                                reinterpret_cast<uint32_t *>(a.k0 + L.tt_tri),

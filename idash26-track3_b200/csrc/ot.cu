@@ -223,14 +223,14 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             if (q >= P.ncomb) break;
             if (P.level_of(q) != l - 1) continue;
             const OtComb &C = P.comb[q];
-            const int j = q - qa, tb = 5 * q, base = 2 * P.base[C.part];
+            const int j = q - qa, tb = 5 * q;
             const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
             const uint32_t ta = tri_bit(tw, tb), tb1 = tri_bit(tw, tb + 1), tb2 = tri_bit(tw, tb + 2);
             const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tri_bit(tw, tb + 3);
             const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tri_bit(tw, tb + 4);
-            const uint32_t lt = st_bit(st, base + 2 * C.h) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
+            const uint32_t lt = st_bit(st, P.hpos(q)) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
             const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
-            const int o = base + 2 * C.out;
+            const int o = P.opos(q);
             st = (st & ~(ST(3) << o)) | (ST(lt) << o) | (ST(eq) << (o + 1));
         }
 #pragma unroll
@@ -252,9 +252,8 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             if (q >= P.ncomb) break;
             if (P.level_of(q) != l) continue;
             const OtComb &C = P.comb[q];
-            const int j = q - qa, tb = 5 * q, base = 2 * P.base[C.part];
-            const uint32_t eH = st_bit(st, base + 2 * C.h + 1), lL = st_bit(st, base + 2 * C.l),
-                           eL = st_bit(st, base + 2 * C.l + 1);
+            const int j = q - qa, tb = 5 * q;
+            const uint32_t eH = st_bit(st, P.hpos(q) + 1), lL = st_bit(st, P.lpos(q)), eL = st_bit(st, P.lpos(q) + 1);
             w |= ((eH ^ tri_bit(tw, tb)) << (3 * j)) | ((lL ^ tri_bit(tw, tb + 1)) << (3 * j + 1));
             if (C.eq) w |= (eL ^ tri_bit(tw, tb + 2)) << (3 * j + 2);
         }
@@ -263,6 +262,7 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
     } else {
         if (P.nd[0]) hl = st_bit(st, 0), he = st_bit(st, 1);
         ll = st_bit(st, 2 * P.base[1]);
+        if (P.mode == PLAN_TT_FULL) ll ^= tri_bit(tw, P.mu_bit());  // the lo compare's mask share
     }
 }
 
@@ -337,8 +337,7 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         static_for<qa, qb>([&](auto qi) {
             constexpr OtPlan P = digit_plan(NB, SB, MODE);
             constexpr int q = decltype(qi)::value;
-            constexpr int j = q - qa, tb = 5 * q, base = 2 * P.base[P.comb[q].part];
-            constexpr int h = base + 2 * (2 * P.comb[q].out + 1), o = base + 2 * P.comb[q].out;
+            constexpr int j = q - qa, tb = 5 * q, h = P.hpos(q), o = P.opos(q);
             constexpr bool ceq = P.comb[q].eq != 0;
             const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
             const uint32_t ta = tbit(tb), tb1 = tbit(tb + 1), tb2 = tbit(tb + 2);
@@ -365,8 +364,7 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         static_for<qa, qb>([&](auto qi) {
             constexpr OtPlan P = digit_plan(NB, SB, MODE);
             constexpr int q = decltype(qi)::value;
-            constexpr int j = q - qa, tb = 5 * q, base = 2 * P.base[P.comb[q].part];
-            constexpr int hb = base + 2 * (2 * P.comb[q].out + 1), lb = base + 2 * (2 * P.comb[q].out);
+            constexpr int j = q - qa, tb = 5 * q, hb = P.hpos(q), lb = P.lpos(q);
             const uint32_t eH = (st >> (hb + 1)) & 1u, lL = (st >> lb) & 1u, eL = (st >> (lb + 1)) & 1u;
             w |= ((eH ^ tbit(tb)) << (3 * j)) | ((lL ^ tbit(tb + 1)) << (3 * j + 1));
             if constexpr (P.comb[q].eq != 0) w |= (eL ^ tbit(tb + 2)) << (3 * j + 2);
@@ -376,6 +374,7 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
     } else {
         if constexpr (P.nd[0] != 0) hl = st & 1u, he = (st >> 1) & 1u;
         ll = (st >> (2 * P.base[1])) & 1u;
+        if constexpr (MODE == PLAN_TT_FULL) ll ^= tbit(P.mu_bit());  // the lo compare's mask share
     }
 }
 
@@ -404,7 +403,10 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
                            wl = __ballot_sync(0xFFFFFFFFu, ll);
             if ((threadIdx.x & 31) == 0) {
                 const uint64_t wi = e >> 5;
-                if (a.bits_hi) a.bits_hi[wi] = wh, a.bits_hi[a.nw + wi] = we;
+                if (a.bits_hi) {
+                    a.bits_hi[wi] = wh;
+                    if (a.P.mode != PLAN_TT_FULL) a.bits_hi[a.nw + wi] = we;
+                }
                 a.bits_lo[wi] = wl;
             }
         }
@@ -487,17 +489,15 @@ static void level_dispatch(const GateLayout &L, const OtLevelArgs &a, int grid, 
 
 const OtPlan &gate_digit_plan(const GateLayout &L)
 {
-    static OtPlan tt[3][2][64];
+    static OtPlan tt[4][2][64];
     static std::once_flag once;
     std::call_once(once, [] {
-        for (int b = 0; b < 2; b++)
-            for (int sc = 1; sc < 64; sc++) {
-                tt[1][b][sc] = digit_plan(b ? 64 : 32, sc, PLAN_TT_RELU);
-                tt[2][b][sc] = digit_plan(b ? 64 : 32, sc, PLAN_TT_LRS);
-            }
+        for (int m = PLAN_TT_RELU; m <= PLAN_TT_FULL; m++)
+            for (int b = 0; b < 2; b++)
+                for (int sc = 1; sc < 64; sc++) tt[m][b][sc] = digit_plan(b ? 64 : 32, sc, m);
     });
     if (L.ot) return ot_plan_cached(L.bw, L.s);
-    return tt[L.kind == GATE_LRS_TT ? 2 : 1][L.bw == 64 ? 1 : 0][L.s > 0 && L.s < 64 ? L.s : 0];
+    return tt[tt_mode_of(L.kind)][L.bw == 64 ? 1 : 0][L.s > 0 && L.s < 64 ? L.s : 0];
 }
 
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
@@ -528,6 +528,8 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     TimedLaunch tl;
     DDG_TRY(tl.begin(st));
     if (L.ot) party == 0 ? level_dispatch<PLAN_OT, 0>(L, a, grid, st) : level_dispatch<PLAN_OT, 1>(L, a, grid, st);
+    else if (P.mode == PLAN_TT_FULL)
+        party == 0 ? level_dispatch<PLAN_TT_FULL, 0>(L, a, grid, st) : level_dispatch<PLAN_TT_FULL, 1>(L, a, grid, st);
     else if (L.kind == GATE_LRS_TT)
         party == 0 ? level_dispatch<PLAN_TT_LRS, 0>(L, a, grid, st) : level_dispatch<PLAN_TT_LRS, 1>(L, a, grid, st);
     else party == 0 ? level_dispatch<PLAN_TT_RELU, 0>(L, a, grid, st) : level_dispatch<PLAN_TT_RELU, 1>(L, a, grid, st);
@@ -544,7 +546,8 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     else bytes += n * P.state_bytes();
     if (level > 1) bytes += n * (8.0 + (L.ot && party == 0 ? 4.0 : 0.0));
     else if (L.ot) bytes += n * 5.0 * Gq;
-    bytes += level <= P.levels ? n * (4.0 + P.state_bytes()) : n * (P.nd[0] ? 3.0 : 1.0) / 8.0;
+    const double arrays = P.mode == PLAN_TT_FULL ? 2.0 : P.nd[0] ? 3.0 : 1.0;
+    bytes += level <= P.levels ? n * (4.0 + P.state_bytes()) : n * arrays / 8.0;
     DDG_TRY(tl.end(st, bytes, 0.0, n));
     return DDG_OK;
 }

@@ -142,12 +142,18 @@ __device__ __forceinline__ void ot_keygen_elem(const E &A, const OtPlan &P, cons
 // at a part's root), c' likewise.  Both parties' triple bits: 5 per combine.
 enum : uint32_t { P_TT_RAND = 0x140 };
 
+// pb: the element's mask-bit word (P_BITS); rho_c = bit 0 ^ bit 1, rho_L = bit
+// 2 ^ bit 3, rho_e = bit 4 ^ bit 5.  PLAN_TT_FULL opens the full compare
+// (cross combine, rho_c) and the lo root with the parties' own shares of
+// rho_L (bits 2 and 3) added at the last level.
 template <class E>
 __device__ __forceinline__ void tt_keygen_elem(const E &A, const OtPlan &P, const uint32_t *dk, uint32_t op,
-                                               uint64_t e, uint64_t N, uint64_t r, uint32_t rho_c, uint32_t rho_e,
-                                               uint32_t rho_L, uint32_t *tab0, uint32_t *tab1, uint32_t *tri0,
-                                               uint32_t *tri1)
+                                               uint64_t e, uint64_t N, uint64_t r, uint32_t pb, uint32_t *tab0,
+                                               uint32_t *tab1, uint32_t *tri0, uint32_t *tri1)
 {
+    const uint32_t rho_c = (pb ^ (pb >> 1)) & 1u, rho_L = ((pb >> 2) ^ (pb >> 3)) & 1u,
+                   rho_e = ((pb >> 4) ^ (pb >> 5)) & 1u;
+    const bool full = P.mode == PLAN_TT_FULL;
     Blk blk{{0u, 0u, 0u, 0u}};
     int held = -1;
     // 32-bit word w of the dealer's random stream for this element
@@ -166,7 +172,7 @@ __device__ __forceinline__ void tt_keygen_elem(const E &A, const OtPlan &P, cons
         const uint32_t alpha =
             uint32_t(p == 0 ? rhi >> (P.wid[0] * g) : rlo >> (P.wid[1] * (g - P.nd[0]))) & uint32_t(W - 1);
         uint64_t lt = alpha ? (uint64_t(1) << alpha) - 1 : 0, eq = uint64_t(1) << alpha;
-        if (P.nd[p] == 1) {
+        if (P.nd[p] == 1 && !full) {
             if (p == 0 ? rho_c : rho_L) lt ^= wm;
             if (p == 0 && rho_e) eq ^= wm;
         }
@@ -196,13 +202,18 @@ __device__ __forceinline__ void tt_keygen_elem(const E &A, const OtPlan &P, cons
         const uint32_t a = v0[0] ^ v1[0], b = v0[1] ^ v1[1], b2 = v0[2] ^ v1[2];
         v1[3] = (a & b) ^ v0[3];
         v1[4] = (a & b2) ^ v0[4];
-        if (C.root) v1[3] ^= C.part == 0 ? rho_c : rho_L, v1[4] ^= C.part == 0 ? rho_e : 0u;
+        if (C.root) v1[3] ^= C.part != 1 ? rho_c : rho_L, v1[4] ^= C.part == 0 ? rho_e : 0u;
         if (!C.eq) v0[4] = 0, v1[4] = 0;
         for (int k = 0; k < 5; k++) {
             const int i = 5 * q + k;
             t0[i >> 5] |= v0[k] << (i & 31);
             t1[i >> 5] |= v1[k] << (i & 31);
         }
+    }
+    if (full) {
+        const int i = P.mu_bit();
+        t0[i >> 5] |= ((pb >> 2) & 1u) << (i & 31);
+        t1[i >> 5] |= ((pb >> 3) & 1u) << (i & 31);
     }
     for (int k = 0; k < P.tri_words(); k++) tri0[uint64_t(k) * N + e] = t0[k], tri1[uint64_t(k) * N + e] = t1[k];
 }

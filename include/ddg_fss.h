@@ -84,6 +84,14 @@ extern "C" {
 #define DDG_GATE_RELU_TT 11
 #define DDG_GATE_RELU_ARS_TT 12
 #define DDG_GATE_LRS_TT 13
+/* RELU_TT / RELU_ARS_TT with one more AND combining the two part roots into
+ * the full (bw-1)-bit comparison: only the full compare bit and the lo
+ * compare bit are opened, and round 2 is that of RELU / RELU_ARS (4 / 8
+ * words instead of 16 / 32).  One more opening per gate, a quarter of the
+ * dealer words; the forward's default ReLU kinds.  Round 2 reads two bit
+ * arrays: [full compare | lo compare]. */
+#define DDG_GATE_RELU_TTF 14
+#define DDG_GATE_RELU_ARS_TTF 15
 
 /* ReLU comparison backends of the forward (ddg_relu_backend) */
 #define DDG_RELU_DCF 0
@@ -393,7 +401,7 @@ int ddg_aes_tables(int tables);
  * with the same setting. */
 int ddg_relu_split(int parts);
 /* Comparison backend of the forward's ReLU gates, process-wide:
- * DDG_RELU_TT (default; DDG_GATE_RELU*_TT, and DDG_GATE_LRS_TT at the
+ * DDG_RELU_TT (default; DDG_GATE_RELU*_TTF, and DDG_GATE_LRS_TT at the
  * truncation sites), DDG_RELU_OT (DDG_GATE_RELU*_OT) or DDG_RELU_DCF (the
  * split chosen by ddg_relu_split).  It changes the key layout like
  * ddg_relu_split. */

@@ -771,7 +771,7 @@ enum { OT_P_PARTY = 0x100, OT_P_AUX = 0x110, OT_P_PAD = 0x120 };
 #define OT_MAXC 16
 
 typedef struct {
-    int mode; /* 0 = OT, 1 = truth-table ReLU, 2 = truth-table carry */
+    int mode; /* 0 = OT, 1 = truth-table ReLU, 2 = truth-table carry, 3 = truth-table full compare */
     int wid[2], bits[2];
     int deq[OT_MAXD], drows[OT_MAXD], drow0[OT_MAXD], rows;
     int n, s, D, G0, nd[2], levels, ncomb, tri0, naux;
@@ -797,7 +797,7 @@ static int digit_plan_build(int n, int s, int mode, ot_plan_t *P)
     P->mode = mode, P->n = n, P->s = s;
     P->bits[0] = mode == 2 ? 0 : n - 1 - s;
     P->bits[1] = s;
-    P->wid[0] = mode == 1 && n == 32 ? 5 : 4;
+    P->wid[0] = (mode == 1 || mode == 3) && n == 32 ? 5 : 4;
     P->wid[1] = mode == 2 ? 6 : 4;
     if ((mode != 2 && P->bits[0] < 1) || P->bits[1] < 1) return 0;
     P->nd[0] = (P->bits[0] + P->wid[0] - 1) / P->wid[0];
@@ -824,16 +824,25 @@ static int digit_plan_build(int n, int s, int mode, ot_plan_t *P)
             for (int i = 0; i < k[p] / 2; i++) {
                 if (q >= OT_MAXC) return 0;
                 P->cpart[q] = p, P->ch[q] = 2 * i + 1, P->cl[q] = 2 * i, P->cout[q] = i;
-                P->ceq[q] = (i > 0 || p == 0), P->croot[q] = (nk == 1), P->clevel[q] = l;
+                P->ceq[q] = (i > 0 || p == 0), P->croot[q] = (nk == 1 && mode != 3), P->clevel[q] = l;
                 q++;
             }
             if (k[p] & 1) P->pfrom[l][p] = k[p] - 1, P->pto[l][p] = k[p] / 2;
             k[p] = nk;
         }
     }
+    if (mode == 3) {
+        /* the cross combine: full compare = hi_lt ^ (hi_eq & lo_lt), written over the hi root */
+        l++;
+        if (l > 7 || q >= OT_MAXC) return 0;
+        P->pfrom[l][0] = P->pfrom[l][1] = P->pto[l][0] = P->pto[l][1] = -1;
+        P->cpart[q] = 2, P->ch[q] = 0, P->cl[q] = 0, P->cout[q] = 0, P->ceq[q] = 0, P->croot[q] = 1;
+        P->clevel[q] = l;
+        q++;
+    }
     P->levels = l, P->ncomb = q, P->tri0 = 6 * P->G0;
     P->naux = (P->tri0 + 5 * q + 127) / 128;
-    return P->naux <= 2 && 5 * q <= 96 && P->rows <= 24;
+    return P->naux <= 2 && 5 * q + 1 <= 96 && P->rows <= 24;
 }
 
 static int ot_plan_build(int n, int s, ot_plan_t *P) { return digit_plan_build(n, s, 0, P); }
@@ -1057,7 +1066,22 @@ void ref_ot_eval_pair(int kind, int n, int s, uint64_t xhat, uint64_t i, const r
  * Dealer stream: 32-bit word w = word w mod 4 of AES_dealer(i || op ||
  * 0x140 + w / 4); party 0's table rows, then its 5 triple bits per combine,
  * then party 1's 3.  Written independently of the CUDA code. */
-enum { GATE_RELU_TT = 11, GATE_RELU_ARS_TT = 12, GATE_LRS_TT = 13 };
+enum { GATE_RELU_TT = 11, GATE_RELU_ARS_TT = 12, GATE_LRS_TT = 13, GATE_RELU_TTF = 14, GATE_RELU_ARS_TTF = 15 };
+
+/* state positions of a combine's H and L inputs and of its output (the cross
+ * combine, part 2, reads the hi root and the lo root and overwrites the hi root) */
+static int comb_hpos(const ot_plan_t *P, int q)
+{
+    return P->cpart[q] == 2 ? 0 : 2 * (P->cpart[q] == 0 ? 0 : P->nd[0]) + 2 * P->ch[q];
+}
+static int comb_lpos(const ot_plan_t *P, int q)
+{
+    return P->cpart[q] == 2 ? 2 * P->nd[0] : 2 * (P->cpart[q] == 0 ? 0 : P->nd[0]) + 2 * P->cl[q];
+}
+static int comb_opos(const ot_plan_t *P, int q)
+{
+    return P->cpart[q] == 2 ? 0 : 2 * (P->cpart[q] == 0 ? 0 : P->nd[0]) + 2 * P->cout[q];
+}
 #define TT_P_RAND 0x140
 
 typedef struct {
@@ -1066,10 +1090,19 @@ typedef struct {
     uint64_t w[32];   /* dealer words of the word kind */
 } ref_tt_key;
 
-static int tt_mode(int kind) { return kind == GATE_LRS_TT ? 2 : 1; }
+static int tt_mode(int kind)
+{
+    return kind == GATE_LRS_TT ? 2 : (kind == GATE_RELU_TTF || kind == GATE_RELU_ARS_TTF) ? 3 : 1;
+}
 static int tt_word_kind(int kind)
 {
-    return kind == GATE_RELU_TT ? GATE_RELU_SPLIT : kind == GATE_RELU_ARS_TT ? GATE_RELU_ARS_SPLIT : GATE_LRS;
+    switch (kind) {
+    case GATE_RELU_TT: return GATE_RELU_SPLIT;
+    case GATE_RELU_ARS_TT: return GATE_RELU_ARS_SPLIT;
+    case GATE_RELU_TTF: return GATE_RELU;
+    case GATE_RELU_ARS_TTF: return GATE_RELU_ARS;
+    default: return GATE_LRS;
+    }
 }
 
 int ref_tt_plan_info(int kind, int n, int s, int *out4)
@@ -1118,7 +1151,7 @@ uint64_t ref_tt_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint6
         uint32_t truth[4] = {0, 0, 0, 0};
         for (int x = 0; x < W; x++) {
             int lt = x < (int)alpha, eq = x == (int)alpha;
-            if (P.nd[part] == 1) {
+            if (P.nd[part] == 1 && P.mode != 3) {
                 lt ^= part == 0 ? rho_c : rho_L;
                 eq ^= part == 0 ? rho_e : 0;
             }
@@ -1141,7 +1174,7 @@ uint64_t ref_tt_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint6
         v1[3] = (a & b) ^ v0[3];
         v1[4] = (a & b2) ^ v0[4];
         if (P.croot[q]) {
-            v1[3] ^= P.cpart[q] == 0 ? rho_c : rho_L;
+            v1[3] ^= P.cpart[q] != 1 ? rho_c : rho_L;
             v1[4] ^= P.cpart[q] == 0 ? rho_e : 0;
         }
         if (!P.ceq[q]) v0[4] = v1[4] = 0;
@@ -1151,6 +1184,11 @@ uint64_t ref_tt_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint6
             k1->tri[bit / 32] |= (uint32_t)v1[k] << (bit % 32);
         }
     }
+    if (P.mode == 3) { /* each party's share of the lo compare's mask bit (P_BITS bits 2 and 3) */
+        int b = 5 * P.ncomb;
+        k0->tri[b / 32] |= (uint32_t)((blk[0] >> 2) & 1) << (b % 32);
+        k1->tri[b / 32] |= (uint32_t)((blk[0] >> 3) & 1) << (b % 32);
+    }
     return r_out;
 }
 
@@ -1159,6 +1197,7 @@ uint64_t ref_tt_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint6
  * party's masked comparison-bit shares in the round-1 encoding (bit0 hi lt,
  * bit1 lo lt, bit2 hi eq; the carry kind only bit1).
  */
+#define TRI_BIT(k, b) ((int)(((k)->tri[(b) / 32] >> ((b) % 32)) & 1))
 void ref_tt_eval_pair(int kind, int n, int s, uint64_t xhat, const ref_tt_key *k0, const ref_tt_key *k1, int *bits0,
                       int *bits1)
 {
@@ -1182,23 +1221,23 @@ void ref_tt_eval_pair(int kind, int n, int s, uint64_t xhat, const ref_tt_key *k
         int e_[OT_MAXC], f_[OT_MAXC], f2_[OT_MAXC];
         for (int q = 0; q < P.ncomb; q++) {
             if (P.clevel[q] != l) continue;
-            int base = 2 * (P.cpart[q] == 0 ? 0 : P.nd[0]);
+            int hp = comb_hpos(&P, q), lp = comb_lpos(&P, q);
             e_[q] = f_[q] = f2_[q] = 0;
             for (int p = 0; p < 2; p++) {
-                e_[q] ^= (int)((st[p] >> (base + 2 * P.ch[q] + 1)) & 1) ^ TRI(p, 5 * q);
-                f_[q] ^= (int)((st[p] >> (base + 2 * P.cl[q])) & 1) ^ TRI(p, 5 * q + 1);
-                if (P.ceq[q]) f2_[q] ^= (int)((st[p] >> (base + 2 * P.cl[q] + 1)) & 1) ^ TRI(p, 5 * q + 2);
+                e_[q] ^= (int)((st[p] >> (hp + 1)) & 1) ^ TRI(p, 5 * q);
+                f_[q] ^= (int)((st[p] >> lp) & 1) ^ TRI(p, 5 * q + 1);
+                if (P.ceq[q]) f2_[q] ^= (int)((st[p] >> (lp + 1)) & 1) ^ TRI(p, 5 * q + 2);
             }
         }
         for (int p = 0; p < 2; p++) {
             for (int q = 0; q < P.ncomb; q++) {
                 if (P.clevel[q] != l) continue;
-                int base = 2 * (P.cpart[q] == 0 ? 0 : P.nd[0]), p0 = p == 0;
+                int p0 = p == 0;
                 int a = TRI(p, 5 * q), b = TRI(p, 5 * q + 1), b2 = TRI(p, 5 * q + 2), c = TRI(p, 5 * q + 3),
                     c2 = TRI(p, 5 * q + 4);
-                int lt = (int)((st[p] >> (base + 2 * P.ch[q])) & 1) ^ c ^ (f_[q] & a) ^ (e_[q] & b) ^ (p0 & e_[q] & f_[q]);
+                int lt = (int)((st[p] >> comb_hpos(&P, q)) & 1) ^ c ^ (f_[q] & a) ^ (e_[q] & b) ^ (p0 & e_[q] & f_[q]);
                 int eq = P.ceq[q] ? (c2 ^ (f2_[q] & a) ^ (e_[q] & b2) ^ (p0 & e_[q] & f2_[q])) : 0;
-                int o = base + 2 * P.cout[q];
+                int o = comb_opos(&P, q);
                 st[p] = (st[p] & ~(3ULL << o)) | ((uint64_t)lt << o) | ((uint64_t)eq << (o + 1));
             }
             for (int pt = 0; pt < 2; pt++) {
@@ -1213,7 +1252,12 @@ void ref_tt_eval_pair(int kind, int n, int s, uint64_t xhat, const ref_tt_key *k
     int *out[2] = {bits0, bits1};
     for (int p = 0; p < 2; p++) {
         int hi = P.nd[0] ? (int)(st[p] & 1) | ((int)((st[p] >> 1) & 1) << 2) : 0;
-        *out[p] = hi | ((int)((st[p] >> (2 * P.nd[0])) & 1) << 1);
+        int lo = (int)((st[p] >> (2 * P.nd[0])) & 1);
+        if (P.mode == 3) { /* full compare and the lo compare with the party's mask share; no equality */
+            hi = (int)(st[p] & 1);
+            lo ^= TRI_BIT(kk[p], 5 * P.ncomb);
+        }
+        *out[p] = hi | (lo << 1);
     }
 }
 

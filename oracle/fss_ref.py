@@ -23,16 +23,18 @@ _SO = os.path.join(_HERE, "libfss_ref.so")
 
 (GATE_RELU, GATE_RELU_ARS, GATE_ARS, GATE_LRS, GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT,
  GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3, GATE_RELU_OT, GATE_RELU_ARS_OT, GATE_RELU_TT, GATE_RELU_ARS_TT,
- GATE_LRS_TT) = range(14)
+ GATE_LRS_TT, GATE_RELU_TTF, GATE_RELU_ARS_TTF) = range(16)
 GATE_NWORDS = {GATE_RELU: 4, GATE_RELU_ARS: 8, GATE_ARS: 6, GATE_LRS: 4, GATE_RELU_SPLIT: 16,
                GATE_RELU_ARS_SPLIT: 32, GATE_LRS_SPLIT: 7, GATE_RELU_SPLIT3: 40, GATE_RELU_ARS_SPLIT3: 80,
-               GATE_RELU_OT: 16, GATE_RELU_ARS_OT: 32, GATE_RELU_TT: 16, GATE_RELU_ARS_TT: 32, GATE_LRS_TT: 4}
+               GATE_RELU_OT: 16, GATE_RELU_ARS_OT: 32, GATE_RELU_TT: 16, GATE_RELU_ARS_TT: 32, GATE_LRS_TT: 4,
+               GATE_RELU_TTF: 4, GATE_RELU_ARS_TTF: 8}
 # OT-leaf kinds and the SPLIT kind whose words and round 2 they use
 OT_KINDS = (GATE_RELU_OT, GATE_RELU_ARS_OT)
 OT_WORD_KIND = {GATE_RELU_OT: GATE_RELU_SPLIT, GATE_RELU_ARS_OT: GATE_RELU_ARS_SPLIT}
 # truth-table kinds and the kind whose words and round 2 they use
-TT_KINDS = (GATE_RELU_TT, GATE_RELU_ARS_TT, GATE_LRS_TT)
-TT_WORD_KIND = {GATE_RELU_TT: GATE_RELU_SPLIT, GATE_RELU_ARS_TT: GATE_RELU_ARS_SPLIT, GATE_LRS_TT: GATE_LRS}
+TT_KINDS = (GATE_RELU_TT, GATE_RELU_ARS_TT, GATE_LRS_TT, GATE_RELU_TTF, GATE_RELU_ARS_TTF)
+TT_WORD_KIND = {GATE_RELU_TT: GATE_RELU_SPLIT, GATE_RELU_ARS_TT: GATE_RELU_ARS_SPLIT, GATE_LRS_TT: GATE_LRS,
+                GATE_RELU_TTF: GATE_RELU, GATE_RELU_ARS_TTF: GATE_RELU_ARS}
 # kinds whose high DCF also outputs equality (three round-1 bit arrays or more)
 SPLIT_KINDS = (GATE_RELU_SPLIT, GATE_RELU_ARS_SPLIT, GATE_LRS_SPLIT, GATE_RELU_SPLIT3, GATE_RELU_ARS_SPLIT3)
 # kinds with a middle DCF with equality output (five round-1 bit arrays)

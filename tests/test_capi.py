@@ -44,7 +44,7 @@ def test_split_lrs_layout(ddg):
     with pytest.raises(ddg.DdgError):
         ddg.gate_key_layout(ddg.GATE_LRS_SPLIT, 32, 1, 10)
     with pytest.raises(ddg.DdgError):
-        ddg.gate_key_layout(ddg.GATE_LRS_TT + 1, 32, 12, 10)
+        ddg.gate_key_layout(ddg.GATE_RELU_ARS_TTF + 1, 32, 12, 10)
 
 
 def test_ot_gate_layout(ddg):
@@ -97,6 +97,14 @@ def test_tt_gate_layout(ddg):
                                                                                         12, 1000) / 3
     assert ddg.gate_key_bytes(ddg.GATE_LRS_TT, 32, 12, 1000) < ddg.gate_key_bytes(ddg.GATE_LRS_SPLIT, 32, 12, 1000)
     assert ddg.gate_round1_arrays(ddg.GATE_LRS_TT, 32, 12) == 1 and ddg.gate_round1_arrays(ddg.GATE_RELU_TT, 32, 12) == 3
+    # the full-compare kinds: one more AND level, two opened arrays, the words of RELU / RELU_ARS
+    for kind, words in ((ddg.GATE_RELU_TTF, 4), (ddg.GATE_RELU_ARS_TTF, 8)):
+        lay = ddg.tt_key_layout(kind, 32, 12, 1000)
+        assert (lay["rows"], lay["digits"], lay["levels"]) == (10, 7, 3)
+        assert lay["bytes"] >= lay["words"] + words * 4 * 1000 and ddg.gate_round1_arrays(kind, 32, 12) == 2
+        assert F.tt_plan_info(kind, 32, 12)["levels"] == 3
+    assert ddg.gate_key_bytes(ddg.GATE_RELU_ARS_TTF, 32, 12, 1000) < ddg.gate_key_bytes(ddg.GATE_RELU_ARS_TT, 32, 12,
+                                                                                         1000) / 2
     with pytest.raises(ddg.DdgError) as e:
         ddg.gate_round1(ddg.GATE_RELU_TT, 32, 12, 10, 1, 1, 1, 1)
     assert e.value.code == 1

@@ -170,9 +170,12 @@ def test_tt_and_ot_gates_match_plaintext_and_dcf_bits(bw):
                 k0, k1, ro = F.ot_keygen(kind, bw, 12, 9, 4, i, r)
                 y = F.ot_gate_pair(kind, bw, 12, xh, i, k0, k1)
                 b0, b1, _, _ = F.ot_eval_pair(kind, bw, 12, xh, i, k0, k1)
-            want = {F.GATE_RELU_SPLIT: R.relu(x), F.GATE_RELU_ARS_SPLIT: R.relu_ars(x, 12),
-                    F.GATE_LRS: R.red(R.signed(x) >> 12)}[wk]
+            want = {F.GATE_RELU_SPLIT: R.relu(x), F.GATE_RELU_ARS_SPLIT: R.relu_ars(x, 12), F.GATE_RELU: R.relu(x),
+                    F.GATE_RELU_ARS: R.relu_ars(x, 12), F.GATE_LRS: R.red(R.signed(x) >> 12)}[wk]
             assert (y - ro) & M == int(want)
             g0, g1, _ = F.gate_keygen(wk, bw, 12, 9, 4, i, r)
             d = F.gate_round1(wk, bw, 12, xh, g0) ^ F.gate_round1(wk, bw, 12, xh, g1)
-            assert b0 ^ b1 == d & (2 if wk == F.GATE_LRS else 7)
+            # the bits each word kind's round 2 reads: LRS the carry, RELU the full compare,
+            # RELU_ARS full compare and carry, the SPLIT kinds hi compare, carry and hi equality
+            m = {F.GATE_LRS: 2, F.GATE_RELU: 1, F.GATE_RELU_ARS: 3}.get(wk, 7)
+            assert (b0 ^ b1) & m == d & m

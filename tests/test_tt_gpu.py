@@ -16,7 +16,8 @@ from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 from tests.test_gates_gpu import make_inputs, plain
 
 S = 12
-TT_KINDS = [F.GATE_RELU_TT, F.GATE_RELU_ARS_TT, F.GATE_LRS_TT]
+TT_KINDS = [F.GATE_RELU_TT, F.GATE_RELU_ARS_TT, F.GATE_LRS_TT, F.GATE_RELU_TTF, F.GATE_RELU_ARS_TTF]
+FULL_KINDS = (F.GATE_RELU_TTF, F.GATE_RELU_ARS_TTF)
 
 
 def run_tt(ddg, kind, bw, n, x, r, seed=5, op=3):
@@ -62,6 +63,7 @@ def test_tt_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
            out["k1"][lay["tri"]:lay["tri"] + 4 * lay["tri_words"] * n].view(np.uint32)]
     w = [out["k0"][lay["words"]:].view(dt), out["k1"][lay["words"]:].view(dt)]
     carry = kind == F.GATE_LRS_TT
+    full = kind in FULL_KINDS
     for e in range(n):
         k0, k1, ry = F.tt_keygen(kind, bw, S, 5, 3, e, int(r[e]))
         assert int(out["rout"][e]) == ry
@@ -76,6 +78,9 @@ def test_tt_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
         for p, bb in ((0, b0), (1, b1)):
             if carry:
                 assert bit(out["bits"][p], 0, e) == (bb >> 1) & 1
+            elif full:  # [full compare | lo compare]
+                assert bit(out["bits"][p], 0, e) == bb & 1
+                assert bit(out["bits"][p], words, e) == (bb >> 1) & 1
             else:
                 assert bit(out["bits"][p], 0, e) == bb & 1
                 assert bit(out["bits"][p], words, e) == (bb >> 2) & 1
@@ -85,7 +90,8 @@ def test_tt_keys_bits_shares_match_oracle(ddg, cuda, bw, kind):
         assert int(out["y1"][e]) == F.tt_round2(kind, bw, S, 1, int(out["xh"][e]), o, k1)
         g0, g1, _ = F.gate_keygen(wk, bw, S, 5, 3, e, int(r[e]))
         d = F.gate_round1(wk, bw, S, int(out["xh"][e]), g0) ^ F.gate_round1(wk, bw, S, int(out["xh"][e]), g1)
-        assert o == (d & (2 if carry else 7))
+        m = {F.GATE_LRS: 2, F.GATE_RELU: 1, F.GATE_RELU_ARS: 3}.get(wk, 7)
+        assert o & m == d & m
     y = (out["y0"] + out["y1"] - out["rout"]).astype(dt)
     assert np.array_equal(y, plain(wk, x, bw))
 
