@@ -149,23 +149,42 @@ static thread_local DcfTiming *t_dcf_sink = nullptr;
 DcfTiming *dcf_timing_sink() { return t_dcf_sink; }
 void set_dcf_timing_sink(DcfTiming *t) { t_dcf_sink = t; }
 
+int DcfTiming::take(cudaEvent_t *e)
+{
+    if (used == pool.size()) {
+        cudaEvent_t n = nullptr;
+        DDG_CUDA(cudaEventCreate(&n));
+        pool.push_back(n);
+    }
+    *e = pool[used++];
+    return DDG_OK;
+}
+
+void DcfTiming::release()
+{
+    for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    pool.clear(), recs.clear(), used = 0;
+}
+
 int TimedLaunch::begin(cudaStream_t st)
 {
     DcfTiming *tm = t_dcf_sink;
-    if (!tm || !tm->enabled || tm->nrec >= int(sizeof(tm->recs) / sizeof(tm->recs[0]))) return DDG_OK;
-    rec = &tm->recs[tm->nrec];
-    DDG_CUDA(cudaEventCreate(&rec->a));
-    DDG_CUDA(cudaEventCreate(&rec->b));
-    DDG_CUDA(cudaEventRecord(rec->a, st));
+    if (!tm || !tm->enabled) return DDG_OK;
+    DcfTiming::Rec r{};
+    DDG_TRY(tm->take(&r.a));
+    DDG_TRY(tm->take(&r.b));
+    DDG_CUDA(cudaEventRecord(r.a, st));
+    tm->recs.push_back(r);
+    sink = tm, idx = tm->recs.size() - 1;
     return DDG_OK;
 }
 
 int TimedLaunch::end(cudaStream_t st, double bytes, double aes, double evals)
 {
-    if (!rec) return DDG_OK;
-    DDG_CUDA(cudaEventRecord(rec->b, st));
-    rec->bytes = bytes, rec->aes = aes, rec->evals = evals;
-    t_dcf_sink->nrec++;
+    if (!sink) return DDG_OK;
+    DcfTiming::Rec &r = sink->recs[idx];
+    DDG_CUDA(cudaEventRecord(r.b, st));
+    r.bytes = bytes, r.aes = aes, r.evals = evals, r.done = true;
     return DDG_OK;
 }
 

@@ -256,6 +256,8 @@ int ddg_party_destroy(ddg_party *h)
     h->P.w.release();
     if (h->P.copy_stream) cudaStreamSynchronize(h->P.copy_stream);
     h->P.release_inputs();
+    h->P.timing.release();
+    if (h->P.ref_event) cudaEventDestroy(h->P.ref_event);
     if (h->P.owns_chan) delete h->P.chan;
     cudaStreamDestroy(h->P.stream);
     delete h;
@@ -445,21 +447,19 @@ int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *c
         set_last_error("party 1: %s", err1.c_str());
         return st1;
     }
-    if (st0 == DDG_OK) st0 = pair_dcf_union(p0->P, p1->P);
     return st0;
 }
 
 int ddg_party_enable_dcf_timing(ddg_party *h, int on)
 {
     DDG_CHECK(h, DDG_ERR_ARG, "null party");
-    h->P.timing.enabled = on != 0;
-    h->P.dcf = DcfAcc();
-    return DDG_OK;
+    return reset_timing(h->P, on != 0);
 }
 
 int ddg_party_dcf_timing(ddg_party *h, double *out6)
 {
     DDG_CHECK(h && out6, DDG_ERR_ARG, "null argument");
+    DDG_TRY(settle_timing(h->P));
     const DcfAcc &a = h->P.dcf;
     double v[6] = {a.launches, a.bytes, a.aes, a.sum_ms, a.union_ms, a.pair_union_ms};
     for (int i = 0; i < 6; i++) out6[i] = v[i];
@@ -596,7 +596,6 @@ int ddg_forward_eval_pair_streamed(ddg_keystream *ks0, ddg_keystream *ks1, int b
         set_last_error("party 1: %s", err1.c_str());
         return st1;
     }
-    if (st0 == DDG_OK) st0 = pair_dcf_union(*ks0->ks.P, *ks1->ks.P);
     return st0;
 }
 

@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cstdio>
+#include <vector>
 #include <cuda_runtime.h>
 
 #include "../../include/ddg_fss.h"
@@ -47,16 +48,22 @@ uint64_t launch_count();
 // Optional timing of the comparison kernels (DCF gate round 1; OT garble and
 // AND-tree levels): when a thread has a sink installed, every such launch is
 // bracketed by CUDA events on its stream together with its algorithmic bytes
-// and AES blocks.
+// and AES blocks.  The events come from a pool that is created once and
+// reused, and the records are read back only when the caller asks for the
+// totals, so that a timed forward spends no host time on them after its
+// stream has drained.
 struct DcfTiming {
     struct Rec {
         cudaEvent_t a, b;
         double bytes, aes, evals;
+        bool done;  // the end event was recorded
     };
-    cudaEvent_t ref = nullptr;  // recorded at forward start on the same stream
-    Rec recs[256];
-    int nrec = 0;
+    std::vector<cudaEvent_t> pool;  // timing events, reused once their records are read back
+    size_t used = 0;
+    std::vector<Rec> recs;          // launches not yet read back
     bool enabled = false;
+    int take(cudaEvent_t *e);
+    void release();                 // destroy the pool (its events must be complete)
 };
 // keep freed stream-ordered allocations of the device's default memory pool
 // cached (release threshold = infinity), once per device (forward.cu)
@@ -67,7 +74,8 @@ void set_dcf_timing_sink(DcfTiming *t);
 
 // brackets one comparison-kernel launch with events when a sink is installed
 struct TimedLaunch {
-    DcfTiming::Rec *rec = nullptr;
+    DcfTiming *sink = nullptr;
+    size_t idx = 0;
     int begin(cudaStream_t st);
     int end(cudaStream_t st, double bytes, double aes, double evals);
 };

@@ -27,6 +27,23 @@ __global__ void k_add(T *out, const T *a, const T *b, uint64_t n)
     GRID_STRIDE(i, n) out[i] = a[i] + b[i];
 }
 
+// the same on 16-byte vectors (all three pointers 16-byte aligned); the
+// n % V tail elements go through k_add
+template <typename T>
+__global__ void k_add_v16(T *out, const T *a, const T *b, uint64_t nv)
+{
+    constexpr int V = 16 / sizeof(T);
+    GRID_STRIDE(i, nv)
+    {
+        uint4 x = reinterpret_cast<const uint4 *>(a)[i], y = reinterpret_cast<const uint4 *>(b)[i];
+        T *xs = reinterpret_cast<T *>(&x);
+        const T *ys = reinterpret_cast<const T *>(&y);
+#pragma unroll
+        for (int k = 0; k < V; k++) xs[k] += ys[k];
+        reinterpret_cast<uint4 *>(out)[i] = x;
+    }
+}
+
 template <typename T>
 __global__ void k_sub(T *out, const T *a, const T *b, uint64_t n)
 {
@@ -37,6 +54,16 @@ template <typename T>
 int ew_add(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st)
 {
     if (!n) return DDG_OK;
+    constexpr uint64_t V = 16 / sizeof(T);
+    const bool vec = ((uintptr_t(out) | uintptr_t(a) | uintptr_t(b)) & 15) == 0 && n >= V;
+    if (vec) {
+        const uint64_t nv = n / V;
+        k_add_v16<T><<<ew_grid(nv), 256, 0, st>>>(out, a, b, nv);
+        note_launch();
+        DDG_CUDA(cudaGetLastError());
+        if (n % V == 0) return DDG_OK;
+        out += nv * V, a += nv * V, b += nv * V, n -= nv * V;
+    }
     k_add<T><<<ew_grid(n), 256, 0, st>>>(out, a, b, n);
     note_launch();
     DDG_CUDA(cudaGetLastError());

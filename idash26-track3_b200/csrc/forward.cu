@@ -787,11 +787,12 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         for (int i = 0; i < 4; i++) e.in[i] = static_cast<const T *>(src[i]);
     }
     const uint64_t sent0 = P.chan->bytes_sent[P.party], rounds0 = P.chan->rounds[P.party];
-    P.intervals.clear();
     if (P.timing.enabled) {
+        // one reference event per timing session: every timed launch of every
+        // forward since enabling is read against it
         if (!P.ref_event) DDG_CUDA(cudaEventCreate(&P.ref_event));
-        DDG_CUDA(cudaEventRecord(P.ref_event, P.stream));
-        P.timing.nrec = 0;
+        if (!P.ref_live) DDG_CUDA(cudaEventRecord(P.ref_event, P.stream));
+        P.ref_live = true;
         set_dcf_timing_sink(&P.timing);
     }
     affinity_graph<T>(e);
@@ -822,20 +823,6 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         if (auto *lp = dynamic_cast<LocalPairChannel *>(P.chan)) lp->fail();
         return e.err;
     }
-    if (P.timing.enabled) {
-        for (int i = 0; i < P.timing.nrec; i++) {
-            auto &r = P.timing.recs[i];
-            float a = 0, b = 0;
-            cudaEventElapsedTime(&a, P.ref_event, r.a);
-            cudaEventElapsedTime(&b, P.ref_event, r.b);
-            P.intervals.emplace_back(double(a), double(b));
-            P.dcf.launches += 1, P.dcf.bytes += r.bytes, P.dcf.aes += r.aes, P.dcf.sum_ms += double(b - a);
-            cudaEventDestroy(r.a);
-            cudaEventDestroy(r.b);
-        }
-        P.timing.nrec = 0;
-        P.dcf.union_ms += union_ms(P.intervals);
-    }
     P.stats.bytes_sent = P.chan->bytes_sent[P.party] - sent0;
     P.stats.rounds = P.chan->rounds[P.party] - rounds0;
     P.stats.key_bytes_used = e.off;
@@ -865,20 +852,57 @@ double union_ms(std::vector<std::pair<double, double>> v)
     return tot;
 }
 
-// union of both parties' DCF launch intervals of the last forward on a common
-// timeline (the two ref events live on the same device)
-int pair_dcf_union(Party &p0, Party &p1)
+// read back the party's pending timed launches (their forwards have finished:
+// the forward drains its stream before returning) into its intervals and
+// totals, and hand their events back to the pool
+int settle_timing(Party &P)
 {
-    Party *ps[2] = {&p0, &p1};
-    return parties_dcf_union(ps, 2);
+    DcfTiming &t = P.timing;
+    if (t.recs.empty()) return DDG_OK;
+    DDG_CHECK(P.ref_live, DDG_ERR_STATE, "timed launches without a reference event");
+    DDG_CUDA(cudaSetDevice(P.device));
+    for (const auto &r : t.recs) {
+        if (!r.done) continue;  // a launch that failed between its two events
+        float a = 0, b = 0;
+        DDG_CUDA(cudaEventElapsedTime(&a, P.ref_event, r.a));
+        DDG_CUDA(cudaEventElapsedTime(&b, P.ref_event, r.b));
+        P.intervals.emplace_back(double(a), double(b));
+        P.dcf.launches += 1, P.dcf.bytes += r.bytes, P.dcf.aes += r.aes, P.dcf.sum_ms += double(b - a);
+    }
+    t.recs.clear(), t.used = 0;
+    // forwards of one party never overlap, so the union over the whole
+    // session is the sum of the per-forward unions
+    P.dcf.union_ms = union_ms(P.intervals);
+    return DDG_OK;
 }
 
-// union of several parties' DCF launch intervals of their last forwards, on
-// the timeline of ps[0] (all on one device); accumulated on ps[0]
+int reset_timing(Party &P, bool on)
+{
+    P.timing.enabled = on;
+    P.timing.recs.clear(), P.timing.used = 0;
+    P.dcf = DcfAcc();
+    P.intervals.clear();
+    P.ref_live = false;
+    if (!on) return DDG_OK;
+    // events for ~28 forwards' comparison launches up front; the pool grows on
+    // demand beyond that, while the host is ahead of the device
+    DDG_CUDA(cudaSetDevice(P.device));
+    while (P.timing.pool.size() < 4096) {
+        cudaEvent_t e = nullptr;
+        DDG_CUDA(cudaEventCreate(&e));
+        P.timing.pool.push_back(e);
+    }
+    return DDG_OK;
+}
+
+// union of several parties' comparison-launch intervals since timing was
+// enabled, on the timeline of ps[0] (all on one device); stored on ps[0]
 int parties_dcf_union(Party *const *ps, int n)
 {
-    for (int i = 0; i < n; i++)
-        if (!ps[i]->timing.enabled || !ps[i]->ref_event) return DDG_OK;
+    for (int i = 0; i < n; i++) {
+        if (!ps[i]->timing.enabled || !ps[i]->ref_live) return DDG_OK;
+        DDG_TRY(settle_timing(*ps[i]));
+    }
     std::vector<std::pair<double, double>> all = ps[0]->intervals;
     for (int i = 1; i < n; i++) {
         DDG_CHECK(ps[i]->device == ps[0]->device, DDG_ERR_ARG, "DCF interval union needs one device");
@@ -886,7 +910,7 @@ int parties_dcf_union(Party *const *ps, int n)
         DDG_CUDA(cudaEventElapsedTime(&off, ps[0]->ref_event, ps[i]->ref_event));
         for (auto &iv : ps[i]->intervals) all.emplace_back(iv.first + off, iv.second + off);
     }
-    ps[0]->dcf.pair_union_ms += union_ms(all);
+    ps[0]->dcf.pair_union_ms = union_ms(all);
     return DDG_OK;
 }
 

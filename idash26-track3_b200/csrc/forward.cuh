@@ -56,8 +56,9 @@ struct Party {
     PartyStats stats;
     DcfTiming timing;
     DcfAcc dcf;
-    cudaEvent_t ref_event = nullptr;                     // start of the last forward
-    std::vector<std::pair<double, double>> intervals;    // last forward's DCF launches, ms after ref_event
+    cudaEvent_t ref_event = nullptr;                     // start of the first forward since timing was enabled
+    bool ref_live = false;                               // ref_event is recorded for this timing session
+    std::vector<std::pair<double, double>> intervals;    // read-back comparison launches, ms after ref_event
     // device staging of host inputs (kept across forwards), copied on a side
     // stream; in_ev[0..3] mark each input's arrival, in_ev[4] the start of a forward
     void *in_buf[4] = {};
@@ -74,7 +75,8 @@ void set_relu_parts(int parts);
 void set_relu_backend(int backend);  // DDG_RELU_DCF or DDG_RELU_OT
 int relu_backend();
 double union_ms(std::vector<std::pair<double, double>> v);
-int pair_dcf_union(Party &p0, Party &p1);
+int settle_timing(Party &P);
+int reset_timing(Party &P, bool on);
 int parties_dcf_union(Party *const *ps, int n);
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
                  bool on_host, int64_t *h_out_raw, double *h_aff);

@@ -27,6 +27,10 @@ int ring_gemm(const GemmArgs<T> &a, cudaStream_t st);
 // the CUDA-core kernel (ring_gemm.cu)
 template <typename T>
 int ring_gemm_simt(const GemmArgs<T> &a, cudaStream_t st);
+// rows [m0, M) of a on the CUDA cores, 16-row blocks (ring_gemm.cu): the
+// ragged last rows of a tensor-core GEMM
+template <typename T>
+int ring_gemm_rows(const GemmArgs<T> &a, int m0, cudaStream_t st);
 // DDG_OK unless a tensor-core GEMM launch gave up on one of its bounded waits
 // since the last clear (reads a device word: synchronises with the device)
 int ring_gemm_tc_error(bool clear);

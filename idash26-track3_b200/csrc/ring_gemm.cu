@@ -126,4 +126,101 @@ int ring_gemm_simt(const GemmArgs<T> &a, cudaStream_t st)
 template int ring_gemm_simt<uint32_t>(const GemmArgs<uint32_t> &, cudaStream_t);
 template int ring_gemm_simt<uint64_t>(const GemmArgs<uint64_t> &, cudaStream_t);
 
+// Thin row blocks: the last M % 128 rows of a GEMM whose other rows run on the
+// tensor cores in whole 128-row tiles (the per-sample Beaver products have
+// 138 rows: a second 128-row tile would do 10 rows of work).  16 rows x 64
+// columns per 256-thread CTA; a thread owns one column of four rows (rows g,
+// g+4, g+8, g+12 of its row group g), so a warp reads one broadcast A element
+// and 32 consecutive B elements per step.  Same formula as ring_gemm_kernel.
+constexpr int TR = 16, TN = 64, TK = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(256) ring_gemm_thin_kernel(const __grid_constant__ GemmArgs<T> a)
+{
+    __shared__ T As[TR][TK + 1];
+    __shared__ T Bs[TK][TN];
+    const int b = blockIdx.z;
+    const int m0 = blockIdx.y * TR, n0 = blockIdx.x * TN;
+    const int col = threadIdx.x % TN, rg = threadIdx.x / TN;
+    T acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int phase = 0; phase < 2; phase++) {
+        const T *A = phase == 0 ? a.A1 : a.A2;
+        const T *B = phase == 0 ? a.B1 : a.B2;
+        if (A == nullptr) continue;
+        const T *Bm = phase == 0 ? a.B1m : nullptr;
+        const T s1 = phase == 0 ? a.s1 : T(1);
+        const int64_t lda = phase == 0 ? a.lda1 : a.lda2, ldb = phase == 0 ? a.ldb1 : a.ldb2;
+        A += int64_t(b) * (phase == 0 ? a.sA1 : a.sA2);
+        if (B) B += int64_t(b) * (phase == 0 ? a.sB1 : a.sB2);
+        if (Bm) Bm += int64_t(b) * a.sB1m;
+        T sub[4] = {0, 0, 0, 0};
+        for (int k0 = 0; k0 < a.K; k0 += TK) {
+#pragma unroll
+            for (int q = 0; q < TR * TK / 256; q++) {
+                const int idx = threadIdx.x + q * 256, r = idx / TK, c = idx % TK;
+                const int gm = m0 + r, gk = k0 + c;
+                As[r][c] = (gm < a.M && gk < a.K) ? A[int64_t(gm) * lda + gk] : T(0);
+            }
+#pragma unroll
+            for (int q = 0; q < TK * TN / 256; q++) {
+                const int idx = threadIdx.x + q * 256, r = idx / TN, c = idx % TN;
+                const int gk = k0 + r, gn = n0 + c;
+                T v = 0;
+                if (gk < a.K && gn < a.N) {
+                    const int64_t o = int64_t(gk) * ldb + gn;
+                    if (B) v = s1 * B[o];
+                    if (Bm) v -= Bm[o];
+                }
+                Bs[r][c] = v;
+            }
+            __syncthreads();
+#pragma unroll 8
+            for (int kk = 0; kk < TK; kk++) {
+                const T bv = Bs[kk][col];
+#pragma unroll
+                for (int i = 0; i < 4; i++) sub[i] += As[rg + 4 * i][kk] * bv;
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[i] = phase == 0 ? sub[i] : acc[i] - sub[i];
+    }
+    const int gn = n0 + col;
+    if (gn >= a.N) return;
+    const T *Add = a.Add ? a.Add + int64_t(b) * a.sAdd : nullptr;
+    T *C = a.C + int64_t(b) * a.sC;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int gm = m0 + rg + 4 * i;
+        if (gm >= a.M) continue;
+        T v = a.sign * acc[i];
+        if (a.bias) v += a.bias[gn];
+        if (Add) v += Add[int64_t(gm) * a.ldAdd + gn];
+        C[int64_t(gm) * a.ldc + gn] = v;
+    }
+}
+
+template <typename T>
+int ring_gemm_rows(const GemmArgs<T> &a, int m0, cudaStream_t st)
+{
+    DDG_CHECK(m0 >= 0 && m0 <= a.M && a.A1 && a.C, DDG_ERR_ARG, "gemm rows: bad row offset or operand");
+    if (m0 == a.M || a.N == 0 || a.batch == 0) return DDG_OK;
+    GemmArgs<T> t = a;
+    t.M = a.M - m0;
+    t.A1 = a.A1 + int64_t(m0) * a.lda1;
+    if (a.A2) t.A2 = a.A2 + int64_t(m0) * a.lda2;
+    if (a.Add) t.Add = a.Add + int64_t(m0) * a.ldAdd;
+    t.C = a.C + int64_t(m0) * a.ldc;
+    dim3 grid((t.N + TN - 1) / TN, (t.M + TR - 1) / TR, t.batch);
+    DDG_CHECK(grid.y <= 65535 && grid.z <= 65535, DDG_ERR_ARG, "gemm grid too large (M=%d batch=%d)", t.M, t.batch);
+    ring_gemm_thin_kernel<T><<<grid, 256, 0, st>>>(t);
+    note_launch();
+    DDG_CUDA(cudaGetLastError());
+    return DDG_OK;
+}
+
+template int ring_gemm_rows<uint32_t>(const GemmArgs<uint32_t> &, int, cudaStream_t);
+template int ring_gemm_rows<uint64_t>(const GemmArgs<uint64_t> &, int, cudaStream_t);
+
 }  // namespace ddg

@@ -706,12 +706,23 @@ constexpr int tc_max_k()
     return sizeof(T) == 4 ? 8192 : 4096;
 }
 
+// rows beyond the last whole 128-row tile that go to the CUDA cores instead
+// of a mostly empty tensor-core tile (default path)
+constexpr int TC_THIN_TAIL = 32;
+
 template <typename T>
 int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
 {
     if (a.M == 0 || a.N == 0 || a.batch == 0) return DDG_OK;
     const int ktot = a.A2 ? 2 * a.K : a.K;
     if (g_gemm_path == 1 || a.K == 0 || ktot > tc_max_k<T>()) return ring_gemm_simt<T>(a, st);
+    const int tail = a.M % TC_BM;
+    if (g_gemm_path == 0 && a.M > TC_BM && tail != 0 && tail <= TC_THIN_TAIL) {
+        GemmArgs<T> whole = a;
+        whole.M = a.M - tail;
+        DDG_TRY(ring_gemm<T>(whole, st));
+        return ring_gemm_rows<T>(a, whole.M, st);
+    }
     if (g_gemm_path == 2) return launch_tc<T, 64, false>(a, st);
     if (g_gemm_path == 3) return launch_tc<T, sizeof(T) == 4 ? 128 : 32, true>(a, st);
     if constexpr (sizeof(T) == 4) {

@@ -370,14 +370,17 @@ int ddg_gemm_status(void);
  * (DCF) launch is bracketed by CUDA events on the party's stream; out6 gets
  * {launches, algorithmic bytes (key bytes + input + output bits), AES blocks,
  * summed launch ms, ms of the union of this party's launches, ms of the union
- * of both parties' launches of an in-process pair (party 0 only)},
- * accumulated since enabling. */
+ * of both parties' launches of an in-process pair (party 0, as of the last
+ * ddg_parties_dcf_union)}, accumulated since enabling.  Enabling pre-creates
+ * the events of about 28 forwards. */
 uint64_t ddg_launch_count(void);
 int ddg_party_enable_dcf_timing(ddg_party *party, int on);
 int ddg_party_dcf_timing(ddg_party *party, double *out6);
-/* after a forward of several parties on one device (e.g. two half-batch
- * lanes of one party): add the union of their DCF launch intervals to
- * parties[0]'s pair-union total (out6[5]) */
+/* several parties on one device (the two parties of an in-process pair, or
+ * half-batch lanes): set parties[0]'s pair-union total (out6[5]) to the union
+ * of all their DCF launch intervals since timing was enabled.  Launch events
+ * are read back here and in ddg_party_dcf_timing, not at the end of each
+ * forward. */
 int ddg_parties_dcf_union(ddg_party *const *parties, int n);
 
 /* Diagnostics: `threads` independent chains of `iters` fixed-key tree

@@ -109,6 +109,40 @@ def test_forward_host_inputs_and_repeat(ddg, synth, cuda):
 
 
 @pytest.mark.gpu
+def test_forward_comparison_timing(ddg, synth, cuda):
+    """Comparison-kernel timing of an in-process pair: launch events are read
+    back after the forwards, counted once per launch, and the pair union lies
+    between the larger party union and their sum."""
+    bw, B = 32, 3
+    inp = synth.Inputs(B, bw, seed=21, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B)
+    ins, keep = dev_inputs(inp)
+    want_raw, want_aff = expected(inp, q, bw)
+    ddg.forward_pair(p0, p1, B, ins[0], ins[1])  # untimed
+    counts = []
+    for nfwd in (1, 3):
+        for p in (p0, p1):
+            p.enable_dcf_timing(True)
+        for _ in range(nfwd):
+            raw, aff = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+            assert np.array_equal(aff, want_aff)
+        ddg.parties_dcf_union([p0, p1])
+        t = [p0.dcf_timing(), p1.dcf_timing()]
+        counts.append(t[0]["launches"])
+        assert t[0]["launches"] == t[1]["launches"] > 0
+        assert t[0]["bytes"] > 0 and t[0]["sum_ms"] > 0
+        for x in t:
+            assert 0 < x["union_ms"] <= x["sum_ms"] + 1e-6
+        assert max(t[0]["union_ms"], t[1]["union_ms"]) - 1e-6 <= t[0]["pair_union_ms"]
+        assert t[0]["pair_union_ms"] <= t[0]["union_ms"] + t[1]["union_ms"] + 1e-6
+        # a second read-back adds nothing
+        assert p0.dcf_timing()["launches"] == t[0]["launches"]
+        for p in (p0, p1):
+            p.enable_dcf_timing(False)
+    assert counts[1] == 3 * counts[0]
+
+
+@pytest.mark.gpu
 def test_forward_edge_graphs(ddg, synth, cuda):
     """kiba-shaped graphs (up to 100 atoms), a 138-atom graph, and an all-zero
     padding sample (degree 0 -> table[0] = 0; deepdtagen_inference.cu:72-79)."""

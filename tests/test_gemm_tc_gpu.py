@@ -61,7 +61,7 @@ def beaver(ddg, bw, Bt, M, K, N, A, rA, Bm, rB, rC, rng):
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("bw", [32, 64])
 @pytest.mark.parametrize("shape", [(2, 138, 138, 94), (1, 1, 5, 3), (3, 65, 17, 70), (1, 300, 40, 130),
-                                   (2, 129, 33, 65)])
+                                   (2, 129, 33, 65), (3, 160, 45, 130), (2, 138, 276, 312)])
 def test_beaver_matmul_paths(engine, cuda, path, bw, shape):
     engine.gemm_path(path)
     dt = ring_dt(bw)
@@ -77,7 +77,8 @@ def test_beaver_matmul_paths(engine, cuda, path, bw, shape):
 @pytest.mark.gpu
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("bw", [32, 64])
-@pytest.mark.parametrize("shape", [(70, 94, 188), (300, 282, 376), (1, 1024, 128), (256, 256, 1), (5, 3, 2)])
+@pytest.mark.parametrize("shape", [(70, 94, 188), (300, 282, 376), (1, 1024, 128), (256, 256, 1), (5, 3, 2),
+                                   (150, 94, 70), (257, 40, 33)])
 def test_fc_paths(engine, cuda, path, bw, shape):
     engine.gemm_path(path)
     L = engine.lib()

@@ -77,7 +77,12 @@ def test_gloo_world2_layout_broadcast_and_max():
 
 
 def _worker_dies(rank, world, port, q):
-    _init(rank, world, port, timeout_s=5)
+    try:
+        _init(rank, world, port, timeout_s=5)
+        dist.barrier()  # both ranks are connected before one of them dies
+    except Exception as e:  # noqa: BLE001
+        q.put("setup failed: " + type(e).__name__)
+        os._exit(1)
     if rank == 1:
         os._exit(3)  # the peer dies before the next collective
     try:
