@@ -345,6 +345,24 @@ def share_buffers(torch, inp, party, device, rows=None):
     return dev, host
 
 
+def h2d_probe(torch, bufs, device):
+    """Host->device bandwidth of this box for the e2e inputs: the same pinned
+    buffers copied once into fresh device tensors (GB/s), outside any timed
+    region; the e2e step's copies run at about this rate."""
+    srcs = [t for b in bufs for t in b[1]]
+    dsts = [torch.empty_like(t, device=device) for t in srcs]
+    st = torch.cuda.Stream(device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        e0.record(st)
+        for d, h in zip(dsts, srcs):
+            d.copy_(h, non_blocking=True)
+        e1.record(st)
+    e1.synchronize()
+    nbytes = sum(int(t.numel()) for t in srcs)
+    return nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -525,7 +543,7 @@ def main():
         h2d = sum(own) if colo else 2 * sum(own)
         e2e = {"value": pairs * B * a.steps / (ms_e2e / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": h2d * pairs, "d2h_bytes_per_step": B * (bw // 8) * pairs,
-               "ms_per_step": ms_e2e / a.steps}
+               "ms_per_step": ms_e2e / a.steps, "h2d_probe_gbs": h2d_probe(torch, bufs, device)}
 
     value = pairs * B * a.steps / (ms / 1e3)
     peak, peak_kind = measured_peaks()

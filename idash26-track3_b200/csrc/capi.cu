@@ -116,6 +116,12 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
     DDG_CHECK(n == 0 || (d_xhat && d_key0 && d_key1 && d_share0 && d_share1), DDG_ERR_ARG, "null pointer");
     if (n == 0) return DDG_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the per-call openings and state come from the device's default pool:
+    // keep freed blocks cached, as the forward does, so repeated calls do not
+    // map and unmap memory each time
+    int dev = 0;
+    DDG_CUDA(cudaGetDevice(&dev));
+    DDG_TRY(keep_pool_memory(dev));
     GateLayout L = gate_layout(kind, bw, scale, n);
     const uint64_t nw = (n + 31) / 32;
     const int nb = ddg_gate_round1_arrays(kind, bw, scale), nh = (L.ot || L.tt) ? 2 : nb - (L.lo ? 1 : 0);

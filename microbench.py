@@ -4,6 +4,7 @@
     python microbench.py lut  [--n 1048576]
     python microbench.py gemm [--batch 256]
     python microbench.py aes
+    python microbench.py tt   [--sizes 23] [--bw 32]
 
 Prints one JSON object.  Everything goes through libddg.so's C ABI on cuda:0:
 
@@ -21,6 +22,9 @@ Prints one JSON object.  Everything goes through libddg.so's C ABI on cuda:0:
   on the tensor cores (tcgen05 kind::i8 limb products; default and wide
   column tiles) and on the CUDA cores.
 * aes  -- the fixed-key AES ceiling of both AES engines.
+* tt   -- both parties of one truth-table gate (full-compare ReLU, ReLU-ARS,
+  truncation carry) through ddg_gate_eval_pair: all AND-tree levels, the
+  openings in place on the device, and round 2.
 
 Timing: CUDA events on the launching stream after warm-up launches; the
 median of the timed repetitions.
@@ -146,6 +150,51 @@ def run_lut(ddg, torch, a):
     return res
 
 
+def run_tt(ddg, torch, a):
+    """Both parties of one truth-table gate on cuda:0 (ddg_gate_eval_pair: every
+    AND-tree level, the openings in place, round 2): the full-compare ReLU and
+    ReLU-ARS gates and the truncation carry, n = 2^k elements."""
+    hbm, _, src = peaks()
+    res = {"hbm_peak_gbs": hbm, "peak_source": src}
+    st = torch.cuda.current_stream().cuda_stream
+    for bw in a.bw:
+        dt = torch.int32 if bw == 32 else torch.int64
+        for kind, name in ((ddg.GATE_RELU_TTF, "relu_ttf"), (ddg.GATE_RELU_ARS_TTF, "relu_ars_ttf"),
+                           (ddg.GATE_LRS_TT, "lrs_tt")):
+            for lg in a.sizes:
+                N = 1 << lg
+                kb = ddg.gate_key_bytes(kind, bw, 12, N)
+                if 2 * kb + 64 * N > 0.8 * torch.cuda.mem_get_info()[0]:
+                    res[f"bw{bw}_{name}_2^{lg}"] = "skipped: keys do not fit"
+                    continue
+                k0 = torch.empty(kb, dtype=torch.uint8, device="cuda")
+                k1 = torch.empty(kb, dtype=torch.uint8, device="cuda")
+                g = torch.Generator(device="cuda").manual_seed(lg + bw)
+                info = torch.iinfo(dt)
+                r = torch.randint(info.min, info.max, (N,), dtype=dt, device="cuda", generator=g)
+                x = torch.randint(info.min, info.max, (N,), dtype=dt, device="cuda", generator=g)
+                if kind == ddg.GATE_LRS_TT:
+                    x = x & info.max  # LRS precondition: x in [0, 2^(bw-1))
+                ro = torch.empty_like(r)
+                ddg.gate_keygen(kind, bw, 12, N, 1, 1, r.data_ptr(), ro.data_ptr(), k0.data_ptr(), k1.data_ptr(), st)
+                xh = x + r
+                words = (N + 31) // 32
+                nb = ddg.gate_round1_arrays(kind, bw, 12)
+                bits = [torch.empty(nb * words, dtype=torch.int32, device="cuda") for _ in range(2)]
+                sh = [torch.empty_like(r) for _ in range(2)]
+                t = timeit(torch, lambda: ddg.gate_eval_pair(kind, bw, 12, N, xh.data_ptr(), k0.data_ptr(),
+                                                             k1.data_ptr(), bits[0].data_ptr(), bits[1].data_ptr(),
+                                                             sh[0].data_ptr(), sh[1].data_ptr(), st))
+                lay = ddg.tt_key_layout(kind, bw, 12, N)
+                res[f"bw{bw}_{name}_2^{lg}"] = {
+                    "elements_per_s": N / t, "ms": t * 1e3, "key_bytes_per_element_per_party": kb / N,
+                    "levels": lay["levels"], "key_gbs_both_parties": 2 * kb / t / 1e9,
+                    "key_hbm_frac": 2 * kb / t / 1e9 / hbm}
+                del k0, k1, r, x, xh, ro, bits, sh
+                torch.cuda.empty_cache()
+    return res
+
+
 def run_gemm(ddg, torch, a):
     hbm, bf16, src = peaks()
     L = ddg.lib()
@@ -193,7 +242,7 @@ def run_gemm(ddg, torch, a):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("what", choices=["dcf", "lut", "gemm", "aes"])
+    ap.add_argument("what", choices=["dcf", "lut", "gemm", "aes", "tt"])
     ap.add_argument("--sizes", type=int, nargs="+", default=[20, 22, 24, 26])
     ap.add_argument("--bw", type=int, nargs="+", default=[32, 64])
     ap.add_argument("--n", type=int, default=1 << 20)
@@ -207,6 +256,8 @@ def main():
         res = run_dcf(ddg, torch, a)
     elif a.what == "lut":
         res = run_lut(ddg, torch, a)
+    elif a.what == "tt":
+        res = run_tt(ddg, torch, a)
     elif a.what == "gemm":
         res = run_gemm(ddg, torch, a)
     else:
