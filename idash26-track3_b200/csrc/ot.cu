@@ -10,6 +10,7 @@
 #include <type_traits>
 
 #include "ot.cuh"
+#include "tt_lanes.cuh"
 
 namespace ddg {
 
@@ -267,18 +268,14 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
 }
 
 // ---- the same step with the plan compiled in.  Every digit, combine and
-// pass is visited by a compile-time loop, and plan fields are read only into
-// constexpr locals, so no plan object exists at run time (a constexpr plan
-// object indexed from unrolled loops ended up in local memory).
-template <int I, int END, class F>
-__device__ __forceinline__ void static_for(const F &f)
-{
-    if constexpr (I < END) {
-        f(std::integral_constant<int, I>{});
-        static_for<I + 1, END>(f);
-    }
-}
-
+// pass is visited by a compile-time loop (static_for, tt_lanes.cuh), and plan
+// fields are read only into constexpr locals, so no plan object exists at run
+// time (a constexpr plan object indexed from unrolled loops ended up in local
+// memory).  The truth-table modes close and open their AND levels with the
+// word-parallel lane layout of tt_lanes.cuh; the OT mode keeps the per-combine
+// form of level_elem.  Both parties and every level of a gate run the same
+// compiled-in plan (level_launch covers levels 1..6), so the two layouts never
+// meet.
 template <int MODE, int NB, int SB, int PARTY, int L>
 __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, uint32_t &hl, uint32_t &he,
                                              uint32_t &ll)
@@ -329,6 +326,9 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
             const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
             st |= (lt << (2 * (g0 + t))) | (eq << (2 * (g0 + t) + 1));
         });
+    } else if constexpr (TT) {
+        const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
+        st = tt_close<MODE, NB, SB, PARTY, L>(st, tw, O);
     } else {
         const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
         constexpr bool cword = !TT && PARTY == 0;
@@ -358,7 +358,10 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
             }
         });
     }
-    if constexpr (L <= P.levels) {
+    if constexpr (TT && L <= P.levels) {
+        a.open_out[e] = tt_open<MODE, NB, SB, L>(st, tw);
+        store_state<uint32_t>(a.state, e, st);
+    } else if constexpr (L <= P.levels) {
         uint32_t w = 0;
         constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
         static_for<qa, qb>([&](auto qi) {
@@ -475,6 +478,7 @@ static void level_launch(const OtLevelArgs &a, int grid, cudaStream_t st)
     case 3: ot_level_kernel<MODE, NB, SB, PARTY, 3><<<grid, 256, 0, st>>>(a); break;
     case 4: ot_level_kernel<MODE, NB, SB, PARTY, 4><<<grid, 256, 0, st>>>(a); break;
     case 5: ot_level_kernel<MODE, NB, SB, PARTY, 5><<<grid, 256, 0, st>>>(a); break;
+    case 6: ot_level_kernel<MODE, NB, SB, PARTY, 6><<<grid, 256, 0, st>>>(a); break;
     default: ot_level_kernel<MODE, NB, SB, PARTY, 0><<<grid, 256, 0, st>>>(a); break;
     }
 }

@@ -1,0 +1,132 @@
+// Word-parallel AND-tree levels of the truth-table comparison gates, for the
+// plans compiled into the level kernel (ot.cu).  Host and device, so that the
+// logic can be checked on the CPU (tests/tt_lanes_check.cpp).
+//
+// The digit-share state of one element keeps 2 bits per digit (lt at 2g, eq
+// at 2g + 1), as the level-1 table read writes it.  In the lane layout the
+// combines never move their outputs down: combine i of a part at level l
+// reads its L node at lane 2*base + i * 2^(l+1) and its H node 2^l bits above,
+// and writes its output over the L node.  Every combine of a level therefore
+// finds its two inputs at the same offsets from its lane, an odd top node is
+// already where the next level looks for it, and the part roots stay at
+// 2*base.  The openings of a level carry (e, f, f') of each combine at
+// (lane, lane + 1, lane + 2); lanes are at least 4 apart, so a level's
+// openings, the triple bits gathered to the lanes, and the closing logic each
+// take one 32-bit word and a few word-wide operations for all its combines.
+// The cross combine of the full-compare plans (H = the hi root at 0, L = the
+// lo root) is alone at its level and uses lanes 0 (e) and 1 (f).
+//
+// Formulas (x ^ y: XOR; products: AND; p0 = 1 for party 0):
+//   open:  e = eq_H ^ a,  f = lt_L ^ b,  f' = eq_L ^ b'
+//   close: lt = lt_H ^ c ^ f a ^ e b ^ p0 e f,  eq = c' ^ f' a ^ e b' ^ p0 e f'
+// with (a, b, b', c, c') the party's triple bits of the combine (5 bits at
+// 5q of its triple words, c = a b, c' = a b' shared by the dealer).
+#pragma once
+#include <cstdint>
+#include <type_traits>
+
+#include "digit_plan.cuh"
+
+namespace ddg {
+
+template <int I, int END, class F>
+__host__ __device__ __forceinline__ void static_for(const F &f)
+{
+    if constexpr (I < END) {
+        f(std::integral_constant<int, I>{});
+        static_for<I + 1, END>(f);
+    }
+}
+
+// lane of combine q at level l (1-based) in the lane layout
+__host__ __device__ constexpr int tt_lane(const OtPlan &P, int q, int l)
+{
+    return P.comb[q].part == 2 ? 0 : 2 * P.base[P.comb[q].part] + int(P.comb[q].out) * (2 << l);
+}
+
+// lanes of the combines of level l (eq_only: those that compute eq)
+__host__ __device__ constexpr uint32_t tt_lane_mask(const OtPlan &P, int l, bool eq_only)
+{
+    uint32_t m = 0;
+    if (l < 1 || l > P.levels) return 0;
+    for (int q = P.lvl_first[l - 1]; q < P.lvl_first[l]; q++)
+        if (!eq_only || P.comb[q].eq) m |= 1u << tt_lane(P, q, l);
+    return m;
+}
+
+// the 5 triple bits (a, b, b', c, c') of combine Q from the party's triple words
+template <int Q>
+__host__ __device__ __forceinline__ uint32_t tri5(const uint32_t (&tw)[3])
+{
+    constexpr int b = 5 * Q, w = b / 32, sh = b % 32;
+    if constexpr (sh + 5 <= 32) {
+        return (tw[w] >> sh) & 31u;
+    } else {
+        return ((tw[w] >> sh) | (tw[w + 1] << (32 - sh))) & 31u;
+    }
+}
+
+// openings of level L (1 <= L <= levels) from the state after level L - 1
+template <int MODE, int NB, int SB, int L>
+__host__ __device__ __forceinline__ uint32_t tt_open(uint32_t st, const uint32_t (&tw)[3])
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
+    if constexpr (qa >= qb) {
+        return 0u;
+    } else if constexpr (P.comb[qa].part == 2) {
+        // the cross combine: e = eq of the hi root, f = lt of the lo root
+        constexpr int lo = 2 * P.base[1];
+        const uint32_t g = tri5<qa>(tw);
+        return (((st >> 1) ^ g) & 1u) | ((((st >> lo) ^ (g >> 1)) & 1u) << 1);
+    } else {
+        uint32_t t3 = 0;  // (a, b, b') of every combine at its lane
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value, lane = tt_lane(P, q, L);
+            t3 |= (tri5<q>(tw) & 7u) << lane;
+        });
+        constexpr uint32_t M = tt_lane_mask(P, L, false), Meq = tt_lane_mask(P, L, true);
+        constexpr int S = 1 << L;  // the H node sits S bits above the lane
+        const uint32_t e = (st >> (S + 1)) ^ t3;
+        const uint32_t f = st ^ (t3 >> 1);
+        const uint32_t f2 = (st >> 1) ^ (t3 >> 2);
+        return (e & M) | ((f & M) << 1) | ((f2 & Meq) << 2);
+    }
+}
+
+// close level L - 1 (2 <= L): O = both parties' openings of level L - 1, XORed
+template <int MODE, int NB, int SB, int PARTY, int L>
+__host__ __device__ __forceinline__ uint32_t tt_close(uint32_t st, const uint32_t (&tw)[3], uint32_t O)
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    constexpr int lf = L - 1;
+    constexpr int qa = lf >= 1 ? P.lvl_first[lf - 1] : 0, qb = lf >= 1 ? P.lvl_first[lf] : 0;
+    if constexpr (qa >= qb) {
+        return st;
+    } else if constexpr (P.comb[qa].part == 2) {
+        const uint32_t g = tri5<qa>(tw);
+        const uint32_t e = O & 1u, f = (O >> 1) & 1u;
+        uint32_t lt = (st ^ (g >> 3) ^ (f & g) ^ (e & (g >> 1))) & 1u;
+        if constexpr (PARTY == 0) lt ^= e & f;
+        return (st & ~3u) | lt;
+    } else {
+        uint32_t t3 = 0, t2 = 0;  // (a, b, b') and (c, c') of every combine at its lane
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value, lane = tt_lane(P, q, lf);
+            const uint32_t g = tri5<q>(tw);
+            t3 |= (g & 7u) << lane;
+            t2 |= (g >> 3) << lane;
+        });
+        constexpr uint32_t M = tt_lane_mask(P, lf, false), Meq = tt_lane_mask(P, lf, true);
+        constexpr int S = 1 << lf;
+        const uint32_t e = O, f = O >> 1, f2 = O >> 2;
+        uint32_t lt = (st >> S) ^ t2 ^ (f & t3) ^ (e & (t3 >> 1));
+        uint32_t eq = (t2 >> 1) ^ (f2 & t3) ^ (e & (t3 >> 2));
+        if constexpr (PARTY == 0) lt ^= e & f, eq ^= e & f2;
+        return (st & ~(M | (M << 1))) | (lt & M) | ((eq & Meq) << 1);
+    }
+}
+
+}  // namespace ddg

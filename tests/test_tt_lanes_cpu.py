@@ -1,0 +1,37 @@
+"""The word-parallel AND-tree levels of the truth-table gates, on the CPU.
+
+The level kernel compiled for (bw, scale) = (32, 12) and (64, 12) closes and
+opens every AND of a level with word-wide operations on a lane layout
+(idash26-track3_b200/csrc/tt_lanes.cuh).  tests/tt_lanes_check.cpp plays the
+whole tree for both parties on random shared digit bits and dealer triples and
+compares the reconstructed roots with the plaintext radix comparison; this test
+compiles it with the host C++ compiler and runs it.  The GPU tests
+(tests/test_tt_gpu.py) then check the kernels against the oracle's keys.
+"""
+import os
+import shutil
+import subprocess
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "..", "idash26-track3_b200", "csrc")
+
+
+def _cuda_include():
+    for d in (os.environ.get("CUDA_HOME", ""), "/usr/local/cuda"):
+        if d and os.path.exists(os.path.join(d, "include", "cuda_runtime.h")):
+            return os.path.join(d, "include")
+    return None
+
+
+def test_lane_levels_reconstruct_the_plaintext_comparison(tmp_path):
+    cxx = shutil.which("g++") or shutil.which("c++")
+    inc = _cuda_include()
+    if cxx is None or inc is None:
+        pytest.skip("needs a host C++ compiler and the CUDA headers")
+    exe = tmp_path / "tt_lanes_check"
+    subprocess.run([cxx, "-std=c++17", "-O2", "-I", CSRC, "-I", inc, os.path.join(HERE, "tt_lanes_check.cpp"), "-o",
+                    str(exe)], check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe), "5000"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
