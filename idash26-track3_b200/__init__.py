@@ -85,6 +85,10 @@ SIGNATURES = {
     "ddg_forward_key_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_forward_eval": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
+    "ddg_forward_graph_create": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                        ctypes.POINTER(_vp)]),
+    "ddg_forward_graph_launch": (_i32, [_vp, _vp, _vp]),
+    "ddg_forward_graph_destroy": (_i32, [_vp]),
     "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
     "ddg_launch_count": (_u64, []),
     "ddg_key_chunk_bytes": (_u64, [_i32, _i32, _i32]),
@@ -300,6 +304,38 @@ def forward_pair(p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
     aff = np.zeros(batch, dtype=np.float64)
     check(lib().ddg_forward_eval_pair(p0.h, p1.h, batch, a0, a1, int(on_host), raw.ctypes.data, aff.ctypes.data))
     return raw, aff
+
+
+class ForwardGraph:
+    """One pair forward of device-resident inputs captured into a CUDA graph
+    (ddg_forward_graph_create) and replayed by launch(); see ddg_fss.h.  Run one
+    ordinary forward_pair of the pair before creating it, and close it before
+    the parties."""
+
+    def __init__(self, p0: Party, p1: Party, batch, inputs0, inputs1):
+        self.batch = batch
+        a0 = (_vp * 4)(*inputs0)
+        a1 = (_vp * 4)(*inputs1)
+        h = _vp()
+        check(lib().ddg_forward_graph_create(p0.h, p1.h, batch, a0, a1, ctypes.byref(h)))
+        self.h = h
+
+    def launch(self, outputs=True):
+        """Replay the forward; returns (raw, affinity) of party 0's reveal, or None."""
+        import numpy as np
+
+        if not outputs:
+            check(lib().ddg_forward_graph_launch(self.h, None, None))
+            return None
+        raw = np.zeros(self.batch, dtype=np.int64)
+        aff = np.zeros(self.batch, dtype=np.float64)
+        check(lib().ddg_forward_graph_launch(self.h, raw.ctypes.data, aff.ctypes.data))
+        return raw, aff
+
+    def close(self):
+        if self.h:
+            check(lib().ddg_forward_graph_destroy(self.h))
+            self.h = None
 
 
 def forward_max_exchange_bytes(bw: int, scale: int, batch: int) -> int:

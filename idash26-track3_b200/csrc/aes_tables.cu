@@ -144,6 +144,19 @@ int aes_device_init()
 static std::atomic<uint64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 uint64_t launch_count() { return g_launches.load(); }
+void add_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int record_timing_event(cudaEvent_t e, cudaStream_t st)
+{
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    DDG_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs == cudaStreamCaptureStatusActive) {
+        DDG_CUDA(cudaEventRecordWithFlags(e, st, cudaEventRecordExternal));
+    } else {
+        DDG_CUDA(cudaEventRecord(e, st));
+    }
+    return DDG_OK;
+}
 
 static thread_local DcfTiming *t_dcf_sink = nullptr;
 DcfTiming *dcf_timing_sink() { return t_dcf_sink; }
@@ -173,7 +186,7 @@ int TimedLaunch::begin(cudaStream_t st)
     DcfTiming::Rec r{};
     DDG_TRY(tm->take(&r.a));
     DDG_TRY(tm->take(&r.b));
-    DDG_CUDA(cudaEventRecord(r.a, st));
+    DDG_TRY(record_timing_event(r.a, st));
     tm->recs.push_back(r);
     sink = tm, idx = tm->recs.size() - 1;
     return DDG_OK;
@@ -183,7 +196,7 @@ int TimedLaunch::end(cudaStream_t st, double bytes, double aes, double evals)
 {
     if (!sink) return DDG_OK;
     DcfTiming::Rec &r = sink->recs[idx];
-    DDG_CUDA(cudaEventRecord(r.b, st));
+    DDG_TRY(record_timing_event(r.b, st));
     r.bytes = bytes, r.aes = aes, r.evals = evals, r.done = true;
     return DDG_OK;
 }

@@ -9,6 +9,7 @@
 #include "forward.cuh"
 #include "gates.cuh"
 #include "keystream.cuh"
+#include "linear.cuh"
 #include "ot.cuh"
 
 using namespace ddg;
@@ -454,6 +455,147 @@ int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *c
         return st1;
     }
     return st0;
+}
+
+struct ddg_forward_graph {
+    ddg_party *p0 = nullptr, *p1 = nullptr;
+    int batch = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    void *d_out = nullptr;          // party 0's revealed output, written by every replay
+    uint64_t launches = 0;          // kernels of one replay
+};
+
+int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
+                             ddg_forward_graph **out)
+{
+    DDG_CHECK(p0 && p1 && in0 && in1 && out && batch > 0, DDG_ERR_ARG, "bad argument");
+    *out = nullptr;
+    DDG_CHECK(p0->P.device == p1->P.device && p0->P.chan && p0->P.chan == p1->P.chan &&
+                  dynamic_cast<LocalPairChannel *>(p0->P.chan),
+              DDG_ERR_STATE, "a forward graph needs an in-process pair on one device (ddg_pair_local)");
+    for (ddg_party *p : {p0, p1})
+        DDG_CHECK(p->P.keys && p->P.key_bytes >= forward_key_bytes(p->P.bw, p->P.s, batch), DDG_ERR_KEY,
+                  "party %d: bound key region smaller than one forward of batch %d", p->P.party, batch);
+    DDG_CUDA(cudaSetDevice(p0->P.device));
+    auto *g = new ddg_forward_graph;
+    g->p0 = p0, g->p1 = p1, g->batch = batch;
+    auto fail = [&](int st) {
+        if (g->d_out) cudaFree(g->d_out);
+        delete g;
+        return st;
+    };
+    if (cudaMalloc(&g->d_out, size_t(batch) * (p0->P.bw / 8)) != cudaSuccess) {
+        set_last_error("cudaMalloc(forward graph output) failed");
+        return fail(DDG_ERR_CUDA);
+    }
+    cudaEvent_t fork = nullptr, join = nullptr;
+    cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
+    const uint64_t n0 = launch_count();
+    int st = DDG_OK;
+    cudaError_t ce = cudaStreamBeginCapture(p0->P.stream, cudaStreamCaptureModeRelaxed);
+    if (ce != cudaSuccess) {
+        set_last_error("cudaStreamBeginCapture: %s", cudaGetErrorString(ce));
+        st = DDG_ERR_CUDA;
+    }
+    bool capturing = st == DDG_OK;
+    if (st == DDG_OK) {
+        // party 1's stream joins the capture through an event of party 0's stream
+        if (cudaEventRecord(fork, p0->P.stream) != cudaSuccess ||
+            cudaStreamWaitEvent(p1->P.stream, fork, 0) != cudaSuccess) {
+            set_last_error("forward graph: fork of party 1's stream failed");
+            st = DDG_ERR_CUDA;
+        }
+    }
+    if (st == DDG_OK) {
+        int st1 = DDG_OK;
+        std::string err1;
+        std::thread t([&] {
+            st1 = forward_capture(p1->P, batch, in1[0], in1[1], in1[2], in1[3], nullptr);
+            if (st1 != DDG_OK) err1 = ddg::last_error();
+        });
+        st = forward_capture(p0->P, batch, in0[0], in0[1], in0[2], in0[3], g->d_out);
+        if (st != DDG_OK) {
+            if (auto *lp = dynamic_cast<LocalPairChannel *>(p0->P.chan)) lp->fail();
+        }
+        t.join();
+        if (st == DDG_OK && st1 != DDG_OK) {
+            set_last_error("party 1: %s", err1.c_str());
+            st = st1;
+        }
+        // party 1's last work joins back into party 0's stream before the capture ends
+        if (cudaEventRecord(join, p1->P.stream) != cudaSuccess ||
+            cudaStreamWaitEvent(p0->P.stream, join, 0) != cudaSuccess) {
+            if (st == DDG_OK) set_last_error("forward graph: join of party 1's stream failed");
+            if (st == DDG_OK) st = DDG_ERR_CUDA;
+        }
+    }
+    if (capturing) {
+        ce = cudaStreamEndCapture(p0->P.stream, &g->graph);
+        if (st == DDG_OK && ce != cudaSuccess) {
+            set_last_error("cudaStreamEndCapture: %s", cudaGetErrorString(ce));
+            st = DDG_ERR_CUDA;
+        }
+    }
+    g->launches = launch_count() - n0;
+    if (st == DDG_OK) {
+        ce = cudaGraphInstantiate(&g->exec, g->graph, 0);
+        if (ce != cudaSuccess) {
+            set_last_error("cudaGraphInstantiate: %s", cudaGetErrorString(ce));
+            st = DDG_ERR_CUDA;
+        }
+    }
+    cudaEventDestroy(fork);
+    cudaEventDestroy(join);
+    cudaGetLastError();  // a failed capture leaves its error here; the status carries it
+    if (st != DDG_OK) {
+        if (g->exec) cudaGraphExecDestroy(g->exec);
+        if (g->graph) cudaGraphDestroy(g->graph);
+        return fail(st);
+    }
+    *out = g;
+    return DDG_OK;
+}
+
+int ddg_forward_graph_launch(ddg_forward_graph *g, int64_t *h_out_raw, double *h_affinity)
+{
+    DDG_CHECK(g && g->exec, DDG_ERR_ARG, "null forward graph");
+    Party &P = g->p0->P;
+    DDG_CUDA(cudaSetDevice(P.device));
+    DDG_CUDA(cudaGraphLaunch(g->exec, P.stream));
+    add_launches(g->launches);
+    cudaError_t ce = cudaStreamSynchronize(P.stream);
+    DDG_CHECK(ce == cudaSuccess, DDG_ERR_CUDA, "forward graph: %s", cudaGetErrorString(ce));
+    DDG_TRY(ring_gemm_tc_check(P.stream));
+    if (!h_out_raw && !h_affinity) return DDG_OK;
+    const int B = g->batch;
+    std::vector<int64_t> v(B);
+    if (P.bw == 32) {
+        std::vector<int32_t> h(B);
+        DDG_CUDA(cudaMemcpy(h.data(), g->d_out, B * sizeof(int32_t), cudaMemcpyDeviceToHost));
+        for (int i = 0; i < B; i++) v[i] = h[i];
+    } else {
+        DDG_CUDA(cudaMemcpy(v.data(), g->d_out, B * sizeof(int64_t), cudaMemcpyDeviceToHost));
+    }
+    for (int i = 0; i < B; i++) {
+        if (h_out_raw) h_out_raw[i] = v[i];
+        // AFFINITY = int32(value) / 2^s (deepdtagen_inference.cu:594-606)
+        if (h_affinity) h_affinity[i] = double(int32_t(uint32_t(uint64_t(v[i])))) / double(1ull << P.s);
+    }
+    return DDG_OK;
+}
+
+int ddg_forward_graph_destroy(ddg_forward_graph *g)
+{
+    if (!g) return DDG_OK;
+    cudaSetDevice(g->p0->P.device);
+    cudaStreamSynchronize(g->p0->P.stream);
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    if (g->d_out) cudaFree(g->d_out);
+    delete g;
+    return DDG_OK;
 }
 
 int ddg_party_enable_dcf_timing(ddg_party *h, int on)

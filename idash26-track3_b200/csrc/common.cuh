@@ -44,6 +44,11 @@ void set_last_error(const char *fmt, ...);
 // number of kernels this library launched (all devices, all threads)
 void note_launch();
 uint64_t launch_count();
+// a replayed CUDA graph runs kernels that were counted when it was captured
+void add_launches(uint64_t n);
+// record a timing event on st: an ordinary record, or, while st is being
+// captured into a CUDA graph, an event-record node that records at every replay
+int record_timing_event(cudaEvent_t e, cudaStream_t st);
 
 // Optional timing of the comparison kernels (DCF gate round 1; OT garble and
 // AND-tree levels): when a thread has a sink installed, every such launch is

@@ -760,9 +760,12 @@ int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uin
                     : dealer_t<uint64_t>(bw, s, B, seed, w, k0, k1, st);
 }
 
+// capture: the stream is being captured into a CUDA graph (forward_capture):
+// the output goes to the device buffer capture_out (when not null) instead of
+// the host, and nothing waits for the device
 template <typename T>
 static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
-                  bool on_host, int64_t *h_out_raw, double *h_aff)
+                  bool on_host, int64_t *h_out_raw, double *h_aff, bool capture = false, void *capture_out = nullptr)
 {
     EvalExec<T> e;
     e.B = B, e.bw = P.bw, e.s = P.s, e.st = P.stream, e.P = &P, e.p = P.party;
@@ -791,20 +794,33 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         // one reference event per timing session: every timed launch of every
         // forward since enabling is read against it
         if (!P.ref_event) DDG_CUDA(cudaEventCreate(&P.ref_event));
-        if (!P.ref_live) DDG_CUDA(cudaEventRecord(P.ref_event, P.stream));
+        if (!P.ref_live) DDG_TRY(record_timing_event(P.ref_event, P.stream));
         P.ref_live = true;
         set_dcf_timing_sink(&P.timing);
     }
     affinity_graph<T>(e);
     set_dcf_timing_sink(nullptr);
     std::vector<T> h(B);
-    if (e.err == DDG_OK)
+    if (e.err == DDG_OK && !capture)
         e.ok(cudaMemcpyAsync(h.data(), e.out, B * sizeof(T), cudaMemcpyDeviceToHost, P.stream) == cudaSuccess
+                 ? DDG_OK : DDG_ERR_CUDA);
+    if (e.err == DDG_OK && capture && capture_out)
+        e.ok(cudaMemcpyAsync(capture_out, e.out, B * sizeof(T), cudaMemcpyDeviceToDevice, P.stream) == cudaSuccess
                  ? DDG_OK : DDG_ERR_CUDA);
     // the peer may still read buffers this party allocated: join before freeing
     int bs = P.chan->barrier(P.party, P.stream);
     if (e.err == DDG_OK) e.err = bs;
     e.free_all();
+    if (capture) {
+        if (e.err != DDG_OK) {
+            if (auto *lp = dynamic_cast<LocalPairChannel *>(P.chan)) lp->fail();
+            return e.err;
+        }
+        P.stats.bytes_sent = P.chan->bytes_sent[P.party] - sent0;
+        P.stats.rounds = P.chan->rounds[P.party] - rounds0;
+        P.stats.key_bytes_used = e.off;
+        return DDG_OK;
+    }
     cudaError_t ce = cudaStreamSynchronize(P.stream);
     if (e.err == DDG_OK && ce != cudaSuccess) {
         set_last_error("forward: %s", cudaGetErrorString(ce));
@@ -912,6 +928,17 @@ int parties_dcf_union(Party *const *ps, int n)
     }
     ps[0]->dcf.pair_union_ms = union_ms(all);
     return DDG_OK;
+}
+
+int forward_capture(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
+                    void *d_out)
+{
+    DDG_CHECK(P.chan, DDG_ERR_STATE, "party %d has no channel", P.party);
+    DDG_CHECK(P.keys, DDG_ERR_STATE, "party %d has no keys bound", P.party);
+    DDG_CHECK(P.w.table, DDG_ERR_STATE, "party %d has no weights", P.party);
+    DDG_CUDA(cudaSetDevice(P.device));
+    return P.bw == 32 ? eval_t<uint32_t>(P, B, x_sh, adj_sh, mask_sh, prot_sh, false, nullptr, nullptr, true, d_out)
+                      : eval_t<uint64_t>(P, B, x_sh, adj_sh, mask_sh, prot_sh, false, nullptr, nullptr, true, d_out);
 }
 
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,

@@ -80,6 +80,11 @@ int reset_timing(Party &P, bool on);
 int parties_dcf_union(Party *const *ps, int n);
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
                  bool on_host, int64_t *h_out_raw, double *h_aff);
+// enqueue one forward of device-resident inputs on P.stream while it is being
+// captured into a CUDA graph: the revealed output (party 0) goes to d_out, and
+// nothing waits for the device (the caller ends the capture and replays it)
+int forward_capture(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
+                    void *d_out);
 int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uint8_t *k0, uint8_t *k1,
                    cudaStream_t st);
 

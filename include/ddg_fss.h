@@ -252,6 +252,24 @@ int ddg_forward_eval(ddg_party *party, int batch, const void *x_share, const voi
  * in0/in1 = {x, adj, mask, protein} share pointers of party 0 / party 1 */
 int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
                           int on_host, int64_t *h_out_raw, double *h_affinity);
+/* The same pair forward captured once into a CUDA graph and replayed (no
+ * counterpart in the reference, whose forward is a host loop of per-layer
+ * calls): ddg_forward_graph_create records both parties' launches, openings
+ * and allocations of one forward of device-resident inputs in0/in1 (the
+ * same pointers at every replay, the same key region: a replay re-reads the
+ * keys, as the reference's benchmark loop rewinds keyBuf) without running
+ * it; ddg_forward_graph_launch replays it on party 0's stream, waits for it
+ * and returns the revealed output like ddg_forward_eval_pair.  Make one
+ * ordinary ddg_forward_eval_pair of the pair first (one-time set-up of the
+ * kernels and tables happens there, not inside a capture).  With DCF timing
+ * enabled on the parties when the graph is created, every replay re-records
+ * the timed launches' events: ddg_parties_dcf_union / ddg_party_dcf_timing
+ * then describe the last replay.  Destroy the graph before its parties. */
+typedef struct ddg_forward_graph ddg_forward_graph;
+int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
+                             ddg_forward_graph **out);
+int ddg_forward_graph_launch(ddg_forward_graph *graph, int64_t *h_out_raw, double *h_affinity);
+int ddg_forward_graph_destroy(ddg_forward_graph *graph);
 /* GPU dealer (replaces DDGOrcaKeygenBatched + ddgSecureAdjNormKeygen,
  * deepdtagen_inference.cu:283-342): both parties' keys of one forward, fresh
  * masks from `seed`, into d_key0 / d_key1 (ddg_forward_key_bytes each) */

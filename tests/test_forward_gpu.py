@@ -143,6 +143,44 @@ def test_forward_comparison_timing(ddg, synth, cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("bw", [32, 64])
+def test_forward_cuda_graph_replays_bit_exact(ddg, synth, cuda, bw):
+    """The pair forward captured into a CUDA graph and replayed twice gives the
+    ordinary forward's outputs bit for bit; each replay counts its kernels, and
+    the comparison-kernel timing sees the launches of one replay."""
+    B = 3
+    inp = synth.Inputs(B, bw, seed=31, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=77)
+    ins, keep = dev_inputs(inp)
+    raw0, aff0 = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    want_raw, want_aff = expected(inp, q, bw)
+    assert np.array_equal(raw0, RF.Ring(bw).signed(want_raw))
+    n_plain = ddg.launch_count()
+    ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    n_plain = ddg.launch_count() - n_plain
+    for p in (p0, p1):
+        p.enable_dcf_timing(True)
+    g = ddg.ForwardGraph(p0, p1, B, ins[0], ins[1])
+    try:
+        for _ in range(2):
+            n = ddg.launch_count()
+            raw, aff = g.launch()
+            assert ddg.launch_count() - n == n_plain
+            assert np.array_equal(raw, raw0) and np.array_equal(aff, aff0)
+        ddg.parties_dcf_union([p0, p1])
+        t = [p0.dcf_timing(), p1.dcf_timing()]
+        assert t[0]["launches"] == t[1]["launches"] > 0
+        assert 0 < t[0]["pair_union_ms"] <= t[0]["union_ms"] + t[1]["union_ms"] + 1e-6
+    finally:
+        g.close()
+        for p in (p0, p1):
+            p.enable_dcf_timing(False)
+    # the parties still run ordinary forwards afterwards
+    raw2, aff2 = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    assert np.array_equal(raw2, raw0)
+
+
+@pytest.mark.gpu
 def test_forward_edge_graphs(ddg, synth, cuda):
     """kiba-shaped graphs (up to 100 atoms), a 138-atom graph, and an all-zero
     padding sample (degree 0 -> table[0] = 0; deepdtagen_inference.cu:72-79)."""
