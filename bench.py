@@ -523,9 +523,22 @@ def main():
     if colo and uses_graph(a):
         # capture after the warm-up forwards (one-time set-up done), with the
         # comparison-kernel timing on, so that every replay records its launches
-        graph[0] = ddg.ForwardGraph(parties[0], parties[1], B, [t.data_ptr() for t in bufs[0][0]],
-                                    [t.data_ptr() for t in bufs[1][0]])
-        graph[0].launch(outputs=False)  # untimed: the first replay uploads the graph
+        try:
+            graph[0] = ddg.ForwardGraph(parties[0], parties[1], B, [t.data_ptr() for t in bufs[0][0]],
+                                        [t.data_ptr() for t in bufs[1][0]])
+            graph[0].launch(outputs=False)  # untimed: the first replay uploads the graph
+        except Exception as ex:  # noqa: BLE001 -- any capture failure falls back to host launches
+            # a failed capture may leave the pair's channel marked failed: pair the
+            # parties again and launch from the host, and say so in config.launch
+            print(f"bench: CUDA-graph capture failed ({ex}); timing host launches instead", file=sys.stderr)
+            if graph[0] is not None:
+                graph[0].close()
+            graph[0] = None
+            a.graph = "off"
+            ddg.pair_local(parties[0], parties[1])
+            step(False)
+            for p in parties:
+                p.enable_dcf_timing(True)
     n0 = ddg.launch_count()
     tw = [0.0, 0.0]
     ms = timed(False, a.steps, tw)
