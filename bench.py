@@ -19,13 +19,19 @@ value    : samples/s of the whole job, inputs (shares) and keys already in HBM.
 e2e      : the same through the C ABI with host (pinned) share buffers: every
            step copies both parties' input shares host->device and the
            revealed affinities device->host.
-roofline : the DCF kernel (gate round 1), algorithmic bytes (key bytes +
-           input + output bits) over the union of its launch intervals,
-           measured with CUDA events on the party streams during the timed
-           region, against the measured HBM copy bandwidth.
+roofline : the comparison kernels of the selected backend (default: the
+           truth-table gates' ot_level_kernel), their algorithmic bytes (key
+           bytes, inputs, state and openings) over the union of their launch
+           intervals, measured with CUDA events on the party streams during
+           the timed region, against the measured HBM copy bandwidth; plus
+           e2e_key_frac, both parties' key bytes per step over the step time.
 cpu_baseline / --impl reference : the reference's own CPU LSS ReLU backend
            (gpu_mpc/lss, compiled by oracle/Makefile into oracle/_ref) over
            loopback, plus the plaintext integer forward of the same graph.
+parity   : (N = 1, with the CPU baseline) the revealed outputs of the
+           warm-up forward, of the CUDA-graph replay and of the e2e forward
+           against the plaintext integer forward of the same inputs, weights
+           and graph, all B samples, bit for bit; the run fails on a mismatch.
 """
 from __future__ import annotations
 
@@ -65,10 +71,14 @@ NMAX, FEAT, POOL, PROT = 138, 94, 376, 128
 RELUS_PER_SAMPLE = 171_076           # 138*(188+282+376) + 376*137 + 2816
 A10_SAMPLES_PER_S = 16 / 0.136       # reference README.md:99-101, A10, B=16, bw=32
 
-# DRAM bytes (read + write) per algorithmic byte of the round-1 DCF kernel,
-# from an ncu capture (profiles/gate_round1_dcf_relu_ars_split_b16.md: 300.0 MB
-# of DRAM traffic for 295.9 MB of algorithmic bytes in one launch).
-NCU_DRAM_BYTES_PER_ALG_BYTE = 300.0 / 295.9
+# DRAM bytes (read + write) per algorithmic byte of each backend's comparison
+# kernel, from ncu captures (dram__bytes_read.sum + dram__bytes_write.sum over
+# the kernel's algorithmic bytes):
+#   tt : ot_level_kernel, AND-tree levels 2 and 3 of the full-compare ReLU gate
+#        at 2^23 elements: 148.2 MB of DRAM traffic for 201.3 MB of
+#        algorithmic bytes per launch (its writes stay in L2 when it ends);
+#   dcf: gate_round1_kernel, three-part ReLU(ARS) at B=16: 300.0 MB for 295.9 MB.
+NCU_DRAM_BYTES_PER_ALG_BYTE = {"tt": 148.2 / 201.3, "dcf": 300.0 / 295.9, "ot": None}
 
 
 def parse():
@@ -271,8 +281,48 @@ class Clocks:
 
 # ------------------------------------------------------------------ CPU baseline
 
-def cpu_baseline(bw, relu_n=8_000_000, fwd_samples=2):
-    """Reference LSS ReLU over loopback (all host cores) + plaintext integer forward."""
+def physical_cores():
+    """Physical cores of this host (distinct (core, socket) pairs of lscpu -p),
+    or None when lscpu is unavailable."""
+    try:
+        out = subprocess.run(["lscpu", "-p=core,socket"], capture_output=True, text=True, timeout=10).stdout
+        pairs = {ln.strip() for ln in out.splitlines() if ln and not ln.startswith("#")}
+        return len(pairs) or None
+    except Exception:
+        return None
+
+
+def check_outputs(bw, inp, q, outs):
+    """Parity of the GPU's revealed outputs: the plaintext integer forward of
+    the same graph (oracle/ring_forward.py protocol_forward, the function the
+    two-party forward must reproduce bit for bit) on all samples of the
+    bench's inputs.  outs: {name: (raw, affinity)} of forwards of those inputs.
+    Returns (seconds per sample of the plaintext forward, parity record)."""
+    import numpy as np
+
+    from oracle import ring_forward as RF
+
+    B = inp.x_ring.shape[0]
+    t0 = time.perf_counter()
+    want_raw, want_aff = RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, 12)
+    fwd_s = (time.perf_counter() - t0) / B
+    want = RF.Ring(bw).signed(want_raw)
+    rec = {"oracle": "plaintext integer forward of the same graph, inputs and weights (protocol_forward)",
+           "samples": int(B)}
+    ok = True
+    for name, (raw, aff) in outs.items():
+        bad = int(np.count_nonzero(np.asarray(raw) != want)) + int(np.count_nonzero(np.asarray(aff) != want_aff))
+        rec[name] = "bit-exact" if bad == 0 else f"MISMATCH: {bad} values differ"
+        ok = ok and bad == 0
+    rec["result"] = "bit-exact" if ok else "MISMATCH"
+    return fwd_s, rec
+
+
+def cpu_baseline(bw, relu_n=8_000_000, fwd_samples=2, check=None):
+    """Reference LSS ReLU over loopback (all host cores) + plaintext integer
+    forward.  With check = (inputs, quantised weights, {name: GPU outputs}) the
+    plaintext forward runs on the bench's own B samples and doubles as the
+    parity check of the GPU outputs."""
     cores = os.cpu_count() or 2
     exe = os.path.join(REPO, "oracle", "_ref", "lss_bench")
     kind, relu_s_per_sample, detail = "port", None, {}
@@ -284,22 +334,40 @@ def cpu_baseline(bw, relu_n=8_000_000, fwd_samples=2):
             kind = "reference"
             relu_s_per_sample = d["seconds"] * RELUS_PER_SAMPLE / relu_n
             detail = d
-    from oracle import ring_forward as RF
+    parity = None
+    if check is not None:
+        inp, q, outs = check
+        fwd_samples = int(inp.x_ring.shape[0])
+        fwd_s, parity = check_outputs(bw, inp, q, outs)
+    else:
+        from oracle import ring_forward as RF
 
-    synth = importlib.import_module("idash26-track3_b200.synth")
-    inp = synth.Inputs(fwd_samples, bw, seed=3, with_protein_cnn=False)
-    q = synth.quantize_weights(synth.affinity_weights(5), 12)
-    t0 = time.perf_counter()
-    RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, 12)
-    fwd_s = (time.perf_counter() - t0) / fwd_samples
+        synth = importlib.import_module("idash26-track3_b200.synth")
+        inp = synth.Inputs(fwd_samples, bw, seed=3, with_protein_cnn=False)
+        q = synth.quantize_weights(synth.affinity_weights(5), 12)
+        t0 = time.perf_counter()
+        RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, 12)
+        fwd_s = (time.perf_counter() - t0) / fwd_samples
     per_sample = fwd_s + (relu_s_per_sample or 0.0)
     sample = (f"reference LSS ReLU (gpu_mpc/lss compiled unmodified, 2 processes over loopback TCP, "
-              f"{max(cores // 2, 1)} OpenMP threads each) on {relu_n} elements at bw={bw}, scaled to "
-              f"{RELUS_PER_SAMPLE} ReLUs/sample; plus the plaintext integer forward (numpy, oracle/ring_forward.py) "
-              f"of {fwd_samples} samples for the linear layers" if kind == "reference" else
+              f"{max(cores // 2, 1)} OpenMP threads each) timed on {relu_n} elements at bw={bw} and extrapolated "
+              f"linearly to the {RELUS_PER_SAMPLE} ReLUs of a sample; plus the plaintext integer forward "
+              f"(numpy, oracle/ring_forward.py, one thread) timed on {fwd_samples} samples for the linear layers"
+              if kind == "reference" else
               f"plaintext integer forward only (oracle/ring_forward.py, {fwd_samples} samples); LSS binary absent")
-    return {"value": 1.0 / per_sample, "unit": "samples/s", "cores": cores, "kind": kind, "sample": sample,
-            "relu_s_per_sample": relu_s_per_sample, "linear_s_per_sample": fwd_s, "lss": detail}
+    out = {"value": 1.0 / per_sample, "unit": "samples/s", "cores": cores, "physical_cores": physical_cores(),
+           "kind": kind, "sample": sample, "relu_s_per_sample": relu_s_per_sample,
+           "relu_extrapolated_from_elements": relu_n if kind == "reference" else None,
+           "linear_s_per_sample": fwd_s, "lss": detail}
+    if parity is not None:
+        out["parity"] = parity
+    return out
+
+
+def np_equal(a, b):
+    import numpy as np
+
+    return all(np.array_equal(np.asarray(x), np.asarray(y)) for x, y in zip(a, b))
 
 
 def run_reference(a, rank, world):
@@ -515,8 +583,12 @@ def main():
     clocks = Clocks(range(world) if world > 1 else [local])
     if rank == 0:
         clocks.start()
+    outs = {}  # revealed outputs of untimed forwards of the timed inputs (colocated, resident keys)
+    o = None
     for _ in range(a.warmup):
-        step(False)
+        o = step(False)
+    if colo and not streams and o is not None:
+        outs["warmup_forward"] = o
     ks_before = [ks.stats() for ks in streams]
     for p in parties:
         p.enable_dcf_timing(True)
@@ -526,7 +598,7 @@ def main():
         try:
             graph[0] = ddg.ForwardGraph(parties[0], parties[1], B, [t.data_ptr() for t in bufs[0][0]],
                                         [t.data_ptr() for t in bufs[1][0]])
-            graph[0].launch(outputs=False)  # untimed: the first replay uploads the graph
+            outs["graph_replay"] = graph[0].launch()  # untimed: the first replay uploads the graph
         except Exception as ex:  # noqa: BLE001 -- any capture failure falls back to host launches
             # a failed capture may leave the pair's channel marked failed: pair the
             # parties again and launch from the host, and say so in config.launch
@@ -574,7 +646,9 @@ def main():
 
     e2e = None
     if not a.no_e2e:
-        step(True)
+        o = step(True)
+        if colo and not streams:
+            outs["e2e_forward"] = o
         ms_e2e = timed(True, a.steps)
         # both parties' input shares of every pair cross host->device each step
         own = [sum(int(t.numel()) for t in b[1]) for b in bufs]
@@ -596,9 +670,18 @@ def main():
         aes = sum(d["aes_blocks"] for d in dcf)
         nl = sum(d["launches"] for d in dcf)
     achieved = alg / (union / 1e3) / 1e9 if union > 0 else 0.0
+    ratio = NCU_DRAM_BYTES_PER_ALG_BYTE.get(a.relu_backend)
+    # both parties' key regions stream from HBM once per step (colocated: on this GPU)
+    key_bytes_per_gpu_step = (2 if colo else 1) * kb
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": peak_kind,
-                "traffic": (alg / nl * NCU_DRAM_BYTES_PER_ALG_BYTE) if (nl and NCU_DRAM_BYTES_PER_ALG_BYTE) else None,
+                "traffic": (alg / nl * ratio) if (nl and ratio) else None,
+                "traffic_note": "DRAM bytes per launch = algorithmic bytes per launch x the DRAM/algorithmic "
+                                "ratio of an ncu capture of the same kernel",
+                "e2e_key_frac": key_bytes_per_gpu_step / (ms / a.steps / 1e3) / 1e9 / peak,
+                "e2e_key_note": "key bytes of both parties of a pair streamed per step on one GPU, over the "
+                                "step time, against the measured HBM copy bandwidth (the key-bytes-over-HBM "
+                                "roofline of the whole forward)",
                 "kernel": {"tt": "comparison kernels: ot_level_kernel (truth tables + AND-tree levels of the "
                                  "ReLU and truncation gates)",
                            "ot": "comparison kernels: ot_garble_kernel + ot_level_kernel (ReLU gates) and "
@@ -621,8 +704,19 @@ def main():
     roofline["aes_frac"] = roofline["aes_gblocks_per_s"] / aes_peak if aes_peak else None
 
     cb = None
+    parity = None
+    # the GPU outputs agree among themselves (graph replay, host launches, host buffers)
+    names = list(outs)
+    same = all(np_equal(outs[n], outs[names[0]]) for n in names[1:]) if names else None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cb = cpu_baseline(bw)
+        q = synth.quantize_weights(synth.affinity_weights(5), s)
+        cb = cpu_baseline(bw, check=(inp, q, outs) if outs else None)
+        parity = cb.pop("parity", None)
+    if parity is None:
+        parity = {"result": "not checked against the oracle (N > 1, streaming or --no-cpu-baseline)",
+                  "gpu_paths_agree": same}
+    else:
+        parity["gpu_paths_agree"] = same
     if rank == 0:
         line = {"metric": "online 2PC samples/sec (full affinity branch)", "value": value, "unit": "samples/s",
                 "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
@@ -634,8 +728,10 @@ def main():
                          "bytes_per_sample": 2 * stats["bytes_sent"] / B,
                          # emulated LAN, full duplex: each party's bytes at 1 Gbps + one 1 ms RTT per opening
                          "lan_1gbps_1ms_rtt_s_per_step": stats["bytes_sent"] * 8 / 1e9 + stats["rounds"] * 1e-3},
-                "key_bytes_per_party_per_step": kb, "stream": stream_info}
+                "key_bytes_per_party_per_step": kb, "stream": stream_info, "parity": parity}
         emit(line)
+        if parity.get("result") == "MISMATCH" or same is False:
+            raise SystemExit("bench: the GPU forward's outputs do not match (see parity in the JSON line)")
     for ks in streams:
         ks.close()
     for p in parties:

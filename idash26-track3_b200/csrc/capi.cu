@@ -1,4 +1,5 @@
 // extern "C" entry points of libddg.so (declared in include/ddg_fss.h).
+#include <algorithm>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -464,7 +465,22 @@ struct ddg_forward_graph {
     cudaGraphExec_t exec = nullptr;
     void *d_out = nullptr;          // party 0's revealed output, written by every replay
     uint64_t launches = 0;          // kernels of one replay
+    // comparison-launch timing records captured into the graph, per party:
+    // their events are the graph's (taken out of the party's pool), and every
+    // replay re-records them
+    std::vector<DcfTiming::Rec> recs[2];
 };
+
+// after a capture: the timing events the capture took from a party's pool
+// belong to the graph from now on (the pool hands out pool[0..used) in order,
+// and the pool was settled before the capture)
+static void adopt_timing(Party &P, std::vector<DcfTiming::Rec> &dst)
+{
+    DcfTiming &t = P.timing;
+    dst = t.recs;
+    t.pool.erase(t.pool.begin(), t.pool.begin() + std::min(t.used, t.pool.size()));
+    t.recs.clear(), t.used = 0;
+}
 
 int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
                              ddg_forward_graph **out)
@@ -478,6 +494,10 @@ int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void
         DDG_CHECK(p->P.keys && p->P.key_bytes >= forward_key_bytes(p->P.bw, p->P.s, batch), DDG_ERR_KEY,
                   "party %d: bound key region smaller than one forward of batch %d", p->P.party, batch);
     DDG_CUDA(cudaSetDevice(p0->P.device));
+    for (ddg_party *p : {p0, p1}) {
+        DDG_CHECK(!p->P.graph_recs, DDG_ERR_STATE, "party %d already has a forward graph", p->P.party);
+        DDG_TRY(settle_timing(p->P));  // pending host-forward launches are read back first
+    }
     auto *g = new ddg_forward_graph;
     g->p0 = p0, g->p1 = p1, g->batch = batch;
     auto fail = [&](int st) {
@@ -552,7 +572,16 @@ int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void
     if (st != DDG_OK) {
         if (g->exec) cudaGraphExecDestroy(g->exec);
         if (g->graph) cudaGraphDestroy(g->graph);
+        for (ddg_party *p : {p0, p1}) p->P.timing.recs.clear(), p->P.timing.used = 0;  // events back to the pool
         return fail(st);
+    }
+    ddg_party *ps[2] = {p0, p1};
+    for (int i = 0; i < 2; i++) {
+        Party &P = ps[i]->P;
+        if (!P.timing.enabled) continue;
+        adopt_timing(P, g->recs[i]);
+        P.graph_recs = &g->recs[i];
+        P.graph_fresh = false;
     }
     *out = g;
     return DDG_OK;
@@ -563,10 +592,23 @@ int ddg_forward_graph_launch(ddg_forward_graph *g, int64_t *h_out_raw, double *h
     DDG_CHECK(g && g->exec, DDG_ERR_ARG, "null forward graph");
     Party &P = g->p0->P;
     DDG_CUDA(cudaSetDevice(P.device));
+    ddg_party *ps[2] = {g->p0, g->p1};
+    for (int i = 0; i < 2; i++) {
+        // the timed launches of a replay are read against the party's reference
+        // event: record it before the first replay of a timing session (both
+        // parties share the device, so party 0's stream serves for both)
+        Party &Q = ps[i]->P;
+        if (!Q.timing.enabled || Q.graph_recs != &g->recs[i] || Q.ref_live) continue;
+        if (!Q.ref_event) DDG_CUDA(cudaEventCreate(&Q.ref_event));
+        DDG_CUDA(cudaEventRecord(Q.ref_event, P.stream));
+        Q.ref_live = true;
+    }
     DDG_CUDA(cudaGraphLaunch(g->exec, P.stream));
     add_launches(g->launches);
     cudaError_t ce = cudaStreamSynchronize(P.stream);
     DDG_CHECK(ce == cudaSuccess, DDG_ERR_CUDA, "forward graph: %s", cudaGetErrorString(ce));
+    for (int i = 0; i < 2; i++)
+        if (ps[i]->P.graph_recs == &g->recs[i]) ps[i]->P.graph_fresh = true;
     DDG_TRY(ring_gemm_tc_check(P.stream));
     if (!h_out_raw && !h_affinity) return DDG_OK;
     const int B = g->batch;
@@ -594,6 +636,12 @@ int ddg_forward_graph_destroy(ddg_forward_graph *g)
     if (g->exec) cudaGraphExecDestroy(g->exec);
     if (g->graph) cudaGraphDestroy(g->graph);
     if (g->d_out) cudaFree(g->d_out);
+    ddg_party *ps[2] = {g->p0, g->p1};
+    for (int i = 0; i < 2; i++) {
+        Party &P = ps[i]->P;
+        if (P.graph_recs == &g->recs[i]) P.graph_recs = nullptr, P.graph_fresh = false;
+        for (const auto &r : g->recs[i]) cudaEventDestroy(r.a), cudaEventDestroy(r.b);
+    }
     delete g;
     return DDG_OK;
 }

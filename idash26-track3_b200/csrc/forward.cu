@@ -792,10 +792,14 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
     const uint64_t sent0 = P.chan->bytes_sent[P.party], rounds0 = P.chan->rounds[P.party];
     if (P.timing.enabled) {
         // one reference event per timing session: every timed launch of every
-        // forward since enabling is read against it
+        // forward since enabling is read against it.  A capture does not record
+        // it (a replay would move it); ddg_forward_graph_launch records it
+        // before the first replay of a session instead.
         if (!P.ref_event) DDG_CUDA(cudaEventCreate(&P.ref_event));
-        if (!P.ref_live) DDG_TRY(record_timing_event(P.ref_event, P.stream));
-        P.ref_live = true;
+        if (!P.ref_live && !capture) {
+            DDG_TRY(record_timing_event(P.ref_event, P.stream));
+            P.ref_live = true;
+        }
         set_dcf_timing_sink(&P.timing);
     }
     affinity_graph<T>(e);
@@ -871,13 +875,9 @@ double union_ms(std::vector<std::pair<double, double>> v)
 // read back the party's pending timed launches (their forwards have finished:
 // the forward drains its stream before returning) into its intervals and
 // totals, and hand their events back to the pool
-int settle_timing(Party &P)
+static int settle_recs(Party &P, const std::vector<DcfTiming::Rec> &recs)
 {
-    DcfTiming &t = P.timing;
-    if (t.recs.empty()) return DDG_OK;
-    DDG_CHECK(P.ref_live, DDG_ERR_STATE, "timed launches without a reference event");
-    DDG_CUDA(cudaSetDevice(P.device));
-    for (const auto &r : t.recs) {
+    for (const auto &r : recs) {
         if (!r.done) continue;  // a launch that failed between its two events
         float a = 0, b = 0;
         DDG_CUDA(cudaEventElapsedTime(&a, P.ref_event, r.a));
@@ -885,7 +885,24 @@ int settle_timing(Party &P)
         P.intervals.emplace_back(double(a), double(b));
         P.dcf.launches += 1, P.dcf.bytes += r.bytes, P.dcf.aes += r.aes, P.dcf.sum_ms += double(b - a);
     }
+    return DDG_OK;
+}
+
+// also adds the launches of the last replay of a CUDA graph that holds this
+// party's timed launches, once per replay that ran since the last read-back
+int settle_timing(Party &P)
+{
+    DcfTiming &t = P.timing;
+    const bool graph = P.timing.enabled && P.graph_recs && P.graph_fresh;
+    if (t.recs.empty() && !graph) return DDG_OK;
+    DDG_CHECK(P.ref_live, DDG_ERR_STATE, "timed launches without a reference event");
+    DDG_CUDA(cudaSetDevice(P.device));
+    DDG_TRY(settle_recs(P, t.recs));
     t.recs.clear(), t.used = 0;
+    if (graph) {
+        DDG_TRY(settle_recs(P, *P.graph_recs));
+        P.graph_fresh = false;
+    }
     // forwards of one party never overlap, so the union over the whole
     // session is the sum of the per-forward unions
     P.dcf.union_ms = union_ms(P.intervals);
@@ -899,6 +916,7 @@ int reset_timing(Party &P, bool on)
     P.dcf = DcfAcc();
     P.intervals.clear();
     P.ref_live = false;
+    P.graph_fresh = false;
     if (!on) return DDG_OK;
     // events for ~28 forwards' comparison launches up front; the pool grows on
     // demand beyond that, while the host is ahead of the device

@@ -59,6 +59,11 @@ struct Party {
     cudaEvent_t ref_event = nullptr;                     // start of the first forward since timing was enabled
     bool ref_live = false;                               // ref_event is recorded for this timing session
     std::vector<std::pair<double, double>> intervals;    // read-back comparison launches, ms after ref_event
+    // comparison launches captured into a CUDA graph (ddg_forward_graph): the
+    // graph owns these records' events and every replay re-records them;
+    // graph_fresh = a replay ran since they were last read back
+    const std::vector<DcfTiming::Rec> *graph_recs = nullptr;
+    bool graph_fresh = false;
     // device staging of host inputs (kept across forwards), copied on a side
     // stream; in_ev[0..3] mark each input's arrival, in_ev[4] the start of a forward
     void *in_buf[4] = {};

@@ -10,7 +10,8 @@
 // pipeline, and deployments whose device memory budget is fixed up front.
 //
 // Limits and sharing: at most DDG_NOALLOC_MAX_N elements per call.  Every
-// GPU that loads the library holds the array (4.25 MiB) until the process
+// GPU that loads the library holds the array (4,325,376 bytes = 4.125 MiB:
+// 4 x 8,192 bit words, then two shares of 262,144 64-bit words) until the process
 // exits.  All calls share it and it keeps the last call's contents; each call
 // overwrites every word it reads, so nothing needs clearing, but calls that
 // overlap on the GPU (different streams, or different host threads on one

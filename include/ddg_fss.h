@@ -173,7 +173,7 @@ int ddg_gate_round2(int kind, int bw, int scale, uint64_t n, int party, const vo
  * exchange + ddg_gate_round2 followed by adding the two shares: d_yhat[n] =
  * f(x) + r_out (masked-public), from d_xhat and both parties' keys.  The
  * round-1 bits and round-2 shares live in one file-scope device array of
- * 4.25 MiB held by every GPU that loads the library until exit; at most
+ * 4,325,376 bytes (4.125 MiB) held by every GPU that loads the library until exit; at most
  * DDG_NOALLOC_MAX_N elements per call, larger n is rejected with DDG_ERR_ARG.
  * Calls share that array: calls that overlap on the GPU race.  The first call
  * on a device looks up the array's address and uploads the AES tables; make
@@ -262,9 +262,12 @@ int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *c
  * and returns the revealed output like ddg_forward_eval_pair.  Make one
  * ordinary ddg_forward_eval_pair of the pair first (one-time set-up of the
  * kernels and tables happens there, not inside a capture).  With DCF timing
- * enabled on the parties when the graph is created, every replay re-records
- * the timed launches' events: ddg_parties_dcf_union / ddg_party_dcf_timing
- * then describe the last replay.  Destroy the graph before its parties. */
+ * enabled on the parties when the graph is created, the graph owns the
+ * events of the timed launches it captured and every replay re-records them;
+ * each ddg_parties_dcf_union / ddg_party_dcf_timing then adds the launches of
+ * the last replay (once, if a replay ran since the previous read-out) to the
+ * party's totals, beside those of its host-launched forwards.  One graph per
+ * party at a time; destroy the graph before its parties. */
 typedef struct ddg_forward_graph ddg_forward_graph;
 int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
                              ddg_forward_graph **out);

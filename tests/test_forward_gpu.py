@@ -216,3 +216,93 @@ def test_forward_rejects_short_key_region(ddg, synth, cuda):
     with pytest.raises(ddg.DdgError) as e:
         ddg.forward_pair(p0, p1, B, ins[0], ins[1])
     assert e.value.code == 3
+
+
+def _cfg_inputs(synth, bw, B, atoms, seed):
+    return synth.Inputs(B, bw, seed=seed, atoms=atoms, with_protein_cnn=False)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bw,B,atoms", [(32, 16, (10, 60)), (32, 256, (10, 60)), (64, 256, (10, 100))],
+                         ids=["pr1-bw32-B16", "bench-bw32-B256", "kiba-bw64-B256"])
+def test_forward_bit_exact_at_benched_configs(ddg, synth, cuda, bw, B, atoms):
+    """The forward at the sizes it is run and benchmarked at: the PR1 reference
+    case (bw=32, B=16, davis-shaped graphs), the bench workload (bw=32, B=256:
+    one party's key region is beyond 2^32 bytes and the largest gate covers
+    11 M elements on a full grid) and the kiba-shaped bw=64 workload at B=256.
+    Every revealed output equals protocol_forward bit for bit, on the host
+    launches and, at B=256, on a replay of the CUDA-graph capture too."""
+    inp = _cfg_inputs(synth, bw, B, atoms, seed=400 + B + bw)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=4000 + B + bw)
+    kb = ddg.forward_key_bytes(bw, S, B)
+    if B == 256:
+        assert kb > 2**32, kb  # 64-bit key offsets are exercised
+    ins, keep = dev_inputs(inp)
+    raw, aff = ddg.forward_pair(p0, p1, B, ins[0], ins[1])
+    want_raw, want_aff = expected(inp, q, bw)
+    want_signed = RF.Ring(bw).signed(want_raw)
+    bad = np.flatnonzero(raw != want_signed)
+    assert bad.size == 0, f"{bad.size} of {B} samples differ, first {bad[:8]}"
+    assert np.array_equal(aff, want_aff)
+    assert p0.stats()["key_bytes_used"] <= kb
+    if B == 256:
+        g = ddg.ForwardGraph(p0, p1, B, ins[0], ins[1])
+        try:
+            graw, gaff = g.launch()
+        finally:
+            g.close()
+        assert np.array_equal(graw, want_signed) and np.array_equal(gaff, want_aff)
+
+
+@pytest.mark.gpu
+def test_forward_graph_timing_readouts_follow_replays(ddg, synth, cuda):
+    """Comparison-kernel timing with a CUDA graph: every read-out adds the
+    launches of the replay that ran since the previous one (replay, read,
+    replay, read), a host-launched forward in between adds its own launches
+    with events of its own (the graph's events are not handed out again), and
+    the replays keep giving the oracle's outputs."""
+    bw, B = 32, 3
+    inp = synth.Inputs(B, bw, seed=41, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=78)
+    ins, keep = dev_inputs(inp)
+    want_raw, want_aff = expected(inp, q, bw)
+    ddg.forward_pair(p0, p1, B, ins[0], ins[1])  # one-time set-up outside the capture
+    for p in (p0, p1):
+        p.enable_dcf_timing(True)
+    g = ddg.ForwardGraph(p0, p1, B, ins[0], ins[1])
+    try:
+        seen = []
+
+        def read():
+            ddg.parties_dcf_union([p0, p1])
+            t = [p0.dcf_timing(), p1.dcf_timing()]
+            assert t[0]["launches"] == t[1]["launches"]
+            seen.append(t[0])
+
+        raw, aff = g.launch()
+        assert np.array_equal(aff, want_aff)
+        read()
+        n1 = seen[0]["launches"]
+        assert n1 > 0
+        read()  # no replay since: nothing added
+        assert seen[1]["launches"] == n1
+        g.launch()
+        read()
+        assert seen[2]["launches"] == 2 * n1
+        # the second replay ran after the first: its intervals extend the union
+        assert seen[2]["union_ms"] > 1.5 * seen[0]["union_ms"]
+        assert seen[2]["pair_union_ms"] > 1.5 * seen[0]["pair_union_ms"]
+        raw, aff = ddg.forward_pair(p0, p1, B, ins[0], ins[1])  # host launches with pool events
+        assert np.array_equal(aff, want_aff)
+        read()
+        assert seen[3]["launches"] == 3 * n1
+        assert seen[3]["union_ms"] > seen[2]["union_ms"]
+        raw, aff = g.launch()
+        assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)) and np.array_equal(aff, want_aff)
+        read()
+        assert seen[4]["launches"] == 4 * n1
+        assert seen[4]["union_ms"] > seen[3]["union_ms"]
+    finally:
+        g.close()
+        for p in (p0, p1):
+            p.enable_dcf_timing(False)

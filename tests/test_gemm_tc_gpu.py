@@ -135,9 +135,10 @@ def test_limb_sums_at_the_exactness_bound(engine, cuda, path, bw, K):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("bw", [32, 64])
-def test_tensor_cores_match_cuda_cores_at_layer_size(engine, cuda, bw):
-    """GCN layer 3 FC at B = 32 samples (M = 4416, K = 282, N = 376): tensor
-    cores and CUDA cores give identical bytes."""
+def test_fc_at_layer_size_matches_numpy(engine, cuda, bw):
+    """GCN layer 3 FC at B = 32 samples (M = 4416, K = 282, N = 376) on the
+    tensor cores and on the CUDA cores: each equals numpy's wrapping product
+    x_hat . W + bias2s + C0 (party 0 of DDGOrcaBase::matmul 4-arg) bit for bit."""
     import torch
 
     L = engine.lib()
@@ -146,13 +147,13 @@ def test_tensor_cores_match_cuda_cores_at_layer_size(engine, cuda, bw):
     rng = np.random.default_rng(bw)
     xh, W, c0 = rnd(rng, bw, (M, K)), rnd(rng, bw, (K, N)), rnd(rng, bw, (M, N))
     b2s = rnd(rng, bw, N)
+    want = (mm(xh, W, dt) + b2s[None, :] + c0).astype(dt).reshape(-1)
     bufs = [to_dev(a) for a in (xh, W, b2s, c0)]
-    outs = []
     for path in (0, 1):
         engine.gemm_path(path)
         out = dev_bytes(M * N * bw // 8)
         engine.check(L.ddg_fc_share(bw, 0, M, K, N, *[ptr(b) for b in bufs], ptr(out), None))
         torch.cuda.synchronize()
-        outs.append(from_dev(out, dt, M * N))
+        got = from_dev(out, dt, M * N)
+        assert np.array_equal(got, want), f"path {path}: {np.count_nonzero(got != want)} elements differ"
     engine.gemm_status()
-    assert np.array_equal(outs[0], outs[1])

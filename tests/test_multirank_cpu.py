@@ -5,7 +5,7 @@ layout (pair i = ranks (i, k+i)), broadcasting the per-pair NCCL unique ids,
 the max-over-ranks reduction of the timed region, and failure detection: a
 rank that dies before a collective makes the survivor's collective fail within
 the process-group timeout instead of hanging (the reference has no failure
-handling beyond asserts; SURVEY failure-detection plan).
+handling beyond asserts).
 """
 import datetime
 import os

@@ -20,6 +20,8 @@ MAX_N = 262144
 
 
 def keys_and_input(ddg, kind, bw, n, seed):
+    """Masked input x_hat = x + r_in and both parties' keys; returns the plain
+    x and the dealer's output mask r_out as well."""
     dt = ring_dt(bw)
     rng = np.random.default_rng(seed)
     hi = np.iinfo(dt).max
@@ -31,7 +33,16 @@ def keys_and_input(ddg, kind, bw, n, seed):
     k0, k1 = dev_bytes(kb), dev_bytes(kb)
     d_r, d_ro = to_dev(r), dev_bytes(n * bw // 8)
     ddg.gate_keygen(kind, bw, S, n, seed, 5, ptr(d_r), ptr(d_ro), ptr(k0), ptr(k1))
-    return to_dev((x + r).astype(dt)), k0, k1
+    return to_dev((x + r).astype(dt)), k0, k1, x, from_dev(d_ro, dt, n).copy()
+
+
+def plaintext(kind, bw, x):
+    """The gate's function on the plain input: ReLU, ReLU(floor(x/2^s)),
+    floor(x/2^s) signed, floor(x/2^s) for x in [0, 2^(bw-1))."""
+    dt = ring_dt(bw)
+    sx = x.view(np.int32 if bw == 32 else np.int64).astype(np.int64)
+    y = {0: np.maximum(sx, 0), 1: np.maximum(sx >> S, 0), 2: sx >> S, 3: sx >> S}[kind]
+    return y.astype(np.int64).view(np.uint64).astype(dt)
 
 
 def existing_entry_points(ddg, kind, bw, n, d_x, k0, k1):
@@ -60,16 +71,23 @@ def noalloc(ddg, kind, bw, n, d_x, k0, k1):
     return from_dev(out, ring_dt(bw), n)
 
 
+# consecutive calls share the scratch array; the order makes every ARS / LRS
+# call follow a call of another kind (LRS writes no high-comparison bits and
+# ARS reads both halves, so stale words from the call before would show), and
+# the first call fills the whole array
+CALLS = ((1, MAX_N, 11), (3, 40_001, 12), (2, 100_003, 13), (0, 77, 14), (3, MAX_N, 15), (2, 33, 16))
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("bw", [32, 64])
-def test_noalloc_two_calls_match_existing_entry_points(ddg, cuda, bw):
-    # first call: the largest allowed size; second call: another gate kind and size,
-    # so stale scratch from the first call would show up
-    for kind, n, seed in ((1, MAX_N, 11), (0, 40_001, 12)):
-        d_x, k0, k1 = keys_and_input(ddg, kind, bw, n, seed)
+def test_noalloc_calls_in_a_row_match_existing_entry_points(ddg, cuda, bw):
+    for kind, n, seed in CALLS:
+        d_x, k0, k1, x, r_out = keys_and_input(ddg, kind, bw, n, seed)
         want = existing_entry_points(ddg, kind, bw, n, d_x, k0, k1)
         got = noalloc(ddg, kind, bw, n, d_x, k0, k1)
         assert np.array_equal(got, want), (kind, n)
+        # and the gate's function itself: y_hat = f(x) + r_out
+        assert np.array_equal(got, (plaintext(kind, bw, x) + r_out).astype(ring_dt(bw))), (kind, n)
 
 
 @pytest.mark.gpu
