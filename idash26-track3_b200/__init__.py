@@ -39,6 +39,34 @@ _lib = None
 
 _u64, _u32, _i32, _vp = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int, ctypes.c_void_p
 
+
+class Cursor(ctypes.Structure):
+    """ddg_cursor: key bytes consumed / written so far, dealer ops so far."""
+    _fields_ = [("offset", _u64), ("ops", _u32), ("reserved", _u32)]
+
+
+class Wire(ctypes.Structure):
+    """ddg_wire: one evaluator's masked-public tensor and its mask share."""
+    _fields_ = [("d_value", _vp), ("n", _u64), ("d_mask_share", _vp)]
+
+
+class MaskWire(ctypes.Structure):
+    """ddg_mask_wire: the dealer's mask of a tensor and both parties' shares of it."""
+    _fields_ = [("d_mask", _vp), ("n", _u64), ("d_share0", _vp), ("d_share1", _vp)]
+
+
+# int exchange(void *user, int party, const void *d_send, void *d_recv, uint64_t bytes, void *stream)
+COMM_EXCHANGE = ctypes.CFUNCTYPE(_i32, _vp, _i32, _vp, _vp, _u64, _vp)
+
+
+class Comm(ctypes.Structure):
+    """ddg_comm: the caller's transport for the openings."""
+    _fields_ = [("user", _vp), ("exchange", COMM_EXCHANGE)]
+
+
+ACT_NONE, ACT_RELU, ACT_TRUNC = 0, 1, 2
+_C, _W, _M = ctypes.POINTER(Cursor), ctypes.POINTER(Wire), ctypes.POINTER(MaskWire)
+
 # name -> (restype, argtypes); kept in the order of include/ddg_fss.h
 SIGNATURES = {
     "ddg_last_error": (ctypes.c_char_p, []),
@@ -90,6 +118,29 @@ SIGNATURES = {
     "ddg_forward_graph_launch": (_i32, [_vp, _vp, _vp]),
     "ddg_forward_graph_destroy": (_i32, [_vp]),
     "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
+    "ddg_party_connect_callback": (_i32, [_vp, ctypes.POINTER(Comm)]),
+    "ddg_op_input_eval": (_i32, [_vp, _C, _u64, _vp, _W]),
+    "ddg_adjnorm_eval": (_i32, [_vp, _C, _i32, _vp, _W]),
+    "ddg_gcn_layer_eval": (_i32, [_vp, _C, _i32, _i32, _W, _W, _W]),
+    "ddg_op_mul_eval": (_i32, [_vp, _C, _i32, _i32, _i32, _W, _W, _i32, _W]),
+    "ddg_op_gate_eval": (_i32, [_vp, _C, _i32, _W, _W]),
+    "ddg_maxpool_eval": (_i32, [_vp, _C, _i32, _W, _W]),
+    "ddg_op_fc_eval": (_i32, [_vp, _C, _i32, _i32, _i32, _W, _W]),
+    "ddg_op_concat_protein_eval": (_i32, [_vp, _C, _i32, _W, _vp, _W]),
+    "ddg_op_output_eval": (_i32, [_vp, _C, _i32, _W, _vp, _vp]),
+    "ddg_dealer_create": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _i32, _u64, _vp, _u64]),
+    "ddg_dealer_bind_keys": (_i32, [_vp, _vp, _vp, _u64]),
+    "ddg_dealer_stream": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "ddg_dealer_destroy": (_i32, [_vp]),
+    "ddg_op_input_keygen": (_i32, [_vp, _C, _u64, _M]),
+    "ddg_adjnorm_keygen": (_i32, [_vp, _C, _i32, _M]),
+    "ddg_gcn_layer_keygen": (_i32, [_vp, _C, _i32, _i32, _M, _M, _M]),
+    "ddg_op_mul_keygen": (_i32, [_vp, _C, _i32, _i32, _i32, _M, _M, _i32, _M]),
+    "ddg_op_gate_keygen": (_i32, [_vp, _C, _i32, _M, _M]),
+    "ddg_maxpool_keygen": (_i32, [_vp, _C, _i32, _M, _M]),
+    "ddg_op_fc_keygen": (_i32, [_vp, _C, _i32, _i32, _i32, _M, _M]),
+    "ddg_op_concat_protein_keygen": (_i32, [_vp, _C, _i32, _M, _M]),
+    "ddg_op_output_keygen": (_i32, [_vp, _C, _M]),
     "ddg_launch_count": (_u64, []),
     "ddg_key_chunk_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_key_checksum": (_i32, [_vp, _u64, ctypes.POINTER(_u64), _vp]),
@@ -261,6 +312,20 @@ class Party:
         """Two party processes on one node: openings through CUDA IPC (see ddg_party_connect_ipc)."""
         check(lib().ddg_party_connect_ipc(self.h, name.encode(), slot_bytes))
 
+    def connect_callback(self, exchange):
+        """Openings through the caller's transport: exchange(party, d_send,
+        d_recv, nbytes, stream) -> 0 on success (see ddg_comm)."""
+
+        def tramp(user, party, d_send, d_recv, nbytes, stream):
+            try:
+                return int(exchange(party, d_send, d_recv, nbytes, stream) or 0)
+            except Exception:  # any failure of the transport fails the opening
+                return 1
+
+        self._comm_fn = COMM_EXCHANGE(tramp)  # kept alive as long as the party
+        self._comm = Comm(None, self._comm_fn)
+        check(lib().ddg_party_connect_callback(self.h, ctypes.byref(self._comm)))
+
     def set_timeout(self, ms: int):
         check(lib().ddg_party_set_timeout(self.h, ms))
 
@@ -281,6 +346,33 @@ class Party:
         check(lib().ddg_forward_eval(self.h, batch, x, adj, mask, prot, int(on_host), raw.ctypes.data,
                                      aff.ctypes.data))
         return (raw, aff) if self.party == 0 else (None, None)
+
+
+class Dealer:
+    """The layer-by-layer GPU dealer (ddg_dealer_*): both parties' keys written
+    at a cursor by the ddg_*_keygen entry points."""
+
+    def __init__(self, bw: int, scale: int, device: int, seed: int, weights_blob):
+        import numpy as np
+
+        blob = np.ascontiguousarray(weights_blob, dtype=np.int64)
+        h = _vp()
+        check(lib().ddg_dealer_create(ctypes.byref(h), bw, scale, device, seed, blob.ctypes.data, blob.size))
+        self.h = h
+
+    def bind_keys(self, d_key0: int, d_key1: int, nbytes: int):
+        check(lib().ddg_dealer_bind_keys(self.h, d_key0, d_key1, nbytes))
+
+    def close(self):
+        if self.h:
+            check(lib().ddg_dealer_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def nccl_unique_id() -> bytes:

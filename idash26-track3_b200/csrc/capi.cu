@@ -234,10 +234,6 @@ int ddg_aes_tables(int tables)
 
 // ------------------------------------------------------------ parties
 
-struct ddg_party {
-    ddg::Party P;
-};
-
 int ddg_party_create(ddg_party **out, int party, int bw, int scale, int device)
 {
     DDG_CHECK(out, DDG_ERR_ARG, "null out");
@@ -299,6 +295,17 @@ int ddg_party_stats(ddg_party *h, uint64_t *out3)
     out3[0] = h->P.stats.bytes_sent;
     out3[1] = h->P.stats.rounds;
     out3[2] = h->P.stats.key_bytes_used;
+    return DDG_OK;
+}
+
+int ddg_party_connect_callback(ddg_party *h, const ddg_comm *comm)
+{
+    DDG_CHECK(h && comm && comm->exchange, DDG_ERR_ARG, "null party, transport or exchange callback");
+    auto *c = new CallbackChannel();
+    c->comm = *comm;
+    c->timeout_ms = h->P.timeout_ms;
+    if (h->P.owns_chan) delete h->P.chan;
+    h->P.chan = c, h->P.owns_chan = true;
     return DDG_OK;
 }
 

@@ -100,6 +100,20 @@ int LocalPairChannel::barrier(int party, cudaStream_t st)
     return DDG_OK;
 }
 
+int CallbackChannel::exchange(int party, cudaStream_t st, const void *send, uint64_t bytes, void *recv,
+                              const void **peer)
+{
+    if (bytes) {
+        const int r = comm.exchange(comm.user, party, send, recv, bytes, st);
+        DDG_CHECK(r == 0, DDG_ERR_PEER, "the caller's exchange callback failed (%d) on an opening of %llu bytes", r,
+                  (unsigned long long)bytes);
+    }
+    *peer = recv;
+    bytes_sent[party] += bytes;
+    rounds[party] += 1;
+    return DDG_OK;
+}
+
 // ------------------------------------------------------------------ IPC channel
 //
 // Two party processes on one node, one GPU each.  Every party owns S = 4

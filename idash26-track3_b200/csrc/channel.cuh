@@ -68,6 +68,19 @@ struct LocalPairChannel : Channel {
     void fail();  // wake a waiting peer with an error (the other party gave up)
 };
 
+// The caller's own transport (ddg_comm, include/ddg_fss.h): every opening
+// hands the caller this party's device send buffer, a device receive buffer
+// and the party's stream; the callback returns once the peer's bytes of the
+// same opening are (or, in stream order, will be) in the receive buffer.
+// This is the reference's GpuPeer::reconstructInPlace (gpu_comms.h:291-302)
+// seam: a caller can run the openings over its own sockets or fabric.
+struct CallbackChannel : Channel {
+    ddg_comm comm{};
+    int exchange(int party, cudaStream_t st, const void *send, uint64_t bytes, void *recv, const void **peer) override;
+    int barrier(int, cudaStream_t) override { return DDG_OK; }  // the peer never reads this party's buffers
+    bool needs_recv_buffer() const override { return true; }
+};
+
 Channel *make_nccl_channel(const void *unique_id, int nranks, int rank, int peer_rank, int device, int *status);
 // CUDA-IPC channel between two party processes on one node (channel.cu); both
 // call it with the same `name` (a POSIX shared-memory name, no slash)

@@ -77,6 +77,7 @@ struct Party {
 
 uint64_t forward_key_bytes(int bw, int s, int B);
 void set_relu_parts(int parts);
+int relu_parts();  // 3 or 2
 void set_relu_backend(int backend);  // DDG_RELU_DCF or DDG_RELU_OT
 int relu_backend();
 double union_ms(std::vector<std::pair<double, double>> v);
@@ -94,3 +95,8 @@ int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uin
                    cudaStream_t st);
 
 }  // namespace ddg
+
+// the opaque handle of the C ABI (include/ddg_fss.h)
+struct ddg_party {
+    ddg::Party P;
+};

@@ -280,6 +280,146 @@ int ddg_dealer_forward(int bw, int scale, int batch, uint64_t seed, const int64_
                        int device, void *d_key0, void *d_key1, void *stream);
 
 /* ------------------------------------------------------------------------
+ * The caller's own transport, and the forward layer by layer.
+ *
+ * The reference's graph calls its backend one layer or op at a time, each
+ * reading the next key section through the caller's keyBuf cursor and
+ * opening through the backend's GpuPeer: ddgSecureAdjNorm{Keygen,Eval}
+ * (gpu_mpc/secure_adj_norm.h:204-213, 394-405), GCNLayer::forward
+ * (gcn_layer.h:99-103), MaskedMaxPoolLayer(B,Nmax,F)::_forward
+ * (masked_maxpool_layer.h:23-47) and the Backend<T> ops matmul (4-arg),
+ * mul, relu, truncateForward and output (ddg_orca_base.h:170-323,
+ * ddg_orca.h:43-123).  The entry points below are that interface.  Each
+ * runs the same layer function as the fused forward on a cursor the caller
+ * holds; called in the graph's order (adjnorm, input x, GCN 0..2, input
+ * mask, mul with truncation, maxpool, FC 3 (ReLU), FC 4 (floor), concat
+ * protein, FC 5..7 (ReLU), FC 8, output) they read exactly the key region of
+ * ddg_forward_key_bytes / ddg_dealer_forward and reveal exactly what
+ * ddg_forward_eval reveals.  Evaluator calls use the party's keys, weights
+ * and channel (any: ddg_pair_local, NCCL, IPC or ddg_party_connect_callback)
+ * and return once the party's stream has drained; both parties make the same
+ * calls in the same order.  Outputs go into caller-provided device buffers.
+ * Gate kinds follow ddg_relu_backend (the TT kinds by default).
+ * ---------------------------------------------------------------------- */
+
+/* A transport for the openings supplied by the caller (replaces the
+ * reference's GpuPeer::reconstructInPlace, gpu_mpc/utils/gpu_comms.h:291-302,
+ * over its TCP SigmaPeer, sigma_comms.cpp:106-150).  For every opening the
+ * library calls exchange(user, party, d_send, d_recv, bytes, stream) on the
+ * thread that called it: d_send holds this party's `bytes` bytes once the
+ * work already queued on `stream` has run; the callback must make the
+ * peer's bytes of the same opening available in the device buffer d_recv to
+ * work queued on `stream` after it returns (for example: synchronise the
+ * stream, copy d_send to the host, send, receive, copy into d_recv).  Both
+ * parties see the same sequence of openings.  A nonzero return fails the op
+ * with DDG_ERR_PEER. */
+typedef struct ddg_comm {
+    void *user;
+    int (*exchange)(void *user, int party, const void *d_send, void *d_recv, uint64_t bytes, void *stream);
+} ddg_comm;
+int ddg_party_connect_callback(ddg_party *party, const ddg_comm *comm);
+
+/* Key cursor (the reference's u8* keyBuf, advanced by every op,
+ * ddg_orca_base.h:41-50): offset = bytes of the bound key region consumed
+ * (evaluators) or written (dealer) so far; ops = dealer ops so far (it seeds
+ * each op's randomness; evaluators leave it alone).  A forward starts at
+ * {0, 0}; a call that fails leaves the cursor where it was. */
+typedef struct ddg_cursor {
+    uint64_t offset;
+    uint32_t ops;
+    uint32_t reserved;
+} ddg_cursor;
+
+/* A masked-public wire held by one evaluator: d_value = x + r (n ring
+ * elements on the device) and d_mask_share, the party's additive share of r
+ * (a pointer into its key region), NULL until an op needs it, which then
+ * reads it at the cursor and stores it here, as the reference's leaf
+ * registry keeps one mask share per tensor (ddg_orca_base.h:72-80).  Pass
+ * the same wire to every later op that uses the tensor.  For an output the
+ * caller provides d_value with room for the stated size; the call sets n and
+ * d_mask_share. */
+typedef struct ddg_wire {
+    void *d_value;
+    uint64_t n;
+    const void *d_mask_share;
+} ddg_wire;
+/* The dealer's view of a wire: the mask r (device) and both parties' shares
+ * of it in their key regions (NULL until an op needs them). */
+typedef struct ddg_mask_wire {
+    void *d_mask;
+    uint64_t n;
+    const void *d_share0;
+    const void *d_share1;
+} ddg_mask_wire;
+
+/* activation of ddg_op_fc_*: none (the output layer), ReLU(floor(y / 2^scale))
+ * (dfc1, ffc1-3 and the GCN FCs), floor(y / 2^scale) (dfc2) */
+#define DDG_ACT_NONE 0
+#define DDG_ACT_RELU 1
+#define DDG_ACT_TRUNC 2
+
+/* evaluator, one party.  Sizes: adjacency (batch,138,138), features
+ * (batch,138,94), GCN layer l output (batch,138,{188,282,376}[l]), max-pool
+ * input (batch,138,376) and output (batch,376), FC layer l (rows x in) ->
+ * (rows x out) with (in,out) of weights.bin layer l, concat (batch,128) ->
+ * (batch,256). */
+/* a secret-shared input leaf: own share + own mask share, opened
+ * (registerLeaf + revealIfLeaf, ddg_orca_base.h:72-80) */
+int ddg_op_input_eval(ddg_party *party, ddg_cursor *cur, uint64_t n, const void *d_share, ddg_wire *out);
+/* ddgSecureAdjNormEval (secure_adj_norm.h:394-659): A_hat at scale from the
+ * party's share of the raw 0/1 adjacency */
+int ddg_adjnorm_eval(ddg_party *party, ddg_cursor *cur, int batch, const void *d_adj_share, ddg_wire *out_ahat);
+/* GCNLayer::forward (gcn_layer.h:99-116), layer 0..2, aggregate first */
+int ddg_gcn_layer_eval(ddg_party *party, ddg_cursor *cur, int layer, int batch, ddg_wire *ahat, ddg_wire *x,
+                       ddg_wire *out);
+/* Backend<T>::mul (ddg_orca.h:43-63): Beaver product a*b, b broadcast per
+ * bcast (0 none, 1 by row, 2 by column of a (., rows, cols) tensor); trunc != 0
+ * adds the exact floor by 2^scale, valid for products in [0, 2^(bw-1)) */
+int ddg_op_mul_eval(ddg_party *party, ddg_cursor *cur, int bcast, int rows, int cols, ddg_wire *a, ddg_wire *b,
+                    int trunc, ddg_wire *out);
+/* Backend<T>::relu / truncateForward (ddg_orca.h:83-123): one gate of any kind
+ * (DDG_GATE_*), with its comparison rounds over the party's channel */
+int ddg_op_gate_eval(ddg_party *party, ddg_cursor *cur, int kind, ddg_wire *x, ddg_wire *out);
+/* MaskedMaxPoolLayer(batch,138,376)::_forward (masked_maxpool_layer.h:47-166)
+ * on the masked features */
+int ddg_maxpool_eval(ddg_party *party, ddg_cursor *cur, int batch, ddg_wire *masked, ddg_wire *out);
+/* FC<T> through Backend<T>::matmul 4-arg (ddg_orca_base.h:208-271), then act */
+int ddg_op_fc_eval(ddg_party *party, ddg_cursor *cur, int layer, int rows, int act, ddg_wire *x, ddg_wire *out);
+/* GPUConcat (deepdtagen.h:45-100): [d2 | protein], the protein revealed from
+ * the parties' shares (party 0 holds zeros) */
+int ddg_op_concat_protein_eval(ddg_party *party, ddg_cursor *cur, int batch, ddg_wire *d2,
+                               const void *d_protein_share, ddg_wire *out);
+/* Backend<T>::output (ddg_orca_base.h:296-302): unmask, shift by scale; the
+ * same outputs as ddg_forward_eval */
+int ddg_op_output_eval(ddg_party *party, ddg_cursor *cur, int batch, ddg_wire *o, int64_t *h_out_raw,
+                       double *h_affinity);
+
+/* dealer (the keygen mirror, DDGOrcaBaseKeygen / ddgSecureAdjNormKeygen,
+ * ddg_orca_base.h:326-525, secure_adj_norm.h:204-374): both parties' keys,
+ * written at the cursor into the bound key regions; masks from `seed`.
+ * Called in the graph's order it writes the keys of ddg_dealer_forward with
+ * the same seed, byte for byte. */
+typedef struct ddg_dealer ddg_dealer;
+int ddg_dealer_create(ddg_dealer **out, int bw, int scale, int device, uint64_t seed, const int64_t *h_weights,
+                      uint64_t n_weights);
+int ddg_dealer_bind_keys(ddg_dealer *dealer, void *d_key0, void *d_key1, uint64_t bytes);
+int ddg_dealer_stream(ddg_dealer *dealer, void **stream);
+int ddg_dealer_destroy(ddg_dealer *dealer);
+int ddg_op_input_keygen(ddg_dealer *dealer, ddg_cursor *cur, uint64_t n, ddg_mask_wire *out);
+int ddg_adjnorm_keygen(ddg_dealer *dealer, ddg_cursor *cur, int batch, ddg_mask_wire *out_ahat);
+int ddg_gcn_layer_keygen(ddg_dealer *dealer, ddg_cursor *cur, int layer, int batch, ddg_mask_wire *ahat,
+                         ddg_mask_wire *x, ddg_mask_wire *out);
+int ddg_op_mul_keygen(ddg_dealer *dealer, ddg_cursor *cur, int bcast, int rows, int cols, ddg_mask_wire *a,
+                      ddg_mask_wire *b, int trunc, ddg_mask_wire *out);
+int ddg_op_gate_keygen(ddg_dealer *dealer, ddg_cursor *cur, int kind, ddg_mask_wire *x, ddg_mask_wire *out);
+int ddg_maxpool_keygen(ddg_dealer *dealer, ddg_cursor *cur, int batch, ddg_mask_wire *masked, ddg_mask_wire *out);
+int ddg_op_fc_keygen(ddg_dealer *dealer, ddg_cursor *cur, int layer, int rows, int act, ddg_mask_wire *x,
+                     ddg_mask_wire *out);
+int ddg_op_concat_protein_keygen(ddg_dealer *dealer, ddg_cursor *cur, int batch, ddg_mask_wire *d2,
+                                 ddg_mask_wire *out);
+int ddg_op_output_keygen(ddg_dealer *dealer, ddg_cursor *cur, ddg_mask_wire *o);
+
+/* ------------------------------------------------------------------------
  * Key chunks and streaming (replaces the chunked key file and the streaming
  * evaluation of deepdtagen_inference.cu:344-416 and :608-826: 4 KiB-padded
  * chunks, 2 pinned + 2 device slots, a copy stream and events).

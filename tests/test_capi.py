@@ -124,3 +124,18 @@ def test_three_part_split_layout(ddg):
         assert lay["bytes"] - lay["words"] >= words * 4 * 1000
     with pytest.raises(ddg.DdgError):  # scale + 6 must stay below bw - 1
         ddg.gate_key_layout(ddg.GATE_RELU_SPLIT3, 32, 25, 10)
+
+
+def test_layer_entry_points_reject_bad_arguments_without_a_gpu(ddg):
+    """The per-layer interface checks its handles, cursor and wires before any
+    device work: a null party, dealer or cursor is DDG_ERR_ARG."""
+    L = ddg.lib()
+    c = ddg.Cursor()
+    w = ddg.Wire(None, 0, None)
+    mw = ddg.MaskWire(None, 0, None, None)
+    for st in (L.ddg_adjnorm_eval(None, c, 1, None, w), L.ddg_gcn_layer_eval(None, c, 0, 1, w, w, w),
+               L.ddg_op_gate_eval(None, c, 0, w, w), L.ddg_maxpool_eval(None, c, 1, w, w),
+               L.ddg_op_output_eval(None, c, 1, w, None, None), L.ddg_adjnorm_keygen(None, c, 1, mw),
+               L.ddg_op_fc_keygen(None, c, 3, 1, 1, mw, mw), L.ddg_party_connect_callback(None, None)):
+        assert st == 1
+    assert L.ddg_dealer_destroy(None) == 0
