@@ -67,24 +67,31 @@ class Bufs:
     def __init__(self, es):
         self.es, self.keep = es, []
 
-    def wire(self, ddg, n):
+    def _buf(self, n):
+        import torch
+
         t = dev_bytes(n * self.es)
+        torch.cuda.synchronize()  # torch zero-fills on its own stream; the library writes on the party's
         self.keep.append(t)
-        return ddg.Wire(ptr(t), n, None)
+        return t
+
+    def wire(self, ddg, n):
+        return ddg.Wire(ptr(self._buf(n)), n, None)
 
     def mask_wire(self, ddg, n):
-        t = dev_bytes(n * self.es)
-        self.keep.append(t)
-        return ddg.MaskWire(ptr(t), n, None, None)
+        return ddg.MaskWire(ptr(self._buf(n)), n, None, None)
 
 
-def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb):
-    """The dealer, layer by layer, in the order of the fused forward."""
+def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb, masks=None):
+    """The dealer, layer by layer, in the order of the fused forward.  masks
+    (dict, optional) receives the dealer's mask of every named wire."""
     L = ddg.lib()
     d = ddg.Dealer(bw, S, 0, seed, blob)
     d.bind_keys(ptr(k0), ptr(k1), kb)
     c = ddg.Cursor()
     bufs = Bufs(bw // 8)
+    if masks is not None:
+        masks["_bufs"] = bufs
     mw = lambda n: bufs.mask_wire(ddg, n)  # noqa: E731
     chk = ddg.check
     try:
@@ -96,6 +103,8 @@ def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb):
             Hn = mw(B * NMAX * LAYER_OUT[l])
             chk(L.ddg_gcn_layer_keygen(d.h, c, l, B, Ah, H, Hn))
             H = Hn
+            if masks is not None:
+                masks[f"gcn{l}.H"] = H
         M = mw(B * NMAX * POOL)
         chk(L.ddg_op_input_keygen(d.h, c, M.n, M))
         Pm = mw(B * NMAX * POOL)
@@ -108,6 +117,7 @@ def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb):
         chk(L.ddg_op_fc_keygen(d.h, c, 4, B, ddg.ACT_TRUNC, d1, d2))
         f = mw(B * 256)
         chk(L.ddg_op_concat_protein_keygen(d.h, c, B, d2, f))
+        f_cat = f
         for l in (5, 6, 7):
             fn = mw(B * LAYER_OUT[l])
             chk(L.ddg_op_fc_keygen(d.h, c, l, B, ddg.ACT_RELU, f, fn))
@@ -115,6 +125,9 @@ def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb):
         o = mw(B)
         chk(L.ddg_op_fc_keygen(d.h, c, 8, B, ddg.ACT_NONE, f, o))
         chk(L.ddg_op_output_keygen(d.h, c, o))
+        if masks is not None:
+            masks.update({"A_hat": Ah, "gcn2.H": H, "masked": Pm, "pooled": pooled, "d1": d1, "d2": d2,
+                          "fused": f_cat, "f3": f, "out2s": o})
         return c.offset
     finally:
         d.close()
@@ -128,6 +141,7 @@ def layered_eval(ddg, party, bw, B, shares, out):
     w = lambda n: bufs.wire(ddg, n)  # noqa: E731
     chk = ddg.check
     h = party.h
+    out["_bufs"] = bufs
     Ah = w(B * NMAX * NMAX)
     chk(L.ddg_adjnorm_eval(h, c, B, ptr(shares[1]), Ah))
     H = w(B * NMAX * FEAT)
@@ -136,6 +150,7 @@ def layered_eval(ddg, party, bw, B, shares, out):
         Hn = w(B * NMAX * LAYER_OUT[l])
         chk(L.ddg_gcn_layer_eval(h, c, l, B, Ah, H, Hn))
         H = Hn
+        out[f"gcn{l}.H"] = H
     M = w(B * NMAX * POOL)
     chk(L.ddg_op_input_eval(h, c, M.n, ptr(shares[2]), M))
     Pm = w(B * NMAX * POOL)
@@ -148,15 +163,30 @@ def layered_eval(ddg, party, bw, B, shares, out):
     chk(L.ddg_op_fc_eval(h, c, 4, B, ddg.ACT_TRUNC, d1, d2))
     f = w(B * 256)
     chk(L.ddg_op_concat_protein_eval(h, c, B, d2, ptr(shares[3]), f))
+    f_cat = f
     for l in (5, 6, 7):
         fn = w(B * LAYER_OUT[l])
         chk(L.ddg_op_fc_eval(h, c, l, B, ddg.ACT_RELU, f, fn))
         f = fn
     o = w(B)
+    chk(L.ddg_op_fc_eval(h, c, 8, B, ddg.ACT_NONE, f, o))
     raw = np.zeros(B, dtype=np.int64)
     aff = np.zeros(B, dtype=np.float64)
     chk(L.ddg_op_output_eval(h, c, B, o, raw.ctypes.data, aff.ctypes.data))
     out["raw"], out["aff"], out["offset"] = raw, aff, c.offset
+    out.update({"A_hat": Ah, "masked": Pm, "pooled": pooled, "d1": d1, "d2": d2, "fused": f_cat, "f3": f,
+                "out2s": o})
+
+
+def wire_host(d_ptr, n, dt):
+    """n ring elements at a device address, copied to the host"""
+    import torch
+
+    torch.cuda.synchronize()
+    buf = np.empty(n, dtype=dt)
+    cr = _cudart()
+    assert cr.cudaMemcpy(buf.ctypes.data, d_ptr, buf.nbytes, 2) == 0
+    return buf
 
 
 def run_both(fn0, fn1):
@@ -205,13 +235,16 @@ def test_layered_keygen_and_eval_match_fused_forward(ddg, synth, cuda, bw):
     fused = [dev_bytes(kb) for _ in range(2)]
     ddg.dealer_forward(bw, S, B, 555, blob, 0, ptr(fused[0]), ptr(fused[1]))
     layered = [dev_bytes(kb) for _ in range(2)]
-    end = layered_keygen(ddg, bw, B, 555, blob, layered[0], layered[1], kb)
+    masks = {}
+    end = layered_keygen(ddg, bw, B, 555, blob, layered[0], layered[1], kb, masks)
     torch.cuda.synchronize()
     assert 0 < end <= kb
     for p in (0, 1):
         assert torch.equal(layered[p], fused[p]), f"party {p}: layered dealer keys differ from ddg_dealer_forward's"
 
-    want_raw, want_aff = RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, S)
+    trace = {}
+    want_raw, want_aff = RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, S,
+                                             trace=trace)
     want_raw = RF.Ring(bw).signed(want_raw)
     ps = parties(ddg, bw, blob, layered, kb)
     ddg.pair_local(ps[0], ps[1])
@@ -220,6 +253,17 @@ def test_layered_keygen_and_eval_match_fused_forward(ddg, synth, cuda, bw):
     outs = [{}, {}]
     run_both(lambda: layered_eval(ddg, ps[0], bw, B, shares[0], outs[0]),
              lambda: layered_eval(ddg, ps[1], bw, B, shares[1], outs[1]))
+    # every intermediate wire, unmasked with the dealer's mask, is the oracle's value
+    dt = np.uint32 if bw == 32 else np.uint64
+    for name in ("A_hat", "gcn0.H", "gcn1.H", "gcn2.H", "masked", "pooled", "d1", "d2", "fused", "f3", "out2s"):
+        n = masks[name].n
+        mask = wire_host(masks[name].d_mask, n, dt)
+        for p in (0, 1):
+            val = wire_host(outs[p][name].d_value, n, dt)
+            got = (val - mask).astype(dt)
+            want = np.asarray(trace[name], dtype=np.uint64).astype(dt).reshape(-1)
+            bad = np.flatnonzero(got != want)
+            assert bad.size == 0, f"party {p}, wire {name}: {bad.size} of {n} values differ (first {bad[:5]})"
     for p in (0, 1):
         assert np.array_equal(outs[p]["raw"], raw_f) and np.array_equal(outs[p]["aff"], aff_f)
         assert outs[p]["offset"] == end  # the evaluators consumed exactly what the dealer wrote
