@@ -122,6 +122,7 @@ SIGNATURES = {
     "ddg_op_input_eval": (_i32, [_vp, _C, _u64, _vp, _W]),
     "ddg_adjnorm_eval": (_i32, [_vp, _C, _i32, _vp, _W]),
     "ddg_gcn_layer_eval": (_i32, [_vp, _C, _i32, _i32, _W, _W, _W]),
+    "ddg_op_matmul_eval": (_i32, [_vp, _C, _i32, _i32, _W, _W, _W]),
     "ddg_op_mul_eval": (_i32, [_vp, _C, _i32, _i32, _i32, _W, _W, _i32, _W]),
     "ddg_op_gate_eval": (_i32, [_vp, _C, _i32, _W, _W]),
     "ddg_maxpool_eval": (_i32, [_vp, _C, _i32, _W, _W]),
@@ -135,6 +136,7 @@ SIGNATURES = {
     "ddg_op_input_keygen": (_i32, [_vp, _C, _u64, _M]),
     "ddg_adjnorm_keygen": (_i32, [_vp, _C, _i32, _M]),
     "ddg_gcn_layer_keygen": (_i32, [_vp, _C, _i32, _i32, _M, _M, _M]),
+    "ddg_op_matmul_keygen": (_i32, [_vp, _C, _i32, _i32, _M, _M, _M]),
     "ddg_op_mul_keygen": (_i32, [_vp, _C, _i32, _i32, _i32, _M, _M, _i32, _M]),
     "ddg_op_gate_keygen": (_i32, [_vp, _C, _i32, _M, _M]),
     "ddg_maxpool_keygen": (_i32, [_vp, _C, _i32, _M, _M]),

@@ -231,6 +231,21 @@ int ddg_gcn_layer_eval(ddg_party *h, ddg_cursor *cur, int layer, int batch, ddg_
 #undef BODY
 }
 
+int ddg_op_matmul_eval(ddg_party *h, ddg_cursor *cur, int batch, int k, ddg_wire *ahat, ddg_wire *x, ddg_wire *out)
+{
+    DDG_TRY(eval_ready(h, cur, batch));
+    DDG_TRY(check_wires({ahat, x, out, out ? out->d_value : nullptr}));
+    DDG_CHECK(k > 0 && ahat->n == uint64_t(batch) * NMAX * NMAX && x->n == uint64_t(batch) * NMAX * k, DDG_ERR_ARG,
+              "matmul: wires are not (%d, %d, %d) and (%d, %d, %d)", batch, NMAX, NMAX, batch, NMAX, k);
+#define BODY(T)                                   \
+    Tn<T> A = tn_of<T>(ahat), H = tn_of<T>(x);     \
+    Tn<T> y = e.matmul(A, H, k);                   \
+    back<T>(ahat, A), back<T>(x, H);               \
+    put<T>(e, out, y);
+    return DDG_DISPATCH_EVAL(h, cur, batch, BODY);
+#undef BODY
+}
+
 int ddg_op_mul_eval(ddg_party *h, ddg_cursor *cur, int bcast, int rows, int cols, ddg_wire *a, ddg_wire *b,
                     int trunc, ddg_wire *out)
 {
@@ -414,6 +429,22 @@ int ddg_gcn_layer_keygen(ddg_dealer *d, ddg_cursor *cur, int layer, int batch, d
 #define BODY(T)                                   \
     Tn<T> A = tn_of<T>(ahat), H = tn_of<T>(x);     \
     Tn<T> y = gcn_layer<T>(e, A, H, layer);        \
+    back<T>(ahat, A), back<T>(x, H);               \
+    put<T>(e, out, y);
+    return DDG_DISPATCH_KEYGEN(d, cur, batch, BODY);
+#undef BODY
+}
+
+int ddg_op_matmul_keygen(ddg_dealer *d, ddg_cursor *cur, int batch, int k, ddg_mask_wire *ahat, ddg_mask_wire *x,
+                         ddg_mask_wire *out)
+{
+    DDG_TRY(keygen_ready(d, cur, batch));
+    DDG_TRY(check_wires({ahat, x, out, out ? out->d_mask : nullptr}));
+    DDG_CHECK(k > 0 && ahat->n == uint64_t(batch) * NMAX * NMAX && x->n == uint64_t(batch) * NMAX * k, DDG_ERR_ARG,
+              "matmul: wires are not (%d, %d, %d) and (%d, %d, %d)", batch, NMAX, NMAX, batch, NMAX, k);
+#define BODY(T)                                   \
+    Tn<T> A = tn_of<T>(ahat), H = tn_of<T>(x);     \
+    Tn<T> y = e.matmul(A, H, k);                   \
     back<T>(ahat, A), back<T>(x, H);               \
     put<T>(e, out, y);
     return DDG_DISPATCH_KEYGEN(d, cur, batch, BODY);

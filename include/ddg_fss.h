@@ -372,6 +372,11 @@ int ddg_adjnorm_eval(ddg_party *party, ddg_cursor *cur, int batch, const void *d
 /* GCNLayer::forward (gcn_layer.h:99-116), layer 0..2, aggregate first */
 int ddg_gcn_layer_eval(ddg_party *party, ddg_cursor *cur, int layer, int batch, ddg_wire *ahat, ddg_wire *x,
                        ddg_wire *out);
+/* Backend<T>::matmul 3-arg (ddg_orca_base.h:170-205, looped per sample in
+ * sytorch/layers/layers.h:67-90): the Beaver product A_hat . x per sample,
+ * ahat (batch,138,138), x (batch,138,k) -> (batch,138,k), no truncation */
+int ddg_op_matmul_eval(ddg_party *party, ddg_cursor *cur, int batch, int k, ddg_wire *ahat, ddg_wire *x,
+                       ddg_wire *out);
 /* Backend<T>::mul (ddg_orca.h:43-63): Beaver product a*b, b broadcast per
  * bcast (0 none, 1 by row, 2 by column of a (., rows, cols) tensor); trunc != 0
  * adds the exact floor by 2^scale, valid for products in [0, 2^(bw-1)) */
@@ -408,6 +413,8 @@ int ddg_dealer_destroy(ddg_dealer *dealer);
 int ddg_op_input_keygen(ddg_dealer *dealer, ddg_cursor *cur, uint64_t n, ddg_mask_wire *out);
 int ddg_adjnorm_keygen(ddg_dealer *dealer, ddg_cursor *cur, int batch, ddg_mask_wire *out_ahat);
 int ddg_gcn_layer_keygen(ddg_dealer *dealer, ddg_cursor *cur, int layer, int batch, ddg_mask_wire *ahat,
+                         ddg_mask_wire *x, ddg_mask_wire *out);
+int ddg_op_matmul_keygen(ddg_dealer *dealer, ddg_cursor *cur, int batch, int k, ddg_mask_wire *ahat,
                          ddg_mask_wire *x, ddg_mask_wire *out);
 int ddg_op_mul_keygen(ddg_dealer *dealer, ddg_cursor *cur, int bcast, int rows, int cols, ddg_mask_wire *a,
                       ddg_mask_wire *b, int trunc, ddg_mask_wire *out);

@@ -82,7 +82,7 @@ class Bufs:
         return ddg.MaskWire(ptr(self._buf(n)), n, None, None)
 
 
-def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb, masks=None):
+def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb, masks=None, ops=False):
     """The dealer, layer by layer, in the order of the fused forward.  masks
     (dict, optional) receives the dealer's mask of every named wire."""
     L = ddg.lib()
@@ -101,7 +101,13 @@ def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb, masks=None):
         chk(L.ddg_op_input_keygen(d.h, c, H.n, H))
         for l in range(3):
             Hn = mw(B * NMAX * LAYER_OUT[l])
-            chk(L.ddg_gcn_layer_keygen(d.h, c, l, B, Ah, H, Hn))
+            if ops:  # GCNLayer::forward from Backend<T> ops: matmul 3-arg, truncation, FC + ReLU
+                Pm, AX = mw(B * NMAX * LAYER_IN[l]), mw(B * NMAX * LAYER_IN[l])
+                chk(L.ddg_op_matmul_keygen(d.h, c, B, LAYER_IN[l], Ah, H, Pm))
+                chk(L.ddg_op_gate_keygen(d.h, c, ddg.GATE_LRS_TT, Pm, AX))
+                chk(L.ddg_op_fc_keygen(d.h, c, l, B * NMAX, ddg.ACT_RELU, AX, Hn))
+            else:
+                chk(L.ddg_gcn_layer_keygen(d.h, c, l, B, Ah, H, Hn))
             H = Hn
             if masks is not None:
                 masks[f"gcn{l}.H"] = H
@@ -133,7 +139,7 @@ def layered_keygen(ddg, bw, B, seed, blob, k0, k1, kb, masks=None):
         d.close()
 
 
-def layered_eval(ddg, party, bw, B, shares, out):
+def layered_eval(ddg, party, bw, B, shares, out, ops=False):
     """One evaluator, layer by layer; shares = device (x, adj, mask, protein)."""
     L = ddg.lib()
     c = ddg.Cursor()
@@ -148,7 +154,13 @@ def layered_eval(ddg, party, bw, B, shares, out):
     chk(L.ddg_op_input_eval(h, c, H.n, ptr(shares[0]), H))
     for l in range(3):
         Hn = w(B * NMAX * LAYER_OUT[l])
-        chk(L.ddg_gcn_layer_eval(h, c, l, B, Ah, H, Hn))
+        if ops:
+            Pm, AX = w(B * NMAX * LAYER_IN[l]), w(B * NMAX * LAYER_IN[l])
+            chk(L.ddg_op_matmul_eval(h, c, B, LAYER_IN[l], Ah, H, Pm))
+            chk(L.ddg_op_gate_eval(h, c, ddg.GATE_LRS_TT, Pm, AX))
+            chk(L.ddg_op_fc_eval(h, c, l, B * NMAX, ddg.ACT_RELU, AX, Hn))
+        else:
+            chk(L.ddg_gcn_layer_eval(h, c, l, B, Ah, H, Hn))
         H = Hn
         out[f"gcn{l}.H"] = H
     M = w(B * NMAX * POOL)
@@ -226,7 +238,8 @@ def parties(ddg, bw, blob, keys, kb):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("bw", [32, 64])
-def test_layered_keygen_and_eval_match_fused_forward(ddg, synth, cuda, bw):
+@pytest.mark.parametrize("gcn", ["layer", "ops"])
+def test_layered_keygen_and_eval_match_fused_forward(ddg, synth, cuda, bw, gcn):
     import torch
 
     B = 3
@@ -236,7 +249,8 @@ def test_layered_keygen_and_eval_match_fused_forward(ddg, synth, cuda, bw):
     ddg.dealer_forward(bw, S, B, 555, blob, 0, ptr(fused[0]), ptr(fused[1]))
     layered = [dev_bytes(kb) for _ in range(2)]
     masks = {}
-    end = layered_keygen(ddg, bw, B, 555, blob, layered[0], layered[1], kb, masks)
+    ops = gcn == "ops"
+    end = layered_keygen(ddg, bw, B, 555, blob, layered[0], layered[1], kb, masks, ops=ops)
     torch.cuda.synchronize()
     assert 0 < end <= kb
     for p in (0, 1):
@@ -251,8 +265,8 @@ def test_layered_keygen_and_eval_match_fused_forward(ddg, synth, cuda, bw):
     raw_f, aff_f = ddg.forward_pair(ps[0], ps[1], B, [ptr(t) for t in shares[0]], [ptr(t) for t in shares[1]])
     assert np.array_equal(raw_f, want_raw)
     outs = [{}, {}]
-    run_both(lambda: layered_eval(ddg, ps[0], bw, B, shares[0], outs[0]),
-             lambda: layered_eval(ddg, ps[1], bw, B, shares[1], outs[1]))
+    run_both(lambda: layered_eval(ddg, ps[0], bw, B, shares[0], outs[0], ops=ops),
+             lambda: layered_eval(ddg, ps[1], bw, B, shares[1], outs[1], ops=ops))
     # every intermediate wire, unmasked with the dealer's mask, is the oracle's value
     dt = np.uint32 if bw == 32 else np.uint64
     for name in ("A_hat", "gcn0.H", "gcn1.H", "gcn2.H", "masked", "pooled", "d1", "d2", "fused", "f3", "out2s"):
