@@ -440,7 +440,7 @@ def launch_count() -> int:
     return int(lib().ddg_launch_count())
 
 
-GEMM_TENSOR, GEMM_CUDA_CORES, GEMM_TENSOR_BK, GEMM_TENSOR_WIDE, GEMM_TENSOR_SYNC = 0, 1, 2, 3, 4
+GEMM_TENSOR, GEMM_CUDA_CORES, GEMM_TENSOR_BK, GEMM_TENSOR_WIDE, GEMM_TENSOR_SYNC, GEMM_TENSOR_INKERNEL = 0, 1, 2, 3, 4, 5
 
 
 def gemm_path(path: int):

@@ -167,7 +167,7 @@ int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, con
 
 int ddg_gemm_path(int path)
 {
-    DDG_CHECK(path >= 0 && path <= 4, DDG_ERR_ARG, "gemm path must be 0..4 (got %d)", path);
+    DDG_CHECK(path >= 0 && path <= 5, DDG_ERR_ARG, "gemm path must be 0..5 (got %d)", path);
     set_gemm_path(path);
     return DDG_OK;
 }

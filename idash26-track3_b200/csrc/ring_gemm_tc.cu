@@ -603,12 +603,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) ring_gemm_tc2_kernel(const __gr
 
 __device__ uint32_t g_tc_err;
 
-// 0: tensor cores (default): for Z_2^32 the asynchronous-staging kernel where
-// the operands allow it, else B MN-major with 64-column tiles; for Z_2^64 B
-// MN-major with 32-column tiles; 1: CUDA cores only; 2: tensor cores, B
-// K-major; 3: tensor cores, 128-column tiles (Z_2^32) or 32-column tiles
-// (Z_2^64); 4: tensor cores, B MN-major, 64-column tiles (the synchronous
-// kernel).  2-4 exist for the layout/tile comparison tests.
+// 0: tensor cores (default): for Z_2^32 the packed-operand kernel
+// (ring_gemm_pk.cu); for Z_2^64 B MN-major with 32-column tiles; 1: CUDA cores
+// only; 2: tensor cores, B K-major; 3: tensor cores, 128-column tiles
+// (Z_2^32) or 32-column tiles (Z_2^64); 4: tensor cores, B MN-major,
+// 64-column tiles (the synchronous kernel); 5: for Z_2^32 the in-kernel
+// operand split (the asynchronous-staging kernel where the operands allow it,
+// else 64-column tiles) with the CUDA cores on ragged last rows.  2-5 exist for
+// the layout/tile comparison tests.
 int g_gemm_path = 0;
 
 template <typename T, int BN, bool B_MN>
@@ -675,6 +677,15 @@ int launch_tc2(const GemmArgs<uint32_t> &a, cudaStream_t st, int *launched)
 
 }  // namespace
 
+// the error word every tensor-core GEMM kernel sets when a bounded wait gives up
+int ring_gemm_err_word(uint32_t **out)
+{
+    DDG_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(out), g_tc_err));
+    return DDG_OK;
+}
+
+int ring_gemm_packed(const GemmArgs<uint32_t> &a, cudaStream_t st);  // ring_gemm_pk.cu
+
 int ring_gemm_tc_error(bool clear)
 {
     uint32_t v = 0;
@@ -716,8 +727,14 @@ int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
     if (a.M == 0 || a.N == 0 || a.batch == 0) return DDG_OK;
     const int ktot = a.A2 ? 2 * a.K : a.K;
     if (g_gemm_path == 1 || a.K == 0 || ktot > tc_max_k<T>()) return ring_gemm_simt<T>(a, st);
+    if constexpr (sizeof(T) == 4) {
+        if (g_gemm_path == 0) {
+            const int ng = (a.M + TC_BM - 1) / TC_BM, nks = (ktot + TC_BK - 1) / TC_BK;
+            if (a.batch <= 65535 && int64_t(ng) * nks <= 65535) return ring_gemm_packed(a, st);
+        }
+    }
     const int tail = a.M % TC_BM;
-    if (g_gemm_path == 0 && a.M > TC_BM && tail != 0 && tail <= TC_THIN_TAIL) {
+    if ((g_gemm_path == 0 || g_gemm_path == 5) && a.M > TC_BM && tail != 0 && tail <= TC_THIN_TAIL) {
         GemmArgs<T> whole = a;
         whole.M = a.M - tail;
         DDG_TRY(ring_gemm<T>(whole, st));
@@ -726,7 +743,7 @@ int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
     if (g_gemm_path == 2) return launch_tc<T, 64, false>(a, st);
     if (g_gemm_path == 3) return launch_tc<T, sizeof(T) == 4 ? 128 : 32, true>(a, st);
     if constexpr (sizeof(T) == 4) {
-        if (g_gemm_path == 0) {
+        if (g_gemm_path == 0 || g_gemm_path == 5) {
             int launched = 0;
             DDG_TRY(launch_tc2(a, st, &launched));
             if (launched) return DDG_OK;

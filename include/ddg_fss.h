@@ -519,12 +519,17 @@ int ddg_fc_share(int bw, int party, int M, int K, int N, const void *d_xhat, con
 
 /* Ring GEMM engine of ddg_matmul_share / ddg_fc_share and the forward.
  * path 0 (default): tcgen05 tensor cores, 8-bit limb products with int32
- * accumulation recombined modulo 2^bw; at bw 32 with even row strides and
- * 8-byte aligned operands (and no Beaver operand rewrite) the kernel with
- * asynchronous (cp.async) operand staging and 128 x 128 tiles, otherwise
- * operand B MN-major in shared memory with 128 x 64 tiles (128 x 32 at bw 64); 1: CUDA cores (integer multiply-add); 2: tensor
- * cores with B K-major; 3: tensor cores with 128 x 128 (bw 32) or 128 x 32
- * (bw 64) tiles; 4: tensor cores, 128 x 64 tiles, synchronous staging.  Reduction lengths beyond the limb sums' exactness bound
+ * accumulation recombined modulo 2^bw; at bw 32 the operands are first split
+ * into byte planes in the tensor cores' shared-memory layout by two streaming
+ * kernels (scratch from the device's stream-ordered pool) and the GEMM moves
+ * them with bulk copies through a 4-stage warp-specialised pipeline, a
+ * 16-row tail tile covering ragged last rows (M % 128 <= 16); at bw 64
+ * operand B MN-major in shared memory with 128 x 32 tiles; 1: CUDA cores
+ * (integer multiply-add); 2: tensor cores with B K-major; 3: tensor cores
+ * with 128 x 128 (bw 32) or 128 x 32 (bw 64) tiles; 4: tensor cores, 128 x 64
+ * tiles, synchronous staging; 5: at bw 32 the in-kernel operand split (with
+ * cp.async staging and 128 x 128 tiles where the operands allow it), ragged
+ * last rows on the CUDA cores.  Reduction lengths beyond the limb sums' exactness bound
  * (K > 8192 at bw 32, K > 4096 at bw 64, counting both Beaver products) always
  * use the CUDA cores.  Process-wide setting.
  * ddg_gemm_status: DDG_OK, or DDG_ERR_CUDA when a tensor-core GEMM gave up on

@@ -14,7 +14,7 @@ import pytest
 
 from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 
-PATHS = [0, 4, 2, 3, 1]
+PATHS = [0, 5, 4, 2, 3, 1]
 
 
 def rnd(rng, bw, shape):
