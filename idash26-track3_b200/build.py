@@ -2,8 +2,10 @@
 
 Each csrc/*.cu / *.cpp is compiled to _build/<name>.o (rebuilt when it or any
 header in csrc/ or include/ is newer), then linked into ./libddg.so next to
-this file, and the command-line drop-in cli/ddg_inference.cpp into
-./ddg_inference against it.  NCCL comes from the pip-installed nvidia-nccl package torch ships
+this file, the command-line drop-in cli/ddg_inference.cpp into
+./ddg_inference against it, and the offline tools cli/ddg_share.cpp and
+cli/ddg_export_weights.cpp (plain C++) into ./ddg_share and
+./ddg_export_weights.  NCCL comes from the pip-installed nvidia-nccl package torch ships
 with, with the system copy as a fallback.
 """
 from __future__ import annotations
@@ -102,6 +104,7 @@ def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> 
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stderr)
     build_cli(force)
+    build_tools(force)
     return LIB
 
 
@@ -119,6 +122,27 @@ def build_cli(force: bool = False) -> str:
     if r.returncode != 0:
         raise RuntimeError("ddg_inference build failed:\n" + r.stderr)
     return out
+
+
+TOOLS = ("ddg_share", "ddg_export_weights")
+
+
+def build_tools(force: bool = False) -> list:
+    """The offline tools (cli/ddg_share.cpp, cli/ddg_export_weights.cpp): plain
+    C++17, no CUDA, built next to libddg.so."""
+    cxx = shutil.which("g++") or "g++"
+    outs = []
+    for name in TOOLS:
+        src = os.path.join(HERE, "cli", name + ".cpp")
+        out = os.path.join(HERE, name)
+        outs.append(out)
+        if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
+            continue
+        r = subprocess.run([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", src, "-o", out], capture_output=True,
+                           text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"{name} build failed:\n" + r.stderr)
+    return outs
 
 
 if __name__ == "__main__":
