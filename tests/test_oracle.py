@@ -105,22 +105,32 @@ def test_ff_restatement_bit_exact_vs_reference_golden(bw, synth):
         assert int(o[0]) == int(out[b])
 
 
+# measured gap |protocol_forward - fixed_forward| on the 16 golden samples per
+# ring (affinity units): bw 32 max 0.0076, mean 0.0030; bw 64 max 0.0132, mean
+# 0.0044.  Pinned just above, so that a change of either function shows.
+BRIDGE = {32: (0.0080, 0.0032), 64: (0.0135, 0.0046)}
+
+
 @pytest.mark.parametrize("bw", [32, 64])
 def test_protocol_forward_bridge_to_reference_fixed_forward(bw, synth):
     """The 2PC graph computes a different integer function from fixed_forward.py
     (aggregate-first truncation, LUT-derived A_hat, mask-multiply pool); the
     reference itself gates their agreement at 0.005 affinity units
-    (scripts/dev_tools/validate_batch_fixed.py:33).  On these random-weight
-    models the measured gap is <= 0.0085 per sample, mean ~0.003."""
+    (scripts/dev_tools/validate_batch_fixed.py:33), on trained weights.  On
+    these random-weight models (N(0,1) * 0.1 init, larger pre-activations than
+    trained ones) the gap is pinned at its measured maximum and mean over 16
+    samples per ring (BRIDGE)."""
     X, A, m, pv, layers, pmvo, out = _golden(bw, synth)
     B = X.shape[0]
+    assert B >= 16
     q = synth.quantize_weights(layers, 12)
     xr, ar = synth.to_ring(X, 12, bw), synth.to_ring(A, 0, bw)
     mr = synth.to_ring(np.broadcast_to(m[:, :, None], (B, 138, 376)), 12, bw)
     pr = synth.to_ring(pv, 12, bw)
     _, aff = RF.protocol_forward(xr, ar, mr, pr, q, bw, 12)
     d = np.abs(aff - out / 4096.0)
-    assert d.max() < 0.02 and d.mean() < 0.005, d
+    top, mean = BRIDGE[bw]
+    assert d.max() <= top and d.mean() <= mean, d
 
 
 def test_weight_blob_roundtrip(synth, tmp_path):
