@@ -15,15 +15,18 @@
 // contiguous blocks (one block = one row group or column tile for one
 // 32-element K-step: exactly the bytes of one pipeline stage), and the GEMM
 // moves each stage with two bulk copies (cp.async.bulk, mbarrier transaction
-// counts) into a 4-deep ring of stages:
+// counts) into a ring of 4 stages (3 with 64-column tiles):
 //
 //   warp 0       producer: one thread issues the bulk copies of stage ks
-//                once the MMAs of stage ks-4 have released it;
+//                once the MMAs of the stage's previous use have released it;
 //   warp 1       owns the tensor memory; one thread issues the limb MMAs of
 //                a stage once its bytes have landed and commits them to the
 //                stage's "empty" barrier, then commits the tile to "acc";
-//   warps 2..5   epilogue: tcgen05.ld of the P partial sums, shift-add,
-//                + bias + Add, stores.
+//   warps 2..5   epilogue: while the mainloop runs, the Add words of the
+//                output tile into shared memory (asynchronous 4-byte copies,
+//                one row per warp step) and its bias words; then per row
+//                (TMEM lane) tcgen05.ld of the P partial sums, shift-add
+//                into the tile with the bias; then coalesced stores of C.
 //
 // A block of A covers a row group of 128 rows; when the last rows of a
 // matrix are a short tail (M % 128 <= 16, e.g. the 10 rows 128..137 of each
@@ -34,12 +37,14 @@
 // tile's base, and the 112 rows past its 16 read other bytes of the same
 // stage (their products land in accumulator rows that are never stored).
 //
-// Two CTAs per SM (90-100 KiB of shared memory, 256 tensor-memory columns
+// Two CTAs per SM (about 108 KiB of shared memory, 256 tensor-memory columns
 // each), so one CTA's epilogue overlaps the other's copies and MMAs.  Every
 // mbarrier wait is bounded (about two seconds of %globaltimer); a wait that
-// gives up sets the error word of ring_gemm_tc_check, the producer then waits
-// (bounded) for the copies it has issued, warp 1 for the MMAs it has issued,
-// and the CTA frees its tensor memory and returns.
+// gives up sets the error word of ring_gemm_tc_check.  Before a CTA leaves,
+// the producer waits (bounded) for the copies it has issued and for the MMA
+// warp's releases of the last stages, warp 1 for the MMAs it has issued, and
+// the CTA frees its tensor memory: no asynchronous arrive or copy may land in
+// shared memory that the next CTA on the SM already uses.
 #include "common.cuh"
 #include "linear.cuh"
 
@@ -52,12 +57,12 @@ namespace {
 constexpr int PK_BM = 128;        // rows of a full tile (TMEM lanes)
 constexpr int PK_BK = 32;         // K elements (bytes per plane row) per stage
 constexpr int PK_THIN = 16;       // rows of a tail tile
-constexpr int PK_STAGES = 4;
 constexpr int PK_THREADS = 192;   // 6 warps
 constexpr uint32_t PK_NCOL = 256; // tensor-memory columns per CTA
 constexpr uint64_t PK_WAIT_NS = 2000000000ull;
 constexpr uint32_t PK_FULL_PLANE = PK_BM * PK_BK;  // 4096 bytes
 constexpr uint32_t PK_THIN_PLANE = PK_THIN * PK_BK;  // 512 bytes
+constexpr int PK_BAR_SLOTS = 4;   // barrier slots per kind (the most stages of either tile width)
 
 // geometry of one packed GEMM (host and device)
 struct PkGeom {
@@ -271,32 +276,64 @@ __global__ void pk_pack_b(const __grid_constant__ GemmArgs<uint32_t> a, PkGeom g
 
 // ---------------------------------------------------------------- the GEMM
 
-// epilogue of one accumulator set (tile t) for the 32 rows of this warp's
-// TMEM lane quadrant q: rows row0 + 32q + lane, columns n0 .. n0 + BN
+// Output tile in shared memory, [rows][BN + 1] words (the odd row pitch keeps
+// both the row-per-thread and the column-per-lane accesses conflict-free).
 template <int BN>
-__device__ __forceinline__ void pk_epilogue(const PkArgs<uint32_t> &a, uint32_t tmem, int t, int q, int lane, int b,
-                                            int row0, int n0, int nrows)
+struct PkTile {
+    static constexpr int ROWS = BN == 32 ? PK_BM + PK_THIN : PK_BM;  // tail tiles come with BN = 32
+    static constexpr int PITCH = BN + 1;
+    static constexpr uint32_t BYTES = uint32_t((ROWS * PITCH + BN) * 4);  // the tile, then BN bias words
+    static constexpr int STAGES = BN == 32 ? 4 : 3;  // two CTAs per SM either way
+    static_assert(STAGES <= PK_BAR_SLOTS, "barrier slots");
+};
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_t src_bytes)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+// epilogue warps, before the accumulators are ready: the Add words of the
+// CTA's output tile into shared memory with asynchronous copies (all of them
+// in flight at once; zero-filled outside the matrix), one row per warp step
+// and one column per lane, and the bias words of its columns.  The copies
+// are waited for (cp.async.wait_all) before the tile is read.
+template <int BN>
+__device__ __forceinline__ void pk_prefetch(const PkArgs<uint32_t> &a, uint32_t *tile, uint32_t *bias_s, int we,
+                                            int lane, int b, int row0, int n0, int rows)
+{
+    const uint32_t *Add = a.Add ? a.Add + int64_t(b) * a.sAdd : nullptr;
+    for (int r = we; r < rows; r += 4) {
+        const int m = row0 + r;
+#pragma unroll
+        for (int c = lane; c < BN; c += 32) {
+            const int n = n0 + c;
+            const bool in = Add && m < a.M && n < a.N;
+            cp_async4(smem_u32(tile + r * PkTile<BN>::PITCH + c), in ? Add + int64_t(m) * a.ldAdd + n : a.C,
+                      in ? 4u : 0u);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (we == 0) {
+#pragma unroll
+        for (int c = lane; c < BN; c += 32) bias_s[c] = (a.bias && n0 + c < a.N) ? __ldg(a.bias + n0 + c) : 0u;
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// one accumulator set (tile t): this thread's row r of the tile gets
+// sum_s S_s << 8s added, from TMEM lane quadrant q (the loads are warp-wide;
+// only threads with `mine` write)
+template <int BN>
+__device__ __forceinline__ void pk_accumulate(uint32_t *tile, const uint32_t *bias_s, uint32_t tmem, int t, int q,
+                                              int r, bool mine)
 {
     constexpr int P = 4;
-    const int r = 32 * q + lane;
-    const int m = row0 + r;
-    const bool row_ok = r < nrows && m < a.M;
-    const uint32_t *Add = a.Add ? a.Add + int64_t(b) * a.sAdd + int64_t(m) * a.ldAdd : nullptr;
-    uint32_t *C = a.C + int64_t(b) * a.sC + int64_t(m) * a.ldc;
     const uint32_t lane_base = uint32_t(32 * q) << 16;
-#pragma unroll 1
-    for (int c = 0; c < BN / 8; c++) {
-        uint32_t extra[8];
+    uint32_t *row = tile + r * PkTile<BN>::PITCH;
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const int n = n0 + 8 * c + e;
-            uint32_t v = 0;
-            if (row_ok && n < a.N) {
-                if (a.bias) v += __ldg(a.bias + n);
-                if (Add) v += __ldg(Add + n);
-            }
-            extra[e] = v;
-        }
+    for (int c = 0; c < BN / 8; c++) {
         uint32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
         for (int s = 0; s < P; s++) {
@@ -306,12 +343,27 @@ __device__ __forceinline__ void pk_epilogue(const PkArgs<uint32_t> &a, uint32_t 
 #pragma unroll
             for (int e = 0; e < 8; e++) acc[e] += v[e] << (8 * s);
         }
-        if (row_ok) {
+        if (mine) {
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const int n = n0 + 8 * c + e;
-                if (n < a.N) C[n] = acc[e] + extra[e];
-            }
+            for (int e = 0; e < 8; e++) row[8 * c + e] += acc[e] + bias_s[8 * c + e];
+        }
+    }
+}
+
+// the finished tile to C, one row per warp step, one column per lane
+template <int BN>
+__device__ __forceinline__ void pk_store(const PkArgs<uint32_t> &a, const uint32_t *tile, int we, int lane, int b,
+                                         int row0, int n0, int rows)
+{
+    uint32_t *C = a.C + int64_t(b) * a.sC;
+#pragma unroll 4
+    for (int r = we; r < rows; r += 4) {
+        const int m = row0 + r;
+        if (m >= a.M) break;
+#pragma unroll
+        for (int c = lane; c < BN; c += 32) {
+            const int n = n0 + c;
+            if (n < a.N) C[int64_t(m) * a.ldc + n] = tile[r * PkTile<BN>::PITCH + c];
         }
     }
 }
@@ -320,11 +372,12 @@ template <int BN>
 __global__ void __launch_bounds__(PK_THREADS) ring_gemm_pk_kernel(const __grid_constant__ PkArgs<uint32_t> a,
                                                                   uint32_t *err)
 {
-    constexpr int P = 4, S = PK_STAGES;
+    constexpr int P = 4, S = PkTile<BN>::STAGES;
+    // barriers at fixed offsets for both tile widths: full[4] | empty[4] | acc | TMEM address | fail flag
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint64_t *const full = reinterpret_cast<uint64_t *>(smem_raw);
-    uint64_t *const empty = full + S;
-    uint64_t *const accb = empty + S;
+    uint64_t *const empty = full + PK_BAR_SLOTS;
+    uint64_t *const accb = empty + PK_BAR_SLOTS;
     uint32_t *const s_tmem = reinterpret_cast<uint32_t *>(accb + 1);
     volatile int *const s_fail = reinterpret_cast<volatile int *>(s_tmem + 1);
     uint8_t *const stages = smem_raw + 128 + ((1024u - ((smem_u32(smem_raw) + 128u) & 1023u)) & 1023u);
@@ -337,6 +390,8 @@ __global__ void __launch_bounds__(PK_THREADS) ring_gemm_pk_kernel(const __grid_c
     const uint32_t bytes_a = tail ? g.sa : P * PK_FULL_PLANE, bytes_b = g.sb;
     const uint32_t stage_bytes = g.sa + g.sb;
     const int nks = g.nks;
+    uint32_t *const tile = reinterpret_cast<uint32_t *>(stages + S * stage_bytes);
+    uint32_t *const bias_s = tile + PkTile<BN>::ROWS * PkTile<BN>::PITCH;
 
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
@@ -378,6 +433,11 @@ __global__ void __launch_bounds__(PK_THREADS) ring_gemm_pk_kernel(const __grid_c
             // the copies this thread issued land before the CTA may leave
             for (int k = issued > S ? issued - S : 0; k < issued; k++)
                 if (!bar_wait(full + k % S, uint32_t((k / S) & 1))) *s_fail = 1;
+            // and so do the MMA warp's releases of the last stages (tcgen05.commit arrives on
+            // empty[]): an arrive that landed after the CTA left would hit the shared memory of
+            // the next CTA on this SM
+            for (int k = nks > S ? nks - S : 0; k < nks; k++)
+                if (!bar_wait(empty + k % S, uint32_t((k / S) & 1))) *s_fail = 1;
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -412,15 +472,23 @@ __global__ void __launch_bounds__(PK_THREADS) ring_gemm_pk_kernel(const __grid_c
         }
         __syncwarp();
     } else {
-        const int q = warp & 3;
-        const bool ok = bar_wait(accb, 0) && !*s_fail;
-        if (!ok) {
-            *s_fail = 1;
-        } else {
+        // epilogue: bias + Add while the mainloop runs, then the accumulators, then C
+        const int q = warp & 3, we = warp - 2;
+        const int rows = PK_BM + (tail ? PK_THIN : 0), row0 = grp * PK_BM, n0 = nt * BN;
+        pk_prefetch<BN>(a, tile, bias_s, we, lane, b, row0, n0, rows);
+        epi_sync();
+        const bool ok = __all_sync(0xffffffffu, bar_wait(accb, 0) ? 1 : 0) && !*s_fail;
+        if (ok) {
             fence_after();
-            pk_epilogue<BN>(a, tmem, 0, q, lane, b, grp * PK_BM, nt * BN, PK_BM);
-            if (tail && q == 0) pk_epilogue<BN>(a, tmem, 1, 0, lane, b, grp * PK_BM + PK_BM, nt * BN, PK_THIN);
+            pk_accumulate<BN>(tile, bias_s, tmem, 0, q, 32 * q + lane, true);
+            // the tail tile's rows sit in TMEM lanes 0..15 of its accumulators
+            if (tail && q == 0)
+                pk_accumulate<BN>(tile, bias_s, tmem, 1, 0, PK_BM + (lane & (PK_THIN - 1)), lane < PK_THIN);
+        } else {
+            *s_fail = 1;
         }
+        epi_sync();
+        if (!*s_fail) pk_store<BN>(a, tile, we, lane, b, row0, n0, rows);
         __syncwarp();
     }
     fence_before();
@@ -458,15 +526,17 @@ PkGeom pk_geometry(const GemmArgs<uint32_t> &a)
 template <int BN>
 int pk_launch(const PkArgs<uint32_t> &pa, int batch, uint32_t *err, cudaStream_t st)
 {
-    const uint32_t smem = PK_SMEM_PAD + PK_STAGES * (pa.g.sa + pa.g.sb);
+    // stages for this tile width: 4 x (18432 + 4096) with a tail tile, 3 x (16384 + 8192) without
+    constexpr uint32_t kMax = PK_SMEM_PAD + PkTile<BN>::STAGES * (4 * PK_FULL_PLANE + (BN == 32 ? 4 * PK_THIN_PLANE : 0) +
+                                                                   4 * BN * PK_BK) + PkTile<BN>::BYTES;
+    const uint32_t smem = PK_SMEM_PAD + PkTile<BN>::STAGES * (pa.g.sa + pa.g.sb) + PkTile<BN>::BYTES;
+    DDG_CHECK(smem <= kMax, DDG_ERR_ARG, "packed GEMM: stage set of %u bytes exceeds %u", smem, kMax);
     auto kern = ring_gemm_pk_kernel<BN>;
     static thread_local int configured_dev = -1;
     int dev = 0;
     DDG_CUDA(cudaGetDevice(&dev));
     if (configured_dev != dev) {
-        // the largest stage set of either configuration (4 x (18432 + 4096) or 4 x (16384 + 8192))
-        DDG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      PK_SMEM_PAD + PK_STAGES * (4 * PK_FULL_PLANE + 4 * 64 * PK_BK)));
+        DDG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax));
         configured_dev = dev;
     }
     dim3 grid(pa.g.nnt, pa.g.ng, batch);
