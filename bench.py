@@ -104,9 +104,11 @@ def parse():
                          "(--comm)")
     ap.add_argument("--peer-timeout", type=int, default=600,
                     help="N>1: seconds a party waits for its peer at one opening before giving up")
-    ap.add_argument("--comm", default="ipc", choices=["ipc", "nccl"],
-                    help="N>1: openings between the two parties of a pair over CUDA IPC (default; both ranks on one "
-                         "node) or NCCL send/recv")
+    ap.add_argument("--comm", default="ipc-push", choices=["ipc-push", "ipc", "nccl"],
+                    help="N>1, split layout: openings between the two parties of a pair over CUDA IPC with the "
+                         "handoff on the device (default: peer stores into the consumer's HBM and a flag), over CUDA "
+                         "IPC with host handoffs (the consumer reads the producer's slot over NVLink), or NCCL "
+                         "send/recv")
     ap.add_argument("--aes-tables", type=int, default=4, choices=[2, 4],
                     help="AES engine: 4 staged round tables (default) or 2 tables + rotation")
     ap.add_argument("--relu-split", type=int, default=0, choices=[0, 2, 3],
@@ -121,14 +123,19 @@ def parse():
     ap.add_argument("--graph", default="on", choices=["on", "off"],
                     help="colocated pairs with resident keys: replay the timed forwards from one CUDA-graph "
                          "capture of both parties (default) or launch them from the host every step")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="skip the sub-records of the line: at N=1 (bw=32) the bw=64 kiba-shaped workload "
+                         "(BASELINE configs[3]), at N>1 (colocated) the split layout (party 0 and party 1 on different "
+                         "GPUs, openings over CUDA IPC)")
+    ap.add_argument("--sub-steps", type=int, default=10, help="timed steps of each sub-record")
     ap.add_argument("--stream", type=int, default=0, metavar="NCHUNKS",
                     help="streaming regime (BASELINE configs[4]): keys of NCHUNKS forwards per party live in pinned "
                          "host memory and are streamed into HBM through the double-buffered key stream, cyclically")
     a = ap.parse_args()
     if a.relu_split == 0:
         a.relu_split = 2 if a.stream else 3
-    if a.lanes < 1 or (a.lanes != 1 and a.comm != "ipc"):
-        raise SystemExit("--lanes: more than 1 lane per rank needs --comm ipc (see --help)")
+    if a.lanes < 1 or (a.lanes != 1 and a.comm == "nccl"):
+        raise SystemExit("--lanes: more than 1 lane per rank needs --comm ipc or ipc-push (see --help)")
     if a.stream and a.batch == 256:
         a.batch = 64  # one chunk per party is ~6.4 GB at bw=32
     return a
@@ -171,7 +178,9 @@ def parallelism(a, n_gpus):
     if colocated(a, n_gpus):
         return f"{n_gpus} party pairs, both parties of a pair on one GPU (openings on the device), " \
                "independent micro-batches per GPU"
-    over = "CUDA IPC (peer slots read over NVLink)" if a.comm == "ipc" else "NCCL send/recv"
+    over = {"ipc": "CUDA IPC (peer slots read over NVLink, host handoffs)",
+            "ipc-push": "CUDA IPC with device-side handoffs (peer stores into the consumer's HBM, flags)",
+            "nccl": "NCCL send/recv"}[a.comm]
     return f"{n_gpus // 2} party pairs over {over}, one party per GPU"
 
 
@@ -441,6 +450,99 @@ def h2d_probe(torch, bufs, device):
     return nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9
 
 
+def _timed_steps(torch, stream, device, fn, k):
+    """k calls of fn() between CUDA events on `stream`, synchronised on both sides; ms"""
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(k):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1)
+
+
+def subrecord_bw64(a, ddg, synth, torch, device, local):
+    """BASELINE configs[3] on the same GPU after the main measurement: bw=64,
+    kiba-shaped graphs (atoms U[10,100]), B = --batch, both parties on the GPU,
+    CUDA-graph replay.  Returns (record, (inputs, outputs)) for the parity check."""
+    bw, s, B = 64, a.scale, a.batch
+    blob = synth.weights_blob(synth.quantize_weights(synth.affinity_weights(5), s))
+    inp = synth.Inputs(B, bw, seed=2000, atoms=atoms_of(bw))
+    kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 2097, blob, device)
+    parties = [ddg.Party(0, bw, s, local), ddg.Party(1, bw, s, local)]
+    for p, k in zip(parties, (k0, k1)):
+        p.set_weights(blob)
+        p.bind_keys(k.data_ptr(), kb)
+    ddg.pair_local(parties[0], parties[1])
+    bufs = [share_buffers(torch, inp, p, device) for p in (0, 1)]
+    ins = [[t.data_ptr() for t in bufs[p][0]] for p in (0, 1)]
+    outs = {}
+    for _ in range(a.warmup):
+        outs["warmup_forward"] = ddg.forward_pair(parties[0], parties[1], B, ins[0], ins[1])
+    g = ddg.ForwardGraph(parties[0], parties[1], B, ins[0], ins[1])
+    try:
+        outs["graph_replay"] = g.launch()
+        stream = torch.cuda.ExternalStream(parties[0].stream, device=device)
+        ms = _timed_steps(torch, stream, device, g.launch, a.sub_steps)
+    finally:
+        g.close()
+    for p in parties:
+        p.close()
+    del k0, k1, bufs
+    torch.cuda.empty_cache()
+    rec = {"workload": f"full affinity branch, bw=64, scale={s}, B={B} kiba-shaped synthetic graphs (atoms "
+                       f"U[10, 100]), keys resident, both parties on the GPU, CUDA-graph replay (BASELINE configs[3])",
+           "value": B * a.sub_steps / (ms / 1e3), "unit": "samples/s", "ms_per_step": ms / a.sub_steps,
+           "steps": a.sub_steps, "warmup": a.warmup, "dtype": "u64", "key_bytes_per_party_per_step": kb,
+           "e2e_key_frac": 2 * kb / (ms / a.sub_steps / 1e3) / 1e9 / measured_peaks()[0]}
+    return rec, (inp, outs)
+
+
+def subrecord_split(a, ddg, synth, torch, dist, rank, world, local, device, push=True):
+    """The split layout on the same GPUs after the colocated measurement: ranks
+    0..k-1 party 0, ranks k..2k-1 party 1, pair i = (i, k+i), each pair on its
+    own micro-batch of B, openings over CUDA IPC (NVLink).  Time max over ranks."""
+    bw, s, B = a.bw, a.scale, a.batch
+    pairs, pair, party, peer = roles(rank, world)
+    blob = synth.weights_blob(synth.quantize_weights(synth.affinity_weights(5), s))
+    inp = synth.Inputs(B, bw, seed=3000 + pair, atoms=atoms_of(bw))
+    tag = uuid.uuid4().hex[:16]
+    names = [[f"ddg_{tag}_s{i}" for i in range(pairs)] if rank == 0 else None]
+    dist.broadcast_object_list(names, src=0)
+    P = ddg.Party(party, bw, s, local)
+    P.set_weights(blob)
+    kb, k0, k1 = make_keys(ddg, torch, bw, s, B, 3000 + 97 * pair, blob, device)
+    mine = k0 if party == 0 else k1
+    del k0, k1
+    torch.cuda.empty_cache()
+    P.bind_keys(mine.data_ptr(), kb)
+    P.set_timeout(1000 * a.peer_timeout)
+    P.connect_ipc(names[0][pair], ddg.forward_max_exchange_bytes(bw, s, B), push=push)
+    buf = share_buffers(torch, inp, party, device)
+    ins = [t.data_ptr() for t in buf[0]]
+    for _ in range(a.warmup):
+        P.forward(B, *ins)
+    dist.barrier()
+    stream = torch.cuda.ExternalStream(P.stream, device=device)
+    ms = _timed_steps(torch, stream, device, lambda: P.forward(B, *ins), a.sub_steps)
+    t = torch.tensor([ms], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    st = P.stats()
+    dist.barrier()
+    P.close()
+    del mine, buf
+    torch.cuda.empty_cache()
+    value = pairs * B * a.sub_steps / (ms / 1e3)
+    return {"layout": "split: ranks 0..k-1 party 0, ranks k..2k-1 party 1, pair i = (i, k+i), one micro-batch per "
+                      "pair, openings over CUDA IPC " + ("with device-side handoffs (peer stores into the consumer's "
+                      "HBM, flags)" if push else "with host handoffs (send slots read in place over NVLink)"),
+            "pairs": pairs, "value": value, "unit": "samples/s", "ms_per_step": ms / a.sub_steps,
+            "steps": a.sub_steps, "warmup": a.warmup, "samples_per_s_per_gpu": value / world,
+            "nvlink_bytes_per_step": 2 * pairs * st["bytes_sent"], "openings_per_step": st["rounds"]}
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -504,7 +606,7 @@ def main():
         inp = synth.Inputs(B, bw, seed=1000 + pair, atoms=atoms_of(bw))
         # one channel per party pair (and lane): a pair's openings never
         # involve the other ranks
-        if a.comm == "ipc":
+        if a.comm != "nccl":
             tag = uuid.uuid4().hex[:16]
             uids = [[[f"ddg_{tag}_{i}_{l}" for l in range(lanes)] for i in range(pairs)] if rank == 0 else None]
         else:
@@ -532,8 +634,8 @@ def main():
                 P.bind_keys(mine.data_ptr(), kb)
                 keep_keys.append(mine)
             P.set_timeout(1000 * a.peer_timeout)
-            if a.comm == "ipc":
-                P.connect_ipc(uids[0][pair][lane], ddg.forward_max_exchange_bytes(bw, s, Bl))
+            if a.comm != "nccl":
+                P.connect_ipc(uids[0][pair][lane], ddg.forward_max_exchange_bytes(bw, s, Bl), push=a.comm == "ipc-push")
             else:
                 P.connect_nccl(uids[0][pair][lane], 2, party, 1 - party)
             parties.append(P)
@@ -703,6 +805,22 @@ def main():
     roofline["aes_peak_gblocks_per_s"] = aes_peak
     roofline["aes_frac"] = roofline["aes_gblocks_per_s"] / aes_peak if aes_peak else None
 
+    # sub-records, after the main run's parties and keys are released
+    for ks in streams:
+        ks.close()
+    for p in parties:
+        p.close()
+    streams, parties, bufs, k0, k1, keep_keys = [], [], None, None, None, None
+    torch.cuda.empty_cache()
+    sub, chk64 = {}, None
+    if not a.no_subrecords and not a.stream and colo:
+        if world == 1 and bw == 32:
+            sub["bw64"], chk64 = subrecord_bw64(a, ddg, synth, torch, device, local)
+        elif world > 1:
+            sub["split"] = subrecord_split(a, ddg, synth, torch, dist, rank, world, local, device, push=True)
+            sub["split_host_handoff"] = subrecord_split(a, ddg, synth, torch, dist, rank, world, local, device,
+                                                        push=False)
+
     cb = None
     parity = None
     # the GPU outputs agree among themselves (graph replay, host launches, host buffers)
@@ -712,6 +830,8 @@ def main():
         q = synth.quantize_weights(synth.affinity_weights(5), s)
         cb = cpu_baseline(bw, check=(inp, q, outs) if outs else None)
         parity = cb.pop("parity", None)
+        if chk64 is not None:
+            _, sub["bw64"]["parity"] = check_outputs(64, chk64[0], q, chk64[1])
     if parity is None:
         parity = {"result": "not checked against the oracle (N > 1, streaming or --no-cpu-baseline)",
                   "gpu_paths_agree": same}
@@ -728,14 +848,12 @@ def main():
                          "bytes_per_sample": 2 * stats["bytes_sent"] / B,
                          # emulated LAN, full duplex: each party's bytes at 1 Gbps + one 1 ms RTT per opening
                          "lan_1gbps_1ms_rtt_s_per_step": stats["bytes_sent"] * 8 / 1e9 + stats["rounds"] * 1e-3},
-                "key_bytes_per_party_per_step": kb, "stream": stream_info, "parity": parity}
+                "key_bytes_per_party_per_step": kb, "stream": stream_info, "parity": parity,
+                "subrecords": sub or None}
         emit(line)
-        if parity.get("result") == "MISMATCH" or same is False:
+        bad64 = sub.get("bw64", {}).get("parity", {}).get("result") == "MISMATCH"
+        if parity.get("result") == "MISMATCH" or same is False or bad64:
             raise SystemExit("bench: the GPU forward's outputs do not match (see parity in the JSON line)")
-    for ks in streams:
-        ks.close()
-    for p in parties:
-        p.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -108,6 +108,7 @@ SIGNATURES = {
     "ddg_party_connect_nccl": (_i32, [_vp, _vp, _i32, _i32, _i32]),
     "ddg_party_set_timeout": (_i32, [_vp, _i32]),
     "ddg_party_connect_ipc": (_i32, [_vp, ctypes.c_char_p, _u64]),
+    "ddg_party_connect_ipc_push": (_i32, [_vp, ctypes.c_char_p, _u64]),
     "ddg_party_exchange_probe": (_i32, [_vp, _u64, _i32, ctypes.POINTER(ctypes.c_double)]),
     "ddg_forward_max_exchange_bytes": (_u64, [_i32, _i32, _i32]),
     "ddg_forward_key_bytes": (_u64, [_i32, _i32, _i32]),
@@ -310,9 +311,12 @@ class Party:
         buf = ctypes.create_string_buffer(bytes(unique_id), 128)
         check(lib().ddg_party_connect_nccl(self.h, buf, nranks, rank, peer_rank))
 
-    def connect_ipc(self, name: str, slot_bytes: int):
-        """Two party processes on one node: openings through CUDA IPC (see ddg_party_connect_ipc)."""
-        check(lib().ddg_party_connect_ipc(self.h, name.encode(), slot_bytes))
+    def connect_ipc(self, name: str, slot_bytes: int, push: bool = False):
+        """Two party processes on one node: openings through CUDA IPC (see
+        ddg_party_connect_ipc); push=True hands them over on the device
+        (ddg_party_connect_ipc_push; the parties on different GPUs)."""
+        fn = lib().ddg_party_connect_ipc_push if push else lib().ddg_party_connect_ipc
+        check(fn(self.h, name.encode(), slot_bytes))
 
     def connect_callback(self, exchange):
         """Openings through the caller's transport: exchange(party, d_send,

@@ -355,6 +355,18 @@ int ddg_party_connect_ipc(ddg_party *h, const char *name, uint64_t slot_bytes)
     return DDG_OK;
 }
 
+int ddg_party_connect_ipc_push(ddg_party *h, const char *name, uint64_t slot_bytes)
+{
+    DDG_CHECK(h && name && *name && slot_bytes, DDG_ERR_ARG, "bad argument");
+    DDG_CHECK(std::strlen(name) < 200 && !std::strchr(name, '/'), DDG_ERR_ARG, "bad shared-memory name");
+    int st = DDG_OK;
+    Channel *c = make_ipc_channel(name, h->P.party, h->P.device, slot_bytes, h->P.timeout_ms, &st, true);
+    DDG_TRY(st);
+    if (h->P.owns_chan) delete h->P.chan;
+    h->P.chan = c, h->P.owns_chan = true;
+    return DDG_OK;
+}
+
 uint64_t ddg_forward_max_exchange_bytes(int bw, int scale, int batch)
 {
     if (check_gate_args(0, bw, scale) != DDG_OK || batch <= 0) return 0;

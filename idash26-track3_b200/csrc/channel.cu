@@ -3,6 +3,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstring>
@@ -142,17 +143,121 @@ struct IpcShared {
     std::atomic<uint32_t> failed;
     std::atomic<uint64_t> posted[2], read[2];
     uint64_t slot_bytes;
+    uint32_t push;                    // push mode (both parties must agree)
     cudaIpcMemHandle_t arena[2];
     cudaIpcEventHandle_t ev_posted[2][4], ev_read[2][4];
+    cudaIpcMemHandle_t flags[2];      // push mode: each party's PushFlags block
+    char bus_id[2][32];               // PCI bus id of each party's GPU
 };
+
+// ------------------------------------------------------------------ push mode (device-side handoff)
+//
+// Every party owns, in its own device memory, S receive slots (the arena) and
+// a PushFlags block; both are mapped into the peer's process.  Exchange g of
+// party p (slot s = (g-1) % S), all of it enqueued on p's stream, no host wait:
+//   1. k_push_gate (one thread): publish "p consumed the peer's generation
+//      g-1" into the peer's flags (every kernel that read it came before this
+//      one on the stream), then wait until the peer has consumed p's
+//      generation g-S, the last one that used slot s on the peer's side;
+//   2. k_push_copy: copy the share into the peer's slot s with peer stores
+//      (16- or 4-byte words), each block fences at system scope, and the last
+//      block to finish raises the peer's `posted` to g;
+//   3. k_push_wait (one thread): wait until the peer's generation g has been
+//      posted into p's own slot s; the consumers then read local HBM.
+// The waits are single-thread kernels (they never fill the GPU), bounded by
+// the party's timeout: one that gives up sets `err`, which the host reads
+// after the forward (status()).  Both parties must be on different GPUs:
+// kernels that wait on one another are never launched on one GPU.
+struct PushFlags {
+    unsigned long long posted;     // the peer's last generation in this party's receive slots
+    unsigned long long consumed;   // this party's last generation that the peer has consumed
+    unsigned int done_blocks;      // k_push_copy's block counter (this party's own)
+    unsigned int err;              // a wait of this party gave up
+    unsigned long long pad[29];
+};
+static_assert(sizeof(PushFlags) == 256, "flags block");
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// bounded spin of one thread until *p >= target; false (and err set) after limit_ns
+__device__ bool spin_until(const unsigned long long *p, unsigned long long target, unsigned long long limit_ns,
+                           unsigned int *err)
+{
+    if (ld_acquire_sys(p) >= target) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (unsigned int it = 0;; it++) {
+        if (ld_acquire_sys(p) >= target) return true;
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
+            atomicOr(err, 1u);
+            return false;
+        }
+        __nanosleep(200);
+    }
+}
+
+__global__ void k_push_gate(PushFlags *me, PushFlags *peer, unsigned long long g, unsigned int S,
+                            unsigned long long limit_ns)
+{
+    if (threadIdx.x != 0) return;
+    st_release_sys(&peer->consumed, g - 1);
+    if (g > S) spin_until(&me->consumed, g - S, limit_ns, &me->err);
+}
+
+__global__ void k_push_copy(const uint32_t *src, uint32_t *dst, uint64_t words, PushFlags *me, PushFlags *peer,
+                            unsigned long long g)
+{
+    const uint64_t tid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x, nth = uint64_t(gridDim.x) * blockDim.x;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        const uint64_t n16 = words / 4;
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+        for (uint64_t i = tid; i < n16; i += nth) d4[i] = s4[i];
+        for (uint64_t i = 4 * n16 + tid; i < words; i += nth) dst[i] = src[i];
+    } else {
+        for (uint64_t i = tid; i < words; i += nth) dst[i] = src[i];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (atomicAdd(&me->done_blocks, 1u) == gridDim.x - 1) {
+            me->done_blocks = 0;
+            __threadfence_system();
+            st_release_sys(&peer->posted, g);
+        }
+    }
+}
+
+__global__ void k_push_wait(PushFlags *me, unsigned long long g, unsigned long long limit_ns)
+{
+    if (threadIdx.x == 0) spin_until(&me->posted, g, limit_ns, &me->err);
+}
 
 struct IpcChannel : Channel {
     static constexpr int S = 4;
     int party = 0, device = 0;
+    bool push = false;
     uint64_t slot_bytes = 0, gen = 0;
     std::string shm_name;
     IpcShared *sh = nullptr;
     uint8_t *arena = nullptr, *peer_arena = nullptr;
+    PushFlags *flags = nullptr, *peer_flags = nullptr;  // push mode
+    unsigned int *h_err = nullptr;                      // pinned mirror of flags->err
+    int push_blocks = 148;
     cudaEvent_t posted[S] = {}, read[S] = {}, peer_posted[S] = {}, peer_read[S] = {};
 
     ~IpcChannel() override
@@ -167,6 +272,9 @@ struct IpcChannel : Channel {
                 std::this_thread::sleep_for(std::chrono::milliseconds(1));
         }
         if (peer_arena) cudaIpcCloseMemHandle(peer_arena);
+        if (peer_flags) cudaIpcCloseMemHandle(peer_flags);
+        if (flags) cudaFree(flags);
+        if (h_err) cudaFreeHost(h_err);
         for (int i = 0; i < S; i++) {
             for (cudaEvent_t e : {posted[i], read[i], peer_posted[i], peer_read[i]})
                 if (e) cudaEventDestroy(e);
@@ -203,12 +311,46 @@ struct IpcChannel : Channel {
         return DDG_OK;
     }
 
+    int exchange_push(int p, cudaStream_t st, const void *send, uint64_t bytes, const void **peer)
+    {
+        DDG_CHECK(bytes % 4 == 0, DDG_ERR_ARG, "IPC push exchange of %llu bytes (not whole 32-bit words)",
+                  (unsigned long long)bytes);
+        const uint64_t g = ++gen;
+        const uint64_t s = (g - 1) % S;
+        const unsigned long long limit = 1000000ull * unsigned(timeout_ms);
+        k_push_gate<<<1, 32, 0, st>>>(flags, peer_flags, g, S, limit);
+        note_launch();
+        const uint64_t words = bytes / 4;
+        const int blocks = words ? int(std::min<uint64_t>(push_blocks, (words + 1023) / 1024)) : 1;
+        k_push_copy<<<blocks, 256, 0, st>>>(static_cast<const uint32_t *>(send),
+                                            reinterpret_cast<uint32_t *>(peer_arena + s * slot_bytes), words, flags,
+                                            peer_flags, g);
+        note_launch();
+        k_push_wait<<<1, 32, 0, st>>>(flags, g, limit);
+        note_launch();
+        DDG_CUDA(cudaGetLastError());
+        *peer = arena + s * slot_bytes;
+        bytes_sent[p] += bytes;
+        rounds[p] += 1;
+        return DDG_OK;
+    }
+
+    int status(int p) override
+    {
+        (void)p;
+        if (!push) return DDG_OK;
+        DDG_CHECK(*reinterpret_cast<volatile unsigned int *>(h_err) == 0, DDG_ERR_PEER,
+                  "IPC push channel: a device-side wait for the peer gave up after %d ms", timeout_ms);
+        return DDG_OK;
+    }
+
     int exchange(int p, cudaStream_t st, const void *send, uint64_t bytes, void *recv, const void **peer) override
     {
         (void)recv;
         const int q = 1 - p;
         DDG_CHECK(bytes <= slot_bytes, DDG_ERR_ARG, "IPC exchange of %llu bytes exceeds the %llu-byte slots",
                   (unsigned long long)bytes, (unsigned long long)slot_bytes);
+        if (push) return exchange_push(p, st, send, bytes, peer);
         DDG_TRY(finish_read(st));  // generation gen (the previous exchange) has been read by work queued on st
         const uint64_t g = ++gen;
         const int s = int((g - 1) % S);
@@ -228,7 +370,7 @@ struct IpcChannel : Channel {
         return DDG_OK;
     }
 
-    bool needs_recv_buffer() const override { return false; }  // the peer's slot is read in place
+    bool needs_recv_buffer() const override { return false; }  // the peer's slot (or this party's) is read in place
 
     int barrier(int p, cudaStream_t st) override
     {
@@ -237,11 +379,14 @@ struct IpcChannel : Channel {
         const void *dummy = nullptr;
         DDG_TRY(exchange(p, st, nullptr, 0, nullptr, &dummy));
         rounds[p] -= 1;
+        // push mode: the device-side waits' verdict, read by status() once the stream has drained
+        if (push) DDG_CUDA(cudaMemcpyAsync(h_err, &flags->err, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
         return DDG_OK;
     }
 };
 
-Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot_bytes, int timeout_ms, int *status)
+Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot_bytes, int timeout_ms, int *status,
+                          bool push)
 {
     *status = DDG_ERR_PEER;
     auto fail = [&](int code, const char *fmt, const char *a) {
@@ -251,6 +396,7 @@ Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot
     };
     if (cudaSetDevice(device) != cudaSuccess) return fail(DDG_ERR_CUDA, "cudaSetDevice failed%s", "");
     auto *c = new IpcChannel();
+    c->push = push;
     c->party = party, c->device = device, c->slot_bytes = (slot_bytes + 255) & ~uint64_t(255);
     c->timeout_ms = timeout_ms;
     c->shm_name = std::string("/") + name;
@@ -309,7 +455,23 @@ Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot
             return fail(DDG_ERR_CUDA, "IPC event creation / export failed%s", "");
         }
     }
-    if (party == 0) sh->slot_bytes = c->slot_bytes;
+    if (push) {
+        // the flags block (zeroed before the peer can see it) and a pinned word for its error flag
+        if (cudaMalloc(&c->flags, sizeof(PushFlags)) != cudaSuccess ||
+            cudaMemset(c->flags, 0, sizeof(PushFlags)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+            cudaIpcGetMemHandle(&sh->flags[party], c->flags) != cudaSuccess ||
+            cudaHostAlloc(reinterpret_cast<void **>(&c->h_err), sizeof(unsigned int), cudaHostAllocDefault) !=
+                cudaSuccess) {
+            c->sh->failed.store(1);  // the peer stops waiting on us
+            delete c;
+            return fail(DDG_ERR_CUDA, "IPC push flags allocation / export failed%s", "");
+        }
+        *c->h_err = 0;
+        cudaDeviceGetAttribute(&c->push_blocks, cudaDevAttrMultiProcessorCount, device);
+    }
+    if (cudaDeviceGetPCIBusId(sh->bus_id[party], sizeof(sh->bus_id[party]), device) != cudaSuccess)
+        sh->bus_id[party][0] = 0;
+    if (party == 0) sh->slot_bytes = c->slot_bytes, sh->push = push ? 1u : 0u;
     sh->ready[party].store(1, std::memory_order_release);
     const auto t1 = std::chrono::steady_clock::now();
     while (!sh->ready[1 - party].load(std::memory_order_acquire)) {
@@ -320,10 +482,16 @@ Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot
         }
         std::this_thread::sleep_for(std::chrono::milliseconds(1));
     }
-    if (sh->slot_bytes != c->slot_bytes) {
+    if (sh->slot_bytes != c->slot_bytes || sh->push != (push ? 1u : 0u)) {
         c->sh->failed.store(1);  // the peer stops waiting on us
         delete c;
-        return fail(DDG_ERR_ARG, "the two parties asked for different IPC slot sizes%s", "");
+        return fail(DDG_ERR_ARG, "the two parties asked for different IPC slot sizes or modes%s", "");
+    }
+    if (push && std::strncmp(sh->bus_id[0], sh->bus_id[1], sizeof(sh->bus_id[0])) == 0) {
+        c->sh->failed.store(1);
+        delete c;
+        return fail(DDG_ERR_ARG, "IPC push mode needs the two parties on different GPUs (both on %s)",
+                    sh->bus_id[party]);
     }
     const int q = 1 - party;
     void *pa = nullptr;
@@ -333,6 +501,15 @@ Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot
         return fail(DDG_ERR_CUDA, "cannot map the peer's IPC arena (are both GPUs on this node?)%s", "");
     }
     c->peer_arena = static_cast<uint8_t *>(pa);
+    if (push) {
+        void *pf = nullptr;
+        if (cudaIpcOpenMemHandle(&pf, sh->flags[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            c->sh->failed.store(1);
+            delete c;
+            return fail(DDG_ERR_CUDA, "cannot map the peer's IPC push flags%s", "");
+        }
+        c->peer_flags = static_cast<PushFlags *>(pf);
+    }
     for (int i = 0; i < S; i++) {
         if (cudaIpcOpenEventHandle(&c->peer_posted[i], sh->ev_posted[q][i]) != cudaSuccess ||
             cudaIpcOpenEventHandle(&c->peer_read[i], sh->ev_read[q][i]) != cudaSuccess) {

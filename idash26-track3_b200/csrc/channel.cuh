@@ -32,6 +32,9 @@ struct Channel {
     // for all work the peer queued before it
     virtual int barrier(int party, cudaStream_t st) = 0;
     virtual bool same_device() const { return false; }
+    // errors the channel's own device-side waits recorded (read after the
+    // party's stream has drained); DDG_OK for channels without device waits
+    virtual int status(int party) { (void)party; return DDG_OK; }
     // exchange() needs the caller's `recv` buffer (it copies the peer's bytes there)
     virtual bool needs_recv_buffer() const { return !same_device(); }
     uint64_t bytes_sent[2] = {0, 0};
@@ -84,7 +87,12 @@ struct CallbackChannel : Channel {
 Channel *make_nccl_channel(const void *unique_id, int nranks, int rank, int peer_rank, int device, int *status);
 // CUDA-IPC channel between two party processes on one node (channel.cu); both
 // call it with the same `name` (a POSIX shared-memory name, no slash)
-Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot_bytes, int timeout_ms, int *status);
+// push = true: each party's kernels write its share into the peer's receive
+// slot (peer stores over NVLink) and raise a flag in the peer's memory; the
+// consumer waits for the flag on the device and reads its own HBM (no host
+// wait per opening).  Needs the two parties on different GPUs.
+Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot_bytes, int timeout_ms, int *status,
+                          bool push = false);
 int nccl_unique_id(void *out128);
 
 }  // namespace ddg

@@ -242,6 +242,7 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
         e.err = DDG_ERR_CUDA;
     }
     if (e.err == DDG_OK) e.err = ring_gemm_tc_check(P.stream);
+    if (e.err == DDG_OK) e.err = P.chan->status(P.party);  // the channel's device-side waits
     // the caller may reuse its host buffers once this returns
     if (P.copy_stream) {
         ce = cudaStreamSynchronize(P.copy_stream);

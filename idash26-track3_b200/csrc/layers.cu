@@ -112,6 +112,7 @@ int run_eval(ddg_party *h, ddg_cursor *cur, int batch, F &&body)
         e.err = DDG_ERR_CUDA;
     }
     if (e.err == DDG_OK) e.err = ring_gemm_tc_check(P.stream);
+    if (e.err == DDG_OK) e.err = P.chan->status(P.party);
     if (e.err != DDG_OK) {
         if (auto *lp = dynamic_cast<LocalPairChannel *>(P.chan)) lp->fail();
         return e.err;

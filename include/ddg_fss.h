@@ -223,6 +223,17 @@ int ddg_party_connect_nccl(ddg_party *party, const void *unique_id128, int nrank
  * Waits on the peer are bounded by the party's timeout (ddg_party_set_timeout
  * before connecting, default 60 s) and end in DDG_ERR_PEER. */
 int ddg_party_connect_ipc(ddg_party *party, const char *name, uint64_t slot_bytes);
+/* The same two-process channel with the handoff on the device (push mode):
+ * each party's kernels write its share into the peer's receive slot with
+ * peer stores over NVLink and raise a flag in the peer's memory; the
+ * consumer's one-thread kernel waits for that flag and the consumers read
+ * their own HBM.  No host thread waits per opening, so a party's host thread
+ * enqueues the whole forward ahead of the GPU.  Needs the two parties on
+ * different GPUs of one node (refused otherwise: kernels that wait on each
+ * other never share a GPU).  A device-side wait that exceeds the party's
+ * timeout ends the forward with DDG_ERR_PEER.  Both parties must connect in
+ * the same mode. */
+int ddg_party_connect_ipc_push(ddg_party *party, const char *name, uint64_t slot_bytes);
 /* Diagnostics: `iters` openings of `bytes` through the party's channel (a
  * memset as producer, a one-thread read of the peer's bytes as consumer),
  * both parties calling it together; ms per opening from CUDA events on the

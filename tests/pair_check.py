@@ -4,7 +4,8 @@ Launched with torchrun (see tests/test_multigpu_gpu.py).  Both ranks run the
 GPU dealer with the same seed (so they hold matching keys), take their own
 party's shares of the same seeded inputs, open every value over the channel
 named by DDG_CHECK_COMM (nccl: ncclSend/ncclRecv; ipc: CUDA-IPC send slots
-read in place), and rank 0 compares the revealed outputs of several forwards
+read in place; ipc-push: peer stores into the consumer's receive slots and
+device-side flags), and rank 0 compares the revealed outputs of several forwards
 with the integer oracle.  Exits non-zero on any mismatch.
 """
 import datetime
@@ -44,10 +45,10 @@ def main():
     P.set_weights(blob)
     P.bind_keys((k0 if rank == 0 else k1).data_ptr(), kb)
     P.set_timeout(120_000)
-    if comm == "ipc":
+    if comm in ("ipc", "ipc-push"):
         uid = [f"ddg_check_{uuid.uuid4().hex[:16]}" if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        P.connect_ipc(uid[0], ddg.forward_max_exchange_bytes(bw, s, B))
+        P.connect_ipc(uid[0], ddg.forward_max_exchange_bytes(bw, s, B), push=comm == "ipc-push")
     else:
         uid = [ddg.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)

@@ -1,4 +1,5 @@
-"""Openings over NCCL and over CUDA IPC between two processes on two GPUs (skipped with fewer GPUs)."""
+"""Openings over NCCL and over CUDA IPC (host handoffs, and device-side handoffs with peer stores)
+between two processes on two GPUs (skipped with fewer GPUs)."""
 import os
 import subprocess
 import sys
@@ -9,7 +10,7 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("comm", ["nccl", "ipc"])
+@pytest.mark.parametrize("comm", ["nccl", "ipc", "ipc-push"])
 @pytest.mark.parametrize("bw", ["32", "64"])
 def test_pair_forward_bit_exact(cuda, bw, comm):
     if cuda.cuda.device_count() < 2:
