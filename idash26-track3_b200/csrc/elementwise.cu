@@ -171,12 +171,75 @@ __global__ void k_pool_split(const T *cur, T *even, T *diff, int B, int cnt, int
     }
 }
 
+// 16-byte vector forms of the max-pool level kernels: a row of F ring words is
+// F / L vectors (L = 4 for Z_2^32, 2 for Z_2^64), and a thread finds its row
+// and vector with two 32-bit divisions per 16 bytes instead of 64-bit
+// divisions per element.  Used when F is a multiple of L, the buffers are
+// 16-byte aligned and the vector count fits 32 bits.
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<uint32_t> {
+    using V = uint4;
+    static constexpr int L = 4;
+    __device__ static V add(V a, V b) { return make_uint4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+    __device__ static V sub(V a, V b) { return make_uint4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w); }
+};
+template <>
+struct Vec16<uint64_t> {
+    using V = ulonglong2;
+    static constexpr int L = 2;
+    __device__ static V add(V a, V b) { return make_ulonglong2(a.x + b.x, a.y + b.y); }
+    __device__ static V sub(V a, V b) { return make_ulonglong2(a.x - b.x, a.y - b.y); }
+};
+
+template <typename T>
+__global__ void k_pool_split_v(const typename Vec16<T>::V *cur, typename Vec16<T>::V *even,
+                               typename Vec16<T>::V *diff, uint32_t pairs, uint32_t cnt, uint32_t fv, uint32_t nvec)
+{
+    using W = Vec16<T>;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += gridDim.x * blockDim.x) {
+        const uint32_t row = t / fv, c = t - row * fv;
+        const uint32_t b = row / pairs, p = row - b * pairs;
+        const uint64_t src = (uint64_t(b) * cnt + 2 * p) * fv + c;
+        const typename W::V ev = cur[src], od = cur[src + fv];
+        even[t] = ev;
+        diff[t] = W::sub(od, ev);
+    }
+}
+
+template <typename T>
+__global__ void k_pool_merge_v(const typename Vec16<T>::V *even, const typename Vec16<T>::V *relu,
+                               const typename Vec16<T>::V *cur, typename Vec16<T>::V *next, uint32_t pairs,
+                               uint32_t cnt, uint32_t fv, uint32_t nvec)
+{
+    using W = Vec16<T>;
+    const uint32_t nxt = pairs + (cnt & 1);
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += gridDim.x * blockDim.x) {
+        const uint32_t row = t / fv, c = t - row * fv;
+        const uint32_t b = row / nxt, q = row - b * nxt;
+        next[t] = q < pairs ? W::add(even[(uint64_t(b) * pairs + q) * fv + c], relu[(uint64_t(b) * pairs + q) * fv + c])
+                            : cur[(uint64_t(b) * cnt + (cnt - 1)) * fv + c];
+    }
+}
+
+inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 template <typename T>
 int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st)
 {
     const uint64_t n = uint64_t(B) * (cnt / 2) * F;
     if (!n) return DDG_OK;
-    k_pool_split<T><<<ew_grid(n), 256, 0, st>>>(cur, even, diff, B, cnt, F);
+    constexpr int L = Vec16<T>::L;
+    if (F % L == 0 && n / L < (1ull << 31) && al16(cur) && al16(even) && al16(diff)) {
+        using V = typename Vec16<T>::V;
+        const uint32_t nvec = uint32_t(n / L);
+        k_pool_split_v<T><<<ew_grid(nvec), 256, 0, st>>>(reinterpret_cast<const V *>(cur), reinterpret_cast<V *>(even),
+                                                         reinterpret_cast<V *>(diff), uint32_t(cnt / 2), uint32_t(cnt),
+                                                         uint32_t(F / L), nvec);
+    } else {
+        k_pool_split<T><<<ew_grid(n), 256, 0, st>>>(cur, even, diff, B, cnt, F);
+    }
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
@@ -209,7 +272,16 @@ int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int c
 {
     const uint64_t n = uint64_t(B) * (cnt / 2 + (cnt & 1)) * F;
     if (!n) return DDG_OK;
-    k_pool_merge<T><<<ew_grid(n), 256, 0, st>>>(even, relu, cur, next, B, cnt, F);
+    constexpr int L = Vec16<T>::L;
+    if (F % L == 0 && n / L < (1ull << 31) && al16(even) && al16(relu) && al16(cur) && al16(next)) {
+        using V = typename Vec16<T>::V;
+        const uint32_t nvec = uint32_t(n / L);
+        k_pool_merge_v<T><<<ew_grid(nvec), 256, 0, st>>>(
+            reinterpret_cast<const V *>(even), reinterpret_cast<const V *>(relu), reinterpret_cast<const V *>(cur),
+            reinterpret_cast<V *>(next), uint32_t(cnt / 2), uint32_t(cnt), uint32_t(F / L), nvec);
+    } else {
+        k_pool_merge<T><<<ew_grid(n), 256, 0, st>>>(even, relu, cur, next, B, cnt, F);
+    }
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
