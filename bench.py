@@ -694,6 +694,7 @@ def main():
     ks_before = [ks.stats() for ks in streams]
     for p in parties:
         p.enable_dcf_timing(True)
+    graph_ok = False
     if colo and uses_graph(a):
         # capture after the warm-up forwards (one-time set-up done), with the
         # comparison-kernel timing on, so that every replay records its launches
@@ -701,6 +702,7 @@ def main():
             graph[0] = ddg.ForwardGraph(parties[0], parties[1], B, [t.data_ptr() for t in bufs[0][0]],
                                         [t.data_ptr() for t in bufs[1][0]])
             outs["graph_replay"] = graph[0].launch()  # untimed: the first replay uploads the graph
+            graph_ok = True
         except Exception as ex:  # noqa: BLE001 -- any capture failure falls back to host launches
             # a failed capture may leave the pair's channel marked failed: pair the
             # parties again and launch from the host, and say so in config.launch
@@ -751,13 +753,35 @@ def main():
         o = step(True)
         if colo and not streams:
             outs["e2e_forward"] = o
-        ms_e2e = timed(True, a.steps)
+        e2e_graph = None
+        if uses_graph(a) and graph_ok:
+            # the same forward with the pinned host inputs captured too: every
+            # replay copies both parties' input shares host -> device
+            try:
+                e2e_graph = ddg.ForwardGraph(parties[0], parties[1], B, [t.data_ptr() for t in bufs[0][1]],
+                                             [t.data_ptr() for t in bufs[1][1]], on_host=True)
+                outs["e2e_graph_replay"] = e2e_graph.launch()
+                graph[0] = e2e_graph
+            except Exception as ex:  # noqa: BLE001 -- fall back to host launches for the e2e steps
+                print(f"bench: host-input graph capture failed ({ex}); e2e with host launches", file=sys.stderr)
+                if e2e_graph is not None:
+                    e2e_graph.close()
+                e2e_graph = None
+                ddg.pair_local(parties[0], parties[1])
+                step(True)
+        ms_e2e = timed(True, a.steps) if e2e_graph is None else timed(False, a.steps)
+        if e2e_graph is not None:
+            e2e_graph.close()
+            graph[0] = None
         # both parties' input shares of every pair cross host->device each step
         own = [sum(int(t.numel()) for t in b[1]) for b in bufs]
         h2d = sum(own) if colo else 2 * sum(own)
         e2e = {"value": pairs * B * a.steps / (ms_e2e / 1e3), "unit": "samples/s",
                "h2d_bytes_per_step": h2d * pairs, "d2h_bytes_per_step": B * (bw // 8) * pairs,
-               "ms_per_step": ms_e2e / a.steps, "h2d_probe_gbs": h2d_probe(torch, bufs, device)}
+               "ms_per_step": ms_e2e / a.steps, "h2d_probe_gbs": h2d_probe(torch, bufs, device),
+               "launch": ("CUDA graph of both parties' forward with the host->device copies of their pinned input "
+                          "shares and the output read-back, replayed every step" if e2e_graph is not None
+                          else "host launches every step")}
 
     value = pairs * B * a.steps / (ms / 1e3)
     peak, peak_kind = measured_peaks()

@@ -116,6 +116,8 @@ SIGNATURES = {
     "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
     "ddg_forward_graph_create": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                         ctypes.POINTER(_vp)]),
+    "ddg_forward_graph_create_ex": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32,
+                                           ctypes.POINTER(_vp)]),
     "ddg_forward_graph_launch": (_i32, [_vp, _vp, _vp]),
     "ddg_forward_graph_destroy": (_i32, [_vp]),
     "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
@@ -410,12 +412,13 @@ class ForwardGraph:
     ordinary forward_pair of the pair before creating it, and close it before
     the parties."""
 
-    def __init__(self, p0: Party, p1: Party, batch, inputs0, inputs1):
+    def __init__(self, p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
+        """on_host: inputs are pinned host buffers copied in by every replay."""
         self.batch = batch
         a0 = (_vp * 4)(*inputs0)
         a1 = (_vp * 4)(*inputs1)
         h = _vp()
-        check(lib().ddg_forward_graph_create(p0.h, p1.h, batch, a0, a1, ctypes.byref(h)))
+        check(lib().ddg_forward_graph_create_ex(p0.h, p1.h, batch, a0, a1, int(on_host), ctypes.byref(h)))
         self.h = h
 
     def launch(self, outputs=True):

@@ -504,6 +504,12 @@ static void adopt_timing(Party &P, std::vector<DcfTiming::Rec> &dst)
 int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
                              ddg_forward_graph **out)
 {
+    return ddg_forward_graph_create_ex(p0, p1, batch, in0, in1, 0, out);
+}
+
+int ddg_forward_graph_create_ex(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0,
+                                const void *const *in1, int on_host, ddg_forward_graph **out)
+{
     DDG_CHECK(p0 && p1 && in0 && in1 && out && batch > 0, DDG_ERR_ARG, "bad argument");
     *out = nullptr;
     DDG_CHECK(p0->P.device == p1->P.device && p0->P.chan && p0->P.chan == p1->P.chan &&
@@ -516,6 +522,7 @@ int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void
     for (ddg_party *p : {p0, p1}) {
         DDG_CHECK(!p->P.graph_recs, DDG_ERR_STATE, "party %d already has a forward graph", p->P.party);
         DDG_TRY(settle_timing(p->P));  // pending host-forward launches are read back first
+        if (on_host) DDG_TRY(prepare_host_inputs(p->P, batch));  // no allocation inside the capture
     }
     auto *g = new ddg_forward_graph;
     g->p0 = p0, g->p1 = p1, g->batch = batch;
@@ -551,10 +558,10 @@ int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void
         int st1 = DDG_OK;
         std::string err1;
         std::thread t([&] {
-            st1 = forward_capture(p1->P, batch, in1[0], in1[1], in1[2], in1[3], nullptr);
+            st1 = forward_capture(p1->P, batch, in1[0], in1[1], in1[2], in1[3], nullptr, on_host != 0);
             if (st1 != DDG_OK) err1 = ddg::last_error();
         });
-        st = forward_capture(p0->P, batch, in0[0], in0[1], in0[2], in0[3], g->d_out);
+        st = forward_capture(p0->P, batch, in0[0], in0[1], in0[2], in0[3], g->d_out, on_host != 0);
         if (st != DDG_OK) {
             if (auto *lp = dynamic_cast<LocalPairChannel *>(p0->P.chan)) lp->fail();
         }

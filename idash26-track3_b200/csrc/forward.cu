@@ -360,15 +360,26 @@ int parties_dcf_union(Party *const *ps, int n)
     return DDG_OK;
 }
 
+int prepare_host_inputs(Party &P, int B)
+{
+    const uint64_t es = P.bw / 8;
+    const uint64_t sizes[4] = {uint64_t(B) * NMAX * FEAT, uint64_t(B) * NMAX * NMAX, uint64_t(B) * NMAX * POOL,
+                               uint64_t(B) * PROT};
+    DDG_CUDA(cudaSetDevice(P.device));
+    DDG_TRY(P.ensure_copy_stream());
+    for (int i = 0; i < 4; i++) DDG_TRY(P.ensure_input(i, sizes[i] * es));
+    return DDG_OK;
+}
+
 int forward_capture(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
-                    void *d_out)
+                    void *d_out, bool on_host)
 {
     DDG_CHECK(P.chan, DDG_ERR_STATE, "party %d has no channel", P.party);
     DDG_CHECK(P.keys, DDG_ERR_STATE, "party %d has no keys bound", P.party);
     DDG_CHECK(P.w.table, DDG_ERR_STATE, "party %d has no weights", P.party);
     DDG_CUDA(cudaSetDevice(P.device));
-    return P.bw == 32 ? eval_t<uint32_t>(P, B, x_sh, adj_sh, mask_sh, prot_sh, false, nullptr, nullptr, true, d_out)
-                      : eval_t<uint64_t>(P, B, x_sh, adj_sh, mask_sh, prot_sh, false, nullptr, nullptr, true, d_out);
+    return P.bw == 32 ? eval_t<uint32_t>(P, B, x_sh, adj_sh, mask_sh, prot_sh, on_host, nullptr, nullptr, true, d_out)
+                      : eval_t<uint64_t>(P, B, x_sh, adj_sh, mask_sh, prot_sh, on_host, nullptr, nullptr, true, d_out);
 }
 
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,

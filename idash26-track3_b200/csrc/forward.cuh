@@ -86,11 +86,15 @@ int reset_timing(Party &P, bool on);
 int parties_dcf_union(Party *const *ps, int n);
 int forward_eval(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
                  bool on_host, int64_t *h_out_raw, double *h_aff);
-// enqueue one forward of device-resident inputs on P.stream while it is being
-// captured into a CUDA graph: the revealed output (party 0) goes to d_out, and
-// nothing waits for the device (the caller ends the capture and replays it)
+// enqueue one forward on P.stream while it is being captured into a CUDA
+// graph: the revealed output (party 0) goes to d_out, and nothing waits for
+// the device (the caller ends the capture and replays it).  on_host: the
+// inputs are pinned host buffers, copied on the party's copy stream (which
+// joins the capture) into its staging buffers (prepare_host_inputs first)
 int forward_capture(Party &P, int B, const void *x_sh, const void *adj_sh, const void *mask_sh, const void *prot_sh,
-                    void *d_out);
+                    void *d_out, bool on_host = false);
+// the party's copy stream and device staging buffers of B samples' inputs
+int prepare_host_inputs(Party &P, int B);
 int dealer_forward(int bw, int s, int B, uint64_t seed, const DevWeights &w, uint8_t *k0, uint8_t *k1,
                    cudaStream_t st);
 

@@ -282,6 +282,13 @@ int ddg_forward_eval_pair(ddg_party *p0, ddg_party *p1, int batch, const void *c
 typedef struct ddg_forward_graph ddg_forward_graph;
 int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0, const void *const *in1,
                              ddg_forward_graph **out);
+/* The same with on_host != 0: in0 / in1 are pinned host buffers (page-locked,
+ * cudaHostAlloc or registered; the same addresses at every replay), and every
+ * replay copies them host -> device on each party's copy stream, each input
+ * ahead of its first use, as ddg_forward_eval_pair with on_host does; the
+ * staging buffers are allocated before the capture. */
+int ddg_forward_graph_create_ex(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0,
+                                const void *const *in1, int on_host, ddg_forward_graph **out);
 int ddg_forward_graph_launch(ddg_forward_graph *graph, int64_t *h_out_raw, double *h_affinity);
 int ddg_forward_graph_destroy(ddg_forward_graph *graph);
 /* GPU dealer (replaces DDGOrcaKeygenBatched + ddgSecureAdjNormKeygen,

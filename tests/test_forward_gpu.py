@@ -306,3 +306,38 @@ def test_forward_graph_timing_readouts_follow_replays(ddg, synth, cuda):
         g.close()
         for p in (p0, p1):
             p.enable_dcf_timing(False)
+
+
+@pytest.mark.gpu
+def test_forward_graph_with_pinned_host_inputs(ddg, synth, cuda):
+    """A graph captured with host inputs (ddg_forward_graph_create_ex, on_host):
+    every replay copies the pinned input shares in and reveals the oracle's
+    outputs; new values written into the same pinned buffers between replays
+    are picked up (the copies are part of the replay)."""
+    import torch
+
+    bw, B = 32, 3
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=91)
+    inps = [synth.Inputs(B, bw, seed=sd, with_protein_cnn=False) for sd in (51, 52)]
+
+    def pinned(inp):
+        return [[torch.from_numpy(np.ascontiguousarray(a[p]).view(np.uint8).copy()).pin_memory()
+                 for a in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)] for p in (0, 1)]
+
+    bufs = pinned(inps[0])
+    ptrs = [[t.data_ptr() for t in bufs[p]] for p in (0, 1)]
+    raw, aff = ddg.forward_pair(p0, p1, B, ptrs[0], ptrs[1], on_host=True)  # one-time set-up
+    g = ddg.ForwardGraph(p0, p1, B, ptrs[0], ptrs[1], on_host=True)
+    try:
+        for k, inp in enumerate(inps):
+            if k:
+                new = pinned(inp)
+                for p in (0, 1):
+                    for dst, src in zip(bufs[p], new[p]):
+                        dst.copy_(src)
+            want_raw, want_aff = expected(inp, q, bw)
+            for _ in range(2):
+                raw, aff = g.launch()
+                assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)) and np.array_equal(aff, want_aff)
+    finally:
+        g.close()
