@@ -34,7 +34,11 @@ def _init(rank, world, port, timeout_s=30):
 def _worker_layout(rank, world, port, q):
     import torch
 
-    _init(rank, world, port)
+    try:
+        _init(rank, world, port)
+    except Exception as e:  # noqa: BLE001 -- reported, so the test retries on another port
+        q.put(("setup failed", rank, type(e).__name__))
+        os._exit(1)
     pairs, pair, party, peer = bench.roles(rank, world)
     # one id per party pair (and lane), as bench.py broadcasts them
     uids = [[[os.urandom(128) for _ in range(1)] for _ in range(pairs)] if rank == 0 else None]
@@ -60,17 +64,34 @@ def test_roles_layout():
         bench.roles(0, 3)
 
 
-def test_gloo_world2_layout_broadcast_and_max():
+def _spawn_world2(target, nmsg, tries=3):
+    """Start the two ranks on a fresh port; a rank that cannot set up the
+    process group (the port was taken meanwhile) reports it, and the pair is
+    started again on another port.  Returns the ranks' messages."""
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    ps = [ctx.Process(target=_worker_layout, args=(r, 2, port, q)) for r in range(2)]
+    for attempt in range(tries):
+        q = ctx.Queue()
+        port = _free_port()
+        ps = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+        for p in ps:
+            p.start()
+        got = [q.get(timeout=120) for _ in range(nmsg)]
+        for p in ps:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+        failed = [m for m in got if isinstance(m, tuple) and m and m[0] == "setup failed"]
+        if not failed or attempt == tries - 1:
+            return got, ps
+    return got, ps
+
+
+def test_gloo_world2_layout_broadcast_and_max():
+    got, ps = _spawn_world2(_worker_layout, 2)
+    assert not any(m[0] == "setup failed" for m in got), got
     for p in ps:
-        p.start()
-    got = sorted(q.get(timeout=120) for _ in range(2))
-    for p in ps:
-        p.join(timeout=60)
         assert p.exitcode == 0
+    got = sorted(got)
     (r0, pairs0, pair0, party0, peer0, u0, m0), (r1, pairs1, pair1, party1, peer1, u1, m1) = got
     assert (party0, party1) == (0, 1) and (peer0, peer1) == (1, 0) and pair0 == pair1 == 0
     assert u0 == u1 and m0 == m1 == 11.0
@@ -81,7 +102,7 @@ def _worker_dies(rank, world, port, q):
         _init(rank, world, port, timeout_s=5)
         dist.barrier()  # both ranks are connected before one of them dies
     except Exception as e:  # noqa: BLE001
-        q.put("setup failed: " + type(e).__name__)
+        q.put(("setup failed", rank, type(e).__name__))
         os._exit(1)
     if rank == 1:
         os._exit(3)  # the peer dies before the next collective
@@ -94,13 +115,6 @@ def _worker_dies(rank, world, port, q):
 
 
 def test_dead_peer_is_detected_not_hung():
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    ps = [ctx.Process(target=_worker_dies, args=(r, 2, port, q)) for r in range(2)]
-    for p in ps:
-        p.start()
-    msg = q.get(timeout=120)
-    for p in ps:
-        p.join(timeout=60)
-    assert msg.startswith("error"), msg
+    got, ps = _spawn_world2(_worker_dies, 1)
+    msg = got[0]
+    assert isinstance(msg, str) and msg.startswith("error"), msg
