@@ -102,7 +102,7 @@ def parse():
                          "(openings stay on the device; weak scaling with the per-GPU work of N=1); split = party 0 "
                          "on ranks 0..N/2-1, party 1 on the others, pair i = (i, N/2+i), openings over NVLink "
                          "(--comm)")
-    ap.add_argument("--peer-timeout", type=int, default=600,
+    ap.add_argument("--peer-timeout", type=int, default=120,
                     help="N>1: seconds a party waits for its peer at one opening before giving up")
     ap.add_argument("--comm", default="ipc-push", choices=["ipc-push", "ipc", "nccl"],
                     help="N>1, split layout: openings between the two parties of a pair over CUDA IPC with the "

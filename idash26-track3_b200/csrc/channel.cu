@@ -168,6 +168,15 @@ struct IpcShared {
 // the party's timeout: one that gives up sets `err`, which the host reads
 // after the forward (status()).  Both parties must be on different GPUs:
 // kernels that wait on one another are never launched on one GPU.
+// Step 3 is enqueued only once the peer's host has enqueued its steps 1-2 of
+// generation g (the shared `posted` counters, published at enqueue time; the
+// previous exchange's step 3 covers the gate's wait on g-S+1 <= g-1).  Every
+// device-side wait therefore depends on work that is already queued on the
+// peer's GPU, never on a launch still to come from the peer's host: a
+// context-wide synchronisation on either GPU (a cudaMalloc or cudaFree, a
+// kernel's first launch under lazy module loading) taken by another thread of
+// the process, e.g. a second party of the same GPU, always drains instead of
+// closing a cycle through the peer's host.
 struct PushFlags {
     unsigned long long posted;     // the peer's last generation in this party's receive slots
     unsigned long long consumed;   // this party's last generation that the peer has consumed
@@ -326,6 +335,8 @@ struct IpcChannel : Channel {
                                             reinterpret_cast<uint32_t *>(peer_arena + s * slot_bytes), words, flags,
                                             peer_flags, g);
         note_launch();
+        sh->posted[p].store(g, std::memory_order_release);
+        DDG_TRY(wait_for(sh->posted[1 - p], g, "enqueue of generation"));
         k_push_wait<<<1, 32, 0, st>>>(flags, g, limit);
         note_launch();
         DDG_CUDA(cudaGetLastError());

@@ -6,7 +6,11 @@ party's shares of the same seeded inputs, open every value over the channel
 named by DDG_CHECK_COMM (nccl: ncclSend/ncclRecv; ipc: CUDA-IPC send slots
 read in place; ipc-push: peer stores into the consumer's receive slots and
 device-side flags), and rank 0 compares the revealed outputs of several forwards
-with the integer oracle.  Exits non-zero on any mismatch.
+with the integer oracle.  With DDG_CHECK_LANES=L > 1 every rank holds L
+parties (lanes), each with its own keys, inputs and channel to the matching
+lane of the other rank, and runs their forwards concurrently from L host
+threads, as the split bench layout with --lanes does.  Exits non-zero on any
+mismatch.
 """
 import datetime
 import importlib
@@ -34,39 +38,52 @@ def main():
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     bw, B, s = int(os.environ.get("DDG_CHECK_BW", "32")), 3, 12
     comm = os.environ.get("DDG_CHECK_COMM", "nccl")
+    lanes = int(os.environ.get("DDG_CHECK_LANES", "1"))
     q = synth.quantize_weights(synth.affinity_weights(5), s)
     blob = synth.weights_blob(q)
     kb = ddg.forward_key_bytes(bw, s, B)
-    k0 = torch.empty(kb, dtype=torch.uint8, device=dev)
-    k1 = torch.empty(kb, dtype=torch.uint8, device=dev)
-    ddg.dealer_forward(bw, s, B, 31, blob, local, k0.data_ptr(), k1.data_ptr())
-    inp = synth.Inputs(B, bw, seed=44, with_protein_cnn=False)
-    P = ddg.Party(rank, bw, s, local)
-    P.set_weights(blob)
-    P.bind_keys((k0 if rank == 0 else k1).data_ptr(), kb)
-    P.set_timeout(120_000)
     if comm in ("ipc", "ipc-push"):
-        uid = [f"ddg_check_{uuid.uuid4().hex[:16]}" if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        P.connect_ipc(uid[0], ddg.forward_max_exchange_bytes(bw, s, B), push=comm == "ipc-push")
+        uid = [[f"ddg_check_{uuid.uuid4().hex[:16]}_{l}" for l in range(lanes)] if rank == 0 else None]
     else:
-        uid = [ddg.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        P.connect_nccl(uid[0], 2, rank, 1 - rank)
-    bufs = [torch.from_numpy(np.ascontiguousarray(a[rank]).view(np.uint8).copy()).to(dev)
-            for a in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)]
+        uid = [[ddg.nccl_unique_id() for _ in range(lanes)] if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    parties, inps, keep = [], [], []
+    for lane in range(lanes):
+        k0 = torch.empty(kb, dtype=torch.uint8, device=dev)
+        k1 = torch.empty(kb, dtype=torch.uint8, device=dev)
+        ddg.dealer_forward(bw, s, B, 31 + lane, blob, local, k0.data_ptr(), k1.data_ptr())
+        inp = synth.Inputs(B, bw, seed=44 + lane, with_protein_cnn=False)
+        P = ddg.Party(rank, bw, s, local)
+        P.set_weights(blob)
+        P.bind_keys((k0 if rank == 0 else k1).data_ptr(), kb)
+        P.set_timeout(120_000)
+        if comm in ("ipc", "ipc-push"):
+            P.connect_ipc(uid[0][lane], ddg.forward_max_exchange_bytes(bw, s, B), push=comm == "ipc-push")
+        else:
+            P.connect_nccl(uid[0][lane], 2, rank, 1 - rank)
+        bufs = [torch.from_numpy(np.ascontiguousarray(a[rank]).view(np.uint8).copy()).to(dev)
+                for a in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)]
+        parties.append(P)
+        inps.append(inp)
+        keep.append((k0, k1, bufs))
+    ins = [[b.data_ptr() for b in k[2]] for k in keep]
     # every forward reuses the IPC send slots many times over (dozens of
     # openings, four slots) and starts where the previous one left them; the
     # same keys and shares give the same outputs every time
-    outs = [P.forward(B, *[b.data_ptr() for b in bufs])[1] for _ in range(3)]
+    if lanes == 1:
+        outs = [[parties[0].forward(B, *ins[0])[1]] for _ in range(3)]
+    else:
+        outs = [[o[1] for o in ddg.forward_lanes(parties, B, ins)] for _ in range(3)]
     ok = 1
     if rank == 0:
-        want_raw, want_aff = RF.protocol_forward(inp.x_ring, inp.adj_ring, inp.mask_ring, inp.protein_ring, q, bw, s)
-        ok = int(all(np.array_equal(aff, want_aff) for aff in outs))
-        print(f"{comm} pair", "OK" if ok else f"MISMATCH {outs} vs {want_aff}", P.stats(), flush=True)
+        want = [RF.protocol_forward(i.x_ring, i.adj_ring, i.mask_ring, i.protein_ring, q, bw, s)[1] for i in inps]
+        ok = int(all(np.array_equal(o[l], want[l]) for o in outs for l in range(lanes)))
+        tag = f"{comm} pair" + (f" x{lanes} lanes" if lanes > 1 else "")
+        print(tag, "OK" if ok else f"MISMATCH {outs} vs {want}", parties[0].stats(), flush=True)
     flag = torch.tensor([ok])
     dist.broadcast(flag, src=0)
-    P.close()
+    for P in parties:
+        P.close()
     dist.destroy_process_group()
     sys.exit(0 if int(flag.item()) else 1)
 

@@ -21,3 +21,21 @@ def test_pair_forward_bit_exact(cuda, bw, comm):
                         os.path.join(REPO, "tests", "pair_check.py")], env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert f"{comm} pair OK" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("comm", ["ipc", "ipc-push"])
+def test_two_lanes_per_rank_bit_exact(cuda, comm):
+    """Two parties per process (lanes), each paired with the other rank's lane
+    over its own channel, forwards run concurrently from two host threads: the
+    device-side waits of one lane never wait on a launch that the peer's host
+    has still to make, so a context-wide synchronisation taken by the other
+    lane (a first launch, an allocation) drains."""
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, DDG_CHECK_BW="32", DDG_CHECK_COMM=comm, DDG_CHECK_LANES="2", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29532",
+                        os.path.join(REPO, "tests", "pair_check.py")], env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert f"{comm} pair x2 lanes OK" in r.stdout
