@@ -207,16 +207,21 @@ def config_of(a, n_gpus):
         "aes": f"T-table AES, {a.aes_tables} round tables staged in shared memory",
         "relu_split": a.relu_split,
         "relu_backend": a.relu_backend,
-        "launch": ("CUDA graph: both parties' forward captured once, replayed every timed step"
-                   if uses_graph(a) else "host launches every step"),
+        "launch": (("CUDA graph: both parties' forward captured once, replayed every timed step"
+                    if a.layout == "colocated" or n_gpus == 1 else
+                    "CUDA graph: each rank's own party forward captured once, replayed every timed step "
+                    "(handoffs on the device)") if uses_graph(a) else "host launches every step"),
         "l2": "inputs larger than L2: every step streams each party's full key region (GBs; "
               "key_bytes_per_party_per_step in the line)",
     }
 
 
 def uses_graph(a):
-    """The timed forwards replay a CUDA graph: colocated pairs with resident keys only."""
-    return a.graph == "on" and a.layout == "colocated" and not a.stream
+    """The timed forwards replay a CUDA graph: colocated pairs, or split parties
+    over push-mode IPC with one lane per rank, resident keys only."""
+    if a.graph != "on" or a.stream:
+        return False
+    return a.layout == "colocated" or (a.comm == "ipc-push" and a.lanes == 1)
 
 
 # ------------------------------------------------------------------ clocks
@@ -521,15 +526,26 @@ def subrecord_split(a, ddg, synth, torch, dist, rank, world, local, device, push
     P.connect_ipc(names[0][pair], ddg.forward_max_exchange_bytes(bw, s, B), push=push)
     buf = share_buffers(torch, inp, party, device)
     ins = [t.data_ptr() for t in buf[0]]
+    o = None
     for _ in range(a.warmup):
-        P.forward(B, *ins)
+        o = P.forward(B, *ins)
+    # push mode: every handoff happens on the device, so each rank replays its
+    # own party's forward from a CUDA graph (both ranks alike)
+    g, agree = None, None
+    if push and a.graph == "on":
+        g = ddg.ForwardGraph(P, None, B, ins)
+        og = g.launch()  # untimed: the first replay uploads the graph
+        agree = bool(o is not None and (o[0] == og[0]).all())
     dist.barrier()
     stream = torch.cuda.ExternalStream(P.stream, device=device)
-    ms = _timed_steps(torch, stream, device, lambda: P.forward(B, *ins), a.sub_steps)
+    ms = _timed_steps(torch, stream, device, (lambda: g.launch()) if g else (lambda: P.forward(B, *ins)),
+                      a.sub_steps)
     t = torch.tensor([ms], device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     st = P.stats()
+    if g is not None:
+        g.close()
     dist.barrier()
     P.close()
     del mine, buf
@@ -540,7 +556,10 @@ def subrecord_split(a, ddg, synth, torch, dist, rank, world, local, device, push
                       "HBM, flags)" if push else "with host handoffs (send slots read in place over NVLink)"),
             "pairs": pairs, "value": value, "unit": "samples/s", "ms_per_step": ms / a.sub_steps,
             "steps": a.sub_steps, "warmup": a.warmup, "samples_per_s_per_gpu": value / world,
-            "nvlink_bytes_per_step": 2 * pairs * st["bytes_sent"], "openings_per_step": st["rounds"]}
+            "nvlink_bytes_per_step": 2 * pairs * st["bytes_sent"], "openings_per_step": st["rounds"],
+            "launch": ("CUDA graph of each rank's own party forward, replayed every step" if g is not None
+                       else "host-launched forward on each rank"),
+            "graph_output_equals_host_forward": agree}
 
 
 def main():
@@ -715,6 +734,13 @@ def main():
             step(False)
             for p in parties:
                 p.enable_dcf_timing(True)
+    elif uses_graph(a):
+        # split, push-mode IPC: every rank captures its own party's forward (all
+        # handoffs on the device) after the warm-up forwards; a failed capture
+        # ends the run (the peer's replays then give up at --peer-timeout)
+        graph[0] = ddg.ForwardGraph(parties[0], None, B, [t.data_ptr() for t in bufs[0][0]])
+        graph[0].launch()  # untimed: the first replay uploads the graph
+        graph_ok = True
     n0 = ddg.launch_count()
     tw = [0.0, 0.0]
     ms = timed(False, a.steps, tw)
@@ -754,7 +780,7 @@ def main():
         if colo and not streams:
             outs["e2e_forward"] = o
         e2e_graph = None
-        if uses_graph(a) and graph_ok:
+        if colo and uses_graph(a) and graph_ok:
             # the same forward with the pinned host inputs captured too: every
             # replay copies both parties' input shares host -> device
             try:

@@ -116,6 +116,7 @@ SIGNATURES = {
     "ddg_forward_eval_pair": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp]),
     "ddg_forward_graph_create": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                         ctypes.POINTER(_vp)]),
+    "ddg_party_graph_create": (_i32, [_vp, _i32, ctypes.POINTER(_vp), _i32, ctypes.POINTER(_vp)]),
     "ddg_forward_graph_create_ex": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32,
                                            ctypes.POINTER(_vp)]),
     "ddg_forward_graph_launch": (_i32, [_vp, _vp, _vp]),
@@ -412,17 +413,22 @@ class ForwardGraph:
     ordinary forward_pair of the pair before creating it, and close it before
     the parties."""
 
-    def __init__(self, p0: Party, p1: Party, batch, inputs0, inputs1, on_host=False):
-        """on_host: inputs are pinned host buffers copied in by every replay."""
+    def __init__(self, p0: Party, p1, batch, inputs0, inputs1=None, on_host=False):
+        """on_host: inputs are pinned host buffers copied in by every replay.
+        p1 None: p0's own forward alone (ddg_party_graph_create), for a party
+        whose peer is another process over a push-mode IPC channel."""
         self.batch = batch
         a0 = (_vp * 4)(*inputs0)
-        a1 = (_vp * 4)(*inputs1)
         h = _vp()
-        check(lib().ddg_forward_graph_create_ex(p0.h, p1.h, batch, a0, a1, int(on_host), ctypes.byref(h)))
+        if p1 is None:
+            check(lib().ddg_party_graph_create(p0.h, batch, a0, int(on_host), ctypes.byref(h)))
+        else:
+            a1 = (_vp * 4)(*inputs1)
+            check(lib().ddg_forward_graph_create_ex(p0.h, p1.h, batch, a0, a1, int(on_host), ctypes.byref(h)))
         self.h = h
 
     def launch(self, outputs=True):
-        """Replay the forward; returns (raw, affinity) of party 0's reveal, or None."""
+        """Replay the forward; returns (raw, affinity) of the (first) party's reveal, or None."""
         import numpy as np
 
         if not outputs:

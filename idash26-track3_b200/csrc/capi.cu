@@ -484,6 +484,7 @@ struct ddg_forward_graph {
     cudaGraphExec_t exec = nullptr;
     void *d_out = nullptr;          // party 0's revealed output, written by every replay
     uint64_t launches = 0;          // kernels of one replay
+    uint64_t exchanges = 0;         // single-party graph: the party's channel exchanges in one replay
     // comparison-launch timing records captured into the graph, per party:
     // their events are the graph's (taken out of the party's pool), and every
     // replay re-records them
@@ -613,13 +614,79 @@ int ddg_forward_graph_create_ex(ddg_party *p0, ddg_party *p1, int batch, const v
     return DDG_OK;
 }
 
+int ddg_party_graph_create(ddg_party *p, int batch, const void *const *in, int on_host, ddg_forward_graph **out)
+{
+    DDG_CHECK(p && in && out && batch > 0, DDG_ERR_ARG, "bad argument");
+    *out = nullptr;
+    DDG_CHECK(p->P.chan, DDG_ERR_STATE, "party %d has no channel", p->P.party);
+    std::string why;
+    DDG_CHECK(p->P.chan->replayable(why), DDG_ERR_STATE, "party %d: no single-party forward graph over %s",
+              p->P.party, why.c_str());
+    DDG_CHECK(p->P.keys && p->P.key_bytes >= forward_key_bytes(p->P.bw, p->P.s, batch), DDG_ERR_KEY,
+              "party %d: bound key region smaller than one forward of batch %d", p->P.party, batch);
+    DDG_CHECK(!p->P.graph_recs, DDG_ERR_STATE, "party %d already has a forward graph", p->P.party);
+    DDG_CUDA(cudaSetDevice(p->P.device));
+    DDG_TRY(settle_timing(p->P));
+    if (on_host) DDG_TRY(prepare_host_inputs(p->P, batch));
+    auto *g = new ddg_forward_graph;
+    g->p0 = p, g->batch = batch;
+    if (cudaMalloc(&g->d_out, size_t(batch) * (p->P.bw / 8)) != cudaSuccess) {
+        delete g;
+        set_last_error("cudaMalloc(forward graph output) failed");
+        return DDG_ERR_CUDA;
+    }
+    const uint64_t n0 = launch_count(), r0 = p->P.chan->rounds[p->P.party];
+    int st = DDG_OK;
+    cudaError_t ce = cudaStreamBeginCapture(p->P.stream, cudaStreamCaptureModeRelaxed);
+    if (ce != cudaSuccess) {
+        set_last_error("cudaStreamBeginCapture: %s", cudaGetErrorString(ce));
+        st = DDG_ERR_CUDA;
+    }
+    const bool capturing = st == DDG_OK;
+    if (st == DDG_OK) st = forward_capture(p->P, batch, in[0], in[1], in[2], in[3], g->d_out, on_host != 0);
+    if (capturing) {
+        ce = cudaStreamEndCapture(p->P.stream, &g->graph);
+        if (st == DDG_OK && ce != cudaSuccess) {
+            set_last_error("cudaStreamEndCapture: %s", cudaGetErrorString(ce));
+            st = DDG_ERR_CUDA;
+        }
+    }
+    g->launches = launch_count() - n0;
+    // the barrier's empty exchange is one of them (the channel does not count it as a round)
+    g->exchanges = p->P.chan->rounds[p->P.party] - r0 + 1;
+    if (st == DDG_OK) {
+        ce = cudaGraphInstantiate(&g->exec, g->graph, 0);
+        if (ce != cudaSuccess) {
+            set_last_error("cudaGraphInstantiate: %s", cudaGetErrorString(ce));
+            st = DDG_ERR_CUDA;
+        }
+    }
+    cudaGetLastError();
+    if (st != DDG_OK) {
+        if (g->exec) cudaGraphExecDestroy(g->exec);
+        if (g->graph) cudaGraphDestroy(g->graph);
+        cudaFree(g->d_out);
+        p->P.timing.recs.clear(), p->P.timing.used = 0;
+        delete g;
+        return st;
+    }
+    if (p->P.timing.enabled) {
+        adopt_timing(p->P, g->recs[0]);
+        p->P.graph_recs = &g->recs[0];
+        p->P.graph_fresh = false;
+    }
+    *out = g;
+    return DDG_OK;
+}
+
 int ddg_forward_graph_launch(ddg_forward_graph *g, int64_t *h_out_raw, double *h_affinity)
 {
     DDG_CHECK(g && g->exec, DDG_ERR_ARG, "null forward graph");
     Party &P = g->p0->P;
     DDG_CUDA(cudaSetDevice(P.device));
     ddg_party *ps[2] = {g->p0, g->p1};
-    for (int i = 0; i < 2; i++) {
+    const int np = g->p1 ? 2 : 1;
+    for (int i = 0; i < np; i++) {
         // the timed launches of a replay are read against the party's reference
         // event: record it before the first replay of a timing session (both
         // parties share the device, so party 0's stream serves for both)
@@ -631,21 +698,24 @@ int ddg_forward_graph_launch(ddg_forward_graph *g, int64_t *h_out_raw, double *h
     }
     DDG_CUDA(cudaGraphLaunch(g->exec, P.stream));
     add_launches(g->launches);
-    cudaError_t ce = cudaStreamSynchronize(P.stream);
-    DDG_CHECK(ce == cudaSuccess, DDG_ERR_CUDA, "forward graph: %s", cudaGetErrorString(ce));
-    for (int i = 0; i < 2; i++)
-        if (ps[i]->P.graph_recs == &g->recs[i]) ps[i]->P.graph_fresh = true;
-    DDG_TRY(ring_gemm_tc_check(P.stream));
-    if (!h_out_raw && !h_affinity) return DDG_OK;
+    if (!g->p1) P.chan->note_replay(P.party, g->exchanges);
     const int B = g->batch;
     std::vector<int64_t> v(B);
-    if (P.bw == 32) {
-        std::vector<int32_t> h(B);
-        DDG_CUDA(cudaMemcpy(h.data(), g->d_out, B * sizeof(int32_t), cudaMemcpyDeviceToHost));
-        for (int i = 0; i < B; i++) v[i] = h[i];
-    } else {
-        DDG_CUDA(cudaMemcpy(v.data(), g->d_out, B * sizeof(int64_t), cudaMemcpyDeviceToHost));
-    }
+    std::vector<int32_t> h32(B);
+    // the read-back stays on the party's stream (no legacy-stream synchronisation)
+    const bool want = h_out_raw || h_affinity;
+    if (want)
+        DDG_CUDA(cudaMemcpyAsync(P.bw == 32 ? static_cast<void *>(h32.data()) : static_cast<void *>(v.data()),
+                                 g->d_out, size_t(B) * (P.bw / 8), cudaMemcpyDeviceToHost, P.stream));
+    cudaError_t ce = cudaStreamSynchronize(P.stream);
+    DDG_CHECK(ce == cudaSuccess, DDG_ERR_CUDA, "forward graph: %s", cudaGetErrorString(ce));
+    for (int i = 0; i < np; i++)
+        if (ps[i]->P.graph_recs == &g->recs[i]) ps[i]->P.graph_fresh = true;
+    DDG_TRY(ring_gemm_tc_check(P.stream));
+    if (!g->p1) DDG_TRY(P.chan->status(P.party));  // the channel's device-side waits
+    if (!want) return DDG_OK;
+    if (P.bw == 32)
+        for (int i = 0; i < B; i++) v[i] = h32[i];
     for (int i = 0; i < B; i++) {
         if (h_out_raw) h_out_raw[i] = v[i];
         // AFFINITY = int32(value) / 2^s (deepdtagen_inference.cu:594-606)
@@ -664,6 +734,7 @@ int ddg_forward_graph_destroy(ddg_forward_graph *g)
     if (g->d_out) cudaFree(g->d_out);
     ddg_party *ps[2] = {g->p0, g->p1};
     for (int i = 0; i < 2; i++) {
+        if (!ps[i]) continue;
         Party &P = ps[i]->P;
         if (P.graph_recs == &g->recs[i]) P.graph_recs = nullptr, P.graph_fresh = false;
         for (const auto &r : g->recs[i]) cudaEventDestroy(r.a), cudaEventDestroy(r.b);

@@ -153,36 +153,47 @@ struct IpcShared {
 // ------------------------------------------------------------------ push mode (device-side handoff)
 //
 // Every party owns, in its own device memory, S receive slots (the arena) and
-// a PushFlags block; both are mapped into the peer's process.  Exchange g of
-// party p (slot s = (g-1) % S), all of it enqueued on p's stream, no host wait:
-//   1. k_push_gate (one thread): publish "p consumed the peer's generation
-//      g-1" into the peer's flags (every kernel that read it came before this
-//      one on the stream), then wait until the peer has consumed p's
-//      generation g-S, the last one that used slot s on the peer's side;
-//   2. k_push_copy: copy the share into the peer's slot s with peer stores
-//      (16- or 4-byte words), each block fences at system scope, and the last
-//      block to finish raises the peer's `posted` to g;
-//   3. k_push_wait (one thread): wait until the peer's generation g has been
-//      posted into p's own slot s; the consumers then read local HBM.
-// The waits are single-thread kernels (they never fill the GPU), bounded by
-// the party's timeout: one that gives up sets `err`, which the host reads
-// after the forward (status()).  Both parties must be on different GPUs:
-// kernels that wait on one another are never launched on one GPU.
-// Step 3 is enqueued only once the peer's host has enqueued its steps 1-2 of
-// generation g (the shared `posted` counters, published at enqueue time; the
-// previous exchange's step 3 covers the gate's wait on g-S+1 <= g-1).  Every
-// device-side wait therefore depends on work that is already queued on the
-// peer's GPU, never on a launch still to come from the peer's host: a
-// context-wide synchronisation on either GPU (a cudaMalloc or cudaFree, a
-// kernel's first launch under lazy module loading) taken by another thread of
-// the process, e.g. a second party of the same GPU, always drains instead of
-// closing a cycle through the peer's host.
+// a PushFlags block; both are mapped into the peer's process.  Generations
+// are numbered on the device: exchange i (1-based) since the last barrier has
+// generation g = base + i, where `base` (this party's own flags) is advanced
+// by the barrier to the next multiple of S above the last generation, so slot
+// s = (g-1) % S = (i-1) % S is known to the host at enqueue time and the same
+// launches replay unchanged from a CUDA graph (both parties advance their
+// bases identically: their exchange sequences are the same).  Exchange g of
+// party p, enqueued on p's stream:
+//   1. k_push_send: every block's first thread publishes "p consumed the
+//      peer's generation g-1" into the peer's flags (every kernel that read
+//      it came before this one on the stream) and waits until the peer has
+//      consumed p's generation g-S, the last one that used slot s on the
+//      peer's side; the blocks then copy the share into the peer's slot s
+//      with peer stores (16- or 4-byte words), each fences at system scope,
+//      and the last block to finish raises the peer's `posted` to g;
+//   2. k_push_wait (one thread), or the last block of k_push_send itself when
+//      the forward is being captured into a graph: wait until the peer's
+//      generation g has been posted into p's own slot s; the consumers then
+//      read local HBM.
+// The waits are bounded by the party's timeout: one that gives up sets `err`,
+// which the host reads after the forward (status()).  Both parties must be on
+// different GPUs: kernels that wait on one another are never launched on one
+// GPU.  A host-launched step 2 is enqueued only once the peer's host has
+// enqueued its step 1 of the same exchange (the shared `posted` counters,
+// published at enqueue time; the slot wait of step 1 is covered by the
+// previous exchange's).  Every device-side wait therefore depends on work
+// that is already queued on the peer's GPU, never on a launch still to come
+// from the peer's host: a context-wide synchronisation on either GPU (a
+// cudaMalloc or cudaFree, a kernel's first launch under lazy module loading)
+// taken by another thread of the process, e.g. a second party of the same
+// GPU, always drains instead of closing a cycle through the peer's host.  A
+// graph replay enqueues the whole forward at once; it is allowed only for a
+// party that is the one push-mode party of its device in the process (no
+// other thread of the process can then wait on its device mid-forward).
 struct PushFlags {
     unsigned long long posted;     // the peer's last generation in this party's receive slots
     unsigned long long consumed;   // this party's last generation that the peer has consumed
-    unsigned int done_blocks;      // k_push_copy's block counter (this party's own)
+    unsigned int done_blocks;      // k_push_send's block counter (this party's own)
     unsigned int err;              // a wait of this party gave up
-    unsigned long long pad[29];
+    unsigned long long base;       // generation base of the exchanges since the last barrier (this party's own)
+    unsigned long long pad[28];
 };
 static_assert(sizeof(PushFlags) == 256, "flags block");
 
@@ -203,42 +214,56 @@ __device__ __forceinline__ unsigned long long globaltimer_ns()
     return t;
 }
 
-// bounded spin of one thread until *p >= target; false (and err set) after limit_ns
+__device__ __forceinline__ void st_release_sys_u32(unsigned int *p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// bounded spin of one thread until *p >= target.  After limit_ns it gives up:
+// it sets this party's err and the peer's (the peer's waits then give up at
+// once instead of each running out its own limit), and returns false; a wait
+// that finds err already set gives up at once.  A channel whose wait gave up
+// is failed: its forward reports DDG_ERR_PEER (status()).
 __device__ bool spin_until(const unsigned long long *p, unsigned long long target, unsigned long long limit_ns,
-                           unsigned int *err)
+                           PushFlags *me, PushFlags *peer)
 {
     if (ld_acquire_sys(p) >= target) return true;
     const unsigned long long t0 = globaltimer_ns();
     for (unsigned int it = 0;; it++) {
         if (ld_acquire_sys(p) >= target) return true;
-        if ((it & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
-            atomicOr(err, 1u);
+        if ((it & 63u) == 0 &&
+            (*reinterpret_cast<volatile unsigned int *>(&me->err) != 0 || globaltimer_ns() - t0 > limit_ns)) {
+            atomicOr(&me->err, 1u);
+            st_release_sys_u32(&peer->err, 1u);
             return false;
         }
         __nanosleep(200);
     }
 }
 
-__global__ void k_push_gate(PushFlags *me, PushFlags *peer, unsigned long long g, unsigned int S,
-                            unsigned long long limit_ns)
+template <bool kWait>
+__global__ void k_push_send(const uint32_t *src, uint32_t *dst, uint64_t words, PushFlags *me, PushFlags *peer,
+                            unsigned long long rel, unsigned int S, unsigned long long limit_ns)
 {
-    if (threadIdx.x != 0) return;
-    st_release_sys(&peer->consumed, g - 1);
-    if (g > S) spin_until(&me->consumed, g - S, limit_ns, &me->err);
-}
-
-__global__ void k_push_copy(const uint32_t *src, uint32_t *dst, uint64_t words, PushFlags *me, PushFlags *peer,
-                            unsigned long long g)
-{
-    const uint64_t tid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x, nth = uint64_t(gridDim.x) * blockDim.x;
-    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-        const uint64_t n16 = words / 4;
-        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
-        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-        for (uint64_t i = tid; i < n16; i += nth) d4[i] = s4[i];
-        for (uint64_t i = 4 * n16 + tid; i < words; i += nth) dst[i] = src[i];
-    } else {
-        for (uint64_t i = tid; i < words; i += nth) dst[i] = src[i];
+    const unsigned long long g = me->base + rel;
+    __shared__ bool go;
+    if (threadIdx.x == 0) {
+        // every block publishes (the same value), so whichever block runs first unblocks the peer
+        st_release_sys(&peer->consumed, g - 1);
+        go = g <= S || spin_until(&me->consumed, g - S, limit_ns, me, peer);
+    }
+    __syncthreads();
+    if (go) {
+        const uint64_t tid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x, nth = uint64_t(gridDim.x) * blockDim.x;
+        if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            const uint64_t n16 = words / 4;
+            const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+            for (uint64_t i = tid; i < n16; i += nth) d4[i] = s4[i];
+            for (uint64_t i = 4 * n16 + tid; i < words; i += nth) dst[i] = src[i];
+        } else {
+            for (uint64_t i = tid; i < words; i += nth) dst[i] = src[i];
+        }
     }
     __threadfence_system();
     __syncthreads();
@@ -247,26 +272,39 @@ __global__ void k_push_copy(const uint32_t *src, uint32_t *dst, uint64_t words, 
             me->done_blocks = 0;
             __threadfence_system();
             st_release_sys(&peer->posted, g);
+            if (kWait) spin_until(&me->posted, g, limit_ns, me, peer);
         }
     }
 }
 
-__global__ void k_push_wait(PushFlags *me, unsigned long long g, unsigned long long limit_ns)
+__global__ void k_push_wait(PushFlags *me, PushFlags *peer, unsigned long long rel, unsigned long long limit_ns)
 {
-    if (threadIdx.x == 0) spin_until(&me->posted, g, limit_ns, &me->err);
+    if (threadIdx.x == 0) spin_until(&me->posted, me->base + rel, limit_ns, me, peer);
 }
+
+// barrier: the next exchange starts a new run of S-aligned generations
+__global__ void k_push_advance(PushFlags *me, unsigned long long rel, unsigned int S)
+{
+    if (threadIdx.x == 0) me->base += (rel + S - 1) / S * S;
+}
+
+// live push-mode parties per device in this process (a graph replay needs to be the only one)
+static std::atomic<int> g_push_parties[64];
 
 struct IpcChannel : Channel {
     static constexpr int S = 4;
     int party = 0, device = 0;
     bool push = false;
     uint64_t slot_bytes = 0, gen = 0;
+    uint64_t rel = 0;   // push mode: exchanges since the last barrier (the device adds its base)
+    uint64_t hgen = 0;  // push mode: exchanges enqueued by this party's host, published for the peer's host
     std::string shm_name;
     IpcShared *sh = nullptr;
     uint8_t *arena = nullptr, *peer_arena = nullptr;
     PushFlags *flags = nullptr, *peer_flags = nullptr;  // push mode
     unsigned int *h_err = nullptr;                      // pinned mirror of flags->err
     int push_blocks = 148;
+    bool counted = false;  // push mode: counted in g_push_parties[device]
     cudaEvent_t posted[S] = {}, read[S] = {}, peer_posted[S] = {}, peer_read[S] = {};
 
     ~IpcChannel() override
@@ -283,6 +321,7 @@ struct IpcChannel : Channel {
         if (peer_arena) cudaIpcCloseMemHandle(peer_arena);
         if (peer_flags) cudaIpcCloseMemHandle(peer_flags);
         if (flags) cudaFree(flags);
+        if (counted) g_push_parties[device].fetch_sub(1);
         if (h_err) cudaFreeHost(h_err);
         for (int i = 0; i < S; i++) {
             for (cudaEvent_t e : {posted[i], read[i], peer_posted[i], peer_read[i]})
@@ -320,30 +359,62 @@ struct IpcChannel : Channel {
         return DDG_OK;
     }
 
+    static bool capturing(cudaStream_t st)
+    {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        return cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive;
+    }
+
     int exchange_push(int p, cudaStream_t st, const void *send, uint64_t bytes, const void **peer)
     {
         DDG_CHECK(bytes % 4 == 0, DDG_ERR_ARG, "IPC push exchange of %llu bytes (not whole 32-bit words)",
                   (unsigned long long)bytes);
-        const uint64_t g = ++gen;
-        const uint64_t s = (g - 1) % S;
+        const uint64_t i = ++rel;
+        const uint64_t s = (i - 1) % S;
         const unsigned long long limit = 1000000ull * unsigned(timeout_ms);
-        k_push_gate<<<1, 32, 0, st>>>(flags, peer_flags, g, S, limit);
-        note_launch();
         const uint64_t words = bytes / 4;
         const int blocks = words ? int(std::min<uint64_t>(push_blocks, (words + 1023) / 1024)) : 1;
-        k_push_copy<<<blocks, 256, 0, st>>>(static_cast<const uint32_t *>(send),
-                                            reinterpret_cast<uint32_t *>(peer_arena + s * slot_bytes), words, flags,
-                                            peer_flags, g);
-        note_launch();
-        sh->posted[p].store(g, std::memory_order_release);
-        DDG_TRY(wait_for(sh->posted[1 - p], g, "enqueue of generation"));
-        k_push_wait<<<1, 32, 0, st>>>(flags, g, limit);
-        note_launch();
+        const uint32_t *src = static_cast<const uint32_t *>(send);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(peer_arena + s * slot_bytes);
+        if (capturing(st)) {
+            // a graph replay enqueues the whole forward at once: post and wait in one launch
+            k_push_send<true><<<blocks, 256, 0, st>>>(src, dst, words, flags, peer_flags, i, S, limit);
+            note_launch();
+        } else {
+            k_push_send<false><<<blocks, 256, 0, st>>>(src, dst, words, flags, peer_flags, i, S, limit);
+            note_launch();
+            sh->posted[p].store(++hgen, std::memory_order_release);
+            DDG_TRY(wait_for(sh->posted[1 - p], hgen, "enqueue of exchange"));
+            k_push_wait<<<1, 32, 0, st>>>(flags, peer_flags, i, limit);
+            note_launch();
+        }
         DDG_CUDA(cudaGetLastError());
         *peer = arena + s * slot_bytes;
         bytes_sent[p] += bytes;
         rounds[p] += 1;
         return DDG_OK;
+    }
+
+    // a graph replay of `exchanges` exchanges was enqueued: publish them for the
+    // peer's host, as the host-launched exchanges do one by one
+    void note_replay(int p, uint64_t exchanges) override
+    {
+        if (!push) return;
+        hgen += exchanges;
+        sh->posted[p].store(hgen, std::memory_order_release);
+    }
+
+    bool replayable(std::string &why) const override
+    {
+        if (!push) {
+            why = "IPC channel with host handoffs (its exchanges wait on the host)";
+            return false;
+        }
+        if (device < 0 || device >= 64 || g_push_parties[device].load() != 1) {
+            why = "more than one push-mode party on this device in the process";
+            return false;
+        }
+        return true;
     }
 
     int status(int p) override
@@ -390,8 +461,14 @@ struct IpcChannel : Channel {
         const void *dummy = nullptr;
         DDG_TRY(exchange(p, st, nullptr, 0, nullptr, &dummy));
         rounds[p] -= 1;
-        // push mode: the device-side waits' verdict, read by status() once the stream has drained
-        if (push) DDG_CUDA(cudaMemcpyAsync(h_err, &flags->err, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
+        if (push) {
+            // the next exchange starts on a slot-aligned generation; the device-side
+            // waits' verdict is read by status() once the stream has drained
+            k_push_advance<<<1, 32, 0, st>>>(flags, rel, S);
+            note_launch();
+            rel = 0;
+            DDG_CUDA(cudaMemcpyAsync(h_err, &flags->err, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
+        }
         return DDG_OK;
     }
 };
@@ -479,6 +556,10 @@ Channel *make_ipc_channel(const char *name, int party, int device, uint64_t slot
         }
         *c->h_err = 0;
         cudaDeviceGetAttribute(&c->push_blocks, cudaDevAttrMultiProcessorCount, device);
+        if (device >= 0 && device < 64) {
+            g_push_parties[device].fetch_add(1);
+            c->counted = true;
+        }
     }
     if (cudaDeviceGetPCIBusId(sh->bus_id[party], sizeof(sh->bus_id[party]), device) != cudaSuccess)
         sh->bus_id[party][0] = 0;

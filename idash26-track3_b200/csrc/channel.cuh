@@ -15,6 +15,7 @@
 #include <condition_variable>
 #include <cstdint>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -37,6 +38,16 @@ struct Channel {
     virtual int status(int party) { (void)party; return DDG_OK; }
     // exchange() needs the caller's `recv` buffer (it copies the peer's bytes there)
     virtual bool needs_recv_buffer() const { return !same_device(); }
+    // one party's forward, captured on its own stream, can be replayed from a
+    // CUDA graph (every handoff of the capture happens on the device); `why`
+    // says what stands in the way otherwise
+    virtual bool replayable(std::string &why) const
+    {
+        why = "a channel whose exchanges wait on the host";
+        return false;
+    }
+    // a graph replay holding `exchanges` exchanges of this party was enqueued
+    virtual void note_replay(int party, uint64_t exchanges) { (void)party, (void)exchanges; }
     uint64_t bytes_sent[2] = {0, 0};
     uint64_t rounds[2] = {0, 0};
     int timeout_ms = 60000;

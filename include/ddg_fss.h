@@ -289,6 +289,19 @@ int ddg_forward_graph_create(ddg_party *p0, ddg_party *p1, int batch, const void
  * staging buffers are allocated before the capture. */
 int ddg_forward_graph_create_ex(ddg_party *p0, ddg_party *p1, int batch, const void *const *in0,
                                 const void *const *in1, int on_host, ddg_forward_graph **out);
+/* One party's forward captured on its own stream, for a party whose peer is
+ * another process (the split deployment, one party per GPU): the channel must
+ * hand off on the device (ddg_party_connect_ipc_push; DDG_ERR_STATE for other
+ * channels, and while another push-mode party lives on the same device in
+ * this process).  The peer replays its own graph of the same forward, or runs
+ * the same forward host-launched: the exchange sequences match either way.
+ * ddg_forward_graph_launch replays it on the party's stream and returns the
+ * revealed output like ddg_forward_eval; a device-side wait for the peer that
+ * gave up is reported as DDG_ERR_PEER.  The rest as ddg_forward_graph_create_ex
+ * (one host-launched ddg_forward_eval first; `in` device or, with on_host,
+ * pinned host buffers). */
+int ddg_party_graph_create(ddg_party *party, int batch, const void *const *in, int on_host,
+                           ddg_forward_graph **out);
 int ddg_forward_graph_launch(ddg_forward_graph *graph, int64_t *h_out_raw, double *h_affinity);
 int ddg_forward_graph_destroy(ddg_forward_graph *graph);
 /* GPU dealer (replaces DDGOrcaKeygenBatched + ddgSecureAdjNormKeygen,

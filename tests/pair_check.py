@@ -9,8 +9,14 @@ device-side flags), and rank 0 compares the revealed outputs of several forwards
 with the integer oracle.  With DDG_CHECK_LANES=L > 1 every rank holds L
 parties (lanes), each with its own keys, inputs and channel to the matching
 lane of the other rank, and runs their forwards concurrently from L host
-threads, as the split bench layout with --lanes does.  Exits non-zero on any
-mismatch.
+threads, as the split bench layout with --lanes does.  With DDG_CHECK_GRAPH=1
+(ipc-push, one lane) every rank then captures its own party's forward into a
+CUDA graph and replays it, a host-launched forward follows the replays, and
+all of them are compared; over host-handoff IPC the capture must be refused.
+With DDG_CHECK_ABSENT=1 as well, rank 0 then replays its graph once more with
+a 2 s limit while rank 1 stays on the host (a flag that nothing sets): the
+replay must end with DDG_ERR_PEER, and rank 0's context must stay usable.
+Exits non-zero on any mismatch.
 """
 import datetime
 import importlib
@@ -24,6 +30,32 @@ import torch.distributed as dist
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, REPO)
+
+
+def absent_peer(ddg, P, B, ins, rank, dev):
+    """Rank 0 replays its forward while rank 1 never runs its own: the first
+    device-side wait for rank 1 gives up after 2 s, the rest give up at once."""
+    import time
+
+    dist.barrier()
+    note = ""
+    if rank == 0:
+        P.set_timeout(2000)
+        g = ddg.ForwardGraph(P, None, B, ins)
+        t0 = time.time()
+        try:
+            g.launch()
+            note = " absent peer NOT detected"
+        except ddg.DdgError as e:
+            note = " absent peer detected" if e.code == 4 else f" absent peer error {e}"  # DDG_ERR_PEER
+        dt = time.time() - t0
+        g.close()
+        assert float(torch.ones(4, device=dev).sum().item()) == 4.0  # the context still works
+        note += f" in {dt:.1f} s"
+        if dt > 30:
+            note += " (too slow: error)"
+    dist.barrier()
+    return note
 
 
 def main():
@@ -74,11 +106,28 @@ def main():
         outs = [[parties[0].forward(B, *ins[0])[1]] for _ in range(3)]
     else:
         outs = [[o[1] for o in ddg.forward_lanes(parties, B, ins)] for _ in range(3)]
+    graph_note = ""
+    if os.environ.get("DDG_CHECK_GRAPH") == "1" and lanes == 1:
+        if comm == "ipc-push":
+            g = ddg.ForwardGraph(parties[0], None, B, ins[0])
+            outs += [[g.launch()[1]] for _ in range(3)]
+            g.close()
+            outs.append([parties[0].forward(B, *ins[0])[1]])  # host-launched after the replays
+            graph_note = " graph"
+            if os.environ.get("DDG_CHECK_ABSENT") == "1":
+                graph_note += absent_peer(ddg, parties[0], B, ins[0], rank, dev)
+        else:
+            try:
+                ddg.ForwardGraph(parties[0], None, B, ins[0]).close()
+                graph_note = " graph NOT refused"
+            except ddg.DdgError as e:
+                graph_note = " graph refused" if e.code == 5 else f" graph error {e}"  # DDG_ERR_STATE
     ok = 1
     if rank == 0:
         want = [RF.protocol_forward(i.x_ring, i.adj_ring, i.mask_ring, i.protein_ring, q, bw, s)[1] for i in inps]
         ok = int(all(np.array_equal(o[l], want[l]) for o in outs for l in range(lanes)))
-        tag = f"{comm} pair" + (f" x{lanes} lanes" if lanes > 1 else "")
+        tag = f"{comm} pair" + (f" x{lanes} lanes" if lanes > 1 else "") + graph_note
+        ok = ok and "NOT" not in graph_note and "error" not in graph_note
         print(tag, "OK" if ok else f"MISMATCH {outs} vs {want}", parties[0].stats(), flush=True)
     flag = torch.tensor([ok])
     dist.broadcast(flag, src=0)
