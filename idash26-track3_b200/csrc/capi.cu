@@ -155,11 +155,11 @@ int ddg_gate_eval_pair(int kind, int bw, int scale, uint64_t n, const void *d_xh
         const int lo_arr = P.mode == PLAN_TT_FULL ? 1 : hi ? 2 : 0;  // index of the lo-compare array
         uint32_t *tab[2] = {}, *tri[2] = {};
         void *state[2];
-        uint32_t *o[2][OT_MAX_LEVELS + 1] = {};
+        void *o[2][OT_MAX_LEVELS + 1] = {};
         for (int p = 0; p < 2; p++) {
             if (L.ot) tab[p] = static_cast<uint32_t *>(grab(sc.tables)), tri[p] = static_cast<uint32_t *>(grab(sc.tri));
             state[p] = grab(sc.state);
-            for (int l = 1; l <= P.levels; l++) o[p][l] = static_cast<uint32_t *>(grab(4 * n));
+            for (int l = 1; l <= P.levels; l++) o[p][l] = grab(uint64_t(ot_open_bytes(L, l)) * n);
         }
         if (L.ot)
             for (int p = 0; p < 2 && err == DDG_OK; p++)

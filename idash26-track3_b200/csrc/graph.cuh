@@ -475,12 +475,14 @@ struct EvalExec : ExecBase<T> {
             if (this->err == DDG_OK) ok(ot_garble(L, p, x.v, k, tab, state, tri, this->st));
             ptab = reinterpret_cast<const uint32_t *>(peer_of(tab, sc.tables));
         }
-        const uint32_t *oo = nullptr, *po = nullptr;
+        const void *oo = nullptr, *po = nullptr;
         for (int l = 1; l <= Pl.levels; l++) {
-            uint32_t *o = static_cast<uint32_t *>(this->alloc_bytes(4 * n));
+            // openings of 1, 2 or 4 bytes per element, exchanged in whole 32-bit words
+            const uint64_t ob = (uint64_t(ot_open_bytes(L, l)) * n + 3) & ~uint64_t(3);
+            void *o = this->alloc_bytes(ob);
             if (this->err == DDG_OK)
                 ok(ot_level(L, p, l, k, ptab, oo, po, state, tri, o, nullptr, nullptr, this->st, x.v));
-            po = reinterpret_cast<const uint32_t *>(peer_of(o, 4 * n));
+            po = peer_of(o, ob);
             oo = o;
         }
         // opened bit arrays: hi lt, hi eq, lo lt (split round 2) / full lt, lo lt / lo lt only

@@ -162,10 +162,10 @@ struct OtLevelArgs {
     const uint32_t *c0;          // OT: party 0's explicit triple c bits [N]
     const void *xhat;            // TT level 1: the masked input (ring words)
     const uint32_t *tables;      // TT level 1: the party's digit truth-table rows [row][N]
-    const uint32_t *open_own, *open_peer;  // level >= 2: the previous level's openings
+    const void *open_own, *open_peer;  // level >= 2: the previous level's openings (ot_open_bytes each)
     void *state;
     const uint32_t *tri;         // [tri_words][N]
-    uint32_t *open_out;          // level <= levels
+    void *open_out;              // level <= levels
     uint32_t *bits_hi, *bits_lo; // level == levels + 1: masked comparison bits (split-gate layout)
 };
 
@@ -215,7 +215,8 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
         }
     } else {
         // close level l - 1: z = c ^ f a ^ e b ^ [p = 0] e f
-        const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
+        const uint32_t O = __ldcs(static_cast<const uint32_t *>(a.open_own) + e) ^
+                           __ldcs(static_cast<const uint32_t *>(a.open_peer) + e);
         const bool cword = !tt && PARTY == 0;  // OT party 0 keeps its triple c bits in a key word
         const uint32_t cw = cword ? __ldcs(a.c0 + e) : 0u;
         const int qa = P.lvl_first[l - 2];
@@ -258,7 +259,7 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             w |= ((eH ^ tri_bit(tw, tb)) << (3 * j)) | ((lL ^ tri_bit(tw, tb + 1)) << (3 * j + 1));
             if (C.eq) w |= (eL ^ tri_bit(tw, tb + 2)) << (3 * j + 2);
         }
-        a.open_out[e] = w;
+        static_cast<uint32_t *>(a.open_out)[e] = w;
         store_state<ST>(a.state, e, st);
     } else {
         if (P.nd[0]) hl = st_bit(st, 0), he = st_bit(st, 1);
@@ -284,9 +285,17 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
     static_assert(P.ok && P.state_bytes() == 4, "compiled-in plans keep a 32-bit state");
     constexpr bool TT = MODE != PLAN_OT;
     constexpr uint32_t p0 = PARTY == 0 ? 1u : 0u;
+    // openings read (level L - 1) and written (level L), each in its own width
+    using OI = open_word_t<open_width(P, L - 1)>;
+    using OO = open_word_t<open_width(P, L)>;
+    using SW = open_word_t<state_width(P)>;
+    auto open_in = [&]() {
+        return uint32_t(__ldcs(static_cast<const OI *>(a.open_own) + e)) ^
+               uint32_t(__ldcs(static_cast<const OI *>(a.open_peer) + e));
+    };
     const uint64_t N = a.N;
     uint32_t st = 0;
-    if constexpr (!(TT && L == 1)) st = load_state<uint32_t>(a.state, e);
+    if constexpr (!(TT && L == 1)) st = uint32_t(load_state<SW>(a.state, e));
     uint32_t tw[3] = {0u, 0u, 0u};
     static_for<0, P.tri_words()>([&](auto wi) {
         constexpr int w = decltype(wi)::value;
@@ -327,10 +336,10 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
             st |= (lt << (2 * (g0 + t))) | (eq << (2 * (g0 + t) + 1));
         });
     } else if constexpr (TT) {
-        const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
+        const uint32_t O = open_in();
         st = tt_close<MODE, NB, SB, PARTY, L>(st, tw, O);
     } else {
-        const uint32_t O = __ldcs(a.open_own + e) ^ __ldcs(a.open_peer + e);
+        const uint32_t O = open_in();
         constexpr bool cword = !TT && PARTY == 0;
         const uint32_t cw = cword ? __ldcs(a.c0 + e) : 0u;
         constexpr int qa = P.lvl_first[L - 2], qb = P.lvl_first[L - 1];
@@ -359,8 +368,8 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         });
     }
     if constexpr (TT && L <= P.levels) {
-        a.open_out[e] = tt_open<MODE, NB, SB, L>(st, tw);
-        store_state<uint32_t>(a.state, e, st);
+        static_cast<OO *>(a.open_out)[e] = OO(tt_open<MODE, NB, SB, L>(st, tw));
+        store_state<SW>(a.state, e, SW(st));
     } else if constexpr (L <= P.levels) {
         uint32_t w = 0;
         constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
@@ -372,8 +381,8 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
             w |= ((eH ^ tbit(tb)) << (3 * j)) | ((lL ^ tbit(tb + 1)) << (3 * j + 1));
             if constexpr (P.comb[q].eq != 0) w |= (eL ^ tbit(tb + 2)) << (3 * j + 2);
         });
-        a.open_out[e] = w;
-        store_state<uint32_t>(a.state, e, st);
+        static_cast<OO *>(a.open_out)[e] = OO(w);
+        store_state<SW>(a.state, e, SW(st));
     } else {
         if constexpr (P.nd[0] != 0) hl = st & 1u, he = (st >> 1) & 1u;
         ll = (st >> (2 * P.base[1])) & 1u;
@@ -504,9 +513,24 @@ const OtPlan &gate_digit_plan(const GateLayout &L)
     return tt[tt_mode_of(L.kind)][L.bw == 64 ? 1 : 0][L.s > 0 && L.s < 64 ? L.s : 0];
 }
 
+// the level kernels take the compiled-in plan exactly when level_dispatch does
+static bool plan_compiled_in(const GateLayout &L) { return L.s == 12 && (L.bw == 32 || L.bw == 64); }
+
+int ot_open_bytes(const GateLayout &L, int level)
+{
+    return plan_compiled_in(L) ? open_width(gate_digit_plan(L), level) : 4;
+}
+
+// bytes per element of the digit-share state the level kernels read and write
+static int ot_state_bytes(const GateLayout &L)
+{
+    const OtPlan &P = gate_digit_plan(L);
+    return plan_compiled_in(L) ? state_width(P) : P.state_bytes();
+}
+
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
-             const uint32_t *open_own, const uint32_t *open_peer, void *state, const uint32_t *tri,
-             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat)
+             const void *open_own, const void *open_peer, void *state, const uint32_t *tri, void *open_out,
+             uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat)
 {
     if (L.n == 0) return DDG_OK;
     DDG_CHECK(L.ot || L.tt, DDG_ERR_ARG, "not an AND-tree gate");
@@ -546,12 +570,13 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     // comparison bit arrays at the last level
     const double n = double(L.n), Gq = P.garbled_by(1 - party);
     double bytes = n * 4.0 * P.tri_words();
+    const double sb = ot_state_bytes(L);
     if (L.tt && level == 1) bytes += n * (L.bw / 8.0 + 4.0 * P.rows);
-    else bytes += n * P.state_bytes();
-    if (level > 1) bytes += n * (8.0 + (L.ot && party == 0 ? 4.0 : 0.0));
+    else bytes += n * sb;
+    if (level > 1) bytes += n * (2.0 * ot_open_bytes(L, level - 1) + (L.ot && party == 0 ? 4.0 : 0.0));
     else if (L.ot) bytes += n * 5.0 * Gq;
     const double arrays = P.mode == PLAN_TT_FULL ? 2.0 : P.nd[0] ? 3.0 : 1.0;
-    bytes += level <= P.levels ? n * (4.0 + P.state_bytes()) : n * arrays / 8.0;
+    bytes += level <= P.levels ? n * (double(ot_open_bytes(L, level)) + sb) : n * arrays / 8.0;
     DDG_TRY(tl.end(st, bytes, 0.0, n));
     return DDG_OK;
 }

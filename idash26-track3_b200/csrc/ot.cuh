@@ -231,7 +231,8 @@ AesKey ot_party_key(const AesKey &dk, uint32_t op, int party);
 int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key, uint32_t *tables, void *state,
               uint32_t *tri, cudaStream_t st);
 // level 1..levels: (level 1: take the peer's tables) close the previous level
-// with both parties' openings, open this level's ANDs into open_out;
+// with both parties' openings, open this level's ANDs into open_out
+// (ot_open_bytes(L, level) bytes per element);
 // level levels + 1: close the last level and write the masked comparison bits
 // (bits_hi: [lt | eq] x ceil(N/32) words, bits_lo: lt)
 // Truth-table (TT) kinds run the same levels without a garble step: level 1
@@ -239,8 +240,12 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
 // the triple words come from the key (tri ignored), and the last level writes
 // bits_lo only for GATE_LRS_TT.
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
-             const uint32_t *open_own, const uint32_t *open_peer, void *state, const uint32_t *tri,
-             uint32_t *open_out, uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat = nullptr);
+             const void *open_own, const void *open_peer, void *state, const uint32_t *tri, void *open_out,
+             uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat = nullptr);
+// bytes per element of the openings of AND level `level` (1..levels): the
+// plans compiled into the level kernel (scale 12) store them in the smallest
+// of 1, 2 or 4 bytes that holds every opened bit, other plans in 4 bytes
+int ot_open_bytes(const GateLayout &L, int level);
 // scratch of one party's OT gate, bytes: garbled tables, state, triple bits
 struct OtScratch {
     uint64_t tables, state, tri;

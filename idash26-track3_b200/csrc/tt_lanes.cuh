@@ -54,6 +54,38 @@ __host__ __device__ constexpr uint32_t tt_lane_mask(const OtPlan &P, int l, bool
     return m;
 }
 
+// bytes per element of the openings of level l (1..levels) in the compiled-in
+// layouts: the smallest of 1, 2, 4 holding every opened bit (TT lanes: e, f,
+// f' at lane, lane + 1, lane + 2; the cross combine: bits 0 and 1; OT: 3 bits
+// per combine of the level from bit 0)
+__host__ __device__ constexpr int open_width(const OtPlan &P, int l)
+{
+    if (l < 1 || l > P.levels) return 4;
+    const int qa = P.lvl_first[l - 1], qb = P.lvl_first[l];
+    uint64_t m = 0;
+    if (P.mode == PLAN_OT) {
+        m = (uint64_t(1) << (3 * (qb - qa))) - 1;
+    } else if (qa < qb && P.comb[qa].part == 2) {
+        m = 3;
+    } else {
+        const uint64_t a = tt_lane_mask(P, l, false), e = tt_lane_mask(P, l, true);
+        m = a | (a << 1) | (e << 2);
+    }
+    return m < (uint64_t(1) << 8) ? 1 : m < (uint64_t(1) << 16) ? 2 : 4;
+}
+
+// bytes per element of the digit-share state in the compiled-in layouts: the
+// truth-table modes keep it in 16 bits when their 2 bits per digit fit (the
+// level kernels alone read and write it); the OT mode's garble step writes
+// the plan's state_bytes()
+__host__ __device__ constexpr int state_width(const OtPlan &P)
+{
+    return P.mode != PLAN_OT && 2 * P.D <= 16 ? 2 : P.state_bytes();
+}
+
+template <int W>
+using open_word_t = typename std::conditional<W == 1, uint8_t, typename std::conditional<W == 2, uint16_t, uint32_t>::type>::type;
+
 // the 5 triple bits (a, b, b', c, c') of combine Q from the party's triple words
 template <int Q>
 __host__ __device__ __forceinline__ uint32_t tri5(const uint32_t (&tw)[3])
