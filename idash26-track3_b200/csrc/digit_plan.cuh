@@ -49,6 +49,18 @@ struct OtPlan {
     // pass-through of an odd top node at level l: part p moves node pass_from to pass_to (-1: none)
     int8_t pass_from[OT_MAX_LEVELS + 1][2] = {}, pass_to[OT_MAX_LEVELS + 1][2] = {};
     OtComb comb[OT_MAX_COMB] = {};
+    // position of combine q's triple bits in the party's triple words: (a, b,
+    // b') at tpa[q] + 0..2, (c, c') at tpc[q] + 0..1 (b' and c' only for a
+    // combine that computes eq: the others have no such bits); the
+    // lo-compare mask bit (PLAN_TT_FULL) at mu_pos.  TT plans group them by AND
+    // level in the lane layout of the level kernels (tt_place: every level's
+    // (a, b, b') of all its combines is one shifted mask of one word, its (c,
+    // c') another), when that fits the plan's triple words (tpacked);
+    // otherwise, and for the OT plans, 5 bits per combine from 5q and the mask
+    // bit at 5 ncomb.
+    uint8_t tpa[OT_MAX_COMB] = {}, tpc[OT_MAX_COMB] = {};
+    int mu_pos = 0;
+    bool tpacked = false;
     int aux_bits = 0, naux = 0, tri0 = 0;  // OT: aux bits used, aux blocks, first triple bit (6 * Gmax)
     int npad[2] = {0, 0};               // OT: pad blocks of party 0 / 1
     bool ok = false;
@@ -87,9 +99,16 @@ struct OtPlan {
     {
         return comb[q].part == 2 ? 2 * base[0] : 2 * base[comb[q].part] + 2 * comb[q].out;
     }
-    // PLAN_TT_FULL: the party's share of the lo compare's mask bit sits in its
-    // triple words right after the combines' bits
-    __host__ __device__ constexpr int mu_bit() const { return 5 * ncomb; }
+    // PLAN_TT_FULL: the position of the party's share of the lo compare's mask bit
+    __host__ __device__ constexpr int mu_bit() const { return mu_pos; }
+    // bit k (0..4 = a, b, b', c, c') of combine q in the triple words
+    __host__ __device__ constexpr int tpos(int q, int k) const { return k < 3 ? tpa[q] + k : tpc[q] + k - 3; }
+    // lane of combine q at its level in the level kernels' word-parallel layout:
+    // 2 base + i 2^(l+1) for combine i of a part at level l; 0 for the cross combine
+    __host__ __device__ constexpr int lane_of(int q) const
+    {
+        return comb[q].part == 2 ? 0 : 2 * base[comb[q].part] + int(comb[q].out) * (2 << level_of(q));
+    }
     // AND-tree level (1-based) of combine q
     __host__ __device__ constexpr int level_of(int q) const
     {
@@ -98,6 +117,59 @@ struct OtPlan {
         return l;
     }
 };
+
+// first fit of the bit group m (offsets from bit 0, all below 32) into the
+// free bits of words [0, words): global position of its bit 0, or -1
+__host__ __device__ constexpr int place_bits(uint32_t (&used)[3], int words, uint32_t m)
+{
+    int hi = 0;
+    for (int b = 0; b < 32; b++)
+        if ((m >> b) & 1u) hi = b;
+    for (int w = 0; w < words; w++)
+        for (int sh = 0; sh + hi < 32; sh++)
+            if (((m << sh) & used[w]) == 0u) {
+                used[w] |= m << sh;
+                return 32 * w + sh;
+            }
+    return -1;
+}
+
+// triple-bit positions of a TT plan (see OtPlan::tpa): per level in order its
+// (a, b, b') group, then its (c, c') group (b', c' only for the combines that
+// compute eq), then the mask bit; first fit, in the plan's tri_words() words.
+// The oracle (oracle/fss_ref.c, tt_place) places them by the same steps.
+__host__ __device__ constexpr void tt_place(OtPlan &P)
+{
+    for (int q = 0; q < P.ncomb; q++) P.tpa[q] = uint8_t(5 * q), P.tpc[q] = uint8_t(5 * q + 3);
+    P.mu_pos = 5 * P.ncomb;
+    P.tpacked = false;
+    if (P.mode == PLAN_OT) return;
+    uint32_t used[3] = {0u, 0u, 0u};
+    uint8_t pa[OT_MAX_COMB] = {}, pc[OT_MAX_COMB] = {};
+    const int words = P.tri_words();
+    for (int l = 1; l <= P.levels; l++) {
+        const int qa = P.lvl_first[l - 1], qb = P.lvl_first[l];
+        if (qa >= qb) continue;
+        uint32_t ma = 0u, mc = 0u;
+        for (int q = qa; q < qb; q++) {
+            const bool eq = P.comb[q].eq != 0;
+            ma |= (eq ? 7u : 3u) << P.lane_of(q), mc |= (eq ? 3u : 1u) << P.lane_of(q);
+        }
+        const int ga = place_bits(used, words, ma);
+        if (ga < 0) return;
+        const int gc = place_bits(used, words, mc);
+        if (gc < 0) return;
+        for (int q = qa; q < qb; q++) pa[q] = uint8_t(ga + P.lane_of(q)), pc[q] = uint8_t(gc + P.lane_of(q));
+    }
+    int mu = 5 * P.ncomb;
+    if (P.mode == PLAN_TT_FULL) {
+        mu = place_bits(used, words, 1u);
+        if (mu < 0) return;
+    }
+    for (int q = 0; q < P.ncomb; q++) P.tpa[q] = pa[q], P.tpc[q] = pc[q];
+    P.mu_pos = mu;
+    P.tpacked = true;
+}
 
 // Plan for an n-bit ring and scale s.  OT and TT ReLU: hi = bits [s, n-1),
 // lo = bits [0, s); TT truncation: lo = bits [0, s) only.  constexpr, so
@@ -168,6 +240,7 @@ __host__ __device__ constexpr OtPlan digit_plan(int n, int s, int mode)
     P.npad[0] = (P.G0 + 3) / 4, P.npad[1] = (P.D - P.G0 + 3) / 4;
     P.ok = (mode != PLAN_OT || (P.naux <= OT_MAX_AUX && P.npad[0] <= OT_MAX_PAD && P.npad[1] <= OT_MAX_PAD)) &&
            P.tri_words() <= 3 && P.rows <= TT_MAX_ROWS;
+    if (P.ok) tt_place(P);
     return P;
 }
 __host__ __device__ constexpr OtPlan ot_plan(int n, int s) { return digit_plan(n, s, PLAN_OT); }

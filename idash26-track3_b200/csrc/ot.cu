@@ -225,11 +225,12 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             if (q >= P.ncomb) break;
             if (P.level_of(q) != l - 1) continue;
             const OtComb &C = P.comb[q];
-            const int j = q - qa, tb = 5 * q;
+            const int j = q - qa;
             const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
-            const uint32_t ta = tri_bit(tw, tb), tb1 = tri_bit(tw, tb + 1), tb2 = tri_bit(tw, tb + 2);
-            const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tri_bit(tw, tb + 3);
-            const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tri_bit(tw, tb + 4);
+            const uint32_t ta = tri_bit(tw, P.tpos(q, 0)), tb1 = tri_bit(tw, P.tpos(q, 1)),
+                           tb2 = tri_bit(tw, P.tpos(q, 2));
+            const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tri_bit(tw, P.tpos(q, 3));
+            const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tri_bit(tw, P.tpos(q, 4));
             const uint32_t lt = st_bit(st, P.hpos(q)) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
             const uint32_t eq = C.eq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
             const int o = P.opos(q);
@@ -254,10 +255,10 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
             if (q >= P.ncomb) break;
             if (P.level_of(q) != l) continue;
             const OtComb &C = P.comb[q];
-            const int j = q - qa, tb = 5 * q;
+            const int j = q - qa;
             const uint32_t eH = st_bit(st, P.hpos(q) + 1), lL = st_bit(st, P.lpos(q)), eL = st_bit(st, P.lpos(q) + 1);
-            w |= ((eH ^ tri_bit(tw, tb)) << (3 * j)) | ((lL ^ tri_bit(tw, tb + 1)) << (3 * j + 1));
-            if (C.eq) w |= (eL ^ tri_bit(tw, tb + 2)) << (3 * j + 2);
+            w |= ((eH ^ tri_bit(tw, P.tpos(q, 0))) << (3 * j)) | ((lL ^ tri_bit(tw, P.tpos(q, 1))) << (3 * j + 1));
+            if (C.eq) w |= (eL ^ tri_bit(tw, P.tpos(q, 2))) << (3 * j + 2);
         }
         static_cast<uint32_t *>(a.open_out)[e] = w;
         store_state<ST>(a.state, e, st);
@@ -346,12 +347,12 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         static_for<qa, qb>([&](auto qi) {
             constexpr OtPlan P = digit_plan(NB, SB, MODE);
             constexpr int q = decltype(qi)::value;
-            constexpr int j = q - qa, tb = 5 * q, h = P.hpos(q), o = P.opos(q);
+            constexpr int j = q - qa, h = P.hpos(q), o = P.opos(q);
             constexpr bool ceq = P.comb[q].eq != 0;
             const uint32_t eo = (O >> (3 * j)) & 1u, f = (O >> (3 * j + 1)) & 1u, f2 = (O >> (3 * j + 2)) & 1u;
-            const uint32_t ta = tbit(tb), tb1 = tbit(tb + 1), tb2 = tbit(tb + 2);
-            const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tbit(tb + 3);
-            const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tbit(tb + 4);
+            const uint32_t ta = tbit(P.tpos(q, 0)), tb1 = tbit(P.tpos(q, 1)), tb2 = tbit(P.tpos(q, 2));
+            const uint32_t c = cword ? (cw >> (2 * q)) & 1u : tbit(P.tpos(q, 3));
+            const uint32_t c2 = cword ? (cw >> (2 * q + 1)) & 1u : tbit(P.tpos(q, 4));
             const uint32_t lt = ((st >> h) & 1u) ^ c ^ (f & ta) ^ (eo & tb1) ^ (p0 & eo & f);
             const uint32_t eq = ceq ? (c2 ^ (f2 & ta) ^ (eo & tb2) ^ (p0 & eo & f2)) : 0u;
             st = (st & ~(3u << o)) | (lt << o) | (eq << (o + 1));
@@ -376,10 +377,10 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         static_for<qa, qb>([&](auto qi) {
             constexpr OtPlan P = digit_plan(NB, SB, MODE);
             constexpr int q = decltype(qi)::value;
-            constexpr int j = q - qa, tb = 5 * q, hb = P.hpos(q), lb = P.lpos(q);
+            constexpr int j = q - qa, hb = P.hpos(q), lb = P.lpos(q);
             const uint32_t eH = (st >> (hb + 1)) & 1u, lL = (st >> lb) & 1u, eL = (st >> (lb + 1)) & 1u;
-            w |= ((eH ^ tbit(tb)) << (3 * j)) | ((lL ^ tbit(tb + 1)) << (3 * j + 1));
-            if constexpr (P.comb[q].eq != 0) w |= (eL ^ tbit(tb + 2)) << (3 * j + 2);
+            w |= ((eH ^ tbit(P.tpos(q, 0))) << (3 * j)) | ((lL ^ tbit(P.tpos(q, 1))) << (3 * j + 1));
+            if constexpr (P.comb[q].eq != 0) w |= (eL ^ tbit(P.tpos(q, 2))) << (3 * j + 2);
         });
         static_cast<OO *>(a.open_out)[e] = OO(w);
         store_state<SW>(a.state, e, SW(st));

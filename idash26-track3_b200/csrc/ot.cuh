@@ -205,7 +205,8 @@ __device__ __forceinline__ void tt_keygen_elem(const E &A, const OtPlan &P, cons
         if (C.root) v1[3] ^= C.part != 1 ? rho_c : rho_L, v1[4] ^= C.part == 0 ? rho_e : 0u;
         if (!C.eq) v0[4] = 0, v1[4] = 0;
         for (int k = 0; k < 5; k++) {
-            const int i = 5 * q + k;
+            if (!C.eq && (k == 2 || k == 4)) continue;  // no b', c' without an eq AND
+            const int i = P.tpos(q, k);
             t0[i >> 5] |= v0[k] << (i & 31);
             t1[i >> 5] |= v1[k] << (i & 31);
         }

@@ -86,15 +86,71 @@ __host__ __device__ constexpr int state_width(const OtPlan &P)
 template <int W>
 using open_word_t = typename std::conditional<W == 1, uint8_t, typename std::conditional<W == 2, uint16_t, uint32_t>::type>::type;
 
-// the 5 triple bits (a, b, b', c, c') of combine Q from the party's triple words
-template <int Q>
+// the 5 triple bits at POS.. of the party's triple words (a combine's (a, b,
+// b', c, c') where the plan keeps them contiguous)
+template <int POS>
 __host__ __device__ __forceinline__ uint32_t tri5(const uint32_t (&tw)[3])
 {
-    constexpr int b = 5 * Q, w = b / 32, sh = b % 32;
-    if constexpr (sh + 5 <= 32) {
+    constexpr int b = POS, w = b / 32, sh = b % 32;
+    // a packed group never straddles words; the 5q layout ends inside word 2
+    if constexpr (sh + 5 <= 32 || w >= 2) {
         return (tw[w] >> sh) & 31u;
     } else {
         return ((tw[w] >> sh) | (tw[w + 1] << (32 - sh))) & 31u;
+    }
+}
+
+// (a, b, b') of every combine of level L at lane, lane + 1, lane + 2 of one
+// word: one shift and mask when the plan groups them (tpacked), else gathered
+// combine by combine
+template <int MODE, int NB, int SB, int L>
+__host__ __device__ __forceinline__ uint32_t tt_gather3(const uint32_t (&tw)[3])
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
+    if constexpr (P.tpacked) {
+        constexpr int g = P.tpa[qa] - tt_lane(P, qa, L);
+        uint32_t m = 0;
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value;
+            m |= (P.comb[q].eq ? 7u : 3u) << tt_lane(P, q, L);
+        });
+        return (tw[g >> 5] >> (g & 31)) & m;
+    } else {
+        uint32_t t3 = 0;
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value;
+            t3 |= (tri5<P.tpa[q]>(tw) & 7u) << tt_lane(P, q, L);
+        });
+        return t3;
+    }
+}
+
+// (c, c') of every combine of level L at lane, lane + 1
+template <int MODE, int NB, int SB, int L>
+__host__ __device__ __forceinline__ uint32_t tt_gather2(const uint32_t (&tw)[3])
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
+    if constexpr (P.tpacked) {
+        constexpr int g = P.tpc[qa] - tt_lane(P, qa, L);
+        uint32_t m = 0;
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value;
+            m |= (P.comb[q].eq ? 3u : 1u) << tt_lane(P, q, L);
+        });
+        return (tw[g >> 5] >> (g & 31)) & m;
+    } else {
+        uint32_t t2 = 0;
+        static_for<qa, qb>([&](auto qi) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int q = decltype(qi)::value;
+            t2 |= (tri5<P.tpc[q]>(tw) & 3u) << tt_lane(P, q, L);
+        });
+        return t2;
     }
 }
 
@@ -109,15 +165,10 @@ __host__ __device__ __forceinline__ uint32_t tt_open(uint32_t st, const uint32_t
     } else if constexpr (P.comb[qa].part == 2) {
         // the cross combine: e = eq of the hi root, f = lt of the lo root
         constexpr int lo = 2 * P.base[1];
-        const uint32_t g = tri5<qa>(tw);
+        const uint32_t g = tri5<P.tpa[qa]>(tw);  // a, b at bits 0, 1
         return (((st >> 1) ^ g) & 1u) | ((((st >> lo) ^ (g >> 1)) & 1u) << 1);
     } else {
-        uint32_t t3 = 0;  // (a, b, b') of every combine at its lane
-        static_for<qa, qb>([&](auto qi) {
-            constexpr OtPlan P = digit_plan(NB, SB, MODE);
-            constexpr int q = decltype(qi)::value, lane = tt_lane(P, q, L);
-            t3 |= (tri5<q>(tw) & 7u) << lane;
-        });
+        const uint32_t t3 = tt_gather3<MODE, NB, SB, L>(tw);  // (a, b, b') of every combine at its lane
         constexpr uint32_t M = tt_lane_mask(P, L, false), Meq = tt_lane_mask(P, L, true);
         constexpr int S = 1 << L;  // the H node sits S bits above the lane
         const uint32_t e = (st >> (S + 1)) ^ t3;
@@ -137,20 +188,14 @@ __host__ __device__ __forceinline__ uint32_t tt_close(uint32_t st, const uint32_
     if constexpr (qa >= qb) {
         return st;
     } else if constexpr (P.comb[qa].part == 2) {
-        const uint32_t g = tri5<qa>(tw);
+        const uint32_t g = tri5<P.tpa[qa]>(tw), c = tri5<P.tpc[qa]>(tw);  // a, b at bits 0, 1; c at bit 0
         const uint32_t e = O & 1u, f = (O >> 1) & 1u;
-        uint32_t lt = (st ^ (g >> 3) ^ (f & g) ^ (e & (g >> 1))) & 1u;
+        uint32_t lt = (st ^ c ^ (f & g) ^ (e & (g >> 1))) & 1u;
         if constexpr (PARTY == 0) lt ^= e & f;
         return (st & ~3u) | lt;
     } else {
-        uint32_t t3 = 0, t2 = 0;  // (a, b, b') and (c, c') of every combine at its lane
-        static_for<qa, qb>([&](auto qi) {
-            constexpr OtPlan P = digit_plan(NB, SB, MODE);
-            constexpr int q = decltype(qi)::value, lane = tt_lane(P, q, lf);
-            const uint32_t g = tri5<q>(tw);
-            t3 |= (g & 7u) << lane;
-            t2 |= (g >> 3) << lane;
-        });
+        // (a, b, b') and (c, c') of every combine at its lane
+        const uint32_t t3 = tt_gather3<MODE, NB, SB, lf>(tw), t2 = tt_gather2<MODE, NB, SB, lf>(tw);
         constexpr uint32_t M = tt_lane_mask(P, lf, false), Meq = tt_lane_mask(P, lf, true);
         constexpr int S = 1 << lf;
         const uint32_t e = O, f = O >> 1, f2 = O >> 2;

@@ -777,6 +777,9 @@ typedef struct {
     int n, s, D, G0, nd[2], levels, ncomb, tri0, naux;
     int cpart[OT_MAXC], ch[OT_MAXC], cl[OT_MAXC], cout[OT_MAXC], ceq[OT_MAXC], croot[OT_MAXC], clevel[OT_MAXC];
     int pfrom[8][2], pto[8][2];
+    /* TT triple-bit positions: (a, b, b') of combine q at tpa[q] + 0..2, (c, c')
+     * at tpc[q] + 0..1, the full compare's lo mask bit at mu_pos (tt_place) */
+    int tpa[OT_MAXC], tpc[OT_MAXC], mu_pos;
 } ot_plan_t;
 
 /* digit width of digit g (the top digit of a part keeps the remainder) */
@@ -791,6 +794,8 @@ static int ot_width(const ot_plan_t *P, int g)
  * carry only [0, s).  Digit widths: OT 4 and 4; TT ReLU 5 (bw=32) or 4, and 4;
  * TT carry 6.  A digit keeps its equality entries unless it is the lowest
  * digit of the lo part (whose root needs only lt). */
+static void tt_place(ot_plan_t *P);
+
 static int digit_plan_build(int n, int s, int mode, ot_plan_t *P)
 {
     memset(P, 0, sizeof(*P));
@@ -842,10 +847,72 @@ static int digit_plan_build(int n, int s, int mode, ot_plan_t *P)
     }
     P->levels = l, P->ncomb = q, P->tri0 = 6 * P->G0;
     P->naux = (P->tri0 + 5 * q + 127) / 128;
-    return P->naux <= 2 && 5 * q + 1 <= 96 && P->rows <= 24;
+    int ok = P->naux <= 2 && 5 * q + 1 <= 96 && P->rows <= 24;
+    if (ok) tt_place(P);
+    return ok;
 }
 
 static int ot_plan_build(int n, int s, ot_plan_t *P) { return digit_plan_build(n, s, 0, P); }
+
+/* Triple-bit positions of a truth-table plan, restating the CUDA plan's
+ * tt_place (idash26-track3_b200/csrc/digit_plan.cuh): combine q of part p at
+ * AND level l has the lane 2 base[p] + out * 2^(l+1) (base[0] = 0, base[1] =
+ * the hi digit count; the cross combine lane 0).  Per level in order, the
+ * level's (a, b, b') group (7 << lane of each combine computing eq, 3 <<
+ * lane of the others: they have no b') and then its (c, c') group (3 or 1
+ * << lane) are placed first-fit (lowest word, then lowest shift) in the free
+ * bits of the tri words, and last the mask bit of the full compare.  When a
+ * group does not fit, every combine keeps (a, b, b', c, c') at 5q and the
+ * mask bit sits at 5 ncomb. */
+static int place_bits(uint32_t used[3], int words, uint32_t m)
+{
+    int hi = 0;
+    for (int b = 0; b < 32; b++)
+        if ((m >> b) & 1) hi = b;
+    for (int w = 0; w < words; w++)
+        for (int sh = 0; sh + hi < 32; sh++)
+            if (((m << sh) & used[w]) == 0) {
+                used[w] |= m << sh;
+                return 32 * w + sh;
+            }
+    return -1;
+}
+
+static int comb_lane(const ot_plan_t *P, int q)
+{
+    if (P->cpart[q] == 2) return 0;
+    return 2 * (P->cpart[q] == 0 ? 0 : P->nd[0]) + P->cout[q] * (2 << P->clevel[q]);
+}
+
+static void tt_place(ot_plan_t *P)
+{
+    for (int q = 0; q < P->ncomb; q++) P->tpa[q] = 5 * q, P->tpc[q] = 5 * q + 3;
+    P->mu_pos = 5 * P->ncomb;
+    if (P->mode == 0) return;
+    uint32_t used[3] = {0, 0, 0};
+    int pa[OT_MAXC], pc[OT_MAXC];
+    const int words = (5 * P->ncomb + (P->mode == 3) + 31) / 32;
+    for (int l = 1; l <= P->levels; l++) {
+        uint32_t ma = 0, mc = 0;
+        for (int q = 0; q < P->ncomb; q++) {
+            if (P->clevel[q] != l) continue;
+            ma |= (P->ceq[q] ? 7u : 3u) << comb_lane(P, q), mc |= (P->ceq[q] ? 3u : 1u) << comb_lane(P, q);
+        }
+        if (!ma) continue;
+        int ga = place_bits(used, words, ma);
+        if (ga < 0) return;
+        int gc = place_bits(used, words, mc);
+        if (gc < 0) return;
+        for (int q = 0; q < P->ncomb; q++)
+            if (P->clevel[q] == l) pa[q] = ga + comb_lane(P, q), pc[q] = gc + comb_lane(P, q);
+    }
+    int mu = 5 * P->ncomb;
+    if (P->mode == 3 && (mu = place_bits(used, words, 1u)) < 0) return;
+    for (int q = 0; q < P->ncomb; q++) P->tpa[q] = pa[q], P->tpc[q] = pc[q];
+    P->mu_pos = mu;
+}
+
+static int tri_pos(const ot_plan_t *P, int q, int k) { return k < 3 ? P->tpa[q] + k : P->tpc[q] + k - 3; }
 
 static int ot_part(const ot_plan_t *P, int g) { return g < P->nd[0] ? 0 : 1; }
 static int ot_shift(const ot_plan_t *P, int g)
@@ -1113,6 +1180,17 @@ int ref_tt_plan_info(int kind, int n, int s, int *out4)
     return 1;
 }
 
+/* the plan's triple-bit positions: out[2q] = tpa[q], out[2q + 1] = tpc[q]
+ * (q < ncomb), then mu_pos; returns ncomb (0: no plan) */
+int ref_tt_tri_positions(int kind, int n, int s, int *out)
+{
+    ot_plan_t P;
+    if (!digit_plan_build(n, s, tt_mode(kind), &P)) return 0;
+    for (int q = 0; q < P.ncomb; q++) out[2 * q] = P.tpa[q], out[2 * q + 1] = P.tpc[q];
+    out[2 * P.ncomb] = P.mu_pos;
+    return P.ncomb;
+}
+
 static uint32_t tt_stream_word(const aes_ks *dk, uint32_t op, uint64_t i, int w)
 {
     uint8_t b[16];
@@ -1179,13 +1257,14 @@ uint64_t ref_tt_keygen(int kind, int n, int s, uint64_t seed, uint32_t op, uint6
         }
         if (!P.ceq[q]) v0[4] = v1[4] = 0;
         for (int k = 0; k < 5; k++) {
-            int bit = 5 * q + k;
+            if (!P.ceq[q] && (k == 2 || k == 4)) continue; /* no b', c' without an eq AND */
+            int bit = tri_pos(&P, q, k);
             k0->tri[bit / 32] |= (uint32_t)v0[k] << (bit % 32);
             k1->tri[bit / 32] |= (uint32_t)v1[k] << (bit % 32);
         }
     }
     if (P.mode == 3) { /* each party's share of the lo compare's mask bit (P_BITS bits 2 and 3) */
-        int b = 5 * P.ncomb;
+        int b = P.mu_pos;
         k0->tri[b / 32] |= (uint32_t)((blk[0] >> 2) & 1) << (b % 32);
         k1->tri[b / 32] |= (uint32_t)((blk[0] >> 3) & 1) << (b % 32);
     }
@@ -1224,17 +1303,17 @@ void ref_tt_eval_pair(int kind, int n, int s, uint64_t xhat, const ref_tt_key *k
             int hp = comb_hpos(&P, q), lp = comb_lpos(&P, q);
             e_[q] = f_[q] = f2_[q] = 0;
             for (int p = 0; p < 2; p++) {
-                e_[q] ^= (int)((st[p] >> (hp + 1)) & 1) ^ TRI(p, 5 * q);
-                f_[q] ^= (int)((st[p] >> lp) & 1) ^ TRI(p, 5 * q + 1);
-                if (P.ceq[q]) f2_[q] ^= (int)((st[p] >> (lp + 1)) & 1) ^ TRI(p, 5 * q + 2);
+                e_[q] ^= (int)((st[p] >> (hp + 1)) & 1) ^ TRI(p, tri_pos(&P, q, 0));
+                f_[q] ^= (int)((st[p] >> lp) & 1) ^ TRI(p, tri_pos(&P, q, 1));
+                if (P.ceq[q]) f2_[q] ^= (int)((st[p] >> (lp + 1)) & 1) ^ TRI(p, tri_pos(&P, q, 2));
             }
         }
         for (int p = 0; p < 2; p++) {
             for (int q = 0; q < P.ncomb; q++) {
                 if (P.clevel[q] != l) continue;
                 int p0 = p == 0;
-                int a = TRI(p, 5 * q), b = TRI(p, 5 * q + 1), b2 = TRI(p, 5 * q + 2), c = TRI(p, 5 * q + 3),
-                    c2 = TRI(p, 5 * q + 4);
+                int a = TRI(p, tri_pos(&P, q, 0)), b = TRI(p, tri_pos(&P, q, 1)), b2 = TRI(p, tri_pos(&P, q, 2)),
+                    c = TRI(p, tri_pos(&P, q, 3)), c2 = TRI(p, tri_pos(&P, q, 4));
                 int lt = (int)((st[p] >> comb_hpos(&P, q)) & 1) ^ c ^ (f_[q] & a) ^ (e_[q] & b) ^ (p0 & e_[q] & f_[q]);
                 int eq = P.ceq[q] ? (c2 ^ (f2_[q] & a) ^ (e_[q] & b2) ^ (p0 & e_[q] & f2_[q])) : 0;
                 int o = comb_opos(&P, q);
@@ -1255,7 +1334,7 @@ void ref_tt_eval_pair(int kind, int n, int s, uint64_t xhat, const ref_tt_key *k
         int lo = (int)((st[p] >> (2 * P.nd[0])) & 1);
         if (P.mode == 3) { /* full compare and the lo compare with the party's mask share; no equality */
             hi = (int)(st[p] & 1);
-            lo ^= TRI_BIT(kk[p], 5 * P.ncomb);
+            lo ^= TRI_BIT(kk[p], P.mu_pos);
         }
         *out[p] = hi | (lo << 1);
     }

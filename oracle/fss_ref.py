@@ -143,6 +143,8 @@ def lib():
         u32p = ctypes.POINTER(ctypes.c_uint32)
         L.ref_tt_plan_info.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         L.ref_tt_plan_info.restype = ctypes.c_int
+        L.ref_tt_tri_positions.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        L.ref_tt_tri_positions.restype = ctypes.c_int
         L.ref_tt_keygen.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32,
                                     ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(TtKey), ctypes.POINTER(TtKey)]
         L.ref_tt_keygen.restype = ctypes.c_uint64
@@ -285,6 +287,17 @@ def tt_plan_info(kind: int, n: int, s: int) -> dict:
     if not lib().ref_tt_plan_info(kind, n, s, o):
         raise ValueError(f"no truth-table plan for kind={kind} n={n} s={s}")
     return dict(zip(("digits", "rows", "levels", "combines"), list(o)))
+
+
+def tt_tri_positions(kind: int, n: int, s: int) -> dict:
+    """Where the plan keeps each combine's triple bits in a party's triple
+    words: tpa[q] (a, b, b' at +0..2), tpc[q] (c, c' at +0..1), mu (the full
+    compare's lo mask bit)."""
+    o = (ctypes.c_int * 40)()
+    nc = lib().ref_tt_tri_positions(kind, n, s, o)
+    if not nc:
+        raise ValueError(f"no truth-table plan for kind={kind} n={n} s={s}")
+    return {"tpa": [o[2 * q] for q in range(nc)], "tpc": [o[2 * q + 1] for q in range(nc)], "mu": o[2 * nc]}
 
 
 def tt_keygen(kind: int, n: int, s: int, seed: int, op: int, i: int, r_in: int):

@@ -35,3 +35,23 @@ def test_lane_levels_reconstruct_the_plaintext_comparison(tmp_path):
                     str(exe)], check=True, capture_output=True, text=True)
     r = subprocess.run([str(exe), "5000"], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+    # the CUDA plan places every triple bit where the C oracle's keygen puts it
+    from oracle import fss_ref as F
+
+    mode_kind = {1: F.GATE_RELU_TT, 2: F.GATE_LRS_TT, 3: F.GATE_RELU_TTF}
+    seen = 0
+    for line in r.stdout.splitlines():
+        if not line.startswith("positions"):
+            continue
+        head, vals = line.split(":")
+        _, _, mode, _, bw, _, packed = head.split()
+        v = [int(x) for x in vals.split()]
+        want = F.tt_tri_positions(mode_kind[int(mode)], int(bw), 12)
+        got_pairs = v[:-1]
+        assert got_pairs[0::2] == want["tpa"] and got_pairs[1::2] == want["tpc"], (line, want)
+        if int(mode) == 3:
+            assert v[-1] == want["mu"], (line, want)
+        if int(bw) == 32:
+            assert packed == "1", line  # the benchmarked plans group their triple bits by level
+        seen += 1
+    assert seen == 6

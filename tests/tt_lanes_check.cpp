@@ -92,10 +92,12 @@ int check(int trials)
             const uint32_t a = rbit(), b = rbit(), b2 = rbit();
             const uint32_t v = a | (b << 1) | (b2 << 2) | ((a & b) << 3) | ((a & b2) << 4);
             const uint32_t s0 = uint32_t(rng() & 31u), s1 = s0 ^ v;
-            const int bit = 5 * q;
+            // at the plan's triple-bit positions (grouped by level where the plan packs them)
             for (int k = 0; k < 5; k++) {
-                tw[0][(bit + k) / 32] |= ((s0 >> k) & 1u) << ((bit + k) % 32);
-                tw[1][(bit + k) / 32] |= ((s1 >> k) & 1u) << ((bit + k) % 32);
+                if (!P.comb[q].eq && (k == 2 || k == 4)) continue;  // no b', c' without an eq AND
+                const int bit = P.tpos(q, k);
+                tw[0][bit / 32] |= ((s0 >> k) & 1u) << (bit % 32);
+                tw[1][bit / 32] |= ((s1 >> k) & 1u) << (bit % 32);
             }
         }
         uint32_t w[2] = {tt_open<MODE, NB, 12, 1>(st[0], tw[0]), tt_open<MODE, NB, 12, 1>(st[1], tw[1])};
@@ -114,6 +116,22 @@ int check(int trials)
                         want.he, want.ll);
     }
     std::printf("mode %d bw %d levels %d combines %d: %d of %d wrong\n", MODE, NB, P.levels, P.ncomb, bad, trials);
+    // the plan's triple-bit positions: distinct, inside the triple words
+    uint32_t seen[3] = {0u, 0u, 0u};
+    const int nbits = 5 * P.ncomb + (MODE == PLAN_TT_FULL ? 1 : 0);
+    for (int i = 0; i < nbits; i++) {
+        if (i < 5 * P.ncomb && !P.comb[i / 5].eq && (i % 5 == 2 || i % 5 == 4)) continue;
+        const int pos = i < 5 * P.ncomb ? P.tpos(i / 5, i % 5) : P.mu_bit();
+        if (pos < 0 || pos >= 32 * P.tri_words() || ((seen[pos / 32] >> (pos % 32)) & 1u)) {
+            std::printf("mode %d bw %d: triple bit %d at %d collides or overflows\n", MODE, NB, i, pos);
+            bad++;
+        } else {
+            seen[pos / 32] |= 1u << (pos % 32);
+        }
+    }
+    std::printf("positions mode %d bw %d packed %d:", MODE, NB, int(P.tpacked));
+    for (int q = 0; q < P.ncomb; q++) std::printf(" %d %d", P.tpa[q], P.tpc[q]);
+    std::printf(" %d\n", P.mu_bit());
     return bad;
 }
 
