@@ -77,6 +77,17 @@ __device__ __forceinline__ void store_state(void *state, uint64_t e, ST st)
 {
     static_cast<ST *>(state)[e] = st;
 }
+// the same with a 32-bit element index (compiled-in plans)
+template <typename ST>
+__device__ __forceinline__ ST load_state32(const void *state, uint32_t e)
+{
+    return static_cast<const ST *>(state)[e];
+}
+template <typename ST>
+__device__ __forceinline__ void store_state32(void *state, uint32_t e, ST st)
+{
+    static_cast<ST *>(state)[e] = st;
+}
 
 // ---------------------------------------------------------------- garble
 
@@ -279,8 +290,8 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
 // compiled-in plan (level_launch covers levels 1..6), so the two layouts never
 // meet.
 template <int MODE, int NB, int SB, int PARTY, int L>
-__device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, uint32_t &hl, uint32_t &he,
-                                             uint32_t &ll)
+__device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint32_t e, uint32_t N, uint32_t &hl,
+                                             uint32_t &he, uint32_t &ll)
 {
     constexpr OtPlan P = digit_plan(NB, SB, MODE);
     static_assert(P.ok && P.state_bytes() == 4, "compiled-in plans keep a 32-bit state");
@@ -294,13 +305,12 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         return uint32_t(__ldcs(static_cast<const OI *>(a.open_own) + e)) ^
                uint32_t(__ldcs(static_cast<const OI *>(a.open_peer) + e));
     };
-    const uint64_t N = a.N;
     uint32_t st = 0;
-    if constexpr (!(TT && L == 1)) st = uint32_t(load_state<SW>(a.state, e));
+    if constexpr (!(TT && L == 1)) st = uint32_t(load_state32<SW>(a.state, e));
     uint32_t tw[3] = {0u, 0u, 0u};
     static_for<0, P.tri_words()>([&](auto wi) {
         constexpr int w = decltype(wi)::value;
-        tw[w] = __ldcs(a.tri + uint64_t(w) * N + e);
+        tw[w] = __ldcs(a.tri + (uint32_t(w) * N + e));
     });
     auto tbit = [&](int i) { return (tw[i >> 5] >> (i & 31)) & 1u; };
     if constexpr (TT && L == 1) {
@@ -312,15 +322,15 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
             constexpr int W = 1 << P.width(g), sh = P.shift(g), r0 = P.drow0(g);
             constexpr bool deq = P.deq(g) != 0;
             const uint32_t xd = uint32_t(x >> sh) & uint32_t(W - 1);
-            const uint32_t *tb = a.tables + uint64_t(r0) * N + e;
+            const uint32_t *tb = a.tables + (uint32_t(r0) * N + e);
             const uint32_t ie = uint32_t(W) + xd;
             uint32_t lt, eq = 0;
             if constexpr (W <= 32) {
                 lt = (__ldcs(tb) >> xd) & 1u;
-                if constexpr (deq) eq = (__ldcs(tb + uint64_t(ie >> 5) * N) >> (ie & 31)) & 1u;
+                if constexpr (deq) eq = (__ldcs(tb + (ie >> 5) * N) >> (ie & 31)) & 1u;
             } else {
-                lt = (__ldcs(tb + uint64_t(xd >> 5) * N) >> (xd & 31)) & 1u;
-                if constexpr (deq) eq = (__ldcs(tb + uint64_t(ie >> 5) * N) >> (ie & 31)) & 1u;
+                lt = (__ldcs(tb + (xd >> 5) * N) >> (xd & 31)) & 1u;
+                if constexpr (deq) eq = (__ldcs(tb + (ie >> 5) * N) >> (ie & 31)) & 1u;
             }
             st |= (lt << (2 * g)) | (eq << (2 * g + 1));
         });
@@ -328,10 +338,9 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
         constexpr int q = 1 - PARTY;
         constexpr int G = P.garbled_by(q), g0 = q == 0 ? 0 : P.G0;
         static_for<0, G>([&](auto ti) {
-            constexpr OtPlan P = digit_plan(NB, SB, MODE);
             constexpr int t = decltype(ti)::value;
-            const uint32_t rec = __ldcs(a.recv + uint64_t(t) * N + e);
-            const uint32_t word = __ldcs(a.peer_tables + uint64_t(t) * N + e);
+            const uint32_t rec = __ldcs(a.recv + (uint32_t(t) * N + e));
+            const uint32_t word = __ldcs(a.peer_tables + (uint32_t(t) * N + e));
             const uint32_t c = rec & 15u;
             const uint32_t lt = ((word >> c) ^ (rec >> 4)) & 1u, eq = ((word >> (16 + c)) ^ (rec >> 5)) & 1u;
             st |= (lt << (2 * (g0 + t))) | (eq << (2 * (g0 + t) + 1));
@@ -370,7 +379,7 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
     }
     if constexpr (TT && L <= P.levels) {
         static_cast<OO *>(a.open_out)[e] = OO(tt_open<MODE, NB, SB, L>(st, tw));
-        store_state<SW>(a.state, e, SW(st));
+        store_state32<SW>(a.state, e, SW(st));
     } else if constexpr (L <= P.levels) {
         uint32_t w = 0;
         constexpr int qa = P.lvl_first[L - 1], qb = P.lvl_first[L];
@@ -383,7 +392,7 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
             if constexpr (P.comb[q].eq != 0) w |= (eL ^ tbit(P.tpos(q, 2))) << (3 * j + 2);
         });
         static_cast<OO *>(a.open_out)[e] = OO(w);
-        store_state<SW>(a.state, e, SW(st));
+        store_state32<SW>(a.state, e, SW(st));
     } else {
         if constexpr (P.nd[0] != 0) hl = st & 1u, he = (st >> 1) & 1u;
         ll = (st >> (2 * P.base[1])) & 1u;
@@ -396,6 +405,29 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint64_t e, u
 template <int MODE, int NB, int SB, int PARTY, int LV>
 __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
 {
+    if constexpr (NB != 0 && LV != 0) {
+        // compiled-in plan: 32-bit element offsets (ot_level routes gates whose
+        // key rows would reach 2^32 words to the runtime-plan kernel)
+        constexpr bool last = LV > digit_plan(NB, SB, MODE).levels;
+        const uint32_t N = uint32_t(a.N), Npad = (N + 31u) & ~31u, stride = gridDim.x * blockDim.x;
+        for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < Npad; e += stride) {
+            uint32_t hl = 0, he = 0, ll = 0;
+            if (e < N) level_elem_c<MODE, NB, SB, PARTY, LV>(a, e, N, hl, he, ll);
+            if constexpr (last) {
+                const uint32_t wh = __ballot_sync(0xFFFFFFFFu, hl), we = __ballot_sync(0xFFFFFFFFu, he),
+                               wl = __ballot_sync(0xFFFFFFFFu, ll);
+                if ((threadIdx.x & 31) == 0) {
+                    const uint32_t wi = e >> 5;
+                    if (a.bits_hi) {
+                        a.bits_hi[wi] = wh;
+                        if constexpr (MODE != PLAN_TT_FULL) a.bits_hi[uint32_t(a.nw) + wi] = we;
+                    }
+                    a.bits_lo[wi] = wl;
+                }
+            }
+        }
+        return;
+    }
     const uint64_t N = a.N;
     const int l = LV ? LV : a.level;
     const uint64_t Npad = (N + 31) & ~uint64_t(31);
@@ -403,9 +435,7 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < Npad; e += uint64_t(gridDim.x) * blockDim.x) {
         uint32_t hl = 0, he = 0, ll = 0;
         if (e < N) {
-            if constexpr (NB != 0 && LV != 0) {
-                level_elem_c<MODE, NB, SB, PARTY, LV>(a, e, hl, he, ll);
-            } else if (a.P.state_bytes() == 4) {
+            if (a.P.state_bytes() == 4) {
                 level_elem<PARTY, uint32_t>(a.P, a, l, e, hl, he, ll);
             } else {
                 level_elem<PARTY, uint64_t>(a.P, a, l, e, hl, he, ll);
@@ -493,11 +523,13 @@ static void level_launch(const OtLevelArgs &a, int grid, cudaStream_t st)
     }
 }
 
+static bool plan_compiled_in(const GateLayout &L);
+
 template <int MODE, int PARTY>
 static void level_dispatch(const GateLayout &L, const OtLevelArgs &a, int grid, cudaStream_t st)
 {
-    if (L.s == 12 && L.bw == 32) level_launch<MODE, 32, 12, PARTY>(a, grid, st);
-    else if (L.s == 12) level_launch<MODE, 64, 12, PARTY>(a, grid, st);
+    if (plan_compiled_in(L) && L.bw == 32) level_launch<MODE, 32, 12, PARTY>(a, grid, st);
+    else if (plan_compiled_in(L)) level_launch<MODE, 64, 12, PARTY>(a, grid, st);
     else ot_level_kernel<MODE, 0, 0, PARTY, 0><<<grid, 256, 0, st>>>(a);
 }
 
@@ -514,8 +546,15 @@ const OtPlan &gate_digit_plan(const GateLayout &L)
     return tt[tt_mode_of(L.kind)][L.bw == 64 ? 1 : 0][L.s > 0 && L.s < 64 ? L.s : 0];
 }
 
-// the level kernels take the compiled-in plan exactly when level_dispatch does
-static bool plan_compiled_in(const GateLayout &L) { return L.s == 12 && (L.bw == 32 || L.bw == 64); }
+// the level kernels take the compiled-in plan exactly when level_dispatch does:
+// the scale-12 plans, on gates whose key rows stay below 2^32 words (its
+// element offsets are 32-bit)
+static bool plan_compiled_in(const GateLayout &L)
+{
+    if (L.s != 12 || (L.bw != 32 && L.bw != 64)) return false;
+    const OtPlan &P = gate_digit_plan(L);
+    return uint64_t(L.n) * uint64_t(P.rows + P.Gmax + P.tri_words() + 4) < (uint64_t(1) << 32);
+}
 
 int ot_open_bytes(const GateLayout &L, int level)
 {
