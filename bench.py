@@ -74,11 +74,13 @@ A10_SAMPLES_PER_S = 16 / 0.136       # reference README.md:99-101, A10, B=16, bw
 # DRAM bytes (read + write) per algorithmic byte of each backend's comparison
 # kernel, from ncu captures (dram__bytes_read.sum + dram__bytes_write.sum over
 # the kernel's algorithmic bytes):
-#   tt : ot_level_kernel, AND-tree levels 2 and 3 of the full-compare ReLU gate
-#        at 2^23 elements: 148.2 MB of DRAM traffic for 201.3 MB of
-#        algorithmic bytes per launch (its writes stay in L2 when it ends);
+#   tt : ot_level_kernel, all four levels of both parties of one full-compare
+#        ReLU gate at 2^23 elements (microbench.py tt): 162.4 MB of DRAM
+#        traffic for 183.0 MB of algorithmic bytes per launch on average (the
+#        level-1 key reads reach DRAM once; part of the openings and state
+#        written stays in L2 for the next level);
 #   dcf: gate_round1_kernel, three-part ReLU(ARS) at B=16: 300.0 MB for 295.9 MB.
-NCU_DRAM_BYTES_PER_ALG_BYTE = {"tt": 148.2 / 201.3, "dcf": 300.0 / 295.9, "ot": None}
+NCU_DRAM_BYTES_PER_ALG_BYTE = {"tt": 162.4 / 183.0, "dcf": 300.0 / 295.9, "ot": None}
 
 
 def parse():
