@@ -38,6 +38,10 @@ struct Channel {
     virtual int status(int party) { (void)party; return DDG_OK; }
     // exchange() needs the caller's `recv` buffer (it copies the peer's bytes there)
     virtual bool needs_recv_buffer() const { return !same_device(); }
+    // the peer's bytes of an exchange stay valid to the end of the forward:
+    // the peer's own buffer in place (an in-process pair) or the caller's recv
+    // buffer; not a channel slot that later exchanges overwrite
+    virtual bool peer_stable() const { return same_device() || needs_recv_buffer(); }
     // one party's forward, captured on its own stream, can be replayed from a
     // CUDA graph (every handoff of the capture happens on the device); `why`
     // says what stands in the way otherwise

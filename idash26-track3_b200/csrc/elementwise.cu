@@ -154,7 +154,7 @@ int rowsum_plus(const T *a, const T *m, T *out, uint64_t rows, int cols, cudaStr
 }
 
 template <typename T>
-__global__ void k_pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F)
+__global__ void k_pool_split(const T *cur, const T *cur2, T *even, T *diff, int B, int cnt, int F)
 {
     const int pairs = cnt / 2;
     const uint64_t n = uint64_t(B) * pairs * F;
@@ -165,7 +165,8 @@ __global__ void k_pool_split(const T *cur, T *even, T *diff, int B, int cnt, int
         const int p = int(bp % pairs);
         const uint64_t b = bp / pairs;
         const uint64_t base = (b * cnt + 2 * p) * uint64_t(F) + f;
-        const T ev = cur[base], od = cur[base + F];
+        T ev = cur[base], od = cur[base + F];
+        if (cur2) ev += cur2[base], od += cur2[base + F];
         even[e] = ev;
         diff[e] = od - ev;
     }
@@ -194,15 +195,17 @@ struct Vec16<uint64_t> {
 };
 
 template <typename T>
-__global__ void k_pool_split_v(const typename Vec16<T>::V *cur, typename Vec16<T>::V *even,
-                               typename Vec16<T>::V *diff, uint32_t pairs, uint32_t cnt, uint32_t fv, uint32_t nvec)
+__global__ void k_pool_split_v(const typename Vec16<T>::V *cur, const typename Vec16<T>::V *cur2,
+                               typename Vec16<T>::V *even, typename Vec16<T>::V *diff, uint32_t pairs, uint32_t cnt,
+                               uint32_t fv, uint32_t nvec)
 {
     using W = Vec16<T>;
     for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += gridDim.x * blockDim.x) {
         const uint32_t row = t / fv, c = t - row * fv;
         const uint32_t b = row / pairs, p = row - b * pairs;
         const uint64_t src = (uint64_t(b) * cnt + 2 * p) * fv + c;
-        const typename W::V ev = cur[src], od = cur[src + fv];
+        typename W::V ev = cur[src], od = cur[src + fv];
+        if (cur2) ev = W::add(ev, cur2[src]), od = W::add(od, cur2[src + fv]);
         even[t] = ev;
         diff[t] = W::sub(od, ev);
     }
@@ -210,7 +213,8 @@ __global__ void k_pool_split_v(const typename Vec16<T>::V *cur, typename Vec16<T
 
 template <typename T>
 __global__ void k_pool_merge_v(const typename Vec16<T>::V *even, const typename Vec16<T>::V *relu,
-                               const typename Vec16<T>::V *cur, typename Vec16<T>::V *next, uint32_t pairs,
+                               const typename Vec16<T>::V *relu2, const typename Vec16<T>::V *cur,
+                               const typename Vec16<T>::V *cur2, typename Vec16<T>::V *next, uint32_t pairs,
                                uint32_t cnt, uint32_t fv, uint32_t nvec)
 {
     using W = Vec16<T>;
@@ -218,27 +222,36 @@ __global__ void k_pool_merge_v(const typename Vec16<T>::V *even, const typename 
     for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += gridDim.x * blockDim.x) {
         const uint32_t row = t / fv, c = t - row * fv;
         const uint32_t b = row / nxt, q = row - b * nxt;
-        next[t] = q < pairs ? W::add(even[(uint64_t(b) * pairs + q) * fv + c], relu[(uint64_t(b) * pairs + q) * fv + c])
-                            : cur[(uint64_t(b) * cnt + (cnt - 1)) * fv + c];
+        typename W::V v;
+        if (q < pairs) {
+            const uint64_t i = (uint64_t(b) * pairs + q) * fv + c;
+            v = W::add(even[i], relu[i]);
+            if (relu2) v = W::add(v, relu2[i]);
+        } else {
+            const uint64_t i = (uint64_t(b) * cnt + (cnt - 1)) * fv + c;
+            v = cur[i];
+            if (cur2) v = W::add(v, cur2[i]);
+        }
+        next[t] = v;
     }
 }
 
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <typename T>
-int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st)
+int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st, const T *cur2)
 {
     const uint64_t n = uint64_t(B) * (cnt / 2) * F;
     if (!n) return DDG_OK;
     constexpr int L = Vec16<T>::L;
-    if (F % L == 0 && n / L < (1ull << 31) && al16(cur) && al16(even) && al16(diff)) {
+    if (F % L == 0 && n / L < (1ull << 31) && al16(cur) && al16(cur2) && al16(even) && al16(diff)) {
         using V = typename Vec16<T>::V;
         const uint32_t nvec = uint32_t(n / L);
-        k_pool_split_v<T><<<ew_grid(nvec), 256, 0, st>>>(reinterpret_cast<const V *>(cur), reinterpret_cast<V *>(even),
-                                                         reinterpret_cast<V *>(diff), uint32_t(cnt / 2), uint32_t(cnt),
-                                                         uint32_t(F / L), nvec);
+        k_pool_split_v<T><<<ew_grid(nvec), 256, 0, st>>>(
+            reinterpret_cast<const V *>(cur), reinterpret_cast<const V *>(cur2), reinterpret_cast<V *>(even),
+            reinterpret_cast<V *>(diff), uint32_t(cnt / 2), uint32_t(cnt), uint32_t(F / L), nvec);
     } else {
-        k_pool_split<T><<<ew_grid(n), 256, 0, st>>>(cur, even, diff, B, cnt, F);
+        k_pool_split<T><<<ew_grid(n), 256, 0, st>>>(cur, cur2, even, diff, B, cnt, F);
     }
     note_launch();
     DDG_CUDA(cudaGetLastError());
@@ -246,7 +259,8 @@ int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream
 }
 
 template <typename T>
-__global__ void k_pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F)
+__global__ void k_pool_merge(const T *even, const T *relu, const T *relu2, const T *cur, const T *cur2, T *next,
+                             int B, int cnt, int F)
 {
     const int pairs = cnt / 2, nxt = pairs + (cnt & 1);
     const uint64_t n = uint64_t(B) * nxt * F;
@@ -260,27 +274,33 @@ __global__ void k_pool_merge(const T *even, const T *relu, const T *cur, T *next
         if (q < pairs) {
             const uint64_t s = (b * pairs + q) * uint64_t(F) + f;
             v = even[s] + relu[s];
+            if (relu2) v += relu2[s];
         } else {
-            v = cur[(b * cnt + (cnt - 1)) * uint64_t(F) + f];
+            const uint64_t s = (b * cnt + (cnt - 1)) * uint64_t(F) + f;
+            v = cur[s];
+            if (cur2) v += cur2[s];
         }
         next[e] = v;
     }
 }
 
 template <typename T>
-int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F, cudaStream_t st)
+int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F, cudaStream_t st,
+               const T *relu2, const T *cur2)
 {
     const uint64_t n = uint64_t(B) * (cnt / 2 + (cnt & 1)) * F;
     if (!n) return DDG_OK;
     constexpr int L = Vec16<T>::L;
-    if (F % L == 0 && n / L < (1ull << 31) && al16(even) && al16(relu) && al16(cur) && al16(next)) {
+    if (F % L == 0 && n / L < (1ull << 31) && al16(even) && al16(relu) && al16(relu2) && al16(cur) && al16(cur2) &&
+        al16(next)) {
         using V = typename Vec16<T>::V;
         const uint32_t nvec = uint32_t(n / L);
         k_pool_merge_v<T><<<ew_grid(nvec), 256, 0, st>>>(
-            reinterpret_cast<const V *>(even), reinterpret_cast<const V *>(relu), reinterpret_cast<const V *>(cur),
-            reinterpret_cast<V *>(next), uint32_t(cnt / 2), uint32_t(cnt), uint32_t(F / L), nvec);
+            reinterpret_cast<const V *>(even), reinterpret_cast<const V *>(relu), reinterpret_cast<const V *>(relu2),
+            reinterpret_cast<const V *>(cur), reinterpret_cast<const V *>(cur2), reinterpret_cast<V *>(next),
+            uint32_t(cnt / 2), uint32_t(cnt), uint32_t(F / L), nvec);
     } else {
-        k_pool_merge<T><<<ew_grid(n), 256, 0, st>>>(even, relu, cur, next, B, cnt, F);
+        k_pool_merge<T><<<ew_grid(n), 256, 0, st>>>(even, relu, relu2, cur, cur2, next, B, cnt, F);
     }
     note_launch();
     DDG_CUDA(cudaGetLastError());
@@ -405,8 +425,9 @@ int split_shares(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uint32_t
                               T *, cudaStream_t);                                                                \
     template int beaver_ew_z<T>(const EwShape &, Bcast, const T *, const T *, const T *, T *, cudaStream_t);     \
     template int rowsum_plus<T>(const T *, const T *, T *, uint64_t, int, cudaStream_t);                         \
-    template int pool_split<T>(const T *, T *, T *, int, int, int, cudaStream_t);                                \
-    template int pool_merge<T>(const T *, const T *, const T *, T *, int, int, int, cudaStream_t);               \
+    template int pool_split<T>(const T *, T *, T *, int, int, int, cudaStream_t, const T *);                     \
+    template int pool_merge<T>(const T *, const T *, const T *, T *, int, int, int, cudaStream_t, const T *,       \
+                               const T *);                                                                        \
     template int concat_rows<T>(const T *, const T *, T *, int, int, int, cudaStream_t);                         \
     template int unmask_ars<T>(const T *, const T *, T *, uint64_t, int, cudaStream_t);                          \
     template int i64_to_ring<T>(const int64_t *, T *, uint64_t, int, cudaStream_t);                              \

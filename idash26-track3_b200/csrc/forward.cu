@@ -180,6 +180,7 @@ static int eval_t(Party &P, int B, const void *x_sh, const void *adj_sh, const v
 {
     EvalExec<T> e;
     e.B = B, e.bw = P.bw, e.s = P.s, e.st = P.stream, e.P = &P, e.p = P.party;
+    e.lazy = P.chan->peer_stable();  // consumers add the two shares of an opening on load
     const uint64_t sizes[4] = {uint64_t(B) * NMAX * FEAT, uint64_t(B) * NMAX * NMAX, uint64_t(B) * NMAX * POOL,
                                uint64_t(B) * PROT};
     const void *src[4] = {x_sh, adj_sh, mask_sh, prot_sh};

@@ -305,7 +305,7 @@ template <typename T>
 struct Round2Args {
     int kind, n, s, party;
     uint64_t N, nw;
-    const T *xhat;
+    const T *xhat, *xhat2;  // xhat2: second addend of the opened input (may be null)
     const uint32_t *hi_own, *hi_peer, *lo_own, *lo_peer;
     const T *words;
     T *share;
@@ -319,7 +319,8 @@ __global__ void gate_round2_kernel(const __grid_constant__ Round2Args<T> a)
     const T p0 = a.party == 0 ? T(1) : T(0);
     const T two_ns = T(1) << (n - s);
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < N; e += uint64_t(gridDim.x) * blockDim.x) {
-        const T x = a.xhat[e];
+        T x = a.xhat[e];
+        if (a.xhat2) x += a.xhat2[e];
         const uint64_t wi = e >> 5;
         const uint32_t bi = uint32_t(e & 31);
         T ch = 0, cl = 0, eh = 0;
@@ -520,12 +521,14 @@ int gate_round1_t(const GateLayout &L, const void *xhat, const void *key, uint32
 
 template <typename T>
 int gate_round2_t(const GateLayout &L, int party, const void *xhat, const uint32_t *hi_own, const uint32_t *hi_peer,
-                  const uint32_t *lo_own, const uint32_t *lo_peer, const void *key, void *share, cudaStream_t st)
+                  const uint32_t *lo_own, const uint32_t *lo_peer, const void *key, void *share, cudaStream_t st,
+                  const void *xhat2)
 {
     if (L.n == 0) return DDG_OK;
     Round2Args<T> a;
     a.kind = L.kind, a.n = L.bw, a.s = L.s, a.party = party, a.N = L.n, a.nw = (L.n + 31) / 32;
     a.xhat = static_cast<const T *>(xhat);
+    a.xhat2 = static_cast<const T *>(xhat2);
     a.hi_own = hi_own, a.hi_peer = hi_peer, a.lo_own = lo_own, a.lo_peer = lo_peer;
     a.words = reinterpret_cast<const T *>(static_cast<const uint8_t *>(key) + L.words);
     a.share = static_cast<T *>(share);
@@ -564,10 +567,12 @@ int gate_round1(const GateLayout &L, const void *xhat, const void *key, uint32_t
 }
 
 int gate_round2(const GateLayout &L, int party, const void *xhat, const uint32_t *hi_own, const uint32_t *hi_peer,
-                const uint32_t *lo_own, const uint32_t *lo_peer, const void *key, void *share, cudaStream_t st)
+                const uint32_t *lo_own, const uint32_t *lo_peer, const void *key, void *share, cudaStream_t st,
+                const void *xhat2)
 {
-    return L.bw == 32 ? gate_round2_t<uint32_t>(L, party, xhat, hi_own, hi_peer, lo_own, lo_peer, key, share, st)
-                      : gate_round2_t<uint64_t>(L, party, xhat, hi_own, hi_peer, lo_own, lo_peer, key, share, st);
+    return L.bw == 32
+               ? gate_round2_t<uint32_t>(L, party, xhat, hi_own, hi_peer, lo_own, lo_peer, key, share, st, xhat2)
+               : gate_round2_t<uint64_t>(L, party, xhat, hi_own, hi_peer, lo_own, lo_peer, key, share, st, xhat2);
 }
 
 }  // namespace ddg

@@ -26,7 +26,10 @@ enum Input { IN_X = 0, IN_ADJ = 1, IN_MASK = 2, IN_PROT = 3 };
 
 template <typename T>
 struct Tn {
-    T *v = nullptr;          // eval: public masked value; dealer: mask
+    // eval: public masked value (v + v2 while an opening is still held as the
+    // two parties' shares: EvalExec::val adds them); dealer: mask
+    mutable T *v = nullptr;
+    mutable const T *v2 = nullptr;
     uint64_t n = 0;
     const T *ms0 = nullptr;  // eval: own mask share; dealer: party 0's
     const T *ms1 = nullptr;  // dealer: party 1's
@@ -304,6 +307,11 @@ struct EvalExec : ExecBase<T> {
     using ExecBase<T>::ok;
     Party *P = nullptr;
     int p = 0;
+    // openings stay as (own share, peer share) until a consumer needs one value
+    // (the level-1 and round-2 kernels of the truth-table gates, the packed
+    // GEMM's operand packing and the pool levels add them on load); only where
+    // the peer's bytes stay valid to the end of the forward (Channel::peer_stable)
+    bool lazy = false;
     const T *in[4] = {};
     cudaEvent_t in_ready[4] = {};  // host inputs: copy-stream event to wait on before first use
     T *out = nullptr;
@@ -340,6 +348,26 @@ struct EvalExec : ExecBase<T> {
         if (this->err == DDG_OK) ok(ew_add<T>(pub, share, peer, n, this->st));
         return pub;
     }
+    // open `share` into t (t.n set): the sum now, or the two addends when lazy
+    void open_to(Tn<T> &t, const T *share)
+    {
+        if (!lazy) {
+            t.v = open(share, t.n);
+            return;
+        }
+        t.v2 = peer_of(share, words(t.n));
+        t.v = const_cast<T *>(share);
+    }
+    // the value of t as one array (adds a held opening once, in place)
+    const T *val(const Tn<T> &t)
+    {
+        if (t.v2 && this->err == DDG_OK) {
+            T *m = alloc(t.n);
+            if (this->err == DDG_OK) ok(ew_add<T>(m, t.v, t.v2, t.n, this->st));
+            t.v = m, t.v2 = nullptr;
+        }
+        return t.v;
+    }
     Tn<T> reveal_input(int which, uint64_t n)
     {
         Tn<T> t;
@@ -348,7 +376,7 @@ struct EvalExec : ExecBase<T> {
         T *sh = alloc(n);
         wait_input(which);
         if (this->err == DDG_OK) ok(ew_add<T>(sh, in[which], t.ms0, n, this->st));
-        t.v = open(sh, n);
+        open_to(t, sh);
         return t;
     }
     Tn<T> reveal_degree(uint64_t rows, int cols)
@@ -360,7 +388,7 @@ struct EvalExec : ExecBase<T> {
         T *sh = alloc(rows);
         wait_input(IN_ADJ);
         if (this->err == DDG_OK) ok(rowsum_plus<T>(in[IN_ADJ], ms, sh, rows, cols, this->st));
-        t.v = open(sh, rows);
+        open_to(t, sh);
         return t;
     }
     Tn<T> reveal_public(int which, uint64_t n)
@@ -379,16 +407,18 @@ struct EvalExec : ExecBase<T> {
         if (relu_backend() == DDG_RELU_TT) {
             TtLutLayout L = tt_lut_layout(this->bw, d.n);
             const uint8_t *k = key_at(L.bytes);
-            if (this->err == DDG_OK) ok(tt_lut_eval<T>(L, d.v, k, sh, this->st));
-            t.v = open(sh, d.n);
+            const T *dv = val(d);
+            if (this->err == DDG_OK) ok(tt_lut_eval<T>(L, dv, k, sh, this->st));
+            open_to(t, sh);
             t.ms0 = reinterpret_cast<const T *>(k + L.rout);
             return t;
         }
         LutLayout L = lut_layout(this->bw, d.n);
         const uint8_t *k = key_at(L.bytes);
+        const T *dv = val(d);
         if (this->err == DDG_OK)
-            ok(lut_eval<T>(L, p, d.v, static_cast<const T *>(P->w.table), k, sh, this->st));
-        t.v = open(sh, d.n);
+            ok(lut_eval<T>(L, p, dv, static_cast<const T *>(P->w.table), k, sh, this->st));
+        open_to(t, sh);
         t.ms0 = reinterpret_cast<const T *>(k + L.rout);
         return t;
     }
@@ -401,10 +431,11 @@ struct EvalExec : ExecBase<T> {
         ensure_ms(a), ensure_ms(b);
         const T *Z = reinterpret_cast<const T *>(key_at(words(sh.n)));
         T *s = alloc(sh.n);
-        if (this->err == DDG_OK) ok(beaver_ew<T>(p, sh, bc, a.v, b.v, a.ms0, b.ms0, Z, s, this->st));
+        const T *av = val(a), *bv = val(b);
+        if (this->err == DDG_OK) ok(beaver_ew<T>(p, sh, bc, av, bv, a.ms0, b.ms0, Z, s, this->st));
         Tn<T> t;
         t.n = sh.n;
-        t.v = open(s, sh.n);
+        open_to(t, s);
         return t;
     }
     Tn<T> matmul(Tn<T> &A, Tn<T> &H, int K)
@@ -417,18 +448,18 @@ struct EvalExec : ExecBase<T> {
             // p0 * A_hat . H_hat - A_hat . [r_H] - [r_A] . H_hat + Z   (per sample)
             GemmArgs<T> g;
             g.M = NMAX, g.N = K, g.K = NMAX, g.batch = this->B;
-            g.A1 = A.v, g.lda1 = NMAX, g.sA1 = int64_t(NMAX) * NMAX;
-            g.B1 = H.v, g.ldb1 = K, g.sB1 = int64_t(NMAX) * K, g.s1 = p == 0 ? T(1) : T(0);
+            g.A1 = A.v, g.A1b = A.v2, g.lda1 = NMAX, g.sA1 = int64_t(NMAX) * NMAX;
+            g.B1 = H.v, g.B1b = H.v2, g.ldb1 = K, g.sB1 = int64_t(NMAX) * K, g.s1 = p == 0 ? T(1) : T(0);
             g.B1m = H.ms0, g.sB1m = int64_t(NMAX) * K;
             g.A2 = A.ms0, g.lda2 = NMAX, g.sA2 = int64_t(NMAX) * NMAX;
-            g.B2 = H.v, g.ldb2 = K, g.sB2 = int64_t(NMAX) * K;
+            g.B2 = H.v, g.B2b = H.v2, g.ldb2 = K, g.sB2 = int64_t(NMAX) * K;
             g.Add = Z, g.ldAdd = K, g.sAdd = int64_t(NMAX) * K;
             g.C = s, g.ldc = K, g.sC = int64_t(NMAX) * K;
             ok(ring_gemm<T>(g, this->st));
         }
         Tn<T> t;
         t.n = n;
-        t.v = open(s, n);
+        open_to(t, s);
         return t;
     }
     Tn<T> fc(const Tn<T> &x, int l, int M)
@@ -442,7 +473,7 @@ struct EvalExec : ExecBase<T> {
             if (this->err == DDG_OK) {
                 GemmArgs<T> g;  // x_hat . W + b<<s + C
                 g.M = M, g.N = N, g.K = K;
-                g.A1 = x.v, g.lda1 = K;
+                g.A1 = x.v, g.A1b = x.v2, g.lda1 = K;
                 g.B1 = static_cast<const T *>(P->w.W[l]), g.ldb1 = N;
                 g.bias = static_cast<const T *>(P->w.b2s[l]);
                 g.Add = C, g.ldAdd = N;
@@ -453,7 +484,7 @@ struct EvalExec : ExecBase<T> {
         }
         Tn<T> t;
         t.n = n;
-        t.v = open(s, n);
+        open_to(t, s);
         return t;
     }
     // AND-tree gates.  OT kinds: garbled digit tables first (one message);
@@ -469,6 +500,7 @@ struct EvalExec : ExecBase<T> {
         void *state = this->alloc_bytes(sc.state);
         uint32_t *tri = nullptr;
         const uint32_t *ptab = nullptr;
+        if (L.ot) val(x);  // the OT garble step reads one input array
         if (L.ot) {
             uint32_t *tab = static_cast<uint32_t *>(this->alloc_bytes(sc.tables));
             tri = static_cast<uint32_t *>(this->alloc_bytes(sc.tri));
@@ -481,7 +513,7 @@ struct EvalExec : ExecBase<T> {
             const uint64_t ob = (uint64_t(ot_open_bytes(L, l)) * n + 3) & ~uint64_t(3);
             void *o = this->alloc_bytes(ob);
             if (this->err == DDG_OK)
-                ok(ot_level(L, p, l, k, ptab, oo, po, state, tri, o, nullptr, nullptr, this->st, x.v));
+                ok(ot_level(L, p, l, k, ptab, oo, po, state, tri, o, nullptr, nullptr, this->st, x.v, x.v2));
             po = peer_of(o, ob);
             oo = o;
         }
@@ -491,15 +523,15 @@ struct EvalExec : ExecBase<T> {
         uint32_t *bl = bits + (nb - 1) * nw;
         if (this->err == DDG_OK)
             ok(ot_level(L, p, Pl.levels + 1, k, ptab, oo, po, state, tri, nullptr, nb > 1 ? bits : nullptr, bl,
-                        this->st, x.v));
+                        this->st, x.v, x.v2));
         const uint32_t *peer = reinterpret_cast<const uint32_t *>(peer_of(bits, 4 * nw * nb));
         T *sh = alloc(n);
         if (this->err == DDG_OK)
             ok(gate_round2(L, p, x.v, nb > 1 ? bits : nullptr, nb > 1 ? peer : nullptr, bl,
-                           peer ? peer + (nb - 1) * nw : nullptr, k, sh, this->st));
+                           peer ? peer + (nb - 1) * nw : nullptr, k, sh, this->st, x.v2));
         Tn<T> t;
         t.n = n;
-        t.v = open(sh, n);
+        open_to(t, sh);
         return t;
     }
     Tn<T> gate(int kind, const Tn<T> &x)
@@ -507,6 +539,7 @@ struct EvalExec : ExecBase<T> {
         GateLayout L = gate_layout(kind, this->bw, this->s, x.n);
         const uint8_t *k = key_at(L.bytes);
         if (L.ot || L.tt) return gate_digits(L, k, x);
+        val(x);  // the DCF rounds read one input array
         const uint64_t nw = (x.n + 31) / 32;
         // split gates also open the equality bits, three-part splits the middle DCF's two bits
         const int nh = L.hi ? (L.mid ? 4 : (L.H.eq ? 2 : 1)) : 0;
@@ -520,7 +553,7 @@ struct EvalExec : ExecBase<T> {
         if (this->err == DDG_OK) ok(gate_round2(L, p, x.v, bh, ph, bl, pl, k, s, this->st));
         Tn<T> t;
         t.n = x.n;
-        t.v = open(s, x.n);
+        open_to(t, s);
         return t;
     }
     void pool_split(const Tn<T> &cur, int cnt, Tn<T> &even, Tn<T> &diff)
@@ -528,29 +561,33 @@ struct EvalExec : ExecBase<T> {
         const uint64_t n = uint64_t(this->B) * (cnt / 2) * POOL;
         even.n = diff.n = n;
         even.v = alloc(n), diff.v = alloc(n);
-        if (this->err == DDG_OK) ok(::ddg::pool_split<T>(cur.v, even.v, diff.v, this->B, cnt, POOL, this->st));
+        if (this->err == DDG_OK)
+            ok(::ddg::pool_split<T>(cur.v, even.v, diff.v, this->B, cnt, POOL, this->st, cur.v2));
     }
     Tn<T> pool_merge(const Tn<T> &even, const Tn<T> &r, const Tn<T> &cur, int cnt)
     {
         Tn<T> t;
         t.n = uint64_t(this->B) * (cnt / 2 + (cnt & 1)) * POOL;
         t.v = alloc(t.n);
-        if (this->err == DDG_OK) ok(::ddg::pool_merge<T>(even.v, r.v, cur.v, t.v, this->B, cnt, POOL, this->st));
+        if (this->err == DDG_OK)
+            ok(::ddg::pool_merge<T>(even.v, r.v, cur.v, t.v, this->B, cnt, POOL, this->st, r.v2, cur.v2));
         return t;
     }
     Tn<T> concat(const Tn<T> &a, const Tn<T> &b)
     {
         Tn<T> t;
         t.n = a.n + b.n;
+        const T *av = val(a), *bv = val(b);
         t.v = alloc(t.n);
-        if (this->err == DDG_OK) ok(concat_rows<T>(a.v, b.v, t.v, this->B, PROT, PROT, this->st));
+        if (this->err == DDG_OK) ok(concat_rows<T>(av, bv, t.v, this->B, PROT, PROT, this->st));
         return t;
     }
     void output(const Tn<T> &o)
     {
         const T *r = reinterpret_cast<const T *>(key_at(words(o.n)));
+        const T *ov = val(o);
         out = alloc(o.n);
-        if (this->err == DDG_OK) ok(unmask_ars<T>(o.v, r, out, o.n, this->s, this->st));
+        if (this->err == DDG_OK) ok(unmask_ars<T>(ov, r, out, o.n, this->s, this->st));
     }
 };
 

@@ -19,6 +19,9 @@ struct GemmArgs {
     int64_t ldAdd = 0, sAdd = 0;
     T *C = nullptr;
     int64_t ldc = 0, sC = 0;
+    // optional second addends of A1, B1, B2 (same strides): the operand is
+    // A1 + A1b etc., an opened value still held as the two parties' shares
+    const T *A1b = nullptr, *B1b = nullptr, *B2b = nullptr;
 };
 
 // tensor-core limb GEMM where the shape allows (ring_gemm_tc.cu), else the CUDA-core kernel
@@ -68,12 +71,15 @@ template <typename T>
 int rowsum_plus(const T *a, const T *m, T *out, uint64_t rows, int cols, cudaStream_t st);
 
 // max-pool tree level over cur (B, cnt, F): even[b,p,f] = cur[b,2p,f],
-// diff[b,p,f] = cur[b,2p+1,f] - cur[b,2p,f] for p < cnt/2
+// diff[b,p,f] = cur[b,2p+1,f] - cur[b,2p,f] for p < cnt/2.  A non-null second
+// addend (cur2, relu2) is added on load: an opened value still held as the
+// two parties' shares.
 template <typename T>
-int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st);
+int pool_split(const T *cur, T *even, T *diff, int B, int cnt, int F, cudaStream_t st, const T *cur2 = nullptr);
 // next[b,p,f] = even[b,p,f] + relu[b,p,f] (p < cnt/2), carried cur[b,cnt-1,f] if cnt odd
 template <typename T>
-int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F, cudaStream_t st);
+int pool_merge(const T *even, const T *relu, const T *cur, T *next, int B, int cnt, int F, cudaStream_t st,
+               const T *relu2 = nullptr, const T *cur2 = nullptr);
 
 // out (B, wa+wb) = [a (B, wa) | b (B, wb)] per row
 template <typename T>

@@ -171,7 +171,7 @@ struct OtLevelArgs {
     const uint8_t *recv;         // OT level 1: the party's receiver records [slot][N]
     const uint32_t *peer_tables; // OT level 1: the peer's tables [slot][N]
     const uint32_t *c0;          // OT: party 0's explicit triple c bits [N]
-    const void *xhat;            // TT level 1: the masked input (ring words)
+    const void *xhat, *xhat2;    // TT level 1: the masked input (ring words; xhat2: its second addend or null)
     const uint32_t *tables;      // TT level 1: the party's digit truth-table rows [row][N]
     const void *open_own, *open_peer;  // level >= 2: the previous level's openings (ot_open_bytes each)
     void *state;
@@ -196,8 +196,11 @@ __device__ __forceinline__ void level_elem(const OtPlan &P, const OtLevelArgs &a
         if (w < P.tri_words()) tw[w] = __ldcs(a.tri + uint64_t(w) * N + e);
     if (tt && l == 1) {
         // the party's share of every digit's (lt, eq): its table read at the public digit
-        const uint64_t x = P.n == 32 ? uint64_t(__ldcs(static_cast<const uint32_t *>(a.xhat) + e))
-                                     : __ldcs(static_cast<const unsigned long long *>(a.xhat) + e);
+        uint64_t x = P.n == 32 ? uint64_t(__ldcs(static_cast<const uint32_t *>(a.xhat) + e))
+                               : __ldcs(static_cast<const unsigned long long *>(a.xhat) + e);
+        if (a.xhat2)
+            x = P.n == 32 ? uint64_t(uint32_t(x + __ldcs(static_cast<const uint32_t *>(a.xhat2) + e)))
+                          : x + __ldcs(static_cast<const unsigned long long *>(a.xhat2) + e);
 #pragma unroll
         for (int g = 0; g < OT_MAX_DIGITS; g++) {
             if (g >= P.D) break;
@@ -314,8 +317,15 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint32_t e, u
     });
     auto tbit = [&](int i) { return (tw[i >> 5] >> (i & 31)) & 1u; };
     if constexpr (TT && L == 1) {
-        const uint64_t x = NB == 32 ? uint64_t(__ldcs(static_cast<const uint32_t *>(a.xhat) + e))
-                                    : __ldcs(static_cast<const unsigned long long *>(a.xhat) + e);
+        uint64_t x;
+        if constexpr (NB == 32) {
+            uint32_t x32 = __ldcs(static_cast<const uint32_t *>(a.xhat) + e);
+            if (a.xhat2) x32 += __ldcs(static_cast<const uint32_t *>(a.xhat2) + e);
+            x = x32;
+        } else {
+            x = __ldcs(static_cast<const unsigned long long *>(a.xhat) + e);
+            if (a.xhat2) x += __ldcs(static_cast<const unsigned long long *>(a.xhat2) + e);
+        }
         static_for<0, P.D>([&](auto gi) {
             constexpr OtPlan P = digit_plan(NB, SB, MODE);
             constexpr int g = decltype(gi)::value;
@@ -570,7 +580,7 @@ static int ot_state_bytes(const GateLayout &L)
 
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
              const void *open_own, const void *open_peer, void *state, const uint32_t *tri, void *open_out,
-             uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat)
+             uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat, const void *xhat2)
 {
     if (L.n == 0) return DDG_OK;
     DDG_CHECK(L.ot || L.tt, DDG_ERR_ARG, "not an AND-tree gate");
@@ -584,7 +594,7 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     a.recv = L.ot ? k + L.ot_recv : nullptr;
     a.peer_tables = peer_tables;
     a.c0 = L.ot ? reinterpret_cast<const uint32_t *>(k + L.ot_c0) : nullptr;
-    a.xhat = xhat;
+    a.xhat = xhat, a.xhat2 = L.tt && level == 1 ? xhat2 : nullptr;
     a.tables = L.tt ? reinterpret_cast<const uint32_t *>(k + L.tt_tables) : nullptr;
     a.open_own = open_own, a.open_peer = open_peer;
     a.state = state;
@@ -611,7 +621,7 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     const double n = double(L.n), Gq = P.garbled_by(1 - party);
     double bytes = n * 4.0 * P.tri_words();
     const double sb = ot_state_bytes(L);
-    if (L.tt && level == 1) bytes += n * (L.bw / 8.0 + 4.0 * P.rows);
+    if (L.tt && level == 1) bytes += n * ((xhat2 ? 2.0 : 1.0) * L.bw / 8.0 + 4.0 * P.rows);
     else bytes += n * sb;
     if (level > 1) bytes += n * (2.0 * ot_open_bytes(L, level - 1) + (L.ot && party == 0 ? 4.0 : 0.0));
     else if (L.ot) bytes += n * 5.0 * Gq;

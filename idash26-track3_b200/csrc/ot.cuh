@@ -237,12 +237,14 @@ int ot_garble(const GateLayout &L, int party, const void *xhat, const void *key,
 // level levels + 1: close the last level and write the masked comparison bits
 // (bits_hi: [lt | eq] x ceil(N/32) words, bits_lo: lt)
 // Truth-table (TT) kinds run the same levels without a garble step: level 1
-// reads the party's digit tables at the digits of x_hat (xhat, TT only),
+// reads the party's digit tables at the digits of x_hat (xhat, TT only; plus
+// xhat2 when not null: the opened input still held as both parties' shares),
 // the triple words come from the key (tri ignored), and the last level writes
 // bits_lo only for GATE_LRS_TT.
 int ot_level(const GateLayout &L, int party, int level, const void *key, const uint32_t *peer_tables,
              const void *open_own, const void *open_peer, void *state, const uint32_t *tri, void *open_out,
-             uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat = nullptr);
+             uint32_t *bits_hi, uint32_t *bits_lo, cudaStream_t st, const void *xhat = nullptr,
+             const void *xhat2 = nullptr);
 // bytes per element of the openings of AND level `level` (1..levels): the
 // plans compiled into the level kernel (scale 12) store them in the smallest
 // of 1, 2 or 4 bytes that holds every opened bit, other plans in 4 bytes

@@ -221,8 +221,13 @@ __global__ void pk_pack_a(const __grid_constant__ GemmArgs<uint32_t> a, PkGeom g
         const int k = ks * PK_BK + 4 * kq + i;
         uint32_t v = 0;
         if (m < a.M && k < ktot) {
-            v = k < a.K ? __ldg(a.A1 + int64_t(b) * a.sA1 + int64_t(m) * a.lda1 + k)
-                        : __ldg(a.A2 + int64_t(b) * a.sA2 + int64_t(m) * a.lda2 + (k - a.K));
+            if (k < a.K) {
+                const int64_t o = int64_t(b) * a.sA1 + int64_t(m) * a.lda1 + k;
+                v = __ldg(a.A1 + o);
+                if (a.A1b) v += __ldg(a.A1b + o);  // an opened operand held as two shares
+            } else {
+                v = __ldg(a.A2 + int64_t(b) * a.sA2 + int64_t(m) * a.lda2 + (k - a.K));
+            }
         }
         e[i] = v;
     }
@@ -256,11 +261,18 @@ __global__ void pk_pack_b(const __grid_constant__ GemmArgs<uint32_t> a, PkGeom g
         if (n < a.N && k < ktot) {
             if (k < a.K) {
                 const int64_t o = int64_t(k) * a.ldb1 + n;
-                if (a.B1) v = s1 * __ldg(a.B1 + int64_t(bb) * a.sB1 + o);
+                if (a.B1) {
+                    uint32_t b1 = __ldg(a.B1 + int64_t(bb) * a.sB1 + o);
+                    if (a.B1b) b1 += __ldg(a.B1b + int64_t(bb) * a.sB1 + o);
+                    v = s1 * b1;
+                }
                 if (a.B1m) v -= __ldg(a.B1m + int64_t(bb) * a.sB1m + o);
                 v *= sgn;
             } else {
-                v = 0u - sgn * __ldg(a.B2 + int64_t(bb) * a.sB2 + int64_t(k - a.K) * a.ldb2 + n);
+                const int64_t o = int64_t(bb) * a.sB2 + int64_t(k - a.K) * a.ldb2 + n;
+                uint32_t b2 = __ldg(a.B2 + o);
+                if (a.B2b) b2 += __ldg(a.B2b + o);
+                v = 0u - sgn * b2;
             }
         }
         e[i] = v;

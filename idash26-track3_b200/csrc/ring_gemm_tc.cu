@@ -33,6 +33,8 @@
 // Every mbarrier wait is bounded (about two seconds of %globaltimer); a wait
 // that gives up sets the error word and the CTA skips to freeing its tensor
 // memory, so a fault in this logic shows up as a status code, not a hang.
+#include <vector>
+
 #include "common.cuh"
 #include "linear.cuh"
 
@@ -721,17 +723,58 @@ constexpr int tc_max_k()
 // of a mostly empty tensor-core tile (default path)
 constexpr int TC_THIN_TAIL = 32;
 
+// the packed-operand engine takes this GEMM (the default at bw=32)
+template <typename T>
+static bool takes_packed(const GemmArgs<T> &a)
+{
+    const int ktot = a.A2 ? 2 * a.K : a.K;
+    if (sizeof(T) != 4 || g_gemm_path != 0 || a.K == 0 || ktot > tc_max_k<T>()) return false;
+    const int ng = (a.M + TC_BM - 1) / TC_BM, nks = (ktot + TC_BK - 1) / TC_BK;
+    return a.batch <= 65535 && int64_t(ng) * nks <= 65535;
+}
+
+// x + y over `extent` words into a stream-ordered temporary
+template <typename T>
+static int sum_operand(const T *x, const T *y, uint64_t extent, cudaStream_t st, const T **out,
+                       std::vector<void *> &tmp)
+{
+    T *p = nullptr;
+    DDG_CUDA(cudaMallocAsync(&p, (extent ? extent : 1) * sizeof(T), st));
+    tmp.push_back(p);
+    DDG_TRY(ew_add<T>(p, x, y, extent, st));
+    *out = p;
+    return DDG_OK;
+}
+
 template <typename T>
 int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
 {
     if (a.M == 0 || a.N == 0 || a.batch == 0) return DDG_OK;
     const int ktot = a.A2 ? 2 * a.K : a.K;
+    if ((a.A1b || a.B1b || a.B2b) && !takes_packed(a)) {
+        // operands held as two addends: the other engines read one operand, so add them first
+        GemmArgs<T> m = a;
+        m.A1b = m.B1b = m.B2b = nullptr;
+        std::vector<void *> tmp;
+        const uint64_t nb = uint64_t(a.batch - 1);
+        int err = DDG_OK;
+        if (a.A1b)
+            err = sum_operand<T>(a.A1, a.A1b, nb * a.sA1 + uint64_t(a.M - 1) * a.lda1 + a.K, st, &m.A1, tmp);
+        if (err == DDG_OK && a.B1b && a.B1)
+            err = sum_operand<T>(a.B1, a.B1b, nb * a.sB1 + uint64_t(a.K - 1) * a.ldb1 + a.N, st, &m.B1, tmp);
+        if (err == DDG_OK && a.B2b && a.B2) {
+            if (a.B2 == a.B1 && a.B2b == a.B1b && a.sB2 == a.sB1 && a.ldb2 == a.ldb1)
+                m.B2 = m.B1;
+            else
+                err = sum_operand<T>(a.B2, a.B2b, nb * a.sB2 + uint64_t(a.K - 1) * a.ldb2 + a.N, st, &m.B2, tmp);
+        }
+        if (err == DDG_OK) err = ring_gemm<T>(m, st);
+        for (void *p : tmp) cudaFreeAsync(p, st);
+        return err;
+    }
     if (g_gemm_path == 1 || a.K == 0 || ktot > tc_max_k<T>()) return ring_gemm_simt<T>(a, st);
     if constexpr (sizeof(T) == 4) {
-        if (g_gemm_path == 0) {
-            const int ng = (a.M + TC_BM - 1) / TC_BM, nks = (ktot + TC_BK - 1) / TC_BK;
-            if (a.batch <= 65535 && int64_t(ng) * nks <= 65535) return ring_gemm_packed(a, st);
-        }
+        if (takes_packed(a)) return ring_gemm_packed(a, st);
     }
     const int tail = a.M % TC_BM;
     if ((g_gemm_path == 0 || g_gemm_path == 5) && a.M > TC_BM && tail != 0 && tail <= TC_THIN_TAIL) {
