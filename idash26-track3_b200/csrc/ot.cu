@@ -178,6 +178,7 @@ struct OtLevelArgs {
     const uint32_t *tri;         // [tri_words][N]
     void *open_out;              // level <= levels
     uint32_t *bits_hi, *bits_lo; // level == levels + 1: masked comparison bits (split-gate layout)
+    int vec4;                    // compiled-in TT level 1: four elements per thread, 16-byte loads
 };
 
 // One element of party PARTY at AND-tree level l (see ot_level): returns the
@@ -410,11 +411,119 @@ __device__ __forceinline__ void level_elem_c(const OtLevelArgs &a, uint32_t e, u
     }
 }
 
+// word j of a 16-byte vector
+__device__ __forceinline__ uint32_t lane4(const uint4 &v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
+
+// word j of row `row` (run-time, < NR) of the rows loaded for a digit
+template <int NR>
+__device__ __forceinline__ uint32_t row_word(const uint4 (&rv)[NR], uint32_t row, int j)
+{
+    uint32_t w = lane4(rv[0], j);
+    static_for<1, NR>([&](auto ki) {
+        constexpr int k = decltype(ki)::value;
+        if (row == uint32_t(k)) w = lane4(rv[k], j);
+    });
+    return w;
+}
+
+// Truth-table level 1 of a compiled-in plan for four consecutive elements
+// e..e+3 (e % 4 == 0): every key row, the triple words and x_hat (+ its second
+// addend) as 16-byte loads (512 contiguous bytes per row and warp instead of
+// 128), the same digit reads, state and openings as level_elem_c, the
+// openings and state stored as one vector each.  ot_level takes it when N is
+// a multiple of 4 and every array is 16-byte aligned.
+template <int MODE, int NB, int SB, int PARTY>
+__device__ __forceinline__ void level1_tt_x4(const OtLevelArgs &a, uint32_t e, uint32_t N)
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    using OO = open_word_t<open_width(P, 1)>;
+    using SW = open_word_t<state_width(P)>;
+    uint32_t tw[4][3] = {{0u, 0u, 0u}, {0u, 0u, 0u}, {0u, 0u, 0u}, {0u, 0u, 0u}};
+    static_for<0, P.tri_words()>([&](auto wi) {
+        constexpr int w = decltype(wi)::value;
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(a.tri + (uint32_t(w) * N + e)));
+        tw[0][w] = v.x, tw[1][w] = v.y, tw[2][w] = v.z, tw[3][w] = v.w;
+    });
+    uint64_t x[4];
+    if constexpr (NB == 32) {
+        uint4 v = __ldcs(reinterpret_cast<const uint4 *>(static_cast<const uint32_t *>(a.xhat) + e));
+        if (a.xhat2) {
+            const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(static_cast<const uint32_t *>(a.xhat2) + e));
+            v.x += w.x, v.y += w.y, v.z += w.z, v.w += w.w;
+        }
+        x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
+    } else {
+        const ulonglong2 *p = reinterpret_cast<const ulonglong2 *>(static_cast<const unsigned long long *>(a.xhat) + e);
+        ulonglong2 v0 = __ldcs(p), v1 = __ldcs(p + 1);
+        if (a.xhat2) {
+            const ulonglong2 *q =
+                reinterpret_cast<const ulonglong2 *>(static_cast<const unsigned long long *>(a.xhat2) + e);
+            const ulonglong2 w0 = __ldcs(q), w1 = __ldcs(q + 1);
+            v0.x += w0.x, v0.y += w0.y, v1.x += w1.x, v1.y += w1.y;
+        }
+        x[0] = v0.x, x[1] = v0.y, x[2] = v1.x, x[3] = v1.y;
+    }
+    uint32_t st[4] = {0u, 0u, 0u, 0u};
+    static_for<0, P.D>([&](auto gi) {
+        constexpr OtPlan P = digit_plan(NB, SB, MODE);
+        constexpr int g = decltype(gi)::value;
+        constexpr int W = 1 << P.width(g), sh = P.shift(g), r0 = P.drow0(g), nr = P.drows(g);
+        constexpr bool deq = P.deq(g) != 0;
+        uint4 rv[nr];
+        static_for<0, nr>([&](auto ki) {
+            constexpr int k = decltype(ki)::value;
+            rv[k] = __ldcs(reinterpret_cast<const uint4 *>(a.tables + (uint32_t(r0 + k) * N + e)));
+        });
+        static_for<0, 4>([&](auto ji) {
+            constexpr int j = decltype(ji)::value;
+            const uint32_t xd = uint32_t(x[j] >> sh) & uint32_t(W - 1);
+            const uint32_t ie = uint32_t(W) + xd;
+            uint32_t lt, eq = 0;
+            if constexpr (W <= 32) {
+                lt = (lane4(rv[0], j) >> xd) & 1u;
+                if constexpr (deq) eq = (lane4(rv[W == 32 ? 1 : 0], j) >> (ie & 31)) & 1u;
+            } else {
+                lt = (row_word<nr>(rv, xd >> 5, j) >> (xd & 31)) & 1u;
+                if constexpr (deq) eq = (row_word<nr>(rv, ie >> 5, j) >> (ie & 31)) & 1u;
+            }
+            st[j] |= (lt << (2 * g)) | (eq << (2 * g + 1));
+        });
+    });
+    uint32_t o[4];
+    static_for<0, 4>([&](auto ji) {
+        constexpr int j = decltype(ji)::value;
+        o[j] = tt_open<MODE, NB, SB, 1>(st[j], tw[j]);
+    });
+    if constexpr (sizeof(OO) == 1) {
+        *reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(a.open_out) + e) =
+            (o[0] & 0xffu) | ((o[1] & 0xffu) << 8) | ((o[2] & 0xffu) << 16) | ((o[3] & 0xffu) << 24);
+    } else if constexpr (sizeof(OO) == 2) {
+        *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(a.open_out) + e) =
+            make_uint2((o[0] & 0xffffu) | ((o[1] & 0xffffu) << 16), (o[2] & 0xffffu) | ((o[3] & 0xffffu) << 16));
+    } else {
+        *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(a.open_out) + e) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if constexpr (sizeof(SW) == 2) {
+        *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(a.state) + e) =
+            make_uint2((st[0] & 0xffffu) | ((st[1] & 0xffffu) << 16), (st[2] & 0xffffu) | ((st[3] & 0xffffu) << 16));
+    } else {
+        *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(a.state) + e) = make_uint4(st[0], st[1], st[2], st[3]);
+    }
+}
+
 // MODE, NB, SB: the plan compiled in (NB = 0: the plan in the arguments);
 // LV: the level compiled in (0 = a.level)
 template <int MODE, int NB, int SB, int PARTY, int LV>
 __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
 {
+    if constexpr (NB != 0 && LV == 1 && MODE != PLAN_OT) {
+        if (a.vec4) {
+            const uint32_t N = uint32_t(a.N), nq = N / 4, stride = gridDim.x * blockDim.x;
+            for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += stride)
+                level1_tt_x4<MODE, NB, SB, PARTY>(a, 4 * q, N);
+            return;
+        }
+    }
     if constexpr (NB != 0 && LV != 0) {
         // compiled-in plan: 32-bit element offsets (ot_level routes gates whose
         // key rows would reach 2^32 words to the runtime-plan kernel)
@@ -600,8 +709,12 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     a.state = state;
     a.tri = L.tt ? reinterpret_cast<const uint32_t *>(k + L.tt_tri) : tri;
     a.open_out = open_out, a.bits_hi = P.nd[0] ? bits_hi : nullptr, a.bits_lo = bits_lo;
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    a.vec4 = L.tt && level == 1 && plan_compiled_in(L) && L.n % 4 == 0 && al16(a.tables) && al16(a.tri) &&
+             al16(xhat) && al16(a.xhat2) && al16(open_out) && al16(state);
     const int sms = device_sms();
-    const uint64_t blocks = (L.n + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
+    const uint64_t threads = a.vec4 ? L.n / 4 : L.n;
+    const uint64_t blocks = (threads + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
     const int grid = int(blocks < cap ? blocks : cap);
     TimedLaunch tl;
     DDG_TRY(tl.begin(st));
