@@ -511,6 +511,82 @@ __device__ __forceinline__ void level1_tt_x4(const OtLevelArgs &a, uint32_t e, u
     }
 }
 
+// Truth-table levels 2..levels+1 of a compiled-in plan for four consecutive
+// elements e..e+3 (e % 4 == 0, all four below N): the triple words, the state
+// and both parties' openings of level L - 1 as vector loads, the closing and
+// opening of level_elem_c per element, the state and openings stored as one
+// vector each.  At the last level it returns the elements' masked comparison
+// bits as nibbles (bit j = element e + j) for the caller to gather per word.
+template <int MODE, int NB, int SB, int PARTY, int L>
+__device__ __forceinline__ void levelN_tt_x4(const OtLevelArgs &a, uint32_t e, uint32_t N, uint32_t &nh,
+                                             uint32_t &ne, uint32_t &nl)
+{
+    constexpr OtPlan P = digit_plan(NB, SB, MODE);
+    using OI = open_word_t<open_width(P, L - 1)>;
+    using OO = open_word_t<open_width(P, L)>;
+    using SW = open_word_t<state_width(P)>;
+    uint32_t tw[4][3] = {{0u, 0u, 0u}, {0u, 0u, 0u}, {0u, 0u, 0u}, {0u, 0u, 0u}};
+    static_for<0, P.tri_words()>([&](auto wi) {
+        constexpr int w = decltype(wi)::value;
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(a.tri + (uint32_t(w) * N + e)));
+        tw[0][w] = v.x, tw[1][w] = v.y, tw[2][w] = v.z, tw[3][w] = v.w;
+    });
+    // four narrow words as their 4, 8 or 16 bytes
+    auto ld4 = [&](const void *base, auto tag, uint32_t (&out)[4]) {
+        using U = decltype(tag);
+        if constexpr (sizeof(U) == 1) {
+            const uint32_t v = __ldcs(reinterpret_cast<const uint32_t *>(static_cast<const uint8_t *>(base) + e));
+            out[0] = v & 0xffu, out[1] = (v >> 8) & 0xffu, out[2] = (v >> 16) & 0xffu, out[3] = v >> 24;
+        } else if constexpr (sizeof(U) == 2) {
+            const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(base) + e));
+            out[0] = v.x & 0xffffu, out[1] = v.x >> 16, out[2] = v.y & 0xffffu, out[3] = v.y >> 16;
+        } else {
+            const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(static_cast<const uint32_t *>(base) + e));
+            out[0] = v.x, out[1] = v.y, out[2] = v.z, out[3] = v.w;
+        }
+    };
+    auto st4 = [&](void *base, auto tag, const uint32_t (&in)[4]) {
+        using U = decltype(tag);
+        if constexpr (sizeof(U) == 1) {
+            *reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(base) + e) =
+                (in[0] & 0xffu) | ((in[1] & 0xffu) << 8) | ((in[2] & 0xffu) << 16) | ((in[3] & 0xffu) << 24);
+        } else if constexpr (sizeof(U) == 2) {
+            *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(base) + e) =
+                make_uint2((in[0] & 0xffffu) | ((in[1] & 0xffffu) << 16), (in[2] & 0xffffu) | ((in[3] & 0xffffu) << 16));
+        } else {
+            *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(base) + e) = make_uint4(in[0], in[1], in[2], in[3]);
+        }
+    };
+    uint32_t st[4], oo[4], op[4];
+    ld4(a.state, SW{}, st);
+    ld4(a.open_own, OI{}, oo);
+    ld4(a.open_peer, OI{}, op);
+    static_for<0, 4>([&](auto ji) {
+        constexpr int j = decltype(ji)::value;
+        st[j] = tt_close<MODE, NB, SB, PARTY, L>(st[j], tw[j], oo[j] ^ op[j]);
+    });
+    if constexpr (L <= P.levels) {
+        uint32_t o[4];
+        static_for<0, 4>([&](auto ji) {
+            constexpr int j = decltype(ji)::value;
+            o[j] = tt_open<MODE, NB, SB, L>(st[j], tw[j]);
+        });
+        st4(a.open_out, OO{}, o);
+        st4(a.state, SW{}, st);
+        nh = ne = nl = 0u;
+    } else {
+        nh = ne = nl = 0u;
+        static_for<0, 4>([&](auto ji) {
+            constexpr OtPlan P = digit_plan(NB, SB, MODE);
+            constexpr int j = decltype(ji)::value;
+            uint32_t ll = (st[j] >> (2 * P.base[1])) & 1u;
+            if constexpr (MODE == PLAN_TT_FULL) ll ^= (tw[j][P.mu_bit() >> 5] >> (P.mu_bit() & 31)) & 1u;
+            if constexpr (P.nd[0] != 0) nh |= (st[j] & 1u) << j, ne |= ((st[j] >> 1) & 1u) << j;
+            nl |= ll << j;
+        });
+    }
+}
+
 // MODE, NB, SB: the plan compiled in (NB = 0: the plan in the arguments);
 // LV: the level compiled in (0 = a.level)
 template <int MODE, int NB, int SB, int PARTY, int LV>
@@ -521,6 +597,38 @@ __global__ void ot_level_kernel(const __grid_constant__ OtLevelArgs a)
             const uint32_t N = uint32_t(a.N), nq = N / 4, stride = gridDim.x * blockDim.x;
             for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += stride)
                 level1_tt_x4<MODE, NB, SB, PARTY>(a, 4 * q, N);
+            return;
+        }
+    }
+    if constexpr (NB != 0 && LV >= 2 && MODE != PLAN_OT) {
+        if (a.vec4) {
+            constexpr bool last = LV > digit_plan(NB, SB, MODE).levels;
+            const uint32_t N = uint32_t(a.N), nq = N / 4, stride = gridDim.x * blockDim.x;
+            // the last level gathers a word of bits from eight lanes: whole warps step together
+            const uint32_t qend = last ? (nq + 31u) & ~31u : nq;
+            for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < qend; q += stride) {
+                uint32_t nh = 0, ne = 0, nl = 0;
+                if (q < nq) levelN_tt_x4<MODE, NB, SB, PARTY, LV>(a, 4 * q, N, nh, ne, nl);
+                if constexpr (last) {
+                    // word q / 8 holds elements 32 (q / 8) .. +31: lane q % 8 of each group of eight gives 4 bits
+                    const int sh = 4 * int(threadIdx.x & 7);
+                    uint32_t wh = nh << sh, we = ne << sh, wl = nl << sh;
+#pragma unroll
+                    for (int m = 1; m < 8; m <<= 1) {
+                        wh |= __shfl_xor_sync(0xFFFFFFFFu, wh, m);
+                        we |= __shfl_xor_sync(0xFFFFFFFFu, we, m);
+                        wl |= __shfl_xor_sync(0xFFFFFFFFu, wl, m);
+                    }
+                    const uint32_t wi = q >> 3;
+                    if ((threadIdx.x & 7) == 0 && uint64_t(wi) * 32 < N) {
+                        if (a.bits_hi) {
+                            a.bits_hi[wi] = wh;
+                            if constexpr (MODE != PLAN_TT_FULL) a.bits_hi[uint32_t(a.nw) + wi] = we;
+                        }
+                        a.bits_lo[wi] = wl;
+                    }
+                }
+            }
             return;
         }
     }
@@ -710,8 +818,11 @@ int ot_level(const GateLayout &L, int party, int level, const void *key, const u
     a.tri = L.tt ? reinterpret_cast<const uint32_t *>(k + L.tt_tri) : tri;
     a.open_out = open_out, a.bits_hi = P.nd[0] ? bits_hi : nullptr, a.bits_lo = bits_lo;
     auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    a.vec4 = L.tt && level == 1 && plan_compiled_in(L) && L.n % 4 == 0 && al16(a.tables) && al16(a.tri) &&
-             al16(xhat) && al16(a.xhat2) && al16(open_out) && al16(state);
+    // four elements per thread (compiled-in TT plans): level 1 reads the tables and x_hat, later levels
+    // the openings of the level before (4-byte aligned at 1-byte openings), the last level writes bit words
+    a.vec4 = L.tt && plan_compiled_in(L) && L.n % 4 == 0 && al16(a.tri) && al16(state) &&
+             (level == 1 ? al16(a.tables) && al16(xhat) && al16(a.xhat2) && al16(open_out)
+                         : al16(open_own) && al16(open_peer) && (level > P.levels || al16(open_out)));
     const int sms = device_sms();
     const uint64_t threads = a.vec4 ? L.n / 4 : L.n;
     const uint64_t blocks = (threads + 255) / 256, cap = uint64_t(sms > 0 ? sms : 148) * 8;
