@@ -312,6 +312,11 @@ struct EvalExec : ExecBase<T> {
     // GEMM's operand packing and the pool levels add them on load); only where
     // the peer's bytes stay valid to the end of the forward (Channel::peer_stable)
     bool lazy = false;
+    // the packed A operand of the Beaver products A_hat . H: the same A_hat (and
+    // its mask share) in every GCN layer, so its byte planes are packed once
+    uint8_t *ah_pk = nullptr;
+    const T *ah_ms0 = nullptr;
+    uint64_t ah_bytes = 0;
     const T *in[4] = {};
     cudaEvent_t in_ready[4] = {};  // host inputs: copy-stream event to wait on before first use
     T *out = nullptr;
@@ -455,7 +460,13 @@ struct EvalExec : ExecBase<T> {
             g.B2 = H.v, g.B2b = H.v2, g.ldb2 = K, g.sB2 = int64_t(NMAX) * K;
             g.Add = Z, g.ldAdd = K, g.sAdd = int64_t(NMAX) * K;
             g.C = s, g.ldc = K, g.sC = int64_t(NMAX) * K;
-            ok(ring_gemm<T>(g, this->st));
+            const uint64_t ab = ring_gemm_a_pack_bytes<T>(g);
+            if (ab) {
+                const bool same = ah_pk && ah_ms0 == A.ms0 && ah_bytes == ab;
+                if (!same) ah_pk = static_cast<uint8_t *>(this->alloc_bytes(ab)), ah_ms0 = A.ms0, ah_bytes = ab;
+                g.apk_keep = ah_pk, g.apk_ready = same ? 1 : 0;
+            }
+            if (this->err == DDG_OK) ok(ring_gemm<T>(g, this->st));
         }
         Tn<T> t;
         t.n = n;

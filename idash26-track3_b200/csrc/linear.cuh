@@ -22,11 +22,19 @@ struct GemmArgs {
     // optional second addends of A1, B1, B2 (same strides): the operand is
     // A1 + A1b etc., an opened value still held as the two parties' shares
     const T *A1b = nullptr, *B1b = nullptr, *B2b = nullptr;
+    // packed engine only: a caller-owned buffer (ring_gemm_a_pack_bytes) for the
+    // A operand's byte planes, kept after the call; apk_ready: it already holds
+    // this A operand (the packing is skipped).  Other engines ignore both.
+    uint8_t *apk_keep = nullptr;
+    int apk_ready = 0;
 };
 
 // tensor-core limb GEMM where the shape allows (ring_gemm_tc.cu), else the CUDA-core kernel
 template <typename T>
 int ring_gemm(const GemmArgs<T> &a, cudaStream_t st);
+// bytes of the packed A operand when the packed engine takes this GEMM, else 0
+template <typename T>
+uint64_t ring_gemm_a_pack_bytes(const GemmArgs<T> &a);
 // the CUDA-core kernel (ring_gemm.cu)
 template <typename T>
 int ring_gemm_simt(const GemmArgs<T> &a, cudaStream_t st);

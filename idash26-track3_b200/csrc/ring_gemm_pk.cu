@@ -572,15 +572,17 @@ int ring_gemm_packed(const GemmArgs<uint32_t> &a, cudaStream_t st)
     DDG_TRY(ring_gemm_err_word(&err));
     const uint64_t abytes = uint64_t(a.batch) * g.ng * g.nks * g.sa;
     const uint64_t bbytes = uint64_t(g.batches_b) * g.nnt * g.nks * g.sb;
-    void *apk = nullptr, *bpk = nullptr;
-    DDG_CUDA(cudaMallocAsync(&apk, abytes, st));
+    // the A planes go to the caller's buffer when given (kept for later GEMMs of the same A)
+    void *apk = a.apk_keep, *bpk = nullptr;
+    const bool own_a = apk == nullptr;
+    if (own_a) DDG_CUDA(cudaMallocAsync(&apk, abytes, st));
     if (cudaMallocAsync(&bpk, bbytes, st) != cudaSuccess) {
-        cudaFreeAsync(apk, st);
+        if (own_a) cudaFreeAsync(apk, st);
         set_last_error("cudaMallocAsync(%llu) for the packed B operand failed", (unsigned long long)bbytes);
         return DDG_ERR_CUDA;
     }
     int rc = DDG_OK;
-    {
+    if (own_a || !a.apk_ready) {
         const int rows = PK_BM + (g.thin ? PK_THIN : 0);
         dim3 grid((rows + 31) / 32, g.ng * g.nks, a.batch);
         pk_pack_a<<<grid, 256, 0, st>>>(a, g, static_cast<uint8_t *>(apk));
@@ -604,9 +606,15 @@ int ring_gemm_packed(const GemmArgs<uint32_t> &a, cudaStream_t st)
         rc = g.bn == 32 ? pk_launch<32>(pa, a.batch, err, st) : pk_launch<64>(pa, a.batch, err, st);
     }
     if (rc != DDG_OK) set_last_error("packed ring GEMM launch failed");
-    cudaFreeAsync(apk, st);
+    if (own_a) cudaFreeAsync(apk, st);
     cudaFreeAsync(bpk, st);
     return rc;
+}
+
+uint64_t ring_gemm_packed_a_bytes(const GemmArgs<uint32_t> &a)
+{
+    const PkGeom g = pk_geometry(a);
+    return uint64_t(a.batch) * g.ng * g.nks * g.sa;
 }
 
 }  // namespace ddg

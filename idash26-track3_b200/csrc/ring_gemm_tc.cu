@@ -687,6 +687,7 @@ int ring_gemm_err_word(uint32_t **out)
 }
 
 int ring_gemm_packed(const GemmArgs<uint32_t> &a, cudaStream_t st);  // ring_gemm_pk.cu
+uint64_t ring_gemm_packed_a_bytes(const GemmArgs<uint32_t> &a);      // ring_gemm_pk.cu
 
 int ring_gemm_tc_error(bool clear)
 {
@@ -802,5 +803,16 @@ int ring_gemm(const GemmArgs<T> &a, cudaStream_t st)
 
 template int ring_gemm<uint32_t>(const GemmArgs<uint32_t> &, cudaStream_t);
 template int ring_gemm<uint64_t>(const GemmArgs<uint64_t> &, cudaStream_t);
+
+template <typename T>
+uint64_t ring_gemm_a_pack_bytes(const GemmArgs<T> &a)
+{
+    if constexpr (sizeof(T) == 4) {
+        if (a.M > 0 && a.N > 0 && a.batch > 0 && takes_packed(a)) return ring_gemm_packed_a_bytes(a);
+    }
+    return 0;
+}
+template uint64_t ring_gemm_a_pack_bytes<uint32_t>(const GemmArgs<uint32_t> &);
+template uint64_t ring_gemm_a_pack_bytes<uint64_t>(const GemmArgs<uint64_t> &);
 
 }  // namespace ddg
