@@ -89,23 +89,25 @@ __device__ __forceinline__ uint64_t bc_index(uint64_t e, int bc, int R, int C)
 
 template <typename T>
 __global__ void k_beaver(T p0, uint64_t n, int bc, int R, int C, const T *xh, const T *yh, const T *msx, const T *msy,
-                         const T *Z, T *out)
+                         const T *Z, T *out, const T *xh2, const T *yh2)
 {
     GRID_STRIDE(e, n)
     {
         const uint64_t j = bc_index(e, bc, R, C);
-        const T x = xh[e], y = yh[j];
+        T x = xh[e], y = yh[j];
+        if (xh2) x += xh2[e];
+        if (yh2) y += yh2[j];
         out[e] = p0 * x * y - x * msy[j] - msx[e] * y + Z[e];
     }
 }
 
 template <typename T>
 int beaver_ew(int party, const EwShape &sh, Bcast bc, const T *xh, const T *yh, const T *msx, const T *msy, const T *Z,
-              T *out, cudaStream_t st)
+              T *out, cudaStream_t st, const T *xh2, const T *yh2)
 {
     if (!sh.n) return DDG_OK;
     k_beaver<T><<<ew_grid(sh.n), 256, 0, st>>>(party == 0 ? T(1) : T(0), sh.n, int(bc), sh.R, sh.C, xh, yh, msx, msy,
-                                               Z, out);
+                                               Z, out, xh2, yh2);
     note_launch();
     DDG_CUDA(cudaGetLastError());
     return DDG_OK;
@@ -422,7 +424,7 @@ int split_shares(const T *v, uint64_t n, const AesKey &dk, uint32_t op, uint32_t
     template int ew_add<T>(T *, const T *, const T *, uint64_t, cudaStream_t);                                   \
     template int ew_sub<T>(T *, const T *, const T *, uint64_t, cudaStream_t);                                   \
     template int beaver_ew<T>(int, const EwShape &, Bcast, const T *, const T *, const T *, const T *, const T *, \
-                              T *, cudaStream_t);                                                                \
+                              T *, cudaStream_t, const T *, const T *);                                                                \
     template int beaver_ew_z<T>(const EwShape &, Bcast, const T *, const T *, const T *, T *, cudaStream_t);     \
     template int rowsum_plus<T>(const T *, const T *, T *, uint64_t, int, cudaStream_t);                         \
     template int pool_split<T>(const T *, T *, T *, int, int, int, cudaStream_t, const T *);                     \

@@ -309,8 +309,9 @@ struct EvalExec : ExecBase<T> {
     int p = 0;
     // openings stay as (own share, peer share) until a consumer needs one value
     // (the level-1 and round-2 kernels of the truth-table gates, the packed
-    // GEMM's operand packing and the pool levels add them on load); only where
-    // the peer's bytes stay valid to the end of the forward (Channel::peer_stable)
+    // GEMM's operand packing, the elementwise Beaver product and the pool
+    // levels add them on load); only where the peer's bytes stay valid to the
+    // end of the forward (Channel::peer_stable)
     bool lazy = false;
     // the packed A operand of the Beaver products A_hat . H: the same A_hat (and
     // its mask share) in every GCN layer, so its byte planes are packed once
@@ -436,8 +437,7 @@ struct EvalExec : ExecBase<T> {
         ensure_ms(a), ensure_ms(b);
         const T *Z = reinterpret_cast<const T *>(key_at(words(sh.n)));
         T *s = alloc(sh.n);
-        const T *av = val(a), *bv = val(b);
-        if (this->err == DDG_OK) ok(beaver_ew<T>(p, sh, bc, av, bv, a.ms0, b.ms0, Z, s, this->st));
+        if (this->err == DDG_OK) ok(beaver_ew<T>(p, sh, bc, a.v, b.v, a.ms0, b.ms0, Z, s, this->st, a.v2, b.v2));
         Tn<T> t;
         t.n = sh.n;
         open_to(t, s);

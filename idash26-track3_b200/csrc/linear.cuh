@@ -66,10 +66,11 @@ int ew_add(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st);
 template <typename T>
 int ew_sub(T *out, const T *a, const T *b, uint64_t n, cudaStream_t st);
 
-// party share of x*y: p0*xh*yh - xh*[r_y] - [r_x]*yh + Z
+// party share of x*y: p0*xh*yh - xh*[r_y] - [r_x]*yh + Z (xh2, yh2: second
+// addends of the opened inputs, or null)
 template <typename T>
 int beaver_ew(int party, const EwShape &sh, Bcast bc, const T *xh, const T *yh, const T *msx, const T *msy, const T *Z,
-              T *out, cudaStream_t st);
+              T *out, cudaStream_t st, const T *xh2 = nullptr, const T *yh2 = nullptr);
 // dealer: Z = r_x * r_y + r_out
 template <typename T>
 int beaver_ew_z(const EwShape &sh, Bcast bc, const T *rx, const T *ry, const T *rout, T *Z, cudaStream_t st);
