@@ -279,11 +279,18 @@ __global__ void pk_pack_b(const __grid_constant__ GemmArgs<uint32_t> a, PkGeom g
     }
     uint32_t p[4];
     planes4(e, p);
-    uint8_t *blk = bpk + ((uint64_t(bb) * g.nnt + nt) * g.nks + ks) * g.sb;
+    // the block's four planes are one contiguous chunk of sb = 4 * bn * 32 bytes:
+    // assemble it in shared memory, then store it as one 16-byte word per thread
+    // (a thread's own 4-byte plane words land 16 bytes apart, 32 bytes per
+    // 128-byte line and store)
+    __shared__ __align__(16) uint8_t img[4 * 64 * PK_BK];
     const uint32_t plane = uint32_t(g.bn) * PK_BK;
     const uint32_t off = kmajor_off(nl, 4 * kq);
 #pragma unroll
-    for (int q = 0; q < 4; q++) *reinterpret_cast<uint32_t *>(blk + q * plane + off) = p[q];
+    for (int q = 0; q < 4; q++) *reinterpret_cast<uint32_t *>(img + q * plane + off) = p[q];
+    __syncthreads();
+    uint8_t *blk = bpk + ((uint64_t(bb) * g.nnt + nt) * g.nks + ks) * g.sb;
+    reinterpret_cast<uint4 *>(blk)[threadIdx.x] = reinterpret_cast<const uint4 *>(img)[threadIdx.x];
 }
 
 // ---------------------------------------------------------------- the GEMM
