@@ -120,6 +120,10 @@ SIGNATURES = {
     "ddg_forward_graph_create_ex": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32,
                                            ctypes.POINTER(_vp)]),
     "ddg_forward_graph_launch": (_i32, [_vp, _vp, _vp]),
+    "ddg_forward_pipeline_create": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp)]),
+    "ddg_forward_pipeline_submit": (_i32, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _vp]),
+    "ddg_forward_pipeline_wait": (_i32, [_vp]),
+    "ddg_forward_pipeline_destroy": (_i32, [_vp]),
     "ddg_forward_graph_destroy": (_i32, [_vp]),
     "ddg_dealer_forward": (_i32, [_i32, _i32, _i32, _u64, _vp, _u64, _i32, _vp, _vp, _vp]),
     "ddg_party_connect_callback": (_i32, [_vp, ctypes.POINTER(Comm)]),
@@ -442,6 +446,41 @@ class ForwardGraph:
     def close(self):
         if self.h:
             check(lib().ddg_forward_graph_destroy(self.h))
+            self.h = None
+
+
+class ForwardPipeline:
+    """Pipelined forwards of an in-process pair on pinned host input shares
+    (ddg_forward_pipeline_*; see ddg_fss.h): submit() queues one step (its
+    input copies overlap the previous step's forward) and returns the (raw,
+    affinity) arrays that the step fills once delivered, by a later submit()
+    or by wait().  Run one ordinary forward_pair first, with DCF timing off."""
+
+    def __init__(self, p0: Party, p1: Party, batch: int):
+        self.batch = batch
+        h = _vp()
+        check(lib().ddg_forward_pipeline_create(p0.h, p1.h, batch, ctypes.byref(h)))
+        self.h = h
+        self._keep = [None, None]  # the arrays of the steps in flight, per staging set
+        self._k = 0
+
+    def submit(self, inputs0, inputs1):
+        import numpy as np
+
+        raw = np.zeros(self.batch, dtype=np.int64)
+        aff = np.zeros(self.batch, dtype=np.float64)
+        a0, a1 = (_vp * 4)(*inputs0), (_vp * 4)(*inputs1)
+        check(lib().ddg_forward_pipeline_submit(self.h, a0, a1, raw.ctypes.data, aff.ctypes.data))
+        self._keep[self._k & 1] = (raw, aff)
+        self._k += 1
+        return raw, aff
+
+    def wait(self):
+        check(lib().ddg_forward_pipeline_wait(self.h))
+
+    def close(self):
+        if self.h:
+            check(lib().ddg_forward_pipeline_destroy(self.h))
             self.h = None
 
 

@@ -743,6 +743,151 @@ int ddg_forward_graph_destroy(ddg_forward_graph *g)
     return DDG_OK;
 }
 
+// ---- pipelined forwards of an in-process pair on host inputs: two graphs of
+// the forward, each reading its own device staging set; step k's host->device
+// copies run on a copy stream while step k-1's graph runs
+
+struct ddg_forward_pipeline {
+    ddg_party *p0 = nullptr, *p1 = nullptr;
+    int batch = 0;
+    ddg_forward_graph *g[2] = {nullptr, nullptr};
+    void *stage[2][2][4] = {};  // [set][party][input: x, adj, mask, protein]
+    uint64_t bytes[4] = {};
+    cudaStream_t copy = nullptr;
+    cudaEvent_t staged[2] = {}, freed[2] = {}, done[2] = {};
+    void *h_out[2] = {};        // pinned read-back of each set's revealed output
+    bool pending[2] = {false, false};
+    int64_t *user_raw[2] = {};
+    double *user_aff[2] = {};
+    uint64_t k = 0;             // steps submitted
+};
+
+static void pipeline_free(ddg_forward_pipeline *pp)
+{
+    cudaSetDevice(pp->p0->P.device);
+    cudaStreamSynchronize(pp->p0->P.stream);
+    if (pp->copy) cudaStreamSynchronize(pp->copy);
+    for (int s = 0; s < 2; s++) {
+        if (pp->g[s]) ddg_forward_graph_destroy(pp->g[s]);
+        for (int q = 0; q < 2; q++)
+            for (int i = 0; i < 4; i++)
+                if (pp->stage[s][q][i]) cudaFree(pp->stage[s][q][i]);
+        for (cudaEvent_t e : {pp->staged[s], pp->freed[s], pp->done[s]})
+            if (e) cudaEventDestroy(e);
+        if (pp->h_out[s]) cudaFreeHost(pp->h_out[s]);
+    }
+    if (pp->copy) cudaStreamDestroy(pp->copy);
+    delete pp;
+}
+
+int ddg_forward_pipeline_create(ddg_party *p0, ddg_party *p1, int batch, ddg_forward_pipeline **out)
+{
+    DDG_CHECK(p0 && p1 && out && batch > 0, DDG_ERR_ARG, "bad argument");
+    *out = nullptr;
+    DDG_CHECK(!p0->P.timing.enabled && !p1->P.timing.enabled, DDG_ERR_STATE,
+              "a forward pipeline needs DCF timing off on both parties (each of its graphs would own the events)");
+    DDG_CUDA(cudaSetDevice(p0->P.device));
+    auto *pp = new ddg_forward_pipeline;
+    pp->p0 = p0, pp->p1 = p1, pp->batch = batch;
+    const uint64_t es = p0->P.bw / 8, B = uint64_t(batch);
+    const uint64_t n[4] = {B * NMAX * FEAT, B * NMAX * NMAX, B * NMAX * POOL, B * PROT};
+    for (int i = 0; i < 4; i++) pp->bytes[i] = n[i] * es;
+    int st = DDG_OK;
+    auto cu = [&](cudaError_t e, const char *what) {
+        if (e != cudaSuccess && st == DDG_OK) {
+            set_last_error("forward pipeline: %s: %s", what, cudaGetErrorString(e));
+            st = DDG_ERR_CUDA;
+        }
+    };
+    for (int s = 0; s < 2 && st == DDG_OK; s++)
+        for (int q = 0; q < 2; q++)
+            for (int i = 0; i < 4; i++) cu(cudaMalloc(&pp->stage[s][q][i], pp->bytes[i]), "staging allocation");
+    cu(cudaStreamCreateWithFlags(&pp->copy, cudaStreamNonBlocking), "copy stream");
+    for (int s = 0; s < 2 && st == DDG_OK; s++) {
+        cu(cudaEventCreateWithFlags(&pp->staged[s], cudaEventDisableTiming), "event");
+        cu(cudaEventCreateWithFlags(&pp->freed[s], cudaEventDisableTiming), "event");
+        cu(cudaEventCreateWithFlags(&pp->done[s], cudaEventDisableTiming), "event");
+        cu(cudaHostAlloc(&pp->h_out[s], B * 8, cudaHostAllocDefault), "pinned read-back");
+        if (st == DDG_OK) cu(cudaEventRecord(pp->freed[s], p0->P.stream), "event record");
+    }
+    for (int s = 0; s < 2 && st == DDG_OK; s++) {
+        const void *in0[4] = {pp->stage[s][0][0], pp->stage[s][0][1], pp->stage[s][0][2], pp->stage[s][0][3]};
+        const void *in1[4] = {pp->stage[s][1][0], pp->stage[s][1][1], pp->stage[s][1][2], pp->stage[s][1][3]};
+        st = ddg_forward_graph_create_ex(p0, p1, batch, in0, in1, 0, &pp->g[s]);
+    }
+    if (st != DDG_OK) {
+        const std::string err = ddg::last_error();
+        pipeline_free(pp);
+        set_last_error("%s", err.c_str());
+        return st;
+    }
+    *out = pp;
+    return DDG_OK;
+}
+
+// step k-2's outputs (staging set s): wait for its read-back and hand it over
+static int pipeline_deliver(ddg_forward_pipeline *pp, int s)
+{
+    if (!pp->pending[s]) return DDG_OK;
+    pp->pending[s] = false;
+    const cudaError_t ce = cudaEventSynchronize(pp->done[s]);
+    DDG_CHECK(ce == cudaSuccess, DDG_ERR_CUDA, "forward pipeline: %s", cudaGetErrorString(ce));
+    const Party &P = pp->p0->P;
+    for (int i = 0; i < pp->batch; i++) {
+        const int64_t v = P.bw == 32 ? int64_t(static_cast<const int32_t *>(pp->h_out[s])[i])
+                                     : static_cast<const int64_t *>(pp->h_out[s])[i];
+        if (pp->user_raw[s]) pp->user_raw[s][i] = v;
+        // AFFINITY = int32(value) / 2^s (deepdtagen_inference.cu:594-606)
+        if (pp->user_aff[s]) pp->user_aff[s][i] = double(int32_t(uint32_t(uint64_t(v)))) / double(1ull << P.s);
+    }
+    return DDG_OK;
+}
+
+int ddg_forward_pipeline_submit(ddg_forward_pipeline *pp, const void *const *in0, const void *const *in1,
+                                int64_t *h_out_raw, double *h_affinity)
+{
+    DDG_CHECK(pp && in0 && in1, DDG_ERR_ARG, "bad argument");
+    const int s = int(pp->k & 1);
+    Party &P = pp->p0->P;
+    DDG_CUDA(cudaSetDevice(P.device));
+    // keeps two steps in flight: the step that last used this staging set has read back
+    DDG_TRY(pipeline_deliver(pp, s));
+    // the copies into set s start once the graph that last read it is done
+    DDG_CUDA(cudaStreamWaitEvent(pp->copy, pp->freed[s], 0));
+    const void *const *in[2] = {in0, in1};
+    for (int q = 0; q < 2; q++)
+        for (int i = 0; i < 4; i++)
+            DDG_CUDA(cudaMemcpyAsync(pp->stage[s][q][i], in[q][i], pp->bytes[i], cudaMemcpyHostToDevice, pp->copy));
+    DDG_CUDA(cudaEventRecord(pp->staged[s], pp->copy));
+    DDG_CUDA(cudaStreamWaitEvent(P.stream, pp->staged[s], 0));
+    DDG_CUDA(cudaGraphLaunch(pp->g[s]->exec, P.stream));
+    add_launches(pp->g[s]->launches);
+    DDG_CUDA(cudaEventRecord(pp->freed[s], P.stream));
+    DDG_CUDA(cudaMemcpyAsync(pp->h_out[s], pp->g[s]->d_out, size_t(pp->batch) * (P.bw / 8), cudaMemcpyDeviceToHost,
+                             P.stream));
+    DDG_CUDA(cudaEventRecord(pp->done[s], P.stream));
+    pp->pending[s] = true, pp->user_raw[s] = h_out_raw, pp->user_aff[s] = h_affinity;
+    pp->k++;
+    return DDG_OK;
+}
+
+int ddg_forward_pipeline_wait(ddg_forward_pipeline *pp)
+{
+    DDG_CHECK(pp, DDG_ERR_ARG, "null pipeline");
+    DDG_CUDA(cudaSetDevice(pp->p0->P.device));
+    const int older = int(pp->k & 1);  // the slot of step k-2 (if pending) comes before step k-1's
+    DDG_TRY(pipeline_deliver(pp, older));
+    DDG_TRY(pipeline_deliver(pp, 1 - older));
+    return ring_gemm_tc_check(pp->p0->P.stream);
+}
+
+int ddg_forward_pipeline_destroy(ddg_forward_pipeline *pp)
+{
+    if (!pp) return DDG_OK;
+    pipeline_free(pp);
+    return DDG_OK;
+}
+
 int ddg_party_enable_dcf_timing(ddg_party *h, int on)
 {
     DDG_CHECK(h, DDG_ERR_ARG, "null party");

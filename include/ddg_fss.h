@@ -304,6 +304,26 @@ int ddg_party_graph_create(ddg_party *party, int batch, const void *const *in, i
                            ddg_forward_graph **out);
 int ddg_forward_graph_launch(ddg_forward_graph *graph, int64_t *h_out_raw, double *h_affinity);
 int ddg_forward_graph_destroy(ddg_forward_graph *graph);
+/* Pipelined forwards of an in-process pair on host-resident input shares (the
+ * overlap of the reference's streaming loop, deepdtagen_inference.cu:608-826,
+ * applied to the inputs): two CUDA graphs of the pair's forward, each reading
+ * its own device staging set; ddg_forward_pipeline_submit copies one step's
+ * input shares (in0 / in1: {x, adj, mask, protein}, pinned host buffers that
+ * stay untouched until the step's outputs are delivered) into the next
+ * staging set on a copy stream, which overlaps the previous step's forward,
+ * then replays that set's graph and reads its revealed output back, all
+ * without waiting.  Outputs reach h_out_raw / h_affinity (either may be NULL;
+ * kept until then) when a later submit reuses the set (two steps in flight)
+ * or at ddg_forward_pipeline_wait, which delivers every submitted step.
+ * Create after one ordinary ddg_forward_eval_pair of the pair, with DCF timing
+ * off on both parties; destroy before the parties.  The keys are re-read by
+ * every step, as for ddg_forward_graph_create. */
+typedef struct ddg_forward_pipeline ddg_forward_pipeline;
+int ddg_forward_pipeline_create(ddg_party *p0, ddg_party *p1, int batch, ddg_forward_pipeline **out);
+int ddg_forward_pipeline_submit(ddg_forward_pipeline *pipeline, const void *const *in0, const void *const *in1,
+                                int64_t *h_out_raw, double *h_affinity);
+int ddg_forward_pipeline_wait(ddg_forward_pipeline *pipeline);
+int ddg_forward_pipeline_destroy(ddg_forward_pipeline *pipeline);
 /* GPU dealer (replaces DDGOrcaKeygenBatched + ddgSecureAdjNormKeygen,
  * deepdtagen_inference.cu:283-342): both parties' keys of one forward, fresh
  * masks from `seed`, into d_key0 / d_key1 (ddg_forward_key_bytes each) */

@@ -341,3 +341,36 @@ def test_forward_graph_with_pinned_host_inputs(ddg, synth, cuda):
                 assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)) and np.array_equal(aff, want_aff)
     finally:
         g.close()
+
+
+@pytest.mark.gpu
+def test_forward_pipeline_on_pinned_host_inputs(ddg, synth, cuda):
+    """Pipelined forwards (ddg_forward_pipeline_*): steps alternate between two
+    pinned input sets, each step's copies overlap the previous step's forward,
+    and every step reveals the oracle's outputs of its own inputs, delivered
+    by a later submit (two steps in flight) or by wait()."""
+    import torch
+
+    bw, B = 32, 3
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=93)
+    inps = [synth.Inputs(B, bw, seed=sd, with_protein_cnn=False) for sd in (61, 62)]
+    bufs = [[[torch.from_numpy(np.ascontiguousarray(a[p]).view(np.uint8).copy()).pin_memory()
+              for a in (inp.x_sh, inp.adj_sh, inp.mask_sh, inp.protein_sh)] for p in (0, 1)] for inp in inps]
+    ptrs = [[[t.data_ptr() for t in b[p]] for p in (0, 1)] for b in bufs]
+    ddg.forward_pair(p0, p1, B, ptrs[0][0], ptrs[0][1], on_host=True)  # one-time set-up
+    want = [expected(inp, q, bw) for inp in inps]
+    pipe = ddg.ForwardPipeline(p0, p1, B)
+    try:
+        outs = []
+        for k in range(5):
+            outs.append((k % 2, pipe.submit(ptrs[k % 2][0], ptrs[k % 2][1])))
+        pipe.wait()
+        for which, (raw, aff) in outs:
+            want_raw, want_aff = want[which]
+            assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)) and np.array_equal(aff, want_aff)
+        # a second round after wait() starts from an idle pipeline
+        raw, aff = pipe.submit(ptrs[1][0], ptrs[1][1])
+        pipe.wait()
+        assert np.array_equal(raw, RF.Ring(bw).signed(want[1][0])) and np.array_equal(aff, want[1][1])
+    finally:
+        pipe.close()
