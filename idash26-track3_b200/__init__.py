@@ -120,6 +120,8 @@ SIGNATURES = {
     "ddg_forward_graph_create_ex": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32,
                                            ctypes.POINTER(_vp)]),
     "ddg_forward_graph_launch": (_i32, [_vp, _vp, _vp]),
+    "ddg_forward_graph_enqueue": (_i32, [_vp]),
+    "ddg_forward_graph_sync": (_i32, [_vp, _vp, _vp]),
     "ddg_forward_pipeline_create": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_vp)]),
     "ddg_forward_pipeline_submit": (_i32, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _vp]),
     "ddg_forward_pipeline_wait": (_i32, [_vp]),
@@ -441,6 +443,22 @@ class ForwardGraph:
         raw = np.zeros(self.batch, dtype=np.int64)
         aff = np.zeros(self.batch, dtype=np.float64)
         check(lib().ddg_forward_graph_launch(self.h, raw.ctypes.data, aff.ctypes.data))
+        return raw, aff
+
+    def enqueue(self):
+        """Queue one replay without waiting (ddg_forward_graph_enqueue)."""
+        check(lib().ddg_forward_graph_enqueue(self.h))
+
+    def sync(self, outputs=True):
+        """Wait for the replays queued; (raw, affinity) of the last one, or None."""
+        import numpy as np
+
+        if not outputs:
+            check(lib().ddg_forward_graph_sync(self.h, None, None))
+            return None
+        raw = np.zeros(self.batch, dtype=np.int64)
+        aff = np.zeros(self.batch, dtype=np.float64)
+        check(lib().ddg_forward_graph_sync(self.h, raw.ctypes.data, aff.ctypes.data))
         return raw, aff
 
     def close(self):

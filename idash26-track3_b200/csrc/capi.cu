@@ -724,6 +724,56 @@ int ddg_forward_graph_launch(ddg_forward_graph *g, int64_t *h_out_raw, double *h
     return DDG_OK;
 }
 
+int ddg_forward_graph_enqueue(ddg_forward_graph *g)
+{
+    DDG_CHECK(g && g->exec, DDG_ERR_ARG, "null forward graph");
+    Party &P = g->p0->P;
+    DDG_CUDA(cudaSetDevice(P.device));
+    ddg_party *ps[2] = {g->p0, g->p1};
+    const int np = g->p1 ? 2 : 1;
+    for (int i = 0; i < np; i++) {
+        Party &Q = ps[i]->P;
+        if (!Q.timing.enabled || Q.graph_recs != &g->recs[i] || Q.ref_live) continue;
+        if (!Q.ref_event) DDG_CUDA(cudaEventCreate(&Q.ref_event));
+        DDG_CUDA(cudaEventRecord(Q.ref_event, P.stream));
+        Q.ref_live = true;
+    }
+    DDG_CUDA(cudaGraphLaunch(g->exec, P.stream));
+    add_launches(g->launches);
+    if (!g->p1) P.chan->note_replay(P.party, g->exchanges);
+    // the timing read-out (after a sync) covers the last replay enqueued
+    for (int i = 0; i < np; i++)
+        if (ps[i]->P.graph_recs == &g->recs[i]) ps[i]->P.graph_fresh = true;
+    return DDG_OK;
+}
+
+int ddg_forward_graph_sync(ddg_forward_graph *g, int64_t *h_out_raw, double *h_affinity)
+{
+    DDG_CHECK(g && g->exec, DDG_ERR_ARG, "null forward graph");
+    Party &P = g->p0->P;
+    DDG_CUDA(cudaSetDevice(P.device));
+    const int B = g->batch;
+    std::vector<int64_t> v(B);
+    std::vector<int32_t> h32(B);
+    const bool want = h_out_raw || h_affinity;
+    if (want)
+        DDG_CUDA(cudaMemcpyAsync(P.bw == 32 ? static_cast<void *>(h32.data()) : static_cast<void *>(v.data()),
+                                 g->d_out, size_t(B) * (P.bw / 8), cudaMemcpyDeviceToHost, P.stream));
+    const cudaError_t ce = cudaStreamSynchronize(P.stream);
+    DDG_CHECK(ce == cudaSuccess, DDG_ERR_CUDA, "forward graph: %s", cudaGetErrorString(ce));
+    DDG_TRY(ring_gemm_tc_check(P.stream));
+    if (!g->p1) DDG_TRY(P.chan->status(P.party));
+    if (!want) return DDG_OK;
+    if (P.bw == 32)
+        for (int i = 0; i < B; i++) v[i] = h32[i];
+    for (int i = 0; i < B; i++) {
+        if (h_out_raw) h_out_raw[i] = v[i];
+        // AFFINITY = int32(value) / 2^s (deepdtagen_inference.cu:594-606)
+        if (h_affinity) h_affinity[i] = double(int32_t(uint32_t(uint64_t(v[i])))) / double(1ull << P.s);
+    }
+    return DDG_OK;
+}
+
 int ddg_forward_graph_destroy(ddg_forward_graph *g)
 {
     if (!g) return DDG_OK;

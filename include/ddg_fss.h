@@ -303,6 +303,13 @@ int ddg_forward_graph_create_ex(ddg_party *p0, ddg_party *p1, int batch, const v
 int ddg_party_graph_create(ddg_party *party, int batch, const void *const *in, int on_host,
                            ddg_forward_graph **out);
 int ddg_forward_graph_launch(ddg_forward_graph *graph, int64_t *h_out_raw, double *h_affinity);
+/* ddg_forward_graph_enqueue: one replay queued on the (first) party's stream
+ * without waiting or reading back, so that replays follow each other with no
+ * host round trip; ddg_forward_graph_sync waits for every replay enqueued and
+ * returns the last one's output like ddg_forward_graph_launch (either output
+ * may be NULL).  DCF timing read-outs come after a sync. */
+int ddg_forward_graph_enqueue(ddg_forward_graph *graph);
+int ddg_forward_graph_sync(ddg_forward_graph *graph, int64_t *h_out_raw, double *h_affinity);
 int ddg_forward_graph_destroy(ddg_forward_graph *graph);
 /* Pipelined forwards of an in-process pair on host-resident input shares (the
  * overlap of the reference's streaming loop, deepdtagen_inference.cu:608-826,

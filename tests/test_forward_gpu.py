@@ -374,3 +374,26 @@ def test_forward_pipeline_on_pinned_host_inputs(ddg, synth, cuda):
         assert np.array_equal(raw, RF.Ring(bw).signed(want[1][0])) and np.array_equal(aff, want[1][1])
     finally:
         pipe.close()
+
+
+@pytest.mark.gpu
+def test_forward_graph_enqueue_then_sync(ddg, synth, cuda):
+    """Replays queued back to back (ddg_forward_graph_enqueue) and one sync:
+    the last replay's output is the oracle's, and a launch after the sync
+    still is."""
+    bw, B = 32, 3
+    inp = synth.Inputs(B, bw, seed=47, with_protein_cnn=False)
+    q, p0, p1, keep_k = setup_pair(ddg, synth, bw, B, seed=79)
+    ins, keep = dev_inputs(inp)
+    want_raw, want_aff = expected(inp, q, bw)
+    ddg.forward_pair(p0, p1, B, ins[0], ins[1])  # one-time set-up outside the capture
+    g = ddg.ForwardGraph(p0, p1, B, ins[0], ins[1])
+    try:
+        for _ in range(4):
+            g.enqueue()
+        raw, aff = g.sync()
+        assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)) and np.array_equal(aff, want_aff)
+        raw, aff = g.launch()
+        assert np.array_equal(raw, RF.Ring(bw).signed(want_raw)) and np.array_equal(aff, want_aff)
+    finally:
+        g.close()
