@@ -852,6 +852,10 @@ def main():
                "h2d_bytes_per_step": h2d * pairs, "d2h_bytes_per_step": B * (bw // 8) * pairs,
                "ms_per_step": ms_e2e / a.steps, "h2d_probe_gbs": h2d_probe(torch, bufs, device),
                "launch": e2e_how}
+        if pipe is not None:
+            e2e["note"] = ("the timed forwards of `value` carry the comparison-kernel event records of the live "
+                           "roofline (about 140 per forward); the pipeline's graphs carry none, and its input copies "
+                           "run beside the forwards, so e2e can read slightly above value")
 
     value = pairs * B * a.steps / (ms / 1e3)
     peak, peak_kind = measured_peaks()
