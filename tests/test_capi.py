@@ -1,5 +1,6 @@
 """The C-ABI library loads and exports every function include/ddg_fss.h declares (no GPU needed)."""
 import os
+import ctypes
 import re
 
 import pytest
@@ -139,3 +140,19 @@ def test_layer_entry_points_reject_bad_arguments_without_a_gpu(ddg):
                L.ddg_op_fc_keygen(None, c, 3, 1, 1, mw, mw), L.ddg_party_connect_callback(None, None)):
         assert st == 1
     assert L.ddg_dealer_destroy(None) == 0
+
+
+def test_graph_and_pipeline_entry_points_reject_bad_arguments_without_a_gpu(ddg):
+    """Forward graphs, queued replays and the forward pipeline check their
+    handles before any device work: null handles are DDG_ERR_ARG, destroying
+    a null handle is a no-op."""
+    L = ddg.lib()
+    out = ddg._vp()
+    assert L.ddg_forward_graph_enqueue(None) == 1
+    assert L.ddg_forward_graph_sync(None, None, None) == 1
+    assert L.ddg_party_graph_create(None, 1, None, 0, ctypes.byref(out)) == 1
+    assert L.ddg_forward_pipeline_create(None, None, 1, ctypes.byref(out)) == 1
+    assert L.ddg_forward_pipeline_submit(None, None, None, None, None) == 1
+    assert L.ddg_forward_pipeline_wait(None) == 1
+    assert L.ddg_forward_pipeline_destroy(None) == 0
+    assert L.ddg_forward_graph_destroy(None) == 0
