@@ -137,13 +137,16 @@ __host__ __device__ constexpr int place_bits(uint32_t (&used)[3], int words, uin
 // triple-bit positions of a TT plan (see OtPlan::tpa): per level in order its
 // (a, b, b') group, then its (c, c') group (b', c' only for the combines that
 // compute eq), then the mask bit; first fit, in the plan's tri_words() words.
+// Plans whose digit state does not fit 32 bits keep 5 bits per combine.
 // The oracle (oracle/fss_ref.c, tt_place) places them by the same steps.
 __host__ __device__ constexpr void tt_place(OtPlan &P)
 {
     for (int q = 0; q < P.ncomb; q++) P.tpa[q] = uint8_t(5 * q), P.tpc[q] = uint8_t(5 * q + 3);
     P.mu_pos = 5 * P.ncomb;
     P.tpacked = false;
-    if (P.mode == PLAN_OT) return;
+    // the lane layout needs the digit state in one 32-bit word (2 D <= 32): its
+    // lanes, and every group's bits lane .. lane + 2, then stay below bit 31
+    if (P.mode == PLAN_OT || 2 * P.D > 32) return;
     uint32_t used[3] = {0u, 0u, 0u};
     uint8_t pa[OT_MAX_COMB] = {}, pc[OT_MAX_COMB] = {};
     const int words = P.tri_words();

@@ -862,8 +862,9 @@ static int ot_plan_build(int n, int s, ot_plan_t *P) { return digit_plan_build(n
  * lane of the others: they have no b') and then its (c, c') group (3 or 1
  * << lane) are placed first-fit (lowest word, then lowest shift) in the free
  * bits of the tri words, and last the mask bit of the full compare.  When a
- * group does not fit, every combine keeps (a, b, b', c, c') at 5q and the
- * mask bit sits at 5 ncomb. */
+ * group does not fit, or the digit state needs more than 32 bits (2 D > 32),
+ * every combine keeps (a, b, b', c, c') at 5q and the mask bit sits at
+ * 5 ncomb. */
 static int place_bits(uint32_t used[3], int words, uint32_t m)
 {
     int hi = 0;
@@ -888,7 +889,7 @@ static void tt_place(ot_plan_t *P)
 {
     for (int q = 0; q < P->ncomb; q++) P->tpa[q] = 5 * q, P->tpc[q] = 5 * q + 3;
     P->mu_pos = 5 * P->ncomb;
-    if (P->mode == 0) return;
+    if (P->mode == 0 || 2 * P->D > 32) return; /* the lane layout needs the digit state in 32 bits */
     uint32_t used[3] = {0, 0, 0};
     int pa[OT_MAXC], pc[OT_MAXC];
     const int words = (5 * P->ncomb + (P->mode == 3) + 31) / 32;
@@ -1180,15 +1181,16 @@ int ref_tt_plan_info(int kind, int n, int s, int *out4)
     return 1;
 }
 
-/* the plan's triple-bit positions: out[2q] = tpa[q], out[2q + 1] = tpc[q]
- * (q < ncomb), then mu_pos; returns ncomb (0: no plan) */
+/* the plan's triple-bit positions: out[0] = ncomb, out[1 + 2q] = tpa[q],
+ * out[2 + 2q] = tpc[q] (q < ncomb), then mu_pos; returns 1, or 0 without a plan */
 int ref_tt_tri_positions(int kind, int n, int s, int *out)
 {
     ot_plan_t P;
     if (!digit_plan_build(n, s, tt_mode(kind), &P)) return 0;
-    for (int q = 0; q < P.ncomb; q++) out[2 * q] = P.tpa[q], out[2 * q + 1] = P.tpc[q];
-    out[2 * P.ncomb] = P.mu_pos;
-    return P.ncomb;
+    out[0] = P.ncomb;
+    for (int q = 0; q < P.ncomb; q++) out[1 + 2 * q] = P.tpa[q], out[2 + 2 * q] = P.tpc[q];
+    out[1 + 2 * P.ncomb] = P.mu_pos;
+    return 1;
 }
 
 static uint32_t tt_stream_word(const aes_ks *dk, uint32_t op, uint64_t i, int w)

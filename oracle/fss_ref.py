@@ -294,10 +294,10 @@ def tt_tri_positions(kind: int, n: int, s: int) -> dict:
     words: tpa[q] (a, b, b' at +0..2), tpc[q] (c, c' at +0..1), mu (the full
     compare's lo mask bit)."""
     o = (ctypes.c_int * 40)()
-    nc = lib().ref_tt_tri_positions(kind, n, s, o)
-    if not nc:
+    if not lib().ref_tt_tri_positions(kind, n, s, o):
         raise ValueError(f"no truth-table plan for kind={kind} n={n} s={s}")
-    return {"tpa": [o[2 * q] for q in range(nc)], "tpc": [o[2 * q + 1] for q in range(nc)], "mu": o[2 * nc]}
+    nc = o[0]
+    return {"tpa": [o[1 + 2 * q] for q in range(nc)], "tpc": [o[2 + 2 * q] for q in range(nc)], "mu": o[1 + 2 * nc]}
 
 
 def tt_keygen(kind: int, n: int, s: int, seed: int, op: int, i: int, r_in: int):

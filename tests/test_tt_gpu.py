@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 
 from oracle import fss_ref as F
+from oracle.ring_forward import Ring
 from tests.gpu_util import dev_bytes, from_dev, ptr, ring_dt, to_dev
 from tests.test_gates_gpu import make_inputs, plain
 
@@ -20,19 +21,19 @@ TT_KINDS = [F.GATE_RELU_TT, F.GATE_RELU_ARS_TT, F.GATE_LRS_TT, F.GATE_RELU_TTF, 
 FULL_KINDS = (F.GATE_RELU_TTF, F.GATE_RELU_ARS_TTF)
 
 
-def run_tt(ddg, kind, bw, n, x, r, seed=5, op=3):
+def run_tt(ddg, kind, bw, n, x, r, seed=5, op=3, s=S):
     dt = ring_dt(bw)
-    kb = ddg.gate_key_bytes(kind, bw, S, n)
+    kb = ddg.gate_key_bytes(kind, bw, s, n)
     k0, k1 = dev_bytes(kb), dev_bytes(kb)
     d_r, d_ro = to_dev(r), dev_bytes(n * (bw // 8))
-    ddg.gate_keygen(kind, bw, S, n, seed, op, ptr(d_r), ptr(d_ro), ptr(k0), ptr(k1))
+    ddg.gate_keygen(kind, bw, s, n, seed, op, ptr(d_r), ptr(d_ro), ptr(k0), ptr(k1))
     xh = (x + r).astype(dt)
     d_x = to_dev(xh)
     words = (n + 31) // 32
-    nb = ddg.gate_round1_arrays(kind, bw, S)
+    nb = ddg.gate_round1_arrays(kind, bw, s)
     bits = [dev_bytes(4 * nb * words) for _ in range(2)]
     shares = [dev_bytes(n * (bw // 8)) for _ in range(2)]
-    ddg.gate_eval_pair(kind, bw, S, n, ptr(d_x), ptr(k0), ptr(k1), ptr(bits[0]), ptr(bits[1]), ptr(shares[0]),
+    ddg.gate_eval_pair(kind, bw, s, n, ptr(d_x), ptr(k0), ptr(k1), ptr(bits[0]), ptr(bits[1]), ptr(shares[0]),
                        ptr(shares[1]))
     import torch
 
@@ -112,3 +113,27 @@ def test_tt_reconstruction_sizes(ddg, cuda, bw, kind, n):
 def test_tt_empty_is_noop(ddg, cuda):
     for kind in TT_KINDS:
         ddg.gate_eval_pair(kind, 32, S, 0, None, None, None, None, None, None, None)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind", [F.GATE_RELU_TTF, F.GATE_RELU_TT])
+def test_tt_relu_with_a_digit_state_wider_than_32_bits(ddg, cuda, kind):
+    """bw=64 at scale 13 has 17 digits (a 34-bit digit state): the runtime-plan
+    level kernel runs and the triple bits keep 5 per AND, since the grouped
+    layout needs the state in 32 bits.  Every key's triple words equal the
+    oracle's and the reconstructed ReLU equals the plaintext one."""
+    bw, sc, n = 64, 13, 3000
+    dt = ring_dt(bw)
+    rng = np.random.default_rng(13 + kind)
+    x = rng.integers(0, np.iinfo(dt).max, size=n, dtype=dt, endpoint=True)
+    r = rng.integers(0, np.iinfo(dt).max, size=n, dtype=dt, endpoint=True)
+    out = run_tt(ddg, kind, bw, n, x, r, s=sc)
+    lay = ddg.tt_key_layout(kind, bw, sc, n)
+    tri = [out[k][lay["tri"]:lay["tri"] + 4 * lay["tri_words"] * n].view(np.uint32) for k in ("k0", "k1")]
+    for e in range(0, n, 97):
+        k0, k1, _ = F.tt_keygen(kind, bw, sc, 5, 3, e, int(r[e]))
+        for p, ref in ((0, k0), (1, k1)):
+            for j in range(lay["tri_words"]):
+                assert int(tri[p][j * n + e]) == ref.tri[j], (p, j, e)
+    y = (out["y0"] + out["y1"] - out["rout"]).astype(dt)
+    assert np.array_equal(y, Ring(bw).relu(x))

@@ -55,3 +55,26 @@ def test_lane_levels_reconstruct_the_plaintext_comparison(tmp_path):
             assert packed == "1", line  # the benchmarked plans group their triple bits by level
         seen += 1
     assert seen == 6
+    # every scale of both ring widths: the same plans exist on both sides and
+    # every triple bit sits where the oracle's keygen puts it (the runtime-plan
+    # kernel and the keygen of other scales follow the same placement)
+    checked = 0
+    for line in r.stdout.splitlines():
+        if not line.startswith("allpos"):
+            continue
+        head, vals = line.split(":")
+        _, mode, bw, sc, ok, packed = head.split()
+        mode, bw, sc, ok = int(mode), int(bw), int(sc), int(ok)
+        try:
+            want = F.tt_tri_positions(mode_kind[mode], bw, sc)
+        except ValueError:
+            want = None
+        assert (want is not None) == bool(ok), line
+        if want is None:
+            continue
+        v = [int(x) for x in vals.split()]
+        assert v[:-1][0::2] == want["tpa"] and v[:-1][1::2] == want["tpc"], (line, want)
+        if mode == 3:
+            assert v[-1] == want["mu"], (line, want)
+        checked += 1
+    assert checked > 200, checked

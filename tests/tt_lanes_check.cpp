@@ -135,12 +135,45 @@ int check(int trials)
     return bad;
 }
 
+// every truth-table plan (modes, both ring widths, every scale): the triple-bit
+// positions distinct and inside the triple words, printed for the oracle check
+int check_positions_all_scales()
+{
+    int bad = 0;
+    for (int mode : {int(PLAN_TT_RELU), int(PLAN_TT_LRS), int(PLAN_TT_FULL)})
+        for (int nb : {32, 64})
+            for (int sc = 1; sc < nb - 1; sc++) {
+                const OtPlan P = digit_plan(nb, sc, mode);
+                std::printf("allpos %d %d %d %d %d:", mode, nb, sc, int(P.ok), int(P.tpacked));
+                if (!P.ok) {
+                    std::printf("\n");
+                    continue;
+                }
+                uint32_t seen[3] = {0u, 0u, 0u};
+                for (int q = 0; q < P.ncomb; q++)
+                    for (int k = 0; k < 5; k++) {
+                        if (!P.comb[q].eq && (k == 2 || k == 4)) continue;
+                        const int pos = P.tpos(q, k);
+                        if (pos < 0 || pos >= 32 * P.tri_words() || ((seen[pos / 32] >> (pos % 32)) & 1u)) bad++;
+                        else seen[pos / 32] |= 1u << (pos % 32);
+                    }
+                if (mode == PLAN_TT_FULL) {
+                    const int pos = P.mu_bit();
+                    if (pos < 0 || pos >= 32 * P.tri_words() || ((seen[pos / 32] >> (pos % 32)) & 1u)) bad++;
+                }
+                for (int q = 0; q < P.ncomb; q++) std::printf(" %d %d", P.tpa[q], P.tpc[q]);
+                std::printf(" %d\n", P.mu_bit());
+            }
+    if (bad) std::printf("all-scale positions: %d collide or overflow\n", bad);
+    return bad;
+}
+
 }  // namespace
 
 int main(int argc, char **argv)
 {
     const int trials = argc > 1 ? std::atoi(argv[1]) : 20000;
-    int bad = 0;
+    int bad = check_positions_all_scales();
     bad += check<PLAN_TT_RELU, 32>(trials);
     bad += check<PLAN_TT_RELU, 64>(trials);
     bad += check<PLAN_TT_LRS, 32>(trials);
