@@ -31,14 +31,21 @@ def _init(rank, world, port, timeout_s=30):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
 
 
+def _put_and_exit(q, msg, code):
+    """os._exit skips the queue's feeder thread: flush the message first."""
+    q.put(msg)
+    q.close()
+    q.join_thread()
+    os._exit(code)
+
+
 def _worker_layout(rank, world, port, q):
     import torch
 
     try:
         _init(rank, world, port)
     except Exception as e:  # noqa: BLE001 -- reported, so the test retries on another port
-        q.put(("setup failed", rank, type(e).__name__))
-        os._exit(1)
+        _put_and_exit(q, ("setup failed", rank, type(e).__name__), 1)
     pairs, pair, party, peer = bench.roles(rank, world)
     # one id per party pair (and lane), as bench.py broadcasts them
     uids = [[[os.urandom(128) for _ in range(1)] for _ in range(pairs)] if rank == 0 else None]
@@ -102,16 +109,15 @@ def _worker_dies(rank, world, port, q):
         _init(rank, world, port, timeout_s=5)
         dist.barrier()  # both ranks are connected before one of them dies
     except Exception as e:  # noqa: BLE001
-        q.put(("setup failed", rank, type(e).__name__))
-        os._exit(1)
+        _put_and_exit(q, ("setup failed", rank, type(e).__name__), 1)
     if rank == 1:
         os._exit(3)  # the peer dies before the next collective
     try:
         dist.broadcast_object_list([None], src=1)
-        q.put("no error")
+        msg = "no error"
     except Exception as e:  # noqa: BLE001 -- any collective failure is the expected outcome
-        q.put("error: " + type(e).__name__)
-    os._exit(0)
+        msg = "error: " + type(e).__name__
+    _put_and_exit(q, msg, 0)
 
 
 def test_dead_peer_is_detected_not_hung():
